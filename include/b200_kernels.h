@@ -1,0 +1,116 @@
+/*
+ * b200_kernels.h — thin C ABI over the hand-written sm_100a kernels.
+ *
+ * Plain pointers (device memory), sizes and a cudaStream_t passed as void*.
+ * No torch or C++ types cross this boundary.  Every entry point returns 0 on
+ * success or a nonzero B200_ERR_* code; b200_last_error() gives the message of
+ * the calling thread's last failure.  Launches are asynchronous on `stream`.
+ *
+ * The PJRT plugin (libb200_pjrt.so) calls these from its executables; tests and
+ * bench.py call them directly through ctypes.
+ */
+#ifndef B200_KERNELS_H_
+#define B200_KERNELS_H_
+
+#include <stdint.h>
+
+#ifndef B200_API
+#define B200_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  B200_OK = 0,
+  B200_ERR_INVALID = 1,     /* bad argument: shape, alignment, dtype */
+  B200_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  B200_ERR_UNSUPPORTED = 3, /* shape/dtype combination without a kernel */
+  B200_ERR_TIMEOUT = 4      /* a bounded device-side wait ran out */
+};
+
+/* Element types, numbered as PJRT_Buffer_Type (S32=4, F32=11, BF16=13). */
+enum { B200_DT_PRED = 1, B200_DT_S32 = 4, B200_DT_U32 = 8, B200_DT_F32 = 11, B200_DT_BF16 = 13 };
+
+B200_API const char* b200_last_error(void);
+/* Library version string "b200-kernels <semver> sm_100a". */
+B200_API const char* b200_kernels_version(void);
+
+/* Fused residual-add + LayerNorm / RMSNorm forward over the last axis.
+ *   h = x + residual        (residual may be NULL: h = x)
+ *   y = norm(h) * gamma + beta   (gamma/beta may be NULL: 1 / 0)
+ *   norm = (h - mean) * rsqrt(var + eps)   for kind 0 (LayerNorm)
+ *        = h * rsqrt(mean(h^2) + eps)      for kind 1 (RMSNorm)
+ * x, residual, y, h_out: [rows, cols] row-major of `dtype` (F32 or BF16);
+ * gamma, beta: [cols] of `dtype`.  h_out may be NULL.  mean_out/rstd_out
+ * (f32 [rows], may be NULL) keep the statistics for the backward pass.
+ * Replaces reference src/jax_mlx_pjrt.cpp:4430-4437 (mlx.layer_norm /
+ * mlx.rms_norm) and :8208-8236 (custom_call mlx_layer_norm), whose residual add
+ * and affine stayed separate MLX ops. */
+B200_API int b200_ln_residual_fwd(const void* x, const void* residual, const void* gamma,
+                         const void* beta, void* y, void* h_out, float* mean_out,
+                         float* rstd_out, int64_t rows, int64_t cols, float eps,
+                         int dtype, int kind, void* stream);
+
+/* LayerNorm backward (kind 0) given the saved statistics:
+ *   dx[r,:], and column sums dgamma = sum_r dy*xhat, dbeta = sum_r dy.
+ * dgamma/dbeta are f32 [cols] (zeroed and written by the call); `ws` is a
+ * caller-provided f32 scratch of b200_ln_bwd_workspace(rows, cols) bytes.
+ * Replaces reference src/jax_mlx_pjrt.cpp:8238-8281 (mlx_layer_norm_bwd via
+ * mx::vjp) and src/jax_mlx/layer_norm.py:59-76 (its math). */
+B200_API int64_t b200_ln_bwd_workspace(int64_t rows, int64_t cols);
+B200_API int b200_ln_bwd(const void* x, const void* gamma, const float* mean, const float* rstd,
+                const void* dy, void* dx, float* dgamma, float* dbeta, void* ws,
+                int64_t rows, int64_t cols, int dtype, void* stream);
+
+/* Scaled dot-product attention forward, layout BTNH (batch, seq, heads, dim):
+ *   O[b,t,n,:] = softmax_s(scale * Q[b,t,n,:].K[b,s,n,:] + mask) V[b,s,n,:]
+ * with mask = -0.7*FLT_MAX where causal and s > t (JAX's large-negative fill).
+ * q: [B,T,N,D]; k, v: [B,S,N,D]; o: [B,T,N,D]; dtype F32 (tensor cores in TF32,
+ * softmax in f32) or BF16 (kind::f16 MMAs, f32 accumulate).  D must be 64.
+ * Replaces reference src/jax_mlx_pjrt.cpp:4440-4446 / :8111-8150
+ * (mlx::fast::scaled_dot_product_attention) and src/jax_mlx/sdpa.py:19-31. */
+B200_API int b200_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B,
+                  int64_t T, int64_t S, int64_t N, int64_t D, float scale, int causal,
+                  int dtype, void* stream);
+
+/* Same computation with explicit element strides (head dim contiguous):
+ * strides[0..2] = q (b,t,n), [3..5] = k (b,s,n), [6..8] = v (b,s,n),
+ * [9..11] = o (b,t,n).  The plugin uses it for attention matched out of a
+ * dot_general -> softmax -> dot_general chain, whose operands may be BTNH or
+ * BNTH views; every stride must be a multiple of 4 elements (16 bytes). */
+B200_API int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v, void* o,
+                                   int64_t B, int64_t T, int64_t S, int64_t N, int64_t D,
+                                   const int64_t* strides, float scale, int causal, int dtype,
+                                   void* stream);
+
+/* Batched GEMM on tcgen05: for b in [0,batch):
+ *   C_b[m,n] = alpha * sum_k A_b[m,k] * B_b[k,n]  (+ bias[n]) (+ relu)
+ * A element (b,m,k) at a + b*sAb + m*sAm + k*sAk (strides in elements), one of
+ * sAm/sAk must be 1; same for B with (b,k,n).  C is dense row-major [batch,M,N]
+ * unless ldc (elements between rows) says otherwise.  in_dtype F32 (TF32 MMA) or
+ * BF16; out_dtype F32 or BF16; accumulation in f32.  epilogue: 0 none, 1 bias,
+ * 2 bias+relu, 3 relu.
+ * Replaces reference src/jax_mlx_pjrt.cpp:4577-4666 (dot_general ->
+ * transpose/reshape -> mlx::core::matmul). */
+B200_API int b200_gemm(const void* a, const void* b, void* c, const void* bias, int64_t batch,
+              int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
+              int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
+              int in_dtype, int out_dtype, int epilogue, void* stream);
+
+/* 1 when b200_gemm would take the tcgen05/TMA path for these arguments, 0 when
+ * it falls back to the SIMT kernel (rows not 16-byte aligned, tiny K, ...). */
+B200_API int b200_gemm_uses_tensor_cores(const void* a, const void* b, int64_t batch, int64_t K,
+                                         int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
+                                         int64_t sBk, int64_t sBn, int in_dtype);
+
+/* Site code recorded by the last bounded device-side wait that ran out on the
+ * current device (0 = none, -1 = could not be read); clear != 0 resets it.
+ * Synchronizes with the device. */
+B200_API int b200_device_error(int clear);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200_KERNELS_H_ */

@@ -1,0 +1,92 @@
+// CUDA C generation for fused elementwise / reduce / window / gather / scatter
+// kernels (compiled with NVRTC for sm_100a at PJRT_Client_Compile time).
+#pragma once
+#include <functional>
+#include <map>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "ir.h"
+#include "plan.h"
+
+namespace b200 {
+
+// Where the generated code reads a value from: a materialized slot, or (slot
+// < 0) recomputed inline from the value's defining node.
+using SlotOf = std::function<int(ValueRef)>;
+
+struct GenKernel {
+  std::string name;
+  std::string code;
+  std::vector<int> ptr_slots;  // kernel pointer parameters, in order
+  std::vector<bool> ptr_written;
+  int64_t grid = 1, block = 256;
+  int64_t grid_y = 1;
+};
+
+class CodeGen {
+ public:
+  CodeGen(const Graph& g, const std::vector<Slot>& slots, SlotOf slot_of)
+      : g_(g), slots_(slots), slot_of_(std::move(slot_of)) {}
+
+  // out = value at each index of `v`'s shape (loop fusion root).
+  GenKernel loop(const std::vector<ValueRef>& roots, const std::vector<int>& out_slots);
+  // Reduce node (variadic) -> out slots (one per result).
+  GenKernel reduce(int node, const std::vector<int>& out_slots);
+  GenKernel reduce_window(int node, const std::vector<int>& out_slots);
+  GenKernel select_and_scatter(int node, int out_slot);
+  GenKernel gather(int node, int out_slot);
+  // scatter: out already holds the operand; this kernel applies the updates.
+  GenKernel scatter(int node, int out_slot);
+  // im2col for a convolution: A[m, k] (row-major, M x K) from the lhs operand.
+  // k_roles: kernel dims (excluding k_out) in K order; m_roles: output dims
+  // (excluding out_feature) in M order.
+  GenKernel im2col(int node, int out_slot, const std::vector<int64_t>& k_roles,
+                   const std::vector<int64_t>& m_roles, int64_t M, int64_t K);
+  // out[j] = src[permuted j]: out dims are src dims[perm[i]] (a transpose copy).
+  GenKernel permute(int src_slot, const std::vector<int64_t>& perm, int out_slot);
+
+  static std::string prelude();
+  int counter = 0;
+
+ private:
+  struct Idx {
+    std::vector<int64_t> dims;
+    std::string lin;
+    std::vector<std::string> multi;
+  };
+  const Graph& g_;
+  const std::vector<Slot>& slots_;
+  SlotOf slot_of_;
+
+  // per-kernel state
+  std::ostringstream body_;
+  std::vector<int> ptrs_;
+  std::vector<bool> written_;
+  std::vector<std::map<std::string, std::string>> memo_;
+  int tmp_ = 0;
+  int indent_ = 1;
+  std::string idx_t_ = "int";
+
+  void reset();
+  std::string fresh(const char* p = "v");
+  void line(const std::string& s);
+  std::string ptr(int slot, bool write);
+  void ensure_multi(Idx& idx);
+  void ensure_lin(Idx& idx);
+  std::string value(ValueRef v, Idx idx);
+  std::string load(int slot, Idx& idx, DType dt);
+  std::string elementwise(const Node& n, const std::vector<std::string>& a, DType in_dt);
+  std::string literal(const Node& n);
+  std::string emit_region(const Graph& r, const std::vector<std::string>& args,
+                          std::vector<std::string>* outs);
+  std::string header(const std::string& name);
+  GenKernel finish(const std::string& name, int64_t total, int64_t block, int64_t max_grid);
+};
+
+std::string ctype(DType t);     // register type
+std::string stype(DType t);     // storage type
+std::string store_conv(DType t, const std::string& v);  // register -> storage
+
+}  // namespace b200

@@ -1,0 +1,1486 @@
+// PJRT C API implementation (GetPjrtApi) for N CUDA devices.
+//
+// Replaces the reference's PJRT surface (src/jax_mlx_pjrt.cpp:535-1650 and
+// the API table at :9481-9670).  Differences that matter to callers:
+//   - every entry point catches C++ exceptions and returns a PJRT_Error;
+//   - events are real (cudaEvent-backed), not always-ready (ref :559-587);
+//   - OutputElementTypes/OutputDimensions report the compiled program's real
+//     types and shapes (ref :1466-1527 always said F32 / left data unset);
+//   - Buffer_IsOnCpu is false (ref :1254-1257 said true);
+//   - DefaultDeviceAssignment is implemented (ref :935 was a stub);
+//   - executables run replicated over several devices with NCCL all_reduce.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <thread>
+
+#include "b200_kernels.h"
+#include "b200_pjrt.h"
+#include "b200_pjrt_inspect.h"
+#include "passes.h"
+#include "plan.h"
+#include "runtime.h"
+
+using namespace b200;
+
+// ------------------------------------------------------------ objects ---
+struct PJRT_Error {
+  PJRT_Error_Code code;
+  std::string msg;
+};
+
+struct PJRT_Event {
+  std::mutex mu;
+  std::condition_variable cv;
+  cudaEvent_t ev = nullptr;
+  int ordinal = -1;
+  bool host_set = false;  // for host-completed events
+  bool host_done = false;
+  PJRT_Error_Code code = PJRT_Error_Code_OK;
+  std::string msg;
+  virtual ~PJRT_Event() {
+    if (ev) cudaEventDestroy(ev);
+  }
+};
+
+struct PJRT_DeviceDescription {
+  int id = 0;
+  int process_index = 0;
+  std::string kind, debug, tostr;
+  std::vector<PJRT_NamedValue> attrs;
+  std::string cc;
+  int64_t cores = 0;
+};
+
+struct PJRT_Memory {
+  int id = 0;
+  std::string kind = "device";
+  std::string debug, tostr;
+  PJRT_Device* device = nullptr;
+};
+
+struct PJRT_Device {
+  PJRT_DeviceDescription desc;
+  Device* dev = nullptr;  // null when not addressable from this process
+  PJRT_Memory* memory = nullptr;
+  int local_hardware_id = -1;
+};
+
+struct PJRT_TopologyDescription {
+  std::vector<PJRT_DeviceDescription*> descs;
+  std::string name = "b200", version;
+};
+
+struct PJRT_Client {
+  std::vector<std::unique_ptr<Device>> local;
+  std::vector<std::unique_ptr<PJRT_Device>> devices;  // global order
+  std::vector<PJRT_Device*> device_ptrs, addressable;
+  std::vector<std::unique_ptr<PJRT_Memory>> memories;
+  std::vector<PJRT_Memory*> memory_ptrs;
+  int process_index = 0, num_nodes = 1;
+  std::string version;
+  PJRT_KeyValueGetCallback kv_get = nullptr;
+  void* kv_get_arg = nullptr;
+  PJRT_KeyValuePutCallback kv_put = nullptr;
+  void* kv_put_arg = nullptr;
+  std::mutex exec_mu;
+  std::map<std::vector<int>, std::unique_ptr<NcclComms>> comms;  // keyed by global device ids
+  std::atomic<int64_t> comm_counter{0};
+  PJRT_TopologyDescription topo;
+};
+
+struct PJRT_Buffer {
+  PJRT_Client* client = nullptr;
+  PJRT_Device* device = nullptr;
+  TensorType type;
+  std::shared_ptr<DeviceMem> mem;
+  std::shared_ptr<PJRT_Event> ready;  // definition event
+  std::atomic<int> ext_refs{0};
+  bool deleted = false;
+  std::vector<int64_t> dims;  // for Dimensions()
+};
+
+namespace {
+
+struct Exe {
+  PJRT_Client* client = nullptr;
+  Plan plan;
+  std::string cubin;
+  std::string name, fingerprint, text, compile_options;
+  std::vector<int64_t> out_dims_flat;
+  std::vector<size_t> out_dim_sizes;
+  std::vector<PJRT_Buffer_Type> out_types;
+  std::vector<const char*> out_kinds;
+  std::vector<size_t> out_kind_sizes;
+  std::mutex mu;
+  std::map<int, std::unique_ptr<LoadedModule>> modules;  // by device ordinal
+  std::vector<PJRT_Device*> addressable;                 // replica order, this process
+  std::vector<int> replica_of;                           // per addressable device
+  int64_t num_replicas = 1;
+  std::vector<PJRT_NamedValue> cost;
+};
+
+}  // namespace
+
+struct PJRT_Executable {
+  std::shared_ptr<Exe> exe;
+};
+struct PJRT_LoadedExecutable {
+  std::shared_ptr<Exe> exe;
+  bool deleted = false;
+};
+
+namespace {
+
+PJRT_Error* make_err(int code, const std::string& msg) {
+  return new PJRT_Error{(PJRT_Error_Code)code, msg};
+}
+
+#define PJRT_TRY try {
+#define PJRT_CATCH                                                     \
+  }                                                                    \
+  catch (const PjrtErr& e) { return make_err(e.code, e.what()); }      \
+  catch (const std::exception& e) { return make_err(13, e.what()); }   \
+  catch (...) { return make_err(2, "unknown exception"); }             \
+  return nullptr;
+
+bool env_flag(const char* n) {
+  const char* v = std::getenv(n);
+  return v && *v && std::strcmp(v, "0") != 0;
+}
+
+std::shared_ptr<PJRT_Event> record_event(Device& d) {
+  auto e = std::make_shared<PJRT_Event>();
+  d.activate();
+  B200_CUDA(cudaEventCreateWithFlags(&e->ev, cudaEventDisableTiming));
+  B200_CUDA(cudaEventRecord(e->ev, d.stream));
+  e->ordinal = d.ordinal;
+  return e;
+}
+PJRT_Event* ready_event() {
+  auto* e = new PJRT_Event;
+  e->host_set = true;
+  e->host_done = true;
+  return e;
+}
+// Event objects handed to PJRT keep a shared_ptr to the underlying state.
+struct EventHandle : PJRT_Event {
+  std::shared_ptr<PJRT_Event> inner;
+};
+
+PJRT_Event* handle_of(const std::shared_ptr<PJRT_Event>& inner) {
+  auto* h = new EventHandle;
+  h->inner = inner;
+  return h;
+}
+
+bool event_ready(PJRT_Event* e, PJRT_Error_Code* code, std::string* msg) {
+  if (auto* h = dynamic_cast<EventHandle*>(e)) return event_ready(h->inner.get(), code, msg);
+  std::lock_guard<std::mutex> lk(e->mu);
+  if (e->host_set) {
+    *code = e->code;
+    *msg = e->msg;
+    return e->host_done;
+  }
+  if (!e->ev) return true;
+  cudaError_t r = cudaEventQuery(e->ev);
+  if (r == cudaErrorNotReady) return false;
+  if (r != cudaSuccess) {
+    *code = PJRT_Error_Code_INTERNAL;
+    *msg = cudaGetErrorString(r);
+  }
+  return true;
+}
+void event_wait(PJRT_Event* e, PJRT_Error_Code* code, std::string* msg) {
+  if (auto* h = dynamic_cast<EventHandle*>(e)) return event_wait(h->inner.get(), code, msg);
+  if (e->host_set) {
+    std::unique_lock<std::mutex> lk(e->mu);
+    e->cv.wait(lk, [&] { return e->host_done; });
+    *code = e->code;
+    *msg = e->msg;
+    return;
+  }
+  if (!e->ev) return;
+  cudaError_t r = cudaEventSynchronize(e->ev);
+  if (r != cudaSuccess) {
+    *code = PJRT_Error_Code_INTERNAL;
+    *msg = cudaGetErrorString(r);
+  }
+}
+
+DType to_dtype(PJRT_Buffer_Type t) {
+  switch (t) {
+    case PJRT_Buffer_Type_PRED: return DType::PRED;
+    case PJRT_Buffer_Type_S8: return DType::S8;
+    case PJRT_Buffer_Type_S16: return DType::S16;
+    case PJRT_Buffer_Type_S32: return DType::S32;
+    case PJRT_Buffer_Type_S64: return DType::S64;
+    case PJRT_Buffer_Type_U8: return DType::U8;
+    case PJRT_Buffer_Type_U16: return DType::U16;
+    case PJRT_Buffer_Type_U32: return DType::U32;
+    case PJRT_Buffer_Type_U64: return DType::U64;
+    case PJRT_Buffer_Type_F32: return DType::F32;
+    case PJRT_Buffer_Type_F64: return DType::F64;
+    case PJRT_Buffer_Type_BF16: return DType::BF16;
+    default: throw PjrtErr(12, "buffer element type " + std::to_string((int)t) + " is not supported");
+  }
+}
+
+int64_t kv_timeout_ms() {
+  const char* v = std::getenv("B200_KV_TIMEOUT_MS");
+  return v ? std::atoll(v) : 120000;
+}
+
+std::string kv_get(PJRT_Client* c, const std::string& key) {
+  if (!c->kv_get) throw PjrtErr(9, "multi-process execution needs the client's KV-store callbacks");
+  PJRT_KeyValueGetCallback_Args a{};
+  a.struct_size = sizeof(a);
+  a.key = key.data();
+  a.key_size = key.size();
+  a.timeout_in_ms = (int)kv_timeout_ms();
+  a.user_arg = c->kv_get_arg;
+  PJRT_Error* e = c->kv_get(&a);
+  if (e) {
+    std::string m = e->msg;
+    delete e;
+    throw PjrtErr(4, "KV get '" + key + "' failed: " + m);
+  }
+  std::string v(a.value, a.value_size);
+  if (a.value_deleter_callback) a.value_deleter_callback(a.value);
+  return v;
+}
+void kv_put(PJRT_Client* c, const std::string& key, const std::string& val) {
+  if (!c->kv_put) throw PjrtErr(9, "multi-process execution needs the client's KV-store callbacks");
+  PJRT_KeyValuePutCallback_Args a{};
+  a.struct_size = sizeof(a);
+  a.key = key.data();
+  a.key_size = key.size();
+  a.value = val.data();
+  a.value_size = val.size();
+  a.user_arg = c->kv_put_arg;
+  PJRT_Error* e = c->kv_put(&a);
+  if (e) {
+    std::string m = e->msg;
+    delete e;
+    throw PjrtErr(13, "KV put '" + key + "' failed: " + m);
+  }
+}
+
+// ---------------------------------------------- bytecode -> text (jaxlib) --
+// JAX hands the plugin a StableHLO portable artifact (MLIR bytecode).  As in
+// the reference (src/jax_mlx_pjrt.cpp:671-830) it is turned into text through
+// the MLIR/StableHLO C API that jaxlib has loaded in this process.
+std::string bytecode_to_text(const std::string& code) {
+  struct StrRef { const char* data; size_t length; };
+  struct Handle { void* ptr; };
+  using CtxCreate = Handle (*)();
+  using CtxDestroy = void (*)(Handle);
+  using Deser = Handle (*)(StrRef, Handle);
+  using GetOp = Handle (*)(Handle);
+  using Print = void (*)(Handle, void (*)(StrRef, void*), void*);
+  using ModDestroy = void (*)(Handle);
+  using Register = void (*)(Handle);
+  void* self = RTLD_DEFAULT;
+  auto deser = (Deser)dlsym(self, "stablehloDeserializePortableArtifactNoError");
+  auto ctxc = (CtxCreate)dlsym(self, "mlirContextCreate");
+  auto ctxd = (CtxDestroy)dlsym(self, "mlirContextDestroy");
+  auto getop = (GetOp)dlsym(self, "mlirModuleGetOperation");
+  auto print = (Print)dlsym(self, "mlirOperationPrint");
+  auto moddel = (ModDestroy)dlsym(self, "mlirModuleDestroy");
+  auto reg = (Register)dlsym(self, "stablehloRegisterAllDialects");
+  if (!deser || !ctxc || !getop || !print)
+    throw PjrtErr(12,
+                  "program is MLIR bytecode but the StableHLO C API is not loaded in this "
+                  "process; pass StableHLO text (format \"mlir\") instead");
+  Handle ctx = ctxc();
+  if (reg) reg(ctx);
+  Handle mod = deser(StrRef{code.data(), code.size()}, ctx);
+  if (!mod.ptr) {
+    if (ctxd) ctxd(ctx);
+    throw PjrtErr(3, "failed to deserialize the StableHLO portable artifact");
+  }
+  std::string out;
+  print(getop(mod), [](StrRef s, void* u) { static_cast<std::string*>(u)->append(s.data, s.length); },
+        &out);
+  if (moddel) moddel(mod);
+  if (ctxd) ctxd(ctx);
+  return out;
+}
+
+// Minimal protobuf walk: CompileOptionsProto.executable_build_options (3)
+// .num_replicas (4) / .num_partitions (5).
+bool pb_varint(const uint8_t*& p, const uint8_t* e, uint64_t* v) {
+  *v = 0;
+  for (int s = 0; p < e && s < 64; s += 7) {
+    uint8_t b = *p++;
+    *v |= (uint64_t)(b & 0x7f) << s;
+    if (!(b & 0x80)) return true;
+  }
+  return false;
+}
+void pb_fields(const std::string& buf, const std::function<void(int, int, uint64_t, const std::string&)>& f) {
+  const uint8_t* p = (const uint8_t*)buf.data();
+  const uint8_t* e = p + buf.size();
+  while (p < e) {
+    uint64_t key;
+    if (!pb_varint(p, e, &key)) return;
+    int field = (int)(key >> 3), wt = (int)(key & 7);
+    if (wt == 0) {
+      uint64_t v;
+      if (!pb_varint(p, e, &v)) return;
+      f(field, wt, v, "");
+    } else if (wt == 2) {
+      uint64_t n;
+      if (!pb_varint(p, e, &n) || p + n > e) return;
+      f(field, wt, 0, std::string((const char*)p, n));
+      p += n;
+    } else if (wt == 1) {
+      p += 8;
+    } else if (wt == 5) {
+      p += 4;
+    } else {
+      return;
+    }
+  }
+}
+void replicas_from_options(const std::string& opts, int64_t* reps, int64_t* parts) {
+  pb_fields(opts, [&](int f, int wt, uint64_t, const std::string& sub) {
+    if (f == 3 && wt == 2)
+      pb_fields(sub, [&](int g, int wt2, uint64_t v, const std::string&) {
+        if (wt2 != 0) return;
+        if (g == 4 && v > 0) *reps = (int64_t)v;
+        if (g == 5 && v > 0) *parts = (int64_t)v;
+      });
+  });
+}
+
+std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std::string& opts) {
+  std::string text = code;
+  if (code.size() >= 4 && code.compare(0, 4, "ML\xefR") == 0) text = bytecode_to_text(code);
+  Module m = parse_module(text);
+  int64_t reps = 1, parts = 1;
+  replicas_from_options(opts, &reps, &parts);
+  if (m.num_replicas > 1) reps = m.num_replicas;
+  if (m.num_partitions > 1) parts = m.num_partitions;
+  if (parts > 1)
+    throw PjrtErr(12, "num_partitions > 1 (SPMD partitioning) is not supported; use pmap or "
+                      "shard_map style replication");
+  m.num_replicas = reps;
+  auto e = std::make_shared<Exe>();
+  e->client = c;
+  e->plan = build_plan(m);
+  e->plan.num_replicas = reps;
+  e->num_replicas = reps;
+  e->text = text;
+  e->compile_options = opts;
+  e->name = m.name.empty() ? "main" : m.name;
+  e->fingerprint = std::to_string(std::hash<std::string>()(text));
+  if (!e->plan.kernel_names.empty()) e->cubin = nvrtc_compile(e->plan.source, "b200_" + e->fingerprint);
+  for (auto& t : e->plan.output_types) {
+    e->out_dim_sizes.push_back(t.dims.size());
+    e->out_dims_flat.insert(e->out_dims_flat.end(), t.dims.begin(), t.dims.end());
+    e->out_types.push_back((PJRT_Buffer_Type)t.dtype);
+    e->out_kinds.push_back("device");
+    e->out_kind_sizes.push_back(6);
+  }
+  // replica r runs on global device r
+  if ((int64_t)c->device_ptrs.size() < reps)
+    throw PjrtErr(3, "program needs " + std::to_string(reps) + " replicas but the client has " +
+                         std::to_string(c->device_ptrs.size()) + " devices");
+  for (int64_t r = 0; r < reps; ++r) {
+    PJRT_Device* d = c->device_ptrs[r];
+    if (d->dev) {
+      e->addressable.push_back(d);
+      e->replica_of.push_back((int)r);
+    }
+  }
+  if (env_flag("B200_DUMP")) {
+    std::fprintf(stderr, "[b200] graph:\n%s\n[b200] plan:\n%s\n", e->plan.graph_dump.c_str(),
+                 dump_plan(e->plan).c_str());
+  }
+  return e;
+}
+
+void kcheck(int rc, const char* what) {
+  if (rc != 0) throw PjrtErr(rc == B200_ERR_INVALID ? 3 : 13, std::string(what) + ": " + b200_last_error());
+}
+
+NcclComms& comms_for(PJRT_Client* c, Exe& e) {
+  std::vector<int> ids;
+  for (int64_t r = 0; r < e.num_replicas; ++r) ids.push_back((int)r);
+  auto it = c->comms.find(ids);
+  if (it != c->comms.end()) return *it->second;
+  std::unique_ptr<NcclComms> comm;
+  if (c->num_nodes == 1) {
+    std::vector<Device*> devs;
+    for (auto* d : e.addressable) devs.push_back(d->dev);
+    comm = nccl_init_all(devs);
+  } else {
+    if (e.addressable.size() != 1)
+      throw PjrtErr(12, "multi-process execution supports one device per process");
+    const int rank = e.replica_of[0];
+    const std::string key = "b200/nccl_uid/" + std::to_string(e.num_replicas);
+    std::vector<char> uid;
+    if (rank == 0) {
+      uid = nccl_unique_id();
+      kv_put(c, key, std::string(uid.begin(), uid.end()));
+    } else {
+      std::string v = kv_get(c, key);
+      uid.assign(v.begin(), v.end());
+    }
+    comm = nccl_init_rank(e.addressable[0]->dev, (int)e.num_replicas, rank, uid);
+  }
+  auto& ref = *comm;
+  c->comms[ids] = std::move(comm);
+  return ref;
+}
+
+void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
+  Exe& e = *le->exe;
+  PJRT_Client* c = e.client;
+  const Plan& p = e.plan;
+  if (le->deleted) throw PjrtErr(9, "executable was deleted");
+  std::vector<PJRT_Device*> devs;
+  if (a->execute_device) {
+    if (a->num_devices != 1) throw PjrtErr(3, "execute_device requires num_devices == 1");
+    devs.push_back(a->execute_device);
+  } else {
+    if (a->num_devices != e.addressable.size())
+      throw PjrtErr(3, "Execute got " + std::to_string(a->num_devices) + " argument lists for " +
+                           std::to_string(e.addressable.size()) + " addressable replicas");
+    devs = e.addressable;
+  }
+  const size_t nd = devs.size();
+  if (a->num_args != p.param_slots.size())
+    throw PjrtErr(3, "Execute got " + std::to_string(a->num_args) + " arguments, program takes " +
+                         std::to_string(p.param_slots.size()));
+  std::lock_guard<std::mutex> xl(c->exec_mu);
+  // modules + constants per device
+  for (auto* pd : devs) {
+    if (!pd->dev) throw PjrtErr(3, "device is not addressable from this process");
+    std::lock_guard<std::mutex> lk(e.mu);
+    auto& slot = e.modules[pd->dev->ordinal];
+    if (!slot) {
+      auto m = load_module(*pd->dev, e.cubin, p.kernel_names);
+      for (auto& cd : p.consts) {
+        (void)cd;
+      }
+      for (size_t s = 0; s < p.slots.size(); ++s) {
+        const Slot& sl = p.slots[s];
+        if (sl.kind != Slot::CONST) continue;
+        auto mem = std::make_shared<DeviceMem>(pd->dev, (size_t)sl.bytes);
+        const ConstData& cd = p.consts.at(sl.index);
+        pd->dev->activate();
+        B200_CUDA(cudaMemcpy(mem->ptr, cd.bytes.data(), (size_t)sl.bytes, cudaMemcpyHostToDevice));
+        if ((int)m->consts.size() <= sl.index) m->consts.resize(sl.index + 1);
+        m->consts[sl.index] = mem;
+      }
+      slot = std::move(m);
+    }
+  }
+  // bind slots
+  std::vector<std::vector<void*>> ptr(nd, std::vector<void*>(p.slots.size(), nullptr));
+  std::vector<std::vector<std::shared_ptr<DeviceMem>>> owned(nd, std::vector<std::shared_ptr<DeviceMem>>(p.slots.size()));
+  for (size_t d = 0; d < nd; ++d) {
+    for (size_t i = 0; i < a->num_args; ++i) {
+      PJRT_Buffer* b = a->argument_lists[d][i];
+      if (!b || b->deleted || !b->mem) throw PjrtErr(3, "argument " + std::to_string(i) + " is deleted or null");
+      const TensorType& want = p.param_types[i];
+      if (b->type != want)
+        throw PjrtErr(3, "argument " + std::to_string(i) + " has type " + b->type.str() +
+                             ", program expects " + want.str());
+      if (b->device != devs[d]) throw PjrtErr(3, "argument " + std::to_string(i) + " lives on another device");
+      ptr[d][p.param_slots[i]] = b->mem->ptr;
+      owned[d][p.param_slots[i]] = b->mem;
+    }
+    auto& mod = *e.modules.at(devs[d]->dev->ordinal);
+    for (size_t s = 0; s < p.slots.size(); ++s)
+      if (p.slots[s].kind == Slot::CONST) ptr[d][s] = mod.consts.at(p.slots[s].index)->ptr;
+  }
+  auto ensure = [&](size_t d, int s) {
+    if (s < 0 || ptr[d][s]) return;
+    const Slot& sl = p.slots[s];
+    owned[d][s] = std::make_shared<DeviceMem>(devs[d]->dev, (size_t)std::max<int64_t>(sl.bytes, 1));
+    ptr[d][s] = owned[d][s]->ptr;
+  };
+  for (size_t si = 0; si < p.steps.size(); ++si) {
+    const Step& st = p.steps[si];
+    for (size_t d = 0; d < nd; ++d) {
+      for (int s : st.out) ensure(d, s);
+      for (int s : st.in) ensure(d, s);
+    }
+    if (st.kind == StepKind::AllReduce) {
+      std::vector<Device*> dd;
+      std::vector<const void*> in;
+      std::vector<void*> out;
+      for (size_t d = 0; d < nd; ++d) {
+        dd.push_back(devs[d]->dev);
+        in.push_back(ptr[d][st.in[0]]);
+        out.push_back(ptr[d][st.out[0]]);
+      }
+      if (e.num_replicas == 1) {
+        for (size_t d = 0; d < nd; ++d) {
+          dd[d]->activate();
+          B200_CUDA(cudaMemcpyAsync(out[d], in[d], (size_t)p.slots[st.out[0]].bytes,
+                                    cudaMemcpyDeviceToDevice, dd[d]->stream));
+        }
+      } else {
+        NcclComms& comm = comms_for(c, e);
+        nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1]);
+      }
+    } else {
+      for (size_t d = 0; d < nd; ++d) {
+        Device& dev = *devs[d]->dev;
+        dev.activate();
+        void* const* P = ptr[d].data();
+        auto slotp = [&](int s) -> void* { return s < 0 ? nullptr : P[s]; };
+        switch (st.kind) {
+          case StepKind::Kernel: {
+            auto& mod = *e.modules.at(dev.ordinal);
+            std::vector<void*> vals;
+            vals.reserve(st.args.size());
+            for (auto& arg : st.args) vals.push_back(slotp(arg.slot));
+            std::vector<void*> args;
+            for (auto& v : vals) args.push_back(&v);
+            launch(dev, mod.fns.at(st.name), st.grid, st.block, st.smem, args);
+            break;
+          }
+          case StepKind::LayerNorm:
+            kcheck(b200_ln_residual_fwd(slotp(st.in[0]), slotp(st.in[1]), slotp(st.in[2]),
+                                        slotp(st.in[3]), slotp(st.out[0]), slotp(st.out[1]), nullptr,
+                                        nullptr, st.ip[0], st.ip[1], st.fp[0], st.dtype,
+                                        (int)st.ip[2], dev.stream),
+                   "layer_norm");
+            break;
+          case StepKind::Sdpa:
+            kcheck(b200_sdpa_fwd_strided(slotp(st.in[0]), slotp(st.in[1]), slotp(st.in[2]),
+                                         slotp(st.out[0]), st.ip[0], st.ip[1], st.ip[2], st.ip[3],
+                                         st.ip[4], st.ip.data() + 5, st.fp[0], (int)st.ip[17],
+                                         st.dtype, dev.stream),
+                   "sdpa");
+            break;
+          case StepKind::Gemm:
+            kcheck(b200_gemm(slotp(st.in[0]), slotp(st.in[1]), slotp(st.out[0]),
+                             st.in.size() > 2 ? slotp(st.in[2]) : nullptr, st.ip[0], st.ip[1],
+                             st.ip[2], st.ip[3], st.ip[4], st.ip[5], st.ip[6], st.ip[7], st.ip[8],
+                             st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2, (int)st.ip[11],
+                             dev.stream),
+                   "gemm");
+            break;
+          case StepKind::Copy:
+            B200_CUDA(cudaMemcpyAsync(slotp(st.out[0]), slotp(st.in[0]),
+                                      (size_t)p.slots[st.out[0]].bytes, cudaMemcpyDeviceToDevice,
+                                      dev.stream));
+            break;
+          default:
+            break;
+        }
+      }
+    }
+    if (env_flag("B200_SYNC_STEPS")) {
+      for (size_t d = 0; d < nd; ++d) {
+        devs[d]->dev->activate();
+        cudaError_t r = cudaStreamSynchronize(devs[d]->dev->stream);
+        if (r != cudaSuccess) throw PjrtErr(13, "step " + st.name + " failed: " + cudaGetErrorString(r));
+      }
+    }
+    // release temps whose last use was this step (stream order makes reuse safe)
+    for (size_t d = 0; d < nd; ++d)
+      for (auto* v : {&st.in, &st.out})
+        for (int s : *v)
+          if (s >= 0 && p.slots[s].kind == Slot::TEMP && p.temp_last[s] == (int)si) {
+            owned[d][s].reset();
+            ptr[d][s] = nullptr;
+          }
+  }
+  for (size_t d = 0; d < nd; ++d) {
+    auto ev = record_event(*devs[d]->dev);
+    if (a->device_complete_events) a->device_complete_events[d] = handle_of(ev);
+    for (size_t o = 0; o < p.output_slots.size(); ++o) {
+      int s = p.output_slots[o];
+      auto* b = new PJRT_Buffer;
+      b->client = c;
+      b->device = devs[d];
+      b->type = p.slots[s].type;
+      b->dims = b->type.dims;
+      b->mem = owned[d][s];
+      if (!b->mem) {  // zero-size output never touched by a step
+        b->mem = std::make_shared<DeviceMem>(devs[d]->dev, 1);
+      }
+      b->ready = ev;
+      a->output_lists[d][o] = b;
+    }
+  }
+}
+
+// ------------------------------------------------------ client creation --
+std::string device_kind() { return "NVIDIA B200"; }
+
+PJRT_Client* create_client(const PJRT_Client_Create_Args* args) {
+  auto c = std::make_unique<PJRT_Client>();
+  std::vector<int> visible;
+  int64_t node_id = 0, num_nodes = 1;
+  for (size_t i = 0; i < args->num_options; ++i) {
+    const PJRT_NamedValue& v = args->create_options[i];
+    std::string name(v.name, v.name_size);
+    if (name == "visible_devices" && v.type == PJRT_NamedValue_kInt64List)
+      for (size_t k = 0; k < v.value_size; ++k) visible.push_back((int)v.int64_array_value[k]);
+    if (name == "node_id" && v.type == PJRT_NamedValue_kInt64) node_id = v.int64_value;
+    if (name == "num_nodes" && v.type == PJRT_NamedValue_kInt64) num_nodes = v.int64_value;
+  }
+  int count = 0;
+  cudaError_t r = cudaGetDeviceCount(&count);
+  if (r != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    throw PjrtErr(14, std::string("no CUDA device available: ") + cudaGetErrorString(r));
+  }
+  if (visible.empty())
+    for (int i = 0; i < count; ++i) visible.push_back(i);
+  c->process_index = (int)node_id;
+  c->num_nodes = (int)num_nodes;
+  c->kv_get = args->kv_get_callback;
+  c->kv_get_arg = args->kv_get_user_arg;
+  c->kv_put = args->kv_put_callback;
+  c->kv_put_arg = args->kv_put_user_arg;
+  int rt = 0, drv = 0;
+  cudaRuntimeGetVersion(&rt);
+  cudaDriverGetVersion(&drv);
+  c->version = "b200-pjrt 0.1.0; cuda runtime " + std::to_string(rt) + ", driver " + std::to_string(drv);
+  const int local_n = (int)visible.size();
+  for (int li = 0; li < local_n; ++li) {
+    auto d = std::make_unique<Device>();
+    d->ordinal = visible[li];
+    B200_CUDA(cudaSetDevice(d->ordinal));
+    B200_CUDA(cudaFree(nullptr));
+    B200_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+    cudaDeviceProp prop;
+    B200_CUDA(cudaGetDeviceProperties(&prop, d->ordinal));
+    d->name = prop.name;
+    d->sms = prop.multiProcessorCount;
+    d->total_mem = (int64_t)prop.totalGlobalMem;
+    d->alloc = std::make_unique<Allocator>(d->ordinal);
+    c->local.push_back(std::move(d));
+  }
+  // global devices: node-major, local_n per node (homogeneous nodes assumed)
+  for (int64_t nidx = 0; nidx < num_nodes; ++nidx)
+    for (int li = 0; li < local_n; ++li) {
+      auto pd = std::make_unique<PJRT_Device>();
+      const int gid = (int)(nidx * local_n + li);
+      pd->desc.id = gid;
+      pd->desc.process_index = (int)nidx;
+      pd->desc.kind = device_kind();
+      pd->desc.debug = "b200:" + std::to_string(gid);
+      pd->desc.tostr = "B200Device(id=" + std::to_string(gid) + ", process=" + std::to_string(nidx) + ")";
+      pd->desc.cc = "10.0";
+      if (nidx == node_id) {
+        pd->dev = c->local[li].get();
+        pd->local_hardware_id = pd->dev->ordinal;
+        pd->desc.cores = pd->dev->sms;
+      }
+      PJRT_NamedValue cc{};
+      cc.struct_size = sizeof(cc);
+      cc.name = "compute_capability";
+      cc.name_size = std::strlen(cc.name);
+      cc.type = PJRT_NamedValue_kString;
+      cc.string_value = pd->desc.cc.c_str();
+      cc.value_size = pd->desc.cc.size();
+      PJRT_NamedValue cores{};
+      cores.struct_size = sizeof(cores);
+      cores.name = "core_count";
+      cores.name_size = std::strlen(cores.name);
+      cores.type = PJRT_NamedValue_kInt64;
+      cores.int64_value = pd->desc.cores;
+      cores.value_size = 1;
+      pd->desc.attrs = {cc, cores};
+      auto mem = std::make_unique<PJRT_Memory>();
+      mem->id = gid;
+      mem->device = pd.get();
+      mem->debug = "b200_hbm:" + std::to_string(gid);
+      mem->tostr = "MEMORY_SPACE(device, id=" + std::to_string(gid) + ")";
+      pd->memory = mem.get();
+      if (pd->dev) {
+        c->addressable.push_back(pd.get());
+        c->memory_ptrs.push_back(mem.get());
+      }
+      c->device_ptrs.push_back(pd.get());
+      c->memories.push_back(std::move(mem));
+      c->devices.push_back(std::move(pd));
+    }
+  for (auto* d : c->device_ptrs) c->topo.descs.push_back(&d->desc);
+  c->topo.version = c->version;
+  return c.release();
+}
+
+// --------------------------------------------------------------- buffers --
+PJRT_Buffer* buffer_from_host(PJRT_Client* c, const PJRT_Client_BufferFromHostBuffer_Args* a,
+                              PJRT_Event** done) {
+  PJRT_Device* pd = a->device;
+  if (!pd && a->memory) pd = a->memory->device;
+  if (!pd) pd = c->addressable.at(0);
+  if (!pd->dev) throw PjrtErr(3, "BufferFromHostBuffer: device is not addressable");
+  TensorType t;
+  t.dtype = to_dtype(a->type);
+  t.dims.assign(a->dims, a->dims + a->num_dims);
+  const int es = dtype_size(t.dtype);
+  if (a->byte_strides && a->num_byte_strides) {
+    int64_t expect = es;
+    for (int i = (int)a->num_dims - 1; i >= 0; --i) {
+      if (t.dims[i] != 1 && a->byte_strides[i] != expect)
+        throw PjrtErr(12, "BufferFromHostBuffer: only dense row-major host layouts are supported");
+      expect *= t.dims[i];
+    }
+  }
+  auto b = std::make_unique<PJRT_Buffer>();
+  b->client = c;
+  b->device = pd;
+  b->type = t;
+  b->dims = t.dims;
+  Device& d = *pd->dev;
+  std::lock_guard<std::recursive_mutex> lk(d.mu);
+  b->mem = std::make_shared<DeviceMem>(&d, (size_t)std::max<int64_t>(t.bytes(), 1));
+  d.activate();
+  if (t.bytes() > 0)
+    B200_CUDA(cudaMemcpyAsync(b->mem->ptr, a->data, (size_t)t.bytes(), cudaMemcpyHostToDevice, d.stream));
+  b->ready = record_event(d);
+  cudaPointerAttributes attr{};
+  const bool pinned = cudaPointerGetAttributes(&attr, a->data) == cudaSuccess &&
+                      (attr.type == cudaMemoryTypeHost);
+  cudaGetLastError();
+  if (pinned && a->host_buffer_semantics == PJRT_HostBufferSemantics_kImmutableOnlyDuringCall) {
+    B200_CUDA(cudaEventSynchronize(b->ready->ev));
+    *done = ready_event();
+  } else if (pinned) {
+    *done = handle_of(b->ready);
+  } else {
+    *done = ready_event();  // pageable source: cudaMemcpyAsync staged it before returning
+  }
+  return b.release();
+}
+
+}  // namespace
+
+// =================================================================== API ===
+extern "C" {
+
+static PJRT_Error* Error_Destroy(PJRT_Error_Destroy_Args* a) {
+  delete a->error;
+  return nullptr;
+}
+static PJRT_Error* Error_Message(PJRT_Error_Message_Args* a) {
+  a->message = a->error->msg.c_str();
+  a->message_size = a->error->msg.size();
+  return nullptr;
+}
+static PJRT_Error* Error_GetCode(PJRT_Error_GetCode_Args* a) {
+  a->code = a->error->code;
+  return nullptr;
+}
+static PJRT_Error* Plugin_Initialize(PJRT_Plugin_Initialize_Args*) { return nullptr; }
+
+static int64_t kStablehloCur[3] = {1, 9, 0};
+static int64_t kStablehloMin[3] = {0, 9, 0};
+static PJRT_NamedValue kPluginAttrs[3];
+static PJRT_Error* Plugin_Attributes(PJRT_Plugin_Attributes_Args* a) {
+  static bool init = [] {
+    auto set_list = [](PJRT_NamedValue& v, const char* n, int64_t* arr) {
+      v = PJRT_NamedValue{};
+      v.struct_size = sizeof(v);
+      v.name = n;
+      v.name_size = std::strlen(n);
+      v.type = PJRT_NamedValue_kInt64List;
+      v.int64_array_value = arr;
+      v.value_size = 3;
+    };
+    set_list(kPluginAttrs[0], "stablehlo_current_version", kStablehloCur);
+    set_list(kPluginAttrs[1], "stablehlo_minimum_version", kStablehloMin);
+    kPluginAttrs[2] = PJRT_NamedValue{};
+    kPluginAttrs[2].struct_size = sizeof(PJRT_NamedValue);
+    kPluginAttrs[2].name = "xla_version";
+    kPluginAttrs[2].name_size = 11;
+    kPluginAttrs[2].type = PJRT_NamedValue_kInt64;
+    kPluginAttrs[2].int64_value = 2;
+    kPluginAttrs[2].value_size = 1;
+    return true;
+  }();
+  (void)init;
+  a->attributes = kPluginAttrs;
+  a->num_attributes = 3;
+  return nullptr;
+}
+
+// ---- events
+static PJRT_Error* Event_Destroy(PJRT_Event_Destroy_Args* a) {
+  delete a->event;
+  return nullptr;
+}
+static PJRT_Error* Event_IsReady(PJRT_Event_IsReady_Args* a) {
+  PJRT_Error_Code code = PJRT_Error_Code_OK;
+  std::string msg;
+  a->is_ready = event_ready(a->event, &code, &msg);
+  return nullptr;
+}
+static PJRT_Error* Event_Error(PJRT_Event_Error_Args* a) {
+  PJRT_Error_Code code = PJRT_Error_Code_OK;
+  std::string msg;
+  event_wait(a->event, &code, &msg);
+  return code == PJRT_Error_Code_OK ? nullptr : make_err(code, msg);
+}
+static PJRT_Error* Event_Await(PJRT_Event_Await_Args* a) {
+  PJRT_Error_Code code = PJRT_Error_Code_OK;
+  std::string msg;
+  event_wait(a->event, &code, &msg);
+  return code == PJRT_Error_Code_OK ? nullptr : make_err(code, msg);
+}
+static PJRT_Error* Event_OnReady(PJRT_Event_OnReady_Args* a) {
+  PJRT_Event* ev = a->event;
+  auto cb = a->callback;
+  void* ua = a->user_arg;
+  PJRT_Error_Code code = PJRT_Error_Code_OK;
+  std::string msg;
+  if (event_ready(ev, &code, &msg)) {
+    cb(code == PJRT_Error_Code_OK ? nullptr : make_err(code, msg), ua);
+    return nullptr;
+  }
+  // wait on a helper thread; the event must outlive the callback (PJRT contract)
+  std::thread([ev, cb, ua] {
+    PJRT_Error_Code c2 = PJRT_Error_Code_OK;
+    std::string m2;
+    event_wait(ev, &c2, &m2);
+    cb(c2 == PJRT_Error_Code_OK ? nullptr : make_err(c2, m2), ua);
+  }).detach();
+  return nullptr;
+}
+static PJRT_Error* Event_Create(PJRT_Event_Create_Args* a) {
+  auto* e = new PJRT_Event;
+  e->host_set = true;
+  a->event = e;
+  return nullptr;
+}
+static PJRT_Error* Event_Set(PJRT_Event_Set_Args* a) {
+  PJRT_Event* e = a->event;
+  {
+    std::lock_guard<std::mutex> lk(e->mu);
+    e->host_done = true;
+    e->code = a->error_code;
+    if (a->error_message) e->msg.assign(a->error_message, a->error_message_size);
+  }
+  e->cv.notify_all();
+  return nullptr;
+}
+
+// ---- client
+static PJRT_Error* Client_Create(PJRT_Client_Create_Args* a) {
+  PJRT_TRY
+  a->client = create_client(a);
+  PJRT_CATCH
+}
+static PJRT_Error* Client_Destroy(PJRT_Client_Destroy_Args* a) {
+  PJRT_TRY
+  PJRT_Client* c = a->client;
+  for (auto& d : c->local) {
+    d->activate();
+    cudaStreamSynchronize(d->stream);
+  }
+  c->comms.clear();
+  for (auto& d : c->local) {
+    d->activate();
+    d->alloc->release_cache();
+    cudaStreamDestroy(d->stream);
+  }
+  delete c;
+  PJRT_CATCH
+}
+static PJRT_Error* Client_PlatformName(PJRT_Client_PlatformName_Args* a) {
+  static const char kName[] = "b200";
+  a->platform_name = kName;
+  a->platform_name_size = 4;
+  return nullptr;
+}
+static PJRT_Error* Client_ProcessIndex(PJRT_Client_ProcessIndex_Args* a) {
+  a->process_index = a->client->process_index;
+  return nullptr;
+}
+static PJRT_Error* Client_PlatformVersion(PJRT_Client_PlatformVersion_Args* a) {
+  a->platform_version = a->client->version.c_str();
+  a->platform_version_size = a->client->version.size();
+  return nullptr;
+}
+static PJRT_Error* Client_Devices(PJRT_Client_Devices_Args* a) {
+  a->devices = a->client->device_ptrs.data();
+  a->num_devices = a->client->device_ptrs.size();
+  return nullptr;
+}
+static PJRT_Error* Client_AddressableDevices(PJRT_Client_AddressableDevices_Args* a) {
+  a->addressable_devices = a->client->addressable.data();
+  a->num_addressable_devices = a->client->addressable.size();
+  return nullptr;
+}
+static PJRT_Error* Client_LookupDevice(PJRT_Client_LookupDevice_Args* a) {
+  for (auto* d : a->client->device_ptrs)
+    if (d->desc.id == a->id) { a->device = d; return nullptr; }
+  return make_err(5, "no device with id " + std::to_string(a->id));
+}
+static PJRT_Error* Client_LookupAddressableDevice(PJRT_Client_LookupAddressableDevice_Args* a) {
+  for (auto* d : a->client->addressable)
+    if (d->local_hardware_id == a->local_hardware_id) { a->addressable_device = d; return nullptr; }
+  return make_err(5, "no addressable device with local id " + std::to_string(a->local_hardware_id));
+}
+static PJRT_Error* Client_AddressableMemories(PJRT_Client_AddressableMemories_Args* a) {
+  a->addressable_memories = a->client->memory_ptrs.data();
+  a->num_addressable_memories = a->client->memory_ptrs.size();
+  return nullptr;
+}
+static PJRT_Error* Client_Compile(PJRT_Client_Compile_Args* a) {
+  PJRT_TRY
+  std::string fmt(a->program->format, a->program->format_size);
+  if (fmt != "mlir") throw PjrtErr(3, "program format '" + fmt + "' is not supported (want mlir)");
+  std::string code(a->program->code, a->program->code_size);
+  std::string opts(a->compile_options ? a->compile_options : "", a->compile_options_size);
+  auto* le = new PJRT_LoadedExecutable;
+  le->exe = compile(a->client, code, opts);
+  a->executable = le;
+  PJRT_CATCH
+}
+static PJRT_Error* Client_DefaultDeviceAssignment(PJRT_Client_DefaultDeviceAssignment_Args* a) {
+  const int64_t need = (int64_t)a->num_replicas * a->num_partitions;
+  if ((int64_t)a->client->device_ptrs.size() < need)
+    return make_err(3, "not enough devices for " + std::to_string(need) + " replicas x partitions");
+  if ((int64_t)a->default_assignment_size < need) return make_err(3, "assignment buffer too small");
+  for (int64_t i = 0; i < need; ++i) a->default_assignment[i] = a->client->device_ptrs[i]->desc.id;
+  return nullptr;
+}
+static PJRT_Error* Client_BufferFromHostBuffer(PJRT_Client_BufferFromHostBuffer_Args* a) {
+  PJRT_TRY
+  PJRT_Event* done = nullptr;
+  a->buffer = buffer_from_host(a->client, a, &done);
+  a->done_with_host_buffer = done;
+  PJRT_CATCH
+}
+static PJRT_Error* Client_CreateViewOfDeviceBuffer(PJRT_Client_CreateViewOfDeviceBuffer_Args* a) {
+  PJRT_TRY
+  PJRT_Device* pd = a->device ? a->device : (a->memory ? a->memory->device : nullptr);
+  if (!pd || !pd->dev) throw PjrtErr(3, "CreateViewOfDeviceBuffer: device required");
+  auto* b = new PJRT_Buffer;
+  b->client = a->client;
+  b->device = pd;
+  b->type.dtype = to_dtype(a->element_type);
+  b->type.dims.assign(a->dims, a->dims + a->num_dims);
+  b->dims = b->type.dims;
+  // a view does not own the memory; the caller's callback runs when it is released
+  auto mem = std::make_shared<DeviceMem>(pd->dev, a->device_buffer_ptr, (size_t)b->type.bytes());
+  auto cb = a->on_delete_callback;
+  void* arg = a->on_delete_callback_arg;
+  if (cb) mem->on_release = [cb, arg](void* p) { cb(p, arg); };
+  b->mem = mem;
+  b->ready = nullptr;
+  a->buffer = b;
+  PJRT_CATCH
+}
+static PJRT_Error* Client_TopologyDescription(PJRT_Client_TopologyDescription_Args* a) {
+  a->topology = &a->client->topo;
+  return nullptr;
+}
+
+// ---- device descriptions / devices / memories
+static PJRT_Error* DeviceDescription_Id(PJRT_DeviceDescription_Id_Args* a) {
+  a->id = a->device_description->id;
+  return nullptr;
+}
+static PJRT_Error* DeviceDescription_ProcessIndex(PJRT_DeviceDescription_ProcessIndex_Args* a) {
+  a->process_index = a->device_description->process_index;
+  return nullptr;
+}
+static PJRT_Error* DeviceDescription_Attributes(PJRT_DeviceDescription_Attributes_Args* a) {
+  a->attributes = a->device_description->attrs.data();
+  a->num_attributes = a->device_description->attrs.size();
+  return nullptr;
+}
+static PJRT_Error* DeviceDescription_Kind(PJRT_DeviceDescription_Kind_Args* a) {
+  a->device_kind = a->device_description->kind.c_str();
+  a->device_kind_size = a->device_description->kind.size();
+  return nullptr;
+}
+static PJRT_Error* DeviceDescription_DebugString(PJRT_DeviceDescription_DebugString_Args* a) {
+  a->debug_string = a->device_description->debug.c_str();
+  a->debug_string_size = a->device_description->debug.size();
+  return nullptr;
+}
+static PJRT_Error* DeviceDescription_ToString(PJRT_DeviceDescription_ToString_Args* a) {
+  a->to_string = a->device_description->tostr.c_str();
+  a->to_string_size = a->device_description->tostr.size();
+  return nullptr;
+}
+static PJRT_Error* Device_GetDescription(PJRT_Device_GetDescription_Args* a) {
+  a->device_description = &a->device->desc;
+  return nullptr;
+}
+static PJRT_Error* Device_IsAddressable(PJRT_Device_IsAddressable_Args* a) {
+  a->is_addressable = a->device->dev != nullptr;
+  return nullptr;
+}
+static PJRT_Error* Device_LocalHardwareId(PJRT_Device_LocalHardwareId_Args* a) {
+  a->local_hardware_id = a->device->local_hardware_id;
+  return nullptr;
+}
+static PJRT_Error* Device_AddressableMemories(PJRT_Device_AddressableMemories_Args* a) {
+  a->memories = &a->device->memory;
+  a->num_memories = a->device->dev ? 1 : 0;
+  return nullptr;
+}
+static PJRT_Error* Device_DefaultMemory(PJRT_Device_DefaultMemory_Args* a) {
+  a->memory = a->device->memory;
+  return nullptr;
+}
+static PJRT_Error* Device_MemoryStats(PJRT_Device_MemoryStats_Args* a) {
+  if (!a->device->dev) return make_err(3, "device is not addressable");
+  Allocator& al = *a->device->dev->alloc;
+  a->bytes_in_use = al.in_use();
+  a->peak_bytes_in_use = al.peak();
+  a->peak_bytes_in_use_is_set = true;
+  a->num_allocs = al.num_allocs();
+  a->num_allocs_is_set = true;
+  a->bytes_reserved = al.reserved();
+  a->bytes_reserved_is_set = true;
+  a->bytes_limit = a->device->dev->total_mem;
+  a->bytes_limit_is_set = true;
+  return nullptr;
+}
+static PJRT_Error* Memory_Id(PJRT_Memory_Id_Args* a) {
+  a->id = a->memory->id;
+  return nullptr;
+}
+static PJRT_Error* Memory_Kind(PJRT_Memory_Kind_Args* a) {
+  a->kind = a->memory->kind.c_str();
+  a->kind_size = a->memory->kind.size();
+  return nullptr;
+}
+static PJRT_Error* Memory_Kind_Id(PJRT_Memory_Kind_Id_Args* a) {
+  a->kind_id = 0;
+  return nullptr;
+}
+static PJRT_Error* Memory_DebugString(PJRT_Memory_DebugString_Args* a) {
+  a->debug_string = a->memory->debug.c_str();
+  a->debug_string_size = a->memory->debug.size();
+  return nullptr;
+}
+static PJRT_Error* Memory_ToString(PJRT_Memory_ToString_Args* a) {
+  a->to_string = a->memory->tostr.c_str();
+  a->to_string_size = a->memory->tostr.size();
+  return nullptr;
+}
+static PJRT_Error* Memory_AddressableByDevices(PJRT_Memory_AddressableByDevices_Args* a) {
+  a->devices = &a->memory->device;
+  a->num_devices = 1;
+  return nullptr;
+}
+
+// ---- executables
+static PJRT_Error* Executable_Destroy(PJRT_Executable_Destroy_Args* a) {
+  delete a->executable;
+  return nullptr;
+}
+static PJRT_Error* Executable_Name(PJRT_Executable_Name_Args* a) {
+  a->executable_name = a->executable->exe->name.c_str();
+  a->executable_name_size = a->executable->exe->name.size();
+  return nullptr;
+}
+static PJRT_Error* Executable_NumReplicas(PJRT_Executable_NumReplicas_Args* a) {
+  a->num_replicas = (size_t)a->executable->exe->num_replicas;
+  return nullptr;
+}
+static PJRT_Error* Executable_NumPartitions(PJRT_Executable_NumPartitions_Args* a) {
+  a->num_partitions = 1;
+  return nullptr;
+}
+static PJRT_Error* Executable_NumOutputs(PJRT_Executable_NumOutputs_Args* a) {
+  a->num_outputs = a->executable->exe->plan.output_types.size();
+  return nullptr;
+}
+static PJRT_Error* Executable_SizeOfGeneratedCodeInBytes(PJRT_Executable_SizeOfGeneratedCodeInBytes_Args* a) {
+  a->size_in_bytes = (int64_t)a->executable->exe->cubin.size();
+  return nullptr;
+}
+static PJRT_Error* Executable_GetCostAnalysis(PJRT_Executable_GetCostAnalysis_Args* a) {
+  a->num_properties = 0;
+  a->properties = nullptr;
+  return nullptr;
+}
+static PJRT_Error* Executable_OutputMemoryKinds(PJRT_Executable_OutputMemoryKinds_Args* a) {
+  Exe& e = *a->executable->exe;
+  a->num_outputs = e.out_kinds.size();
+  a->memory_kinds = e.out_kinds.data();
+  a->memory_kind_sizes = e.out_kind_sizes.data();
+  return nullptr;
+}
+static PJRT_Error* Executable_OutputElementTypes(PJRT_Executable_OutputElementTypes_Args* a) {
+  Exe& e = *a->executable->exe;
+  a->output_types = e.out_types.data();
+  a->num_output_types = e.out_types.size();
+  return nullptr;
+}
+static PJRT_Error* Executable_OutputDimensions(PJRT_Executable_OutputDimensions_Args* a) {
+  Exe& e = *a->executable->exe;
+  a->num_outputs = e.out_dim_sizes.size();
+  a->dims = e.out_dims_flat.data();
+  a->dim_sizes = e.out_dim_sizes.data();
+  return nullptr;
+}
+static PJRT_Error* Executable_Fingerprint(PJRT_Executable_Fingerprint_Args* a) {
+  a->executable_fingerprint = a->executable->exe->fingerprint.c_str();
+  a->executable_fingerprint_size = a->executable->exe->fingerprint.size();
+  return nullptr;
+}
+static PJRT_Error* Executable_OptimizedProgram(PJRT_Executable_OptimizedProgram_Args* a) {
+  Exe& e = *a->executable->exe;
+  PJRT_Program* p = a->program;
+  static const char kFmt[] = "mlir";
+  if (!p->code) {
+    p->code_size = e.text.size();
+  } else {
+    std::memcpy(p->code, e.text.data(), std::min(p->code_size, e.text.size()));
+    p->code_size = e.text.size();
+  }
+  p->format = kFmt;
+  p->format_size = 4;
+  return nullptr;
+}
+struct SerializedBlob {
+  std::string bytes;
+};
+static void delete_blob(PJRT_SerializedExecutable* b) { delete reinterpret_cast<SerializedBlob*>(b); }
+static void delete_opts(PJRT_SerializedCompileOptions* b) { delete reinterpret_cast<SerializedBlob*>(b); }
+static PJRT_Error* Executable_Serialize(PJRT_Executable_Serialize_Args* a) {
+  // Serialized form: magic, the program text and the compile options; loading
+  // it recompiles (the NVRTC cubin cache makes that cheap).
+  const Exe& e = *a->executable->exe;
+  auto* blob = new SerializedBlob;
+  auto put = [&](const std::string& s) {
+    uint64_t n = s.size();
+    blob->bytes.append((const char*)&n, 8);
+    blob->bytes += s;
+  };
+  blob->bytes = "B200EXE1";
+  put(e.text);
+  put(e.compile_options);
+  a->serialized_bytes = blob->bytes.data();
+  a->serialized_bytes_size = blob->bytes.size();
+  a->serialized_executable = reinterpret_cast<PJRT_SerializedExecutable*>(blob);
+  a->serialized_executable_deleter = delete_blob;
+  return nullptr;
+}
+static PJRT_Error* Executable_GetCompileOptions(PJRT_Executable_GetCompileOptions_Args* a) {
+  auto* blob = new SerializedBlob{a->executable->exe->compile_options};
+  a->serialized_bytes = blob->bytes.data();
+  a->serialized_bytes_size = blob->bytes.size();
+  a->serialized_compile_options = reinterpret_cast<PJRT_SerializedCompileOptions*>(blob);
+  a->serialized_compile_options_deleter = delete_opts;
+  return nullptr;
+}
+static PJRT_Error* Executable_DeserializeAndLoad(PJRT_Executable_DeserializeAndLoad_Args* a) {
+  PJRT_TRY
+  std::string s(a->serialized_executable, a->serialized_executable_size);
+  if (s.size() < 16 || s.compare(0, 8, "B200EXE1") != 0) throw PjrtErr(3, "not a B200 serialized executable");
+  size_t off = 8;
+  auto get = [&]() {
+    if (off + 8 > s.size()) throw PjrtErr(3, "truncated serialized executable");
+    uint64_t n;
+    std::memcpy(&n, s.data() + off, 8);
+    off += 8;
+    if (off + n > s.size()) throw PjrtErr(3, "truncated serialized executable");
+    std::string r = s.substr(off, n);
+    off += n;
+    return r;
+  };
+  std::string text = get();
+  std::string opts = get();
+  if (a->overridden_serialized_compile_options && a->overridden_serialized_compile_options_size)
+    opts.assign(a->overridden_serialized_compile_options, a->overridden_serialized_compile_options_size);
+  auto* le = new PJRT_LoadedExecutable;
+  le->exe = compile(a->client, text, opts);
+  a->loaded_executable = le;
+  PJRT_CATCH
+}
+static PJRT_Error* LoadedExecutable_Destroy(PJRT_LoadedExecutable_Destroy_Args* a) {
+  delete a->executable;
+  return nullptr;
+}
+static PJRT_Error* LoadedExecutable_GetExecutable(PJRT_LoadedExecutable_GetExecutable_Args* a) {
+  a->executable = new PJRT_Executable{a->loaded_executable->exe};
+  return nullptr;
+}
+static PJRT_Error* LoadedExecutable_AddressableDevices(PJRT_LoadedExecutable_AddressableDevices_Args* a) {
+  a->addressable_devices = a->executable->exe->addressable.data();
+  a->num_addressable_devices = a->executable->exe->addressable.size();
+  return nullptr;
+}
+static PJRT_Error* LoadedExecutable_Delete(PJRT_LoadedExecutable_Delete_Args* a) {
+  a->executable->deleted = true;
+  return nullptr;
+}
+static PJRT_Error* LoadedExecutable_IsDeleted(PJRT_LoadedExecutable_IsDeleted_Args* a) {
+  a->is_deleted = a->executable->deleted;
+  return nullptr;
+}
+static PJRT_Error* LoadedExecutable_Execute(PJRT_LoadedExecutable_Execute_Args* a) {
+  PJRT_TRY
+  execute(a->executable, a);
+  PJRT_CATCH
+}
+static PJRT_Error* LoadedExecutable_Fingerprint(PJRT_LoadedExecutable_Fingerprint_Args* a) {
+  a->executable_fingerprint = a->executable->exe->fingerprint.c_str();
+  a->executable_fingerprint_size = a->executable->exe->fingerprint.size();
+  return nullptr;
+}
+
+// ---- buffers
+static PJRT_Error* Buffer_Destroy(PJRT_Buffer_Destroy_Args* a) {
+  delete a->buffer;
+  return nullptr;
+}
+static PJRT_Error* Buffer_ElementType(PJRT_Buffer_ElementType_Args* a) {
+  a->type = (PJRT_Buffer_Type)a->buffer->type.dtype;
+  return nullptr;
+}
+static PJRT_Error* Buffer_Dimensions(PJRT_Buffer_Dimensions_Args* a) {
+  a->dims = a->buffer->dims.data();
+  a->num_dims = a->buffer->dims.size();
+  return nullptr;
+}
+static PJRT_Error* Buffer_UnpaddedDimensions(PJRT_Buffer_UnpaddedDimensions_Args* a) {
+  a->unpadded_dims = a->buffer->dims.data();
+  a->num_dims = a->buffer->dims.size();
+  return nullptr;
+}
+static PJRT_Error* Buffer_DynamicDimensionIndices(PJRT_Buffer_DynamicDimensionIndices_Args* a) {
+  a->dynamic_dim_indices = nullptr;
+  a->num_dynamic_dims = 0;
+  return nullptr;
+}
+static PJRT_Error* Buffer_OnDeviceSizeInBytes(PJRT_Buffer_OnDeviceSizeInBytes_Args* a) {
+  a->on_device_size_in_bytes = (size_t)a->buffer->type.bytes();
+  return nullptr;
+}
+static PJRT_Error* Buffer_Device(PJRT_Buffer_Device_Args* a) {
+  a->device = a->buffer->device;
+  return nullptr;
+}
+static PJRT_Error* Buffer_Memory(PJRT_Buffer_Memory_Args* a) {
+  a->memory = a->buffer->device->memory;
+  return nullptr;
+}
+static PJRT_Error* Buffer_Delete(PJRT_Buffer_Delete_Args* a) {
+  a->buffer->deleted = true;
+  a->buffer->mem.reset();
+  return nullptr;
+}
+static PJRT_Error* Buffer_IsDeleted(PJRT_Buffer_IsDeleted_Args* a) {
+  a->is_deleted = a->buffer->deleted;
+  return nullptr;
+}
+static PJRT_Error* Buffer_IsOnCpu(PJRT_Buffer_IsOnCpu_Args* a) {
+  a->is_on_cpu = false;
+  return nullptr;
+}
+static PJRT_Error* Buffer_ReadyEvent(PJRT_Buffer_ReadyEvent_Args* a) {
+  a->event = a->buffer->ready ? handle_of(a->buffer->ready) : ready_event();
+  return nullptr;
+}
+static PJRT_Error* Buffer_UnsafePointer(PJRT_Buffer_UnsafePointer_Args* a) {
+  a->buffer_pointer = a->buffer->mem ? (uintptr_t)a->buffer->mem->ptr : 0;
+  return nullptr;
+}
+static PJRT_Error* Buffer_OpaqueDeviceMemoryDataPointer(PJRT_Buffer_OpaqueDeviceMemoryDataPointer_Args* a) {
+  a->device_memory_ptr = a->buffer->mem ? a->buffer->mem->ptr : nullptr;
+  return nullptr;
+}
+static PJRT_Error* Buffer_IncreaseExternalReferenceCount(PJRT_Buffer_IncreaseExternalReferenceCount_Args* a) {
+  a->buffer->ext_refs++;
+  return nullptr;
+}
+static PJRT_Error* Buffer_DecreaseExternalReferenceCount(PJRT_Buffer_DecreaseExternalReferenceCount_Args* a) {
+  if (a->buffer->ext_refs.load() <= 0) return make_err(9, "external reference count is already zero");
+  a->buffer->ext_refs--;
+  return nullptr;
+}
+static PJRT_Error* Buffer_ToHostBuffer(PJRT_Buffer_ToHostBuffer_Args* a) {
+  PJRT_TRY
+  PJRT_Buffer* b = a->src;
+  const size_t need = (size_t)b->type.bytes();
+  if (!a->dst) {
+    a->dst_size = need;
+    return nullptr;
+  }
+  if (b->deleted || !b->mem) throw PjrtErr(9, "ToHostBuffer on a deleted buffer");
+  if (a->dst_size < need) throw PjrtErr(3, "ToHostBuffer: destination too small");
+  Device& d = *b->device->dev;
+  std::lock_guard<std::recursive_mutex> lk(d.mu);
+  d.activate();
+  if (need) B200_CUDA(cudaMemcpyAsync(a->dst, b->mem->ptr, need, cudaMemcpyDeviceToHost, d.stream));
+  a->event = handle_of(record_event(d));
+  PJRT_CATCH
+}
+static PJRT_Error* Buffer_CopyRawToHost(PJRT_Buffer_CopyRawToHost_Args* a) {
+  PJRT_TRY
+  PJRT_Buffer* b = a->buffer;
+  if (b->deleted || !b->mem) throw PjrtErr(9, "CopyRawToHost on a deleted buffer");
+  if (a->offset < 0 || a->offset + a->transfer_size > b->type.bytes()) throw PjrtErr(11, "CopyRawToHost out of range");
+  Device& d = *b->device->dev;
+  d.activate();
+  B200_CUDA(cudaMemcpyAsync(a->dst, (char*)b->mem->ptr + a->offset, (size_t)a->transfer_size,
+                            cudaMemcpyDeviceToHost, d.stream));
+  a->event = handle_of(record_event(d));
+  PJRT_CATCH
+}
+static PJRT_Error* Buffer_CopyToDevice(PJRT_Buffer_CopyToDevice_Args* a) {
+  PJRT_TRY
+  PJRT_Buffer* b = a->buffer;
+  PJRT_Device* dst = a->dst_device;
+  if (!dst->dev || !b->device->dev) throw PjrtErr(3, "CopyToDevice needs addressable devices");
+  auto* nb = new PJRT_Buffer;
+  nb->client = b->client;
+  nb->device = dst;
+  nb->type = b->type;
+  nb->dims = b->dims;
+  nb->mem = std::make_shared<DeviceMem>(dst->dev, (size_t)std::max<int64_t>(b->type.bytes(), 1));
+  // order after the source's producer, then copy on the destination stream
+  b->device->dev->activate();
+  auto src_ev = record_event(*b->device->dev);
+  dst->dev->activate();
+  B200_CUDA(cudaStreamWaitEvent(dst->dev->stream, src_ev->ev, 0));
+  B200_CUDA(cudaMemcpyPeerAsync(nb->mem->ptr, dst->dev->ordinal, b->mem->ptr, b->device->dev->ordinal,
+                                (size_t)b->type.bytes(), dst->dev->stream));
+  nb->ready = record_event(*dst->dev);
+  // keep the source alive until the copy is done
+  B200_CUDA(cudaStreamWaitEvent(b->device->dev->stream, nb->ready->ev, 0));
+  a->dst_buffer = nb;
+  PJRT_CATCH
+}
+static PJRT_Error* Buffer_CopyToMemory(PJRT_Buffer_CopyToMemory_Args* a) {
+  PJRT_Buffer_CopyToDevice_Args c{};
+  c.struct_size = sizeof(c);
+  c.buffer = a->buffer;
+  c.dst_device = a->dst_memory->device;
+  PJRT_Error* e = Buffer_CopyToDevice(&c);
+  a->dst_buffer = c.dst_buffer;
+  return e;
+}
+
+// ---- topology
+static PJRT_Error* TopologyDescription_Destroy(PJRT_TopologyDescription_Destroy_Args*) { return nullptr; }
+static PJRT_Error* TopologyDescription_PlatformName(PJRT_TopologyDescription_PlatformName_Args* a) {
+  a->platform_name = "b200";
+  a->platform_name_size = 4;
+  return nullptr;
+}
+static PJRT_Error* TopologyDescription_PlatformVersion(PJRT_TopologyDescription_PlatformVersion_Args* a) {
+  a->platform_version = a->topology->version.c_str();
+  a->platform_version_size = a->topology->version.size();
+  return nullptr;
+}
+static PJRT_Error* TopologyDescription_GetDeviceDescriptions(PJRT_TopologyDescription_GetDeviceDescriptions_Args* a) {
+  a->descriptions = a->topology->descs.data();
+  a->num_descriptions = a->topology->descs.size();
+  return nullptr;
+}
+static PJRT_Error* TopologyDescription_Attributes(PJRT_TopologyDescription_Attributes_Args* a) {
+  a->attributes = nullptr;
+  a->num_attributes = 0;
+  return nullptr;
+}
+
+static PJRT_Error* Unimplemented(void*) { return make_err(12, "this PJRT entry point is not implemented by the B200 plugin"); }
+
+static PJRT_Api g_api;
+
+__attribute__((visibility("default"))) const PJRT_Api* GetPjrtApi(void) {
+  static bool init = [] {
+    std::memset(&g_api, 0, sizeof(g_api));
+    g_api.struct_size = sizeof(PJRT_Api);
+    g_api.pjrt_api_version.struct_size = sizeof(PJRT_Api_Version);
+    g_api.pjrt_api_version.major_version = B200_PJRT_API_MAJOR;
+    g_api.pjrt_api_version.minor_version = B200_PJRT_API_MINOR;
+    // every slot starts as Unimplemented, then the implemented ones are set
+#define B200_FILL(name) g_api.PJRT_##name = reinterpret_cast<decltype(g_api.PJRT_##name)>(&Unimplemented);
+    B200_PJRT_API_SLOTS(B200_FILL)
+#undef B200_FILL
+#define SET(name) g_api.PJRT_##name = reinterpret_cast<decltype(g_api.PJRT_##name)>(&name);
+    SET(Error_Destroy) SET(Error_Message) SET(Error_GetCode)
+    SET(Plugin_Initialize) SET(Plugin_Attributes)
+    SET(Event_Destroy) SET(Event_IsReady) SET(Event_Error) SET(Event_Await) SET(Event_OnReady)
+    SET(Event_Create) SET(Event_Set)
+    SET(Client_Create) SET(Client_Destroy) SET(Client_PlatformName) SET(Client_ProcessIndex)
+    SET(Client_PlatformVersion) SET(Client_Devices) SET(Client_AddressableDevices)
+    SET(Client_LookupDevice) SET(Client_LookupAddressableDevice) SET(Client_AddressableMemories)
+    SET(Client_Compile) SET(Client_DefaultDeviceAssignment) SET(Client_BufferFromHostBuffer)
+    SET(Client_CreateViewOfDeviceBuffer) SET(Client_TopologyDescription)
+    SET(DeviceDescription_Id) SET(DeviceDescription_ProcessIndex) SET(DeviceDescription_Attributes)
+    SET(DeviceDescription_Kind) SET(DeviceDescription_DebugString) SET(DeviceDescription_ToString)
+    SET(Device_GetDescription) SET(Device_IsAddressable) SET(Device_LocalHardwareId)
+    SET(Device_AddressableMemories) SET(Device_DefaultMemory) SET(Device_MemoryStats)
+    SET(Memory_Id) SET(Memory_Kind) SET(Memory_Kind_Id) SET(Memory_DebugString) SET(Memory_ToString)
+    SET(Memory_AddressableByDevices)
+    SET(Executable_Destroy) SET(Executable_Name) SET(Executable_NumReplicas)
+    SET(Executable_NumPartitions) SET(Executable_NumOutputs)
+    SET(Executable_SizeOfGeneratedCodeInBytes) SET(Executable_GetCostAnalysis)
+    SET(Executable_OutputMemoryKinds) SET(Executable_OptimizedProgram) SET(Executable_Serialize)
+    SET(Executable_OutputElementTypes) SET(Executable_OutputDimensions) SET(Executable_Fingerprint)
+    SET(Executable_GetCompileOptions) SET(Executable_DeserializeAndLoad)
+    SET(LoadedExecutable_Destroy) SET(LoadedExecutable_GetExecutable)
+    SET(LoadedExecutable_AddressableDevices) SET(LoadedExecutable_Delete)
+    SET(LoadedExecutable_IsDeleted) SET(LoadedExecutable_Execute) SET(LoadedExecutable_Fingerprint)
+    SET(Buffer_Destroy) SET(Buffer_ElementType) SET(Buffer_Dimensions) SET(Buffer_UnpaddedDimensions)
+    SET(Buffer_DynamicDimensionIndices) SET(Buffer_OnDeviceSizeInBytes) SET(Buffer_Device)
+    SET(Buffer_Memory) SET(Buffer_Delete) SET(Buffer_IsDeleted) SET(Buffer_CopyToDevice)
+    SET(Buffer_ToHostBuffer) SET(Buffer_IsOnCpu) SET(Buffer_ReadyEvent) SET(Buffer_UnsafePointer)
+    SET(Buffer_IncreaseExternalReferenceCount) SET(Buffer_DecreaseExternalReferenceCount)
+    SET(Buffer_OpaqueDeviceMemoryDataPointer) SET(Buffer_CopyToMemory) SET(Buffer_CopyRawToHost)
+    SET(TopologyDescription_Destroy) SET(TopologyDescription_PlatformName)
+    SET(TopologyDescription_PlatformVersion) SET(TopologyDescription_GetDeviceDescriptions)
+    SET(TopologyDescription_Attributes)
+#undef SET
+    return true;
+  }();
+  (void)init;
+  return &g_api;
+}
+
+// ---- diagnostics (no GPU needed)
+__attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, size_t len, int what,
+                                                             char** out) {
+  std::string res;
+  int code = 0;
+  try {
+    Module m = parse_module(std::string(mlir, len));
+    Plan p = build_plan(m);
+    if (what == 0) res = p.graph_dump;
+    else if (what == 1) res = dump_plan(p);
+    else if (what == 2) res = p.source;
+    else if (what == 3) {
+      std::string cubin = p.kernel_names.empty() ? "" : nvrtc_compile(p.source, "inspect");
+      res = "ok " + std::to_string(cubin.size());
+    } else res = "bad 'what'";
+  } catch (const PjrtErr& e) {
+    code = e.code;
+    res = e.what();
+  } catch (const std::exception& e) {
+    code = 13;
+    res = e.what();
+  }
+  *out = (char*)std::malloc(res.size() + 1);
+  std::memcpy(*out, res.c_str(), res.size() + 1);
+  return code;
+}
+__attribute__((visibility("default"))) void b200_pjrt_free(char* p) { std::free(p); }
+
+__attribute__((visibility("default"))) void* b200_pjrt_device_stream(void* device) {
+  auto* d = static_cast<PJRT_Device*>(device);
+  return d && d->dev ? (void*)d->dev->stream : nullptr;
+}
+
+}  // extern "C"

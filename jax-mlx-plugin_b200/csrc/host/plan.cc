@@ -1,0 +1,590 @@
+// Executable planner: IR -> slots + launch steps.
+//
+// Fusion policy (what the reference left to mx::compile, src/jax_mlx_pjrt.cpp
+// :9056-9143): elementwise and layout ops are recomputed inside their
+// consumers' kernels when they have a single consumer or are pure index
+// arithmetic (broadcast, reshape, transpose, slice, convert, iota, constants);
+// everything else is materialized once.  Reductions, windows, gathers and
+// scatters read their operands through the same fused expressions.  dot_general
+// and convolution lower to the tcgen05 GEMM (convolution through an im2col
+// kernel), the matched SDPA / LayerNorm nodes to their hand-written kernels.
+#include "plan.h"
+
+#include <algorithm>
+#include <cmath>
+#include <functional>
+#include <map>
+#include <set>
+#include <sstream>
+
+#include "codegen.h"
+#include "passes.h"
+
+namespace b200 {
+namespace {
+
+bool is_fusible(Op op) {
+  switch (op) {
+    case Op::Constant: case Op::Iota:
+    case Op::Neg: case Op::Abs: case Op::Exp: case Op::Expm1: case Op::Log: case Op::Log1p:
+    case Op::Sqrt: case Op::Rsqrt: case Op::Cbrt: case Op::Tanh: case Op::Logistic: case Op::Sin:
+    case Op::Cos: case Op::Tan: case Op::Erf: case Op::Floor: case Op::Ceil: case Op::RoundAfz:
+    case Op::RoundEven: case Op::Sign: case Op::Not: case Op::IsFinite:
+    case Op::Add: case Op::Sub: case Op::Mul: case Op::Div: case Op::Rem: case Op::Max:
+    case Op::Min: case Op::Pow: case Op::Atan2: case Op::And: case Op::Or: case Op::Xor:
+    case Op::ShiftLeft: case Op::ShiftRightArith: case Op::ShiftRightLogical:
+    case Op::Compare: case Op::Select: case Op::Clamp: case Op::Convert: case Op::BitcastConvert:
+    case Op::BroadcastInDim: case Op::Reshape: case Op::Transpose: case Op::Slice:
+    case Op::DynamicSlice: case Op::DynamicUpdateSlice: case Op::Pad: case Op::Concatenate:
+    case Op::Reverse:
+      return true;
+    default:
+      return false;
+  }
+}
+// Ops whose recomputation costs only index arithmetic.
+bool is_cheap(const Node& n) {
+  switch (n.op) {
+    case Op::Constant: case Op::Iota: case Op::BroadcastInDim: case Op::Reshape:
+    case Op::Transpose: case Op::Slice: case Op::Reverse: case Op::Convert: case Op::Neg:
+      return true;
+    default:
+      return false;
+  }
+}
+// Consumers that read operands through generated expressions.
+bool reads_expressions(Op op) {
+  return is_fusible(op) || op == Op::Reduce || op == Op::ReduceWindow ||
+         op == Op::SelectAndScatter || op == Op::Gather || op == Op::Scatter;
+}
+
+struct Builder {
+  Plan& p;
+  Graph& g;
+  Uses u;
+  std::map<ValueRef, int> slot;  // materialized values
+  CodeGen cg;
+  std::vector<GenKernel> kernels;
+
+  Builder(Plan& pl, Graph& gr)
+      : p(pl), g(gr), u(compute_uses(gr)),
+        cg(gr, pl.slots, [this](ValueRef v) {
+          auto it = slot.find(v);
+          return it == slot.end() ? -1 : it->second;
+        }) {}
+
+  int new_slot(Slot::Kind k, const TensorType& t, const std::string& what, int index = -1) {
+    Slot s;
+    s.kind = k;
+    s.type = t;
+    s.bytes = t.bytes();
+    s.index = index;
+    s.what = what;
+    p.slots.push_back(s);
+    return (int)p.slots.size() - 1;
+  }
+  int temp_for(ValueRef v) {
+    auto it = slot.find(v);
+    if (it != slot.end()) return it->second;
+    const Node& n = g.nodes[v.node];
+    int s = new_slot(Slot::TEMP, g.type(v), n.name.empty() ? op_name(n.op) : n.name);
+    slot[v] = s;
+    return s;
+  }
+  void add_kernel(GenKernel k) {
+    Step st;
+    st.kind = StepKind::Kernel;
+    st.name = k.name;
+    st.grid[0] = k.grid;
+    if (k.grid_y < 0) {  // reduce: 2-D block (32, RY)
+      st.block[0] = 32;
+      st.block[1] = -k.grid_y;
+    } else {
+      st.block[0] = k.block;
+    }
+    for (size_t i = 0; i < k.ptr_slots.size(); ++i) {
+      Arg a;
+      a.kind = Arg::PTR;
+      a.slot = k.ptr_slots[i];
+      st.args.push_back(a);
+      (k.ptr_written[i] ? st.out : st.in).push_back(k.ptr_slots[i]);
+    }
+    p.steps.push_back(st);
+    p.kernel_names.push_back(k.name);
+    kernels.push_back(std::move(k));
+  }
+
+  // ----------------------------------------------------------- ordering --
+  std::vector<int> topo() {
+    std::vector<int> order, state(g.nodes.size(), 0);
+    std::function<void(int)> visit = [&](int n) {
+      if (state[n] == 2) return;
+      if (state[n] == 1) throw PjrtErr(13, "cycle in graph");
+      state[n] = 1;
+      for (auto& o : g.nodes[n].operands) visit(o.node);
+      state[n] = 2;
+      order.push_back(n);
+    };
+    for (auto& o : g.outputs) visit(o.node);
+    return order;
+  }
+
+  bool must_materialize(int n) {
+    const Node& nd = g.nodes[n];
+    if (nd.op == Op::Parameter) return true;
+    if (nd.op == Op::Constant && !nd.cdata.splat && nd.results[0].numel() > 1) return true;
+    if (!is_fusible(nd.op)) return true;
+    if (u.output_refs[n]) return true;
+    for (int c : u.users[n])
+      if (!reads_expressions(g.nodes[c].op)) {
+        // convolution reads its lhs through the im2col expression
+        if (g.nodes[c].op == Op::Convolution && g.nodes[c].operands[0].node == n &&
+            g.nodes[c].operands[1].node != n)
+          continue;
+        return true;
+      }
+    if (u.count(n) <= 1) return false;
+    return !is_cheap(nd);
+  }
+
+  // ---------------------------------------------------------------- GEMM --
+  struct Group {
+    int64_t size = 1, stride = 0;
+    bool ok = true;
+  };
+  static Group group(const TensorType& t, const std::vector<int64_t>& dims) {
+    std::vector<int64_t> st(t.rank(), 1);
+    for (int i = t.rank() - 2; i >= 0; --i) st[i] = st[i + 1] * t.dims[i + 1];
+    Group gr;
+    int64_t prev = -1;
+    for (auto d : dims) {
+      if (t.dims[d] == 1) continue;
+      gr.size *= t.dims[d];
+      if (prev >= 0 && st[prev] != st[d] * t.dims[d]) gr.ok = false;
+      prev = d;
+      gr.stride = st[d];
+    }
+    if (gr.size == 1) gr.stride = 0;
+    return gr;
+  }
+  void emit_gemm(int a, int b, int c, int64_t batch, int64_t M, int64_t N, int64_t K,
+                 Group ab, Group am, Group ak, Group bb, Group bk, Group bn, DType in_dt,
+                 DType out_dt) {
+    Step st;
+    st.kind = StepKind::Gemm;
+    st.name = "gemm";
+    st.in = {a, b};
+    st.out = {c};
+    // strides of size-1 groups do not matter; give them a legal value
+    auto fix = [](Group& x, int64_t other_unit) { if (x.size == 1) x.stride = other_unit ? 0 : 1; };
+    fix(ab, 1); fix(bb, 1);
+    if (am.size == 1) am.stride = ak.stride == 1 ? std::max<int64_t>(K, 1) : 1;
+    if (ak.size == 1) ak.stride = am.stride == 1 ? std::max<int64_t>(M, 1) : 1;
+    if (bn.size == 1) bn.stride = bk.stride == 1 ? std::max<int64_t>(K, 1) : 1;
+    if (bk.size == 1) bk.stride = bn.stride == 1 ? std::max<int64_t>(N, 1) : 1;
+    st.ip = {batch, M, N, K, ab.stride, am.stride, ak.stride, bb.stride, bk.stride, bn.stride, N, 0};
+    st.fp = {1.0f};
+    st.dtype = (int)in_dt;
+    st.dtype2 = (int)out_dt;
+    p.steps.push_back(st);
+  }
+  int permuted_copy(int src, const std::vector<int64_t>& perm, const std::string& what) {
+    const TensorType& t = p.slots[src].type;
+    TensorType o;
+    o.dtype = t.dtype;
+    for (auto d : perm) o.dims.push_back(t.dims[d]);
+    int dst = new_slot(Slot::TEMP, o, what);
+    add_kernel(cg.permute(src, perm, dst));
+    return dst;
+  }
+  void lower_dot(int n) {
+    const Node& nd = g.nodes[n];
+    ValueRef L = nd.operands[0], R = nd.operands[1];
+    int ls = slot.at(L), rs = slot.at(R);
+    TensorType lt = g.type(L), rt = g.type(R);
+    const TensorType& ot = nd.results[0];
+    if (lt.dtype != rt.dtype) throw PjrtErr(12, "dot_general with mixed operand types");
+    if (lt.dtype != DType::F32 && lt.dtype != DType::BF16)
+      throw PjrtErr(12, std::string("dot_general on ") + dtype_name(lt.dtype) + " is not supported");
+    auto free_dims = [](int rank, const std::vector<int64_t>& a, const std::vector<int64_t>& b) {
+      std::vector<int64_t> f;
+      for (int64_t d = 0; d < rank; ++d)
+        if (std::find(a.begin(), a.end(), d) == a.end() && std::find(b.begin(), b.end(), d) == b.end())
+          f.push_back(d);
+      return f;
+    };
+    auto lf = free_dims(lt.rank(), nd.lhs_batch, nd.lhs_contract);
+    auto rf = free_dims(rt.rank(), nd.rhs_batch, nd.rhs_contract);
+    Group ab = group(lt, nd.lhs_batch), am = group(lt, lf), ak = group(lt, nd.lhs_contract);
+    Group bb = group(rt, nd.rhs_batch), bk = group(rt, nd.rhs_contract), bn = group(rt, rf);
+    auto unit_ok = [](const Group& x, const Group& y) {
+      return x.size == 1 || y.size == 1 || x.stride == 1 || y.stride == 1;
+    };
+    if (!(ab.ok && am.ok && ak.ok) || !unit_ok(am, ak)) {
+      std::vector<int64_t> perm = nd.lhs_batch;
+      perm.insert(perm.end(), lf.begin(), lf.end());
+      perm.insert(perm.end(), nd.lhs_contract.begin(), nd.lhs_contract.end());
+      ls = permuted_copy(ls, perm, "dot_lhs_T");
+      lt = p.slots[ls].type;
+      std::vector<int64_t> b(nd.lhs_batch.size()), f(lf.size()), c(nd.lhs_contract.size());
+      int64_t k = 0;
+      for (auto& x : b) x = k++;
+      for (auto& x : f) x = k++;
+      for (auto& x : c) x = k++;
+      ab = group(lt, b); am = group(lt, f); ak = group(lt, c);
+    }
+    if (!(bb.ok && bk.ok && bn.ok) || !unit_ok(bk, bn)) {
+      std::vector<int64_t> perm = nd.rhs_batch;
+      perm.insert(perm.end(), rf.begin(), rf.end());
+      perm.insert(perm.end(), nd.rhs_contract.begin(), nd.rhs_contract.end());
+      rs = permuted_copy(rs, perm, "dot_rhs_T");
+      rt = p.slots[rs].type;
+      std::vector<int64_t> b(nd.rhs_batch.size()), f(rf.size()), c(nd.rhs_contract.size());
+      int64_t k = 0;
+      for (auto& x : b) x = k++;
+      for (auto& x : f) x = k++;
+      for (auto& x : c) x = k++;
+      bb = group(rt, b); bn = group(rt, f); bk = group(rt, c);
+    }
+    if (ab.size != bb.size || ak.size != bk.size) throw PjrtErr(3, "dot_general: shape mismatch");
+    int cs = temp_for(ValueRef{n, 0});
+    emit_gemm(ls, rs, cs, ab.size, am.size, bn.size, ak.size, ab, am, ak, bb, bk, bn, lt.dtype,
+              ot.dtype);
+  }
+
+  void lower_conv(int n) {
+    const Node& nd = g.nodes[n];
+    if (nd.feature_groups != 1 || nd.batch_groups != 1)
+      throw PjrtErr(12, "convolution with feature/batch groups is not supported");
+    const ConvDims& c = nd.conv;
+    const TensorType& lt = g.type(nd.operands[0]);
+    const TensorType& kt = g.type(nd.operands[1]);
+    const TensorType& ot = nd.results[0];
+    if (lt.dtype != DType::F32 && lt.dtype != DType::BF16)
+      throw PjrtErr(12, "convolution dtype not supported");
+    std::vector<int64_t> k_roles, m_roles;
+    for (int d = 0; d < kt.rank(); ++d)
+      if (d != c.k_out) k_roles.push_back(d);
+    for (int d = 0; d < ot.rank(); ++d)
+      if (d != c.out_feature) m_roles.push_back(d);
+    int64_t M = 1, K = 1;
+    for (auto d : m_roles) M *= ot.dims[d];
+    for (auto d : k_roles) K *= kt.dims[d];
+    const int64_t N = kt.dims[c.k_out];
+    TensorType at{lt.dtype, {M, K}};
+    int as = new_slot(Slot::TEMP, at, "im2col");
+    add_kernel(cg.im2col(n, as, k_roles, m_roles, M, K));
+    int ks = slot.at(nd.operands[1]);
+    Group bk, bn;
+    if (c.k_out == kt.rank() - 1) {
+      bk.size = K; bk.stride = N; bn.size = N; bn.stride = 1;
+    } else if (c.k_out == 0) {
+      bk.size = K; bk.stride = 1; bn.size = N; bn.stride = K;
+    } else {
+      std::vector<int64_t> perm = k_roles;
+      perm.push_back(c.k_out);
+      ks = permuted_copy(ks, perm, "conv_kernel_T");
+      bk.size = K; bk.stride = N; bn.size = N; bn.stride = 1;
+    }
+    Group ab, am, ak, bb;
+    am.size = M; am.stride = K; ak.size = K; ak.stride = 1;
+    const bool direct = c.out_feature == ot.rank() - 1;
+    int cs;
+    if (direct) {
+      cs = temp_for(ValueRef{n, 0});
+    } else {
+      cs = new_slot(Slot::TEMP, TensorType{ot.dtype, {M, N}}, "conv_out_MN");
+    }
+    emit_gemm(as, ks, cs, 1, M, N, K, ab, am, ak, bb, bk, bn, lt.dtype, ot.dtype);
+    if (!direct) {
+      // [M..., N] -> output dims: out dim d takes (m_roles position | feature)
+      TensorType mn;
+      mn.dtype = ot.dtype;
+      for (auto d : m_roles) mn.dims.push_back(ot.dims[d]);
+      mn.dims.push_back(N);
+      p.slots[cs].type = mn;
+      std::vector<int64_t> perm(ot.rank());
+      for (int d = 0; d < ot.rank(); ++d) {
+        if (d == c.out_feature) { perm[d] = (int64_t)m_roles.size(); continue; }
+        perm[d] = std::find(m_roles.begin(), m_roles.end(), d) - m_roles.begin();
+      }
+      int os = temp_for(ValueRef{n, 0});
+      add_kernel(cg.permute(cs, perm, os));
+    }
+  }
+
+  // ------------------------------------------------------------ fused ops --
+  void lower_sdpa_custom(int n, const Node& nd) {
+    // custom_call @mlx_sdpa(Q, K, V), layout (B, T, N, H), backend_config {"scale": s}
+    const TensorType& qt = g.type(nd.operands[0]);
+    const TensorType& kt = g.type(nd.operands[1]);
+    if (qt.rank() != 4) throw PjrtErr(3, "mlx_sdpa expects rank-4 (B,T,N,H) operands");
+    float scale = 1.0f / std::sqrt((float)qt.dims[3]);
+    auto pos = nd.backend_config.find("scale");
+    if (pos != std::string::npos) {
+      pos = nd.backend_config.find(':', pos);
+      if (pos != std::string::npos) scale = std::stof(nd.backend_config.substr(pos + 1));
+    }
+    Step st;
+    st.kind = StepKind::Sdpa;
+    st.name = "sdpa";
+    const int64_t B = qt.dims[0], T = qt.dims[1], N = qt.dims[2], D = qt.dims[3], S = kt.dims[1];
+    st.in = {slot.at(nd.operands[0]), slot.at(nd.operands[1]), slot.at(nd.operands[2])};
+    st.out = {temp_for(ValueRef{n, 0})};
+    st.ip = {B, T, S, N, D, T * N * D, N * D, D, S * N * D, N * D, D, S * N * D, N * D, D,
+             T * N * D, N * D, D, 0};
+    st.fp = {scale};
+    st.dtype = (int)qt.dtype;
+    p.steps.push_back(st);
+    p.num_sdpa++;
+  }
+  void lower_fused_sdpa(int n, const Node& nd) {
+    Step st;
+    st.kind = StepKind::Sdpa;
+    st.name = "sdpa";
+    st.in = {slot.at(nd.operands[0]), slot.at(nd.operands[1]), slot.at(nd.operands[2])};
+    st.out = {temp_for(ValueRef{n, 0})};
+    st.ip = nd.dims;  // B T S N D
+    st.ip.insert(st.ip.end(), nd.strides.begin(), nd.strides.end());
+    st.ip.push_back(nd.i_flags & 1);
+    st.fp = {nd.f_scale};
+    st.dtype = (int)g.type(nd.operands[0]).dtype;
+    p.steps.push_back(st);
+    p.num_sdpa++;
+  }
+  void lower_fused_ln(int n, const Node& nd) {
+    Step st;
+    st.kind = StepKind::LayerNorm;
+    st.name = "layer_norm";
+    int k = 0;
+    const int x = slot.at(nd.operands[k++]);
+    const int r = (nd.i_flags & 2) ? slot.at(nd.operands[k++]) : -1;
+    const int ga = (nd.i_flags & 4) ? slot.at(nd.operands[k++]) : -1;
+    const int be = (nd.i_flags & 8) ? slot.at(nd.operands[k++]) : -1;
+    const TensorType& yt = nd.results[0];
+    st.in = {x, r, ga, be};
+    st.out = {temp_for(ValueRef{n, 0}), (nd.i_flags & 16) ? temp_for(ValueRef{n, 1}) : -1};
+    const int64_t cols = yt.dims.back();
+    st.ip = {yt.numel() / cols, cols, nd.i_flags & 1};
+    st.fp = {nd.f_eps};
+    st.dtype = (int)yt.dtype;
+    p.steps.push_back(st);
+    p.num_ln++;
+  }
+  void lower_ln_custom(int n, const Node& nd) {
+    // custom_call @mlx_layer_norm(x, w, b) {"eps": e}: LayerNorm over the last axis
+    float eps = 1e-5f;
+    auto pos = nd.backend_config.find("eps");
+    if (pos != std::string::npos) {
+      pos = nd.backend_config.find(':', pos);
+      if (pos != std::string::npos) eps = std::stof(nd.backend_config.substr(pos + 1));
+    }
+    Step st;
+    st.kind = StepKind::LayerNorm;
+    st.name = "layer_norm";
+    const TensorType& yt = nd.results[0];
+    st.in = {slot.at(nd.operands[0]), -1, nd.operands.size() > 1 ? slot.at(nd.operands[1]) : -1,
+             nd.operands.size() > 2 ? slot.at(nd.operands[2]) : -1};
+    st.out = {temp_for(ValueRef{n, 0}), -1};
+    const int64_t cols = yt.dims.back();
+    st.ip = {yt.numel() / cols, cols, 0};
+    st.fp = {eps};
+    st.dtype = (int)yt.dtype;
+    p.steps.push_back(st);
+    p.num_ln++;
+  }
+
+  void lower_all_reduce(int n, const Node& nd) {
+    const Graph& r = *nd.regions.at(0);
+    const Node& b = r.nodes.at(r.outputs.at(0).node);
+    int op = 0;  // 0 sum, 1 prod, 2 max, 3 min
+    if (b.op == Op::Add) op = 0;
+    else if (b.op == Op::Mul) op = 1;
+    else if (b.op == Op::Max) op = 2;
+    else if (b.op == Op::Min) op = 3;
+    else throw PjrtErr(12, "all_reduce with an unsupported reduction body");
+    for (size_t k = 0; k < nd.operands.size(); ++k) {
+      Step st;
+      st.kind = StepKind::AllReduce;
+      st.name = "all_reduce";
+      st.in = {slot.at(nd.operands[k])};
+      st.out = {temp_for(ValueRef{n, (int)k})};
+      st.ip = {nd.results[k].numel(), op, (int64_t)nd.replica_groups.size(),
+               nd.replica_groups.empty() ? 0 : (int64_t)nd.replica_groups[0].size()};
+      for (auto& grp : nd.replica_groups) st.ip.insert(st.ip.end(), grp.begin(), grp.end());
+      st.dtype = (int)nd.results[k].dtype;
+      p.steps.push_back(st);
+    }
+  }
+
+  // -------------------------------------------------------------- driver --
+  void run() {
+    auto order = topo();
+    // parameters
+    for (size_t i = 0; i < g.nodes.size(); ++i) {
+      const Node& n = g.nodes[i];
+      if (n.op != Op::Parameter || n.dead) continue;
+      int s = new_slot(Slot::PARAM, n.results[0], n.name, (int)n.param_index);
+      slot[ValueRef{(int)i, 0}] = s;
+    }
+    p.param_slots.assign(g.param_types.size(), -1);
+    for (auto& kv : slot) p.param_slots.at(p.slots[kv.second].index) = kv.second;
+    for (size_t i = 0; i < p.param_slots.size(); ++i)
+      if (p.param_slots[i] < 0)
+        p.param_slots[i] = new_slot(Slot::PARAM, g.param_types[i], "%arg" + std::to_string(i), (int)i);
+    p.param_types = g.param_types;
+
+    for (int n : order) {
+      Node& nd = g.nodes[n];
+      if (nd.op == Op::Parameter) continue;
+      if (nd.op == Op::Constant) {
+        if (!nd.cdata.splat && nd.results[0].numel() > 1) {
+          int s = new_slot(Slot::CONST, nd.results[0], nd.name, (int)p.consts.size());
+          p.consts.push_back(nd.cdata);
+          slot[ValueRef{n, 0}] = s;
+          continue;
+        }
+        if (!must_materialize(n)) continue;
+      }
+      if (is_fusible(nd.op)) {
+        if (!must_materialize(n)) continue;
+        int s = temp_for(ValueRef{n, 0});
+        // temporarily hide the slot so the kernel computes the value instead of loading it
+        slot.erase(ValueRef{n, 0});
+        GenKernel k = cg.loop({ValueRef{n, 0}}, {s});
+        slot[ValueRef{n, 0}] = s;
+        add_kernel(std::move(k));
+        continue;
+      }
+      switch (nd.op) {
+        case Op::Reduce: {
+          std::vector<int> outs;
+          for (size_t k = 0; k < nd.results.size(); ++k) outs.push_back(temp_for(ValueRef{n, (int)k}));
+          add_kernel(cg.reduce(n, outs));
+          break;
+        }
+        case Op::ReduceWindow: {
+          std::vector<int> outs;
+          for (size_t k = 0; k < nd.results.size(); ++k) outs.push_back(temp_for(ValueRef{n, (int)k}));
+          add_kernel(cg.reduce_window(n, outs));
+          break;
+        }
+        case Op::SelectAndScatter:
+          add_kernel(cg.select_and_scatter(n, temp_for(ValueRef{n, 0})));
+          break;
+        case Op::Gather:
+          add_kernel(cg.gather(n, temp_for(ValueRef{n, 0})));
+          break;
+        case Op::Scatter: {
+          int out = temp_for(ValueRef{n, 0});
+          auto it = slot.find(nd.operands[0]);
+          if (it != slot.end()) {
+            Step c;
+            c.kind = StepKind::Copy;
+            c.name = "copy";
+            c.in = {it->second};
+            c.out = {out};
+            p.steps.push_back(c);
+          } else {
+            add_kernel(cg.loop({nd.operands[0]}, {out}));
+          }
+          add_kernel(cg.scatter(n, out));
+          break;
+        }
+        case Op::DotGeneral: lower_dot(n); break;
+        case Op::Convolution: lower_conv(n); break;
+        case Op::FusedSdpa: lower_fused_sdpa(n, nd); break;
+        case Op::FusedLayerNorm: lower_fused_ln(n, nd); break;
+        case Op::AllReduce: lower_all_reduce(n, nd); break;
+        case Op::CustomCall:
+          if (nd.target == "mlx_sdpa") { lower_sdpa_custom(n, nd); break; }
+          if (nd.target == "mlx_layer_norm") { lower_ln_custom(n, nd); break; }
+          throw PjrtErr(12, "custom_call @" + nd.target + " is not supported by the B200 plugin");
+        default:
+          throw PjrtErr(12, std::string("op ") + op_name(nd.op) + " is not supported by the B200 plugin");
+      }
+    }
+    // outputs
+    std::set<int> used;
+    for (size_t i = 0; i < g.outputs.size(); ++i) {
+      ValueRef v = g.outputs[i];
+      const TensorType& t = g.type(v);
+      p.output_types.push_back(t);
+      auto it = slot.find(v);
+      if (it == slot.end()) throw PjrtErr(13, "output value was not materialized");
+      int s = it->second;
+      Slot& sl = p.slots[s];
+      if (sl.kind == Slot::TEMP && !used.count(s)) {
+        sl.kind = Slot::OUTPUT;
+        sl.index = (int)i;
+        used.insert(s);
+        p.output_slots.push_back(s);
+      } else {
+        int o = new_slot(Slot::OUTPUT, t, "out" + std::to_string(i), (int)i);
+        Step c;
+        c.kind = StepKind::Copy;
+        c.name = "copy";
+        c.in = {s};
+        c.out = {o};
+        p.steps.push_back(c);
+        p.output_slots.push_back(o);
+      }
+    }
+    // temp lifetimes
+    p.temp_first.assign(p.slots.size(), -1);
+    p.temp_last.assign(p.slots.size(), -1);
+    for (size_t i = 0; i < p.steps.size(); ++i) {
+      for (auto* v : {&p.steps[i].in, &p.steps[i].out})
+        for (int s : *v) {
+          if (s < 0) continue;
+          if (p.temp_first[s] < 0) p.temp_first[s] = (int)i;
+          p.temp_last[s] = (int)i;
+        }
+    }
+    std::ostringstream src;
+    src << CodeGen::prelude();
+    for (auto& k : kernels) src << "\n" << k.code;
+    p.source = src.str();
+  }
+};
+
+}  // namespace
+
+Plan build_plan(const Module& m) {
+  Plan p;
+  p.num_replicas = m.num_replicas;
+  Graph g = inline_calls(m);
+  simplify(g);
+  dce(g);
+  MatchStats ms = match_patterns(g);
+  (void)ms;
+  simplify(g);
+  dce(g);
+  p.graph_dump = dump_graph(g);
+  Builder b(p, g);
+  b.run();
+  return p;
+}
+
+std::string dump_plan(const Plan& p) {
+  std::ostringstream os;
+  os << "slots:\n";
+  for (size_t i = 0; i < p.slots.size(); ++i) {
+    const Slot& s = p.slots[i];
+    static const char* kinds[] = {"param", "output", "temp", "const"};
+    os << "  s" << i << " " << kinds[s.kind] << "[" << s.index << "] " << s.type.str() << " "
+       << s.what << "\n";
+  }
+  os << "steps:\n";
+  for (auto& st : p.steps) {
+    os << "  " << st.name << " in=";
+    for (int s : st.in) os << "s" << s << ",";
+    os << " out=";
+    for (int s : st.out) os << "s" << s << ",";
+    if (!st.ip.empty()) os << " ip=" << join_ints(st.ip);
+    os << "\n";
+  }
+  return os.str();
+}
+
+}  // namespace b200

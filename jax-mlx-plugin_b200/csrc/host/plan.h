@@ -1,0 +1,69 @@
+// Compiled, device-independent program of one executable: memory slots and an
+// ordered list of launch steps.  Built from the IR by plan.cc (fusion planning,
+// GEMM/conv lowering) with NVRTC sources from codegen.cc; run by runtime.cc.
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "ir.h"
+
+namespace b200 {
+
+struct Slot {
+  enum Kind { PARAM, OUTPUT, TEMP, CONST } kind = TEMP;
+  int index = -1;  // parameter / output / constant index
+  TensorType type;
+  int64_t bytes = 0;
+  std::string what;  // producing value, for dumps
+};
+
+struct Arg {
+  enum Kind { PTR, I64, F32 } kind = PTR;
+  int slot = -1;
+  int64_t i = 0;
+  float f = 0.f;
+};
+
+enum class StepKind {
+  Kernel,     // NVRTC-generated kernel: name, grid/block, args
+  LayerNorm,  // b200_ln_residual_fwd
+  Sdpa,       // tcgen05 attention
+  Gemm,       // tcgen05 or SIMT GEMM
+  AllReduce,  // NCCL sum over replicas
+  Copy,       // device-to-device copy of slot bytes
+};
+
+struct Step {
+  StepKind kind = StepKind::Kernel;
+  std::string name;
+  int64_t grid[3] = {1, 1, 1}, block[3] = {1, 1, 1};
+  int smem = 0;
+  std::vector<Arg> args;
+  std::vector<int> in, out;  // slots read / written (liveness; kernel-specific order)
+  std::vector<int64_t> ip;   // integer parameters
+  std::vector<float> fp;     // float parameters
+  int dtype = 0, dtype2 = 0;
+};
+
+struct Plan {
+  std::vector<Slot> slots;
+  std::vector<Step> steps;
+  std::vector<int> param_slots, output_slots;
+  std::vector<ConstData> consts;
+  std::vector<TensorType> param_types, output_types;
+  std::string source;  // NVRTC program (all generated kernels)
+  std::vector<std::string> kernel_names;
+  int64_t num_replicas = 1;
+  std::vector<int> temp_first, temp_last;  // per slot: first/last step touching it
+  std::string graph_dump;
+  int num_sdpa = 0, num_ln = 0;
+};
+
+// Compile a parsed module into a Plan (throws PjrtErr on unsupported input).
+Plan build_plan(const Module& m);
+
+// Human-readable listing of the plan (steps, kernels, slots).
+std::string dump_plan(const Plan& p);
+
+}  // namespace b200

@@ -1,0 +1,302 @@
+// Device runtime implementation.  The CUDA driver is reached through
+// cudaGetDriverEntryPoint and NCCL through dlopen, so the plugin library loads
+// on a machine without a GPU driver (where every device call fails cleanly).
+#include "runtime.h"
+
+#include <dlfcn.h>
+#include <nccl.h>
+#include <nvrtc.h>
+
+#include <cstring>
+#include <functional>
+
+namespace b200 {
+
+void cuda_fail(cudaError_t e, const char* what) {
+  throw PjrtErr(e == cudaErrorMemoryAllocation ? 8 : 13,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------ allocator --
+size_t Allocator::round(size_t b) {
+  if (b == 0) b = 1;
+  if (b < (1u << 20)) return (b + 511) & ~size_t(511);
+  return (b + (2u << 20) - 1) & ~size_t((2u << 20) - 1);
+}
+void* Allocator::alloc(size_t bytes) {
+  const size_t sz = round(bytes);
+  std::lock_guard<std::mutex> lk(mu_);
+  auto it = cache_.find(sz);
+  void* p = nullptr;
+  if (it != cache_.end() && !it->second.empty()) {
+    p = it->second.back();
+    it->second.pop_back();
+  } else {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != ordinal_) cudaSetDevice(ordinal_);
+    cudaError_t e = cudaMalloc(&p, sz);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      // give cached blocks back and retry once
+      for (auto& kv : cache_)
+        for (void* q : kv.second) { cudaFree(q); reserved_ -= (int64_t)kv.first; }
+      cache_.clear();
+      e = cudaMalloc(&p, sz);
+    }
+    if (cur != ordinal_) cudaSetDevice(cur);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw PjrtErr(8, "device " + std::to_string(ordinal_) + ": out of memory allocating " +
+                           std::to_string(sz) + " bytes");
+    }
+    reserved_ += (int64_t)sz;
+  }
+  in_use_ += (int64_t)sz;
+  peak_ = std::max(peak_, in_use_);
+  ++num_allocs_;
+  return p;
+}
+void Allocator::free(void* p, size_t bytes) {
+  if (!p) return;
+  const size_t sz = round(bytes);
+  std::lock_guard<std::mutex> lk(mu_);
+  cache_[sz].push_back(p);
+  in_use_ -= (int64_t)sz;
+}
+void Allocator::release_cache() {
+  std::lock_guard<std::mutex> lk(mu_);
+  for (auto& kv : cache_)
+    for (void* q : kv.second) { cudaFree(q); reserved_ -= (int64_t)kv.first; }
+  cache_.clear();
+}
+Allocator::~Allocator() { release_cache(); }
+
+void Device::activate() const {
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != ordinal) B200_CUDA(cudaSetDevice(ordinal));
+}
+
+DeviceMem::DeviceMem(Device* d, size_t b) : dev(d), bytes(b) { ptr = d->alloc->alloc(b); }
+DeviceMem::~DeviceMem() {
+  if (owned && dev && ptr) dev->alloc->free(ptr, bytes);
+  if (!owned && on_release) on_release(ptr);
+}
+
+// --------------------------------------------------------- driver entry --
+namespace {
+template <typename F>
+F driver_fn(const char* name) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn)
+    throw PjrtErr(13, std::string("CUDA driver entry point not found: ") + name);
+  return reinterpret_cast<F>(fn);
+}
+struct Driver {
+  CUresult (*ModuleLoadData)(CUmodule*, const void*);
+  CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*);
+  CUresult (*ModuleUnload)(CUmodule);
+  CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                           unsigned, CUstream, void**, void**);
+  CUresult (*GetErrorString)(CUresult, const char**);
+  static Driver& get() {
+    static Driver d = [] {
+      Driver x;
+      x.ModuleLoadData = driver_fn<decltype(x.ModuleLoadData)>("cuModuleLoadData");
+      x.ModuleGetFunction = driver_fn<decltype(x.ModuleGetFunction)>("cuModuleGetFunction");
+      x.ModuleUnload = driver_fn<decltype(x.ModuleUnload)>("cuModuleUnload");
+      x.LaunchKernel = driver_fn<decltype(x.LaunchKernel)>("cuLaunchKernel");
+      x.GetErrorString = driver_fn<decltype(x.GetErrorString)>("cuGetErrorString");
+      return x;
+    }();
+    return d;
+  }
+};
+void cu_check(CUresult r, const char* what) {
+  if (r == CUDA_SUCCESS) return;
+  const char* s = "unknown";
+  Driver::get().GetErrorString(r, &s);
+  throw PjrtErr(13, std::string(what) + ": " + s);
+}
+}  // namespace
+
+// ----------------------------------------------------------------- NVRTC --
+std::string nvrtc_compile(const std::string& source, const std::string& name) {
+  static std::mutex mu;
+  static std::map<size_t, std::string> cache;
+  const size_t h = std::hash<std::string>()(source);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(h);
+    if (it != cache.end()) return it->second;
+  }
+  nvrtcProgram prog;
+  if (nvrtcCreateProgram(&prog, source.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) !=
+      NVRTC_SUCCESS)
+    throw PjrtErr(13, "nvrtcCreateProgram failed");
+  const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "-lineinfo",
+                        "--fmad=true", "--diag-suppress=177,550"};
+  nvrtcResult r = nvrtcCompileProgram(prog, 5, opts);
+  if (r != NVRTC_SUCCESS) {
+    size_t n = 0;
+    nvrtcGetProgramLogSize(prog, &n);
+    std::string log(n, '\0');
+    nvrtcGetProgramLog(prog, &log[0]);
+    nvrtcDestroyProgram(&prog);
+    throw PjrtErr(13, "NVRTC compile of generated kernels failed: " + log.substr(0, 4000));
+  }
+  size_t n = 0;
+  nvrtcGetCUBINSize(prog, &n);
+  std::string cubin(n, '\0');
+  nvrtcGetCUBIN(prog, &cubin[0]);
+  nvrtcDestroyProgram(&prog);
+  std::lock_guard<std::mutex> lk(mu);
+  cache[h] = cubin;
+  return cubin;
+}
+
+LoadedModule::~LoadedModule() {
+  if (mod) Driver::get().ModuleUnload(mod);
+}
+
+std::unique_ptr<LoadedModule> load_module(Device& d, const std::string& cubin,
+                                          const std::vector<std::string>& names) {
+  auto m = std::make_unique<LoadedModule>();
+  if (names.empty()) return m;
+  d.activate();
+  cudaFree(nullptr);  // make the primary context current
+  auto& drv = Driver::get();
+  cu_check(drv.ModuleLoadData(&m->mod, cubin.data()), "cuModuleLoadData");
+  for (auto& n : names) {
+    CUfunction f;
+    cu_check(drv.ModuleGetFunction(&f, m->mod, n.c_str()), "cuModuleGetFunction");
+    m->fns[n] = f;
+  }
+  return m;
+}
+
+void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[3], int smem,
+            std::vector<void*>& args) {
+  cu_check(Driver::get().LaunchKernel(f, (unsigned)grid[0], (unsigned)grid[1], (unsigned)grid[2],
+                                      (unsigned)block[0], (unsigned)block[1], (unsigned)block[2],
+                                      (unsigned)smem, (CUstream)d.stream, args.data(), nullptr),
+           "cuLaunchKernel");
+}
+
+// ------------------------------------------------------------------ NCCL --
+struct Nccl {
+  void* h = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommInitAll)(ncclComm_t*, int, const int*) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*GroupStart)() = nullptr;
+  ncclResult_t (*GroupEnd)() = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  std::string why;
+  static Nccl& get() {
+    static Nccl n = [] {
+      Nccl x;
+      const char* env = std::getenv("B200_NCCL_LIBRARY");
+      const char* cands[] = {env, "libnccl.so.2", "/usr/lib/x86_64-linux-gnu/libnccl.so.2"};
+      for (const char* c : cands) {
+        if (!c) continue;
+        x.h = dlopen(c, RTLD_NOW | RTLD_NOLOAD);
+        if (!x.h) x.h = dlopen(c, RTLD_NOW | RTLD_LOCAL);
+        if (x.h) break;
+      }
+      if (!x.h) { x.why = "libnccl.so.2 not found"; return x; }
+      auto sym = [&](const char* s) { return dlsym(x.h, s); };
+      x.GetUniqueId = (decltype(x.GetUniqueId))sym("ncclGetUniqueId");
+      x.CommInitRank = (decltype(x.CommInitRank))sym("ncclCommInitRank");
+      x.CommInitAll = (decltype(x.CommInitAll))sym("ncclCommInitAll");
+      x.CommDestroy = (decltype(x.CommDestroy))sym("ncclCommDestroy");
+      x.AllReduce = (decltype(x.AllReduce))sym("ncclAllReduce");
+      x.GroupStart = (decltype(x.GroupStart))sym("ncclGroupStart");
+      x.GroupEnd = (decltype(x.GroupEnd))sym("ncclGroupEnd");
+      x.GetErrorString = (decltype(x.GetErrorString))sym("ncclGetErrorString");
+      if (!x.AllReduce || !x.CommInitAll || !x.CommInitRank) x.why = "libnccl lacks symbols";
+      return x;
+    }();
+    return n;
+  }
+};
+static void nccl_check(ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return;
+  auto& n = Nccl::get();
+  throw PjrtErr(13, std::string(what) + ": " + (n.GetErrorString ? n.GetErrorString(r) : "error"));
+}
+bool nccl_available(std::string* why) {
+  auto& n = Nccl::get();
+  if (why) *why = n.why;
+  return n.why.empty();
+}
+NcclComms::~NcclComms() {
+  auto& n = Nccl::get();
+  for (void* c : comms)
+    if (c && n.CommDestroy) n.CommDestroy((ncclComm_t)c);
+}
+std::vector<char> nccl_unique_id() {
+  auto& n = Nccl::get();
+  if (!n.why.empty()) throw PjrtErr(9, "NCCL unavailable: " + n.why);
+  ncclUniqueId id;
+  nccl_check(n.GetUniqueId(&id), "ncclGetUniqueId");
+  return std::vector<char>(id.internal, id.internal + sizeof(id.internal));
+}
+std::unique_ptr<NcclComms> nccl_init_all(const std::vector<Device*>& devs) {
+  auto& n = Nccl::get();
+  if (!n.why.empty()) throw PjrtErr(9, "NCCL unavailable: " + n.why);
+  auto c = std::make_unique<NcclComms>();
+  std::vector<int> ords;
+  for (auto* d : devs) ords.push_back(d->ordinal);
+  std::vector<ncclComm_t> cs(devs.size());
+  nccl_check(n.CommInitAll(cs.data(), (int)devs.size(), ords.data()), "ncclCommInitAll");
+  for (auto x : cs) c->comms.push_back(x);
+  return c;
+}
+std::unique_ptr<NcclComms> nccl_init_rank(Device* dev, int nranks, int rank,
+                                          const std::vector<char>& uid) {
+  auto& n = Nccl::get();
+  if (!n.why.empty()) throw PjrtErr(9, "NCCL unavailable: " + n.why);
+  ncclUniqueId id;
+  if (uid.size() != sizeof(id.internal)) throw PjrtErr(3, "bad NCCL unique id size");
+  std::memcpy(id.internal, uid.data(), uid.size());
+  dev->activate();
+  ncclComm_t comm;
+  nccl_check(n.CommInitRank(&comm, nranks, id, rank), "ncclCommInitRank");
+  auto c = std::make_unique<NcclComms>();
+  c->comms.push_back(comm);
+  return c;
+}
+void nccl_all_reduce(const std::vector<Device*>& devs, NcclComms& c,
+                     const std::vector<const void*>& in, const std::vector<void*>& out,
+                     int64_t count, DType dt, int op) {
+  auto& n = Nccl::get();
+  ncclDataType_t t;
+  switch (dt) {
+    case DType::F32: t = ncclFloat32; break;
+    case DType::BF16: t = ncclBfloat16; break;
+    case DType::F64: t = ncclFloat64; break;
+    case DType::S32: t = ncclInt32; break;
+    case DType::U32: t = ncclUint32; break;
+    case DType::S64: t = ncclInt64; break;
+    case DType::U64: t = ncclUint64; break;
+    default: throw PjrtErr(12, "all_reduce element type not supported by NCCL");
+  }
+  const ncclRedOp_t ops[] = {ncclSum, ncclProd, ncclMax, ncclMin};
+  nccl_check(n.GroupStart(), "ncclGroupStart");
+  for (size_t i = 0; i < devs.size(); ++i) {
+    devs[i]->activate();
+    nccl_check(n.AllReduce(in[i], out[i], (size_t)count, t, ops[op], (ncclComm_t)c.comms.at(i),
+                           devs[i]->stream),
+               "ncclAllReduce");
+  }
+  nccl_check(n.GroupEnd(), "ncclGroupEnd");
+}
+
+}  // namespace b200

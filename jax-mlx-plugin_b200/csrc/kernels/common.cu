@@ -1,0 +1,84 @@
+// Error state and version of the kernel library.
+#include "common.cuh"
+
+namespace b200 {
+namespace {
+thread_local std::string g_last_error;
+}
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+}  // namespace b200
+
+extern "C" const char* b200_last_error(void) { return b200::g_last_error.c_str(); }
+extern "C" const char* b200_kernels_version(void) { return "b200-kernels 0.1.0 sm_100a"; }
+
+// ------------------------------------------------------------ TMA + errors --
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tc.cuh"
+
+namespace b200 {
+
+int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+              const uint64_t* strides_bytes, const uint32_t* box, int elem_bytes) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }();
+  if (!encode) return set_error(B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((uintptr_t)base % 16) return set_error(B200_ERR_INVALID, "TMA base address not 16-byte aligned");
+  cuuint64_t gdim[5];
+  cuuint64_t gstr[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i > 0) {
+      if (strides_bytes[i - 1] % 16) return set_error(B200_ERR_INVALID, "TMA stride not a multiple of 16 bytes");
+      gstr[i - 1] = strides_bytes[i - 1];
+    }
+  }
+  const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = encode(map, dt, (cuuint32_t)rank, const_cast<void*>(base), gdim, gstr, bx, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(B200_ERR_INVALID, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return B200_OK;
+}
+
+int* device_error_word() {
+  static std::mutex mu;
+  static int* words[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!words[dev]) {
+    if (cudaMalloc(&words[dev], sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(words[dev], 0, sizeof(int));
+    cudaDeviceSynchronize();
+  }
+  return words[dev];
+}
+
+}  // namespace b200
+
+extern "C" int b200_device_error(int clear) {
+  int* w = b200::device_error_word();
+  if (!w) return -1;
+  int v = 0;
+  if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+  if (clear && v) cudaMemset(w, 0, sizeof(int));
+  return v;
+}

@@ -1,0 +1,413 @@
+// Scaled dot-product attention forward (flash-style, causal or not) on sm_100a.
+//
+// One CTA = 128 query rows of one (batch, head); 4 warps, one query row per
+// thread.  Per key block of 128: thread 0 issues S = Q K^T (tcgen05.mma,
+// kind::tf32 for f32 inputs, kind::f16 for bf16) into TMEM; every thread reads
+// its row of S (tcgen05.ld), applies scale and the causal mask, updates the
+// running max / sum in f32 and writes P to shared memory in the UMMA operand
+// layout (128-byte swizzle); thread 0 issues O_blk = P V into TMEM; threads
+// rescale-and-add O_blk into their f32 register accumulator.  K and V tiles
+// are double-buffered TMA loads issued one block ahead.  The [T, S] score
+// matrix never touches HBM.  Causal CTAs skip key blocks above the diagonal
+// and are launched heaviest first.
+//
+// Math: reference src/jax_mlx/sdpa.py:19-31 (softmax(QK^T*scale)V, BTNH
+// layout) plus the causal mask JAX applies (keys s > t excluded); replaces
+// mlx::fast::scaled_dot_product_attention (src/jax_mlx_pjrt.cpp:4440-4446,
+// :8111-8150).
+#include <cfloat>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace b200 {
+namespace {
+
+struct SdpaArgs {
+  int B, T, S, N;
+  float scale;
+  int causal;
+  void* o;
+  int64_t o_sb, o_st, o_sn;
+  int* err;
+};
+
+template <int ES>
+struct SdpaCfg {
+  static constexpr int E = 128 / ES;               // elements per 128-byte row
+  static constexpr int DCH = 64 / E;               // 128-byte chunks per head-dim row
+  static constexpr int Q_BYTES = 128 * 64 * ES;    // 128 rows x 64 dims
+  static constexpr int KV_BYTES = 128 * 64 * ES;   // 128 keys x 64 dims
+  static constexpr int P_BYTES = 128 * 128 * ES;   // 128 rows x 128 keys
+  static constexpr int SMEM = Q_BYTES + 4 * KV_BYTES + P_BYTES + 1024 + 256;
+};
+
+template <int ES>
+__global__ void __launch_bounds__(128, 1)
+    sdpa_fwd_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
+                const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
+  using C = SdpaCfg<ES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + C::Q_BYTES;          // 2 buffers
+  uint8_t* sV = sK + 2 * C::KV_BYTES;     // 2 buffers
+  uint8_t* sP = sV + 2 * C::KV_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);
+  uint64_t* bar_q = bars;
+  uint64_t* bar_k = bars + 1;  // [2]
+  uint64_t* bar_v = bars + 3;  // [2]
+  uint64_t* bar_s = bars + 5;
+  uint64_t* bar_o = bars + 6;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nq = (p.T + 127) / 128;
+  const int qt = p.causal ? nq - 1 - (int)blockIdx.x : (int)blockIdx.x;
+  const int n = blockIdx.y, b = blockIdx.z;
+  const int t0 = qt * 128;
+  const int nkb_all = (p.S + 127) / 128;
+  const int nkb = p.causal ? min(nkb_all, (t0 + 127) / 128 + 1) : nkb_all;
+
+  if (tid == 0) {
+    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], 1);
+    *abort = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tQ);
+    tma_prefetch_desc(&tK);
+    tma_prefetch_desc(&tV);
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+  auto load_kv = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int kb) {
+    mbar_expect_tx(bar, C::KV_BYTES);
+#pragma unroll
+    for (int c = 0; c < C::DCH; ++c) tma_load_4d(dst + c * (128 * 128), map, bar, c * C::E, n, kb * 128, b);
+  };
+  if (tid == 0 && nkb > 0) {
+    mbar_expect_tx(bar_q, C::Q_BYTES);
+#pragma unroll
+    for (int c = 0; c < C::DCH; ++c) tma_load_4d(sQ + c * (128 * 128), &tQ, bar_q, c * C::E, n, t0, b);
+    load_kv(sK, &tK, &bar_k[0], 0);
+    load_kv(sV, &tV, &bar_v[0], 0);
+    if (nkb > 1) {
+      load_kv(sK + C::KV_BYTES, &tK, &bar_k[1], 1);
+      load_kv(sV + C::KV_BYTES, &tV, &bar_v[1], 1);
+    }
+  }
+
+  constexpr uint32_t fmt = ES == 4 ? 2u : 1u;
+  constexpr uint32_t idesc_s = umma_idesc(fmt, 0, 0, 128, 128);
+  constexpr uint32_t idesc_o = umma_idesc(fmt, 0, 1, 64, 128);
+  const int row = warp * 32 + lane;
+  const int t = t0 + row;
+  float o[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) o[i] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = true;
+
+  for (int j = 0; j < nkb && ok; ++j) {
+    const int buf = j & 1;
+    if (tid == 0) {
+      bool w = true;
+      if (j == 0) w = mbar_wait(bar_q, 0, abort, p.err, 201);
+      w = w && mbar_wait(&bar_k[buf], (j >> 1) & 1, abort, p.err, 202);
+      if (w) {
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + buf * C::KV_BYTES);
+        constexpr int KSTEPS = 64 / (32 / ES);  // head-dim MMA steps (8 tf32, 4 bf16)
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+          const uint32_t off = (kk / 4) * (128 * 128) + (kk % 4) * 32;
+          const uint64_t ad = umma_desc(q0 + off, 16, 1024), bd = umma_desc(k0 + off, 16, 1024);
+          if (ES == 4) umma_tf32(tS, ad, bd, idesc_s, kk != 0);
+          else umma_f16(tS, ad, bd, idesc_s, kk != 0);
+        }
+        umma_commit(bar_s);
+      }
+    }
+    ok = mbar_wait(bar_s, j & 1, abort, p.err, 203);
+    ok = __syncthreads_and(ok) != 0;  // block-uniform: no thread may skip a later barrier
+    if (!ok) break;
+    tc_fence_after();
+    // ---- pass 1: row max of this block
+    const int kbase = j * 128;
+    float bmax = -INFINITY;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(tS + lane_base + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int key = kbase + c * 32 + i;
+        const bool valid = key < p.S && !(p.causal && key > t);
+        if (valid) bmax = fmaxf(bmax, v[i] * p.scale);
+      }
+    }
+    const float m_new = fmaxf(m_run, bmax);
+    const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+    // ---- pass 2: P = exp(s*scale - m_new) into shared memory (swizzled K-major)
+    float lsum = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(tS + lane_base + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int key = kbase + c * 32 + i;
+        const bool valid = key < p.S && !(p.causal && key > t);
+        const float e = valid ? expf(v[i] * p.scale - m_new) : 0.f;
+        v[i] = e;
+        lsum += e;
+      }
+      if (ES == 4) {
+        // 32 f32 keys = one 128-byte chunk row; 8 units of 4 floats
+        uint8_t* prow = sP + c * (128 * 128) + row * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          float4 w4 = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+          *reinterpret_cast<float4*>(prow + ((u ^ (row & 7)) * 16)) = w4;
+        }
+      } else {
+        // 32 bf16 keys = half a 128-byte chunk row; 4 units of 8 bf16
+        uint8_t* prow = sP + (c / 2) * (128 * 128) + row * 128;
+#pragma unroll
+        for (int u4 = 0; u4 < 4; ++u4) {
+          const int u = (c & 1) * 4 + u4;
+          uint32_t w[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            __nv_bfloat162 pr = __floats2bfloat162_rn(v[8 * u4 + 2 * h], v[8 * u4 + 2 * h + 1]);
+            w[h] = *reinterpret_cast<uint32_t*>(&pr);
+          }
+          *reinterpret_cast<uint4*>(prow + ((u ^ (row & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+    l_run = l_run * alpha + lsum;
+    m_run = m_new;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      if (mbar_wait(&bar_v[buf], (j >> 1) & 1, abort, p.err, 204)) {
+        const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sV + buf * C::KV_BYTES);
+        constexpr int KSTEPS = 128 / (32 / ES);  // key MMA steps (16 tf32, 8 bf16)
+        constexpr uint32_t VSTEP = (32 / ES) * 128;
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+          const uint64_t ad = umma_desc(p0 + (kk / 4) * (128 * 128) + (kk % 4) * 32, 16, 1024);
+          const uint64_t bd = umma_desc(v0 + kk * VSTEP, 128 * 128, 1024);
+          if (ES == 4) umma_tf32(tO, ad, bd, idesc_o, kk != 0);
+          else umma_f16(tO, ad, bd, idesc_o, kk != 0);
+        }
+        umma_commit(bar_o);
+      }
+      // K buffer `buf` is free (S of block j finished): prefetch block j+2
+      if (j + 2 < nkb) load_kv(sK + buf * C::KV_BYTES, &tK, &bar_k[buf], j + 2);
+    }
+    ok = mbar_wait(bar_o, j & 1, abort, p.err, 205);
+    ok = __syncthreads_and(ok) != 0;  // block-uniform: no thread may skip a later barrier
+    if (!ok) break;
+    tc_fence_after();
+    if (tid == 0 && j + 2 < nkb) load_kv(sV + buf * C::KV_BYTES, &tV, &bar_v[buf], j + 2);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float v[32];
+      tmem_ld32(tO + lane_base + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha + v[i];
+    }
+    // the next block's P writes must not overtake this block's TMEM/smem reads
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+
+  if (ok && t < p.T) {
+    const float inv = 1.f / l_run;
+    const int64_t off = (int64_t)b * p.o_sb + (int64_t)t * p.o_st + (int64_t)n * p.o_sn;
+    if (ES == 4) {
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + off);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.o) + off);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          __nv_bfloat162 pr = __floats2bfloat162_rn(o[8 * i + 2 * h] * inv, o[8 * i + 2 * h + 1] * inv);
+          w[h] = *reinterpret_cast<uint32_t*>(&pr);
+        }
+        dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && tid == 0) {
+    const uint64_t t1 = globaltimer();
+    while (globaltimer() - t1 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// SIMT fallback for shapes the tensor-core kernel does not take (head dim !=
+// 64, unaligned strides): one block per (query row, head, batch), scores in
+// shared memory, exact f32 arithmetic.
+template <typename T>
+__global__ void __launch_bounds__(128)
+    sdpa_fwd_simt(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                  T* __restrict__ o, int S, int D, const int64_t* __restrict__ st, float scale,
+                  int causal) {
+  extern __shared__ float sc[];  // S scores, then D query values
+  float* qv = sc + S;
+  const int t = blockIdx.x, n = blockIdx.y, b = blockIdx.z;
+  const T* qr = q + b * st[0] + t * st[1] + n * st[2];
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qv[d] = Io<T>::to_f(qr[d]);
+  __syncthreads();
+  const int send = causal ? min(S, t + 1) : S;
+  for (int s = threadIdx.x; s < send; s += blockDim.x) {
+    const T* kr = k + b * st[3] + s * st[4] + n * st[5];
+    float acc = 0.f;
+    for (int d = 0; d < D; ++d) acc = fmaf(qv[d], Io<T>::to_f(kr[d]), acc);
+    sc[s] = acc * scale;
+  }
+  __syncthreads();
+  __shared__ float red[32];
+  float mx = -INFINITY;
+  for (int s = threadIdx.x; s < send; s += blockDim.x) mx = fmaxf(mx, sc[s]);
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = -INFINITY;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, red[i]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int s = threadIdx.x; s < send; s += blockDim.x) {
+    const float e = expf(sc[s] - mx);
+    sc[s] = e;
+    sum += e;
+  }
+  sum = warp_sum(sum);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) sum += red[i];
+  const float inv = 1.f / sum;
+  T* orow = o + b * st[9] + t * st[10] + n * st[11];
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < send; ++s) acc = fmaf(sc[s], Io<T>::to_f(v[b * st[6] + s * st[7] + n * st[8] + d]), acc);
+    orow[d] = Io<T>::from_f(acc * inv);
+  }
+}
+
+template <int ES>
+int launch_tc(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t T,
+              int64_t S, int64_t N, const int64_t* st, float scale, int causal, cudaStream_t s) {
+  using C = SdpaCfg<ES>;
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[4] = {(uint32_t)C::E, 1, 128, 1};
+  {
+    const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)T, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)(st[2] * ES), (uint64_t)(st[1] * ES), (uint64_t)(st[0] * ES)};
+    if (int rc = make_tmap(&tq, q, 4, dims, str, box, ES)) return rc;
+  }
+  {
+    const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)S, (uint64_t)B};
+    const uint64_t sk[3] = {(uint64_t)(st[5] * ES), (uint64_t)(st[4] * ES), (uint64_t)(st[3] * ES)};
+    if (int rc = make_tmap(&tk, k, 4, dims, sk, box, ES)) return rc;
+    const uint64_t sv[3] = {(uint64_t)(st[8] * ES), (uint64_t)(st[7] * ES), (uint64_t)(st[6] * ES)};
+    if (int rc = make_tmap(&tv, v, 4, dims, sv, box, ES)) return rc;
+  }
+  SdpaArgs a;
+  a.B = (int)B;
+  a.T = (int)T;
+  a.S = (int)S;
+  a.N = (int)N;
+  a.scale = scale;
+  a.causal = causal;
+  a.o = o;
+  a.o_sb = st[9];
+  a.o_st = st[10];
+  a.o_sn = st[11];
+  a.err = device_error_word();
+  if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
+  static bool attr = cudaFuncSetAttribute(sdpa_fwd_tc<ES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          C::SMEM) == cudaSuccess;
+  if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(sdpa_fwd_tc) failed");
+  dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
+  sdpa_fwd_tc<ES><<<grid, 128, C::SMEM, s>>>(tq, tk, tv, a);
+  B200_LAUNCH_CHECK();
+  return B200_OK;
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v, void* o,
+                                     int64_t B, int64_t T, int64_t S, int64_t N, int64_t D,
+                                     const int64_t* st, float scale, int causal, int dtype,
+                                     void* stream) {
+  using namespace b200;
+  B200_CHECK_ARG(q && k && v && o && st, "sdpa: null argument");
+  B200_CHECK_ARG(B > 0 && T > 0 && S > 0 && N > 0 && D > 0, "sdpa: bad shape");
+  B200_CHECK_ARG(B < 65536 && N < 65536 && T < (1 << 30) && S < (1 << 30), "sdpa: shape too large");
+  B200_CHECK_ARG(dtype == B200_DT_F32 || dtype == B200_DT_BF16, "sdpa: dtype must be F32 or BF16");
+  auto s = (cudaStream_t)stream;
+  const int es = dtype == B200_DT_F32 ? 4 : 2;
+  bool tc = D == 64;
+  for (int i = 0; i < 12; ++i) tc = tc && ((st[i] * es) % 16 == 0);
+  const void* ptrs[4] = {q, k, v, o};
+  for (int i = 0; i < 4; ++i) tc = tc && ((uintptr_t)ptrs[i] % 16 == 0);
+  if (tc) {
+    if (es == 4) return launch_tc<4>(q, k, v, o, B, T, S, N, st, scale, causal, s);
+    return launch_tc<2>(q, k, v, o, B, T, S, N, st, scale, causal, s);
+  }
+  B200_CHECK_ARG(S <= 8192, "sdpa: the fallback kernel supports S <= 8192");
+  // strides to device memory (small, stream-ordered)
+  int64_t* dst = nullptr;
+  B200_CUDA_TRY(cudaMallocAsync((void**)&dst, 12 * sizeof(int64_t), s));
+  B200_CUDA_TRY(cudaMemcpyAsync(dst, st, 12 * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+  const size_t smem = (size_t)(S + D) * sizeof(float);
+  dim3 grid((unsigned)T, (unsigned)N, (unsigned)B);
+  if (es == 4)
+    sdpa_fwd_simt<float><<<grid, 128, smem, s>>>((const float*)q, (const float*)k, (const float*)v,
+                                                 (float*)o, (int)S, (int)D, dst, scale, causal);
+  else
+    sdpa_fwd_simt<__nv_bfloat16><<<grid, 128, smem, s>>>(
+        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+        (__nv_bfloat16*)o, (int)S, (int)D, dst, scale, causal);
+  B200_LAUNCH_CHECK();
+  B200_CUDA_TRY(cudaFreeAsync(dst, s));
+  return B200_OK;
+}
+
+extern "C" int b200_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B,
+                             int64_t T, int64_t S, int64_t N, int64_t D, float scale, int causal,
+                             int dtype, void* stream) {
+  const int64_t st[12] = {T * N * D, N * D, D, S * N * D, N * D, D,
+                          S * N * D, N * D, D, T * N * D, N * D, D};
+  return b200_sdpa_fwd_strided(q, k, v, o, B, T, S, N, D, st, scale, causal, dtype, stream);
+}

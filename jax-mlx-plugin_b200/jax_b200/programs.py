@@ -1,0 +1,143 @@
+"""The five benchmark programs, as ``jax.jit`` would lower them to StableHLO.
+
+Each builder mirrors the JAX source of its configuration:
+
+* ``sdpa``: ``jax.nn.dot_product_attention(q, k, v, is_causal=True)`` on the
+  XLA path -- einsum logits, ``* scale``, ``jnp.where(tril_mask, logits,
+  -0.7*finfo.max)``, ``jax.nn.softmax`` in f32, einsum with V.
+* ``layer_norm``: ``h = x + r; (h - mean) * rsqrt(var + eps) * gamma + beta``
+  with ``jnp.mean`` / ``jnp.square`` (two-pass variance).
+* ``mlp_step`` / ``cnn_step``: ``jax.value_and_grad`` of softmax cross-entropy,
+  SGD update; with ``num_replicas > 1`` the pmap form whose gradients and loss
+  are ``lax.pmean``-ed (``all_reduce`` + divide).
+"""
+from __future__ import annotations
+
+import math
+from typing import List, Sequence, Tuple
+
+from .hlo import Builder, V
+
+F32_MAX = 3.4028234663852886e38
+
+
+def softmax(b: Builder, x: V, axis: int = -1) -> V:
+    ax = axis % len(x.shape)
+    m = b.stop_gradient(b.max(x, [ax], keepdims=True))
+    e = b.exp(x - m)
+    return e / b.sum(e, [ax], keepdims=True)
+
+
+def log_softmax(b: Builder, x: V, axis: int = -1) -> V:
+    ax = axis % len(x.shape)
+    shifted = x - b.stop_gradient(b.max(x, [ax], keepdims=True))
+    lse = b.log(b.sum(b.exp(shifted), [ax], keepdims=True))
+    return shifted - lse
+
+
+def cross_entropy(b: Builder, logits: V, labels: V) -> V:
+    """mean over the batch of -sum(one_hot(labels) * log_softmax(logits))."""
+    n, c = logits.shape
+    logp = log_softmax(b, logits)
+    classes = b.iota((n, c), 1, labels.dtype)
+    lab = b.broadcast_in_dim(labels, (n, c), [0])
+    onehot = b.convert(b.compare(lab, classes, "EQ"), logits.dtype)
+    per = b.neg(b.sum(onehot * logp, [1]))
+    return b.sum(per, [0]) / float(n)
+
+
+def sdpa(B=8, T=512, N=8, H=64, causal=True, dt="f32") -> str:
+    b = Builder("jit_dot_product_attention")
+    q, k, v = b.param((B, T, N, H), dt), b.param((B, T, N, H), dt), b.param((B, T, N, H), dt)
+    logits = b.dot_general(q, k, ([3], [3]), ([0, 2], [0, 2]))  # [B, N, T, S]
+    logits = logits * (1.0 / math.sqrt(H))
+    if causal:
+        row = b.iota((T, T), 0)
+        col = b.iota((T, T), 1)
+        tri = b.compare(row + b.constant(0, "i32", (T, T)), col, "GE", "SIGNED")
+        ones = b.constant(True, "i1", (T, T))
+        zeros = b.constant(False, "i1", (T, T))
+        mask = b.select(tri, ones, zeros)
+        mask = b.reshape(mask, (1, 1, T, T))
+        big_neg = b.constant(-0.7 * F32_MAX, dt, logits.shape)
+        logits = b.select(b.broadcast_to(mask, logits.shape), logits, big_neg)
+    probs = softmax(b, b.convert(logits, "f32"))
+    probs = b.convert(probs, dt)
+    enc = b.dot_general(probs, v, ([3], [1]), ([0, 1], [0, 2]))  # [B, N, T, H]
+    out = b.transpose(enc, [0, 2, 1, 3])
+    return b.module([out])
+
+
+def layer_norm(rows=4096, cols=1024, eps=1e-5, dt="f32") -> str:
+    b = Builder("jit_residual_layer_norm")
+    x, r = b.param((rows, cols), dt), b.param((rows, cols), dt)
+    gamma, beta = b.param((cols,), dt), b.param((cols,), dt)
+    h = x + r
+    mean = b.sum(h, [1], keepdims=True) / float(cols)
+    d = h - mean
+    var = b.sum(d * d, [1], keepdims=True) / float(cols)
+    y = d * b.rsqrt(var + eps) * gamma + beta
+    return b.module([y])
+
+
+def _dp_mean(b: Builder, xs: List[V], num_replicas: int) -> List[V]:
+    if num_replicas == 1:
+        return xs
+    groups = [list(range(num_replicas))]
+    return [b.all_reduce_sum(x, groups) / float(num_replicas) for x in xs]
+
+
+def mlp_step(batch=1024, dims=(784, 1024, 1024, 1024, 10), lr=1e-2, num_replicas=1, emit="params") -> str:
+    """One SGD step of the 784-1024-1024-1024-10 ReLU MLP.  Inputs: W1,b1,...,W4,b4,
+    x [batch, 784] f32, labels [batch] i32.  Outputs: loss, updated params (or the
+    gradients themselves with emit="grads")."""
+    b = Builder("jit_train_step", num_replicas)
+    params = []
+    for i in range(len(dims) - 1):
+        params.append(b.param((dims[i], dims[i + 1])))
+        params.append(b.param((dims[i + 1],)))
+    x = b.param((batch, dims[0]))
+    labels = b.param((batch,), "i32")
+    h = x
+    nl = len(dims) - 1
+    for i in range(nl):
+        h = b.matmul(h, params[2 * i]) + params[2 * i + 1]
+        if i < nl - 1:
+            h = b.maximum(h, 0.0)
+    loss = cross_entropy(b, h, labels)
+    grads = b.grad(loss, params)
+    both = _dp_mean(b, [loss] + grads, num_replicas)
+    loss, grads = both[0], both[1:]
+    if emit == "grads":
+        return b.module([loss] + grads)
+    new = [p - g * lr for p, g in zip(params, grads)]
+    return b.module([loss] + new)
+
+
+def cnn_step(batch=256, lr=1e-2, num_replicas=1, emit="params") -> str:
+    """conv3x3(32)+ReLU -> maxpool2 -> conv3x3(64)+ReLU -> maxpool2 -> flatten ->
+    Dense 256 ReLU -> Dense 10, softmax CE, SGD.  Inputs: w1,b1,w2,b2,w3,b3,w4,b4,
+    x [batch,28,28,1] f32, labels [batch] i32.  Outputs: loss, updated params."""
+    b = Builder("jit_cnn_train_step", num_replicas)
+    w1, b1 = b.param((3, 3, 1, 32)), b.param((32,))
+    w2, b2 = b.param((3, 3, 32, 64)), b.param((64,))
+    w3, b3 = b.param((7 * 7 * 64, 256)), b.param((256,))
+    w4, b4 = b.param((256, 10)), b.param((10,))
+    params = [w1, b1, w2, b2, w3, b3, w4, b4]
+    x = b.param((batch, 28, 28, 1))
+    labels = b.param((batch,), "i32")
+    h = b.maximum(b.conv(x, w1, padding=((1, 1), (1, 1))) + b1, 0.0)
+    h = b.max_pool(h, (1, 2, 2, 1), (1, 2, 2, 1))
+    h = b.maximum(b.conv(h, w2, padding=((1, 1), (1, 1))) + b2, 0.0)
+    h = b.max_pool(h, (1, 2, 2, 1), (1, 2, 2, 1))
+    h = b.reshape(h, (batch, 7 * 7 * 64))
+    h = b.maximum(b.matmul(h, w3) + b3, 0.0)
+    logits = b.matmul(h, w4) + b4
+    loss = cross_entropy(b, logits, labels)
+    grads = b.grad(loss, params)
+    both = _dp_mean(b, [loss] + grads, num_replicas)
+    loss, grads = both[0], both[1:]
+    if emit == "grads":
+        return b.module([loss] + grads)
+    new = [p - g * lr for p, g in zip(params, grads)]
+    return b.module([loss] + new)

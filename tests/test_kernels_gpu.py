@@ -1,0 +1,237 @@
+"""GPU: the hand-written sm_100a kernels, called through their C ABI
+(include/b200_kernels.h), against the float64 oracle.
+
+Tolerances (written per test): fp32 non-contraction ops 1e-5 relative, with an
+error floor of 1e-5 * rms(reference); contractions 2e-3 relative with a floor of
+2e-3 * rms(reference) (TF32 / bf16 tensor-core inputs); bf16 outputs 1e-2."""
+import numpy as np
+import pytest
+
+from helpers import assert_close
+from jax_b200 import kernels
+from oracle import restate
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def bf16_dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda().to(torch.bfloat16)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.float().cpu().numpy()
+
+
+@pytest.fixture(autouse=True)
+def no_device_error():
+    kernels.device_error(clear=True)
+    yield
+    assert kernels.device_error(clear=True) == 0, "a bounded device-side wait gave up"
+
+
+# ------------------------------------------------------------------ LayerNorm
+@pytest.mark.parametrize("rows,cols", [(4096, 1024), (7, 1000), (33, 128), (5, 4096), (3, 50)])
+def test_ln_residual_f32(rows, cols):
+    rng = np.random.default_rng(rows * 7 + cols)
+    x, r = (rng.standard_normal((rows, cols)).astype(np.float32) for _ in range(2))
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(cols)).astype(np.float32)
+    X, R, G, B = dev(x), dev(r), dev(g), dev(b)
+    Y = torch.empty_like(X)
+    H = torch.empty_like(X)
+    mean = torch.empty(rows, device="cuda")
+    rstd = torch.empty(rows, device="cuda")
+    kernels.ln_residual_fwd(X.data_ptr(), R.data_ptr(), G.data_ptr(), B.data_ptr(), Y.data_ptr(),
+                            H.data_ptr(), mean.data_ptr(), rstd.data_ptr(), rows, cols, 1e-5,
+                            kernels.DT_F32, 0, stream())
+    ref = restate.layer_norm_ref(x, r, g, b)
+    assert_close(host(Y), ref, 1e-5, "ln y", atol_rms=1.0)
+    np.testing.assert_array_equal(host(H), x + r)  # the residual sum is exact in f32
+    h64 = x.astype(np.float64) + r
+    assert_close(host(mean), h64.mean(-1), 1e-5, "mean")
+    assert_close(host(rstd), 1 / np.sqrt(h64.var(-1) + 1e-5), 1e-5, "rstd")
+
+
+def test_ln_no_residual_no_affine_and_rms():
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((64, 512)).astype(np.float32)
+    X = dev(x)
+    Y = torch.empty_like(X)
+    kernels.ln_residual_fwd(X.data_ptr(), 0, 0, 0, Y.data_ptr(), 0, 0, 0, 64, 512, 1e-6,
+                            kernels.DT_F32, 0, stream())
+    assert_close(host(Y), restate.layer_norm_ref(x, None, None, None, 1e-6), 1e-5, "ln")
+    kernels.ln_residual_fwd(X.data_ptr(), 0, 0, 0, Y.data_ptr(), 0, 0, 0, 64, 512, 1e-6,
+                            kernels.DT_F32, 1, stream())
+    xd = x.astype(np.float64)
+    rms_ref = xd / np.sqrt((xd * xd).mean(-1, keepdims=True) + 1e-6)
+    assert_close(host(Y), rms_ref, 1e-5, "rms")
+
+
+def test_ln_bf16():
+    rng = np.random.default_rng(12)
+    rows, cols = 256, 512
+    x, r = (rng.standard_normal((rows, cols)).astype(np.float32) for _ in range(2))
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(cols)).astype(np.float32)
+    X, R, G, B = bf16_dev(x), bf16_dev(r), bf16_dev(g), bf16_dev(b)
+    Y = torch.empty_like(X)
+    kernels.ln_residual_fwd(X.data_ptr(), R.data_ptr(), G.data_ptr(), B.data_ptr(), Y.data_ptr(),
+                            0, 0, 0, rows, cols, 1e-5, kernels.DT_BF16, 0, stream())
+    xr = [host(t) for t in (X, R, G, B)]
+    assert_close(host(Y), restate.layer_norm_ref(*xr), 1e-2, "ln bf16")
+
+
+def test_ln_bwd_f32():
+    rng = np.random.default_rng(13)
+    rows, cols = 100, 256
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    dy = rng.standard_normal((rows, cols)).astype(np.float32)
+    X, Gd, DY = dev(x), dev(g), dev(dy)
+    Y = torch.empty_like(X)
+    mean = torch.empty(rows, device="cuda")
+    rstd = torch.empty(rows, device="cuda")
+    kernels.ln_residual_fwd(X.data_ptr(), 0, Gd.data_ptr(), 0, Y.data_ptr(), 0, mean.data_ptr(),
+                            rstd.data_ptr(), rows, cols, 1e-5, kernels.DT_F32, 0, stream())
+    DX = torch.empty_like(X)
+    dg = torch.empty(cols, device="cuda")
+    db = torch.empty(cols, device="cuda")
+    ws = torch.empty(kernels.ln_bwd_workspace(rows, cols) // 4, device="cuda")
+    kernels.ln_bwd(X.data_ptr(), Gd.data_ptr(), mean.data_ptr(), rstd.data_ptr(), DY.data_ptr(),
+                   DX.data_ptr(), dg.data_ptr(), db.data_ptr(), ws.data_ptr(), rows, cols,
+                   kernels.DT_F32, stream())
+    rdx, rdg, rdb = restate.layer_norm_bwd_ref(x, g, dy)
+    assert_close(host(DX), rdx, 1e-4, "dx")
+    assert_close(host(dg), rdg, 1e-4, "dgamma")
+    assert_close(host(db), rdb, 1e-4, "dbeta")
+
+
+# ----------------------------------------------------------------------- SDPA
+@pytest.mark.parametrize("B,T,N,causal", [(8, 512, 8, True), (8, 512, 8, False), (2, 200, 3, True),
+                                          (1, 128, 1, True), (2, 384, 2, False), (1, 1, 1, True)])
+def test_sdpa_f32(B, T, N, causal):
+    rng = np.random.default_rng(B * 1000 + T + N)
+    q, k, v = (rng.standard_normal((B, T, N, 64)).astype(np.float32) for _ in range(3))
+    Q, K, V = dev(q), dev(k), dev(v)
+    O = torch.empty_like(Q)
+    kernels.sdpa_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), B, T, T, N, 64,
+                     0.125, causal, kernels.DT_F32, stream())
+    assert_close(host(O), restate.sdpa_ref(q, k, v, 0.125, causal), 2e-3, "sdpa f32")
+
+
+def test_sdpa_cross_lengths_non_causal():
+    rng = np.random.default_rng(21)
+    B, T, S, N = 2, 130, 300, 2
+    q = rng.standard_normal((B, T, N, 64)).astype(np.float32)
+    k, v = (rng.standard_normal((B, S, N, 64)).astype(np.float32) for _ in range(2))
+    Q, K, V = dev(q), dev(k), dev(v)
+    O = torch.empty_like(Q)
+    kernels.sdpa_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), B, T, S, N, 64,
+                     0.125, False, kernels.DT_F32, stream())
+    assert_close(host(O), restate.sdpa_ref(q, k, v, 0.125, False), 2e-3, "sdpa T!=S")
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_sdpa_bf16(causal):
+    rng = np.random.default_rng(22)
+    B, T, N = 4, 256, 8
+    q, k, v = (rng.standard_normal((B, T, N, 64)).astype(np.float32) for _ in range(3))
+    Q, K, V = bf16_dev(q), bf16_dev(k), bf16_dev(v)
+    O = torch.empty_like(Q)
+    kernels.sdpa_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), B, T, T, N, 64,
+                     0.125, causal, kernels.DT_BF16, stream())
+    ref = restate.sdpa_ref(host(Q), host(K), host(V), 0.125, causal)
+    assert_close(host(O), ref, 2e-2, "sdpa bf16")
+
+
+def test_sdpa_bnth_strides_and_simt_fallback():
+    """BNTH views through the strided entry point, and head dim 32 (SIMT path)."""
+    rng = np.random.default_rng(23)
+    B, N, T = 2, 4, 256
+    qb, kb, vb = (rng.standard_normal((B, N, T, 64)).astype(np.float32) for _ in range(3))
+    Q, K, V = dev(qb), dev(kb), dev(vb)
+    O = torch.empty((B, T, N, 64), device="cuda")
+    st = [N * T * 64, 64, T * 64] * 3 + [T * N * 64, N * 64, 64]
+    kernels.sdpa_fwd_strided(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), B, T, T, N, 64,
+                             st, 0.125, True, kernels.DT_F32, stream())
+    tr = lambda a: np.transpose(a, (0, 2, 1, 3))
+    assert_close(host(O), restate.sdpa_ref(tr(qb), tr(kb), tr(vb), 0.125, True), 2e-3, "bnth")
+    q, k, v = (rng.standard_normal((1, 64, 2, 32)).astype(np.float32) for _ in range(3))
+    Q, K, V = dev(q), dev(k), dev(v)
+    O = torch.empty_like(Q)
+    kernels.sdpa_fwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), 1, 64, 64, 2, 32,
+                     0.2, True, kernels.DT_F32, stream())
+    assert_close(host(O), restate.sdpa_ref(q, k, v, 0.2, True), 1e-5, "simt")
+
+
+# ----------------------------------------------------------------------- GEMM
+def _gemm_case(M, N, K, a_t, b_t, dt, batch=1, epi=0, seed=0):
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((batch, M, K)).astype(np.float32)
+    b = rng.standard_normal((batch, K, N)).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    conv = bf16_dev if dt == kernels.DT_BF16 else dev
+    # physical layouts: a_t -> stored [batch, K, M]; b_t -> stored [batch, N, K]
+    A = conv(np.swapaxes(a, 1, 2).copy() if a_t else a)
+    Bm = conv(np.swapaxes(b, 1, 2).copy() if b_t else b)
+    if dt == kernels.DT_BF16:
+        a = host(A) if not a_t else np.swapaxes(host(A), 1, 2)
+        b = host(Bm) if not b_t else np.swapaxes(host(Bm), 1, 2)
+    sAb, sAm, sAk = M * K, (1 if a_t else K), (M if a_t else 1)
+    sBb, sBk, sBn = K * N, (1 if b_t else N), (K if b_t else 1)
+    out_t = torch.bfloat16 if dt == kernels.DT_BF16 else torch.float32
+    C = torch.empty((batch, M, N), device="cuda", dtype=out_t)
+    BIAS = conv(bias)
+    tc = kernels.gemm_uses_tensor_cores(A.data_ptr(), Bm.data_ptr(), batch, K, sAb, sAm, sAk, sBb,
+                                        sBk, sBn, dt)
+    kernels.gemm(A.data_ptr(), Bm.data_ptr(), C.data_ptr(), BIAS.data_ptr(), batch, M, N, K, sAb, sAm,
+                 sAk, sBb, sBk, sBn, N, 1.0, dt, dt, epi, stream())
+    ref = np.einsum("bmk,bkn->bmn", a.astype(np.float64), b.astype(np.float64))
+    if epi in (1, 2):
+        ref = ref + (host(BIAS) if dt == kernels.DT_BF16 else bias)
+    if epi >= 2:
+        ref = np.maximum(ref, 0)
+    return host(C), ref, tc
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("dt", [kernels.DT_F32, kernels.DT_BF16])
+def test_gemm_layouts(a_t, b_t, dt):
+    got, ref, tc = _gemm_case(300, 264, 200, a_t, b_t, dt, seed=a_t * 2 + b_t)
+    assert tc, "expected the tcgen05 path"
+    assert_close(got, ref, 2e-3 if dt == kernels.DT_F32 else 1e-2, f"gemm a_t={a_t} b_t={b_t}")
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 784), (1024, 1024, 1024), (128, 128, 32), (1, 64, 16),
+                                   (200704, 32, 12)])
+def test_gemm_config_shapes_f32(M, N, K):
+    got, ref, tc = _gemm_case(M, N, K, False, False, kernels.DT_F32, seed=M + N + K)
+    assert tc
+    assert_close(got, ref, 2e-3, f"gemm {M}x{N}x{K}")
+
+
+def test_gemm_batched_and_epilogues():
+    for epi in (1, 2, 3):
+        got, ref, tc = _gemm_case(256, 192, 96, False, True, kernels.DT_F32, batch=3, epi=epi, seed=epi)
+        assert tc
+        assert_close(got, ref, 2e-3, f"epi {epi}")
+
+
+def test_gemm_simt_fallback_for_unaligned_rows():
+    got, ref, tc = _gemm_case(1024, 10, 1024, False, False, kernels.DT_F32, seed=9)
+    assert not tc
+    assert_close(got, ref, 1e-5, "simt N=10")
+    got, ref, tc = _gemm_case(33, 17, 9, True, False, kernels.DT_F32, seed=10)
+    assert not tc
+    assert_close(got, ref, 1e-5, "simt odd")

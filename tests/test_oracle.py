@@ -1,0 +1,99 @@
+"""CPU: pin the oracle (numpy StableHLO interpreter + closed forms) against the
+reference's known-answer cases and against each other.  No GPU, no plugin."""
+import numpy as np
+import pytest
+
+from cases import cases
+from helpers import assert_close
+from jax_b200 import programs
+from oracle import hlo_interp, restate
+
+
+@pytest.mark.parametrize("case", cases(), ids=lambda c: c[0])
+def test_interpreter_matches_golden(case):
+    name, prog, inputs, expected = case
+    got = hlo_interp.run(prog, [inputs])[0][0]
+    np.testing.assert_allclose(got, expected, rtol=1e-6, atol=1e-6, err_msg=name)
+
+
+def test_sdpa_program_matches_closed_form():
+    rng = np.random.default_rng(1)
+    B, T, N, H = 2, 40, 3, 64
+    q, k, v = (rng.standard_normal((B, T, N, H)).astype(np.float32) for _ in range(3))
+    for causal in (True, False):
+        got = hlo_interp.run(programs.sdpa(B, T, N, H, causal=causal), [[q, k, v]])[0][0]
+        np.testing.assert_allclose(got, restate.sdpa_ref(q, k, v, causal=causal), rtol=1e-12, atol=1e-12)
+
+
+def test_layer_norm_program_matches_closed_form():
+    rng = np.random.default_rng(2)
+    x, r = (rng.standard_normal((16, 128)).astype(np.float32) for _ in range(2))
+    g = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(128)).astype(np.float32)
+    got = hlo_interp.run(programs.layer_norm(16, 128), [[x, r, g, b]])[0][0]
+    np.testing.assert_allclose(got, restate.layer_norm_ref(x, r, g, b), rtol=1e-12, atol=1e-12)
+
+
+def _mlp_inputs(rng, dims, batch):
+    params = []
+    for i in range(len(dims) - 1):
+        params.append((rng.standard_normal((dims[i], dims[i + 1])) * 0.3).astype(np.float32))
+        params.append((rng.standard_normal(dims[i + 1]) * 0.1).astype(np.float32))
+    x = rng.random((batch, dims[0])).astype(np.float32)
+    lab = rng.integers(0, dims[-1], batch).astype(np.int32)
+    return params, x, lab
+
+
+def test_mlp_step_program_matches_hand_backprop():
+    rng = np.random.default_rng(3)
+    dims, batch = (20, 16, 16, 5), 8
+    params, x, lab = _mlp_inputs(rng, dims, batch)
+    outs = hlo_interp.run(programs.mlp_step(batch=batch, dims=dims), [params + [x, lab]])[0]
+    loss, new = restate.mlp_step_ref(params, x, lab)
+    assert abs(outs[0] - loss) < 1e-12
+    for a, b in zip(outs[1:], new):
+        np.testing.assert_allclose(a, b, rtol=1e-12, atol=1e-12)
+
+
+def test_data_parallel_program_equals_full_batch():
+    """pmean over 2 replicas of half batches == one replica on the full batch."""
+    rng = np.random.default_rng(4)
+    dims, batch = (20, 16, 16, 5), 8
+    params, x, lab = _mlp_inputs(rng, dims, batch)
+    full = hlo_interp.run(programs.mlp_step(batch=batch, dims=dims), [params + [x, lab]])[0]
+    dp = hlo_interp.run(programs.mlp_step(batch=batch // 2, dims=dims, num_replicas=2),
+                        [params + [x[:4], lab[:4]], params + [x[4:], lab[4:]]])
+    for rep in dp:
+        for a, b in zip(rep, full):
+            np.testing.assert_allclose(a, b, rtol=1e-12, atol=1e-13)
+
+
+def test_cnn_gradients_match_finite_differences():
+    rng = np.random.default_rng(5)
+    shapes = [(3, 3, 1, 32), (32,), (3, 3, 32, 64), (64,), (3136, 256), (256,), (256, 10), (10,)]
+    ps = [(rng.standard_normal(s) * 0.1).astype(np.float64) for s in shapes]
+    x = rng.random((2, 28, 28, 1))
+    lab = np.array([1, 7], dtype=np.int32)
+    prog = programs.cnn_step(batch=2)
+    interp = hlo_interp.Interp(prog)
+    out = interp.run([ps + [x, lab]])[0]
+    lr, eps = 1e-2, 1e-6
+    for pi, idx in [(0, (1, 1, 0, 3)), (2, (0, 2, 5, 7)), (4, (100, 3)), (7, (4,))]:
+        g_prog = (ps[pi][idx] - out[1 + pi][idx]) / lr
+        pp = [p.copy() for p in ps]
+        pp[pi][idx] += eps
+        pm = [p.copy() for p in ps]
+        pm[pi][idx] -= eps
+        fd = (interp.run([pp + [x, lab]])[0][0] - interp.run([pm + [x, lab]])[0][0]) / (2 * eps)
+        assert abs(g_prog - fd) <= 1e-6 + 1e-4 * abs(fd), (pi, idx, g_prog, fd)
+
+
+def test_bf16_rounding_is_round_to_nearest_even():
+    x = np.array([1.0, 1.00390625, 1.005859375, -2.0e-40, 3.0e38], np.float32)
+    r = hlo_interp.bf16_round(x)
+    assert r[0] == 1.0
+    assert r[1] == 1.0                 # halfway, even mantissa stays
+    assert r[2] == np.float32(1.0078125)
+    assert np.isfinite(r[3])
+    bits = hlo_interp.f32_to_bf16_bits(x)
+    np.testing.assert_array_equal(hlo_interp.bf16_bits_to_f32(bits), r)

@@ -1,0 +1,217 @@
+"""GPU: programs through the PJRT C API (what jax.jit does), against the oracle.
+
+Each test compiles StableHLO text with PJRT_Client_Compile, moves inputs with
+PJRT_Client_BufferFromHostBuffer, runs PJRT_LoadedExecutable_Execute and reads
+results back with PJRT_Buffer_ToHostBuffer.  Tolerances: 1e-5 relative for fp32
+non-contraction programs, 2e-3 relative for programs with contractions (TF32
+tensor cores), each with an error floor of the same factor times rms(reference)."""
+import numpy as np
+import pytest
+
+from cases import cases
+from helpers import assert_close
+from jax_b200 import kernels, pjrt, programs
+from oracle import hlo_interp, restate
+
+pytestmark = pytest.mark.gpu
+
+CONTRACTIONS = {"conv_same_ones", "matmul", "dot_general_ones"}
+
+
+@pytest.fixture(scope="module")
+def client():
+    c = pjrt.Client()
+    yield c
+
+
+@pytest.fixture(autouse=True)
+def no_device_error():
+    kernels.device_error(clear=True)
+    yield
+    assert kernels.device_error(clear=True) == 0
+
+
+def run(client, text, inputs, bf16_args=()):
+    exe = client.compile(text)
+    bufs = [client.buffer_from_numpy(a, bf16=i in bf16_args) for i, a in enumerate(inputs)]
+    outs = exe.execute([bufs])[0]
+    return [o.to_numpy() for o in outs]
+
+
+def test_client_surface(client):
+    assert client.platform_name == "b200"
+    assert "b200-pjrt" in client.platform_version
+    assert len(client.addressable_devices) >= 1
+    assert "B200" in client.device_kind(client.addressable_devices[0])
+    assert [client.device_id(d) for d in client.devices] == list(range(len(client.devices)))
+
+
+def test_buffer_round_trip(client):
+    for arr in (np.arange(24, dtype=np.float32).reshape(2, 3, 4), np.arange(10, dtype=np.int32),
+                np.array(3.5, np.float32), np.zeros((0, 4), np.float32)):
+        b = client.buffer_from_numpy(arr)
+        assert b.shape == arr.shape
+        np.testing.assert_array_equal(b.to_numpy(), arr)
+        assert not pjrt.api().call("Buffer_IsOnCpu", buffer=b.handle).is_on_cpu
+
+
+@pytest.mark.parametrize("case", cases(), ids=lambda c: c[0])
+def test_golden_cases_through_plugin(client, case):
+    name, prog, inputs, expected = case
+    got = run(client, prog, inputs)[0]
+    tol = 2e-3 if name in CONTRACTIONS else 1e-5
+    assert_close(got, expected, tol, name)
+
+
+def test_layer_norm_config(client):
+    """x, r [4096,1024] f32 N(0,1); gamma = 1+0.1N, beta = 0.1N; eps 1e-5."""
+    rng = np.random.default_rng(4)
+    x, r = (rng.standard_normal((4096, 1024)).astype(np.float32) for _ in range(2))
+    g = (1 + 0.1 * rng.standard_normal(1024)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(1024)).astype(np.float32)
+    text = programs.layer_norm()
+    assert "fused_layer_norm" in pjrt.inspect(text, 0)
+    y = run(client, text, [x, r, g, b])[0]
+    assert_close(y, restate.layer_norm_ref(x, r, g, b), 1e-5, "residual layer norm")
+
+
+def test_sdpa_config(client):
+    """causal SDPA, Q,K,V [8,512,8,64] f32 N(0,1), scale 1/8."""
+    rng = np.random.default_rng(1)
+    q, k, v = (rng.standard_normal((8, 512, 8, 64)).astype(np.float32) for _ in range(3))
+    text = programs.sdpa()
+    assert "fused_sdpa" in pjrt.inspect(text, 0)
+    o = run(client, text, [q, k, v])[0]
+    assert_close(o, restate.sdpa_ref(q, k, v, 0.125, True), 2e-3, "causal sdpa")
+
+
+def test_sdpa_unfused_fallback_agrees(client):
+    """With the softmax probabilities also returned, the chain is not fused: the
+    GEMM + generated-kernel path must give the same output."""
+    from jax_b200.hlo import Builder
+    rng = np.random.default_rng(2)
+    q, k, v = (rng.standard_normal((2, 128, 2, 64)).astype(np.float32) for _ in range(3))
+    b = Builder()
+    Q, K, Vv = (b.param((2, 128, 2, 64)) for _ in range(3))
+    logits = b.dot_general(Q, K, ([3], [3]), ([0, 2], [0, 2])) * 0.125
+    m = b.max(logits, [3], keepdims=True)
+    e = b.exp(logits - m)
+    p = e / b.sum(e, [3], keepdims=True)
+    o = b.transpose(b.dot_general(p, Vv, ([3], [1]), ([0, 1], [0, 2])), [0, 2, 1, 3])
+    text = b.module([o, p])
+    assert "fused_sdpa" not in pjrt.inspect(text, 0)
+    got_o, got_p = run(client, text, [q, k, v])
+    assert_close(got_o, restate.sdpa_ref(q, k, v, 0.125, False), 2e-3, "unfused sdpa")
+
+
+def _mlp_params(rng, dims):
+    params = []
+    for i in range(len(dims) - 1):
+        lim = np.sqrt(6.0 / (dims[i] + dims[i + 1]))
+        params.append(rng.uniform(-lim, lim, (dims[i], dims[i + 1])).astype(np.float32))
+        params.append(np.zeros(dims[i + 1], np.float32))
+    return params
+
+
+def test_mlp_step_config_gradients(client):
+    """configs[2] at full size: loss and every gradient vs hand backprop (f64)."""
+    rng = np.random.default_rng(8)
+    dims = (784, 1024, 1024, 1024, 10)
+    params = _mlp_params(rng, dims)
+    x = rng.random((1024, 784)).astype(np.float32)
+    lab = rng.integers(0, 10, 1024).astype(np.int32)
+    outs = run(client, programs.mlp_step(emit="grads"), params + [x, lab])
+    loss, new = restate.mlp_step_ref(params, x, lab, lr=1.0)
+    assert_close(outs[0], loss, 2e-3, "loss")
+    for i, (p, g, r) in enumerate(zip(params, outs[1:], new)):
+        assert_close(g, p.astype(np.float64) - r, 2e-3, f"grad {i}")
+
+
+def test_mlp_step_updates_params(client):
+    rng = np.random.default_rng(9)
+    dims = (784, 1024, 1024, 1024, 10)
+    params = _mlp_params(rng, dims)
+    x = rng.random((1024, 784)).astype(np.float32)
+    lab = rng.integers(0, 10, 1024).astype(np.int32)
+    outs = run(client, programs.mlp_step(), params + [x, lab])
+    loss, new = restate.mlp_step_ref(params, x, lab, lr=1e-2)
+    assert_close(outs[0], loss, 2e-3, "loss")
+    for i, (g, r) in enumerate(zip(outs[1:], new)):
+        assert_close(g, r, 2e-3, f"param {i}")
+
+
+def test_cnn_step_matches_interpreter(client):
+    """configs[4] network at batch 4 (the interpreter's select_and_scatter is slow)."""
+    rng = np.random.default_rng(15)
+    shapes = [(3, 3, 1, 32), (32,), (3, 3, 32, 64), (64,), (3136, 256), (256,), (256, 10), (10,)]
+    ps = []
+    for s in shapes:
+        fan_in = int(np.prod(s[:-1])) if len(s) > 1 else 1
+        ps.append((rng.standard_normal(s) * np.sqrt(2.0 / fan_in)).astype(np.float32) if len(s) > 1
+                  else np.zeros(s, np.float32))
+    x = rng.random((4, 28, 28, 1)).astype(np.float32)
+    lab = rng.integers(0, 10, 4).astype(np.int32)
+    text = programs.cnn_step(batch=4, emit="grads")
+    got = run(client, text, ps + [x, lab])
+    ref = hlo_interp.run(text, [ps + [x, lab]])[0]
+    for i, (g, r) in enumerate(zip(got, ref)):
+        assert_close(g, r, 2e-3, f"cnn output {i}")
+
+
+def test_cnn_step_full_batch_runs(client):
+    rng = np.random.default_rng(16)
+    shapes = [(3, 3, 1, 32), (32,), (3, 3, 32, 64), (64,), (3136, 256), (256,), (256, 10), (10,)]
+    ps = [(rng.standard_normal(s) * 0.05).astype(np.float32) for s in shapes]
+    x = rng.random((256, 28, 28, 1)).astype(np.float32)
+    lab = rng.integers(0, 10, 256).astype(np.int32)
+    outs = run(client, programs.cnn_step(), ps + [x, lab])
+    assert np.isfinite(outs[0]) and 1.0 < float(outs[0]) < 5.0
+    assert all(np.isfinite(o).all() for o in outs)
+
+
+def test_wrong_argument_type_is_invalid_argument(client):
+    exe = client.compile(programs.layer_norm(8, 128))
+    bad = [client.buffer_from_numpy(np.zeros((8, 128), np.int32))] * 2 + \
+          [client.buffer_from_numpy(np.zeros(128, np.float32))] * 2
+    with pytest.raises(pjrt.PjrtError) as e:
+        exe.execute([bad])
+    assert e.value.code == 3
+
+
+def test_serialize_deserialize_round_trip(client):
+    rng = np.random.default_rng(3)
+    text = programs.layer_norm(16, 256)
+    exe = client.compile(text)
+    exe2 = client.deserialize(exe.serialize())
+    ins = [rng.standard_normal((16, 256)).astype(np.float32) for _ in range(2)] + \
+          [np.ones(256, np.float32), np.zeros(256, np.float32)]
+    a = exe.execute([[client.buffer_from_numpy(v) for v in ins]])[0][0].to_numpy()
+    b = exe2.execute([[client.buffer_from_numpy(v) for v in ins]])[0][0].to_numpy()
+    np.testing.assert_array_equal(a, b)
+
+
+def test_output_metadata(client):
+    exe = client.compile(programs.mlp_step(batch=64, dims=(32, 16, 10)))
+    assert exe.num_outputs == 5
+    assert exe.output_types == [pjrt.F32] * 5
+    assert exe.output_shapes == [(), (32, 16), (16,), (16, 10), (10,)]
+
+
+def test_data_parallel_two_devices_in_process(client):
+    if len(client.addressable_devices) < 2:
+        pytest.skip("needs 2 GPUs")
+    rng = np.random.default_rng(10)
+    dims = (64, 128, 10)
+    params = _mlp_params(rng, dims)
+    x = rng.random((64, 64)).astype(np.float32)
+    lab = rng.integers(0, 10, 64).astype(np.int32)
+    exe = client.compile(programs.mlp_step(batch=32, dims=dims, num_replicas=2, emit="grads"))
+    args = [[client.buffer_from_numpy(a, device=client.addressable_devices[d]) for a in
+             params + [x[32 * d:32 * (d + 1)], lab[32 * d:32 * (d + 1)]]] for d in range(2)]
+    outs = exe.execute(args)
+    loss, new = restate.mlp_step_ref(params, x, lab, lr=1.0)
+    for d in range(2):
+        got = [o.to_numpy() for o in outs[d]]
+        assert_close(got[0], loss, 2e-3, "dp loss")
+        for p, g, r in zip(params, got[1:], new):
+            assert_close(g, p.astype(np.float64) - r, 2e-3, "dp grad")

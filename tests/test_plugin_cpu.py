@@ -1,0 +1,152 @@
+"""CPU: the C-ABI libraries load and export what include/*.h declares; the PJRT
+table layout matches the header; the compile pipeline (parse -> SDPA/LN match ->
+plan -> NVRTC) works without a device.  No kernel is launched."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from cases import cases
+from jax_b200 import kernels, pjrt, programs
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INC = os.path.join(ROOT, "include")
+
+
+def _declared(header):
+    text = open(os.path.join(INC, header)).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = set(re.findall(r"\b((?:b200|GetPjrt)\w*)\s*\(", text))
+    return {n for n in names if not n.startswith("B200_")}
+
+
+def test_kernel_library_exports_every_declared_symbol():
+    lib = C.CDLL(kernels.KERNELS_LIB)
+    declared = _declared("b200_kernels.h")
+    assert {"b200_ln_residual_fwd", "b200_sdpa_fwd", "b200_gemm"} <= declared
+    missing = [n for n in declared if not hasattr(lib, n)]
+    assert not missing, missing
+    assert lib.b200_kernels_version and kernels.lib().b200_kernels_version().startswith(b"b200-kernels")
+
+
+def test_pjrt_library_exports_every_declared_symbol():
+    lib = C.CDLL(pjrt.PJRT_LIB)
+    declared = _declared("b200_pjrt.h") | _declared("b200_pjrt_inspect.h")
+    assert "GetPjrtApi" in declared
+    missing = [n for n in declared if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_api_table_matches_header():
+    text = open(os.path.join(INC, "b200_pjrt.h")).read()
+    block = text[text.index("#define B200_PJRT_API_SLOTS(X)"):text.index("#define B200_PJRT_SLOT_FIELD")]
+    slots = re.findall(r"X\((\w+)\)", block)
+    assert slots == pjrt.API_SLOTS
+    assert len(slots) == 128
+    api = pjrt.api()
+    assert api.version == (0, 90)
+    assert api.struct_size == 40 + 8 * 128
+    # every slot is filled (unimplemented ones return an error, never NULL)
+    assert all(api._fn[n] is not None for n in pjrt.API_SLOTS)
+
+
+def test_unimplemented_slot_returns_error_not_crash():
+    api = pjrt.api()
+
+    class Args(C.Structure):
+        _fields_ = [("struct_size", C.c_size_t), ("extension_start", C.c_void_p), ("pad", C.c_void_p * 8)]
+    err = api.raw("CopyToDeviceStream_Destroy", Args())
+    with pytest.raises(pjrt.PjrtError) as e:
+        api.check(err)
+    assert e.value.code == 12
+
+
+def test_client_create_without_device_fails_cleanly():
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.Client()
+    assert e.value.code in (13, 14)
+
+
+def test_config_programs_fuse_and_compile():
+    g = pjrt.inspect(programs.sdpa(), 0)
+    assert "fused_sdpa" in g and "causal=1" in g and "scale=0.125" in g
+    assert "dot_general" not in g and "exponential" not in g
+    g = pjrt.inspect(programs.layer_norm(), 0)
+    assert "fused_layer_norm" in g and "flags=14" in g
+    assert pjrt.inspect(programs.layer_norm(), 1).count("layer_norm in=") == 1
+    for text in (programs.mlp_step(), programs.cnn_step(), programs.mlp_step(batch=512, num_replicas=2)):
+        assert pjrt.inspect(text, 3).startswith("ok ")
+    plan = pjrt.inspect(programs.mlp_step(batch=512, num_replicas=2), 1)
+    assert plan.count("all_reduce") == 9
+
+
+def test_non_causal_and_bnth_attention_also_match():
+    g = pjrt.inspect(programs.sdpa(2, 256, 4, 64, causal=False), 0)
+    assert "fused_sdpa" in g and "causal=0" in g
+
+
+def test_external_consumer_blocks_fusion():
+    """An intermediate of the softmax chain that is also a program output must
+    stay materialized: no fused_sdpa (reference src/jax_mlx_pjrt.cpp:1843-1855)."""
+    from jax_b200.hlo import Builder
+    b = Builder()
+    q, k, v = (b.param((1, 128, 2, 64)) for _ in range(3))
+    logits = b.dot_general(q, k, ([3], [3]), ([0, 2], [0, 2])) * 0.125
+    m = b.max(logits, [3], keepdims=True)
+    e = b.exp(logits - m)
+    p = e / b.sum(e, [3], keepdims=True)
+    o = b.dot_general(p, v, ([3], [1]), ([0, 1], [0, 2]))
+    g = pjrt.inspect(b.module([o, p]), 0)
+    assert "fused_sdpa" not in g
+
+
+@pytest.mark.parametrize("case", cases(), ids=lambda c: c[0])
+def test_golden_case_programs_compile(case):
+    assert pjrt.inspect(case[1], 3).startswith("ok")
+
+
+def test_parse_errors_are_invalid_argument():
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.inspect("module { func.func @main(%a: tensor<4xf32>) -> tensor<4xf32> { %0 = stablehlo.add %a, : tensor<4xf32> return %0 : tensor<4xf32> } }", 0)
+    assert e.value.code == 3
+
+
+def test_unsupported_op_is_unimplemented():
+    text = ('module @m { func.func public @main(%arg0: tensor<8xf32>) -> tensor<8xf32> {\n'
+            '  %0 = "stablehlo.sort"(%arg0) <{dimension = 0 : i64}> ({\n'
+            '  ^bb0(%a: tensor<f32>, %b: tensor<f32>):\n'
+            '    %c = stablehlo.compare  LT, %a, %b,  FLOAT : (tensor<f32>, tensor<f32>) -> tensor<i1>\n'
+            '    stablehlo.return %c : tensor<i1>\n  }) : (tensor<8xf32>) -> tensor<8xf32>\n'
+            '  return %0 : tensor<8xf32>\n} }\n')
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.inspect(text, 1)
+    assert e.value.code == 12
+
+
+def test_generic_printing_and_func_call_inlining():
+    text = '''module @jit_f attributes {mhlo.num_partitions = 1 : i32, mhlo.num_replicas = 1 : i32} {
+  func.func public @main(%arg0: tensor<4x8xf32> {mhlo.layout_mode = "default"}) -> (tensor<4x8xf32> {jax.result_info = ""}) {
+    %0 = call @relu(%arg0) : (tensor<4x8xf32>) -> tensor<4x8xf32>
+    %1 = "stablehlo.add"(%0, %0) : (tensor<4x8xf32>, tensor<4x8xf32>) -> tensor<4x8xf32>
+    return %1 : tensor<4x8xf32>
+  }
+  func.func private @relu(%arg0: tensor<4x8xf32>) -> tensor<4x8xf32> {
+    %cst = stablehlo.constant dense<0.000000e+00> : tensor<f32>
+    %0 = stablehlo.broadcast_in_dim %cst, dims = [] : (tensor<f32>) -> tensor<4x8xf32>
+    %1 = stablehlo.maximum %arg0, %0 : tensor<4x8xf32>
+    return %1 : tensor<4x8xf32>
+  }
+}
+'''
+    g = pjrt.inspect(text, 0)
+    assert "call" not in g and "maximum" in g
+    plan = pjrt.inspect(text, 1)
+    assert plan.count("_loop") == 1  # relu and add fuse into one kernel
