@@ -31,6 +31,16 @@ __attribute__((visibility("default"))) void b200_pjrt_free(char* p);
  * caller is ordered with the plugin's work. */
 __attribute__((visibility("default"))) void* b200_pjrt_device_stream(void* device);
 
+/* With B200_TIMING=1 in the environment, every Execute records CUDA events on
+ * the first device's stream around its launch sequence (after host-side
+ * preparation).  This returns how many executions were recorded since the last
+ * call and writes up to `max` of their device times in milliseconds to `ms`
+ * (waiting for them to finish), then forgets them.  The reference's
+ * counterpart is its MLX_TIMING print of ExecuteGraph time
+ * (src/jax_mlx_pjrt.cpp:246-250, :9340-9351). */
+__attribute__((visibility("default"))) int b200_pjrt_execute_times(void* loaded_executable,
+                                                                  double* ms, int max);
+
 #ifdef __cplusplus
 }
 #endif

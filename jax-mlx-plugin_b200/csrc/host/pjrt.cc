@@ -124,6 +124,9 @@ struct Exe {
   std::vector<int> replica_of;                           // per addressable device
   int64_t num_replicas = 1;
   std::vector<PJRT_NamedValue> cost;
+  // B200_TIMING=1: device time of each Execute's launch sequence (device 0)
+  std::mutex timing_mu;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timings;
 };
 
 }  // namespace
@@ -503,6 +506,14 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
     for (size_t s = 0; s < p.slots.size(); ++s)
       if (p.slots[s].kind == Slot::CONST) ptr[d][s] = mod.consts.at(p.slots[s].index)->ptr;
   }
+  static const bool timing = env_flag("B200_TIMING");
+  cudaEvent_t t_start = nullptr, t_stop = nullptr;
+  if (timing) {
+    devs[0]->dev->activate();
+    B200_CUDA(cudaEventCreate(&t_start));
+    B200_CUDA(cudaEventCreate(&t_stop));
+    B200_CUDA(cudaEventRecord(t_start, devs[0]->dev->stream));
+  }
   auto ensure = [&](size_t d, int s) {
     if (s < 0 || ptr[d][s]) return;
     const Slot& sl = p.slots[s];
@@ -598,6 +609,12 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
             owned[d][s].reset();
             ptr[d][s] = nullptr;
           }
+  }
+  if (timing) {
+    devs[0]->dev->activate();
+    B200_CUDA(cudaEventRecord(t_stop, devs[0]->dev->stream));
+    std::lock_guard<std::mutex> lk(e.timing_mu);
+    e.timings.emplace_back(t_start, t_stop);
   }
   for (size_t d = 0; d < nd; ++d) {
     auto ev = record_event(*devs[d]->dev);
@@ -1477,6 +1494,26 @@ __attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, s
   return code;
 }
 __attribute__((visibility("default"))) void b200_pjrt_free(char* p) { std::free(p); }
+
+__attribute__((visibility("default"))) int b200_pjrt_execute_times(void* loaded_executable,
+                                                                  double* ms, int max) {
+  auto* le = static_cast<PJRT_LoadedExecutable*>(loaded_executable);
+  if (!le) return -1;
+  Exe& e = *le->exe;
+  std::lock_guard<std::mutex> lk(e.timing_mu);
+  int n = 0;
+  for (auto& pr : e.timings) {
+    float t = 0.f;
+    cudaEventSynchronize(pr.second);
+    if (cudaEventElapsedTime(&t, pr.first, pr.second) != cudaSuccess) t = -1.f;
+    if (n < max && ms) ms[n] = t;
+    ++n;
+    cudaEventDestroy(pr.first);
+    cudaEventDestroy(pr.second);
+  }
+  e.timings.clear();
+  return n;
+}
 
 __attribute__((visibility("default"))) void* b200_pjrt_device_stream(void* device) {
   auto* d = static_cast<PJRT_Device*>(device);

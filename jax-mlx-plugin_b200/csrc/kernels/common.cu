@@ -24,7 +24,7 @@ extern "C" const char* b200_kernels_version(void) { return "b200-kernels 0.1.0 s
 namespace b200 {
 
 int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-              const uint64_t* strides_bytes, const uint32_t* box, int elem_bytes) {
+              const uint64_t* strides_bytes, const uint32_t* box, int elem_bytes, bool atom32) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -50,7 +50,8 @@ int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
   const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUresult r = encode(map, dt, (cuuint32_t)rank, const_cast<void*>(base), gdim, gstr, bx, es,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(B200_ERR_INVALID, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));

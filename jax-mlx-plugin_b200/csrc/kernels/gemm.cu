@@ -21,7 +21,6 @@
 namespace b200 {
 namespace {
 
-constexpr int kStages = 4;
 
 struct GemmArgs {
   int M, N, K;
@@ -47,21 +46,59 @@ __device__ __forceinline__ float load_bias(const void* b, int n) {
   return Io<TO>::to_f(reinterpret_cast<const TO*>(b)[n]);
 }
 
-template <int BN, int ES, typename TO>
+// Stage count and shared-memory bytes of one gemm_tc configuration.
+template <int BN, int ES, bool SPLIT>
+struct TcCfg {
+  static constexpr int A_BYTES = 128 * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
+  static constexpr int STAGES = (STAGE * 4 <= 200 * 1024) ? 4 : 3;
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+};
+
+// f32 -> tf32 with round-to-nearest (ties away); low 13 mantissa bits cleared.
+__device__ __forceinline__ float to_tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// hi/lo split of a staged f32 tile in place: tile <- tf32(x), lo <- x - tf32(x).
+// Elementwise, so the TMA's swizzled layout carries over to both copies.
+__device__ __forceinline__ void split_tile(uint8_t* tile, uint8_t* lo, int bytes, int tid, int nthr) {
+  for (int off = tid * 16; off < bytes; off += nthr * 16) {
+    float4 v = *reinterpret_cast<float4*>(tile + off);
+    float4 h = make_float4(to_tf32_rna(v.x), to_tf32_rna(v.y), to_tf32_rna(v.z), to_tf32_rna(v.w));
+    *reinterpret_cast<float4*>(tile + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+  }
+}
+
+// SPLIT (f32 operands only): 3xTF32 -- each operand is split into tf32 hi and
+// lo parts in shared memory by warps 2-5 and the MMA warp accumulates
+// A_lo*B_hi + A_hi*B_lo + A_hi*B_hi, which keeps f32-level accuracy (the
+// dropped A_lo*B_lo term is below 2^-20 relative).
+template <int BN, int ES, typename TO, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
             GemmArgs p) {
+  using Cfg = TcCfg<BN, ES, SPLIT>;
+  constexpr int S = Cfg::STAGES;
   constexpr int BK = 128 / ES;  // K elements per 128-byte row
   constexpr int E = 128 / ES;   // MN elements per 128-byte chunk
-  constexpr int A_BYTES = 128 * 128;
-  constexpr int B_BYTES = BN * 128;
+  constexpr int A_BYTES = Cfg::A_BYTES;
+  constexpr int B_BYTES = Cfg::B_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + kStages * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * B_BYTES);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
+  // stage s: [A | B | A_lo | B_lo]
+  auto sA = [&](int s) { return smem + s * Cfg::STAGE; };
+  auto sB = [&](int s) { return smem + s * Cfg::STAGE + A_BYTES; };
+  auto sAlo = [&](int s) { return smem + s * Cfg::STAGE + A_BYTES + B_BYTES; };
+  auto sBlo = [&](int s) { return smem + s * Cfg::STAGE + 2 * A_BYTES + B_BYTES; };
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::STAGE);
+  uint64_t* split = full + S;
+  uint64_t* empty = split + S;
+  uint64_t* tfull = empty + S;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
@@ -70,8 +107,9 @@ __global__ void __launch_bounds__(192, 1)
   const int KB = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&split[s], 4);
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
@@ -92,23 +130,22 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer
       for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % kStages;
-        if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) + 1) & 1, abort, p.err, 101))
-          break;
+        const int s = kb % S;
+        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) + 1) & 1, abort, p.err, 101)) break;
         mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
         if (!p.a_mn) {
-          tma_load_3d(sA + s * A_BYTES, &tA, &full[s], kb * BK, m0, bz);
+          tma_load_3d(sA(s), &tA, &full[s], kb * BK, m0, bz);
         } else {
 #pragma unroll
           for (int i = 0; i < 128 / E; ++i)
-            tma_load_3d(sA + s * A_BYTES + i * (BK * 128), &tA, &full[s], m0 + i * E, kb * BK, bz);
+            tma_load_3d(sA(s) + i * (BK * 128), &tA, &full[s], m0 + i * E, kb * BK, bz);
         }
         if (!p.b_mn) {
-          tma_load_3d(sB + s * B_BYTES, &tB, &full[s], kb * BK, n0, bz);
+          tma_load_3d(sB(s), &tB, &full[s], kb * BK, n0, bz);
         } else {
 #pragma unroll
           for (int i = 0; i < BN / E; ++i)
-            tma_load_3d(sB + s * B_BYTES + i * (BK * 128), &tB, &full[s], n0 + i * E, kb * BK, bz);
+            tma_load_3d(sB(s) + i * (BK * 128), &tB, &full[s], n0 + i * E, kb * BK, bz);
         }
       }
     }
@@ -116,26 +153,59 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {  // ---- MMA issuer
       const uint32_t idesc = umma_idesc(ES == 4 ? 2u : 1u, (uint32_t)p.a_mn, (uint32_t)p.b_mn, BN, 128);
       constexpr uint32_t KSTEP_MN = (32 / ES) * 128;  // bytes per MMA K-step, MN-major
+      constexpr uint32_t MN_LAYOUT = ES == 4 ? kUmmaSW128Base32 : kUmmaSW128;
+      constexpr uint32_t MN_SBO = ES == 4 ? 512 : 1024;
+      // MN-major: LBO = stride between 128-byte MN chunks (one TMA box each),
+      // SBO = stride between K-row groups (8 rows of 128 B; 4 for the tf32 layout)
+      auto adesc = [&](uint32_t base, int kk) {
+        return p.a_mn ? umma_desc(base + kk * KSTEP_MN, BK * 128, MN_SBO, MN_LAYOUT)
+                      : umma_desc(base + kk * 32, 16, 1024);
+      };
+      auto bdesc = [&](uint32_t base, int kk) {
+        return p.b_mn ? umma_desc(base + kk * KSTEP_MN, BK * 128, MN_SBO, MN_LAYOUT)
+                      : umma_desc(base + kk * 32, 16, 1024);
+      };
       bool ok = true;
       for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % kStages;
-        if (!mbar_wait(&full[s], (kb / kStages) & 1, abort, p.err, 102)) { ok = false; break; }
+        const int s = kb % S;
+        const bool w = SPLIT ? mbar_wait(&split[s], (kb / S) & 1, abort, p.err, 102)
+                             : mbar_wait(&full[s], (kb / S) & 1, abort, p.err, 102);
+        if (!w) { ok = false; break; }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+        const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = p.a_mn ? umma_desc(a0 + kk * KSTEP_MN, BK * 128, 1024)
-                                     : umma_desc(a0 + kk * 32, 16, 1024);
-          const uint64_t bd = p.b_mn ? umma_desc(b0 + kk * KSTEP_MN, BK * 128, 1024)
-                                     : umma_desc(b0 + kk * 32, 16, 1024);
-          if (ES == 4) umma_tf32(tmem, ad, bd, idesc, (kb | kk) != 0);
-          else umma_f16(tmem, ad, bd, idesc, (kb | kk) != 0);
+          const uint64_t ad = adesc(a0, kk), bd = bdesc(b0, kk);
+          if (ES == 4) {
+            if (SPLIT) {
+              umma_tf32(tmem, adesc(smem_u32(sAlo(s)), kk), bd, idesc, (kb | kk) != 0);
+              umma_tf32(tmem, ad, bdesc(smem_u32(sBlo(s)), kk), idesc, 1);
+              umma_tf32(tmem, ad, bd, idesc, 1);
+            } else {
+              umma_tf32(tmem, ad, bd, idesc, (kb | kk) != 0);
+            }
+          } else {
+            umma_f16(tmem, ad, bd, idesc, (kb | kk) != 0);
+          }
         }
         umma_commit(&empty[s]);
       }
       if (ok) umma_commit(tfull);
     }
-  } else {  // ---- epilogue: warps 2..5 drain TMEM lanes 32*(warp%4) ...
+  } else {  // ---- warps 2..5: operand split (3xTF32), then the epilogue
+    if (SPLIT) {
+      const int tid = threadIdx.x - 64;
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % S;
+        bool w = mbar_wait(&full[s], (kb / S) & 1, abort, p.err, 104);
+        if (!__all_sync(0xffffffffu, w)) break;
+        split_tile(sA(s), sAlo(s), A_BYTES, tid, 128);
+        split_tile(sB(s), sBlo(s), B_BYTES, tid, 128);
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.mma
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&split[s]);
+      }
+    }
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const int m = m0 + row;
@@ -231,7 +301,7 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-template <int BN, int ES, typename TO>
+template <int BN, int ES, typename TO, bool SPLIT>
 int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
               int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
               int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn,
@@ -240,28 +310,34 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   constexpr int E = 128 / ES;
   CUtensorMap ta, tb;
   int rc;
+  const bool atom32 = ES == 4;  // tf32 MN-major tiles need the 32-byte-unit swizzle
+  // with a single batch the batch stride is never used: give TMA a legal one
+  auto bstride = [&](int64_t s, int64_t outer_stride, int64_t outer_dim) -> uint64_t {
+    const int64_t v = batch == 1 ? outer_stride * outer_dim : s;
+    return (uint64_t)(((v * ES) + 15) / 16 * 16);
+  };
   if (!a_mn) {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
-    uint64_t str[2] = {(uint64_t)(sAm * ES), (uint64_t)(std::max<int64_t>(sAb, 1) * ES)};
+    uint64_t str[2] = {(uint64_t)(sAm * ES), bstride(sAb, sAm, M)};
     uint32_t box[3] = {(uint32_t)BK, 128, 1};
     rc = make_tmap(&ta, a, 3, dims, str, box, ES);
   } else {
     uint64_t dims[3] = {(uint64_t)M, (uint64_t)K, (uint64_t)batch};
-    uint64_t str[2] = {(uint64_t)(sAk * ES), (uint64_t)(std::max<int64_t>(sAb, 1) * ES)};
+    uint64_t str[2] = {(uint64_t)(sAk * ES), bstride(sAb, sAk, K)};
     uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
-    rc = make_tmap(&ta, a, 3, dims, str, box, ES);
+    rc = make_tmap(&ta, a, 3, dims, str, box, ES, atom32);
   }
   if (rc) return rc;
   if (!b_mn) {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)batch};
-    uint64_t str[2] = {(uint64_t)(sBn * ES), (uint64_t)(std::max<int64_t>(sBb, 1) * ES)};
+    uint64_t str[2] = {(uint64_t)(sBn * ES), bstride(sBb, sBn, N)};
     uint32_t box[3] = {(uint32_t)BK, (uint32_t)BN, 1};
     rc = make_tmap(&tb, b, 3, dims, str, box, ES);
   } else {
     uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)batch};
-    uint64_t str[2] = {(uint64_t)(sBk * ES), (uint64_t)(std::max<int64_t>(sBb, 1) * ES)};
+    uint64_t str[2] = {(uint64_t)(sBk * ES), bstride(sBb, sBk, K)};
     uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
-    rc = make_tmap(&tb, b, 3, dims, str, box, ES);
+    rc = make_tmap(&tb, b, 3, dims, str, box, ES, atom32);
   }
   if (rc) return rc;
   GemmArgs p;
@@ -278,14 +354,14 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   p.sCb = M * ldc;
   p.err = device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
-  const int smem = kStages * (128 * 128 + BN * 128) + 1024 + 256;
+  const int smem = TcCfg<BN, ES, SPLIT>::SMEM;
   static bool attr = [&] {
-    return cudaFuncSetAttribute(gemm_tc<BN, ES, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(gemm_tc<BN, ES, TO, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 smem) == cudaSuccess;
   }();
   if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(gemm_tc) failed");
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 127) / 128), (unsigned)batch);
-  gemm_tc<BN, ES, TO><<<grid, 192, smem, st>>>(ta, tb, p);
+  gemm_tc<BN, ES, TO, SPLIT><<<grid, 192, smem, st>>>(ta, tb, p);
   B200_LAUNCH_CHECK();
   return B200_OK;
 }
@@ -300,6 +376,16 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
                                           epi);
   B200_LAUNCH_CHECK();
   return B200_OK;
+}
+
+// f32 matmuls: 3xTF32 (default; f32-level accuracy) or 1xTF32 with
+// B200_F32_MATMUL=tf32 (one MMA per step, ~1e-3 relative error).
+bool f32_matmul_3x() {
+  static bool x3 = [] {
+    const char* v = std::getenv("B200_F32_MATMUL");
+    return !(v && std::strcmp(v, "tf32") == 0);
+  }();
+  return x3;
 }
 
 bool force_simt() {
@@ -343,15 +429,20 @@ extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias
   if (tc) {
     const int64_t tiles128 = ((M + 127) / 128) * ((N + 127) / 128) * batch;
     const bool bn64 = N <= 64 || tiles128 < num_sms();
-#define B200_TC(BN_, ES_, TO_)                                                                      \
-  return launch_tc<BN_, ES_, TO_>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, \
-                                  alpha, epilogue, a_mn, b_mn, st)
+#define B200_TC(BN_, ES_, TO_, SPLIT_)                                                              \
+  return launch_tc<BN_, ES_, TO_, SPLIT_>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, \
+                                          ldc, alpha, epilogue, a_mn, b_mn, st)
     if (es == 4) {
-      if (bn64) { if (obf) B200_TC(64, 4, __nv_bfloat16); else B200_TC(64, 4, float); }
-      if (obf) B200_TC(128, 4, __nv_bfloat16); else B200_TC(128, 4, float);
+      const bool x3 = f32_matmul_3x();
+      if (x3) {
+        if (bn64) { if (obf) B200_TC(64, 4, __nv_bfloat16, true); else B200_TC(64, 4, float, true); }
+        if (obf) B200_TC(128, 4, __nv_bfloat16, true); else B200_TC(128, 4, float, true);
+      }
+      if (bn64) { if (obf) B200_TC(64, 4, __nv_bfloat16, false); else B200_TC(64, 4, float, false); }
+      if (obf) B200_TC(128, 4, __nv_bfloat16, false); else B200_TC(128, 4, float, false);
     } else {
-      if (bn64) { if (obf) B200_TC(64, 2, __nv_bfloat16); else B200_TC(64, 2, float); }
-      if (obf) B200_TC(128, 2, __nv_bfloat16); else B200_TC(128, 2, float);
+      if (bn64) { if (obf) B200_TC(64, 2, __nv_bfloat16, false); else B200_TC(64, 2, float, false); }
+      if (obf) B200_TC(128, 2, __nv_bfloat16, false); else B200_TC(128, 2, float, false);
     }
 #undef B200_TC
   }

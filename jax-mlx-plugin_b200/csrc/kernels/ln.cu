@@ -16,7 +16,9 @@
 namespace b200 {
 namespace {
 
-constexpr int kWarpsPerBlock = 8;
+// 4 rows (warps) per block: 1024 blocks for the 4096-row config, all resident at
+// once (<= 64 registers -> 8 blocks per SM), so no second partial wave.
+constexpr int kWarpsPerBlock = 4;
 
 template <typename T>
 __device__ __forceinline__ void unpack16(const uint4& u, float* f);
@@ -67,7 +69,7 @@ __device__ __forceinline__ void st_stream(void* p, const uint4& v) {
 
 // Register-resident forward: NV 16-byte vectors per lane, cols = 32*NV*E.
 template <typename T, int NV>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, NV <= 8 ? 8 : 4)
     ln_fwd_reg(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ gamma,
                const T* __restrict__ beta, T* __restrict__ y, T* __restrict__ h,
                float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t rows,

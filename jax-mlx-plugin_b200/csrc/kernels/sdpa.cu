@@ -16,6 +16,8 @@
 // mlx::fast::scaled_dot_product_attention (src/jax_mlx_pjrt.cpp:4440-4446,
 // :8111-8150).
 #include <cfloat>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -209,7 +211,10 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
           const uint64_t ad = umma_desc(p0 + (kk / 4) * (128 * 128) + (kk % 4) * 32, 16, 1024);
-          const uint64_t bd = umma_desc(v0 + kk * VSTEP, 128 * 128, 1024);
+          // V is MN-major (head dim contiguous): LBO = stride between 128-byte
+          // head-dim chunks, SBO = stride between key-row groups
+          const uint64_t bd = ES == 4 ? umma_desc(v0 + kk * VSTEP, 128 * 128, 512, kUmmaSW128Base32)
+                                      : umma_desc(v0 + kk * VSTEP, 128 * 128, 1024);
           if (ES == 4) umma_tf32(tO, ad, bd, idesc_o, kk != 0);
           else umma_f16(tO, ad, bd, idesc_o, kk != 0);
         }
@@ -269,6 +274,249 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// f32 inputs, 3xTF32: every operand is split into tf32 hi and lo parts in shared
+// memory and each product is formed as lo*hi + hi*lo + hi*hi, which keeps the
+// scores and the output at f32-level accuracy (plain TF32 truncation leaves
+// ~1e-3 relative error in the logits, which exp() passes on).  Key blocks of 64
+// so that Q, K (double-buffered), V and P with their lo parts fit in 224 KB.
+constexpr int X3_KEYS = 64;
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+__device__ __forceinline__ void split16(uint8_t* tile, uint8_t* lo, int bytes, int tid) {
+  for (int off = tid * 16; off < bytes; off += 128 * 16) {
+    float4 v = *reinterpret_cast<float4*>(tile + off);
+    float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+    *reinterpret_cast<float4*>(tile + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+  }
+}
+
+struct X3Cfg {
+  static constexpr int Q = 128 * 64 * 4;        // 32 KB (two 16 KB head-dim chunks)
+  static constexpr int KV = X3_KEYS * 64 * 4;   // 16 KB (two 8 KB chunks)
+  static constexpr int P = 128 * X3_KEYS * 4;   // 32 KB (two 16 KB key chunks)
+  // Q, Qlo | K0, K0lo, K1, K1lo | V, Vlo | P, Plo
+  static constexpr int SMEM = 2 * Q + 4 * KV + 2 * KV + 2 * P + 1024 + 256;
+};
+
+__global__ void __launch_bounds__(128, 1)
+    sdpa_fwd_tc_x3(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
+                   const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
+  using C = X3Cfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;
+  uint8_t* sQlo = sQ + C::Q;
+  uint8_t* sK = sQlo + C::Q;                // buffer b: sK + b * 2*KV, lo at +KV
+  uint8_t* sV = sK + 4 * C::KV;             // V, then Vlo at +KV
+  uint8_t* sP = sV + 2 * C::KV;             // P, then Plo at +P
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P);
+  uint64_t* bar_q = bars;
+  uint64_t* bar_k = bars + 1;  // [2]
+  uint64_t* bar_v = bars + 3;
+  uint64_t* bar_s = bars + 4;
+  uint64_t* bar_o = bars + 5;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nq = (p.T + 127) / 128;
+  const int qt = p.causal ? nq - 1 - (int)blockIdx.x : (int)blockIdx.x;
+  const int n = blockIdx.y, b = blockIdx.z;
+  const int t0 = qt * 128;
+  const int nkb_all = (p.S + X3_KEYS - 1) / X3_KEYS;
+  const int nkb = p.causal ? min(nkb_all, (t0 + 127) / X3_KEYS + 1) : nkb_all;
+
+  if (tid == 0) {
+    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
+    *abort = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tQ);
+    tma_prefetch_desc(&tK);
+    tma_prefetch_desc(&tV);
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tS = tmem, tO = tmem + 64;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+  auto load_k = [&](int buf, int kb) {
+    uint64_t* bar = &bar_k[buf];
+    mbar_expect_tx(bar, C::KV);
+    for (int c = 0; c < 2; ++c)
+      tma_load_4d(sK + buf * 2 * C::KV + c * (X3_KEYS * 128), &tK, bar, c * 32, n, kb * X3_KEYS, b);
+  };
+  auto load_v = [&](int kb) {
+    mbar_expect_tx(bar_v, C::KV);
+    for (int c = 0; c < 2; ++c)
+      tma_load_4d(sV + c * (X3_KEYS * 128), &tV, bar_v, c * 32, n, kb * X3_KEYS, b);
+  };
+  if (tid == 0 && nkb > 0) {
+    mbar_expect_tx(bar_q, C::Q);
+    for (int c = 0; c < 2; ++c) tma_load_4d(sQ + c * (128 * 128), &tQ, bar_q, c * 32, n, t0, b);
+    load_k(0, 0);
+    if (nkb > 1) load_k(1, 1);
+    load_v(0);
+  }
+  constexpr uint32_t idesc_s = umma_idesc(2, 0, 0, X3_KEYS, 128);
+  constexpr uint32_t idesc_o = umma_idesc(2, 0, 1, 64, 128);
+  const int row = warp * 32 + lane;
+  const int t = t0 + row;
+  float o[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) o[i] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+  bool ok = nkb > 0;
+  if (ok) {
+    ok = mbar_wait(bar_q, 0, abort, p.err, 211);
+    ok = __syncthreads_and(ok) != 0;
+    if (ok) split16(sQ, sQlo, C::Q, tid);
+  }
+
+  for (int j = 0; j < nkb && ok; ++j) {
+    const int buf = j & 1;
+    uint8_t* kh = sK + buf * 2 * C::KV;
+    uint8_t* kl = kh + C::KV;
+    ok = mbar_wait(&bar_k[buf], (j >> 1) & 1, abort, p.err, 212);
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    split16(kh, kl, C::KV, tid);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t qh0 = smem_u32(sQ), ql0 = smem_u32(sQlo), kh0 = smem_u32(kh), kl0 = smem_u32(kl);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {  // head dim: 8 steps of 8
+        const uint32_t qo = (kk / 4) * (128 * 128) + (kk % 4) * 32;
+        const uint32_t ko = (kk / 4) * (X3_KEYS * 128) + (kk % 4) * 32;
+        const uint64_t qh = umma_desc(qh0 + qo, 16, 1024), ql = umma_desc(ql0 + qo, 16, 1024);
+        const uint64_t kdh = umma_desc(kh0 + ko, 16, 1024), kdl = umma_desc(kl0 + ko, 16, 1024);
+        umma_tf32(tS, ql, kdh, idesc_s, kk != 0);
+        umma_tf32(tS, qh, kdl, idesc_s, 1);
+        umma_tf32(tS, qh, kdh, idesc_s, 1);
+      }
+      umma_commit(bar_s);
+    }
+    ok = mbar_wait(bar_s, j & 1, abort, p.err, 213);
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    tc_fence_after();
+    // K buffer `buf` is free again (S of block j finished): prefetch block j+2
+    if (tid == 0 && j + 2 < nkb) load_k(buf, j + 2);
+    const int kbase = j * X3_KEYS;
+    float sv[64];
+    tmem_ld32(tS + lane_base, sv);
+    tmem_ld32(tS + lane_base + 32, sv + 32);
+    float bmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const int key = kbase + i;
+      const bool valid = key < p.S && !(p.causal && key > t);
+      sv[i] = valid ? sv[i] * p.scale : -INFINITY;
+      bmax = fmaxf(bmax, sv[i]);
+    }
+    const float m_new = fmaxf(m_run, bmax);
+    const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+    float lsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float e = sv[i] == -INFINITY ? 0.f : expf(sv[i] - m_new);
+      sv[i] = e;
+      lsum += e;
+    }
+    l_run = l_run * alpha + lsum;
+    m_run = m_new;
+    // P hi/lo into shared memory (K-major over keys, 128-byte swizzle)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint8_t* ph = sP + c * (128 * 128) + row * 128;
+      uint8_t* pl = ph + C::P;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float* e = sv + c * 32 + 4 * u;
+        float4 h = make_float4(tf32_rna(e[0]), tf32_rna(e[1]), tf32_rna(e[2]), tf32_rna(e[3]));
+        const int sw = (u ^ (row & 7)) * 16;
+        *reinterpret_cast<float4*>(ph + sw) = h;
+        *reinterpret_cast<float4*>(pl + sw) = make_float4(e[0] - h.x, e[1] - h.y, e[2] - h.z, e[3] - h.w);
+      }
+    }
+    ok = mbar_wait(bar_v, j & 1, abort, p.err, 214);
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    split16(sV, sV + C::KV, C::KV, tid);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ph0 = smem_u32(sP), pl0 = smem_u32(sP + C::P);
+      const uint32_t vh0 = smem_u32(sV), vl0 = smem_u32(sV + C::KV);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {  // keys: 8 steps of 8
+        const uint32_t po = (kk / 4) * (128 * 128) + (kk % 4) * 32;
+        const uint64_t pdh = umma_desc(ph0 + po, 16, 1024), pdl = umma_desc(pl0 + po, 16, 1024);
+        // V MN-major (head dim contiguous): LBO = 8 KB between 32-dim chunks,
+        // SBO = 512 B between 4-key row groups (tf32 layout)
+        const uint64_t vdh = umma_desc(vh0 + kk * 1024, X3_KEYS * 128, 512, kUmmaSW128Base32);
+        const uint64_t vdl = umma_desc(vl0 + kk * 1024, X3_KEYS * 128, 512, kUmmaSW128Base32);
+        umma_tf32(tO, pdl, vdh, idesc_o, kk != 0);
+        umma_tf32(tO, pdh, vdl, idesc_o, 1);
+        umma_tf32(tO, pdh, vdh, idesc_o, 1);
+      }
+      umma_commit(bar_o);
+    }
+    ok = mbar_wait(bar_o, j & 1, abort, p.err, 215);
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    tc_fence_after();
+    if (tid == 0 && j + 1 < nkb) load_v(j + 1);  // V buffer free: PV of block j finished
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float v[32];
+      tmem_ld32(tO + lane_base + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha + v[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+
+  if (ok && t < p.T) {
+    const float inv = 1.f / l_run;
+    const int64_t off = (int64_t)b * p.o_sb + (int64_t)t * p.o_st + (int64_t)n * p.o_sn;
+    float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + off);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && tid == 0) {
+    const uint64_t t1 = globaltimer();
+    while (globaltimer() - t1 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
   }
 }
 
@@ -339,7 +587,7 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, int64_t B, i
     const uint64_t sk[3] = {(uint64_t)(st[5] * ES), (uint64_t)(st[4] * ES), (uint64_t)(st[3] * ES)};
     if (int rc = make_tmap(&tk, k, 4, dims, sk, box, ES)) return rc;
     const uint64_t sv[3] = {(uint64_t)(st[8] * ES), (uint64_t)(st[7] * ES), (uint64_t)(st[6] * ES)};
-    if (int rc = make_tmap(&tv, v, 4, dims, sv, box, ES)) return rc;
+    if (int rc = make_tmap(&tv, v, 4, dims, sv, box, ES, /*atom32=*/ES == 4)) return rc;
   }
   SdpaArgs a;
   a.B = (int)B;
@@ -363,6 +611,45 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, int64_t B, i
   return B200_OK;
 }
 
+int launch_x3(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t T,
+              int64_t S, int64_t N, const int64_t* st, float scale, int causal, cudaStream_t s) {
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)T, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)(st[2] * 4), (uint64_t)(st[1] * 4), (uint64_t)(st[0] * 4)};
+    const uint32_t box[4] = {32, 1, 128, 1};
+    if (int rc = make_tmap(&tq, q, 4, dims, str, box, 4)) return rc;
+  }
+  {
+    const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)S, (uint64_t)B};
+    const uint32_t box[4] = {32, 1, X3_KEYS, 1};
+    const uint64_t sk[3] = {(uint64_t)(st[5] * 4), (uint64_t)(st[4] * 4), (uint64_t)(st[3] * 4)};
+    if (int rc = make_tmap(&tk, k, 4, dims, sk, box, 4)) return rc;
+    const uint64_t sv[3] = {(uint64_t)(st[8] * 4), (uint64_t)(st[7] * 4), (uint64_t)(st[6] * 4)};
+    if (int rc = make_tmap(&tv, v, 4, dims, sv, box, 4, /*atom32=*/true)) return rc;
+  }
+  SdpaArgs a;
+  a.B = (int)B;
+  a.T = (int)T;
+  a.S = (int)S;
+  a.N = (int)N;
+  a.scale = scale;
+  a.causal = causal;
+  a.o = o;
+  a.o_sb = st[9];
+  a.o_st = st[10];
+  a.o_sn = st[11];
+  a.err = device_error_word();
+  if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
+  static bool attr = cudaFuncSetAttribute(sdpa_fwd_tc_x3, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          X3Cfg::SMEM) == cudaSuccess;
+  if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(sdpa_fwd_tc_x3) failed");
+  dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
+  sdpa_fwd_tc_x3<<<grid, 128, X3Cfg::SMEM, s>>>(tq, tk, tv, a);
+  B200_LAUNCH_CHECK();
+  return B200_OK;
+}
+
 }  // namespace
 }  // namespace b200
 
@@ -382,7 +669,14 @@ extern "C" int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v
   const void* ptrs[4] = {q, k, v, o};
   for (int i = 0; i < 4; ++i) tc = tc && ((uintptr_t)ptrs[i] % 16 == 0);
   if (tc) {
-    if (es == 4) return launch_tc<4>(q, k, v, o, B, T, S, N, st, scale, causal, s);
+    if (es == 4) {
+      static const bool x3 = [] {
+        const char* e = std::getenv("B200_F32_MATMUL");
+        return !(e && std::strcmp(e, "tf32") == 0);
+      }();
+      if (x3) return launch_x3(q, k, v, o, B, T, S, N, st, scale, causal, s);
+      return launch_tc<4>(q, k, v, o, B, T, S, N, st, scale, causal, s);
+    }
     return launch_tc<2>(q, k, v, o, B, T, S, N, st, scale, causal, s);
   }
   B200_CHECK_ARG(S <= 8192, "sdpa: the fallback kernel supports S <= 8192");

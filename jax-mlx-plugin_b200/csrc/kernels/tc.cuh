@@ -154,15 +154,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// UMMA shared-memory layouts (descriptor bits 61-63).
+constexpr uint32_t kUmmaSW128 = 2;        // 128B rows, 16-byte units XOR row%8 (1024 B atoms)
+constexpr uint32_t kUmmaSW128Base32 = 1;  // 128B rows, 32-byte units XOR row%4 (512 B atoms);
+                                          // the only MN-major layout tcgen05 takes for tf32
+
 // UMMA shared-memory matrix descriptor (sm_100): start address, leading and
-// stride byte offsets (16-byte units), version 1, layout (2 = 128B swizzle).
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// stride byte offsets (16-byte units), version 1, layout type.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout = kUmmaSW128) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;
   return d;
 }
 // Instruction descriptor: f32 accumulate, A/B format (0 f16, 1 bf16, 2 tf32),
@@ -177,11 +183,13 @@ __host__ __device__ constexpr uint32_t umma_idesc(uint32_t fmt, uint32_t a_mn, u
 
 // Host helpers (common.cu).
 namespace b200 {
-// Encode a tiled TMA descriptor with 128-byte swizzle and zero fill.  dims and
-// box innermost first; strides in bytes for dims 1..rank-1.  Returns B200_OK or
-// an error code (message in b200_last_error()).
+// Encode a tiled TMA descriptor with zero fill and a 128-byte swizzle: 16-byte
+// units (atom32 = false; matches kUmmaSW128) or 32-byte units (atom32 = true;
+// matches kUmmaSW128Base32).  dims and box innermost first; strides in bytes for
+// dims 1..rank-1.  Returns B200_OK or an error code (b200_last_error()).
 int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-              const uint64_t* strides_bytes, const uint32_t* box, int elem_bytes);
+              const uint64_t* strides_bytes, const uint32_t* box, int elem_bytes,
+              bool atom32 = false);
 // Per-device error word passed to kernels with bounded waits (zeroed once).
 int* device_error_word();
 }

@@ -362,6 +362,14 @@ class Executable:
                 api().raw("Event_Destroy", ARGS["Event_Destroy"](event=e))
         return [[Buffer(self.client, outs[d][o]) for o in range(self.num_outputs)] for d in range(nd)]
 
+    def device_times_ms(self) -> List[float]:
+        """Device time of each Execute since the last call (needs B200_TIMING=1)."""
+        f = api().lib.b200_pjrt_execute_times
+        f.restype, f.argtypes = C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.c_int]
+        buf = (C.c_double * 4096)()
+        n = f(self.handle, buf, 4096)
+        return [buf[i] for i in range(min(n, 4096))]
+
     def serialize(self) -> bytes:
         exe = api().call("LoadedExecutable_GetExecutable", loaded_executable=self.handle).executable
         try:
@@ -510,7 +518,7 @@ class Client:
         return Buffer(self, a.buffer), a.done_with_host_buffer
 
     def buffer_from_numpy(self, x: np.ndarray, device: Optional[int] = None, bf16: bool = False) -> Buffer:
-        x = np.ascontiguousarray(x)
+        x = np.require(x, requirements="C")  # keeps 0-d arrays 0-d
         t = BF16 if bf16 else _NP2PJRT[x.dtype]
         b, ev = self.buffer_from_host_ptr(x.ctypes.data, t, x.shape, device, semantics=0)
         api().await_event(ev)
