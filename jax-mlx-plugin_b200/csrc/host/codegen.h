@@ -22,7 +22,8 @@ struct GenKernel {
   std::vector<int> ptr_slots;  // kernel pointer parameters, in order
   std::vector<bool> ptr_written;
   int64_t grid = 1, block = 256;
-  int64_t grid_y = 1;
+  int64_t grid_y = 1;   // >1: split reduction (blockIdx.y = split index)
+  int64_t block_y = 1;  // >1: 2-D block (32, block_y) of column reductions
 };
 
 class CodeGen {
@@ -32,8 +33,12 @@ class CodeGen {
 
   // out = value at each index of `v`'s shape (loop fusion root).
   GenKernel loop(const std::vector<ValueRef>& roots, const std::vector<int>& out_slots);
-  // Reduce node (variadic) -> out slots (one per result).
-  GenKernel reduce(int node, const std::vector<int>& out_slots);
+  // Reduce node (variadic) -> out slots (one per result).  With split > 1 the
+  // reduced range is divided over gridDim.y blocks and out_slots receive
+  // [split, OUT] partials, combined by reduce_partials.
+  GenKernel reduce(int node, const std::vector<int>& out_slots, int split = 1);
+  GenKernel reduce_partials(int node, const std::vector<int>& partial_slots,
+                            const std::vector<int>& out_slots, int split);
   GenKernel reduce_window(int node, const std::vector<int>& out_slots);
   GenKernel select_and_scatter(int node, int out_slot);
   GenKernel gather(int node, int out_slot);

@@ -96,9 +96,10 @@ struct Builder {
     st.kind = StepKind::Kernel;
     st.name = k.name;
     st.grid[0] = k.grid;
-    if (k.grid_y < 0) {  // reduce: 2-D block (32, RY)
+    st.grid[1] = std::max<int64_t>(k.grid_y, 1);
+    if (k.block_y > 1) {  // column reduction: 2-D block (32, RY)
       st.block[0] = 32;
-      st.block[1] = -k.grid_y;
+      st.block[1] = k.block_y;
     } else {
       st.block[0] = k.block;
     }
@@ -145,6 +146,38 @@ struct Builder {
       }
     if (u.count(n) <= 1) return false;
     return !is_cheap(nd);
+  }
+
+  // Split a reduction over several blocks when its outputs alone would leave
+  // most of the GPU idle (e.g. a bias gradient: 32 outputs, 200k rows each).
+  // Only for init values that are the combiner's identity (0 for add, -inf /
+  // +inf for max / min), which every jnp reduction uses: each block row starts
+  // from the init, so a non-identity init would be counted once per split.
+  int reduce_split(const Node& nd) {
+    const int nin = (int)nd.operands.size() / 2;
+    if (nin != 1) return 1;
+    const Graph& r = *nd.regions.at(0);
+    const Node& body = r.nodes.at(r.outputs.at(0).node);
+    const Node& init = g.nodes[nd.operands[1].node];
+    if (init.op != Op::Constant || !(init.cdata.splat || init.results[0].numel() == 1)) return 1;
+    auto hv = host_eval(g, nd.operands[1]);
+    if (!hv || hv->v.empty()) return 1;
+    const double iv = hv->v[0];
+    const bool identity = (body.op == Op::Add && iv == 0.0) ||
+                          (body.op == Op::Max && std::isinf(iv) && iv < 0) ||
+                          (body.op == Op::Min && std::isinf(iv) && iv > 0);
+    if (!identity) return 1;
+    const TensorType& it = g.type(nd.operands[0]);
+    std::set<int64_t> red(nd.dims.begin(), nd.dims.end());
+    int64_t OUT = 1, RED = 1;
+    for (int d = 0; d < it.rank(); ++d) (red.count(d) ? RED : OUT) *= it.dims[d];
+    const bool rowlike = it.rank() > 0 && red.count(it.rank() - 1);
+    const int64_t threads = rowlike ? OUT * 32 : OUT * (OUT < 148 * 32 * 4 ? 32 : 8);
+    if (threads >= 148 * 512 || RED < 8192) return 1;
+    int64_t split = (148 * 1024) / std::max<int64_t>(threads, 1);
+    split = std::min<int64_t>(split, RED / 1024);
+    split = std::min<int64_t>(split, 512);
+    return (int)std::max<int64_t>(split, 1);
   }
 
   // ---------------------------------------------------------------- GEMM --
@@ -460,7 +493,19 @@ struct Builder {
         case Op::Reduce: {
           std::vector<int> outs;
           for (size_t k = 0; k < nd.results.size(); ++k) outs.push_back(temp_for(ValueRef{n, (int)k}));
-          add_kernel(cg.reduce(n, outs));
+          const int split = reduce_split(nd);
+          if (split > 1) {
+            std::vector<int> parts;
+            for (size_t k = 0; k < nd.results.size(); ++k) {
+              TensorType pt = nd.results[k];
+              pt.dims.insert(pt.dims.begin(), split);
+              parts.push_back(new_slot(Slot::TEMP, pt, "reduce_partials"));
+            }
+            add_kernel(cg.reduce(n, parts, split));
+            add_kernel(cg.reduce_partials(n, parts, outs, split));
+          } else {
+            add_kernel(cg.reduce(n, outs));
+          }
           break;
         }
         case Op::ReduceWindow: {

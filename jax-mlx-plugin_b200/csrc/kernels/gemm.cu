@@ -12,6 +12,7 @@
 //
 // Replaces reference src/jax_mlx_pjrt.cpp:4577-4666 (dot_general lowered to
 // transpose + reshape + mlx::core::matmul).
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 
@@ -31,6 +32,11 @@ struct GemmArgs {
   void* c;
   int64_t ldc, sCb;
   int* err;
+  // split-K: gridDim.z = batch * splits; split s covers k-blocks
+  // [s*kb_per_split, (s+1)*kb_per_split) and writes raw f32 partial sums to
+  // ws[(b*splits + s)][M][N] (alpha/bias/activation applied by splitk_reduce).
+  int splits, kb_per_split;
+  float* ws;
 };
 
 template <typename TO>
@@ -103,8 +109,11 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * 128, bz = blockIdx.z;
-  const int KB = (p.K + BK - 1) / BK;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * 128;
+  const int bz = blockIdx.z / p.splits, ks = blockIdx.z % p.splits;
+  const int KB_all = (p.K + BK - 1) / BK;
+  const int kb0 = ks * p.kb_per_split;
+  const int KB = max(0, min(KB_all, kb0 + p.kb_per_split) - kb0);  // k-blocks of this CTA
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -129,9 +138,9 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % S;
-        if (kb >= S && !mbar_wait(&empty[s], ((kb / S) + 1) & 1, abort, p.err, 101)) break;
+      for (int i = 0; i < KB; ++i) {
+        const int s = i % S, kb = kb0 + i;
+        if (i >= S && !mbar_wait(&empty[s], ((i / S) + 1) & 1, abort, p.err, 101)) break;
         mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
         if (!p.a_mn) {
           tma_load_3d(sA(s), &tA, &full[s], kb * BK, m0, bz);
@@ -166,10 +175,10 @@ __global__ void __launch_bounds__(192, 1)
                       : umma_desc(base + kk * 32, 16, 1024);
       };
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % S;
-        const bool w = SPLIT ? mbar_wait(&split[s], (kb / S) & 1, abort, p.err, 102)
-                             : mbar_wait(&full[s], (kb / S) & 1, abort, p.err, 102);
+      for (int i = 0; i < KB; ++i) {
+        const int s = i % S;
+        const bool w = SPLIT ? mbar_wait(&split[s], (i / S) & 1, abort, p.err, 102)
+                             : mbar_wait(&full[s], (i / S) & 1, abort, p.err, 102);
         if (!w) { ok = false; break; }
         tc_fence_after();
         const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
@@ -178,14 +187,14 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t ad = adesc(a0, kk), bd = bdesc(b0, kk);
           if (ES == 4) {
             if (SPLIT) {
-              umma_tf32(tmem, adesc(smem_u32(sAlo(s)), kk), bd, idesc, (kb | kk) != 0);
+              umma_tf32(tmem, adesc(smem_u32(sAlo(s)), kk), bd, idesc, (i | kk) != 0);
               umma_tf32(tmem, ad, bdesc(smem_u32(sBlo(s)), kk), idesc, 1);
               umma_tf32(tmem, ad, bd, idesc, 1);
             } else {
-              umma_tf32(tmem, ad, bd, idesc, (kb | kk) != 0);
+              umma_tf32(tmem, ad, bd, idesc, (i | kk) != 0);
             }
           } else {
-            umma_f16(tmem, ad, bd, idesc, (kb | kk) != 0);
+            umma_f16(tmem, ad, bd, idesc, (i | kk) != 0);
           }
         }
         umma_commit(&empty[s]);
@@ -195,9 +204,9 @@ __global__ void __launch_bounds__(192, 1)
   } else {  // ---- warps 2..5: operand split (3xTF32), then the epilogue
     if (SPLIT) {
       const int tid = threadIdx.x - 64;
-      for (int kb = 0; kb < KB; ++kb) {
-        const int s = kb % S;
-        bool w = mbar_wait(&full[s], (kb / S) & 1, abort, p.err, 104);
+      for (int i = 0; i < KB; ++i) {
+        const int s = i % S;
+        bool w = mbar_wait(&full[s], (i / S) & 1, abort, p.err, 104);
         if (!__all_sync(0xffffffffu, w)) break;
         split_tile(sA(s), sAlo(s), A_BYTES, tid, 128);
         split_tile(sB(s), sBlo(s), B_BYTES, tid, 128);
@@ -209,10 +218,27 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const int m = m0 + row;
-    bool ok = mbar_wait(tfull, 0, abort, p.err, 103);
+    bool ok = KB == 0 || mbar_wait(tfull, 0, abort, p.err, 103);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
-    if (ok) {
+    if (ok && p.splits > 1) {
+      float* prow = p.ws + ((int64_t)blockIdx.z * p.M + m) * p.N;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        if (KB > 0) {
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        if (m < p.M) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + c + j < p.N) prow[n0 + c + j] = v[j];
+        }
+      }
+    } else if (ok) {
       TO* crow = reinterpret_cast<TO*>(p.c) + (int64_t)bz * p.sCb + (int64_t)m * p.ldc;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
@@ -254,23 +280,24 @@ __global__ void __launch_bounds__(256)
     gemm_simt(const TI* __restrict__ A, const TI* __restrict__ B, TO* __restrict__ C,
               const void* bias, int M, int N, int K, int64_t sAb, int64_t sAm, int64_t sAk,
               int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, int64_t sCb, float alpha,
-              int epi) {
+              int epi, int splits, int kchunk, float* __restrict__ ws) {
   __shared__ float As[16][64 + 1];
   __shared__ float Bs[16][64 + 1];
-  const int bz = blockIdx.z;
+  const int bz = blockIdx.z / splits, ks = blockIdx.z % splits;
   const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
   A += (int64_t)bz * sAb;
   B += (int64_t)bz * sBb;
+  const int kbeg = ks * kchunk, kend = min(K, kbeg + kchunk);
   float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 16) {
+  for (int k0 = kbeg; k0 < kend; k0 += 16) {
     for (int i = threadIdx.x; i < 64 * 16; i += 256) {
       const int mm = i / 16, kk = i % 16;  // A tile [64 m][16 k]
       const int gm = m0 + mm, gk = k0 + kk;
-      As[kk][mm] = (gm < M && gk < K) ? Io<TI>::to_f(A[gm * sAm + gk * sAk]) : 0.f;
+      As[kk][mm] = (gm < M && gk < kend) ? Io<TI>::to_f(A[gm * sAm + gk * sAk]) : 0.f;
       const int kk2 = i / 64, nn = i % 64;  // B tile [16 k][64 n]
       const int gk2 = k0 + kk2, gn = n0 + nn;
-      Bs[kk2][nn] = (gk2 < K && gn < N) ? Io<TI>::to_f(B[gk2 * sBk + gn * sBn]) : 0.f;
+      Bs[kk2][nn] = (gk2 < kend && gn < N) ? Io<TI>::to_f(B[gk2 * sBk + gn * sBn]) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -293,6 +320,10 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
       if (n >= N) continue;
+      if (splits > 1) {
+        ws[((int64_t)blockIdx.z * M + m) * N + n] = acc[i][j];
+        continue;
+      }
       float x = acc[i][j] * alpha;
       if (epi == 1 || epi == 2) x += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n]);
       if (epi >= 2) x = fmaxf(x, 0.f);
@@ -301,11 +332,81 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Split-K plan: when the output tiles alone cannot fill the GPU, the K loop is
+// divided so that about two CTAs per SM run; each split keeps at least
+// `min_blocks` k-blocks so the partial-sum traffic stays small next to the
+// operand traffic.
+struct SplitPlan {
+  int splits = 1, per_split = 1;
+};
+SplitPlan plan_splits(int64_t tiles, int kblocks, int min_blocks, int64_t batch) {
+  SplitPlan sp;
+  sp.per_split = std::max(kblocks, 1);
+  const int64_t target = 2 * (int64_t)num_sms();
+  if (tiles >= num_sms() || kblocks < 2 * min_blocks) return sp;
+  int64_t want = (target + tiles - 1) / tiles;
+  want = std::min<int64_t>(want, kblocks / min_blocks);
+  want = std::min<int64_t>(want, 64);
+  want = std::min<int64_t>(want, 65535 / std::max<int64_t>(batch, 1));
+  if (want <= 1) return sp;
+  sp.per_split = (int)((kblocks + want - 1) / want);
+  sp.splits = (kblocks + sp.per_split - 1) / sp.per_split;
+  return sp;
+}
+
+// Where split-K partial sums live.  b200_gemm takes stream-ordered memory from
+// the CUDA memory pool (cudaMallocAsync / cudaFreeAsync on the launch stream);
+// a caller may instead lend a fixed buffer.
+struct Scratch {
+  void* lent = nullptr;
+  size_t lent_bytes = 0;
+  void* owned = nullptr;
+  cudaStream_t owned_stream = nullptr;
+  int get(size_t bytes, cudaStream_t st, float** out) {
+    if (lent) {
+      if (bytes > lent_bytes)
+        return set_error(B200_ERR_INVALID, "gemm: split-K needs " + std::to_string(bytes) +
+                                               " scratch bytes, the lent buffer has " +
+                                               std::to_string(lent_bytes));
+      *out = static_cast<float*>(lent);
+      return B200_OK;
+    }
+    B200_CUDA_TRY(cudaMallocAsync(&owned, bytes, st));
+    owned_stream = st;
+    *out = static_cast<float*>(owned);
+    return B200_OK;
+  }
+  ~Scratch() {
+    if (owned) cudaFreeAsync(owned, owned_stream);
+  }
+};
+
+// Sums the split-K partials in a fixed order (deterministic) and applies the
+// epilogue: C[b,m,n] = epi(alpha * sum_s ws[b*splits+s][m][n] (+ bias[n])).
+template <typename TO>
+__global__ void __launch_bounds__(256)
+    splitk_reduce(const float* __restrict__ ws, TO* __restrict__ C, const void* bias, int batch,
+                  int M, int N, int splits, int64_t ldc, int64_t sCb, float alpha, int epi) {
+  const int64_t total = (int64_t)batch * M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / ((int64_t)M * N), mn = i % ((int64_t)M * N);
+    const int m = (int)(mn / N), n = (int)(mn % N);
+    const float* src = ws + (b * splits) * (int64_t)M * N + mn;
+    float x = 0.f;
+    for (int k = 0; k < splits; ++k) x += src[(int64_t)k * M * N];
+    x *= alpha;
+    if (epi == 1 || epi == 2) x += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n]);
+    if (epi >= 2) x = fmaxf(x, 0.f);
+    store_out<TO>(C + b * sCb + (int64_t)m * ldc + n, x);
+  }
+}
+
 template <int BN, int ES, typename TO, bool SPLIT>
 int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
               int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
               int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn,
-              cudaStream_t st) {
+              cudaStream_t st, Scratch& scratch) {
   constexpr int BK = 128 / ES;
   constexpr int E = 128 / ES;
   CUtensorMap ta, tb;
@@ -360,21 +461,51 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
                                 smem) == cudaSuccess;
   }();
   if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(gemm_tc) failed");
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 127) / 128), (unsigned)batch);
+  const int64_t gx = (N + BN - 1) / BN, gy = (M + 127) / 128;
+  const int KB_all = (int)((K + BK - 1) / BK);
+  const SplitPlan sp = plan_splits(gx * gy * batch, KB_all, 4, batch);
+  p.splits = sp.splits;
+  p.kb_per_split = sp.per_split;
+  p.ws = nullptr;
+  if (sp.splits > 1) {
+    if (int rc2 = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &p.ws)) return rc2;
+  }
+  dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(batch * sp.splits));
   gemm_tc<BN, ES, TO, SPLIT><<<grid, 192, smem, st>>>(ta, tb, p);
   B200_LAUNCH_CHECK();
+  if (sp.splits > 1) {
+    const int64_t total = batch * M * N;
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    splitk_reduce<TO><<<blocks, 256, 0, st>>>(p.ws, (TO*)c, bias, (int)batch, (int)M, (int)N,
+                                              sp.splits, ldc, M * ldc, alpha, epi);
+    B200_LAUNCH_CHECK();
+  }
   return B200_OK;
 }
 
 template <typename TI, typename TO>
 int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
                 int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
-                int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, cudaStream_t st) {
-  dim3 grid((unsigned)((N + 63) / 64), (unsigned)((M + 63) / 64), (unsigned)batch);
+                int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, cudaStream_t st,
+                Scratch& scratch) {
+  const int64_t gx = (N + 63) / 64, gy = (M + 63) / 64;
+  const SplitPlan sp = plan_splits(gx * gy * batch, (int)((K + 15) / 16), 8, batch);
+  float* ws = nullptr;
+  if (sp.splits > 1) {
+    if (int rc = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &ws)) return rc;
+  }
+  dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(batch * sp.splits));
   gemm_simt<TI, TO><<<grid, 256, 0, st>>>((const TI*)a, (const TI*)b, (TO*)c, bias, (int)M, (int)N,
                                           (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, M * ldc, alpha,
-                                          epi);
+                                          epi, sp.splits, sp.per_split * 16, ws);
   B200_LAUNCH_CHECK();
+  if (sp.splits > 1) {
+    const int64_t total = batch * M * N;
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    splitk_reduce<TO><<<blocks, 256, 0, st>>>(ws, (TO*)c, bias, (int)batch, (int)M, (int)N,
+                                              sp.splits, ldc, M * ldc, alpha, epi);
+    B200_LAUNCH_CHECK();
+  }
   return B200_OK;
 }
 
@@ -416,6 +547,7 @@ extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias
   if (M == 0 || N == 0) return B200_OK;
   auto st = (cudaStream_t)stream;
   if (K == 0) return set_error(B200_ERR_UNSUPPORTED, "gemm: K == 0 is not supported");
+  Scratch scratch;
   const int es = in_dtype == B200_DT_F32 ? 4 : 2;
   auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
   auto m16 = [&](int64_t s) { return ((s * es) & 15) == 0; };
@@ -431,7 +563,7 @@ extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias
     const bool bn64 = N <= 64 || tiles128 < num_sms();
 #define B200_TC(BN_, ES_, TO_, SPLIT_)                                                              \
   return launch_tc<BN_, ES_, TO_, SPLIT_>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, \
-                                          ldc, alpha, epilogue, a_mn, b_mn, st)
+                                          ldc, alpha, epilogue, a_mn, b_mn, st, scratch)
     if (es == 4) {
       const bool x3 = f32_matmul_3x();
       if (x3) {
@@ -447,11 +579,11 @@ extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias
 #undef B200_TC
   }
   if (es == 4) {
-    if (obf) return launch_simt<float, __nv_bfloat16>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st);
-    return launch_simt<float, float>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st);
+    if (obf) return launch_simt<float, __nv_bfloat16>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st, scratch);
+    return launch_simt<float, float>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st, scratch);
   }
-  if (obf) return launch_simt<__nv_bfloat16, __nv_bfloat16>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st);
-  return launch_simt<__nv_bfloat16, float>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st);
+  if (obf) return launch_simt<__nv_bfloat16, __nv_bfloat16>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st, scratch);
+  return launch_simt<__nv_bfloat16, float>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st, scratch);
 }
 
 // Which path b200_gemm takes for these arguments: 1 tensor cores, 0 SIMT.

@@ -228,6 +228,24 @@ def test_gemm_batched_and_epilogues():
         assert_close(got, ref, 2e-3, f"epi {epi}")
 
 
+@pytest.mark.parametrize("M,N,K,a_t,b_t", [(288, 64, 50176, False, False), (9, 32, 200704, False, False),
+                                           (3136, 256, 256, True, False), (1024, 1024, 1024, True, False)])
+def test_gemm_split_k_tall_skinny(M, N, K, a_t, b_t):
+    """Few output tiles and a long K loop: the K range is split over CTAs and
+    the partial sums reduced in a fixed order (conv weight gradients, dense wgrads)."""
+    got, ref, tc = _gemm_case(M, N, K, a_t, b_t, kernels.DT_F32, seed=M + K)
+    assert tc
+    assert_close(got, ref, 2e-3, f"split-k {M}x{N}x{K}")
+    got2, _, _ = _gemm_case(M, N, K, a_t, b_t, kernels.DT_F32, seed=M + K)
+    np.testing.assert_array_equal(got, got2)  # deterministic
+
+
+def test_gemm_simt_split_k_small_n():
+    got, ref, tc = _gemm_case(1024, 10, 4096, False, False, kernels.DT_F32, seed=12)
+    assert not tc
+    assert_close(got, ref, 1e-5, "simt split-k")
+
+
 def test_gemm_simt_fallback_for_unaligned_rows():
     got, ref, tc = _gemm_case(1024, 10, 1024, False, False, kernels.DT_F32, seed=9)
     assert not tc
