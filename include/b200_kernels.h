@@ -12,6 +12,7 @@
 #ifndef B200_KERNELS_H_
 #define B200_KERNELS_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifndef B200_API
@@ -98,6 +99,37 @@ B200_API int b200_gemm(const void* a, const void* b, void* c, const void* bias, 
               int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
               int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
               int in_dtype, int out_dtype, int epilogue, void* stream);
+
+/* b200_gemm that allocates no device memory, for callers that cannot allocate:
+ *  - a host program whose device memory belongs to another allocator, such as
+ *    a JAX/XLA process whose PJRT client has reserved most of HBM up front, so a
+ *    library-side cudaMallocAsync either fails or takes memory that allocator
+ *    was counting on;
+ *  - code that must not let a library grow or touch the CUDA memory pool
+ *    behind its back (a fixed memory budget, or a pool owned by someone else).
+ * b200_gemm takes its split-K partial sums from cudaMallocAsync on `stream`;
+ * this variant keeps them in one fixed 8 MiB device array inside the library
+ * (every GPU that loads the library holds it until the process exits), and its
+ * bounded-wait error word is a fixed device variable too (b200_device_error
+ * reports it).  It calls no cudaMalloc, cudaMallocAsync, cudaFree or other
+ * allocating routine.
+ * Limit: a call whose split-K plan needs more than 8 MiB of partial sums
+ * (splits x batch x M x N x 4 bytes) returns B200_ERR_INVALID and
+ * b200_last_error() names both sizes; shapes that need no split use no scratch.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current, so make that first call
+ * before any stream capture.  All calls on a device share the array, which
+ * keeps the last call's contents: two calls that overlap on the GPU (different
+ * streams, or host threads that do not order their calls) race on it.  Each
+ * call writes every partial sum it reads, so nothing needs clearing between
+ * calls.  Arguments, results and error codes are otherwise those of b200_gemm.
+ * No counterpart in the reference: it has no split-K scratch and allocates
+ * through MLX. */
+B200_API int b200_gemm_noalloc(const void* a, const void* b, void* c, const void* bias,
+                               int64_t batch, int64_t M, int64_t N, int64_t K, int64_t sAb,
+                               int64_t sAm, int64_t sAk, int64_t sBb, int64_t sBk, int64_t sBn,
+                               int64_t ldc, float alpha, int in_dtype, int out_dtype, int epilogue,
+                               void* stream);
 
 /* 1 when b200_gemm would take the tcgen05/TMA path for these arguments, 0 when
  * it falls back to the SIMT kernel (rows not 16-byte aligned, tiny K, ...). */

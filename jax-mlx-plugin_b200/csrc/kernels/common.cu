@@ -81,5 +81,7 @@ extern "C" int b200_device_error(int clear) {
   int v = 0;
   if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
   if (clear && v) cudaMemset(w, 0, sizeof(int));
-  return v;
+  const int v2 = b200::noalloc_error_take(clear);
+  if (v2 < 0) return -1;
+  return v ? v : v2;
 }

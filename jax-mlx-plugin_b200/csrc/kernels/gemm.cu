@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -360,13 +361,14 @@ SplitPlan plan_splits(int64_t tiles, int kblocks, int min_blocks, int64_t batch)
 struct Scratch {
   void* lent = nullptr;
   size_t lent_bytes = 0;
+  int* err = nullptr;  // bounded-wait error word; nullptr: device_error_word()
   void* owned = nullptr;
   cudaStream_t owned_stream = nullptr;
   int get(size_t bytes, cudaStream_t st, float** out) {
     if (lent) {
       if (bytes > lent_bytes)
         return set_error(B200_ERR_INVALID, "gemm: split-K needs " + std::to_string(bytes) +
-                                               " scratch bytes, the lent buffer has " +
+                                               " bytes of scratch, the fixed scratch array holds " +
                                                std::to_string(lent_bytes));
       *out = static_cast<float*>(lent);
       return B200_OK;
@@ -453,7 +455,7 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   p.c = c;
   p.ldc = ldc;
   p.sCb = M * ldc;
-  p.err = device_error_word();
+  p.err = scratch.err ? scratch.err : device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   const int smem = TcCfg<BN, ES, SPLIT>::SMEM;
   static bool attr = [&] {
@@ -530,11 +532,12 @@ bool force_simt() {
 }  // namespace
 }  // namespace b200
 
-extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias, int64_t batch,
-                         int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
-                         int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
-                         int in_dtype, int out_dtype, int epilogue, void* stream) {
-  using namespace b200;
+namespace b200 {
+namespace {
+int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64_t batch,
+                  int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
+                  int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
+                  int in_dtype, int out_dtype, int epilogue, void* stream, Scratch& scratch) {
   B200_CHECK_ARG(a && b && c, "gemm: null operand");
   B200_CHECK_ARG(batch >= 1 && M >= 0 && N >= 0 && K >= 0, "gemm: bad shape");
   B200_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31) && batch < 65536,
@@ -547,7 +550,6 @@ extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias
   if (M == 0 || N == 0) return B200_OK;
   auto st = (cudaStream_t)stream;
   if (K == 0) return set_error(B200_ERR_UNSUPPORTED, "gemm: K == 0 is not supported");
-  Scratch scratch;
   const int es = in_dtype == B200_DT_F32 ? 4 : 2;
   auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
   auto m16 = [&](int64_t s) { return ((s * es) & 15) == 0; };
@@ -584,6 +586,85 @@ extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias
   }
   if (obf) return launch_simt<__nv_bfloat16, __nv_bfloat16>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st, scratch);
   return launch_simt<__nv_bfloat16, float>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, epilogue, st, scratch);
+}
+
+}  // namespace
+}  // namespace b200
+
+extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias, int64_t batch,
+                         int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
+                         int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
+                         int in_dtype, int out_dtype, int epilogue, void* stream) {
+  b200::Scratch scratch;  // split-K partials from cudaMallocAsync on `stream`
+  return b200::gemm_dispatch(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
+                             alpha, in_dtype, out_dtype, epilogue, stream, scratch);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free GEMM.  Split-K partial sums go to this fixed array instead of
+// stream-ordered allocations, and the bounded-wait error word is a fixed
+// device variable too, so a call never allocates device memory.  Every GPU
+// that loads the library holds the array (kNoAllocScratchBytes) until the
+// process exits; all calls on a device share it.
+static constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+static __device__ int g_noalloc_err;  // zero at load; set only by a wait that runs out
+
+namespace b200 {
+namespace {
+struct NoAllocDevice {
+  float* scratch = nullptr;
+  int* err = nullptr;
+};
+
+// Device addresses of the fixed array and error word for the current device.
+// In host code `g_noalloc_scratch` names a host-side stand-in, not device
+// memory, so the address is looked up once per device (with that device
+// current) and cached.
+int noalloc_device(NoAllocDevice* out) {
+  static std::mutex mu;
+  static NoAllocDevice per[64];
+  static bool ready[64] = {false};
+  int dev = -1;
+  B200_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(B200_ERR_INVALID, "gemm_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ready[dev]) {
+    B200_CUDA_TRY(cudaGetSymbolAddress((void**)&per[dev].scratch, g_noalloc_scratch));
+    B200_CUDA_TRY(cudaGetSymbolAddress((void**)&per[dev].err, g_noalloc_err));
+    ready[dev] = true;
+  }
+  *out = per[dev];
+  return B200_OK;
+}
+}  // namespace
+
+// Reads (and optionally clears) the allocation-free GEMM's error word on the
+// current device; b200_device_error reports it together with its own word.
+int noalloc_error_take(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_noalloc_err, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+}  // namespace b200
+
+extern "C" int b200_gemm_noalloc(const void* a, const void* b, void* c, const void* bias,
+                                 int64_t batch, int64_t M, int64_t N, int64_t K, int64_t sAb,
+                                 int64_t sAm, int64_t sAk, int64_t sBb, int64_t sBk, int64_t sBn,
+                                 int64_t ldc, float alpha, int in_dtype, int out_dtype,
+                                 int epilogue, void* stream) {
+  b200::NoAllocDevice nd;
+  if (int rc = b200::noalloc_device(&nd)) return rc;
+  b200::Scratch scratch;
+  scratch.lent = nd.scratch;
+  scratch.lent_bytes = kNoAllocScratchBytes;
+  scratch.err = nd.err;
+  return b200::gemm_dispatch(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
+                             alpha, in_dtype, out_dtype, epilogue, stream, scratch);
 }
 
 // Which path b200_gemm takes for these arguments: 1 tensor cores, 0 SIMT.

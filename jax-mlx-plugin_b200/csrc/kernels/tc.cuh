@@ -192,4 +192,7 @@ int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
               bool atom32 = false);
 // Per-device error word passed to kernels with bounded waits (zeroed once).
 int* device_error_word();
+// The allocation-free GEMM's error word on the current device (gemm.cu):
+// its value, -1 on a CUDA error; cleared when `clear` is set.
+int noalloc_error_take(int clear);
 }

@@ -29,6 +29,8 @@ EXPORTS = {
                               [C.POINTER(C.c_int64), C.c_float, C.c_int, C.c_int, C.c_void_p]),
     "b200_gemm": (C.c_int, [C.c_void_p] * 4 + [C.c_int64] * 11 + [C.c_float, C.c_int, C.c_int,
                                                                   C.c_int, C.c_void_p]),
+    "b200_gemm_noalloc": (C.c_int, [C.c_void_p] * 4 + [C.c_int64] * 11 +
+                          [C.c_float, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "b200_gemm_uses_tensor_cores": (C.c_int, [C.c_void_p, C.c_void_p] + [C.c_int64] * 8 + [C.c_int]),
     "b200_device_error": (C.c_int, [C.c_int]),
 }
@@ -88,6 +90,15 @@ def gemm(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha
          out_dtype, epilogue, stream):
     _check(lib().b200_gemm(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha,
                            in_dtype, out_dtype, epilogue, stream), "gemm")
+
+
+def gemm_noalloc(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha,
+                 in_dtype, out_dtype, epilogue, stream):
+    """b200_gemm_noalloc: same call as gemm(), but the library allocates no device
+    memory (split-K partials live in its fixed 8 MiB per-device array)."""
+    _check(lib().b200_gemm_noalloc(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn,
+                                   ldc, alpha, in_dtype, out_dtype, epilogue, stream),
+           "gemm_noalloc")
 
 
 def gemm_uses_tensor_cores(a, b, batch, K, sAb, sAm, sAk, sBb, sBk, sBn, in_dtype) -> bool:
