@@ -1,21 +1,22 @@
 """Benchmark of the B200 PJRT plugin on BASELINE.json's configurations.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload ln|sdpa|mlp|cnn] [--no-extra]
+                    [--workload ln|sdpa|mlp|cnn|transformer] [--no-extra]
 
 Default workload: configs[1], the jitted residual-add + LayerNorm forward
 (x, r [4096,1024] f32), whose metric is HBM GB/s.  One step = one PJRT
 Execute of the compiled program on inputs resident in HBM; the L2 (126 MB) is
-flushed by a 512 MB write between timed steps, and each step is timed with CUDA
-events on the plugin's own stream.  ``e2e`` repeats the measurement through the
+flushed between timed steps by reading a 2 GB buffer, and each step is timed
+with CUDA events on the plugin's own stream.  ``e2e`` repeats the measurement through the
 same PJRT calls a jax.jit user triggers, with the inputs copied from pinned host
 memory (BufferFromHostBuffer) and the output read back (ToHostBuffer) inside
 the timed region.  At N=1 the line also carries the other configurations
-(causal SDPA TFLOP/s, MLP and CNN training-step samples/s) under "extra".
+(causal SDPA TFLOP/s, MLP, CNN and transformer training-step samples/s) under
+"extra".
 
 Multi-GPU (torchrun, one process per GPU): LayerNorm and SDPA are independent
-replicas (no collective); the MLP/CNN steps shard the global batch and
-all-reduce gradients through the plugin's NCCL all_reduce.
+replicas (no collective); the MLP/CNN/transformer steps shard the global batch
+and all-reduce gradients through the plugin's NCCL all_reduce.
 
 --impl reference times the reference's CPU path for the same workload.  The
 reference plugin needs macOS + Metal (MLX) and cannot be built here, so its
@@ -51,6 +52,10 @@ SDPA_FLOPS = 4 * 8 * 8 * 64 * (512 * 513 // 2)                  # 2,151,677,952 
 MLP_DIMS = (784, 1024, 1024, 1024, 10)
 MLP_FLOPS = 16_236_150_784
 CNN_FLOPS = 7_017_332_736
+# 6 * (matmul params 6*3,145,728 + head 16,384,000) * 16,384 tokens
+# + attention 3 (fwd + 2x bwd) * 6 layers * 4 * 64 * 256^2 * 512
+TR_CFG = dict(batch=64, seq=256, layers=6, d=512, heads=8, ffn=2048, vocab=32000)
+TR_FLOPS = 6 * (6 * 3_145_728 + 16_384_000) * 64 * 256 + 3 * 6 * 4 * 64 * 256 * 256 * 512
 
 
 def peaks():
@@ -266,31 +271,61 @@ def _cnn_args(rng, batch):
     return ps + [x, lab]
 
 
+def _transformer_bufs(rig: Rig, rng, per, rank):
+    """configs[3] arguments: N(0, 0.02) bf16 params, zero f32 Adam moments,
+    count 0, this rank's slice of the [64, 256] tokens and next-token targets."""
+    from jax_b200 import pjrt, programs
+    c = TR_CFG
+    shapes = programs.transformer_param_shapes(c["layers"], c["d"], c["heads"], c["ffn"], c["vocab"],
+                                               c["seq"])
+    bufs = [rig.client.buffer_from_numpy(pjrt.to_bf16_bits(rng.standard_normal(s).astype(np.float32)
+                                                           * np.float32(0.02)), rig.dev, bf16=True)
+            for _, s in shapes]
+    zeros = [np.zeros(s, np.float32) for _, s in shapes]
+    tok = rng.integers(0, c["vocab"], (c["batch"], c["seq"])).astype(np.int32)
+    tgt = np.roll(tok, -1, axis=1)
+    sl = slice(rank * per, (rank + 1) * per)
+    return bufs + rig.bufs(zeros + zeros + [np.array(0, np.int32), tok[sl], tgt[sl]])
+
+
 def bench_train(rig: Rig, kind, steps, warmup, world=1, rank=0):
     from jax_b200 import programs
-    gb = 1024 if kind == "mlp" else 256
+    gb = {"mlp": 1024, "cnn": 256, "transformer": TR_CFG["batch"]}[kind]
     per = gb // world
-    text = programs.mlp_step(batch=per, num_replicas=world) if kind == "mlp" else \
-        programs.cnn_step(batch=per, num_replicas=world)
+    if kind == "mlp":
+        text = programs.mlp_step(batch=per, num_replicas=world)
+    elif kind == "cnn":
+        text = programs.cnn_step(batch=per, num_replicas=world)
+    else:
+        text = programs.transformer_step(**dict(TR_CFG, batch=per), num_replicas=world)
     exe = rig.client.compile(text)
-    rng = np.random.default_rng(8 if kind == "mlp" else 13)
-    full = _mlp_args(rng, gb) if kind == "mlp" else _cnn_args(rng, gb)
-    arrays = full[:-2] + [full[-2][rank * per:(rank + 1) * per], full[-1][rank * per:(rank + 1) * per]]
-    args = rig.bufs(arrays)
+    rng = np.random.default_rng({"mlp": 8, "cnn": 13, "transformer": 11}[kind])
+    if kind == "transformer":
+        args = _transformer_bufs(rig, rng, per, rank)
+        n_state = len(args) - 2  # params, moments and count feed the next step
+    else:
+        full = _mlp_args(rng, gb) if kind == "mlp" else _cnn_args(rng, gb)
+        arrays = full[:-2] + [full[-2][rank * per:(rank + 1) * per],
+                              full[-1][rank * per:(rank + 1) * per]]
+        args = rig.bufs(arrays)
+        n_state = len(args) - 2
     holder = []
 
     def step():
-        # the updated params feed the next step, as a training loop does
+        # the updated state feeds the next step, as a training loop does
         outs = exe.execute([args])[0]
         holder[:] = outs
-        args[:len(outs) - 1] = outs[1:]
+        args[:n_state] = outs[1:1 + n_state]
     ts = rig.time_steps(step, steps, warmup, flush=False)
     exe.device_times_ms()
     t = float(np.mean(ts))  # back-to-back steps: host launch overhead is part of a training step
-    flops = MLP_FLOPS if kind == "mlp" else CNN_FLOPS
-    return {"metric": f"{kind.upper()} training step (jitted value_and_grad + SGD)", "unit": "samples/s",
-            "value": gb / t, "ms_per_step": t * 1e3, "global_batch": gb, "flops_per_step": flops,
-            "tflops": flops / t / 1e12, "launches_per_step": plan_launches(text)}
+    flops = {"mlp": MLP_FLOPS, "cnn": CNN_FLOPS, "transformer": TR_FLOPS}[kind]
+    opt = "Adam" if kind == "transformer" else "SGD"
+    return {"metric": f"{kind.upper()} training step (jitted value_and_grad + {opt})",
+            "unit": "samples/s", "value": gb / t, "ms_per_step": t * 1e3, "global_batch": gb,
+            "flops_per_step": flops, "tflops": flops / t / 1e12,
+            "launches_per_step": plan_launches(text),
+            "dtype": "bf16" if kind == "transformer" else "f32"}
 
 
 # -------------------------------------------------------- CPU baseline ---
@@ -321,7 +356,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="ln", choices=["ln", "sdpa", "mlp", "cnn"])
+    ap.add_argument("--workload", default="ln", choices=["ln", "sdpa", "mlp", "cnn", "transformer"])
     ap.add_argument("--no-extra", action="store_true")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
@@ -356,7 +391,7 @@ def main():
         from datetime import timedelta
         torch.cuda.set_device(local_rank)
         dist.init_process_group("gloo", timeout=timedelta(seconds=300))
-    dp = a.workload in ("mlp", "cnn") and world > 1
+    dp = a.workload in ("mlp", "cnn", "transformer") and world > 1
     kv = None
     if dp:
         store = dist.distributed_c10d._get_default_store()
@@ -423,7 +458,7 @@ def main():
                              "peak_kind": pk_kind}
         except Exception as e:  # report, do not hide
             extra["sdpa"] = {"error": str(e)[:300]}
-        for kind in ("mlp", "cnn"):
+        for kind in ("mlp", "cnn", "transformer"):
             try:
                 extra[f"{kind}_step"] = bench_train(rig, kind, 20, 3)
             except Exception as e:

@@ -70,6 +70,10 @@ class CodeGen {
   std::vector<int> ptrs_;
   std::vector<bool> written_;
   std::vector<std::map<std::string, std::string>> memo_;
+  // Set while emitting a reduction's combiner: bf16 partial results stay in
+  // f32 and are rounded once when stored (XLA accumulates bf16 reductions in
+  // f32 rather than rounding after every add).
+  bool accum_f32_ = false;
   int tmp_ = 0;
   int indent_ = 1;
   std::string idx_t_ = "int";

@@ -221,10 +221,11 @@ struct Builder {
     st.dtype2 = (int)out_dt;
     p.steps.push_back(st);
   }
-  int permuted_copy(int src, const std::vector<int64_t>& perm, const std::string& what) {
+  int permuted_copy(int src, const std::vector<int64_t>& perm, const std::string& what,
+                    DType to = DType::INVALID) {
     const TensorType& t = p.slots[src].type;
     TensorType o;
-    o.dtype = t.dtype;
+    o.dtype = to == DType::INVALID ? t.dtype : to;
     for (auto d : perm) o.dims.push_back(t.dims[d]);
     int dst = new_slot(Slot::TEMP, o, what);
     add_kernel(cg.permute(src, perm, dst));
@@ -236,7 +237,20 @@ struct Builder {
     int ls = slot.at(L), rs = slot.at(R);
     TensorType lt = g.type(L), rt = g.type(R);
     const TensorType& ot = nd.results[0];
-    if (lt.dtype != rt.dtype) throw PjrtErr(12, "dot_general with mixed operand types");
+    if (lt.dtype != rt.dtype) {
+      // Mixed f32 x bf16 operands (JAX's transpose rule for a bf16 dot with an
+      // f32 preferred_element_type emits them): widen the bf16 side to f32, the
+      // type XLA computes such a product in.
+      auto widen = [&](int& s, TensorType& t) {
+        std::vector<int64_t> id(t.rank());
+        for (int i = 0; i < t.rank(); ++i) id[i] = i;
+        s = permuted_copy(s, id, "dot_widen", DType::F32);
+        t = p.slots[s].type;
+      };
+      if (lt.dtype == DType::BF16 && rt.dtype == DType::F32) widen(ls, lt);
+      else if (rt.dtype == DType::BF16 && lt.dtype == DType::F32) widen(rs, rt);
+      else throw PjrtErr(12, "dot_general with mixed operand types");
+    }
     if (lt.dtype != DType::F32 && lt.dtype != DType::BF16)
       throw PjrtErr(12, std::string("dot_general on ") + dtype_name(lt.dtype) + " is not supported");
     auto free_dims = [](int rank, const std::vector<int64_t>& a, const std::vector<int64_t>& b) {
@@ -499,6 +513,7 @@ struct Builder {
             for (size_t k = 0; k < nd.results.size(); ++k) {
               TensorType pt = nd.results[k];
               pt.dims.insert(pt.dims.begin(), split);
+              if (pt.dtype == DType::BF16) pt.dtype = DType::F32;  // partials stay f32 until the final store
               parts.push_back(new_slot(Slot::TEMP, pt, "reduce_partials"));
             }
             add_kernel(cg.reduce(n, parts, split));

@@ -459,14 +459,18 @@ class Builder:
         g_lf = list(range(nb, nb + len(lf)))
         g_rf = list(range(nb + len(lf), nb + len(lf) + len(rf)))
         # dA = g . B over rf (and batch): result [batch, lf, rc-dims of B in order]
-        da = self.dot_general(g, b, (g_rf, rf), (g_b, rb), out_dt=a.dtype)
+        # JAX's transpose rule keeps the forward's preferred_element_type (the
+        # operands may then be mixed, e.g. f32 cotangent x bf16 operand) and
+        # converts the product to the primal's dtype afterwards.
+        pref = out.dtype
+        da = self.convert(self.dot_general(g, b, (g_rf, rf), (g_b, rb), out_dt=pref), a.dtype)
         # da dims: [batch (a's lb order), lf..., b's remaining dims = rc order]
         src_order = lb + lf + [lc[rc.index(d)] for d in sorted(rc)] if rc else lb + lf
         # map each a-dim to its position in da
         perm = [src_order.index(d) for d in range(len(a.shape))]
         acc(a, self.transpose(da, perm) if perm != list(range(len(perm))) else da)
         # dB = A . g over lf (and batch): result [batch, a's remaining = lc order, rf...]
-        db = self.dot_general(a, g, (lf, g_lf), (lb, g_b), out_dt=b.dtype)
+        db = self.convert(self.dot_general(a, g, (lf, g_lf), (lb, g_b), out_dt=pref), b.dtype)
         src_b = rb + [rc[lc.index(d)] for d in sorted(lc)] + rf
         perm_b = [src_b.index(d) for d in range(len(b.shape))]
         acc(b, self.transpose(db, perm_b) if perm_b != list(range(len(perm_b))) else db)

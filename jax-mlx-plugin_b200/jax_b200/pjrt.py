@@ -73,6 +73,19 @@ _NP2PJRT = {np.dtype(np.bool_): PRED, np.dtype(np.int8): S8, np.dtype(np.int16):
 _PJRT2NP = {v: k for k, v in _NP2PJRT.items()}
 _PJRT2NP[BF16] = np.dtype(np.uint16)  # bf16 bits travel as uint16 on the host
 
+
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """f32 values -> bf16 bit patterns (uint16), round to nearest even."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    nan = np.isnan(np.asarray(x, dtype=np.float32))
+    return np.where(nan, 0x7FC0, r).astype(np.uint16)
+
+
+def from_bf16_bits(b: np.ndarray) -> np.ndarray:
+    """bf16 bit patterns (uint16) -> f32 values."""
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
 ERROR_CODES = {0: "OK", 1: "CANCELLED", 2: "UNKNOWN", 3: "INVALID_ARGUMENT",
                4: "DEADLINE_EXCEEDED", 5: "NOT_FOUND", 6: "ALREADY_EXISTS",
                7: "PERMISSION_DENIED", 8: "RESOURCE_EXHAUSTED", 9: "FAILED_PRECONDITION",

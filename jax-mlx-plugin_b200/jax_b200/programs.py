@@ -10,6 +10,10 @@ Each builder mirrors the JAX source of its configuration:
 * ``mlp_step`` / ``cnn_step``: ``jax.value_and_grad`` of softmax cross-entropy,
   SGD update; with ``num_replicas > 1`` the pmap form whose gradients and loss
   are ``lax.pmean``-ed (``all_reduce`` + divide).
+* ``transformer_step``: a pre-LN causal encoder in bf16 (flax-style
+  ``DenseGeneral`` q/k/v/out projections, ``jax.nn.dot_product_attention``
+  with f32 logits and softmax, tanh GELU, learned positions, untied head),
+  f32 next-token cross-entropy, and an Adam update with f32 moments.
 """
 from __future__ import annotations
 
@@ -141,3 +145,109 @@ def cnn_step(batch=256, lr=1e-2, num_replicas=1, emit="params") -> str:
         return b.module([loss] + grads)
     new = [p - g * lr for p, g in zip(params, grads)]
     return b.module([loss] + new)
+
+
+def _layer_norm_bf16(b: Builder, x: V, g: V, beta: V, eps: float = 1e-6) -> V:
+    """flax LayerNorm on bf16 activations: statistics and affine in f32, result bf16."""
+    ax = len(x.shape) - 1
+    n = float(x.shape[ax])
+    h = b.convert(x, "f32")
+    mean = b.sum(h, [ax], keepdims=True) / n
+    d = h - mean
+    var = b.sum(d * d, [ax], keepdims=True) / n
+    y = d * b.rsqrt(var + eps) * b.convert(g, "f32") + b.convert(beta, "f32")
+    return b.convert(y, x.dtype)
+
+
+def _gelu_tanh(b: Builder, x: V) -> V:
+    """jax.nn.gelu(approximate=True), in the activation dtype."""
+    inner = (x + x * x * x * 0.044715) * math.sqrt(2.0 / math.pi)
+    return x * ((b.tanh(inner) + 1.0) * 0.5)
+
+
+def _causal_attention(b: Builder, q: V, k: V, v: V) -> V:
+    """jax.nn.dot_product_attention(q, k, v, is_causal=True) for bf16 [B,T,N,H]:
+    f32 logits, f32 softmax, bf16 probabilities."""
+    B, T, N, H = q.shape
+    logits = b.dot_general(q, k, ([3], [3]), ([0, 2], [0, 2]), out_dt="f32")  # [B,N,T,S]
+    logits = logits * (1.0 / math.sqrt(H))
+    row, col = b.iota((T, T), 0), b.iota((T, T), 1)
+    mask = b.reshape(b.compare(row, col, "GE", "SIGNED"), (1, 1, T, T))
+    big_neg = b.constant(-0.7 * F32_MAX, "f32", logits.shape)
+    logits = b.select(b.broadcast_to(mask, logits.shape), logits, big_neg)
+    probs = b.convert(softmax(b, logits), v.dtype)
+    enc = b.dot_general(probs, v, ([3], [1]), ([0, 1], [0, 2]))  # [B,N,T,H]
+    return b.transpose(enc, [0, 2, 1, 3])
+
+
+TRANSFORMER_PARAMS_PER_LAYER = ("ln1_g", "ln1_b", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo",
+                                "ln2_g", "ln2_b", "w1", "b1", "w2", "b2")
+
+
+def transformer_param_shapes(layers=6, d=512, heads=8, ffn=2048, vocab=32000, seq=256):
+    """[(name, shape)] in argument order: embeddings, blocks, final LN, head."""
+    hd = d // heads
+    per = {"ln1_g": (d,), "ln1_b": (d,), "wq": (d, heads, hd), "bq": (heads, hd),
+           "wk": (d, heads, hd), "bk": (heads, hd), "wv": (d, heads, hd), "bv": (heads, hd),
+           "wo": (heads, hd, d), "bo": (d,), "ln2_g": (d,), "ln2_b": (d,), "w1": (d, ffn),
+           "b1": (ffn,), "w2": (ffn, d), "b2": (d,)}
+    out = [("tok_emb", (vocab, d)), ("pos_emb", (seq, d))]
+    for i in range(layers):
+        out += [(f"l{i}.{n}", per[n]) for n in TRANSFORMER_PARAMS_PER_LAYER]
+    out += [("lnf_g", (d,)), ("lnf_b", (d,)), ("w_head", (d, vocab)), ("b_head", (vocab,))]
+    return out
+
+
+def transformer_step(batch=64, seq=256, layers=6, d=512, heads=8, ffn=2048, vocab=32000,
+                     lr=3e-4, b1=0.9, b2=0.999, eps=1e-8, num_replicas=1, emit="state") -> str:
+    """One Adam step of the pre-LN causal transformer.
+
+    Arguments: the bf16 parameters in ``transformer_param_shapes`` order, then the
+    f32 first and second Adam moments in the same order, the i32 step count,
+    tokens [batch, seq] i32 and next-token targets [batch, seq] i32.
+    Outputs: f32 loss, new parameters, new moments (m then v), new count
+    (optax.adam: count += 1; mu_hat = mu / (1 - b1^count); p -= lr * mu_hat /
+    (sqrt(nu_hat) + eps)); with emit="grads", the loss and the bf16 gradients."""
+    b = Builder("jit_transformer_train_step", num_replicas)
+    shapes = transformer_param_shapes(layers, d, heads, ffn, vocab, seq)
+    params = [b.param(s, "bf16") for _, s in shapes]
+    ms = [b.param(s, "f32") for _, s in shapes]
+    vs = [b.param(s, "f32") for _, s in shapes]
+    count = b.param((), "i32")
+    tokens = b.param((batch, seq), "i32")
+    targets = b.param((batch, seq), "i32")
+    P = dict(zip([n for n, _ in shapes], params))
+    x = b.take_rows(P["tok_emb"], tokens) + b.broadcast_in_dim(P["pos_emb"], (batch, seq, d), [1, 2])
+    for i in range(layers):
+        L = lambda n: P[f"l{i}.{n}"]
+        y = _layer_norm_bf16(b, x, L("ln1_g"), L("ln1_b"))
+        qkv = [b.dot_general(y, L(w), ([2], [0])) + L(bb) for w, bb in (("wq", "bq"), ("wk", "bk"),
+                                                                     ("wv", "bv"))]
+        att = _causal_attention(b, *qkv)
+        x = x + (b.dot_general(att, L("wo"), ([2, 3], [0, 1])) + L("bo"))
+        y = _layer_norm_bf16(b, x, L("ln2_g"), L("ln2_b"))
+        f = _gelu_tanh(b, b.dot_general(y, L("w1"), ([2], [0])) + L("b1"))
+        x = x + (b.dot_general(f, L("w2"), ([2], [0])) + L("b2"))
+    y = _layer_norm_bf16(b, x, P["lnf_g"], P["lnf_b"])
+    logits = b.dot_general(y, P["w_head"], ([2], [0])) + P["b_head"]
+    logits = b.convert(b.reshape(logits, (batch * seq, vocab)), "f32")
+    loss = cross_entropy(b, logits, b.reshape(targets, (batch * seq,)))
+    grads = b.grad(loss, params)
+    both = _dp_mean(b, [loss] + grads, num_replicas)
+    loss, grads = both[0], both[1:]
+    if emit == "grads":
+        return b.module([loss] + grads)
+    cnt = count + b.constant(1, "i32")
+    cf = b.convert(cnt, "f32")
+    bc1 = 1.0 - b.power(b.constant(b1, "f32"), cf)
+    bc2 = 1.0 - b.power(b.constant(b2, "f32"), cf)
+    new_p, new_m, new_v = [], [], []
+    for p, m, v, g in zip(params, ms, vs, grads):
+        g32 = b.convert(g, "f32")
+        m2 = m * b1 + g32 * (1.0 - b1)
+        v2 = v * b2 + g32 * g32 * (1.0 - b2)
+        upd = (m2 / b.broadcast_to(bc1, m2.shape)) / (b.sqrt(v2 / b.broadcast_to(bc2, v2.shape)) + eps)
+        new_p.append(b.convert(b.convert(p, "f32") - upd * lr, "bf16"))
+        new_m.append(m2)
+        new_v.append(v2)
+    return b.module([loss] + new_p + new_m + new_v + [cnt])

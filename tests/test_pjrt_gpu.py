@@ -229,3 +229,115 @@ def test_data_parallel_two_devices_in_process(client):
         assert_close(got[0], loss, 2e-3, "dp loss")
         for p, g, r in zip(params, got[1:], new):
             assert_close(g, p.astype(np.float64) - r, 2e-3, "dp grad")
+
+
+# ------------------------------------------------------------ transformer (c4)
+TR_SMALL = dict(batch=4, seq=64, layers=2, d=128, heads=2, ffn=256, vocab=512)
+# bf16 programs: every bf16 op output is rounded to bf16 on both sides, but an
+# accumulation that lands on the other side of a bf16 rounding boundary moves a
+# value by one bf16 ulp (2^-8 relative), and such flips propagate through the
+# layers.  The bound is therefore 2e-2 relative with the error floor at the
+# tensor's rms, i.e. a few bf16 ulps.
+BF16_PROGRAM_TOL = 2e-2
+
+
+def _tr_inputs(cfg, seed, moments=False):
+    rng = np.random.default_rng(seed)
+    shapes = programs.transformer_param_shapes(cfg["layers"], cfg["d"], cfg["heads"], cfg["ffn"],
+                                               cfg["vocab"], cfg["seq"])
+    params = [hlo_interp.bf16_round((rng.standard_normal(s) * 0.02).astype(np.float32))
+              for _, s in shapes]
+    if moments:  # a mid-training Adam state: smooth updates, no sign(g) steps
+        ms = [(rng.standard_normal(s) * 1e-3).astype(np.float32) for _, s in shapes]
+        vs = [(rng.random(s) * 1e-6 + 1e-7).astype(np.float32) for _, s in shapes]
+        count = 7
+    else:
+        ms = [np.zeros(s, np.float32) for _, s in shapes]
+        vs = [np.zeros(s, np.float32) for _, s in shapes]
+        count = 0
+    tok = rng.integers(0, cfg["vocab"], (cfg["batch"], cfg["seq"])).astype(np.int32)
+    return params, ms, vs, np.array(count, np.int32), tok, np.roll(tok, -1, axis=1)
+
+
+def _tr_run(client, text, params, ms, vs, count, tok, tgt):
+    exe = client.compile(text)
+    bufs = ([client.buffer_from_numpy(pjrt.to_bf16_bits(p), bf16=True) for p in params] +
+            [client.buffer_from_numpy(a) for a in ms + vs + [count, tok, tgt]])
+    outs = []
+    for o in exe.execute([bufs])[0]:
+        a = o.to_numpy()
+        outs.append(pjrt.from_bf16_bits(a) if o.dtype == pjrt.BF16 else a)
+    return outs
+
+
+def test_transformer_step_gradients_match_interpreter(client):
+    """configs[3] architecture at reduced size: loss and every bf16 gradient vs
+    the interpreter (f64 arithmetic, bf16 rounding after every bf16 op)."""
+    params, ms, vs, count, tok, tgt = _tr_inputs(TR_SMALL, 31)
+    text = programs.transformer_step(**TR_SMALL, emit="grads")
+    got = _tr_run(client, text, params, ms, vs, count, tok, tgt)
+    ref = hlo_interp.run(text, [params + ms + vs + [count, tok, tgt]])[0]
+    assert_close(got[0], ref[0], 2e-3, "transformer loss")
+    names = [n for n, _ in programs.transformer_param_shapes(TR_SMALL["layers"], TR_SMALL["d"],
+             TR_SMALL["heads"], TR_SMALL["ffn"], TR_SMALL["vocab"], TR_SMALL["seq"])]
+    grads = dict(zip(names, zip(got[1:], ref[1:])))
+    failures = []
+    for n, (g, r) in grads.items():
+        if n.endswith(".bk"):
+            # softmax is invariant to the per-query constant q.bk that the key
+            # bias adds to every logit, so d loss / d bk is zero in exact
+            # arithmetic and both sides hold only the rounding noise of summing
+            # B*T bf16 key gradients; a real error would be the size of
+            # d loss / d bq, so bound it well below that
+            scale = np.sqrt(np.mean(np.square(grads[n[:-2] + "bq"][1].astype(np.float64))))
+            if np.abs(g).max() > 0.1 * scale:
+                failures.append(f"{n}: max |grad| {np.abs(g).max():.3e} vs bq scale {scale:.3e}")
+            continue
+        try:
+            assert_close(g, r, BF16_PROGRAM_TOL, f"grad {n}")
+        except AssertionError as e:
+            failures.append(str(e))
+    assert not failures, "\n".join(failures)
+
+
+def test_transformer_adam_step_matches_interpreter(client):
+    """Full step with Adam from a mid-training state: new params, moments, count."""
+    params, ms, vs, count, tok, tgt = _tr_inputs(TR_SMALL, 32, moments=True)
+    text = programs.transformer_step(**TR_SMALL)
+    got = _tr_run(client, text, params, ms, vs, count, tok, tgt)
+    ref = hlo_interp.run(text, [params + ms + vs + [count, tok, tgt]])[0]
+    P = len(params)
+    assert_close(got[0], ref[0], 2e-3, "loss")
+    failures = []
+    for i in range(P):
+        # new bf16 parameters: p - lr * update lands within one bf16 ulp of the
+        # reference (the f32 update is rounded to bf16 at the end), and the
+        # applied updates agree in aggregate
+        g, r = got[1 + i].astype(np.float64), ref[1 + i].astype(np.float64)
+        # ulp of the operands of p - lr * update (a result that cancels to
+        # near zero carries their absolute rounding error, not its own ulp)
+        big = np.maximum(np.maximum(np.abs(g), np.abs(r)), np.abs(params[i]))
+        ulp = np.exp2(np.floor(np.log2(np.maximum(big, 1e-30))) - 7)
+        if (np.abs(g - r) > ulp).any():
+            failures.append(f"param {i}: {(np.abs(g - r) > ulp).sum()} elements beyond one bf16 ulp")
+        du_g, du_r = params[i] - g, params[i] - r
+        if np.sqrt(np.mean((du_g - du_r) ** 2)) > BF16_PROGRAM_TOL * np.sqrt(np.mean(du_r ** 2)):
+            failures.append(f"update {i}: rms difference above {BF16_PROGRAM_TOL} of rms(update)")
+        for gg, rr, what in ((got[1 + P + i], ref[1 + P + i], f"m {i}"),
+                             (got[1 + 2 * P + i], ref[1 + 2 * P + i], f"v {i}")):
+            try:
+                assert_close(gg, rr, BF16_PROGRAM_TOL, what)
+            except AssertionError as e:
+                failures.append(str(e))
+    assert not failures, "\n".join(failures)
+    assert int(got[-1]) == 8
+
+
+def test_transformer_step_full_config_runs(client):
+    """configs[3] at full size (6 blocks, d 512, vocab 32000, 64x256 tokens):
+    the first-step loss is ln(32000) +- a little for N(0, 0.02) weights."""
+    cfg = dict(batch=64, seq=256, layers=6, d=512, heads=8, ffn=2048, vocab=32000)
+    params, ms, vs, count, tok, tgt = _tr_inputs(cfg, 33)
+    outs = _tr_run(client, programs.transformer_step(**cfg), params, ms, vs, count, tok, tgt)
+    assert abs(float(outs[0]) - np.log(32000)) < 0.5
+    assert all(np.isfinite(o).all() for o in outs)
