@@ -16,6 +16,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -275,6 +276,291 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent bf16 GEMM: one CTA per SM walks a static tile schedule
+// (t = blockIdx.x, += gridDim.x).  Warp 0 streams A/B k-blocks through an
+// S-stage TMA ring that runs continuously across tiles; warp 1 issues
+// tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators, so the
+// epilogue of tile i overlaps the MMAs of tile i+1; warps 2-5 drain TMEM
+// (tcgen05.ld), apply alpha / bias / ReLU, convert, write 32-row x 128-byte
+// chunks into swizzled shared memory and store them with TMA (bulk groups,
+// double-buffered per warp).  With split-K the raw f32 partial sums go to the
+// workspace through the same TMA-store path.
+template <int BN>
+struct PcCfg {
+  static constexpr int A_BYTES = 128 * 128;  // 128 rows x 64 bf16
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024 / STAGE) > 8 ? 8 : (192 * 1024 / STAGE);
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
+};
+
+struct PersArgs {
+  int M, N, K;
+  int a_mn, b_mn;
+  float alpha;
+  const void* bias;
+  int epi;  // 0 none, 1 bias, 2 bias+relu, 3 relu (ignored when out_ws)
+  int tiles_m, tiles_n, batch, splits, kb_per_split, kb_all;
+  int n_fast;  // 1: consecutive tiles step along N (fewer N tiles than M tiles)
+  int out_ws;  // 1: store raw f32 partials to the split-K workspace map
+  int* err;
+};
+
+template <int BN, typename TO>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_pers(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
+                 const __grid_constant__ CUtensorMap tC, PersArgs p) {
+  using Cfg = PcCfg<BN>;
+  constexpr int S = Cfg::STAGES;
+  constexpr int BK = 64;  // bf16 K elements per 128-byte row
+  constexpr int E = 64;   // bf16 MN elements per 128-byte chunk
+  constexpr int A_BYTES = Cfg::A_BYTES;
+  constexpr int B_BYTES = Cfg::B_BYTES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* epi_smem = smem + S * Cfg::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;   // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;  // [2] accumulator drained
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+  auto sA = [&](int s) { return smem + s * Cfg::STAGE; };
+  auto sB = [&](int s) { return smem + s * Cfg::STAGE + A_BYTES; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_mn = p.tiles_m * p.tiles_n;
+  const int num_tiles = tiles_mn * p.batch * p.splits;
+  auto decode = [&](int t, int& m0, int& n0, int& bz, int& ks, int& kb0, int& nkb) {
+    const int bs = t / tiles_mn, r = t - bs * tiles_mn;
+    int mi, ni;
+    if (p.n_fast) {
+      ni = r % p.tiles_n;
+      mi = r / p.tiles_n;
+    } else {
+      mi = r % p.tiles_m;
+      ni = r / p.tiles_m;
+    }
+    m0 = mi * 128;
+    n0 = ni * BN;
+    bz = bs / p.splits;
+    ks = bs - bz * p.splits;
+    kb0 = ks * p.kb_per_split;
+    nkb = max(0, min(p.kb_all, kb0 + p.kb_per_split) - kb0);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tA);
+    tma_prefetch_desc(&tB);
+    tma_prefetch_desc(&tC);
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+        int m0, n0, bz, ks, kb0, nkb;
+        decode(t, m0, n0, bz, ks, kb0, nkb);
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % S, kb = kb0 + i;
+          if (it >= S && !mbar_wait(&empty[s], ((it / S) + 1) & 1, abort, p.err, 111)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+          if (!p.a_mn) {
+            tma_load_3d(sA(s), &tA, &full[s], kb * BK, m0, bz);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 128 / E; ++j)
+              tma_load_3d(sA(s) + j * (BK * 128), &tA, &full[s], m0 + j * E, kb * BK, bz);
+          }
+          if (!p.b_mn) {
+            tma_load_3d(sB(s), &tB, &full[s], kb * BK, n0, bz);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / E; ++j)
+              tma_load_3d(sB(s) + j * (BK * 128), &tB, &full[s], n0 + j * E, kb * BK, bz);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      const uint32_t idesc = umma_idesc(1u, (uint32_t)p.a_mn, (uint32_t)p.b_mn, BN, 128);
+      constexpr uint32_t KSTEP_MN = 16 * 128;  // bytes per K=16 step, MN-major
+      auto adesc = [&](uint32_t base, int kk) {
+        return p.a_mn ? umma_desc(base + kk * KSTEP_MN, BK * 128, 1024)
+                      : umma_desc(base + kk * 32, 16, 1024);
+      };
+      auto bdesc = [&](uint32_t base, int kk) {
+        return p.b_mn ? umma_desc(base + kk * KSTEP_MN, BK * 128, 1024)
+                      : umma_desc(base + kk * 32, 16, 1024);
+      };
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x, ++tl) {
+        int m0, n0, bz, ks, kb0, nkb;
+        decode(t, m0, n0, bz, ks, kb0, nkb);
+        const int acc = tl & 1;
+        if (tl >= 2 && !mbar_wait(&tempty[acc], ((tl >> 1) + 1) & 1, abort, p.err, 112)) break;
+        tc_fence_after();
+        const uint32_t dt = tmem + (uint32_t)(acc * BN);
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort, p.err, 113)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(dt, adesc(a0, kk), bdesc(b0, kk), idesc, (i | kk) != 0);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        if (nkb > 0) umma_commit(&tfull[acc]);
+        else mbar_arrive(&tfull[acc]);
+      }
+    }
+  } else {  // ---- warps 2..5: epilogue
+    using TS = typename std::conditional<std::is_same<TO, float>::value, float, TO>::type;
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    uint8_t* stg = epi_smem + (warp - 2) * 8192;
+    int tl = 0, nstore = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
+      int m0, n0, bz, ks, kb0, nkb;
+      decode(t, m0, n0, bz, ks, kb0, nkb);
+      const int acc = tl & 1;
+      bool ok = mbar_wait(&tfull[acc], (tl >> 1) & 1, abort, p.err, 114);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const int rowbase = m0 + q * 32;
+      const int zc = p.out_ws ? bz * p.splits + ks : bz;
+      if (p.out_ws) {
+        // raw f32 partial sums: 32 columns per 128-byte chunk
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int nc = n0 + c * 32;
+          if (nc >= p.N || rowbase >= p.M) continue;
+          float v[32];
+          if (nkb > 0) {
+            tmem_ld32(trow + (uint32_t)(c * 32), v);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          uint8_t* buf = stg + (nstore & 1) * 4096;
+          if (lane == 0 && nstore >= 2) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tC, buf, nc, rowbase, zc);
+            bulk_commit_group();
+          }
+          ++nstore;
+        }
+      } else {
+        constexpr int CW = 128 / (int)sizeof(TO);  // output columns per 128-byte chunk
+#pragma unroll 1
+        for (int c = 0; c < BN / CW; ++c) {
+          const int nc = n0 + c * CW;
+          if (nc >= p.N || rowbase >= p.M) continue;
+          float v[CW];
+          if (nkb > 0) {
+            tmem_ld32(trow + (uint32_t)(c * CW), v);
+            if (CW == 64) tmem_ld32(trow + (uint32_t)(c * CW + 32), v + 32);
+          } else {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) v[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < CW; ++j) {
+            float x = v[j] * p.alpha;
+            if (p.epi == 1 || p.epi == 2) {
+              const int n = nc + j;
+              x += n < p.N ? load_bias<TO>(p.bias, n) : 0.f;
+            }
+            if (p.epi >= 2) x = fmaxf(x, 0.f);
+            v[j] = x;
+          }
+          uint8_t* buf = stg + (nstore & 1) * 4096;
+          if (lane == 0 && nstore >= 2) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            uint4 w;
+            if (sizeof(TO) == 4) {
+              w = make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                             __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
+            } else {
+              auto pk = [&](int j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(v[j], v[j + 1]);
+                return *reinterpret_cast<uint32_t*>(&h);
+              };
+              w = make_uint4(pk(8 * u), pk(8 * u + 2), pk(8 * u + 4), pk(8 * u + 6));
+            }
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) = w;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tC, buf, nc, rowbase, zc);
+            bulk_commit_group();
+          }
+          ++nstore;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && threadIdx.x == 0) {
+    // let TMA copies already in flight land before the CTA's shared memory goes away
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
 // SIMT fallback: 64x64 tile, 256 threads, 4x4 outputs per thread, f32 FMA.
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(256)
@@ -485,6 +771,115 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   return B200_OK;
 }
 
+// Persistent bf16 launch.  Returns B200_ERR_UNSUPPORTED (without launching)
+// when the output cannot be stored with TMA (unaligned base or row pitch), so
+// the caller can fall back to gemm_tc.
+template <int BN, typename TO>
+int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
+                int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
+                int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn,
+                cudaStream_t st, Scratch& scratch) {
+  constexpr int ES = 2, BK = 64, E = 64;
+  const int tiles_m = (int)((M + 127) / 128), tiles_n = (int)((N + BN - 1) / BN);
+  const int KB_all = (int)((K + BK - 1) / BK);
+  const SplitPlan sp = plan_splits((int64_t)tiles_m * tiles_n * batch, KB_all, 4, batch);
+  const bool ws = sp.splits > 1;
+  const int so = ws ? 4 : (int)sizeof(TO);
+  if (ws ? (N * 4) % 16 != 0
+         : (((uintptr_t)c & 15) != 0 || (ldc * so) % 16 != 0 || (batch > 1 && ((M * ldc * so) % 16) != 0)))
+    return B200_ERR_UNSUPPORTED;
+  auto bstride = [&](int64_t s, int64_t outer_stride, int64_t outer_dim) -> uint64_t {
+    const int64_t v = batch == 1 ? outer_stride * outer_dim : s;
+    return (uint64_t)(((v * ES) + 15) / 16 * 16);
+  };
+  CUtensorMap ta, tb, tc;
+  int rc;
+  if (!a_mn) {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sAm * ES), bstride(sAb, sAm, M)};
+    uint32_t box[3] = {(uint32_t)BK, 128, 1};
+    rc = make_tmap(&ta, a, 3, dims, str, box, ES);
+  } else {
+    uint64_t dims[3] = {(uint64_t)M, (uint64_t)K, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sAk * ES), bstride(sAb, sAk, K)};
+    uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
+    rc = make_tmap(&ta, a, 3, dims, str, box, ES);
+  }
+  if (rc) return rc;
+  if (!b_mn) {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sBn * ES), bstride(sBb, sBn, N)};
+    uint32_t box[3] = {(uint32_t)BK, (uint32_t)BN, 1};
+    rc = make_tmap(&tb, b, 3, dims, str, box, ES);
+  } else {
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sBk * ES), bstride(sBb, sBk, K)};
+    uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
+    rc = make_tmap(&tb, b, 3, dims, str, box, ES);
+  }
+  if (rc) return rc;
+  PersArgs p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.alpha = alpha;
+  p.bias = bias;
+  p.epi = epi;
+  p.tiles_m = tiles_m;
+  p.tiles_n = tiles_n;
+  p.batch = (int)batch;
+  p.splits = sp.splits;
+  p.kb_per_split = sp.per_split;
+  p.kb_all = KB_all;
+  p.n_fast = tiles_n <= tiles_m ? 1 : 0;
+  p.out_ws = ws ? 1 : 0;
+  p.err = scratch.err ? scratch.err : device_error_word();
+  if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
+  float* wsp = nullptr;
+  if (ws) {
+    if (int rc2 = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &wsp)) return rc2;
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)(batch * sp.splits)};
+    uint64_t str[2] = {(uint64_t)(N * 4), (uint64_t)(M * N * 4)};
+    uint32_t box[3] = {32, 32, 1};
+    rc = make_tmap(&tc, wsp, 3, dims, str, box, 4);
+  } else {
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)batch};
+    const int64_t sc = batch == 1 ? M * ldc : M * ldc;
+    uint64_t str[2] = {(uint64_t)(ldc * so), (uint64_t)(((sc * so) + 15) / 16 * 16)};
+    uint32_t box[3] = {(uint32_t)(128 / so), 32, 1};
+    rc = make_tmap(&tc, c, 3, dims, str, box, so);
+  }
+  if (rc) return rc;
+  const int smem = PcCfg<BN>::SMEM;
+  static bool attr = [&] {
+    return cudaFuncSetAttribute(gemm_tc_pers<BN, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                smem) == cudaSuccess;
+  }();
+  if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(gemm_tc_pers) failed");
+  const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch * sp.splits;
+  const unsigned grid = (unsigned)std::min<int64_t>(num_tiles, num_sms());
+  gemm_tc_pers<BN, TO><<<grid, 192, smem, st>>>(ta, tb, tc, p);
+  B200_LAUNCH_CHECK();
+  if (ws) {
+    const int64_t total = batch * M * N;
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    splitk_reduce<TO><<<blocks, 256, 0, st>>>(wsp, (TO*)c, bias, (int)batch, (int)M, (int)N,
+                                              sp.splits, ldc, M * ldc, alpha, epi);
+    B200_LAUNCH_CHECK();
+  }
+  return B200_OK;
+}
+
+bool use_persistent() {
+  static bool on = [] {
+    const char* v = std::getenv("B200_GEMM_PERSISTENT");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
 template <typename TI, typename TO>
 int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
                 int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
@@ -575,6 +970,17 @@ int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64
       if (bn64) { if (obf) B200_TC(64, 4, __nv_bfloat16, false); else B200_TC(64, 4, float, false); }
       if (obf) B200_TC(128, 4, __nv_bfloat16, false); else B200_TC(128, 4, float, false);
     } else {
+      if (use_persistent()) {
+        int prc;
+#define B200_PERS(BN_, TO_)                                                                       \
+  prc = launch_pers<BN_, TO_>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,  \
+                              alpha, epilogue, a_mn, b_mn, st, scratch)
+        if (N <= 64) { if (obf) B200_PERS(64, __nv_bfloat16); else B200_PERS(64, float); }
+        else if (N <= 128) { if (obf) B200_PERS(128, __nv_bfloat16); else B200_PERS(128, float); }
+        else { if (obf) B200_PERS(256, __nv_bfloat16); else B200_PERS(256, float); }
+#undef B200_PERS
+        if (prc != B200_ERR_UNSUPPORTED) return prc;
+      }
       if (bn64) { if (obf) B200_TC(64, 2, __nv_bfloat16, false); else B200_TC(64, 2, float, false); }
       if (obf) B200_TC(128, 2, __nv_bfloat16, false); else B200_TC(128, 2, float, false);
     }

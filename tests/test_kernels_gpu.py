@@ -176,7 +176,7 @@ def test_sdpa_bnth_strides_and_simt_fallback():
 
 
 # ----------------------------------------------------------------------- GEMM
-def _gemm_case(M, N, K, a_t, b_t, dt, batch=1, epi=0, seed=0):
+def _gemm_case(M, N, K, a_t, b_t, dt, batch=1, epi=0, seed=0, out_dt=None):
     rng = np.random.default_rng(seed)
     a = rng.standard_normal((batch, M, K)).astype(np.float32)
     b = rng.standard_normal((batch, K, N)).astype(np.float32)
@@ -190,16 +190,17 @@ def _gemm_case(M, N, K, a_t, b_t, dt, batch=1, epi=0, seed=0):
         b = host(Bm) if not b_t else np.swapaxes(host(Bm), 1, 2)
     sAb, sAm, sAk = M * K, (1 if a_t else K), (M if a_t else 1)
     sBb, sBk, sBn = K * N, (1 if b_t else N), (K if b_t else 1)
-    out_t = torch.bfloat16 if dt == kernels.DT_BF16 else torch.float32
+    out_dt = dt if out_dt is None else out_dt
+    out_t = torch.bfloat16 if out_dt == kernels.DT_BF16 else torch.float32
     C = torch.empty((batch, M, N), device="cuda", dtype=out_t)
-    BIAS = conv(bias)
+    BIAS = (bf16_dev if out_dt == kernels.DT_BF16 else dev)(bias)  # bias has the output's type
     tc = kernels.gemm_uses_tensor_cores(A.data_ptr(), Bm.data_ptr(), batch, K, sAb, sAm, sAk, sBb,
                                         sBk, sBn, dt)
     kernels.gemm(A.data_ptr(), Bm.data_ptr(), C.data_ptr(), BIAS.data_ptr(), batch, M, N, K, sAb, sAm,
-                 sAk, sBb, sBk, sBn, N, 1.0, dt, dt, epi, stream())
+                 sAk, sBb, sBk, sBn, N, 1.0, dt, out_dt, epi, stream())
     ref = np.einsum("bmk,bkn->bmn", a.astype(np.float64), b.astype(np.float64))
     if epi in (1, 2):
-        ref = ref + (host(BIAS) if dt == kernels.DT_BF16 else bias)
+        ref = ref + host(BIAS)
     if epi >= 2:
         ref = np.maximum(ref, 0)
     return host(C), ref, tc
@@ -253,3 +254,30 @@ def test_gemm_simt_fallback_for_unaligned_rows():
     got, ref, tc = _gemm_case(33, 17, 9, True, False, kernels.DT_F32, seed=10)
     assert not tc
     assert_close(got, ref, 1e-5, "simt odd")
+
+
+# bf16 operands take the persistent kernel (two TMEM accumulators, TMA-store
+# epilogue); these cover its tile edges, MN-major operands, f32 and bf16
+# outputs, epilogues, batching and split-K.
+@pytest.mark.parametrize("M,N,K,a_t,b_t,out_f32", [
+    (1024, 2048, 512, False, False, False),    # FFN up
+    (520, 776, 264, False, True, True),        # ragged edges, B transposed, f32 out
+    (256, 512, 4096, True, False, False),      # weight-gradient form, split-K
+    (300, 96, 192, True, True, True),          # BN 128, both transposed
+    (4096, 64, 256, False, False, False),      # BN 64
+])
+def test_gemm_bf16_persistent(M, N, K, a_t, b_t, out_f32):
+    if a_t and M % 8:
+        M += 8 - M % 8  # an MN-major bf16 A needs 16-byte rows
+    out = kernels.DT_F32 if out_f32 else kernels.DT_BF16
+    got, ref, tc = _gemm_case(M, N, K, a_t, b_t, kernels.DT_BF16, seed=M + N, out_dt=out)
+    assert tc
+    assert_close(got, ref, 1e-2, f"bf16 gemm {M}x{N}x{K}")
+
+
+def test_gemm_bf16_persistent_batched_epilogues():
+    for epi in (1, 2, 3):
+        got, ref, tc = _gemm_case(256, 256, 64, False, True, kernels.DT_BF16, batch=12, epi=epi,
+                                  seed=40 + epi, out_dt=kernels.DT_F32)
+        assert tc
+        assert_close(got, ref, 1e-2, f"bf16 batched epi {epi}")
