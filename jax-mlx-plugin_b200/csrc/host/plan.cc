@@ -145,7 +145,47 @@ struct Builder {
         return true;
       }
     if (u.count(n) <= 1) return false;
-    return !is_cheap(nd);
+    if (is_cheap(nd)) return false;
+    // A value with a few consumers is recomputed inside each of them when its
+    // fused expression is small: on HBM-bound kernels re-reading the inputs
+    // (often narrower, e.g. bf16 logits) beats writing and re-reading an f32
+    // intermediate.  Consumers that read each element several times (windows,
+    // im2col, gathers, broadcasts) keep it materialized.
+    if (u.count(n) <= 4 && !amplified(n)) {
+      std::set<int> seen;
+      if (expr_cost(n, seen) <= kRecomputeOps) return false;
+    }
+    return true;
+  }
+  static constexpr int kRecomputeOps = 8;
+  // Non-cheap ops in n's fused expression, shared subexpressions counted once,
+  // stopping at values that live in memory.
+  int expr_cost(int n, std::set<int>& seen) {
+    if (seen.count(n) || slot.count(ValueRef{n, 0})) return 0;
+    seen.insert(n);
+    const Node& nd = g.nodes[n];
+    if (!is_fusible(nd.op)) return 0;
+    int c = is_cheap(nd) ? 0 : 1;
+    for (const auto& o : nd.operands) {
+      c += expr_cost(o.node, seen);
+      if (c > kRecomputeOps) break;
+    }
+    return c;
+  }
+  bool amplified(int n) {
+    const int64_t size = g.nodes[n].results[0].numel();
+    for (int c : u.users[n]) {
+      const Node& cn = g.nodes[c];
+      switch (cn.op) {
+        case Op::ReduceWindow: case Op::SelectAndScatter: case Op::Gather: case Op::Scatter:
+        case Op::Convolution: case Op::Pad: case Op::Concatenate:
+          return true;
+        default:
+          break;
+      }
+      if (cn.op != Op::Reduce && !cn.results.empty() && cn.results[0].numel() > size) return true;
+    }
+    return false;
   }
 
   // Split a reduction over several blocks when its outputs alone would leave
@@ -464,6 +504,23 @@ struct Builder {
     }
   }
 
+  std::vector<int> pending;  // materialized loop values not yet emitted
+  void flush_loops() {
+    if (pending.empty()) return;
+    std::vector<ValueRef> roots;
+    std::vector<int> outs;
+    for (int n : pending) {
+      roots.push_back(ValueRef{n, 0});
+      outs.push_back(slot.at(ValueRef{n, 0}));
+    }
+    // hide the slots so the kernel computes the values instead of loading them
+    for (auto& r : roots) slot.erase(r);
+    GenKernel k = cg.loop(roots, outs);
+    for (size_t i = 0; i < roots.size(); ++i) slot[roots[i]] = outs[i];
+    pending.clear();
+    add_kernel(std::move(k));
+  }
+
   // -------------------------------------------------------------- driver --
   void run() {
     auto order = topo();
@@ -495,14 +552,18 @@ struct Builder {
       }
       if (is_fusible(nd.op)) {
         if (!must_materialize(n)) continue;
-        int s = temp_for(ValueRef{n, 0});
-        // temporarily hide the slot so the kernel computes the value instead of loading it
-        slot.erase(ValueRef{n, 0});
-        GenKernel k = cg.loop({ValueRef{n, 0}}, {s});
-        slot[ValueRef{n, 0}] = s;
-        add_kernel(std::move(k));
+        // Loop outputs of one shape are emitted together: one kernel computes
+        // them all (e.g. an optimizer's new parameter and both moments, or
+        // every same-shaped parameter's update), sharing loads and
+        // subexpressions.  Any other kernel flushes the group first.
+        if (!pending.empty() &&
+            (g.nodes[pending[0]].results[0].dims != nd.results[0].dims || pending.size() >= 24))
+          flush_loops();
+        temp_for(ValueRef{n, 0});
+        pending.push_back(n);
         continue;
       }
+      flush_loops();
       switch (nd.op) {
         case Op::Reduce: {
           std::vector<int> outs;
@@ -564,6 +625,7 @@ struct Builder {
           throw PjrtErr(12, std::string("op ") + op_name(nd.op) + " is not supported by the B200 plugin");
       }
     }
+    flush_loops();
     // outputs
     std::set<int> used;
     for (size_t i = 0; i < g.outputs.size(); ++i) {
