@@ -56,10 +56,19 @@ class CodeGen {
   int counter = 0;
 
  private:
+  // An element index: row-major linear form (lin) and/or per-dimension form
+  // (multi), as C expressions.  Vector form (lane >= 0): the index is element
+  // `lane` of a group of vec_ consecutive elements along the innermost
+  // dimension -- lin == lin_base + lane with lin_base a multiple of vec_, and
+  // multi.back() == inner_base + lane with the other entries lane-independent.
+  // Loads of slots through a vector-form index become one 16-byte (or 8/32)
+  // load per group, shared by the group's lanes.
   struct Idx {
     std::vector<int64_t> dims;
     std::string lin;
     std::vector<std::string> multi;
+    int lane = -1;
+    std::string lin_base, inner_base;
   };
   const Graph& g_;
   const std::vector<Slot>& slots_;
@@ -74,6 +83,7 @@ class CodeGen {
   // f32 and are rounded once when stored (XLA accumulates bf16 reductions in
   // f32 rather than rounding after every add).
   bool accum_f32_ = false;
+  int vec_ = 1;  // elements per thread group in vector-form kernels
   int tmp_ = 0;
   int indent_ = 1;
   std::string idx_t_ = "int";
@@ -86,6 +96,9 @@ class CodeGen {
   void ensure_lin(Idx& idx);
   std::string value(ValueRef v, Idx idx);
   std::string load(int slot, Idx& idx, DType dt);
+  Idx vec_idx(const std::vector<int64_t>& dims, const std::string& base, int lane);
+  void vec_load(const std::string& dst, int slot, const std::string& base);
+  void vec_store(int slot, const std::string& base, const std::vector<std::string>& vals, DType dt);
   std::string elementwise(const Node& n, const std::vector<std::string>& a, DType in_dt);
   std::string literal(const Node& n);
   std::string emit_region(const Graph& r, const std::vector<std::string>& args,
