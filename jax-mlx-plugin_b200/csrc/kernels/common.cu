@@ -18,6 +18,8 @@ extern "C" const char* b200_kernels_version(void) { return "b200-kernels 0.1.0 s
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <set>
+#include <string>
 
 #include "tc.cuh"
 
@@ -55,6 +57,19 @@ int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(B200_ERR_INVALID, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return B200_OK;
+}
+
+int allow_dynamic_smem(const void* fn, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;  // (kernel, device)
+  int dev = 0;
+  B200_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count({fn, dev})) return B200_OK;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return set_error(B200_ERR_CUDA, std::string("cudaFuncSetAttribute(") + what + ") failed");
+  done.insert({fn, dev});
   return B200_OK;
 }
 

@@ -744,11 +744,7 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   p.err = scratch.err ? scratch.err : device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   const int smem = TcCfg<BN, ES, SPLIT>::SMEM;
-  static bool attr = [&] {
-    return cudaFuncSetAttribute(gemm_tc<BN, ES, TO, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                smem) == cudaSuccess;
-  }();
-  if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(gemm_tc) failed");
+  if (int rc2 = allow_dynamic_smem((const void*)gemm_tc<BN, ES, TO, SPLIT>, smem, "gemm_tc")) return rc2;
   const int64_t gx = (N + BN - 1) / BN, gy = (M + 127) / 128;
   const int KB_all = (int)((K + BK - 1) / BK);
   const SplitPlan sp = plan_splits(gx * gy * batch, KB_all, 4, batch);
@@ -853,11 +849,7 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   }
   if (rc) return rc;
   const int smem = PcCfg<BN>::SMEM;
-  static bool attr = [&] {
-    return cudaFuncSetAttribute(gemm_tc_pers<BN, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                smem) == cudaSuccess;
-  }();
-  if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(gemm_tc_pers) failed");
+  if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pers<BN, TO>, smem, "gemm_tc_pers")) return rc2;
   const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch * sp.splits;
   const unsigned grid = (unsigned)std::min<int64_t>(num_tiles, num_sms());
   gemm_tc_pers<BN, TO><<<grid, 192, smem, st>>>(ta, tb, tc, p);

@@ -602,9 +602,7 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, int64_t B, i
   a.o_sn = st[11];
   a.err = device_error_word();
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
-  static bool attr = cudaFuncSetAttribute(sdpa_fwd_tc<ES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          C::SMEM) == cudaSuccess;
-  if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(sdpa_fwd_tc) failed");
+  if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_tc<ES>, C::SMEM, "sdpa_fwd_tc")) return rc;
   dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
   sdpa_fwd_tc<ES><<<grid, 128, C::SMEM, s>>>(tq, tk, tv, a);
   B200_LAUNCH_CHECK();
@@ -641,9 +639,7 @@ int launch_x3(const void* q, const void* k, const void* v, void* o, int64_t B, i
   a.o_sn = st[11];
   a.err = device_error_word();
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
-  static bool attr = cudaFuncSetAttribute(sdpa_fwd_tc_x3, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          X3Cfg::SMEM) == cudaSuccess;
-  if (!attr) return set_error(B200_ERR_CUDA, "cudaFuncSetAttribute(sdpa_fwd_tc_x3) failed");
+  if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_tc_x3, X3Cfg::SMEM, "sdpa_fwd_tc_x3")) return rc;
   dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
   sdpa_fwd_tc_x3<<<grid, 128, X3Cfg::SMEM, s>>>(tq, tk, tv, a);
   B200_LAUNCH_CHECK();

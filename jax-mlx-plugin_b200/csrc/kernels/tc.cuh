@@ -1,5 +1,5 @@
 // Blackwell (sm_100a) building blocks in inline PTX: mbarriers with bounded
-// waits, TMA tensor loads (no multicast), tcgen05 TMEM allocation, MMA issue,
+// waits, TMA tensor loads (each into its own CTA), tcgen05 TMEM allocation, MMA issue,
 // commit and TMEM loads, and the UMMA shared-memory / instruction descriptors.
 #pragma once
 #include <cuda.h>
@@ -84,7 +84,7 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "r"(smem_u32(bar))
       : "memory");
 }
-// Shared -> global tensor store (bulk-group completion; no multicast).
+// Shared -> global tensor store (bulk-group completion).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1,
                                              int c2) {
   asm volatile(
@@ -213,6 +213,9 @@ int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
               bool atom32 = false);
 // Per-device error word passed to kernels with bounded waits (zeroed once).
 int* device_error_word();
+// Opt `fn` into `bytes` of dynamic shared memory on the current device (once
+// per kernel and device; the attribute is per device).
+int allow_dynamic_smem(const void* fn, int bytes, const char* what);
 // The allocation-free GEMM's error word on the current device (gemm.cu):
 // its value, -1 on a CUDA error; cleared when `clear` is set.
 int noalloc_error_take(int clear);
