@@ -520,6 +520,437 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialized attention forward, head dim 64, key blocks of 64.
+//
+// One CTA = 128 query rows of one (batch, head), 320 threads in four roles:
+//   warps 0-3  softmax: one query row per thread; read S_j from TMEM, online
+//              max / sum in f32, write P_j to shared memory, then fold the
+//              previous block's P V product (TMEM) into the f32 row of O held in
+//              registers;
+//   warp 4     TMA: Q once, then K_j / V_j into a two-slot ring;
+//   warp 5     MMA issue: S_j = Q K_j^T into one of two TMEM S buffers, then
+//              O_{j-1} = P_{j-1} V_{j-1} into one of two TMEM O buffers, so the
+//              tensor core works on block j while the softmax warps work on j-1;
+//   warps 6-9  (f32 inputs) split each f32 tile into bf16 hi and lo parts.
+// f32 inputs run every product as three bf16 MMAs, hi*hi + hi*lo + lo*hi
+// (the dropped lo*lo term is ~2^-16 relative), on Q, K, V and P; bf16 inputs
+// run one.  All shared-memory operand tiles are 128-byte rows with the 16-byte
+// unit swizzle (unit ^ row % 8): K-major for Q, K and P, MN-major for V.
+template <bool X3>
+struct WsCfg {
+  static constexpr int QB = 128 * 128;   // bf16 Q tile: 128 rows x 128 B
+  static constexpr int KB = 64 * 128;    // bf16 K or V tile: 64 keys x 128 B
+  static constexpr int PB = 128 * 128;   // bf16 P tile: 128 rows x 64 keys
+  static constexpr int PARTS = X3 ? 2 : 1;
+  static constexpr int Q_OFF = 0;                                  // Q hi [, lo]
+  static constexpr int KV_OFF = Q_OFF + PARTS * QB;                // slot s: K hi, [K lo,] V hi [, V lo]
+  static constexpr int KV_SLOT = 2 * PARTS * KB;
+  static constexpr int P_OFF = KV_OFF + 2 * KV_SLOT;               // slot s: P hi [, P lo]
+  static constexpr int P_SLOT = PARTS * PB;
+  static constexpr int ST_OFF = P_OFF + 2 * P_SLOT;                // f32 staging (X3): K, V of one block
+  static constexpr int ST_BYTES = X3 ? 2 * 64 * 256 : 0;
+  static constexpr int QST_OFF = P_OFF;                            // f32 Q staging aliases the P slots
+  static constexpr int RED_OFF = ST_OFF + ST_BYTES;                // softmax max / sum exchange
+  static constexpr int BAR_OFF = RED_OFF + 2 * 2 * 128 * 4;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// Split 4 f32 into bf16 hi (rounded) and lo (rounded residual), 8 bytes each.
+__device__ __forceinline__ void split4(float4 x, uint2& hi, uint2& lo) {
+  __nv_bfloat162 h0 = __floats2bfloat162_rn(x.x, x.y), h1 = __floats2bfloat162_rn(x.z, x.w);
+  const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+  hi = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+  lo = make_uint2(pack_bf16x2(x.x - f0.x, x.y - f0.y), pack_bf16x2(x.z - f1.x, x.w - f1.y));
+}
+// f32 staging tile (rows x 64, two 128-byte-swizzled chunks of 32 columns,
+// chunk c at c * rows * 128) -> bf16 hi / lo tiles (rows x 128 B, swizzled).
+__device__ __forceinline__ void split_rows(const uint8_t* st, uint8_t* hi, uint8_t* lo, int rows,
+                                           int ctid) {
+  for (int f = ctid; f < rows * 16; f += 128) {
+    const int r = f >> 4, c = (f >> 3) & 1, u = f & 7;
+    const float4 x = *reinterpret_cast<const float4*>(st + c * rows * 128 + r * 128 + ((u ^ (r & 7)) << 4));
+    uint2 h, l;
+    split4(x, h, l);
+    const int U = c * 4 + (u >> 1);
+    const int off = r * 128 + ((U ^ (r & 7)) << 4) + (u & 1) * 8;
+    *reinterpret_cast<uint2*>(hi + off) = h;
+    *reinterpret_cast<uint2*>(lo + off) = l;
+  }
+}
+
+// Thread roles (448 threads): warps 0-7 softmax (warp w owns TMEM lane quarter
+// w % 4, i.e. 32 query rows, and key / head-dim half w / 4), warp 8 TMA, warp 9
+// MMA issue, warps 10-13 f32 split.
+constexpr int kWsThreads = 448;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool X3>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    sdpa_fwd_ws(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
+                const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
+  using C = WsCfg<X3>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* q_hi = smem + C::Q_OFF;
+  uint8_t* q_lo = q_hi + C::QB;
+  auto k_hi = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT; };
+  auto k_lo = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + C::KB; };
+  auto v_hi = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + C::PARTS * C::KB; };
+  auto v_lo = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + 3 * C::KB; };
+  auto p_hi = [&](int s) { return smem + C::P_OFF + s * C::P_SLOT; };
+  auto p_lo = [&](int s) { return smem + C::P_OFF + s * C::P_SLOT + C::PB; };
+  uint8_t* k_st = smem + C::ST_OFF;
+  uint8_t* v_st = smem + C::ST_OFF + 64 * 256;
+  uint8_t* q_st = smem + C::QST_OFF;
+  float* red = reinterpret_cast<float*>(smem + C::RED_OFF);  // [2 block parities][2 halves][128 rows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_ready = bars + 1;
+  uint64_t* kv_full = bars + 2;   // [2]
+  uint64_t* kv_conv = bars + 4;   // [2]
+  uint64_t* kv_free = bars + 6;   // [2]
+  uint64_t* s_full = bars + 8;    // [2]
+  uint64_t* s_free = bars + 10;   // [2]
+  uint64_t* p_full = bars + 12;   // [2]
+  uint64_t* o_full = bars + 14;   // [2]
+  uint64_t* ob_free = bars + 16;  // [2]
+  uint64_t* mx_bar = bars + 18;   // [4 quarters][2]: both halves' block maxima written
+  uint64_t* l_bar = bars + 26;    // [4 quarters]: both halves' row sums written
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 30);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nq = (p.T + 127) / 128;
+  const int qt = p.causal ? nq - 1 - (int)blockIdx.x : (int)blockIdx.x;
+  const int n = blockIdx.y, b = blockIdx.z;
+  const int t0 = qt * 128;
+  const int nkb_all = (p.S + 63) / 64;
+  const int nkb = p.causal ? min(nkb_all, (t0 + 127) / 64 + 1) : nkb_all;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_conv[i], 4);
+      mbar_init(&kv_free[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 8);
+      mbar_init(&p_full[i], 8);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&ob_free[i], 8);
+    }
+    for (int i = 0; i < 8; ++i) mbar_init(&mx_bar[i], 2);
+    for (int i = 0; i < 4; ++i) mbar_init(&l_bar[i], 2);
+    *abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  // TMEM columns: S buffers at 0 and 64, O buffers at 128 and 192 (f32, 64 wide)
+  auto tS = [&](int s) { return tmem + (uint32_t)(s * 64); };
+  auto tO = [&](int s) { return tmem + 128u + (uint32_t)(s * 64); };
+
+  if (warp == 8) {
+    if (lane == 0 && nkb > 0) {  // ---- TMA producer
+      tma_prefetch_desc(&tQ);
+      tma_prefetch_desc(&tK);
+      tma_prefetch_desc(&tV);
+      if (X3) {
+        mbar_expect_tx(q_full, 128 * 64 * 4);
+        for (int c = 0; c < 2; ++c) tma_load_4d(q_st + c * 128 * 128, &tQ, q_full, c * 32, n, t0, b);
+      } else {
+        mbar_expect_tx(q_full, 128 * 64 * 2);
+        tma_load_4d(q_hi, &tQ, q_full, 0, n, t0, b);
+      }
+      for (int j = 0; j < nkb; ++j) {
+        const int s = j & 1, use = j >> 1;
+        if (X3) {
+          // one f32 staging buffer: block j may land once block j-1 has been split
+          if (j >= 1 && !mbar_wait(&kv_conv[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, p.err, 211)) break;
+          mbar_expect_tx(&kv_full[0], 2 * 64 * 64 * 4);
+          for (int c = 0; c < 2; ++c) {
+            tma_load_4d(k_st + c * 64 * 128, &tK, &kv_full[0], c * 32, n, j * 64, b);
+            tma_load_4d(v_st + c * 64 * 128, &tV, &kv_full[0], c * 32, n, j * 64, b);
+          }
+        } else {
+          if (j >= 2 && !mbar_wait(&kv_free[s], (use - 1) & 1, abort, p.err, 211)) break;
+          mbar_expect_tx(&kv_full[s], 2 * 64 * 64 * 2);
+          tma_load_4d(k_hi(s), &tK, &kv_full[s], 0, n, j * 64, b);
+          tma_load_4d(v_hi(s), &tV, &kv_full[s], 0, n, j * 64, b);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0 && nkb > 0) {  // ---- MMA issuer
+      constexpr uint32_t idesc_s = umma_idesc(1u, 0, 0, 64, 128);
+      constexpr uint32_t idesc_o = umma_idesc(1u, 0, 1, 64, 128);
+      bool ok = mbar_wait(X3 ? q_ready : q_full, 0, abort, p.err, 212);
+      for (int j = 0; ok && j <= nkb; ++j) {
+        if (j < nkb) {
+          const int s = j & 1, use = j >> 1;
+          ok = mbar_wait(X3 ? &kv_conv[s] : &kv_full[s], use & 1, abort, p.err, 213);
+          if (ok && j >= 2) ok = mbar_wait(&s_free[s], (use - 1) & 1, abort, p.err, 214);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t qh = smem_u32(q_hi), ql = smem_u32(q_lo);
+          const uint32_t kh = smem_u32(k_hi(s)), kl = smem_u32(k_lo(s));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t off = kk * 32;
+            umma_f16(tS(s), umma_desc(qh + off, 16, 1024), umma_desc(kh + off, 16, 1024), idesc_s, kk != 0);
+            if (X3) {
+              umma_f16(tS(s), umma_desc(qh + off, 16, 1024), umma_desc(kl + off, 16, 1024), idesc_s, 1);
+              umma_f16(tS(s), umma_desc(ql + off, 16, 1024), umma_desc(kh + off, 16, 1024), idesc_s, 1);
+            }
+          }
+          umma_commit(&s_full[s]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, s1 = jj & 1, use1 = jj >> 1;
+          ok = mbar_wait(&p_full[s1], use1 & 1, abort, p.err, 215);
+          if (ok && jj >= 2) ok = mbar_wait(&ob_free[s1], (use1 - 1) & 1, abort, p.err, 216);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t ph = smem_u32(p_hi(s1)), pl = smem_u32(p_lo(s1));
+          const uint32_t vh = smem_u32(v_hi(s1)), vl = smem_u32(v_lo(s1));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            // P: K-major, 16 keys = 32 bytes; V: MN-major, 16 keys = 16 rows of 128 B
+            const uint32_t pa = kk * 32, vb = kk * 2048;
+            umma_f16(tO(s1), umma_desc(ph + pa, 16, 1024), umma_desc(vh + vb, 8192, 1024), idesc_o, kk != 0);
+            if (X3) {
+              umma_f16(tO(s1), umma_desc(ph + pa, 16, 1024), umma_desc(vl + vb, 8192, 1024), idesc_o, 1);
+              umma_f16(tO(s1), umma_desc(pl + pa, 16, 1024), umma_desc(vh + vb, 8192, 1024), idesc_o, 1);
+            }
+          }
+          umma_commit(&o_full[s1]);
+          umma_commit(&kv_free[s1]);
+        }
+      }
+    }
+  } else if (warp >= 10) {
+    if (X3 && nkb > 0) {  // ---- f32 -> bf16 hi/lo split
+      const int ctid = tid - 320;
+      bool ok = mbar_wait(q_full, 0, abort, p.err, 217);
+      if (__all_sync(0xffffffffu, ok)) {
+        split_rows(q_st, q_hi, q_lo, 128, ctid);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(q_ready);
+        for (int j = 0; j < nkb; ++j) {
+          const int s = j & 1, use = j >> 1;
+          ok = mbar_wait(&kv_full[0], j & 1, abort, p.err, 218);
+          if (ok && j >= 2) ok = mbar_wait(&kv_free[s], (use - 1) & 1, abort, p.err, 219);
+          if (!__all_sync(0xffffffffu, ok)) break;
+          split_rows(k_st, k_hi(s), k_lo(s), 64, ctid);
+          split_rows(v_st, v_hi(s), v_lo(s), 64, ctid);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&kv_conv[s]);
+        }
+      }
+    }
+  } else {  // ---- warps 0-7: softmax and output
+    const int q = warp & 3, h = warp >> 2;  // TMEM lane quarter, key / head-dim half
+    const int row = q * 32 + lane;
+    const int t = t0 + row;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const float sl2 = p.scale * 1.4426950408889634f;  // scale * log2(e)
+    float o[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, m_acc = -INFINITY;
+    float m_hist0 = -INFINITY, m_hist1 = -INFINITY;
+    bool ok = true;
+    auto fold = [&](int jj) {  // o = o * 2^(m_acc - m_jj) + (P_jj V_jj)[this half]
+      const int s1 = jj & 1;
+      bool w = mbar_wait(&o_full[s1], (jj >> 1) & 1, abort, p.err, 220);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      const float mj = s1 ? m_hist1 : m_hist0;
+      const float a = m_acc == -INFINITY ? 0.f : ex2(m_acc - mj);
+      float v[32];
+      tmem_ld32(tO(s1) + lane_base + h * 32, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ob_free[s1]);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], a, v[i]);
+      m_acc = mj;
+      return true;
+    };
+    for (int j = 0; j < nkb; ++j) {
+      const int s = j & 1, use = j >> 1;
+      bool w = mbar_wait(&s_full[s], use & 1, abort, p.err, 221);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      float v[32];
+      tmem_ld32(tS(s) + lane_base + h * 32, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[s]);  // S_j is in registers
+      const int kbase = j * 64 + h * 32;
+      const bool need_mask = kbase + 32 > p.S || (p.causal && kbase + 31 > t0);
+      if (need_mask) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = kbase + i;
+          if (key >= p.S || (p.causal && key > t)) v[i] = -INFINITY;
+        }
+      }
+      float bmax = v[0];
+#pragma unroll
+      for (int i = 1; i < 32; ++i) bmax = fmaxf(bmax, v[i]);
+      // row max over both halves: exchange through shared memory; the mbarrier
+      // of this quarter and block parity completes once both warps have written
+      // (a later reuse of the buffer happens only after the partner's next
+      // arrival, i.e. after it has read this one)
+      float* rb = red + (j & 1) * 256;
+      rb[h * 128 + row] = bmax;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mx_bar[q * 2 + s]);
+      w = mbar_wait(&mx_bar[q * 2 + s], use & 1, abort, p.err, 222);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      bmax = fmaxf(rb[row], rb[128 + row]);
+      const float m_new = fmaxf(m_run, bmax * sl2);
+      const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - m_new);
+      const float mo = m_new == -INFINITY ? 0.f : m_new;
+      float lsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float e = ex2(fmaf(v[i], sl2, -mo));  // masked: 2^-inf = 0
+        v[i] = e;
+        lsum += e;
+      }
+      uint8_t* ph = p_hi(s);
+      uint8_t* pl = p_lo(s);
+#pragma unroll
+      for (int u4 = 0; u4 < 4; ++u4) {
+        const int U = h * 4 + u4;
+        const int off = row * 128 + ((U ^ (row & 7)) << 4);
+        if (X3) {
+          uint2 h0, l0, h1, l1;
+          split4(make_float4(v[8 * u4], v[8 * u4 + 1], v[8 * u4 + 2], v[8 * u4 + 3]), h0, l0);
+          split4(make_float4(v[8 * u4 + 4], v[8 * u4 + 5], v[8 * u4 + 6], v[8 * u4 + 7]), h1, l1);
+          *reinterpret_cast<uint4*>(ph + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+          *reinterpret_cast<uint4*>(pl + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+        } else {
+          *reinterpret_cast<uint4*>(ph + off) =
+              make_uint4(pack_bf16x2(v[8 * u4], v[8 * u4 + 1]), pack_bf16x2(v[8 * u4 + 2], v[8 * u4 + 3]),
+                         pack_bf16x2(v[8 * u4 + 4], v[8 * u4 + 5]), pack_bf16x2(v[8 * u4 + 6], v[8 * u4 + 7]));
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[s]);
+      l_run = l_run * alpha + lsum;
+      m_run = m_new;
+      if (s) m_hist1 = m_new; else m_hist0 = m_new;
+      if (j >= 1 && !fold(j - 1)) { ok = false; break; }
+    }
+    if (ok && nkb > 0) ok = fold(nkb - 1);
+    // row sum over both halves
+    // (the exchange buffer of parity nkb & 1 was last read for block nkb - 2,
+    // before the partner's arrival for block nkb - 1 that this warp waited on)
+    float* lb = red + (nkb & 1) * 256;
+    if (ok) {
+      lb[h * 128 + row] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&l_bar[q]);
+      const bool w = mbar_wait(&l_bar[q], 0, abort, p.err, 223);
+      ok = __all_sync(0xffffffffu, w) != 0;
+    }
+    if (ok && t < p.T) {
+      const float inv = 1.f / (lb[row] + lb[128 + row]);
+      const int64_t off = (int64_t)b * p.o_sb + (int64_t)t * p.o_st + (int64_t)n * p.o_sn + h * 32;
+      if (X3) {
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.o) + off);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(pack_bf16x2(o[8 * i] * inv, o[8 * i + 1] * inv),
+                              pack_bf16x2(o[8 * i + 2] * inv, o[8 * i + 3] * inv),
+                              pack_bf16x2(o[8 * i + 4] * inv, o[8 * i + 5] * inv),
+                              pack_bf16x2(o[8 * i + 6] * inv, o[8 * i + 7] * inv));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && tid == 0) {
+    const uint64_t t1 = globaltimer();
+    while (globaltimer() - t1 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+template <bool X3>
+int launch_ws(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t T,
+              int64_t S, int64_t N, const int64_t* st, float scale, int causal, cudaStream_t s) {
+  using C = WsCfg<X3>;
+  constexpr int ES = X3 ? 4 : 2;
+  constexpr uint32_t inner = X3 ? 32 : 64;  // 128-byte rows
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)T, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)(st[2] * ES), (uint64_t)(st[1] * ES), (uint64_t)(st[0] * ES)};
+    const uint32_t box[4] = {inner, 1, 128, 1};
+    if (int rc = make_tmap(&tq, q, 4, dims, str, box, ES)) return rc;
+  }
+  {
+    const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)S, (uint64_t)B};
+    const uint32_t box[4] = {inner, 1, 64, 1};
+    const uint64_t sk[3] = {(uint64_t)(st[5] * ES), (uint64_t)(st[4] * ES), (uint64_t)(st[3] * ES)};
+    if (int rc = make_tmap(&tk, k, 4, dims, sk, box, ES)) return rc;
+    const uint64_t sv[3] = {(uint64_t)(st[8] * ES), (uint64_t)(st[7] * ES), (uint64_t)(st[6] * ES)};
+    if (int rc = make_tmap(&tv, v, 4, dims, sv, box, ES)) return rc;
+  }
+  SdpaArgs a;
+  a.B = (int)B;
+  a.T = (int)T;
+  a.S = (int)S;
+  a.N = (int)N;
+  a.scale = scale;
+  a.causal = causal;
+  a.o = o;
+  a.o_sb = st[9];
+  a.o_st = st[10];
+  a.o_sn = st[11];
+  a.err = device_error_word();
+  if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
+  if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_ws<X3>, C::SMEM, "sdpa_fwd_ws")) return rc;
+  dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
+  sdpa_fwd_ws<X3><<<grid, kWsThreads, C::SMEM, s>>>(tq, tk, tv, a);
+  B200_LAUNCH_CHECK();
+  return B200_OK;
+}
+
 // SIMT fallback for shapes the tensor-core kernel does not take (head dim !=
 // 64, unaligned strides): one block per (query row, head, batch), scores in
 // shared memory, exact f32 arithmetic.
@@ -665,6 +1096,14 @@ extern "C" int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v
   const void* ptrs[4] = {q, k, v, o};
   for (int i = 0; i < 4; ++i) tc = tc && ((uintptr_t)ptrs[i] % 16 == 0);
   if (tc) {
+    static const bool legacy = [] {
+      const char* e = std::getenv("B200_SDPA_LEGACY");
+      return e && std::strcmp(e, "1") == 0;
+    }();
+    if (!legacy && scale > 0.f) {  // (the kernel masks with -inf before scaling)
+      if (es == 4) return launch_ws<true>(q, k, v, o, B, T, S, N, st, scale, causal, s);
+      return launch_ws<false>(q, k, v, o, B, T, S, N, st, scale, causal, s);
+    }
     if (es == 4) {
       static const bool x3 = [] {
         const char* e = std::getenv("B200_F32_MATMUL");

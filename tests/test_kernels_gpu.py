@@ -119,7 +119,8 @@ def test_ln_bwd_f32():
 
 # ----------------------------------------------------------------------- SDPA
 @pytest.mark.parametrize("B,T,N,causal", [(8, 512, 8, True), (8, 512, 8, False), (2, 200, 3, True),
-                                          (1, 128, 1, True), (2, 384, 2, False), (1, 1, 1, True)])
+                                          (1, 128, 1, True), (2, 384, 2, False), (1, 1, 1, True),
+                                          (1, 1024, 2, True), (1, 1000, 2, False)])
 def test_sdpa_f32(B, T, N, causal):
     rng = np.random.default_rng(B * 1000 + T + N)
     q, k, v = (rng.standard_normal((B, T, N, 64)).astype(np.float32) for _ in range(3))
