@@ -553,7 +553,7 @@ struct WsCfg {
   static constexpr int QST_OFF = P_OFF;                            // f32 Q staging aliases the P slots
   static constexpr int RED_OFF = ST_OFF + ST_BYTES;                // softmax max / sum exchange
   static constexpr int BAR_OFF = RED_OFF + 2 * 2 * 128 * 4;
-  static constexpr int SMEM = BAR_OFF + 256 + 1024;
+  static constexpr int SMEM = BAR_OFF + 512 + 1024;
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -626,7 +626,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   uint64_t* ob_free = bars + 16;  // [2]
   uint64_t* mx_bar = bars + 18;   // [4 quarters][2]: both halves' block maxima written
   uint64_t* l_bar = bars + 26;    // [4 quarters]: both halves' row sums written
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 30);
+  uint64_t* kst_full = bars + 30;  // f32 K staging loaded (X3)
+  uint64_t* vst_full = bars + 31;  // f32 V staging loaded (X3)
+  uint64_t* kst_used = bars + 32;  // f32 K staging split (count 4 warps)
+  uint64_t* vst_used = bars + 33;  // f32 V staging split
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 34);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -652,6 +656,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     for (int i = 0; i < 8; ++i) mbar_init(&mx_bar[i], 2);
     for (int i = 0; i < 4; ++i) mbar_init(&l_bar[i], 2);
+    mbar_init(kst_full, 1);
+    mbar_init(vst_full, 1);
+    mbar_init(kst_used, 4);
+    mbar_init(vst_used, 4);
     *abort = 0;
     mbar_fence_init();
   }
@@ -682,13 +690,14 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int j = 0; j < nkb; ++j) {
         const int s = j & 1, use = j >> 1;
         if (X3) {
-          // one f32 staging buffer: block j may land once block j-1 has been split
-          if (j >= 1 && !mbar_wait(&kv_conv[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, p.err, 211)) break;
-          mbar_expect_tx(&kv_full[0], 2 * 64 * 64 * 4);
-          for (int c = 0; c < 2; ++c) {
-            tma_load_4d(k_st + c * 64 * 128, &tK, &kv_full[0], c * 32, n, j * 64, b);
-            tma_load_4d(v_st + c * 64 * 128, &tV, &kv_full[0], c * 32, n, j * 64, b);
-          }
+          // one f32 staging buffer each for K and V: block j's K may land once
+          // block j-1's K has been split (while its V is being split)
+          if (j >= 1 && !mbar_wait(kst_used, (j - 1) & 1, abort, p.err, 211)) break;
+          mbar_expect_tx(kst_full, 64 * 64 * 4);
+          for (int c = 0; c < 2; ++c) tma_load_4d(k_st + c * 64 * 128, &tK, kst_full, c * 32, n, j * 64, b);
+          if (j >= 1 && !mbar_wait(vst_used, (j - 1) & 1, abort, p.err, 210)) break;
+          mbar_expect_tx(vst_full, 64 * 64 * 4);
+          for (int c = 0; c < 2; ++c) tma_load_4d(v_st + c * 64 * 128, &tV, vst_full, c * 32, n, j * 64, b);
         } else {
           if (j >= 2 && !mbar_wait(&kv_free[s], (use - 1) & 1, abort, p.err, 211)) break;
           mbar_expect_tx(&kv_full[s], 2 * 64 * 64 * 2);
@@ -756,14 +765,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (lane == 0) mbar_arrive(q_ready);
         for (int j = 0; j < nkb; ++j) {
           const int s = j & 1, use = j >> 1;
-          ok = mbar_wait(&kv_full[0], j & 1, abort, p.err, 218);
-          if (ok && j >= 2) ok = mbar_wait(&kv_free[s], (use - 1) & 1, abort, p.err, 219);
+          ok = j < 2 || mbar_wait(&kv_free[s], (use - 1) & 1, abort, p.err, 219);
+          ok = ok && mbar_wait(kst_full, j & 1, abort, p.err, 218);
           if (!__all_sync(0xffffffffu, ok)) break;
           split_rows(k_st, k_hi(s), k_lo(s), 64, ctid);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(kst_used);
+          ok = mbar_wait(vst_full, j & 1, abort, p.err, 224);
+          if (!__all_sync(0xffffffffu, ok)) break;
           split_rows(v_st, v_hi(s), v_lo(s), 64, ctid);
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&kv_conv[s]);
+          if (lane == 0) {
+            mbar_arrive(vst_used);
+            mbar_arrive(&kv_conv[s]);
+          }
         }
       }
     }
