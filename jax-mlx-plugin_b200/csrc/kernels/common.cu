@@ -18,6 +18,7 @@ extern "C" const char* b200_kernels_version(void) { return "b200-kernels 0.1.0 s
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <map>
 #include <set>
 #include <string>
 
@@ -62,14 +63,15 @@ int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
 
 int allow_dynamic_smem(const void* fn, int bytes, const char* what) {
   static std::mutex mu;
-  static std::set<std::pair<const void*, int>> done;  // (kernel, device)
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes allowed
   int dev = 0;
   B200_CUDA_TRY(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(mu);
-  if (done.count({fn, dev})) return B200_OK;
+  auto it = done.find({fn, dev});
+  if (it != done.end() && it->second >= bytes) return B200_OK;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
     return set_error(B200_ERR_CUDA, std::string("cudaFuncSetAttribute(") + what + ") failed");
-  done.insert({fn, dev});
+  done[{fn, dev}] = bytes;
   return B200_OK;
 }
 

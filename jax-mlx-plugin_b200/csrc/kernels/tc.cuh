@@ -213,8 +213,8 @@ int make_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
               bool atom32 = false);
 // Per-device error word passed to kernels with bounded waits (zeroed once).
 int* device_error_word();
-// Opt `fn` into `bytes` of dynamic shared memory on the current device (once
-// per kernel and device; the attribute is per device).
+// Opt `fn` into at least `bytes` of dynamic shared memory on the current device
+// (the attribute is per device; raised when a larger size is asked for).
 int allow_dynamic_smem(const void* fn, int bytes, const char* what);
 // The allocation-free GEMM's error word on the current device (gemm.cu):
 // its value, -1 on a CUDA error; cleared when `clear` is set.
