@@ -1,7 +1,7 @@
 """Benchmark of the B200 PJRT plugin on BASELINE.json's configurations.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload ln|sdpa|mlp|cnn|transformer] [--no-extra]
+                    [--workload ln|sdpa|mlp|cnn|transformer|gemm] [--no-extra]
 
 Default workload: configs[1], the jitted residual-add + LayerNorm forward
 (x, r [4096,1024] f32), whose metric is HBM GB/s.  One step = one PJRT
@@ -304,6 +304,35 @@ def bench_sdpa(rig: Rig, steps, warmup):
             "l2": "flushed between steps"}
 
 
+def bench_gemm(rig: Rig, steps, warmup, shape, dtype="bf16", trans=""):
+    """The dot_general GEMM kernel alone through the C ABI (b200_gemm): C[M,N] =
+    A[M,K] B[K,N] with A stored [K,M] when trans contains 'a' and B stored [N,K]
+    when it contains 'b'.  Inputs larger than L2 are not guaranteed, so L2 is
+    flushed between steps."""
+    from jax_b200 import kernels
+    torch = rig.torch
+    M, N, K = shape
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    code = kernels.DT_BF16 if dtype == "bf16" else kernels.DT_F32
+    a_t, b_t = "a" in trans, "b" in trans
+    A = torch.randn((K, M) if a_t else (M, K), device="cuda", dtype=tdt)
+    B = torch.randn((N, K) if b_t else (K, N), device="cuda", dtype=tdt)
+    C = torch.empty((M, N), device="cuda", dtype=tdt)
+    st = rig.client.device_stream(rig.dev)
+    sAm, sAk = (1, M) if a_t else (K, 1)
+    sBk, sBn = (1, K) if b_t else (N, 1)
+
+    def step():
+        kernels.gemm(A.data_ptr(), B.data_ptr(), C.data_ptr(), 0, 1, M, N, K, 0, sAm, sAk, 0, sBk, sBn,
+                     N, 1.0, code, code, 0, st)
+    ts = rig.time_steps(step, steps, warmup)
+    t = float(np.mean(ts))
+    fl = 2.0 * M * N * K
+    return {"metric": f"GEMM {M}x{N}x{K} {dtype} ({'A^T' if a_t else 'A'}, {'B^T' if b_t else 'B'})",
+            "unit": "TFLOP/s", "value": fl / t / 1e12, "ms_per_step": t * 1e3, "flops_per_step": fl,
+            "launches_per_step": 1, "dtype": dtype}
+
+
 def _mlp_args(rng, batch):
     params = []
     for i in range(len(MLP_DIMS) - 1):
@@ -414,7 +443,10 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="ln", choices=["ln", "sdpa", "mlp", "cnn", "transformer"])
+    ap.add_argument("--workload", default="ln", choices=["ln", "sdpa", "mlp", "cnn", "transformer", "gemm"])
+    ap.add_argument("--gemm-shape", default="8192,8192,8192", help="M,N,K for --workload gemm")
+    ap.add_argument("--gemm-dtype", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--gemm-trans", default="", help="'a', 'b' or 'ab': operands stored transposed")
     ap.add_argument("--no-extra", action="store_true")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
@@ -467,6 +499,9 @@ def main():
     elif a.workload == "sdpa":
         res = bench_sdpa(rig, a.steps, a.warmup)
         res.update(bound="tensor", kernel_time_s=res["ms_per_step"] * 1e-3, algorithmic=SDPA_FLOPS)
+    elif a.workload == "gemm":
+        res = bench_gemm(rig, a.steps, a.warmup, tuple(int(v) for v in a.gemm_shape.split(",")),
+                         a.gemm_dtype, a.gemm_trans)
     else:
         res = bench_train(rig, a.workload, a.steps, a.warmup, world, rank)
     t_local = res["ms_per_step"]
@@ -506,9 +541,13 @@ def main():
         if world == 1:
             line["cpu_baseline"] = cpu_ln_baseline(host_cores(), budget_s=10.0)
     else:
-        line.update(value=res["value"] if a.workload == "sdpa" else res["global_batch"] / (t_max * 1e-3),
-                    ms_per_step=t_max, scaling="weak" if a.workload == "sdpa" else "strong",
+        kernel_only = a.workload in ("sdpa", "gemm")
+        line.update(value=res["value"] * (world if kernel_only else 1) if kernel_only
+                    else res["global_batch"] / (t_max * 1e-3),
+                    ms_per_step=t_max, scaling="weak" if kernel_only else "strong",
                     config={"workload": a.workload, "parallelism": f"dp{world}" if dp else f"replicas x{world}"})
+        if a.workload == "gemm":
+            line["config"].update(shape=a.gemm_shape, trans=a.gemm_trans, l2="flushed between steps")
         line["gpu_launches"] = res["launches_per_step"] * a.steps
     if world == 1 and not a.no_extra and a.workload == "ln":
         extra = {}

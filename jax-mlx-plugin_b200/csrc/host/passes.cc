@@ -6,6 +6,8 @@
 // mask that JAX emits for is_causal=True.
 #include "passes.h"
 
+#include "custom_calls.h"
+
 #include <cmath>
 #include <cstring>
 #include <functional>
@@ -34,6 +36,21 @@ void inline_into(const Module& m, const Graph& src, const std::vector<ValueRef>&
       if (it == m.funcs.end()) throw PjrtErr(3, "call to undefined function @" + n.target);
       std::vector<ValueRef> r;
       inline_into(m, *it->second, ops, dst, r, depth + 1);
+      map[i] = r;
+      continue;
+    }
+    if (n.op == Op::CustomCall && expands_custom_call(n.target)) {
+      // backward custom calls become ordinary StableHLO (custom_calls.cc)
+      std::vector<TensorType> types;
+      for (auto& o : ops) types.push_back(dst.type(o));
+      Module sub = parse_module(custom_call_expansion(n, types));
+      std::vector<ValueRef> r;
+      inline_into(sub, *sub.main(), ops, dst, r, depth + 1);
+      if (r.size() != n.results.size()) throw PjrtErr(13, "custom call expansion result count");
+      for (size_t k = 0; k < r.size(); ++k)
+        if (dst.type(r[k]) != n.results[k])
+          throw PjrtErr(3, "custom_call @" + n.target + " result " + std::to_string(k) + " has type " +
+                               n.results[k].str() + ", expected " + dst.type(r[k]).str());
       map[i] = r;
       continue;
     }

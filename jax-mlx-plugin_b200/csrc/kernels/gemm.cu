@@ -304,6 +304,7 @@ struct PersArgs {
   int epi;  // 0 none, 1 bias, 2 bias+relu, 3 relu (ignored when out_ws)
   int tiles_m, tiles_n, batch, splits, kb_per_split, kb_all;
   int n_fast;  // 1: consecutive tiles step along N (fewer N tiles than M tiles)
+  int group;   // > 1: grouped (swizzled) tile order, `group` M tiles per group
   int out_ws;  // 1: store raw f32 partials to the split-K workspace map
   int* err;
 };
@@ -336,7 +337,16 @@ __global__ void __launch_bounds__(192, 1)
   auto decode = [&](int t, int& m0, int& n0, int& bz, int& ks, int& kb0, int& nkb) {
     const int bs = t / tiles_mn, r = t - bs * tiles_mn;
     int mi, ni;
-    if (p.n_fast) {
+    if (p.group > 1) {
+      // groups of `group` M tiles, N-major inside a group: the tiles resident at
+      // once cover a squarish block of C, whose A and B panels stay in L2
+      const int gsz = p.group * p.tiles_n;
+      const int g = r / gsz, gm0 = g * p.group;
+      const int gm = min(p.group, p.tiles_m - gm0);
+      const int in = r - g * gsz;
+      mi = gm0 + in % gm;
+      ni = in / gm;
+    } else if (p.n_fast) {
       ni = r % p.tiles_n;
       mi = r / p.tiles_n;
     } else {
@@ -830,6 +840,8 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   p.kb_per_split = sp.per_split;
   p.kb_all = KB_all;
   p.n_fast = tiles_n <= tiles_m ? 1 : 0;
+  // large 2-D tile grids: 16 M tiles x (num_sms / 16) N tiles are resident at once
+  p.group = (tiles_m >= 32 && tiles_n >= 16) ? 16 : 1;
   p.out_ws = ws ? 1 : 0;
   p.err = scratch.err ? scratch.err : device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");

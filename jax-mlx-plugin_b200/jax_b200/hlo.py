@@ -337,6 +337,21 @@ class Builder:
             f"      stablehlo.return %s : tensor<{dt}>\n    }}) : ({zeros.ty}, {ids2.ty}, {upd.ty}) -> {zeros.ty}",
             zeros.shape, dt)
 
+    # --------------------------------------------------------- custom call --
+    def custom_call(self, target: str, operands: Sequence[V], results: Sequence[Tuple[Sequence[int], str]],
+                    backend_config: str = ""):
+        """stablehlo.custom_call as jax's mlir.custom_call prints it; one V per result."""
+        rt = [ttype(sh, dt) for sh, dt in results]
+        cfg = backend_config.replace('"', "\\22")
+        ins = ", ".join(o.name for o in operands)
+        sig = f"({', '.join(o.ty for o in operands)}) -> " + (rt[0] if len(rt) == 1 else f"({', '.join(rt)})")
+        name = self._fresh()
+        head = name if len(rt) == 1 else f"{name}:{len(rt)}"
+        self.stmts.append(f'{head} = stablehlo.custom_call @{target}({ins}) {{backend_config = "{cfg}"}} : {sig}')
+        if len(rt) == 1:
+            return V(self, name, tuple(results[0][0]), results[0][1])
+        return [V(self, f"{name}#{i}", tuple(sh), dt) for i, (sh, dt) in enumerate(results)]
+
     # -------------------------------------------------------- collectives --
     def all_reduce_sum(self, x: V, groups: Sequence[Sequence[int]]) -> V:
         g = "[" + ", ".join("[" + ", ".join(map(str, r)) + "]" for r in groups) + "]"

@@ -251,3 +251,28 @@ def transformer_step(batch=64, seq=256, layers=6, d=512, heads=8, ffn=2048, voca
         new_m.append(m2)
         new_v.append(v2)
     return b.module([loss] + new_p + new_m + new_v + [cnt])
+
+
+def sdpa_custom_calls(B=2, T=128, N=2, H=64, scale=0.125, dt="f32") -> str:
+    """The reference's custom_vjp attention (src/jax_mlx/sdpa.py:154-190) under
+    jax.vjp: forward mlx_sdpa(Q, K, V) and backward mlx_sdpa_bwd(Q, K, V, dO).
+    Inputs Q, K, V, dO [B, T, N, H]; outputs O, dQ, dK, dV."""
+    b = Builder("jit_sdpa_vjp")
+    q, k, v, g = (b.param((B, T, N, H), dt) for _ in range(4))
+    cfg = '{"scale": %s}' % repr(float(scale))
+    o = b.custom_call("mlx_sdpa", [q, k, v], [((B, T, N, H), dt)], cfg)
+    dq, dk, dv = b.custom_call("mlx_sdpa_bwd", [q, k, v, g], [((B, T, N, H), dt)] * 3, cfg)
+    return b.module([o, dq, dk, dv])
+
+
+def layer_norm_custom_calls(rows=64, cols=256, eps=1e-5, dt="f32") -> str:
+    """The reference's custom_vjp LayerNorm (src/jax_mlx/layer_norm.py:141-171)
+    under jax.vjp: mlx_layer_norm(x, w, b) and mlx_layer_norm_bwd(x, w, b, dy).
+    Outputs y, dx, dw, db."""
+    b = Builder("jit_layer_norm_vjp")
+    x, w, bb, dy = b.param((rows, cols), dt), b.param((cols,), dt), b.param((cols,), dt), b.param((rows, cols), dt)
+    cfg = '{"eps": %s}' % repr(float(eps))
+    y = b.custom_call("mlx_layer_norm", [x, w, bb], [((rows, cols), dt)], cfg)
+    dx, dw, db = b.custom_call("mlx_layer_norm_bwd", [x, w, bb, dy],
+                               [((rows, cols), dt), ((cols,), dt), ((cols,), dt)], cfg)
+    return b.module([y, dx, dw, db])

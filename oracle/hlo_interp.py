@@ -302,7 +302,10 @@ class Interp:
             crop = tuple(slice(-min(l, 0) or None, full.shape[k] + min(h, 0)) for k, (l, h) in enumerate(zip(lo, hi)))
             return c(full[crop])
         if op == "custom_call":
-            return c(self._custom(rhs, a, t))
+            r = self._custom(rhs, a, t)
+            if isinstance(r, tuple):  # multi-result: one type per result, last in the signature
+                return tuple(_cast(x, tt.dt) for x, tt in zip(r, tys[-len(r):]))
+            return c(r)
         raise NotImplementedError(f"oracle: op {op}")
 
     # ---------------------------------------------------------------- ops --
@@ -433,6 +436,14 @@ class Interp:
             eps = float(m.group(1)) if m else 1e-5
             from .restate import layer_norm_ref
             return layer_norm_ref(a[0], None, a[1], a[2], eps)
+        if target == "mlx_sdpa_bwd":
+            m = re.search(r"scale\\?\"?\\?\"?:\s*([-\d.eE+]+)", rhs.replace("\\22", '"'))
+            from .restate import sdpa_bwd_ref
+            return tuple(sdpa_bwd_ref(a[0], a[1], a[2], a[3], float(m.group(1)) if m else 1.0))
+        if target == "mlx_layer_norm_bwd":
+            m = re.search(r"eps\\?\"?\\?\"?:\s*([-\d.eE+]+)", rhs.replace("\\22", '"'))
+            from .restate import layer_norm_bwd_ref
+            return tuple(layer_norm_bwd_ref(a[0], a[1], a[3], float(m.group(1)) if m else 1e-5))
         raise NotImplementedError(f"oracle custom_call @{target}")
 
 

@@ -36,6 +36,26 @@ def sdpa_ref(q, k, v, scale=None, causal=False):
     return np.transpose(w @ vb, (0, 2, 1, 3))
 
 
+def sdpa_bwd_ref(q, k, v, g, scale):
+    """dQ, dK, dV of non-causal softmax(Q K^T scale) V, layout (B, T, N, H).
+
+    Follows reference src/jax_mlx/sdpa.py:65-87 (_mlx_sdpa_bwd_impl): weights =
+    softmax(logits), dv = weights^T g, d_weights = g v^T, d_scores = weights *
+    (d_weights - sum(d_weights * weights, -1)) * scale, dq = d_scores k,
+    dk = d_scores^T q."""
+    q, k, v, g = (np.transpose(np.asarray(a, dtype=np.float64), (0, 2, 1, 3)) for a in (q, k, v, g))
+    logits = q @ np.swapaxes(k, -1, -2) * scale
+    w = np.exp(logits - logits.max(-1, keepdims=True))
+    w /= w.sum(-1, keepdims=True)
+    dv = np.swapaxes(w, -1, -2) @ g
+    dw = g @ np.swapaxes(v, -1, -2)
+    ds = w * (dw - (dw * w).sum(-1, keepdims=True)) * scale
+    dq = ds @ k
+    dk = np.swapaxes(ds, -1, -2) @ q
+    t = lambda a: np.transpose(a, (0, 2, 1, 3))
+    return t(dq), t(dk), t(dv)
+
+
 def layer_norm_ref(x, residual, gamma, beta, eps=1e-5):
     """LayerNorm over the last axis of (x + residual), then * gamma + beta.
 

@@ -341,3 +341,51 @@ def test_transformer_step_full_config_runs(client):
     outs = _tr_run(client, programs.transformer_step(**cfg), params, ms, vs, count, tok, tgt)
     assert abs(float(outs[0]) - np.log(32000)) < 0.5
     assert all(np.isfinite(o).all() for o in outs)
+
+
+# ------------------------------------------- reference custom calls (A5/A6/A12)
+def _as_dt(a, dt):
+    return hlo_interp.bf16_round(a) if dt == "bf16" else a
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_custom_call_sdpa_and_backward(client, dt):
+    """mlx_sdpa / mlx_sdpa_bwd (the reference's custom_vjp attention) through the
+    plugin vs the closed forms of src/jax_mlx/sdpa.py:19-31 and :65-87."""
+    rng = np.random.default_rng(41)
+    B, T, N, H = 2, 128, 2, 64
+    q, k, v, g = (_as_dt(rng.standard_normal((B, T, N, H)).astype(np.float32), dt) for _ in range(4))
+    text = programs.sdpa_custom_calls(B, T, N, H, 0.125, dt)
+    exe = client.compile(text)
+    bf = dt == "bf16"
+    bufs = [client.buffer_from_numpy(pjrt.to_bf16_bits(a) if bf else a, bf16=bf) for a in (q, k, v, g)]
+    got = [o.to_numpy() for o in exe.execute([bufs])[0]]
+    if bf:
+        got = [pjrt.from_bf16_bits(o) for o in got]
+    tol = 2e-2 if bf else 2e-3
+    assert_close(got[0], restate.sdpa_ref(q, k, v, 0.125, False), tol, "mlx_sdpa")
+    for name, gg, r in zip(("dq", "dk", "dv"), got[1:], restate.sdpa_bwd_ref(q, k, v, g, 0.125)):
+        assert_close(gg, r, tol, f"mlx_sdpa_bwd {name}")
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_custom_call_layer_norm_and_backward(client, dt):
+    """mlx_layer_norm / mlx_layer_norm_bwd through the plugin vs the closed forms
+    of src/jax_mlx/layer_norm.py:20-25 and :59-76."""
+    rng = np.random.default_rng(42)
+    rows, cols = 96, 512
+    x = _as_dt(rng.standard_normal((rows, cols)).astype(np.float32), dt)
+    w = _as_dt((1 + 0.1 * rng.standard_normal(cols)).astype(np.float32), dt)
+    bb = _as_dt((0.1 * rng.standard_normal(cols)).astype(np.float32), dt)
+    dy = _as_dt(rng.standard_normal((rows, cols)).astype(np.float32), dt)
+    text = programs.layer_norm_custom_calls(rows, cols, 1e-5, dt)
+    exe = client.compile(text)
+    bf = dt == "bf16"
+    bufs = [client.buffer_from_numpy(pjrt.to_bf16_bits(a) if bf else a, bf16=bf) for a in (x, w, bb, dy)]
+    got = [o.to_numpy() for o in exe.execute([bufs])[0]]
+    if bf:
+        got = [pjrt.from_bf16_bits(o) for o in got]
+    tol = 2e-2 if bf else 1e-5
+    assert_close(got[0], restate.layer_norm_ref(x, None, w, bb, 1e-5), tol, "mlx_layer_norm")
+    for name, gg, r in zip(("dx", "dw", "db"), got[1:], restate.layer_norm_bwd_ref(x, w, dy, 1e-5)):
+        assert_close(gg, r, tol, f"mlx_layer_norm_bwd {name}")

@@ -150,3 +150,15 @@ def test_generic_printing_and_func_call_inlining():
     assert "call" not in g and "maximum" in g
     plan = pjrt.inspect(text, 1)
     assert plan.count("_loop") == 1  # relu and add fuse into one kernel
+
+
+def test_backward_custom_calls_expand_to_kernels():
+    """mlx_sdpa_bwd / mlx_layer_norm_bwd (reference custom_vjp backward targets)
+    compile: expanded into StableHLO, lowered to GEMMs and fused kernels."""
+    from jax_b200 import programs
+    plan = pjrt.inspect(programs.sdpa_custom_calls(), 1)
+    steps = plan.split("steps:")[1]
+    assert steps.count("gemm ") == 5 and "sdpa " in steps
+    plan = pjrt.inspect(programs.layer_norm_custom_calls(), 1)
+    steps = plan.split("steps:")[1]
+    assert "layer_norm " in steps and "_reduce" in steps
