@@ -523,37 +523,39 @@ __global__ void __launch_bounds__(128, 1)
 // ---------------------------------------------------------------------------
 // Warp-specialized attention forward, head dim 64, key blocks of 64.
 //
-// One CTA = 128 query rows of one (batch, head), 320 threads in four roles:
-//   warps 0-3  softmax: one query row per thread; read S_j from TMEM, online
-//              max / sum in f32, write P_j to shared memory, then fold the
-//              previous block's P V product (TMEM) into the f32 row of O held in
-//              registers;
-//   warp 4     TMA: Q once, then K_j / V_j into a two-slot ring;
-//   warp 5     MMA issue: S_j = Q K_j^T into one of two TMEM S buffers, then
-//              O_{j-1} = P_{j-1} V_{j-1} into one of two TMEM O buffers, so the
-//              tensor core works on block j while the softmax warps work on j-1;
-//   warps 6-9  (f32 inputs) split each f32 tile into bf16 hi and lo parts.
+// One CTA = 128 query rows of one (batch, head), 448 threads in four roles:
+//   warps 0-7  softmax: warp w owns TMEM lane quarter w % 4 (32 query rows)
+//              and half w / 4 of each key block and of the head dim; reads S_j
+//              from TMEM, exchanges the row max with its partner warp, keeps
+//              the online max / sum in f32, writes P_j as bf16 into TMEM, and
+//              folds the previous block's P V product (TMEM) into its f32 half
+//              row of O held in registers;
+//   warp 8     TMA: Q once, then K_j / V_j into a three-slot ring;
+//   warp 9     MMA issue: S_j = Q K_j^T (A = Q in shared memory) into one of two
+//              TMEM S buffers, then O_{j-1} = P_{j-1} V_{j-1} with A = P read
+//              straight from TMEM into one of two TMEM O buffers, so the tensor
+//              core works on block j while the softmax warps work on block j-1;
+//   warps 10-13 (f32 inputs) split each f32 tile into bf16 hi and lo parts.
 // f32 inputs run every product as three bf16 MMAs, hi*hi + hi*lo + lo*hi
 // (the dropped lo*lo term is ~2^-16 relative), on Q, K, V and P; bf16 inputs
-// run one.  All shared-memory operand tiles are 128-byte rows with the 16-byte
-// unit swizzle (unit ^ row % 8): K-major for Q, K and P, MN-major for V.
+// run one.  Shared-memory operand tiles are 128-byte rows with the 16-byte
+// unit swizzle (unit ^ row % 8): K-major for Q and K, MN-major for V.
 template <bool X3>
 struct WsCfg {
   static constexpr int QB = 128 * 128;   // bf16 Q tile: 128 rows x 128 B
   static constexpr int KB = 64 * 128;    // bf16 K or V tile: 64 keys x 128 B
-  static constexpr int PB = 128 * 128;   // bf16 P tile: 128 rows x 64 keys
   static constexpr int PARTS = X3 ? 2 : 1;
+  static constexpr int SLOTS = 3;                                  // K/V ring depth
   static constexpr int Q_OFF = 0;                                  // Q hi [, lo]
   static constexpr int KV_OFF = Q_OFF + PARTS * QB;                // slot s: K hi, [K lo,] V hi [, V lo]
   static constexpr int KV_SLOT = 2 * PARTS * KB;
-  static constexpr int P_OFF = KV_OFF + 2 * KV_SLOT;               // slot s: P hi [, P lo]
-  static constexpr int P_SLOT = PARTS * PB;
-  static constexpr int ST_OFF = P_OFF + 2 * P_SLOT;                // f32 staging (X3): K, V of one block
+  static constexpr int ST_OFF = KV_OFF + SLOTS * KV_SLOT;          // f32 staging (X3): K, V of one block
   static constexpr int ST_BYTES = X3 ? 2 * 64 * 256 : 0;
-  static constexpr int QST_OFF = P_OFF;                            // f32 Q staging aliases the P slots
+  static constexpr int QST_OFF = KV_OFF + 2 * KV_SLOT;             // f32 Q staging aliases K/V slot 2
   static constexpr int RED_OFF = ST_OFF + ST_BYTES;                // softmax max / sum exchange
   static constexpr int BAR_OFF = RED_OFF + 2 * 2 * 128 * 4;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;
+  static_assert(!X3 || KV_SLOT >= 128 * 256, "f32 Q staging must fit in one K/V slot");
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -583,9 +585,8 @@ __device__ __forceinline__ void split_rows(const uint8_t* st, uint8_t* hi, uint8
   }
 }
 
-// Thread roles (448 threads): warps 0-7 softmax (warp w owns TMEM lane quarter
-// w % 4, i.e. 32 query rows, and key / head-dim half w / 4), warp 8 TMA, warp 9
-// MMA issue, warps 10-13 f32 split.
+// Thread roles (448 threads): warps 0-7 softmax, warp 8 TMA, warp 9 MMA issue,
+// warps 10-13 f32 split.
 constexpr int kWsThreads = 448;
 
 __device__ __forceinline__ float ex2(float x) {
@@ -599,6 +600,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     sdpa_fwd_ws(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                 const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
   using C = WsCfg<X3>;
+  constexpr int NS = C::SLOTS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* q_hi = smem + C::Q_OFF;
@@ -607,8 +609,6 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   auto k_lo = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + C::KB; };
   auto v_hi = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + C::PARTS * C::KB; };
   auto v_lo = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + 3 * C::KB; };
-  auto p_hi = [&](int s) { return smem + C::P_OFF + s * C::P_SLOT; };
-  auto p_lo = [&](int s) { return smem + C::P_OFF + s * C::P_SLOT + C::PB; };
   uint8_t* k_st = smem + C::ST_OFF;
   uint8_t* v_st = smem + C::ST_OFF + 64 * 256;
   uint8_t* q_st = smem + C::QST_OFF;
@@ -616,21 +616,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars + 0;
   uint64_t* q_ready = bars + 1;
-  uint64_t* kv_full = bars + 2;   // [2]
-  uint64_t* kv_conv = bars + 4;   // [2]
-  uint64_t* kv_free = bars + 6;   // [2]
-  uint64_t* s_full = bars + 8;    // [2]
-  uint64_t* s_free = bars + 10;   // [2]
-  uint64_t* p_full = bars + 12;   // [2]
-  uint64_t* o_full = bars + 14;   // [2]
-  uint64_t* ob_free = bars + 16;  // [2]
-  uint64_t* mx_bar = bars + 18;   // [4 quarters][2]: both halves' block maxima written
-  uint64_t* l_bar = bars + 26;    // [4 quarters]: both halves' row sums written
-  uint64_t* kst_full = bars + 30;  // f32 K staging loaded (X3)
-  uint64_t* vst_full = bars + 31;  // f32 V staging loaded (X3)
-  uint64_t* kst_used = bars + 32;  // f32 K staging split (count 4 warps)
-  uint64_t* vst_used = bars + 33;  // f32 V staging split
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 34);
+  uint64_t* kv_full = bars + 2;    // [3] K/V slot loaded (bf16 inputs)
+  uint64_t* kv_conv = bars + 5;    // [3] K/V slot split (f32 inputs)
+  uint64_t* kv_free = bars + 8;    // [3] K/V slot consumed by the MMAs
+  uint64_t* s_full = bars + 11;    // [2]
+  uint64_t* s_free = bars + 13;    // [2]
+  uint64_t* p_full = bars + 15;    // [2]
+  uint64_t* o_full = bars + 17;    // [2]
+  uint64_t* ob_free = bars + 19;   // [2]
+  uint64_t* mx_bar = bars + 21;    // [4 quarters][2]: both halves' block maxima written
+  uint64_t* l_bar = bars + 29;     // [4 quarters]: both halves' row sums written
+  uint64_t* kst_full = bars + 33;  // f32 K staging loaded
+  uint64_t* vst_full = bars + 34;  // f32 V staging loaded
+  uint64_t* kst_used = bars + 35;  // f32 K staging split (count 4 warps)
+  uint64_t* vst_used = bars + 36;  // f32 V staging split
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 37);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -644,10 +644,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   if (tid == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_ready, 4);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_conv[i], 4);
       mbar_init(&kv_free[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 8);
       mbar_init(&p_full[i], 8);
@@ -664,16 +666,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     mbar_fence_init();
   }
   if (warp == 0) {
-    tmem_alloc(tslot, 256);
+    tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  // TMEM columns: S buffers at 0 and 64, O buffers at 128 and 192 (f32, 64 wide)
+  // TMEM columns (f32 / packed bf16x2, 64 wide each): S buffers at 0 and 64,
+  // O buffers at 128 and 192, P buffers at 256 and 320 (hi in the first 32
+  // columns, lo in the last 32)
   auto tS = [&](int s) { return tmem + (uint32_t)(s * 64); };
   auto tO = [&](int s) { return tmem + 128u + (uint32_t)(s * 64); };
+  auto tP = [&](int s) { return tmem + 256u + (uint32_t)(s * 64); };
 
   if (warp == 8) {
     if (lane == 0 && nkb > 0) {  // ---- TMA producer
@@ -688,7 +693,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         tma_load_4d(q_hi, &tQ, q_full, 0, n, t0, b);
       }
       for (int j = 0; j < nkb; ++j) {
-        const int s = j & 1, use = j >> 1;
+        const int ks = j % NS, kuse = j / NS;
         if (X3) {
           // one f32 staging buffer each for K and V: block j's K may land once
           // block j-1's K has been split (while its V is being split)
@@ -699,10 +704,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           mbar_expect_tx(vst_full, 64 * 64 * 4);
           for (int c = 0; c < 2; ++c) tma_load_4d(v_st + c * 64 * 128, &tV, vst_full, c * 32, n, j * 64, b);
         } else {
-          if (j >= 2 && !mbar_wait(&kv_free[s], (use - 1) & 1, abort, p.err, 211)) break;
-          mbar_expect_tx(&kv_full[s], 2 * 64 * 64 * 2);
-          tma_load_4d(k_hi(s), &tK, &kv_full[s], 0, n, j * 64, b);
-          tma_load_4d(v_hi(s), &tV, &kv_full[s], 0, n, j * 64, b);
+          if (j >= NS && !mbar_wait(&kv_free[ks], (kuse - 1) & 1, abort, p.err, 211)) break;
+          mbar_expect_tx(&kv_full[ks], 2 * 64 * 64 * 2);
+          tma_load_4d(k_hi(ks), &tK, &kv_full[ks], 0, n, j * 64, b);
+          tma_load_4d(v_hi(ks), &tV, &kv_full[ks], 0, n, j * 64, b);
         }
       }
     }
@@ -713,44 +718,43 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       bool ok = mbar_wait(X3 ? q_ready : q_full, 0, abort, p.err, 212);
       for (int j = 0; ok && j <= nkb; ++j) {
         if (j < nkb) {
-          const int s = j & 1, use = j >> 1;
-          ok = mbar_wait(X3 ? &kv_conv[s] : &kv_full[s], use & 1, abort, p.err, 213);
-          if (ok && j >= 2) ok = mbar_wait(&s_free[s], (use - 1) & 1, abort, p.err, 214);
+          const int ks = j % NS, kuse = j / NS, sb = j & 1, suse = j >> 1;
+          ok = mbar_wait(X3 ? &kv_conv[ks] : &kv_full[ks], kuse & 1, abort, p.err, 213);
+          if (ok && j >= 2) ok = mbar_wait(&s_free[sb], (suse - 1) & 1, abort, p.err, 214);
           if (!ok) break;
           tc_fence_after();
           const uint32_t qh = smem_u32(q_hi), ql = smem_u32(q_lo);
-          const uint32_t kh = smem_u32(k_hi(s)), kl = smem_u32(k_lo(s));
+          const uint32_t kh = smem_u32(k_hi(ks)), kl = smem_u32(k_lo(ks));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t off = kk * 32;
-            umma_f16(tS(s), umma_desc(qh + off, 16, 1024), umma_desc(kh + off, 16, 1024), idesc_s, kk != 0);
+            umma_f16(tS(sb), umma_desc(qh + off, 16, 1024), umma_desc(kh + off, 16, 1024), idesc_s, kk != 0);
             if (X3) {
-              umma_f16(tS(s), umma_desc(qh + off, 16, 1024), umma_desc(kl + off, 16, 1024), idesc_s, 1);
-              umma_f16(tS(s), umma_desc(ql + off, 16, 1024), umma_desc(kh + off, 16, 1024), idesc_s, 1);
+              umma_f16(tS(sb), umma_desc(qh + off, 16, 1024), umma_desc(kl + off, 16, 1024), idesc_s, 1);
+              umma_f16(tS(sb), umma_desc(ql + off, 16, 1024), umma_desc(kh + off, 16, 1024), idesc_s, 1);
             }
           }
-          umma_commit(&s_full[s]);
+          umma_commit(&s_full[sb]);
         }
         if (j >= 1) {
-          const int jj = j - 1, s1 = jj & 1, use1 = jj >> 1;
-          ok = mbar_wait(&p_full[s1], use1 & 1, abort, p.err, 215);
-          if (ok && jj >= 2) ok = mbar_wait(&ob_free[s1], (use1 - 1) & 1, abort, p.err, 216);
+          const int jj = j - 1, ks1 = jj % NS, b1 = jj & 1, use1 = jj >> 1;
+          ok = mbar_wait(&p_full[b1], use1 & 1, abort, p.err, 215);
+          if (ok && jj >= 2) ok = mbar_wait(&ob_free[b1], (use1 - 1) & 1, abort, p.err, 216);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t ph = smem_u32(p_hi(s1)), pl = smem_u32(p_lo(s1));
-          const uint32_t vh = smem_u32(v_hi(s1)), vl = smem_u32(v_lo(s1));
+          const uint32_t vh = smem_u32(v_hi(ks1)), vl = smem_u32(v_lo(ks1));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            // P: K-major, 16 keys = 32 bytes; V: MN-major, 16 keys = 16 rows of 128 B
-            const uint32_t pa = kk * 32, vb = kk * 2048;
-            umma_f16(tO(s1), umma_desc(ph + pa, 16, 1024), umma_desc(vh + vb, 8192, 1024), idesc_o, kk != 0);
+            // P in TMEM: 16 keys = 8 packed columns; V: MN-major, 16 keys = 16 rows of 128 B
+            const uint32_t pa = tP(b1) + kk * 8, vb = kk * 2048;
+            umma_f16_ts(tO(b1), pa, umma_desc(vh + vb, 8192, 1024), idesc_o, kk != 0);
             if (X3) {
-              umma_f16(tO(s1), umma_desc(ph + pa, 16, 1024), umma_desc(vl + vb, 8192, 1024), idesc_o, 1);
-              umma_f16(tO(s1), umma_desc(pl + pa, 16, 1024), umma_desc(vh + vb, 8192, 1024), idesc_o, 1);
+              umma_f16_ts(tO(b1), pa, umma_desc(vl + vb, 8192, 1024), idesc_o, 1);
+              umma_f16_ts(tO(b1), pa + 32, umma_desc(vh + vb, 8192, 1024), idesc_o, 1);
             }
           }
-          umma_commit(&o_full[s1]);
-          umma_commit(&kv_free[s1]);
+          umma_commit(&o_full[b1]);
+          umma_commit(&kv_free[ks1]);
         }
       }
     }
@@ -764,21 +768,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(q_ready);
         for (int j = 0; j < nkb; ++j) {
-          const int s = j & 1, use = j >> 1;
-          ok = j < 2 || mbar_wait(&kv_free[s], (use - 1) & 1, abort, p.err, 219);
+          const int ks = j % NS, kuse = j / NS;
+          ok = j < NS || mbar_wait(&kv_free[ks], (kuse - 1) & 1, abort, p.err, 219);
           ok = ok && mbar_wait(kst_full, j & 1, abort, p.err, 218);
           if (!__all_sync(0xffffffffu, ok)) break;
-          split_rows(k_st, k_hi(s), k_lo(s), 64, ctid);
+          split_rows(k_st, k_hi(ks), k_lo(ks), 64, ctid);
           __syncwarp();
           if (lane == 0) mbar_arrive(kst_used);
           ok = mbar_wait(vst_full, j & 1, abort, p.err, 224);
           if (!__all_sync(0xffffffffu, ok)) break;
-          split_rows(v_st, v_hi(s), v_lo(s), 64, ctid);
+          split_rows(v_st, v_hi(ks), v_lo(ks), 64, ctid);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
             mbar_arrive(vst_used);
-            mbar_arrive(&kv_conv[s]);
+            mbar_arrive(&kv_conv[ks]);
           }
         }
       }
@@ -855,25 +859,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         v[i] = e;
         lsum += e;
       }
-      uint8_t* ph = p_hi(s);
-      uint8_t* pl = p_lo(s);
+      // P_j half row -> TMEM (packed bf16 pairs; hi, and lo for f32 inputs).
+      // P buffer s was last read by P_{j-2} V_{j-2}, folded before this block.
+      uint32_t ph[16], pl[16];
 #pragma unroll
-      for (int u4 = 0; u4 < 4; ++u4) {
-        const int U = h * 4 + u4;
-        const int off = row * 128 + ((U ^ (row & 7)) << 4);
+      for (int c = 0; c < 16; ++c) {
+        __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * c], v[2 * c + 1]);
+        ph[c] = *reinterpret_cast<uint32_t*>(&hh);
         if (X3) {
-          uint2 h0, l0, h1, l1;
-          split4(make_float4(v[8 * u4], v[8 * u4 + 1], v[8 * u4 + 2], v[8 * u4 + 3]), h0, l0);
-          split4(make_float4(v[8 * u4 + 4], v[8 * u4 + 5], v[8 * u4 + 6], v[8 * u4 + 7]), h1, l1);
-          *reinterpret_cast<uint4*>(ph + off) = make_uint4(h0.x, h0.y, h1.x, h1.y);
-          *reinterpret_cast<uint4*>(pl + off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
-        } else {
-          *reinterpret_cast<uint4*>(ph + off) =
-              make_uint4(pack_bf16x2(v[8 * u4], v[8 * u4 + 1]), pack_bf16x2(v[8 * u4 + 2], v[8 * u4 + 3]),
-                         pack_bf16x2(v[8 * u4 + 4], v[8 * u4 + 5]), pack_bf16x2(v[8 * u4 + 6], v[8 * u4 + 7]));
+          const float2 f = __bfloat1622float2(hh);
+          pl[c] = pack_bf16x2(v[2 * c] - f.x, v[2 * c + 1] - f.y);
         }
       }
-      fence_proxy_async_smem();
+      tmem_st16(tP(s) + lane_base + h * 16, ph);
+      if (X3) tmem_st16(tP(s) + lane_base + 32 + h * 16, pl);
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[s]);
       l_run = l_run * alpha + lsum;
@@ -922,7 +922,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
