@@ -286,11 +286,11 @@ __global__ void __launch_bounds__(192, 1)
 // chunks into swizzled shared memory and store them with TMA (bulk groups,
 // double-buffered per warp).  With split-K the raw f32 partial sums go to the
 // workspace through the same TMA-store path.
-template <int BN>
+template <int BN, bool X3 = false>
 struct PcCfg {
   static constexpr int A_BYTES = 128 * 128;  // 128 rows x 64 bf16
   static constexpr int B_BYTES = BN * 128;
-  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGE = (A_BYTES + B_BYTES) * (X3 ? 2 : 1);  // [A | B | A lo | B lo]
   static constexpr int STAGES = (192 * 1024 / STAGE) > 8 ? 8 : (192 * 1024 / STAGE);
   static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x (32 rows x 128 B)
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
@@ -309,11 +309,14 @@ struct PersArgs {
   int* err;
 };
 
-template <int BN, typename TO>
+// X3 (f32 operands): A and B arrive as bf16 hi and lo planes (split_planes);
+// every K step issues hi*hi + hi*lo + lo*hi.
+template <int BN, typename TO, bool X3>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_pers(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
-                 const __grid_constant__ CUtensorMap tC, PersArgs p) {
-  using Cfg = PcCfg<BN>;
+                 const __grid_constant__ CUtensorMap tC, const __grid_constant__ CUtensorMap tAl,
+                 const __grid_constant__ CUtensorMap tBl, PersArgs p) {
+  using Cfg = PcCfg<BN, X3>;
   constexpr int S = Cfg::STAGES;
   constexpr int BK = 64;  // bf16 K elements per 128-byte row
   constexpr int E = 64;   // bf16 MN elements per 128-byte chunk
@@ -330,6 +333,8 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
   auto sA = [&](int s) { return smem + s * Cfg::STAGE; };
   auto sB = [&](int s) { return smem + s * Cfg::STAGE + A_BYTES; };
+  auto sAl = [&](int s) { return smem + s * Cfg::STAGE + A_BYTES + B_BYTES; };
+  auto sBl = [&](int s) { return smem + s * Cfg::STAGE + 2 * A_BYTES + B_BYTES; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_mn = p.tiles_m * p.tiles_n;
@@ -375,6 +380,10 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tA);
     tma_prefetch_desc(&tB);
     tma_prefetch_desc(&tC);
+    if (X3) {
+      tma_prefetch_desc(&tAl);
+      tma_prefetch_desc(&tBl);
+    }
   }
   if (warp == 0) {
     tmem_alloc(tslot, 2 * BN);
@@ -398,20 +407,27 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
-          if (!p.a_mn) {
-            tma_load_3d(sA(s), &tA, &full[s], kb * BK, m0, bz);
-          } else {
+          mbar_expect_tx(&full[s], Cfg::STAGE);
 #pragma unroll
-            for (int j = 0; j < 128 / E; ++j)
-              tma_load_3d(sA(s) + j * (BK * 128), &tA, &full[s], m0 + j * E, kb * BK, bz);
-          }
-          if (!p.b_mn) {
-            tma_load_3d(sB(s), &tB, &full[s], kb * BK, n0, bz);
-          } else {
+          for (int part = 0; part < (X3 ? 2 : 1); ++part) {
+            const CUtensorMap* ma = part ? &tAl : &tA;
+            const CUtensorMap* mb = part ? &tBl : &tB;
+            uint8_t* da = part ? sAl(s) : sA(s);
+            uint8_t* db = part ? sBl(s) : sB(s);
+            if (!p.a_mn) {
+              tma_load_3d(da, ma, &full[s], kb * BK, m0, bz);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / E; ++j)
-              tma_load_3d(sB(s) + j * (BK * 128), &tB, &full[s], n0 + j * E, kb * BK, bz);
+              for (int j = 0; j < 128 / E; ++j)
+                tma_load_3d(da + j * (BK * 128), ma, &full[s], m0 + j * E, kb * BK, bz);
+            }
+            if (!p.b_mn) {
+              tma_load_3d(db, mb, &full[s], kb * BK, n0, bz);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / E; ++j)
+                tma_load_3d(db + j * (BK * 128), mb, &full[s], n0 + j * E, kb * BK, bz);
+            }
           }
         }
       }
@@ -446,8 +462,13 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
+          for (int kk = 0; kk < 4; ++kk) {
             umma_f16(dt, adesc(a0, kk), bdesc(b0, kk), idesc, (i | kk) != 0);
+            if (X3) {
+              umma_f16(dt, adesc(a0, kk), bdesc(smem_u32(sBl(s)), kk), idesc, 1);
+              umma_f16(dt, adesc(smem_u32(sAl(s)), kk), bdesc(b0, kk), idesc, 1);
+            }
+          }
           umma_commit(&empty[s]);
         }
         if (!ok) break;
@@ -658,7 +679,8 @@ struct Scratch {
   void* lent = nullptr;
   size_t lent_bytes = 0;
   int* err = nullptr;  // bounded-wait error word; nullptr: device_error_word()
-  void* owned = nullptr;
+  void* owned[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  int n_owned = 0;
   cudaStream_t owned_stream = nullptr;
   int get(size_t bytes, cudaStream_t st, float** out) {
     if (lent) {
@@ -669,15 +691,53 @@ struct Scratch {
       *out = static_cast<float*>(lent);
       return B200_OK;
     }
-    B200_CUDA_TRY(cudaMallocAsync(&owned, bytes, st));
+    return get_owned(bytes, st, reinterpret_cast<void**>(out));
+  }
+  // Stream-ordered memory from the CUDA pool, released when the call returns
+  // (after its kernels in stream order).
+  int get_owned(size_t bytes, cudaStream_t st, void** out) {
+    if (n_owned == 6) return set_error(B200_ERR_INVALID, "gemm: too many scratch buffers");
+    B200_CUDA_TRY(cudaMallocAsync(&owned[n_owned], bytes, st));
     owned_stream = st;
-    *out = static_cast<float*>(owned);
+    *out = owned[n_owned++];
     return B200_OK;
   }
   ~Scratch() {
-    if (owned) cudaFreeAsync(owned, owned_stream);
+    for (int i = 0; i < n_owned; ++i) cudaFreeAsync(owned[i], owned_stream);
   }
 };
+
+// f32 -> bf16 hi (rounded) and lo (rounded residual) planes, same element
+// offsets: x ~= hi + lo to ~2^-16 relative.
+__global__ void __launch_bounds__(256)
+    split_planes(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
+                 __nv_bfloat16* __restrict__ lo, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
+    if (i + 4 <= n && ((reinterpret_cast<uintptr_t>(x + i) | reinterpret_cast<uintptr_t>(hi + i) |
+                        reinterpret_cast<uintptr_t>(lo + i)) & 7) == 0 &&
+        ((reinterpret_cast<uintptr_t>(x + i)) & 15) == 0) {
+      const float4 v = *reinterpret_cast<const float4*>(x + i);
+      const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+      const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+      const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+      const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+      uint2 hv, lv;
+      hv.x = *reinterpret_cast<const uint32_t*>(&h0);
+      hv.y = *reinterpret_cast<const uint32_t*>(&h1);
+      lv.x = *reinterpret_cast<const uint32_t*>(&l0);
+      lv.y = *reinterpret_cast<const uint32_t*>(&l1);
+      *reinterpret_cast<uint2*>(hi + i) = hv;
+      *reinterpret_cast<uint2*>(lo + i) = lv;
+    } else {
+      for (int64_t k = i; k < n && k < i + 4; ++k) {
+        const __nv_bfloat16 h = __float2bfloat16_rn(x[k]);
+        hi[k] = h;
+        lo[k] = __float2bfloat16_rn(x[k] - __bfloat162float(h));
+      }
+    }
+  }
+}
 
 // Sums the split-K partials in a fixed order (deterministic) and applies the
 // epilogue: C[b,m,n] = epi(alpha * sum_s ws[b*splits+s][m][n] (+ bias[n])).
@@ -780,7 +840,12 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
 // Persistent bf16 launch.  Returns B200_ERR_UNSUPPORTED (without launching)
 // when the output cannot be stored with TMA (unaligned base or row pitch), so
 // the caller can fall back to gemm_tc.
-template <int BN, typename TO>
+// Elements spanned by a strided operand (the highest offset + 1).
+int64_t operand_span(int64_t batch, int64_t sb, int64_t r, int64_t sr, int64_t c, int64_t sc) {
+  return (batch - 1) * sb + (r - 1) * sr + (c - 1) * sc + 1;
+}
+
+template <int BN, typename TO, bool X3 = false>
 int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
                 int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
                 int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn,
@@ -798,7 +863,35 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
     const int64_t v = batch == 1 ? outer_stride * outer_dim : s;
     return (uint64_t)(((v * ES) + 15) / 16 * 16);
   };
-  CUtensorMap ta, tb, tc;
+  // f32 operands: split into bf16 hi / lo planes with the same element strides
+  const void* a_lo = nullptr;
+  const void* b_lo = nullptr;
+  if (X3) {
+    if (scratch.lent) return B200_ERR_UNSUPPORTED;  // planes need memory: use the tf32 kernel
+    // the planes' row pitch (2-byte elements) must still be a multiple of 16 bytes
+    auto ok16 = [](int64_t s) { return s == 1 || (s * 2) % 16 == 0; };
+    if (!ok16(sAm) || !ok16(sAk) || !ok16(sBk) || !ok16(sBn) ||
+        (batch > 1 && (!ok16(sAb) || !ok16(sBb))))
+      return B200_ERR_UNSUPPORTED;
+    const int64_t na = operand_span(batch, sAb, M, sAm, K, sAk);
+    const int64_t nb = operand_span(batch, sBb, K, sBk, N, sBn);
+    void *ah, *al, *bh, *bl;
+    if (int r = scratch.get_owned(2 * (size_t)na, st, &ah)) return r;
+    if (int r = scratch.get_owned(2 * (size_t)na, st, &al)) return r;
+    if (int r = scratch.get_owned(2 * (size_t)nb, st, &bh)) return r;
+    if (int r = scratch.get_owned(2 * (size_t)nb, st, &bl)) return r;
+    const unsigned ga = (unsigned)std::min<int64_t>((na + 1023) / 1024, 148 * 8);
+    const unsigned gb = (unsigned)std::min<int64_t>((nb + 1023) / 1024, 148 * 8);
+    split_planes<<<ga, 256, 0, st>>>((const float*)a, (__nv_bfloat16*)ah, (__nv_bfloat16*)al, na);
+    B200_LAUNCH_CHECK();
+    split_planes<<<gb, 256, 0, st>>>((const float*)b, (__nv_bfloat16*)bh, (__nv_bfloat16*)bl, nb);
+    B200_LAUNCH_CHECK();
+    a = ah;
+    b = bh;
+    a_lo = al;
+    b_lo = bl;
+  }
+  CUtensorMap ta, tb, tc, tal, tbl;
   int rc;
   if (!a_mn) {
     uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
@@ -824,6 +917,35 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
     rc = make_tmap(&tb, b, 3, dims, str, box, ES);
   }
   if (rc) return rc;
+  if (X3) {  // lo planes: same shapes and strides as the hi planes
+    if (!a_mn) {
+      uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
+      uint64_t str[2] = {(uint64_t)(sAm * ES), bstride(sAb, sAm, M)};
+      uint32_t box[3] = {(uint32_t)BK, 128, 1};
+      rc = make_tmap(&tal, a_lo, 3, dims, str, box, ES);
+    } else {
+      uint64_t dims[3] = {(uint64_t)M, (uint64_t)K, (uint64_t)batch};
+      uint64_t str[2] = {(uint64_t)(sAk * ES), bstride(sAb, sAk, K)};
+      uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
+      rc = make_tmap(&tal, a_lo, 3, dims, str, box, ES);
+    }
+    if (rc) return rc;
+    if (!b_mn) {
+      uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)batch};
+      uint64_t str[2] = {(uint64_t)(sBn * ES), bstride(sBb, sBn, N)};
+      uint32_t box[3] = {(uint32_t)BK, (uint32_t)BN, 1};
+      rc = make_tmap(&tbl, b_lo, 3, dims, str, box, ES);
+    } else {
+      uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)batch};
+      uint64_t str[2] = {(uint64_t)(sBk * ES), bstride(sBb, sBk, K)};
+      uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
+      rc = make_tmap(&tbl, b_lo, 3, dims, str, box, ES);
+    }
+    if (rc) return rc;
+  } else {
+    tal = ta;
+    tbl = tb;
+  }
   PersArgs p;
   p.M = (int)M;
   p.N = (int)N;
@@ -860,11 +982,11 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
     rc = make_tmap(&tc, c, 3, dims, str, box, so);
   }
   if (rc) return rc;
-  const int smem = PcCfg<BN>::SMEM;
-  if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pers<BN, TO>, smem, "gemm_tc_pers")) return rc2;
+  const int smem = PcCfg<BN, X3>::SMEM;
+  if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pers<BN, TO, X3>, smem, "gemm_tc_pers")) return rc2;
   const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch * sp.splits;
   const unsigned grid = (unsigned)std::min<int64_t>(num_tiles, num_sms());
-  gemm_tc_pers<BN, TO><<<grid, 192, smem, st>>>(ta, tb, tc, p);
+  gemm_tc_pers<BN, TO, X3><<<grid, 192, smem, st>>>(ta, tb, tc, tal, tbl, p);
   B200_LAUNCH_CHECK();
   if (ws) {
     const int64_t total = batch * M * N;
@@ -967,6 +1089,18 @@ int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64
                                           ldc, alpha, epilogue, a_mn, b_mn, st, scratch)
     if (es == 4) {
       const bool x3 = f32_matmul_3x();
+      if (x3 && use_persistent()) {
+        // bf16 hi/lo planes on the persistent kernel (3 bf16 MMAs per step)
+        int prc;
+#define B200_PERS3(BN_, TO_)                                                                      \
+  prc = launch_pers<BN_, TO_, true>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, \
+                                    ldc, alpha, epilogue, a_mn, b_mn, st, scratch)
+        if (N <= 64) { if (obf) B200_PERS3(64, __nv_bfloat16); else B200_PERS3(64, float); }
+        else if (N <= 128) { if (obf) B200_PERS3(128, __nv_bfloat16); else B200_PERS3(128, float); }
+        else { if (obf) B200_PERS3(256, __nv_bfloat16); else B200_PERS3(256, float); }
+#undef B200_PERS3
+        if (prc != B200_ERR_UNSUPPORTED) return prc;
+      }
       if (x3) {
         if (bn64) { if (obf) B200_TC(64, 4, __nv_bfloat16, true); else B200_TC(64, 4, float, true); }
         if (obf) B200_TC(128, 4, __nv_bfloat16, true); else B200_TC(128, 4, float, true);
