@@ -650,6 +650,56 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Narrow outputs (N <= 16, e.g. the 10-class logits and their gradients): one
+// thread per output row keeps all N accumulators; each block stages a 64-deep
+// slab of B in shared memory (read by every thread, broadcast).
+template <typename TI, typename TO, int NMAX>
+__global__ void __launch_bounds__(128)
+    gemm_skinny(const TI* __restrict__ A, const TI* __restrict__ B, TO* __restrict__ C,
+                const void* bias, int M, int N, int K, int64_t sAb, int64_t sAm, int64_t sAk,
+                int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, int64_t sCb, float alpha,
+                int epi, int splits, int kchunk, float* __restrict__ ws) {
+  __shared__ float Bs[64][NMAX];
+  const int bz = blockIdx.z / splits, ks = blockIdx.z % splits;
+  const int m = blockIdx.x * 128 + threadIdx.x;
+  A += (int64_t)bz * sAb;
+  B += (int64_t)bz * sBb;
+  const int kbeg = ks * kchunk, kend = min(K, kbeg + kchunk);
+  float acc[NMAX];
+#pragma unroll
+  for (int n = 0; n < NMAX; ++n) acc[n] = 0.f;
+  for (int k0 = kbeg; k0 < kend; k0 += 64) {
+    for (int i = threadIdx.x; i < 64 * NMAX; i += 128) {
+      const int kk = i / NMAX, n = i % NMAX, gk = k0 + kk;
+      Bs[kk][n] = (gk < kend && n < N) ? Io<TI>::to_f(B[(int64_t)gk * sBk + (int64_t)n * sBn]) : 0.f;
+    }
+    __syncthreads();
+    const int kn = min(64, kend - k0);
+    if (m < M) {
+      const TI* ar = A + (int64_t)m * sAm + (int64_t)k0 * sAk;
+      for (int kk = 0; kk < kn; ++kk) {
+        const float a = Io<TI>::to_f(ar[(int64_t)kk * sAk]);
+#pragma unroll
+        for (int n = 0; n < NMAX; ++n) acc[n] = fmaf(a, Bs[kk][n], acc[n]);
+      }
+    }
+    __syncthreads();
+  }
+  if (m >= M) return;
+#pragma unroll
+  for (int n = 0; n < NMAX; ++n) {
+    if (n >= N) break;
+    if (splits > 1) {
+      ws[((int64_t)blockIdx.z * M + m) * N + n] = acc[n];
+      continue;
+    }
+    float x = acc[n] * alpha;
+    if (epi == 1 || epi == 2) x += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n]);
+    if (epi >= 2) x = fmaxf(x, 0.f);
+    store_out<TO>(C + (int64_t)bz * sCb + (int64_t)m * ldc + n, x);
+  }
+}
+
 // Split-K plan: when the output tiles alone cannot fill the GPU, the K loop is
 // divided so that about two CTAs per SM run; each split keeps at least
 // `min_blocks` k-blocks so the partial-sum traffic stays small next to the
@@ -741,22 +791,71 @@ __global__ void __launch_bounds__(256)
 
 // Sums the split-K partials in a fixed order (deterministic) and applies the
 // epilogue: C[b,m,n] = epi(alpha * sum_s ws[b*splits+s][m][n] (+ bias[n])).
+// One thread per 4 consecutive outputs of a row (N % 4 == 0; rows = batch * M
+// of N outputs each); partials read as float4.
 template <typename TO>
 __global__ void __launch_bounds__(256)
     splitk_reduce(const float* __restrict__ ws, TO* __restrict__ C, const void* bias, int batch,
                   int M, int N, int splits, int64_t ldc, int64_t sCb, float alpha, int epi) {
-  const int64_t total = (int64_t)batch * M * N;
+  const int nq = N >> 2;
+  const int64_t total = (int64_t)batch * M * nq;
+  const int64_t mn_all = (int64_t)M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t b = i / ((int64_t)M * N), mn = i % ((int64_t)M * N);
-    const int m = (int)(mn / N), n = (int)(mn % N);
-    const float* src = ws + (b * splits) * (int64_t)M * N + mn;
+    const int64_t row = i / nq;  // b * M + m
+    const int n = (int)(i - row * nq) * 4;
+    const int64_t b = row / M;
+    const int m = (int)(row - b * M);
+    const float* src = ws + b * splits * mn_all + (int64_t)m * N + n;
+    float4 x = *reinterpret_cast<const float4*>(src);
+    for (int k = 1; k < splits; ++k) {
+      const float4 y = *reinterpret_cast<const float4*>(src + (int64_t)k * mn_all);
+      x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
+    }
+    float v[4] = {x.x * alpha, x.y * alpha, x.z * alpha, x.w * alpha};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (epi == 1 || epi == 2) v[j] += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n + j]);
+      if (epi >= 2) v[j] = fmaxf(v[j], 0.f);
+    }
+    TO* dst = C + b * sCb + (int64_t)m * ldc + n;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) store_out<TO>(dst + j, v[j]);
+  }
+}
+// Any N: one thread per output.
+template <typename TO>
+__global__ void __launch_bounds__(256)
+    splitk_reduce1(const float* __restrict__ ws, TO* __restrict__ C, const void* bias, int batch,
+                   int M, int N, int splits, int64_t ldc, int64_t sCb, float alpha, int epi) {
+  const int64_t total = (int64_t)batch * M * N;
+  const int64_t mn_all = (int64_t)M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / mn_all, mn = i - b * mn_all;
+    const int m = (int)(mn / N), n = (int)(mn - (int64_t)m * N);
+    const float* src = ws + b * splits * mn_all + mn;
     float x = 0.f;
-    for (int k = 0; k < splits; ++k) x += src[(int64_t)k * M * N];
+    for (int k = 0; k < splits; ++k) x += src[(int64_t)k * mn_all];
     x *= alpha;
     if (epi == 1 || epi == 2) x += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n]);
     if (epi >= 2) x = fmaxf(x, 0.f);
     store_out<TO>(C + b * sCb + (int64_t)m * ldc + n, x);
+  }
+}
+template <typename TO>
+void launch_splitk_reduce(const float* ws, TO* C, const void* bias, int64_t batch, int64_t M,
+                          int64_t N, int splits, int64_t ldc, float alpha, int epi, cudaStream_t st) {
+  if (N % 4 == 0) {
+    const int64_t total = batch * M * (N / 4);
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    splitk_reduce<TO><<<blocks, 256, 0, st>>>(ws, C, bias, (int)batch, (int)M, (int)N, splits, ldc,
+                                              M * ldc, alpha, epi);
+  } else {
+    const int64_t total = batch * M * N;
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
+    splitk_reduce1<TO><<<blocks, 256, 0, st>>>(ws, C, bias, (int)batch, (int)M, (int)N, splits, ldc,
+                                               M * ldc, alpha, epi);
   }
 }
 
@@ -828,10 +927,7 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   gemm_tc<BN, ES, TO, SPLIT><<<grid, 192, smem, st>>>(ta, tb, p);
   B200_LAUNCH_CHECK();
   if (sp.splits > 1) {
-    const int64_t total = batch * M * N;
-    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-    splitk_reduce<TO><<<blocks, 256, 0, st>>>(p.ws, (TO*)c, bias, (int)batch, (int)M, (int)N,
-                                              sp.splits, ldc, M * ldc, alpha, epi);
+    launch_splitk_reduce<TO>(p.ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
     B200_LAUNCH_CHECK();
   }
   return B200_OK;
@@ -989,10 +1085,7 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   gemm_tc_pers<BN, TO, X3><<<grid, 192, smem, st>>>(ta, tb, tc, tal, tbl, p);
   B200_LAUNCH_CHECK();
   if (ws) {
-    const int64_t total = batch * M * N;
-    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-    splitk_reduce<TO><<<blocks, 256, 0, st>>>(wsp, (TO*)c, bias, (int)batch, (int)M, (int)N,
-                                              sp.splits, ldc, M * ldc, alpha, epi);
+    launch_splitk_reduce<TO>(wsp, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
     B200_LAUNCH_CHECK();
   }
   return B200_OK;
@@ -1011,6 +1104,24 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
                 int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
                 int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, cudaStream_t st,
                 Scratch& scratch) {
+  if (N <= 16) {
+    const int64_t gx = (M + 127) / 128;
+    const SplitPlan sp = plan_splits(gx * batch, (int)((K + 63) / 64), 2, batch);
+    float* ws = nullptr;
+    if (sp.splits > 1) {
+      if (int rc = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &ws)) return rc;
+    }
+    dim3 grid((unsigned)gx, 1, (unsigned)(batch * sp.splits));
+    gemm_skinny<TI, TO, 16><<<grid, 128, 0, st>>>((const TI*)a, (const TI*)b, (TO*)c, bias, (int)M,
+                                                  (int)N, (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
+                                                  M * ldc, alpha, epi, sp.splits, sp.per_split * 64, ws);
+    B200_LAUNCH_CHECK();
+    if (sp.splits > 1) {
+      launch_splitk_reduce<TO>(ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
+      B200_LAUNCH_CHECK();
+    }
+    return B200_OK;
+  }
   const int64_t gx = (N + 63) / 64, gy = (M + 63) / 64;
   const SplitPlan sp = plan_splits(gx * gy * batch, (int)((K + 15) / 16), 8, batch);
   float* ws = nullptr;
@@ -1023,10 +1134,7 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
                                           epi, sp.splits, sp.per_split * 16, ws);
   B200_LAUNCH_CHECK();
   if (sp.splits > 1) {
-    const int64_t total = batch * M * N;
-    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-    splitk_reduce<TO><<<blocks, 256, 0, st>>>(ws, (TO*)c, bias, (int)batch, (int)M, (int)N,
-                                              sp.splits, ldc, M * ldc, alpha, epi);
+    launch_splitk_reduce<TO>(ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
     B200_LAUNCH_CHECK();
   }
   return B200_OK;
