@@ -21,6 +21,7 @@
 #include <thread>
 
 #include "b200_kernels.h"
+#include "gemm_ws.h"
 #include "b200_pjrt.h"
 #include "b200_pjrt_inspect.h"
 #include "passes.h"
@@ -576,14 +577,26 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
                                          st.dtype, dev.stream),
                    "sdpa");
             break;
-          case StepKind::Gemm:
-            kcheck(b200_gemm(slotp(st.in[0]), slotp(st.in[1]), slotp(st.out[0]),
-                             st.in.size() > 2 ? slotp(st.in[2]) : nullptr, st.ip[0], st.ip[1],
-                             st.ip[2], st.ip[3], st.ip[4], st.ip[5], st.ip[6], st.ip[7], st.ip[8],
-                             st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2, (int)st.ip[11],
-                             dev.stream),
+          case StepKind::Gemm: {
+            // split-K partials / bf16 planes come from the caching allocator
+            // (released after the launch: stream order protects the reuse)
+            const void* ga = slotp(st.in[0]);
+            const void* gb = slotp(st.in[1]);
+            void* gc = slotp(st.out[0]);
+            const void* gbias = st.in.size() > 2 ? slotp(st.in[2]) : nullptr;
+            const int64_t wsb = b200_gemm_workspace_bytes(
+                ga, gb, gc, gbias, st.ip[0], st.ip[1], st.ip[2], st.ip[3], st.ip[4], st.ip[5],
+                st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2,
+                (int)st.ip[11], dev.stream);
+            std::shared_ptr<DeviceMem> ws;
+            if (wsb > 0) ws = std::make_shared<DeviceMem>(&dev, (size_t)wsb);
+            kcheck(b200_gemm_ws(ga, gb, gc, gbias, st.ip[0], st.ip[1], st.ip[2], st.ip[3], st.ip[4],
+                                st.ip[5], st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10], st.fp[0],
+                                st.dtype, st.dtype2, (int)st.ip[11], dev.stream,
+                                ws ? ws->ptr : nullptr, wsb > 0 ? (size_t)wsb : 0),
                    "gemm");
             break;
+          }
           case StepKind::Copy:
             B200_CUDA(cudaMemcpyAsync(slotp(st.out[0]), slotp(st.in[0]),
                                       (size_t)p.slots[st.out[0]].bytes, cudaMemcpyDeviceToDevice,

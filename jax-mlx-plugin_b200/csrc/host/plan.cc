@@ -157,15 +157,26 @@ struct Builder {
     }
     return true;
   }
-  static constexpr int kRecomputeOps = 8;
-  // Non-cheap ops in n's fused expression, shared subexpressions counted once,
-  // stopping at values that live in memory.
+  // Recompute budget in arithmetic ops (a transcendental counts 4): an HBM
+  // byte costs far more than that many ops on this GPU.
+  static constexpr int kRecomputeOps = 16;
+  // Cost of n's fused expression, shared subexpressions counted once, stopping
+  // at values that live in memory.
   int expr_cost(int n, std::set<int>& seen) {
     if (seen.count(n) || slot.count(ValueRef{n, 0})) return 0;
     seen.insert(n);
     const Node& nd = g.nodes[n];
     if (!is_fusible(nd.op)) return 0;
-    int c = is_cheap(nd) ? 0 : 1;
+    int c = 0;
+    switch (nd.op) {
+      case Op::Exp: case Op::Expm1: case Op::Log: case Op::Log1p: case Op::Tanh:
+      case Op::Logistic: case Op::Erf: case Op::Pow: case Op::Sin: case Op::Cos: case Op::Tan:
+      case Op::Atan2: case Op::Cbrt:
+        c = 4;
+        break;
+      default:
+        c = is_cheap(nd) ? 0 : 1;
+    }
     for (const auto& o : nd.operands) {
       c += expr_cost(o.node, seen);
       if (c > kRecomputeOps) break;

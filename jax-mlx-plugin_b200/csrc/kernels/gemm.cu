@@ -19,6 +19,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "gemm_ws.h"
 #include "tc.cuh"
 
 namespace b200 {
@@ -725,9 +726,18 @@ SplitPlan plan_splits(int64_t tiles, int kblocks, int min_blocks, int64_t batch)
 // Where split-K partial sums live.  b200_gemm takes stream-ordered memory from
 // the CUDA memory pool (cudaMallocAsync / cudaFreeAsync on the launch stream);
 // a caller may instead lend a fixed buffer.
+// Returned by the launchers (before any launch) when a Scratch is only
+// measuring how much workspace a call needs.
+constexpr int kWorkspaceQueried = 1000;
+
 struct Scratch {
-  void* lent = nullptr;
+  void* lent = nullptr;  // one fixed buffer for split-K partials (b200_gemm_noalloc)
   size_t lent_bytes = 0;
+  bool has_arena = false;  // caller's workspace, carved in 256-byte units (b200_gemm_ws)
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0, arena_used = 0;
+  bool query = false;   // record sizes only (b200_gemm_workspace_bytes)
+  size_t queried = 0;
   int* err = nullptr;  // bounded-wait error word; nullptr: device_error_word()
   void* owned[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   int n_owned = 0;
@@ -743,9 +753,24 @@ struct Scratch {
     }
     return get_owned(bytes, st, reinterpret_cast<void**>(out));
   }
-  // Stream-ordered memory from the CUDA pool, released when the call returns
-  // (after its kernels in stream order).
+  // Workspace for this call: carved from the caller's arena, or stream-ordered
+  // memory from the CUDA pool released when the call returns (after its
+  // kernels in stream order).
   int get_owned(size_t bytes, cudaStream_t st, void** out) {
+    const size_t rounded = (bytes + 255) / 256 * 256;
+    if (query) {
+      queried += rounded;
+      *out = reinterpret_cast<void*>((uintptr_t)4096);  // encodes descriptors; never launched
+      return B200_OK;
+    }
+    if (has_arena) {
+      if (arena_used + rounded > arena_bytes)
+        return set_error(B200_ERR_INVALID, "gemm: workspace of " + std::to_string(arena_bytes) +
+                                               " bytes is too small");
+      *out = arena + arena_used;
+      arena_used += rounded;
+      return B200_OK;
+    }
     if (n_owned == 6) return set_error(B200_ERR_INVALID, "gemm: too many scratch buffers");
     B200_CUDA_TRY(cudaMallocAsync(&owned[n_owned], bytes, st));
     owned_stream = st;
@@ -923,6 +948,7 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   if (sp.splits > 1) {
     if (int rc2 = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &p.ws)) return rc2;
   }
+  if (scratch.query) return kWorkspaceQueried;
   dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(batch * sp.splits));
   gemm_tc<BN, ES, TO, SPLIT><<<grid, 192, smem, st>>>(ta, tb, p);
   B200_LAUNCH_CHECK();
@@ -962,6 +988,8 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   // f32 operands: split into bf16 hi / lo planes with the same element strides
   const void* a_lo = nullptr;
   const void* b_lo = nullptr;
+  int64_t na = 0, nb = 0;
+  void *ah = nullptr, *al = nullptr, *bh = nullptr, *bl = nullptr;
   if (X3) {
     if (scratch.lent) return B200_ERR_UNSUPPORTED;  // planes need memory: use the tf32 kernel
     // the planes' row pitch (2-byte elements) must still be a multiple of 16 bytes
@@ -969,13 +997,22 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
     if (!ok16(sAm) || !ok16(sAk) || !ok16(sBk) || !ok16(sBn) ||
         (batch > 1 && (!ok16(sAb) || !ok16(sBb))))
       return B200_ERR_UNSUPPORTED;
-    const int64_t na = operand_span(batch, sAb, M, sAm, K, sAk);
-    const int64_t nb = operand_span(batch, sBb, K, sBk, N, sBn);
-    void *ah, *al, *bh, *bl;
+  }
+  // all workspace first, so that a size query stops before anything launches
+  float* wsp = nullptr;
+  if (ws) {
+    if (int rc2 = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &wsp)) return rc2;
+  }
+  if (X3) {
+    na = operand_span(batch, sAb, M, sAm, K, sAk);
+    nb = operand_span(batch, sBb, K, sBk, N, sBn);
     if (int r = scratch.get_owned(2 * (size_t)na, st, &ah)) return r;
     if (int r = scratch.get_owned(2 * (size_t)na, st, &al)) return r;
     if (int r = scratch.get_owned(2 * (size_t)nb, st, &bh)) return r;
     if (int r = scratch.get_owned(2 * (size_t)nb, st, &bl)) return r;
+  }
+  if (scratch.query) return kWorkspaceQueried;
+  if (X3) {
     const unsigned ga = (unsigned)std::min<int64_t>((na + 1023) / 1024, 148 * 8);
     const unsigned gb = (unsigned)std::min<int64_t>((nb + 1023) / 1024, 148 * 8);
     split_planes<<<ga, 256, 0, st>>>((const float*)a, (__nv_bfloat16*)ah, (__nv_bfloat16*)al, na);
@@ -1063,9 +1100,7 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   p.out_ws = ws ? 1 : 0;
   p.err = scratch.err ? scratch.err : device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
-  float* wsp = nullptr;
   if (ws) {
-    if (int rc2 = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &wsp)) return rc2;
     uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)(batch * sp.splits)};
     uint64_t str[2] = {(uint64_t)(N * 4), (uint64_t)(M * N * 4)};
     uint32_t box[3] = {32, 32, 1};
@@ -1111,6 +1146,7 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
     if (sp.splits > 1) {
       if (int rc = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &ws)) return rc;
     }
+    if (scratch.query) return kWorkspaceQueried;
     dim3 grid((unsigned)gx, 1, (unsigned)(batch * sp.splits));
     gemm_skinny<TI, TO, 16><<<grid, 128, 0, st>>>((const TI*)a, (const TI*)b, (TO*)c, bias, (int)M,
                                                   (int)N, (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
@@ -1128,6 +1164,7 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
   if (sp.splits > 1) {
     if (int rc = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &ws)) return rc;
   }
+  if (scratch.query) return kWorkspaceQueried;
   dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(batch * sp.splits));
   gemm_simt<TI, TO><<<grid, 256, 0, st>>>((const TI*)a, (const TI*)b, (TO*)c, bias, (int)M, (int)N,
                                           (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, M * ldc, alpha,
@@ -1248,6 +1285,37 @@ extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias
                          int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
                          int in_dtype, int out_dtype, int epilogue, void* stream) {
   b200::Scratch scratch;  // split-K partials from cudaMallocAsync on `stream`
+  return b200::gemm_dispatch(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
+                             alpha, in_dtype, out_dtype, epilogue, stream, scratch);
+}
+
+// Workspace the call would take (split-K partials, bf16 planes of f32
+// operands), without launching anything; the PJRT runtime hands it over from
+// its caching allocator through b200_gemm_ws.  -1 on an argument error.
+extern "C" int64_t b200_gemm_workspace_bytes(const void* a, const void* b, void* c, const void* bias,
+                                             int64_t batch, int64_t M, int64_t N, int64_t K,
+                                             int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
+                                             int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
+                                             int in_dtype, int out_dtype, int epilogue, void* stream) {
+  b200::Scratch scratch;
+  scratch.query = true;
+  const int rc = b200::gemm_dispatch(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn,
+                                     ldc, alpha, in_dtype, out_dtype, epilogue, stream, scratch);
+  if (rc != b200::kWorkspaceQueried && rc != B200_OK) return -1;
+  return (int64_t)scratch.queried;
+}
+
+// b200_gemm taking its workspace from the caller (`ws`, `ws_bytes` from
+// b200_gemm_workspace_bytes for the same arguments; may be null when that is 0).
+extern "C" int b200_gemm_ws(const void* a, const void* b, void* c, const void* bias, int64_t batch,
+                            int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
+                            int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha,
+                            int in_dtype, int out_dtype, int epilogue, void* stream, void* ws,
+                            size_t ws_bytes) {
+  b200::Scratch scratch;
+  scratch.has_arena = true;
+  scratch.arena = static_cast<uint8_t*>(ws);
+  scratch.arena_bytes = ws ? ws_bytes : 0;
   return b200::gemm_dispatch(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
                              alpha, in_dtype, out_dtype, epilogue, stream, scratch);
 }
