@@ -527,7 +527,43 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
       for (int s : st.out) ensure(d, s);
       for (int s : st.in) ensure(d, s);
     }
-    if (st.kind == StepKind::AllReduce) {
+    if (st.kind == StepKind::AllReduce && !st.args.empty()) {
+      // bucketed: copy the pieces into one flat buffer, one collective, copy back
+      const size_t es = (size_t)dtype_size((DType)st.dtype);
+      const int bucket = st.out.back();
+      std::vector<Device*> dd;
+      std::vector<const void*> in;
+      std::vector<void*> out;
+      for (size_t d = 0; d < nd; ++d) {
+        Device& dev = *devs[d]->dev;
+        dev.activate();
+        uint8_t* bk = static_cast<uint8_t*>(ptr[d][bucket]);
+        for (size_t k = 0; k < st.args.size(); k += 2) {
+          if (e.num_replicas == 1) {
+            B200_CUDA(cudaMemcpyAsync(ptr[d][st.args[k + 1].slot], ptr[d][st.args[k].slot],
+                                      (size_t)st.args[k + 1].i * es, cudaMemcpyDeviceToDevice, dev.stream));
+          } else {
+            B200_CUDA(cudaMemcpyAsync(bk + (size_t)st.args[k].i * es, ptr[d][st.args[k].slot],
+                                      (size_t)st.args[k + 1].i * es, cudaMemcpyDeviceToDevice, dev.stream));
+          }
+        }
+        dd.push_back(devs[d]->dev);
+        in.push_back(bk);
+        out.push_back(bk);
+      }
+      if (e.num_replicas != 1) {
+        NcclComms& comm = comms_for(c, e);
+        nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1]);
+        for (size_t d = 0; d < nd; ++d) {
+          Device& dev = *devs[d]->dev;
+          dev.activate();
+          const uint8_t* bk = static_cast<const uint8_t*>(ptr[d][bucket]);
+          for (size_t k = 0; k < st.args.size(); k += 2)
+            B200_CUDA(cudaMemcpyAsync(ptr[d][st.args[k + 1].slot], bk + (size_t)st.args[k].i * es,
+                                      (size_t)st.args[k + 1].i * es, cudaMemcpyDeviceToDevice, dev.stream));
+        }
+      }
+    } else if (st.kind == StepKind::AllReduce) {
       std::vector<Device*> dd;
       std::vector<const void*> in;
       std::vector<void*> out;

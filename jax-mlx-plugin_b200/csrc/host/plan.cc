@@ -515,6 +515,60 @@ struct Builder {
     }
   }
 
+  // Consecutive all_reduce steps over the same replica groups, reduction and
+  // element type become one NCCL call on a flat bucket (data-parallel gradient
+  // means: one collective instead of one per parameter).  args[2k] = (input
+  // slot, offset in elements), args[2k+1] = (output slot, element count); the
+  // bucket is the last output slot.
+  void bucket_all_reduces() {
+    std::vector<Step> merged;
+    for (size_t i = 0; i < p.steps.size();) {
+      const Step& a = p.steps[i];
+      size_t j = i + 1;
+      if (a.kind == StepKind::AllReduce && a.args.empty()) {
+        auto same = [&](const Step& b) {
+          return b.kind == StepKind::AllReduce && b.args.empty() && b.dtype == a.dtype &&
+                 std::vector<int64_t>(b.ip.begin() + 1, b.ip.end()) ==
+                     std::vector<int64_t>(a.ip.begin() + 1, a.ip.end());
+        };
+        while (j < p.steps.size() && same(p.steps[j])) ++j;
+      }
+      if (j - i < 2) {
+        merged.push_back(p.steps[i]);
+        i = j;
+        continue;
+      }
+      Step b;
+      b.kind = StepKind::AllReduce;
+      b.name = "all_reduce_bucket";
+      b.dtype = a.dtype;
+      int64_t off = 0;
+      for (size_t k = i; k < j; ++k) {
+        const Step& s = p.steps[k];
+        Arg in;
+        in.slot = s.in[0];
+        in.i = off;
+        Arg out;
+        out.slot = s.out[0];
+        out.i = s.ip[0];
+        b.args.push_back(in);
+        b.args.push_back(out);
+        b.in.push_back(s.in[0]);
+        b.out.push_back(s.out[0]);
+        off += (s.ip[0] + 63) / 64 * 64;  // 256-byte aligned pieces
+      }
+      TensorType bt;
+      bt.dtype = (DType)a.dtype;
+      bt.dims = {off};
+      b.out.push_back(new_slot(Slot::TEMP, bt, "all_reduce_bucket"));
+      b.ip = a.ip;
+      b.ip[0] = off;
+      merged.push_back(b);
+      i = j;
+    }
+    p.steps.swap(merged);
+  }
+
   std::vector<int> pending;  // materialized loop values not yet emitted
   void flush_loops() {
     if (pending.empty()) return;
@@ -533,8 +587,37 @@ struct Builder {
   }
 
   // -------------------------------------------------------------- driver --
+  // Schedule every all_reduce whose operands do not themselves come out of an
+  // all_reduce right after the last node it does not depend on, and their
+  // consumers after them: the collectives become consecutive steps that
+  // bucket_all_reduces merges (one NCCL call for all of a step's gradients).
+  std::vector<int> group_all_reduces(const std::vector<int>& order) {
+    std::vector<char> dep(g.nodes.size(), 0);  // depends on an all_reduce output
+    bool any = false;
+    for (int n : order) {
+      const Node& nd = g.nodes[n];
+      char d = 0;
+      for (auto& o : nd.operands) d |= dep[o.node];
+      if (nd.op == Op::AllReduce) any = true;
+      dep[n] = d || nd.op == Op::AllReduce;
+    }
+    if (!any) return order;
+    std::vector<int> head, mid, tail;
+    for (int n : order) {
+      const Node& nd = g.nodes[n];
+      bool in_dep = false;
+      for (auto& o : nd.operands) in_dep |= dep[o.node] != 0;
+      if (!dep[n]) head.push_back(n);
+      else if (nd.op == Op::AllReduce && !in_dep) mid.push_back(n);
+      else tail.push_back(n);
+    }
+    head.insert(head.end(), mid.begin(), mid.end());
+    head.insert(head.end(), tail.begin(), tail.end());
+    return head;
+  }
+
   void run() {
-    auto order = topo();
+    auto order = group_all_reduces(topo());
     // parameters
     for (size_t i = 0; i < g.nodes.size(); ++i) {
       const Node& n = g.nodes[i];
@@ -637,6 +720,7 @@ struct Builder {
       }
     }
     flush_loops();
+    bucket_all_reduces();
     // outputs
     std::set<int> used;
     for (size_t i = 0; i < g.outputs.size(); ++i) {

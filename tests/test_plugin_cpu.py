@@ -84,8 +84,12 @@ def test_config_programs_fuse_and_compile():
     assert pjrt.inspect(programs.layer_norm(), 1).count("layer_norm in=") == 1
     for text in (programs.mlp_step(), programs.cnn_step(), programs.mlp_step(batch=512, num_replicas=2)):
         assert pjrt.inspect(text, 3).startswith("ok ")
+    # the loss and all 8 gradient means go out as one bucketed collective
     plan = pjrt.inspect(programs.mlp_step(batch=512, num_replicas=2), 1)
-    assert plan.count("all_reduce") == 9
+    steps = plan.split("steps:")[1]
+    assert steps.count("all_reduce_bucket in=") == 1 and steps.count("all_reduce in=") == 0
+    bucket = [l for l in steps.splitlines() if "all_reduce_bucket" in l][0]
+    assert bucket.split(" out=")[0].count(",") == 9  # 9 inputs, comma-terminated
 
 
 def test_non_causal_and_bnth_attention_also_match():
