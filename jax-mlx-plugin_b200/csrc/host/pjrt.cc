@@ -128,6 +128,27 @@ struct Exe {
   // B200_TIMING=1: device time of each Execute's launch sequence (device 0)
   std::mutex timing_mu;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timings;
+  // CUDA-graph replay (one device per Execute), by device ordinal
+  std::map<int, std::unique_ptr<struct GraphState>> graphs;
+  int graph_ok = -1;  // -1 undecided, 0 no, 1 yes
+};
+
+// CUDA-graph replay of a plan on one device.  The plan's slots get fixed
+// buffers; the launch sequence between collectives is captured once (after an
+// eager warm-up run) and replayed: an Execute then costs one copy per argument
+// into the fixed parameter buffers, one graph launch per segment, and one copy
+// per output into a fresh buffer, instead of a host launch per kernel.
+struct GraphState {
+  int eager_runs = 0;
+  bool disabled = false;
+  std::vector<std::vector<void*>> ptr;  // [1][slot] fixed pointers
+  std::vector<std::shared_ptr<DeviceMem>> mem;
+  std::shared_ptr<DeviceMem> gemm_ws;   // workspace shared by the captured GEMMs
+  std::vector<std::pair<int, int>> items;  // (0, graph index) or (1, step index)
+  std::vector<cudaGraphExec_t> execs;
+  ~GraphState() {
+    for (auto g : execs) cudaGraphExecDestroy(g);
+  }
 };
 
 }  // namespace
@@ -445,6 +466,113 @@ NcclComms& comms_for(PJRT_Client* c, Exe& e) {
   return ref;
 }
 
+// Graph replay applies to single-device Executes of plans whose slots fit a
+// fixed 1 GiB (each slot gets its own buffer, no reuse); B200_GRAPHS=0 turns it
+// off.
+GraphState* graph_state(Exe& e, const std::vector<PJRT_Device*>& devs) {
+  if (devs.size() != 1) return nullptr;
+  static const bool off = [] {
+    const char* v = std::getenv("B200_GRAPHS");
+    return v && std::strcmp(v, "0") == 0;
+  }();
+  if (off) return nullptr;
+  const Plan& p = e.plan;
+  if (e.graph_ok < 0) {
+    int64_t bytes = 0;
+    for (auto& sl : p.slots)
+      if (sl.kind != Slot::CONST) bytes += sl.bytes;
+    e.graph_ok = (bytes <= (1ll << 30) && p.steps.size() >= 4) ? 1 : 0;
+  }
+  if (!e.graph_ok) return nullptr;
+  auto& g = e.graphs[devs[0]->dev->ordinal];
+  if (!g) g = std::make_unique<GraphState>();
+  return g->disabled ? nullptr : g.get();
+}
+
+template <typename StepFn>
+void build_graphs(Exe& e, GraphState& gs, PJRT_Device* pd, StepFn& exec_step,
+                  std::shared_ptr<DeviceMem>*& gemm_ws_override) {
+  const Plan& p = e.plan;
+  Device& dev = *pd->dev;
+  dev.activate();
+  auto& mod = *e.modules.at(dev.ordinal);
+  gs.ptr.assign(1, std::vector<void*>(p.slots.size(), nullptr));
+  gs.mem.assign(p.slots.size(), nullptr);
+  for (size_t s = 0; s < p.slots.size(); ++s) {
+    const Slot& sl = p.slots[s];
+    if (sl.kind == Slot::CONST) {
+      gs.ptr[0][s] = mod.consts.at(sl.index)->ptr;
+    } else {
+      gs.mem[s] = std::make_shared<DeviceMem>(&dev, (size_t)std::max<int64_t>(sl.bytes, 1));
+      gs.ptr[0][s] = gs.mem[s]->ptr;
+    }
+  }
+  int64_t ws = 0;
+  auto P = [&](int s) -> void* { return s < 0 ? nullptr : gs.ptr[0][s]; };
+  for (const Step& st : p.steps)
+    if (st.kind == StepKind::Gemm)
+      ws = std::max<int64_t>(ws, b200_gemm_workspace_bytes(
+                                     P(st.in[0]), P(st.in[1]), P(st.out[0]),
+                                     st.in.size() > 2 ? P(st.in[2]) : nullptr, st.ip[0], st.ip[1],
+                                     st.ip[2], st.ip[3], st.ip[4], st.ip[5], st.ip[6], st.ip[7],
+                                     st.ip[8], st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2,
+                                     (int)st.ip[11], dev.stream));
+  if (ws > 0) gs.gemm_ws = std::make_shared<DeviceMem>(&dev, (size_t)ws);
+  gemm_ws_override = &gs.gemm_ws;
+  try {
+    size_t si = 0;
+    while (si < p.steps.size()) {
+      if (p.steps[si].kind == StepKind::AllReduce) {
+        gs.items.push_back({1, (int)si});
+        ++si;
+        continue;
+      }
+      cudaGraph_t graph = nullptr;
+      B200_CUDA(cudaStreamBeginCapture(dev.stream, cudaStreamCaptureModeRelaxed));
+      try {
+        for (; si < p.steps.size() && p.steps[si].kind != StepKind::AllReduce; ++si) exec_step(si, gs.ptr);
+      } catch (...) {
+        cudaStreamEndCapture(dev.stream, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+      }
+      B200_CUDA(cudaStreamEndCapture(dev.stream, &graph));
+      cudaGraphExec_t exec = nullptr;
+      const cudaError_t r = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      B200_CUDA(r);
+      gs.items.push_back({0, (int)gs.execs.size()});
+      gs.execs.push_back(exec);
+    }
+  } catch (...) {
+    // capture did not work for this plan: stay eager
+    for (auto g : gs.execs) cudaGraphExecDestroy(g);
+    gs.execs.clear();
+    gs.items.clear();
+    gs.disabled = true;
+    cudaGetLastError();
+  }
+  gemm_ws_override = nullptr;
+}
+
+template <typename StepFn>
+void run_graphs(Exe& e, GraphState& gs, PJRT_Device* pd, const std::vector<void*>& args,
+                StepFn& exec_step, std::shared_ptr<DeviceMem>*& gemm_ws_override) {
+  const Plan& p = e.plan;
+  Device& dev = *pd->dev;
+  dev.activate();
+  for (int s : p.param_slots)
+    if (p.slots[s].bytes > 0)
+      B200_CUDA(cudaMemcpyAsync(gs.ptr[0][s], args[s], (size_t)p.slots[s].bytes,
+                                cudaMemcpyDeviceToDevice, dev.stream));
+  gemm_ws_override = &gs.gemm_ws;
+  for (auto& it : gs.items) {
+    if (it.first == 0) B200_CUDA(cudaGraphLaunch(gs.execs[it.second], dev.stream));
+    else exec_step((size_t)it.second, gs.ptr);
+  }
+  gemm_ws_override = nullptr;
+}
+
 void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
   Exe& e = *le->exe;
   PJRT_Client* c = e.client;
@@ -521,12 +649,10 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
     owned[d][s] = std::make_shared<DeviceMem>(devs[d]->dev, (size_t)std::max<int64_t>(sl.bytes, 1));
     ptr[d][s] = owned[d][s]->ptr;
   };
-  for (size_t si = 0; si < p.steps.size(); ++si) {
+  std::shared_ptr<DeviceMem>* gemm_ws_override = nullptr;
+  // one step of the plan on every device, with slot pointers `ptr`
+  auto exec_step = [&](size_t si, std::vector<std::vector<void*>>& ptr) {
     const Step& st = p.steps[si];
-    for (size_t d = 0; d < nd; ++d) {
-      for (int s : st.out) ensure(d, s);
-      for (int s : st.in) ensure(d, s);
-    }
     if (st.kind == StepKind::AllReduce && !st.args.empty()) {
       // bucketed: copy the pieces into one flat buffer, one collective, copy back
       const size_t es = (size_t)dtype_size((DType)st.dtype);
@@ -625,7 +751,11 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
                 st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2,
                 (int)st.ip[11], dev.stream);
             std::shared_ptr<DeviceMem> ws;
-            if (wsb > 0) ws = std::make_shared<DeviceMem>(&dev, (size_t)wsb);
+            if (wsb > 0) {
+              // graph capture / replay: the graph's fixed workspace
+              if (gemm_ws_override && *gemm_ws_override) ws = *gemm_ws_override;
+              else ws = std::make_shared<DeviceMem>(&dev, (size_t)wsb);
+            }
             kcheck(b200_gemm_ws(ga, gb, gc, gbias, st.ip[0], st.ip[1], st.ip[2], st.ip[3], st.ip[4],
                                 st.ip[5], st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10], st.fp[0],
                                 st.dtype, st.dtype2, (int)st.ip[11], dev.stream,
@@ -643,6 +773,26 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
         }
       }
     }
+  };
+  GraphState* gs = graph_state(e, devs);
+  if (gs && gs->execs.empty() && gs->eager_runs >= 1) build_graphs(e, *gs, devs[0], exec_step, gemm_ws_override);
+  if (gs && !gs->execs.empty()) {
+    run_graphs(e, *gs, devs[0], ptr[0], exec_step, gemm_ws_override);
+    for (size_t o = 0; o < p.output_slots.size(); ++o) {
+      const int sl = p.output_slots[o];
+      owned[0][sl] = std::make_shared<DeviceMem>(devs[0]->dev, (size_t)std::max<int64_t>(p.slots[sl].bytes, 1));
+      B200_CUDA(cudaMemcpyAsync(owned[0][sl]->ptr, gs->ptr[0][sl], (size_t)p.slots[sl].bytes,
+                                cudaMemcpyDeviceToDevice, devs[0]->dev->stream));
+    }
+  } else {
+  if (gs) gs->eager_runs++;
+  for (size_t si = 0; si < p.steps.size(); ++si) {
+    const Step& st = p.steps[si];
+    for (size_t d = 0; d < nd; ++d) {
+      for (int s : st.out) ensure(d, s);
+      for (int s : st.in) ensure(d, s);
+    }
+    exec_step(si, ptr);
     if (env_flag("B200_SYNC_STEPS")) {
       for (size_t d = 0; d < nd; ++d) {
         devs[d]->dev->activate();
@@ -658,6 +808,7 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
             owned[d][s].reset();
             ptr[d][s] = nullptr;
           }
+  }
   }
   if (timing) {
     devs[0]->dev->activate();

@@ -389,3 +389,19 @@ def test_custom_call_layer_norm_and_backward(client, dt):
     assert_close(got[0], restate.layer_norm_ref(x, None, w, bb, 1e-5), tol, "mlx_layer_norm")
     for name, gg, r in zip(("dx", "dw", "db"), got[1:], restate.layer_norm_bwd_ref(x, w, dy, 1e-5)):
         assert_close(gg, r, tol, f"mlx_layer_norm_bwd {name}")
+
+
+def test_repeated_execute_replays_cuda_graph(client):
+    """The second and later Executes of a small plan replay a captured CUDA graph
+    (fixed buffers, arguments copied in, outputs copied out): every call must
+    still compute from its own arguments."""
+    dims = (64, 128, 10)
+    exe = client.compile(programs.mlp_step(batch=32, dims=dims, emit="grads"))
+    for seed in (20, 21, 22, 23):
+        rng = np.random.default_rng(seed)
+        params, x, lab = _exact_mlp_inputs(rng, dims, 32)
+        outs = [o.to_numpy() for o in exe.execute([[client.buffer_from_numpy(a) for a in params + [x, lab]]])[0]]
+        loss, new = restate.mlp_step_ref(params, x, lab, lr=1.0)
+        assert_close(outs[0], loss, 2e-3, f"loss (call {seed - 19})")
+        for p, g, r in zip(params, outs[1:], new):
+            assert_close(g, p.astype(np.float64) - r, 2e-3, f"grad (call {seed - 19})")
