@@ -141,6 +141,13 @@ class Rig:
         self.stream = torch.cuda.ExternalStream(self.client.device_stream(self.dev))
         self.flush = torch.ones(2 * 1024 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
         self.sink = None
+        self.world = world
+
+    def barrier(self):
+        """All ranks enter (and leave) a timed region together."""
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
 
     def time_steps(self, fn, steps: int, warmup: int, flush: bool = True):
         torch = self.torch
@@ -151,10 +158,13 @@ class Rig:
         # loaded a full collection stalls the launching thread for tens of ms)
         gc.collect()
         gc.disable()
+        self.barrier()
         try:
-            return self._timed(fn, steps, flush)
+            ts = self._timed(fn, steps, flush)
         finally:
             gc.enable()
+        self.barrier()
+        return ts
 
     def _timed(self, fn, steps: int, flush: bool):
         torch = self.torch
