@@ -7,6 +7,7 @@
 #include <nccl.h>
 #include <nvrtc.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 
@@ -99,17 +100,16 @@ struct Driver {
   CUresult (*ModuleLoadData)(CUmodule*, const void*);
   CUresult (*ModuleGetFunction)(CUfunction*, CUmodule, const char*);
   CUresult (*ModuleUnload)(CUmodule);
-  CUresult (*LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
-                           unsigned, CUstream, void**, void**);
   CUresult (*GetErrorString)(CUresult, const char**);
+  CUresult (*LaunchKernelEx)(const CUlaunchConfig*, CUfunction, void**, void**);
   static Driver& get() {
     static Driver d = [] {
       Driver x;
       x.ModuleLoadData = driver_fn<decltype(x.ModuleLoadData)>("cuModuleLoadData");
       x.ModuleGetFunction = driver_fn<decltype(x.ModuleGetFunction)>("cuModuleGetFunction");
       x.ModuleUnload = driver_fn<decltype(x.ModuleUnload)>("cuModuleUnload");
-      x.LaunchKernel = driver_fn<decltype(x.LaunchKernel)>("cuLaunchKernel");
       x.GetErrorString = driver_fn<decltype(x.GetErrorString)>("cuGetErrorString");
+      x.LaunchKernelEx = driver_fn<decltype(x.LaunchKernelEx)>("cuLaunchKernelEx");
       return x;
     }();
     return d;
@@ -178,12 +178,30 @@ std::unique_ptr<LoadedModule> load_module(Device& d, const std::string& cubin,
   return m;
 }
 
+// Generated kernels begin with griddepcontrol.wait, so they are launched with
+// programmatic stream serialization (B200_PDL=0 turns it off): a kernel's
+// blocks may be scheduled while the previous kernel on the stream finishes.
 void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[3], int smem,
             std::vector<void*>& args) {
-  cu_check(Driver::get().LaunchKernel(f, (unsigned)grid[0], (unsigned)grid[1], (unsigned)grid[2],
-                                      (unsigned)block[0], (unsigned)block[1], (unsigned)block[2],
-                                      (unsigned)smem, (CUstream)d.stream, args.data(), nullptr),
-           "cuLaunchKernel");
+  static const bool pdl = [] {
+    const char* e = getenv("B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  CUlaunchAttribute attr[1];
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  CUlaunchConfig cfg = {};
+  cfg.gridDimX = (unsigned)grid[0];
+  cfg.gridDimY = (unsigned)grid[1];
+  cfg.gridDimZ = (unsigned)grid[2];
+  cfg.blockDimX = (unsigned)block[0];
+  cfg.blockDimY = (unsigned)block[1];
+  cfg.blockDimZ = (unsigned)block[2];
+  cfg.sharedMemBytes = (unsigned)smem;
+  cfg.hStream = (CUstream)d.stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cu_check(Driver::get().LaunchKernelEx(&cfg, f, args.data(), nullptr), "cuLaunchKernelEx");
 }
 
 // ------------------------------------------------------------------ NCCL --

@@ -1,6 +1,8 @@
 // Error state and version of the kernel library.
 #include "common.cuh"
 
+#include <stdlib.h>
+
 namespace b200 {
 namespace {
 thread_local std::string g_last_error;
@@ -8,6 +10,13 @@ thread_local std::string g_last_error;
 int set_error(int code, const std::string& msg) {
   g_last_error = msg;
   return code;
+}
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 }  // namespace b200
 

@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <string>
+#include <utility>
 
 #include "b200_kernels.h"
 
@@ -49,6 +50,42 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+
+// Programmatic dependent launch.  Kernels started through launch_k() may be
+// launched while the previous kernel on the stream is still finishing.  Every
+// such kernel calls pdl_wait() before its first global memory access:
+// griddepcontrol.wait returns once the previous grid has completed and its
+// writes are visible, so reads after it see the producer's results and writes
+// after it cannot race the producer's reads.  No kernel triggers its dependents
+// early (griddepcontrol.launch_dependents): the trigger is the implicit one at
+// block exit, so the next grid's launch overlaps only this grid's drain.  The
+// wait is a no-op for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// False when the environment sets B200_PDL=0 (every launch then waits for the
+// previous kernel to finish before it starts, as a plain <<<>>> launch does).
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with the programmatic-serialization attribute; the kernel
+// must begin with pdl_wait().
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// launch_k + the launch-error check, returning from the calling function.
+#define B200_LAUNCH(...) B200_CUDA_TRY(::b200::launch_k(__VA_ARGS__))
 
 inline int num_sms() {
   static int n = [] {

@@ -91,6 +91,7 @@ template <int BN, int ES, typename TO, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
             GemmArgs p) {
+  pdl_wait();
   using Cfg = TcCfg<BN, ES, SPLIT>;
   constexpr int S = Cfg::STAGES;
   constexpr int BK = 128 / ES;  // K elements per 128-byte row
@@ -317,6 +318,7 @@ __global__ void __launch_bounds__(192, 1)
     gemm_tc_pers(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
                  const __grid_constant__ CUtensorMap tC, const __grid_constant__ CUtensorMap tAl,
                  const __grid_constant__ CUtensorMap tBl, PersArgs p) {
+  pdl_wait();
   using Cfg = PcCfg<BN, X3>;
   constexpr int S = Cfg::STAGES;
   constexpr int BK = 64;  // bf16 K elements per 128-byte row
@@ -600,6 +602,7 @@ __global__ void __launch_bounds__(256)
               const void* bias, int M, int N, int K, int64_t sAb, int64_t sAm, int64_t sAk,
               int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, int64_t sCb, float alpha,
               int epi, int splits, int kchunk, float* __restrict__ ws) {
+  pdl_wait();
   __shared__ float As[16][64 + 1];
   __shared__ float Bs[16][64 + 1];
   const int bz = blockIdx.z / splits, ks = blockIdx.z % splits;
@@ -660,6 +663,7 @@ __global__ void __launch_bounds__(128)
                 const void* bias, int M, int N, int K, int64_t sAb, int64_t sAm, int64_t sAk,
                 int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, int64_t sCb, float alpha,
                 int epi, int splits, int kchunk, float* __restrict__ ws) {
+  pdl_wait();
   __shared__ float Bs[64][NMAX];
   const int bz = blockIdx.z / splits, ks = blockIdx.z % splits;
   const int m = blockIdx.x * 128 + threadIdx.x;
@@ -787,6 +791,7 @@ struct Scratch {
 __global__ void __launch_bounds__(256)
     split_planes(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
                  __nv_bfloat16* __restrict__ lo, int64_t n) {
+  pdl_wait();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
   for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
     if (i + 4 <= n && ((reinterpret_cast<uintptr_t>(x + i) | reinterpret_cast<uintptr_t>(hi + i) |
@@ -822,6 +827,7 @@ template <typename TO>
 __global__ void __launch_bounds__(256)
     splitk_reduce(const float* __restrict__ ws, TO* __restrict__ C, const void* bias, int batch,
                   int M, int N, int splits, int64_t ldc, int64_t sCb, float alpha, int epi) {
+  pdl_wait();
   const int nq = N >> 2;
   const int64_t total = (int64_t)batch * M * nq;
   const int64_t mn_all = (int64_t)M * N;
@@ -853,6 +859,7 @@ template <typename TO>
 __global__ void __launch_bounds__(256)
     splitk_reduce1(const float* __restrict__ ws, TO* __restrict__ C, const void* bias, int batch,
                    int M, int N, int splits, int64_t ldc, int64_t sCb, float alpha, int epi) {
+  pdl_wait();
   const int64_t total = (int64_t)batch * M * N;
   const int64_t mn_all = (int64_t)M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -869,19 +876,20 @@ __global__ void __launch_bounds__(256)
   }
 }
 template <typename TO>
-void launch_splitk_reduce(const float* ws, TO* C, const void* bias, int64_t batch, int64_t M,
-                          int64_t N, int splits, int64_t ldc, float alpha, int epi, cudaStream_t st) {
+int launch_splitk_reduce(const float* ws, TO* C, const void* bias, int64_t batch, int64_t M,
+                         int64_t N, int splits, int64_t ldc, float alpha, int epi, cudaStream_t st) {
   if (N % 4 == 0) {
     const int64_t total = batch * M * (N / 4);
     const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-    splitk_reduce<TO><<<blocks, 256, 0, st>>>(ws, C, bias, (int)batch, (int)M, (int)N, splits, ldc,
-                                              M * ldc, alpha, epi);
+    B200_LAUNCH(splitk_reduce<TO>, dim3(blocks), dim3(256), 0, st, ws, C, bias, (int)batch, (int)M,
+                (int)N, splits, ldc, M * ldc, alpha, epi);
   } else {
     const int64_t total = batch * M * N;
     const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-    splitk_reduce1<TO><<<blocks, 256, 0, st>>>(ws, C, bias, (int)batch, (int)M, (int)N, splits, ldc,
-                                               M * ldc, alpha, epi);
+    B200_LAUNCH(splitk_reduce1<TO>, dim3(blocks), dim3(256), 0, st, ws, C, bias, (int)batch,
+                (int)M, (int)N, splits, ldc, M * ldc, alpha, epi);
   }
+  return B200_OK;
 }
 
 template <int BN, int ES, typename TO, bool SPLIT>
@@ -950,12 +958,9 @@ int launch_tc(const void* a, const void* b, void* c, const void* bias, int64_t b
   }
   if (scratch.query) return kWorkspaceQueried;
   dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(batch * sp.splits));
-  gemm_tc<BN, ES, TO, SPLIT><<<grid, 192, smem, st>>>(ta, tb, p);
-  B200_LAUNCH_CHECK();
-  if (sp.splits > 1) {
-    launch_splitk_reduce<TO>(p.ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
-    B200_LAUNCH_CHECK();
-  }
+  B200_LAUNCH(gemm_tc<BN, ES, TO, SPLIT>, grid, dim3(192), smem, st, ta, tb, p);
+  if (sp.splits > 1)
+    return launch_splitk_reduce<TO>(p.ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
   return B200_OK;
 }
 
@@ -1015,10 +1020,10 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   if (X3) {
     const unsigned ga = (unsigned)std::min<int64_t>((na + 1023) / 1024, 148 * 8);
     const unsigned gb = (unsigned)std::min<int64_t>((nb + 1023) / 1024, 148 * 8);
-    split_planes<<<ga, 256, 0, st>>>((const float*)a, (__nv_bfloat16*)ah, (__nv_bfloat16*)al, na);
-    B200_LAUNCH_CHECK();
-    split_planes<<<gb, 256, 0, st>>>((const float*)b, (__nv_bfloat16*)bh, (__nv_bfloat16*)bl, nb);
-    B200_LAUNCH_CHECK();
+    B200_LAUNCH(split_planes, dim3(ga), dim3(256), 0, st, (const float*)a, (__nv_bfloat16*)ah,
+                (__nv_bfloat16*)al, na);
+    B200_LAUNCH(split_planes, dim3(gb), dim3(256), 0, st, (const float*)b, (__nv_bfloat16*)bh,
+                (__nv_bfloat16*)bl, nb);
     a = ah;
     b = bh;
     a_lo = al;
@@ -1117,12 +1122,9 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pers<BN, TO, X3>, smem, "gemm_tc_pers")) return rc2;
   const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch * sp.splits;
   const unsigned grid = (unsigned)std::min<int64_t>(num_tiles, num_sms());
-  gemm_tc_pers<BN, TO, X3><<<grid, 192, smem, st>>>(ta, tb, tc, tal, tbl, p);
-  B200_LAUNCH_CHECK();
-  if (ws) {
-    launch_splitk_reduce<TO>(wsp, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
-    B200_LAUNCH_CHECK();
-  }
+  B200_LAUNCH(gemm_tc_pers<BN, TO, X3>, dim3(grid), dim3(192), smem, st, ta, tb, tc, tal, tbl, p);
+  if (ws)
+    return launch_splitk_reduce<TO>(wsp, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
   return B200_OK;
 }
 
@@ -1148,14 +1150,11 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
     }
     if (scratch.query) return kWorkspaceQueried;
     dim3 grid((unsigned)gx, 1, (unsigned)(batch * sp.splits));
-    gemm_skinny<TI, TO, 16><<<grid, 128, 0, st>>>((const TI*)a, (const TI*)b, (TO*)c, bias, (int)M,
-                                                  (int)N, (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
-                                                  M * ldc, alpha, epi, sp.splits, sp.per_split * 64, ws);
-    B200_LAUNCH_CHECK();
-    if (sp.splits > 1) {
-      launch_splitk_reduce<TO>(ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
-      B200_LAUNCH_CHECK();
-    }
+    B200_LAUNCH(gemm_skinny<TI, TO, 16>, grid, dim3(128), 0, st, (const TI*)a, (const TI*)b, (TO*)c,
+                bias, (int)M, (int)N, (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, M * ldc, alpha, epi,
+                sp.splits, sp.per_split * 64, ws);
+    if (sp.splits > 1)
+      return launch_splitk_reduce<TO>(ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
     return B200_OK;
   }
   const int64_t gx = (N + 63) / 64, gy = (M + 63) / 64;
@@ -1166,14 +1165,11 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
   }
   if (scratch.query) return kWorkspaceQueried;
   dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)(batch * sp.splits));
-  gemm_simt<TI, TO><<<grid, 256, 0, st>>>((const TI*)a, (const TI*)b, (TO*)c, bias, (int)M, (int)N,
-                                          (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, M * ldc, alpha,
-                                          epi, sp.splits, sp.per_split * 16, ws);
-  B200_LAUNCH_CHECK();
-  if (sp.splits > 1) {
-    launch_splitk_reduce<TO>(ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
-    B200_LAUNCH_CHECK();
-  }
+  B200_LAUNCH(gemm_simt<TI, TO>, grid, dim3(256), 0, st, (const TI*)a, (const TI*)b, (TO*)c, bias,
+              (int)M, (int)N, (int)K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, M * ldc, alpha, epi,
+              sp.splits, sp.per_split * 16, ws);
+  if (sp.splits > 1)
+    return launch_splitk_reduce<TO>(ws, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
   return B200_OK;
 }
 

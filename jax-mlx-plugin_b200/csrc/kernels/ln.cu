@@ -74,6 +74,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, NV <= 8 ? 8 : 4)
                const T* __restrict__ beta, T* __restrict__ y, T* __restrict__ h,
                float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t rows,
                float eps, int kind) {
+  pdl_wait();
   constexpr int E = 16 / sizeof(T);
   constexpr int COLS = 32 * NV * E;
   const int lane = threadIdx.x & 31;
@@ -156,6 +157,7 @@ __global__ void __launch_bounds__(256)
                    const T* __restrict__ gamma, const T* __restrict__ beta, T* __restrict__ y,
                    T* __restrict__ h, float* __restrict__ mean_out, float* __restrict__ rstd_out,
                    int64_t cols, float eps, int kind) {
+  pdl_wait();
   __shared__ float red[32];
   __shared__ float stat;
   const int64_t row = blockIdx.x;
@@ -217,6 +219,7 @@ __global__ void __launch_bounds__(256)
                 const float* __restrict__ mean, const float* __restrict__ rstd,
                 const T* __restrict__ dy, T* __restrict__ dx, float* __restrict__ ws,
                 int64_t rows, int64_t cols) {
+  pdl_wait();
   __shared__ float red[2][32];
   __shared__ float stat[2];
   const int64_t r0 = (int64_t)blockIdx.x * kBwdRowsPerBlock;
@@ -260,6 +263,7 @@ __global__ void __launch_bounds__(256)
 
 __global__ void ln_bwd_colsum(const float* __restrict__ ws, float* __restrict__ dgamma,
                               float* __restrict__ dbeta, int64_t nblk, int64_t cols) {
+  pdl_wait();
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols) return;
   float g = 0.f, b = 0.f;
@@ -287,16 +291,15 @@ int launch_fwd(const void* x, const void* res, const void* gamma, const void* be
   if (aligned && cols == nv * 32 * E) {
     switch (nv) {
 #define B200_LN_CASE(n) \
-  case n: ln_fwd_reg<T, n><<<grid, block, 0, st>>>(X, R, G, B, Y, H, mean_out, rstd_out, rows, eps, kind); B200_LAUNCH_CHECK(); return B200_OK;
+  case n: B200_LAUNCH(ln_fwd_reg<T, n>, grid, block, 0, st, X, R, G, B, Y, H, mean_out, rstd_out, rows, eps, kind); return B200_OK;
       B200_LN_CASE(1) B200_LN_CASE(2) B200_LN_CASE(3) B200_LN_CASE(4) B200_LN_CASE(5)
       B200_LN_CASE(6) B200_LN_CASE(7) B200_LN_CASE(8) B200_LN_CASE(12) B200_LN_CASE(16)
 #undef B200_LN_CASE
       default: break;
     }
   }
-  ln_fwd_generic<T><<<(unsigned)rows, 256, 0, st>>>(X, R, G, B, Y, H, mean_out, rstd_out, cols,
-                                                    eps, kind);
-  B200_LAUNCH_CHECK();
+  B200_LAUNCH(ln_fwd_generic<T>, dim3((unsigned)rows), dim3(256), 0, st, X, R, G, B, Y, H,
+              mean_out, rstd_out, cols, eps, kind);
   return B200_OK;
 }
 
@@ -305,12 +308,10 @@ int launch_bwd(const void* x, const void* gamma, const float* mean, const float*
                const void* dy, void* dx, float* dgamma, float* dbeta, void* ws, int64_t rows,
                int64_t cols, cudaStream_t st) {
   const int64_t nblk = (rows + kBwdRowsPerBlock - 1) / kBwdRowsPerBlock;
-  ln_bwd_rows<T><<<(unsigned)nblk, 256, 0, st>>>((const T*)x, (const T*)gamma, mean, rstd,
-                                                 (const T*)dy, (T*)dx, (float*)ws, rows, cols);
-  B200_LAUNCH_CHECK();
-  ln_bwd_colsum<<<(unsigned)((cols + 255) / 256), 256, 0, st>>>((const float*)ws, dgamma, dbeta,
-                                                                nblk, cols);
-  B200_LAUNCH_CHECK();
+  B200_LAUNCH(ln_bwd_rows<T>, dim3((unsigned)nblk), dim3(256), 0, st, (const T*)x,
+              (const T*)gamma, mean, rstd, (const T*)dy, (T*)dx, (float*)ws, rows, cols);
+  B200_LAUNCH(ln_bwd_colsum, dim3((unsigned)((cols + 255) / 256)), dim3(256), 0, st,
+              (const float*)ws, dgamma, dbeta, nblk, cols);
   return B200_OK;
 }
 

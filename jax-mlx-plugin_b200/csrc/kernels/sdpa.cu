@@ -48,6 +48,7 @@ template <int ES>
 __global__ void __launch_bounds__(128, 1)
     sdpa_fwd_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                 const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
+  pdl_wait();
   using C = SdpaCfg<ES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -310,6 +311,7 @@ struct X3Cfg {
 __global__ void __launch_bounds__(128, 1)
     sdpa_fwd_tc_x3(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                    const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
+  pdl_wait();
   using C = X3Cfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -599,6 +601,7 @@ template <bool X3>
 __global__ void __launch_bounds__(kWsThreads, 1)
     sdpa_fwd_ws(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                 const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
+  pdl_wait();
   using C = WsCfg<X3>;
   constexpr int NS = C::SLOTS;
   extern __shared__ uint8_t smem_raw[];
@@ -962,8 +965,7 @@ int launch_ws(const void* q, const void* k, const void* v, void* o, int64_t B, i
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_ws<X3>, C::SMEM, "sdpa_fwd_ws")) return rc;
   dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
-  sdpa_fwd_ws<X3><<<grid, kWsThreads, C::SMEM, s>>>(tq, tk, tv, a);
-  B200_LAUNCH_CHECK();
+  B200_LAUNCH(sdpa_fwd_ws<X3>, grid, dim3(kWsThreads), C::SMEM, s, tq, tk, tv, a);
   return B200_OK;
 }
 
@@ -975,6 +977,7 @@ __global__ void __launch_bounds__(128)
     sdpa_fwd_simt(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
                   T* __restrict__ o, int S, int D, const int64_t* __restrict__ st, float scale,
                   int causal) {
+  pdl_wait();
   extern __shared__ float sc[];  // S scores, then D query values
   float* qv = sc + S;
   const int t = blockIdx.x, n = blockIdx.y, b = blockIdx.z;
@@ -1051,8 +1054,7 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, int64_t B, i
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_tc<ES>, C::SMEM, "sdpa_fwd_tc")) return rc;
   dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
-  sdpa_fwd_tc<ES><<<grid, 128, C::SMEM, s>>>(tq, tk, tv, a);
-  B200_LAUNCH_CHECK();
+  B200_LAUNCH(sdpa_fwd_tc<ES>, grid, dim3(128), C::SMEM, s, tq, tk, tv, a);
   return B200_OK;
 }
 
@@ -1088,8 +1090,7 @@ int launch_x3(const void* q, const void* k, const void* v, void* o, int64_t B, i
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_tc_x3, X3Cfg::SMEM, "sdpa_fwd_tc_x3")) return rc;
   dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
-  sdpa_fwd_tc_x3<<<grid, 128, X3Cfg::SMEM, s>>>(tq, tk, tv, a);
-  B200_LAUNCH_CHECK();
+  B200_LAUNCH(sdpa_fwd_tc_x3, grid, dim3(128), X3Cfg::SMEM, s, tq, tk, tv, a);
   return B200_OK;
 }
 
@@ -1138,13 +1139,12 @@ extern "C" int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v
   const size_t smem = (size_t)(S + D) * sizeof(float);
   dim3 grid((unsigned)T, (unsigned)N, (unsigned)B);
   if (es == 4)
-    sdpa_fwd_simt<float><<<grid, 128, smem, s>>>((const float*)q, (const float*)k, (const float*)v,
-                                                 (float*)o, (int)S, (int)D, dst, scale, causal);
+    B200_LAUNCH(sdpa_fwd_simt<float>, grid, dim3(128), smem, s, (const float*)q, (const float*)k,
+                (const float*)v, (float*)o, (int)S, (int)D, (const int64_t*)dst, scale, causal);
   else
-    sdpa_fwd_simt<__nv_bfloat16><<<grid, 128, smem, s>>>(
-        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
-        (__nv_bfloat16*)o, (int)S, (int)D, dst, scale, causal);
-  B200_LAUNCH_CHECK();
+    B200_LAUNCH(sdpa_fwd_simt<__nv_bfloat16>, grid, dim3(128), smem, s, (const __nv_bfloat16*)q,
+                (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (__nv_bfloat16*)o, (int)S, (int)D,
+                (const int64_t*)dst, scale, causal);
   B200_CUDA_TRY(cudaFreeAsync(dst, s));
   return B200_OK;
 }
