@@ -3,6 +3,7 @@
 #pragma once
 #include <functional>
 #include <map>
+#include <set>
 #include <sstream>
 #include <string>
 #include <vector>
@@ -15,6 +16,14 @@ namespace b200 {
 // Where the generated code reads a value from: a materialized slot, or (slot
 // < 0) recomputed inline from the value's defining node.
 using SlotOf = std::function<int(ValueRef)>;
+
+// One phase of a row group: a reduction of the last dimension, or a set of
+// values stored at every element of the rows.
+struct RowPhase {
+  int reduce = -1;               // Reduce node, or -1 for a loop phase
+  std::vector<ValueRef> roots;   // loop phase: the values stored
+  std::vector<int> out_slots;    // reduce results / loop outputs, in order
+};
 
 struct GenKernel {
   std::string name;
@@ -51,6 +60,13 @@ class CodeGen {
                    const std::vector<int64_t>& m_roles, int64_t M, int64_t K);
   // out[j] = src[permuted j]: out dims are src dims[perm[i]] (a transpose copy).
   GenKernel permute(int src_slot, const std::vector<int64_t>& perm, int out_slot);
+  // Several row-wise phases over the same OUT rows of RED elements in one
+  // kernel: one warp (RED <= 4096) or one block per row runs the phases in
+  // order, with a barrier between them, so that a phase reads what earlier
+  // phases wrote for its row (still in L1/L2) instead of a separate kernel
+  // reading it back from HBM.  Every read of a phase output by a later phase
+  // must be at the same row (the planner checks this).
+  GenKernel rowgroup(const std::vector<RowPhase>& phases, int64_t OUT, int64_t RED);
 
   static std::string prelude();
   int counter = 0;
@@ -79,6 +95,11 @@ class CodeGen {
   std::vector<int> ptrs_;
   std::vector<bool> written_;
   std::vector<std::map<std::string, std::string>> memo_;
+  // Values computed inline even though they have a slot (the roots a loop
+  // phase is storing), and slots written earlier in the same kernel (read
+  // through the coherent path, not the read-only cache).
+  std::set<ValueRef> hidden_;
+  std::set<int> coherent_;
   // Set while emitting a reduction's combiner: bf16 partial results stay in
   // f32 and are rounded once when stored (XLA accumulates bf16 reductions in
   // f32 rather than rounding after every add).

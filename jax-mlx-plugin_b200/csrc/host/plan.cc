@@ -11,6 +11,7 @@
 #include "plan.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <functional>
 #include <map>
@@ -145,17 +146,39 @@ struct Builder {
         return true;
       }
     if (u.count(n) <= 1) return false;
-    if (is_cheap(nd)) return false;
     // A value with a few consumers is recomputed inside each of them when its
     // fused expression is small: on HBM-bound kernels re-reading the inputs
     // (often narrower, e.g. bf16 logits) beats writing and re-reading an f32
     // intermediate.  Consumers that read each element several times (windows,
-    // im2col, gathers, broadcasts) keep it materialized.
-    if (u.count(n) <= 4 && !amplified(n)) {
+    // im2col, gathers, broadcasts) keep it materialized.  Layout ops and
+    // converts are free to recompute.  In both cases the expression's memory
+    // inputs, read once more by every extra consumer, must not cost more than
+    // writing the value once and reading it back in each consumer: a long
+    // residual chain (embedding + every block's output) is stored, not summed
+    // again from a dozen tensors in each of its readers.
+    if (!is_cheap(nd)) {
+      if (u.count(n) > 4 || amplified(n)) return true;
       std::set<int> seen;
-      if (expr_cost(n, seen) <= kRecomputeOps) return false;
+      if (expr_cost(n, seen) > kRecomputeOps) return true;
     }
-    return true;
+    std::set<int> seen;
+    const int64_t k = u.count(n), in_bytes = input_bytes(n, seen);
+    return (k - 1) * in_bytes > (k + 1) * nd.results[0].bytes();
+  }
+  // Bytes of the memory-resident values (materialized slots, parameters,
+  // results of non-fused ops) that n's fused expression reads, each once.
+  int64_t input_bytes(int n, std::set<int>& seen) {
+    if (seen.count(n)) return 0;
+    seen.insert(n);
+    const Node& nd = g.nodes[n];
+    if (slot.count(ValueRef{n, 0}) || !is_fusible(nd.op)) {
+      int64_t b = 0;
+      for (const auto& t : nd.results) b += t.bytes();
+      return b;
+    }
+    int64_t b = 0;
+    for (const auto& o : nd.operands) b += input_bytes(o.node, seen);
+    return b;
   }
   // Recompute budget in arithmetic ops (a transcendental counts 4): an HBM
   // byte costs far more than that many ops on this GPU.
@@ -569,6 +592,174 @@ struct Builder {
     p.steps.swap(merged);
   }
 
+  // ------------------------------------------------------------ row groups --
+  // Consecutive row-wise kernels over the same OUT rows of RED elements --
+  // reductions of the last dimension and loops whose last dimension is RED --
+  // are gathered into one row-group kernel (CodeGen::rowgroup) when every
+  // value a phase reads from an earlier phase is read at its own row.  A
+  // softmax (max, sum of exponentials, normalise), a cross-entropy (max, sum,
+  // target logit, gradient) or a layer norm (mean, variance, normalise) then
+  // reads each row from HBM once instead of once per kernel.
+  std::vector<RowPhase> rg;
+  int64_t rg_out = 0, rg_red = 0;
+  std::set<int> rg_nodes;  // nodes whose values the open group's phases write
+
+  static bool elementwise_op(Op op) { return op >= Op::Neg && op <= Op::Convert; }
+
+  // B200_ROW_GROUPS=0 emits every phase as a kernel of its own.
+  static bool row_groups_on() {
+    static const bool on = [] {
+      const char* e = getenv("B200_ROW_GROUPS");
+      return !(e && e[0] == '0');
+    }();
+    return on;
+  }
+  bool reduce_rows(int n, int64_t* out, int64_t* red) {
+    if (!row_groups_on()) return false;
+    const Node& nd = g.nodes[n];
+    if (nd.op != Op::Reduce || nd.dims.size() != 1) return false;
+    const TensorType& it = g.type(nd.operands[0]);
+    if (it.rank() < 2 || nd.dims[0] != it.rank() - 1 || it.dims.back() < 2) return false;
+    *red = it.dims.back();
+    *out = it.numel() / *red;
+    return *out > 0;
+  }
+  bool loop_rows(const std::vector<int>& nodes, int64_t* out, int64_t* red) {
+    if (!row_groups_on()) return false;
+    const TensorType& t = g.nodes[nodes[0]].results[0];
+    if (t.rank() < 2 || t.dims.back() < 2) return false;
+    for (int n : nodes)
+      if (g.nodes[n].results[0].dims != t.dims) return false;
+    *red = t.dims.back();
+    *out = t.numel() / *red;
+    return *out > 0;
+  }
+  // Does v's fused expression read a value the open group writes?
+  bool reads_group(ValueRef v, std::set<int>& seen) {
+    if (rg_nodes.count(v.node)) return true;
+    if (slot.count(v) || !seen.insert(v.node).second) return false;
+    const Node& nd = g.nodes[v.node];
+    if (!is_fusible(nd.op)) return false;
+    for (const auto& o : nd.operands)
+      if (reads_group(o, seen)) return true;
+    return false;
+  }
+  // True when every group value v's expression reads is read at the row of
+  // the element being computed.  The row of an element of a value with
+  // OUT*RED elements is its linear index / RED; of a value with OUT elements,
+  // its linear index.  Elementwise ops and reshapes keep linear indices; a
+  // broadcast of a per-row value along the last dimension keeps the row.
+  bool row_aligned_node(int n) {
+    const Node& nd = g.nodes[n];
+    const TensorType& t = nd.results[0];
+    auto sub = [&](ValueRef o) {
+      std::set<int> seen;
+      if (!reads_group(o, seen)) return true;
+      if (rg_nodes.count(o.node)) return true;
+      return row_aligned_node(o.node);
+    };
+    if (nd.op == Op::Constant || nd.op == Op::Iota) return true;
+    if (elementwise_op(nd.op)) {
+      for (const auto& o : nd.operands)
+        if (g.type(o).numel() != t.numel() && g.type(o).numel() != 1) return false;
+      for (const auto& o : nd.operands)
+        if (!sub(o)) return false;
+      return true;
+    }
+    if (nd.op == Op::Reshape) return g.type(nd.operands[0]).numel() == t.numel() && sub(nd.operands[0]);
+    if (nd.op == Op::BroadcastInDim) {
+      const TensorType& it = g.type(nd.operands[0]);
+      {
+        std::set<int> seen;
+        if (!reads_group(nd.operands[0], seen)) return true;
+      }
+      if (it.numel() == t.numel()) {  // only size-1 dimensions added
+        int last = -1;
+        for (size_t i = 0; i < nd.dims.size(); ++i) {
+          if (it.dims[i] == 1) continue;
+          if (nd.dims[i] <= last) return false;
+          last = (int)nd.dims[i];
+        }
+        return sub(nd.operands[0]);
+      }
+      // per-row value along the rows: input dims of size > 1 map, in order,
+      // onto every leading output dimension of size > 1
+      if (t.numel() != rg_out * rg_red || t.dims.back() != rg_red || it.numel() != rg_out) return false;
+      int last = -1;
+      int64_t covered = 1;
+      for (size_t i = 0; i < nd.dims.size(); ++i) {
+        if (it.dims[i] == 1) continue;
+        const int64_t d = nd.dims[i];
+        if (d <= last || d >= t.rank() - 1 || t.dims[d] != it.dims[i]) return false;
+        last = (int)d;
+        covered *= it.dims[i];
+      }
+      return covered == rg_out && sub(nd.operands[0]);
+    }
+    return false;
+  }
+  // `reads`: values the phase reads at the element it computes (a reduction's
+  // operands); `roots`: nodes a loop phase computes there.
+  bool phase_fits(int64_t out, int64_t red, const std::vector<ValueRef>& reads,
+                  const std::vector<int>& roots) {
+    if (rg.empty()) return true;
+    if (out != rg_out || red != rg_red) return false;
+    for (const auto& v : reads) {
+      if (rg_nodes.count(v.node)) continue;
+      std::set<int> seen;
+      if (!reads_group(v, seen)) continue;
+      if (!row_aligned_node(v.node)) return false;
+    }
+    for (int n : roots) {
+      bool reads_any = false;
+      for (const auto& o : g.nodes[n].operands) {
+        std::set<int> seen;
+        if (rg_nodes.count(o.node) || reads_group(o, seen)) reads_any = true;
+      }
+      if (reads_any && !row_aligned_node(n)) return false;
+    }
+    return true;
+  }
+  void open_phase(int64_t out, int64_t red) {
+    if (rg.empty()) {
+      rg_out = out;
+      rg_red = red;
+    }
+  }
+  void flush_rg() {
+    if (rg.empty()) return;
+    if (rg.size() == 1) {
+      const RowPhase ph = rg[0];
+      rg.clear();
+      rg_nodes.clear();
+      if (ph.reduce >= 0) {
+        add_kernel(cg.reduce(ph.reduce, ph.out_slots));
+      } else {
+        for (auto& r : ph.roots) slot.erase(r);
+        GenKernel k = cg.loop(ph.roots, ph.out_slots);
+        for (size_t i = 0; i < ph.roots.size(); ++i) slot[ph.roots[i]] = ph.out_slots[i];
+        add_kernel(std::move(k));
+      }
+      return;
+    }
+    GenKernel k = cg.rowgroup(rg, rg_out, rg_red);
+    rg.clear();
+    rg_nodes.clear();
+    add_kernel(std::move(k));
+  }
+  // A row-wise reduction (split == 1): joins or opens the row group.
+  void add_reduce_phase(int n, const std::vector<int>& outs, int64_t out, int64_t red) {
+    const Node& nd = g.nodes[n];
+    std::vector<ValueRef> reads(nd.operands.begin(), nd.operands.end());
+    if (!phase_fits(out, red, reads, {})) flush_rg();
+    open_phase(out, red);
+    RowPhase ph;
+    ph.reduce = n;
+    ph.out_slots = outs;
+    rg.push_back(ph);
+    rg_nodes.insert(n);
+  }
+
   std::vector<int> pending;  // materialized loop values not yet emitted
   void flush_loops() {
     if (pending.empty()) return;
@@ -578,6 +769,19 @@ struct Builder {
       roots.push_back(ValueRef{n, 0});
       outs.push_back(slot.at(ValueRef{n, 0}));
     }
+    int64_t out = 0, red = 0;
+    if (loop_rows(pending, &out, &red)) {
+      if (!phase_fits(out, red, {}, pending)) flush_rg();
+      open_phase(out, red);
+      RowPhase ph;
+      ph.roots = roots;
+      ph.out_slots = outs;
+      rg.push_back(ph);
+      for (int n : pending) rg_nodes.insert(n);
+      pending.clear();
+      return;
+    }
+    flush_rg();
     // hide the slots so the kernel computes the values instead of loading them
     for (auto& r : roots) slot.erase(r);
     GenKernel k = cg.loop(roots, outs);
@@ -658,11 +862,18 @@ struct Builder {
         continue;
       }
       flush_loops();
+      if (nd.op != Op::Reduce) flush_rg();
       switch (nd.op) {
         case Op::Reduce: {
           std::vector<int> outs;
           for (size_t k = 0; k < nd.results.size(); ++k) outs.push_back(temp_for(ValueRef{n, (int)k}));
           const int split = reduce_split(nd);
+          int64_t rows = 0, red = 0;
+          if (split == 1 && reduce_rows(n, &rows, &red)) {
+            add_reduce_phase(n, outs, rows, red);
+            break;
+          }
+          flush_rg();
           if (split > 1) {
             std::vector<int> parts;
             for (size_t k = 0; k < nd.results.size(); ++k) {
@@ -720,6 +931,7 @@ struct Builder {
       }
     }
     flush_loops();
+    flush_rg();
     bucket_all_reduces();
     // outputs
     std::set<int> used;

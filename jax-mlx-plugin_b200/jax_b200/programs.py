@@ -50,6 +50,33 @@ def cross_entropy(b: Builder, logits: V, labels: V) -> V:
     return b.sum(per, [0]) / float(n)
 
 
+def logits_cross_entropy(rows=64, cols=5000, dt="f32") -> str:
+    """value_and_grad of the mean softmax cross-entropy of logits + bias (the
+    language-model head's loss) with respect to both.  Inputs: logits
+    [rows, cols], bias [cols] (both `dt`), labels [rows] i32.  Outputs: loss
+    (f32), d logits, d bias.  Exercises row-wise reductions and loops over long
+    rows."""
+    b = Builder("jit_logits_cross_entropy")
+    logits, bias = b.param((rows, cols), dt), b.param((cols,), dt)
+    labels = b.param((rows,), "i32")
+    z = logits + bias
+    if dt != "f32":
+        z = b.convert(z, "f32")
+    loss = cross_entropy(b, z, labels)
+    grads = b.grad(loss, [logits, bias])
+    return b.module([loss] + grads)
+
+
+def softmax_then_transposed_sum(n=96) -> str:
+    """p = softmax(x) over rows; out = sum over the last axis of p^T * x.  The
+    second reduction reads p at transposed positions, so it cannot run in the
+    same row pass as the softmax."""
+    b = Builder("jit_softmax_transposed")
+    x = b.param((n, n))
+    p = softmax(b, x)
+    return b.module([p, b.sum(b.transpose(p, [1, 0]) * x, [1])])
+
+
 def sdpa(B=8, T=512, N=8, H=64, causal=True, dt="f32") -> str:
     b = Builder("jit_dot_product_attention")
     q, k, v = b.param((B, T, N, H), dt), b.param((B, T, N, H), dt), b.param((B, T, N, H), dt)

@@ -33,9 +33,11 @@ def no_device_error():
 
 def run(client, text, inputs, bf16_args=()):
     exe = client.compile(text)
-    bufs = [client.buffer_from_numpy(a, bf16=i in bf16_args) for i, a in enumerate(inputs)]
+    bufs = [client.buffer_from_numpy(pjrt.to_bf16_bits(a), bf16=True) if i in bf16_args
+            else client.buffer_from_numpy(a) for i, a in enumerate(inputs)]
     outs = exe.execute([bufs])[0]
-    return [o.to_numpy() for o in outs]
+    return [pjrt.from_bf16_bits(o.to_numpy()) if o.dtype == pjrt.BF16 else o.to_numpy()
+            for o in outs]
 
 
 def test_client_surface(client):
@@ -341,6 +343,37 @@ def test_transformer_step_full_config_runs(client):
     outs = _tr_run(client, programs.transformer_step(**cfg), params, ms, vs, count, tok, tgt)
     assert abs(float(outs[0]) - np.log(32000)) < 0.5
     assert all(np.isfinite(o).all() for o in outs)
+
+
+# --------------------------------------------------------- row-group kernels
+@pytest.mark.parametrize("rows,cols,dt", [(2400, 5000, "f32"), (2400, 1000, "f32"),
+                                          (2400, 6000, "bf16"), (3000, 10, "f32")])
+def test_logits_cross_entropy_row_groups(client, rows, cols, dt):
+    """Loss, d logits and d bias of softmax cross-entropy over long rows (a block
+    per row above 4096 columns, a warp per row below) vs the interpreter.  f32:
+    1e-5 relative (no contraction); bf16 inputs and gradients: 1e-2 (one bf16
+    ulp of the rounded outputs)."""
+    rng = np.random.default_rng(rows + cols)
+    logits = _as_dt((rng.standard_normal((rows, cols)) * 3).astype(np.float32), dt)
+    bias = _as_dt(rng.standard_normal(cols).astype(np.float32), dt)
+    labels = rng.integers(0, cols, rows).astype(np.int32)
+    text = programs.logits_cross_entropy(rows, cols, dt)
+    bf = dt == "bf16"
+    got = run(client, text, [logits, bias, labels], bf16_args=(0, 1) if bf else ())
+    ref = hlo_interp.run(text, [[logits, bias, labels]])[0]
+    tol = 1e-2 if bf else 1e-5
+    for name, g, r in zip(("loss", "dlogits", "dbias"), got, ref):
+        assert_close(np.asarray(g, np.float32), np.asarray(r, np.float32), tol, f"{name} {rows}x{cols} {dt}")
+
+
+def test_softmax_with_transposed_reader(client):
+    rng = np.random.default_rng(97)
+    x = rng.standard_normal((96, 96)).astype(np.float32)
+    text = programs.softmax_then_transposed_sum(96)
+    got = run(client, text, [x])
+    ref = hlo_interp.run(text, [[x]])[0]
+    for g, r in zip(got, ref):
+        assert_close(g, r, 1e-5, "softmax + transposed reader")
 
 
 # ------------------------------------------- reference custom calls (A5/A6/A12)

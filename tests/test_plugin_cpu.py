@@ -92,6 +92,24 @@ def test_config_programs_fuse_and_compile():
     assert bucket.split(" out=")[0].count(",") == 9  # 9 inputs, comma-terminated
 
 
+def test_row_wise_kernels_share_one_pass():
+    """Row reductions and loops over the same rows run as one row-group kernel
+    (one HBM pass per row); a reduction reading an earlier phase's output at
+    transposed positions starts a kernel of its own."""
+    steps = pjrt.inspect(programs.logits_cross_entropy(2400, 5000), 1).split("steps:")[1]
+    names = [l.split()[0] for l in steps.strip().splitlines()]
+    # forward statistics (max, sum of exponentials, target logit) in one kernel,
+    # the logits gradient (with its row sums) in another, then the bias column sum
+    assert names[0].endswith("_rows") and sum(n.endswith("_rows") for n in names) == 2
+    assert not any(n.endswith("_loop") and "in=s0," in n for n in names)
+    steps = pjrt.inspect(programs.softmax_then_transposed_sum(), 1).split("steps:")[1]
+    names = [l.split()[0] for l in steps.strip().splitlines()]
+    assert names == ["k0_rows", "k1_reduce"]
+    # transformer step: every layer norm, attention softmax and the loss
+    steps = pjrt.inspect(programs.transformer_step(), 1).split("steps:")[1]
+    assert steps.count("_rows in=") >= 6 * 4 + 2
+
+
 def test_non_causal_and_bnth_attention_also_match():
     g = pjrt.inspect(programs.sdpa(2, 256, 4, 64, causal=False), 0)
     assert "fused_sdpa" in g and "causal=0" in g
