@@ -21,6 +21,10 @@ using SlotOf = std::function<int(ValueRef)>;
 // values stored at every element of the rows.
 struct RowPhase {
   int reduce = -1;               // Reduce node, or -1 for a loop phase
+  // With reduce a row max M of X: a second reduce node summing exp(X - M),
+  // computed in the same pass with a running maximum (out_slots: M, then the
+  // sum).
+  int sum_reduce = -1;
   std::vector<ValueRef> roots;   // loop phase: the values stored
   std::vector<int> out_slots;    // reduce results / loop outputs, in order
 };
@@ -67,6 +71,13 @@ class CodeGen {
   // reading it back from HBM.  Every read of a phase output by a later phase
   // must be at the same row (the planner checks this).
   GenKernel rowgroup(const std::vector<RowPhase>& phases, int64_t OUT, int64_t RED);
+  // A sum over the last dimension of one_hot * Y -- one_hot being
+  // convert(compare(EQ, iota along that dimension, a value constant along it)),
+  // reached through negations and float converts -- has one nonzero term per
+  // row: the one at the compared value.  Returns that value (any position of
+  // the row gives it), or node -1.  rowgroup evaluates such a reduction at that
+  // one position instead of over the whole row.
+  ValueRef onehot_pick(int reduce_node) const;
 
   static std::string prelude();
   int counter = 0;

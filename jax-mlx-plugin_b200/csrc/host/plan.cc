@@ -728,7 +728,8 @@ struct Builder {
   }
   void flush_rg() {
     if (rg.empty()) return;
-    if (rg.size() == 1) {
+    if (rg.size() == 1 && rg[0].sum_reduce < 0 &&
+        !(rg[0].reduce >= 0 && cg.onehot_pick(rg[0].reduce).node >= 0)) {
       const RowPhase ph = rg[0];
       rg.clear();
       rg_nodes.clear();
@@ -747,10 +748,48 @@ struct Builder {
     rg_nodes.clear();
     add_kernel(std::move(k));
   }
+  // Reduce whose body is a single `op` and whose init is the constant `init`.
+  bool simple_reduce(const Node& nd, Op op, double init) {
+    if (nd.op != Op::Reduce || nd.operands.size() != 2) return false;
+    const Graph& r = *nd.regions.at(0);
+    if (r.outputs.size() != 1 || r.nodes.at(r.outputs[0].node).op != op) return false;
+    auto hv = host_eval(g, nd.operands[1]);
+    return hv && hv->v.size() == 1 && hv->v[0] == init;
+  }
+  // s sums exp(X - M) over the rows, where m (M) is the row max of the same
+  // f32 X: the pair is computed in one pass (RowPhase::sum_reduce).
+  bool softmax_sum_of(int s, int m) {
+    const Node& sn = g.nodes[s];
+    const Node& mn = g.nodes[m];
+    if (!simple_reduce(mn, Op::Max, -INFINITY) || !simple_reduce(sn, Op::Add, 0.0)) return false;
+    if (mn.results[0].dtype != DType::F32 || sn.results[0].dtype != DType::F32) return false;
+    const ValueRef x = mn.operands[0];
+    const ValueRef ev = sn.operands[0];
+    if (slot.count(ev)) return false;
+    const Node& e = g.nodes[ev.node];
+    if (e.op != Op::Exp || e.results[0].dtype != DType::F32 || slot.count(e.operands[0])) return false;
+    const Node& d = g.nodes[e.operands[0].node];
+    if (d.op != Op::Sub || !(d.operands[0] == x)) return false;
+    ValueRef b = d.operands[1];  // M broadcast along the row (alignment: phase_fits)
+    while (!(b.node == m && b.idx == 0)) {
+      const Node& bn = g.nodes[b.node];
+      if (slot.count(b) || (bn.op != Op::BroadcastInDim && bn.op != Op::Reshape)) return false;
+      b = bn.operands[0];
+    }
+    return true;
+  }
   // A row-wise reduction (split == 1): joins or opens the row group.
   void add_reduce_phase(int n, const std::vector<int>& outs, int64_t out, int64_t red) {
     const Node& nd = g.nodes[n];
     std::vector<ValueRef> reads(nd.operands.begin(), nd.operands.end());
+    if (!rg.empty() && rg.back().reduce >= 0 && rg.back().sum_reduce < 0 &&
+        rg.back().out_slots.size() == 1 && phase_fits(out, red, reads, {}) &&
+        softmax_sum_of(n, rg.back().reduce)) {
+      rg.back().sum_reduce = n;
+      rg.back().out_slots.push_back(outs[0]);
+      rg_nodes.insert(n);
+      return;
+    }
     if (!phase_fits(out, red, reads, {})) flush_rg();
     open_phase(out, red);
     RowPhase ph;

@@ -37,10 +37,11 @@ def _fmt_float(v: float, dt: str) -> str:
 
 
 class V:
-    __slots__ = ("b", "name", "shape", "dtype")
+    __slots__ = ("b", "name", "shape", "dtype", "stopped")
 
-    def __init__(self, b, name, shape, dtype):
+    def __init__(self, b, name, shape, dtype, stopped=False):
         self.b, self.name, self.shape, self.dtype = b, name, tuple(shape), dtype
+        self.stopped = stopped  # lax.stop_gradient: same SSA value, no gradient through it
 
     @property
     def ty(self):
@@ -181,7 +182,9 @@ class Builder:
         return self._emit(f"stablehlo.iota dim = {dim} : {ttype(shape, dt)}", shape, dt)
 
     def stop_gradient(self, x: V) -> V:
-        return self._rec("stop", x, [])
+        """lax.stop_gradient: emits nothing (as jax.jit does); the returned handle
+        names the same value but gradients reaching it are dropped."""
+        return V(self, x.name, x.shape, x.dtype, stopped=True)
 
     # ------------------------------------------------------------ layout --
     def broadcast_in_dim(self, x: V, shape, dims) -> V:
@@ -369,7 +372,7 @@ class Builder:
         ct: Dict[str, V] = {loss.name: self.constant(1.0, loss.dtype)}
 
         def acc(v: V, g: V):
-            if g is None:
+            if g is None or v.stopped:
                 return
             if g.shape != v.shape:
                 g = self.reshape(g, v.shape)
@@ -377,7 +380,7 @@ class Builder:
 
         for kind, out, ins, kw in reversed(self.tape):
             g = ct.get(out.name)
-            if g is None or kind == "stop":
+            if g is None:
                 continue
             if kind == "add":
                 acc(ins[0], g); acc(ins[1], g)

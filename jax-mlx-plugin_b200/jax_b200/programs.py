@@ -67,6 +67,17 @@ def logits_cross_entropy(rows=64, cols=5000, dt="f32") -> str:
     return b.module([loss] + grads)
 
 
+def row_softmax(rows=2400, cols=300) -> str:
+    """jax.nn.softmax over the last axis of f32 x [rows, cols] and the row
+    log-sum-exp (max + log of the shifted sum)."""
+    b = Builder("jit_row_softmax")
+    x = b.param((rows, cols))
+    m = b.stop_gradient(b.max(x, [1], keepdims=True))
+    e = b.exp(x - m)
+    s = b.sum(e, [1], keepdims=True)
+    return b.module([e / s, b.reshape(m + b.log(s), (rows,))])
+
+
 def softmax_then_transposed_sum(n=96) -> str:
     """p = softmax(x) over rows; out = sum over the last axis of p^T * x.  The
     second reduction reads p at transposed positions, so it cannot run in the

@@ -366,6 +366,32 @@ def test_logits_cross_entropy_row_groups(client, rows, cols, dt):
         assert_close(np.asarray(g, np.float32), np.asarray(r, np.float32), tol, f"{name} {rows}x{cols} {dt}")
 
 
+@pytest.mark.parametrize("cols", [300, 5000])
+def test_row_softmax_statistics_edge_values(client, cols):
+    """One-pass row max + sum of exponentials (warp and block per row) vs the
+    interpreter's two passes: rows with -inf entries (masked positions), a row
+    of -inf only (NaN, as exp(-inf - -inf) gives), a row holding +inf (NaN)
+    and a row of huge finite values.  1e-5 relative on finite outputs; NaN at
+    the same places."""
+    rows = 2400
+    rng = np.random.default_rng(cols)
+    x = (rng.standard_normal((rows, cols)) * 4).astype(np.float32)
+    x[rng.random((rows, cols)) < 0.3] = -np.inf
+    x[5, :] = -np.inf
+    x[7, cols // 2] = np.inf
+    x[9, :] = np.float32(3e38)
+    text = programs.row_softmax(rows, cols)
+    got = run(client, text, [x])
+    with np.errstate(invalid="ignore", over="ignore"):
+        ref = hlo_interp.run(text, [[x]])[0]
+    for name, g, r in zip(("softmax", "logsumexp"), got, ref):
+        g, r = np.asarray(g, np.float64), np.asarray(r, np.float64)
+        assert (np.isnan(g) == np.isnan(r)).all(), f"{name}: NaN positions differ"
+        assert (np.isinf(g) == np.isinf(r)).all() and (g[np.isinf(g)] == r[np.isinf(r)]).all()
+        fin = np.isfinite(r)
+        assert_close(g[fin], r[fin], 1e-5, f"{name} {rows}x{cols}")
+
+
 def test_softmax_with_transposed_reader(client):
     rng = np.random.default_rng(97)
     x = rng.standard_normal((96, 96)).astype(np.float32)
