@@ -656,7 +656,9 @@ __global__ void __launch_bounds__(256)
 
 // Narrow outputs (N <= 16, e.g. the 10-class logits and their gradients): one
 // thread per output row keeps all N accumulators; each block stages a 64-deep
-// slab of B in shared memory (read by every thread, broadcast).
+// slab of A (read along its contiguous dimension, so both A and A^T load
+// coalesced) and of B in shared memory.  K is split over blocks until the grid
+// covers the GPU (partials summed in split order by splitk_reduce1).
 template <typename TI, typename TO, int NMAX>
 __global__ void __launch_bounds__(128)
     gemm_skinny(const TI* __restrict__ A, const TI* __restrict__ B, TO* __restrict__ C,
@@ -664,9 +666,11 @@ __global__ void __launch_bounds__(128)
                 int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, int64_t sCb, float alpha,
                 int epi, int splits, int kchunk, float* __restrict__ ws) {
   pdl_wait();
+  __shared__ float As[64][129];  // [k][m]: conflict-free column reads and either-major fills
   __shared__ float Bs[64][NMAX];
   const int bz = blockIdx.z / splits, ks = blockIdx.z % splits;
-  const int m = blockIdx.x * 128 + threadIdx.x;
+  const int m0 = blockIdx.x * 128;
+  const int m = m0 + threadIdx.x;
   A += (int64_t)bz * sAb;
   B += (int64_t)bz * sBb;
   const int kbeg = ks * kchunk, kend = min(K, kbeg + kchunk);
@@ -674,35 +678,47 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
   for (int n = 0; n < NMAX; ++n) acc[n] = 0.f;
   for (int k0 = kbeg; k0 < kend; k0 += 64) {
+    // A tile (64 k x 128 m), read along whichever of k / m is contiguous
+    if (sAk == 1) {
+      for (int i = threadIdx.x; i < 64 * 128; i += 128) {
+        const int mm = i >> 6, kk = i & 63, gm = m0 + mm, gk = k0 + kk;
+        As[kk][mm] = (gm < M && gk < kend) ? Io<TI>::to_f(A[(int64_t)gm * sAm + gk]) : 0.f;
+      }
+    } else {
+      for (int i = threadIdx.x; i < 64 * 128; i += 128) {
+        const int kk = i >> 7, mm = i & 127, gm = m0 + mm, gk = k0 + kk;
+        As[kk][mm] =
+            (gm < M && gk < kend) ? Io<TI>::to_f(A[(int64_t)gm * sAm + (int64_t)gk * sAk]) : 0.f;
+      }
+    }
     for (int i = threadIdx.x; i < 64 * NMAX; i += 128) {
       const int kk = i / NMAX, n = i % NMAX, gk = k0 + kk;
       Bs[kk][n] = (gk < kend && n < N) ? Io<TI>::to_f(B[(int64_t)gk * sBk + (int64_t)n * sBn]) : 0.f;
     }
     __syncthreads();
     const int kn = min(64, kend - k0);
-    if (m < M) {
-      const TI* ar = A + (int64_t)m * sAm + (int64_t)k0 * sAk;
-      for (int kk = 0; kk < kn; ++kk) {
-        const float a = Io<TI>::to_f(ar[(int64_t)kk * sAk]);
+    for (int kk = 0; kk < kn; ++kk) {
+      const float a = As[kk][threadIdx.x];
 #pragma unroll
-        for (int n = 0; n < NMAX; ++n) acc[n] = fmaf(a, Bs[kk][n], acc[n]);
-      }
+      for (int n = 0; n < NMAX; ++n) acc[n] = fmaf(a, Bs[kk][n], acc[n]);
     }
     __syncthreads();
   }
-  if (m >= M) return;
-#pragma unroll
-  for (int n = 0; n < NMAX; ++n) {
-    if (n >= N) break;
-    if (splits > 1) {
-      ws[((int64_t)blockIdx.z * M + m) * N + n] = acc[n];
-      continue;
+  auto finish = [&](float* v) {
+    for (int n = 0; n < N && n < NMAX; ++n) {
+      float x = v[n] * alpha;
+      if (epi == 1 || epi == 2) x += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n]);
+      if (epi >= 2) x = fmaxf(x, 0.f);
+      store_out<TO>(C + (int64_t)bz * sCb + (int64_t)m * ldc + n, x);
     }
-    float x = acc[n] * alpha;
-    if (epi == 1 || epi == 2) x += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n]);
-    if (epi >= 2) x = fmaxf(x, 0.f);
-    store_out<TO>(C + (int64_t)bz * sCb + (int64_t)m * ldc + n, x);
+  };
+  if (m >= M) return;
+  if (splits == 1) {
+    finish(acc);
+    return;
   }
+  // split-K partials, summed in split order by splitk_reduce1
+  for (int n = 0; n < N && n < NMAX; ++n) ws[((int64_t)blockIdx.z * M + m) * N + n] = acc[n];
 }
 
 // Split-K plan: when the output tiles alone cannot fill the GPU, the K loop is
@@ -787,11 +803,21 @@ struct Scratch {
 };
 
 // f32 -> bf16 hi (rounded) and lo (rounded residual) planes, same element
-// offsets: x ~= hi + lo to ~2^-16 relative.
-__global__ void __launch_bounds__(256)
-    split_planes(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
-                 __nv_bfloat16* __restrict__ lo, int64_t n) {
+// offsets: x ~= hi + lo to ~2^-16 relative.  blockIdx.y selects one of two
+// operands (both GEMM operands in one launch).
+struct PlaneJob {
+  const float* x;
+  __nv_bfloat16* hi;
+  __nv_bfloat16* lo;
+  int64_t n;
+};
+__global__ void __launch_bounds__(256) split_planes(PlaneJob j0, PlaneJob j1) {
   pdl_wait();
+  const PlaneJob& j = blockIdx.y ? j1 : j0;
+  const float* __restrict__ x = j.x;
+  __nv_bfloat16* __restrict__ hi = j.hi;
+  __nv_bfloat16* __restrict__ lo = j.lo;
+  const int64_t n = j.n;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
   for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
     if (i + 4 <= n && ((reinterpret_cast<uintptr_t>(x + i) | reinterpret_cast<uintptr_t>(hi + i) |
@@ -1018,12 +1044,10 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   }
   if (scratch.query) return kWorkspaceQueried;
   if (X3) {
-    const unsigned ga = (unsigned)std::min<int64_t>((na + 1023) / 1024, 148 * 8);
-    const unsigned gb = (unsigned)std::min<int64_t>((nb + 1023) / 1024, 148 * 8);
-    B200_LAUNCH(split_planes, dim3(ga), dim3(256), 0, st, (const float*)a, (__nv_bfloat16*)ah,
-                (__nv_bfloat16*)al, na);
-    B200_LAUNCH(split_planes, dim3(gb), dim3(256), 0, st, (const float*)b, (__nv_bfloat16*)bh,
-                (__nv_bfloat16*)bl, nb);
+    const unsigned g = (unsigned)std::min<int64_t>((std::max(na, nb) + 1023) / 1024, 148 * 4);
+    const PlaneJob ja{(const float*)a, (__nv_bfloat16*)ah, (__nv_bfloat16*)al, (int64_t)na};
+    const PlaneJob jb{(const float*)b, (__nv_bfloat16*)bh, (__nv_bfloat16*)bl, (int64_t)nb};
+    B200_LAUNCH(split_planes, dim3(g, 2), dim3(256), 0, st, ja, jb);
     a = ah;
     b = bh;
     a_lo = al;
@@ -1143,7 +1167,7 @@ int launch_simt(const void* a, const void* b, void* c, const void* bias, int64_t
                 Scratch& scratch) {
   if (N <= 16) {
     const int64_t gx = (M + 127) / 128;
-    const SplitPlan sp = plan_splits(gx * batch, (int)((K + 63) / 64), 2, batch);
+    const SplitPlan sp = plan_splits(gx * batch, (int)((K + 63) / 64), 1, batch);
     float* ws = nullptr;
     if (sp.splits > 1) {
       if (int rc = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &ws)) return rc;
