@@ -112,7 +112,7 @@ namespace {
 struct Exe {
   PJRT_Client* client = nullptr;
   Plan plan;
-  std::string cubin;
+  std::vector<std::string> cubins;  // one per compilation unit of the plan
   std::string name, fingerprint, text, compile_options;
   std::vector<int64_t> out_dims_flat;
   std::vector<size_t> out_dim_sizes;
@@ -406,7 +406,7 @@ std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std:
   e->compile_options = opts;
   e->name = m.name.empty() ? "main" : m.name;
   e->fingerprint = std::to_string(std::hash<std::string>()(text));
-  if (!e->plan.kernel_names.empty()) e->cubin = nvrtc_compile(e->plan.source, "b200_" + e->fingerprint);
+  if (!e->plan.kernel_names.empty()) e->cubins = nvrtc_compile_all(e->plan.units, "b200_" + e->fingerprint);
   for (auto& t : e->plan.output_types) {
     e->out_dim_sizes.push_back(t.dims.size());
     e->out_dims_flat.insert(e->out_dims_flat.end(), t.dims.begin(), t.dims.end());
@@ -599,7 +599,7 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
     std::lock_guard<std::mutex> lk(e.mu);
     auto& slot = e.modules[pd->dev->ordinal];
     if (!slot) {
-      auto m = load_module(*pd->dev, e.cubin, p.kernel_names);
+      auto m = load_module(*pd->dev, e.cubins, p.unit_names, p.kernel_alias);
       for (auto& cd : p.consts) {
         (void)cd;
       }
@@ -1320,7 +1320,9 @@ static PJRT_Error* Executable_NumOutputs(PJRT_Executable_NumOutputs_Args* a) {
   return nullptr;
 }
 static PJRT_Error* Executable_SizeOfGeneratedCodeInBytes(PJRT_Executable_SizeOfGeneratedCodeInBytes_Args* a) {
-  a->size_in_bytes = (int64_t)a->executable->exe->cubin.size();
+  int64_t n = 0;
+  for (auto& c : a->executable->exe->cubins) n += (int64_t)c.size();
+  a->size_in_bytes = n;
   return nullptr;
 }
 static PJRT_Error* Executable_GetCostAnalysis(PJRT_Executable_GetCostAnalysis_Args* a) {
@@ -1679,8 +1681,10 @@ __attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, s
     else if (what == 1) res = dump_plan(p);
     else if (what == 2) res = p.source;
     else if (what == 3) {
-      std::string cubin = p.kernel_names.empty() ? "" : nvrtc_compile(p.source, "inspect");
-      res = "ok " + std::to_string(cubin.size());
+      size_t n = 0;
+      if (!p.kernel_names.empty())
+        for (auto& c : nvrtc_compile_all(p.units, "inspect")) n += c.size();
+      res = "ok " + std::to_string(n);
     } else res = "bad 'what'";
   } catch (const PjrtErr& e) {
     code = e.code;

@@ -1009,10 +1009,40 @@ struct Builder {
           p.temp_last[s] = (int)i;
         }
     }
+    // distinct kernel bodies, spread over units of similar code size
+    std::map<std::string, std::string> seen;  // code with the name blanked -> kernel
+    std::vector<const GenKernel*> uniq;
+    for (auto& k : kernels) {
+      std::string key = k.code;
+      const size_t at = key.find(" " + k.name + "(");
+      if (at != std::string::npos) key.replace(at + 1, k.name.size(), "@");
+      auto it = seen.find(key);
+      if (it != seen.end()) {
+        p.kernel_alias[k.name] = it->second;
+        continue;
+      }
+      seen.emplace(std::move(key), k.name);
+      uniq.push_back(&k);
+    }
     std::ostringstream src;
     src << CodeGen::prelude();
-    for (auto& k : kernels) src << "\n" << k.code;
+    for (auto* k : uniq) src << "\n" << k->code;
     p.source = src.str();
+    size_t total = 0;
+    for (auto* k : uniq) total += k->code.size();
+    const size_t nunits = std::min<size_t>(uniq.size(), std::max<size_t>(1, (total + 24000) / 24000));
+    const size_t units = std::min<size_t>(nunits, 32);
+    std::vector<std::ostringstream> us(units);
+    std::vector<size_t> load(units, 0);
+    p.unit_names.assign(units, {});
+    for (auto& u : us) u << CodeGen::prelude();
+    for (auto* k : uniq) {
+      const size_t i = std::min_element(load.begin(), load.end()) - load.begin();
+      us[i] << "\n" << k->code;
+      load[i] += k->code.size();
+      p.unit_names[i].push_back(k->name);
+    }
+    for (auto& u : us) p.units.push_back(u.str());
   }
 };
 

@@ -3,6 +3,7 @@
 // GEMM/conv lowering) with NVRTC sources from codegen.cc; run by runtime.cc.
 #pragma once
 #include <cstdint>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -52,8 +53,15 @@ struct Plan {
   std::vector<int> param_slots, output_slots;
   std::vector<ConstData> consts;
   std::vector<TensorType> param_types, output_types;
-  std::string source;  // NVRTC program (all generated kernels)
-  std::vector<std::string> kernel_names;
+  std::string source;  // NVRTC program (all generated kernels, each body once)
+  std::vector<std::string> kernel_names;  // every step's kernel name
+  // Compilation units (prelude + a share of the distinct kernels), compiled in
+  // parallel, and the kernel names each defines.  A kernel whose code equals an
+  // earlier one's (e.g. the same layer norm in every block) is compiled once:
+  // kernel_alias maps its name to the compiled one.
+  std::vector<std::string> units;
+  std::vector<std::vector<std::string>> unit_names;
+  std::map<std::string, std::string> kernel_alias;
   int64_t num_replicas = 1;
   std::vector<int> temp_first, temp_last;  // per slot: first/last step touching it
   std::string graph_dump;

@@ -8,6 +8,10 @@
 #include <nvrtc.h>
 
 #include <cstdlib>
+#include <cstdio>
+#include <unistd.h>
+#include <atomic>
+#include <thread>
 #include <cstring>
 #include <functional>
 
@@ -124,22 +128,60 @@ void cu_check(CUresult r, const char* what) {
 }  // namespace
 
 // ----------------------------------------------------------------- NVRTC --
+namespace {
+const char* const kNvrtcOpts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "-lineinfo",
+                                  "--fmad=true", "--diag-suppress=177,550"};
+// 128-bit name for a source: FNV-1a and std::hash, plus the length.
+std::string source_key(const std::string& source) {
+  uint64_t f = 1469598103934665603ull;
+  for (unsigned char ch : source) f = (f ^ ch) * 1099511628211ull;
+  char buf[64];
+  snprintf(buf, sizeof buf, "%016llx%016llx-%zu", (unsigned long long)f,
+           (unsigned long long)std::hash<std::string>()(source), source.size());
+  return buf;
+}
+std::string cache_path(const std::string& key) {
+  const char* dir = getenv("B200_CACHE_DIR");
+  if (!dir || !*dir) return "";
+  int ver[2] = {0, 0};
+  nvrtcVersion(&ver[0], &ver[1]);
+  return std::string(dir) + "/b200-nvrtc" + std::to_string(ver[0]) + "." + std::to_string(ver[1]) +
+         "-" + key + ".cubin";
+}
+}  // namespace
+
 std::string nvrtc_compile(const std::string& source, const std::string& name) {
   static std::mutex mu;
-  static std::map<size_t, std::string> cache;
-  const size_t h = std::hash<std::string>()(source);
+  static std::map<std::string, std::string> cache;
+  std::string opt_text;
+  for (const char* o : kNvrtcOpts) opt_text += std::string(o) + " ";
+  const std::string key = source_key(opt_text + source);
   {
     std::lock_guard<std::mutex> lk(mu);
-    auto it = cache.find(h);
+    auto it = cache.find(key);
     if (it != cache.end()) return it->second;
+  }
+  const std::string path = cache_path(key);
+  if (!path.empty()) {
+    if (FILE* f = fopen(path.c_str(), "rb")) {
+      std::string cubin;
+      char buf[1 << 16];
+      size_t n;
+      while ((n = fread(buf, 1, sizeof buf, f)) > 0) cubin.append(buf, n);
+      fclose(f);
+      if (!cubin.empty()) {
+        std::lock_guard<std::mutex> lk(mu);
+        cache[key] = cubin;
+        return cubin;
+      }
+    }
   }
   nvrtcProgram prog;
   if (nvrtcCreateProgram(&prog, source.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) !=
       NVRTC_SUCCESS)
     throw PjrtErr(13, "nvrtcCreateProgram failed");
-  const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "-lineinfo",
-                        "--fmad=true", "--diag-suppress=177,550"};
-  nvrtcResult r = nvrtcCompileProgram(prog, 5, opts);
+  nvrtcResult r = nvrtcCompileProgram(prog, (int)(sizeof kNvrtcOpts / sizeof kNvrtcOpts[0]),
+                                      kNvrtcOpts);
   if (r != NVRTC_SUCCESS) {
     size_t n = 0;
     nvrtcGetProgramLogSize(prog, &n);
@@ -153,28 +195,71 @@ std::string nvrtc_compile(const std::string& source, const std::string& name) {
   std::string cubin(n, '\0');
   nvrtcGetCUBIN(prog, &cubin[0]);
   nvrtcDestroyProgram(&prog);
+  if (!path.empty()) {  // write-then-rename: readers never see a partial file
+    const std::string tmp = path + ".tmp" + std::to_string((unsigned long long)getpid());
+    if (FILE* f = fopen(tmp.c_str(), "wb")) {
+      const bool ok = fwrite(cubin.data(), 1, cubin.size(), f) == cubin.size();
+      if (fclose(f) == 0 && ok) rename(tmp.c_str(), path.c_str());
+      else remove(tmp.c_str());
+    }
+  }
   std::lock_guard<std::mutex> lk(mu);
-  cache[h] = cubin;
+  cache[key] = cubin;
   return cubin;
 }
 
-LoadedModule::~LoadedModule() {
-  if (mod) Driver::get().ModuleUnload(mod);
+std::vector<std::string> nvrtc_compile_all(const std::vector<std::string>& sources,
+                                           const std::string& name) {
+  std::vector<std::string> out(sources.size());
+  if (sources.size() <= 1) {
+    for (size_t i = 0; i < sources.size(); ++i) out[i] = nvrtc_compile(sources[i], name);
+    return out;
+  }
+  std::vector<std::string> errs(sources.size());
+  std::vector<std::thread> th;
+  std::atomic<size_t> next{0};
+  const size_t nt = std::min<size_t>(sources.size(),
+                                     std::max<unsigned>(1, std::thread::hardware_concurrency()));
+  for (size_t t = 0; t < nt; ++t)
+    th.emplace_back([&] {
+      for (size_t i; (i = next++) < sources.size();) {
+        try {
+          out[i] = nvrtc_compile(sources[i], name + "_" + std::to_string(i));
+        } catch (const std::exception& e) {
+          errs[i] = e.what();
+        }
+      }
+    });
+  for (auto& t : th) t.join();
+  for (auto& e : errs)
+    if (!e.empty()) throw PjrtErr(13, e);
+  return out;
 }
 
-std::unique_ptr<LoadedModule> load_module(Device& d, const std::string& cubin,
-                                          const std::vector<std::string>& names) {
+LoadedModule::~LoadedModule() {
+  for (CUmodule m : mods)
+    if (m) Driver::get().ModuleUnload(m);
+}
+
+std::unique_ptr<LoadedModule> load_module(Device& d, const std::vector<std::string>& cubins,
+                                          const std::vector<std::vector<std::string>>& names,
+                                          const std::map<std::string, std::string>& alias) {
   auto m = std::make_unique<LoadedModule>();
-  if (names.empty()) return m;
+  if (cubins.empty()) return m;
   d.activate();
   cudaFree(nullptr);  // make the primary context current
   auto& drv = Driver::get();
-  cu_check(drv.ModuleLoadData(&m->mod, cubin.data()), "cuModuleLoadData");
-  for (auto& n : names) {
-    CUfunction f;
-    cu_check(drv.ModuleGetFunction(&f, m->mod, n.c_str()), "cuModuleGetFunction");
-    m->fns[n] = f;
+  for (size_t u = 0; u < cubins.size(); ++u) {
+    CUmodule mod = nullptr;
+    cu_check(drv.ModuleLoadData(&mod, cubins[u].data()), "cuModuleLoadData");
+    m->mods.push_back(mod);
+    for (auto& n : names.at(u)) {
+      CUfunction f;
+      cu_check(drv.ModuleGetFunction(&f, mod, n.c_str()), "cuModuleGetFunction");
+      m->fns[n] = f;
+    }
   }
+  for (auto& kv : alias) m->fns[kv.first] = m->fns.at(kv.second);
   return m;
 }
 

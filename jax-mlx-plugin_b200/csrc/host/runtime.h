@@ -71,18 +71,25 @@ struct DeviceMem {
   DeviceMem& operator=(const DeviceMem&) = delete;
 };
 
-// NVRTC: CUDA C source -> sm_100a cubin (cached by source hash).
+// NVRTC: CUDA C source -> sm_100a cubin, cached in the process by source hash
+// and, when B200_CACHE_DIR names a directory, on disk across processes.
 std::string nvrtc_compile(const std::string& source, const std::string& name);
+// Several sources compiled on parallel threads (one cubin each, same order).
+std::vector<std::string> nvrtc_compile_all(const std::vector<std::string>& sources,
+                                           const std::string& name);
 
 // Loaded generated kernels of one executable on one device.
 struct LoadedModule {
-  CUmodule mod = nullptr;
+  std::vector<CUmodule> mods;
   std::map<std::string, CUfunction> fns;
   std::vector<std::shared_ptr<DeviceMem>> consts;
   ~LoadedModule();
 };
-std::unique_ptr<LoadedModule> load_module(Device& d, const std::string& cubin,
-                                          const std::vector<std::string>& names);
+// One module per cubin, names[i] defined by cubins[i]; `alias` entries map a
+// name to the function of another.
+std::unique_ptr<LoadedModule> load_module(Device& d, const std::vector<std::string>& cubins,
+                                          const std::vector<std::vector<std::string>>& names,
+                                          const std::map<std::string, std::string>& alias);
 
 // Launch a generated kernel.
 void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[3], int smem,

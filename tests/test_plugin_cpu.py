@@ -110,6 +110,29 @@ def test_row_wise_kernels_share_one_pass():
     assert steps.count("_rows in=") >= 6 * 4 + 2
 
 
+def test_identical_kernels_compile_once_and_cache_on_disk(tmp_path, monkeypatch):
+    """Every block's layer norm, softmax and update kernels are the same code:
+    each distinct body is compiled once (the others alias it), in parallel
+    units; with B200_CACHE_DIR the cubins of a new program are written there
+    and a later compile of the same units reads them back."""
+    text = programs.transformer_step(batch=2, seq=32, layers=3, d=64, heads=2, ffn=128, vocab=96)
+    steps = pjrt.inspect(text, 1).split("steps:")[1].strip().splitlines()
+    kernels = [l for l in steps if l.split()[0].startswith("k")]
+    bodies = pjrt.inspect(text, 2).count("__global__")
+    assert bodies < len(kernels) * 0.6, (bodies, len(kernels))
+    # a program no earlier test compiled (its constant is unique to this test)
+    from jax_b200.hlo import Builder
+    b = Builder("cache_probe")
+    x = b.param((3, 1000))
+    prog = b.module([b.exp(x * 0.123456789) + b.sum(x, [1], keepdims=True)])
+    monkeypatch.setenv("B200_CACHE_DIR", str(tmp_path))
+    first = pjrt.inspect(prog, 3)
+    files = sorted(tmp_path.glob("b200-nvrtc*.cubin"))
+    assert first.startswith("ok ") and files
+    assert sum(f.stat().st_size for f in files) == int(first.split()[1])
+    assert not list(tmp_path.glob("*.tmp*"))
+
+
 def test_non_causal_and_bnth_attention_also_match():
     g = pjrt.inspect(programs.sdpa(2, 256, 4, 64, causal=False), 0)
     assert "fused_sdpa" in g and "causal=0" in g
