@@ -42,7 +42,8 @@ struct GenKernel {
 class CodeGen {
  public:
   CodeGen(const Graph& g, const std::vector<Slot>& slots, SlotOf slot_of)
-      : g_(g), slots_(slots), slot_of_(std::move(slot_of)) {}
+      : g_(g), slots_(slots), slot_of_(std::move(slot_of)),
+        round_each_op_(bf16_round_each_op_from_env()) {}
 
   // out = value at each index of `v`'s shape (loop fusion root).
   GenKernel loop(const std::vector<ValueRef>& roots, const std::vector<int>& out_slots);
@@ -115,6 +116,10 @@ class CodeGen {
   // f32 and are rounded once when stored (XLA accumulates bf16 reductions in
   // f32 rather than rounding after every add).
   bool accum_f32_ = false;
+  // Round every bf16 op's result (B200_BF16_ROUND_EACH_OP=1 when compiling);
+  // otherwise bf16 values stay f32 until stored or converted.
+  bool round_each_op_ = false;
+  static bool bf16_round_each_op_from_env();
   int vec_ = 1;  // elements per thread group in vector-form kernels
   int tmp_ = 0;
   int indent_ = 1;

@@ -5,7 +5,9 @@ tests compare against (reference ``tests/test_exhaustive.py:112-155`` runs each
 jitted lambda on JAX's CPU backend and on the plugin).  JAX is not installed
 here, so this module stands in for "the same jitted program on JAX's CPU
 backend": it evaluates the identical StableHLO text op by op in float64 (f32
-programs) or with per-op bf16 rounding (bf16 values), on the host.
+programs) and with per-op bf16 rounding (bf16 values), on the host -- or, with
+``excess_bf16=True``, keeping bf16 elementwise chains unrounded until a convert,
+a non-elementwise op or a program output (XLA's default excess precision).
 
 Only tests/, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may
 import this module.  It has its own small parser, independent of the plugin's
@@ -120,10 +122,23 @@ def _const(body: str, t: TT):
     return _cast(np.array(vals).reshape(t.shape), t.dt)
 
 
+# Elementwise ops whose bf16 results stay unrounded in excess-precision mode.
+_EXCESS_OPS = {"negate", "exponential", "log", "tanh", "sqrt", "abs", "rsqrt", "logistic",
+               "exponential_minus_one", "log_plus_one", "sine", "cosine", "add", "subtract",
+               "multiply", "maximum", "minimum", "power", "divide", "select", "clamp"}
+
+
 class Interp:
-    def __init__(self, text: str):
+    """excess_bf16: bf16 elementwise results are not rounded (only explicit
+    converts, non-elementwise ops such as reduce / dot_general and the
+    program's outputs round to bf16) -- XLA's default excess-precision
+    treatment of bf16 chains, which a fusing compiler follows.  Default: every
+    bf16 op's result is rounded."""
+
+    def __init__(self, text: str, excess_bf16: bool = False):
         self.text = re.sub(r"\s*loc\([^)]*\)", "", text)
         self.funcs = self._split_funcs(self.text)
+        self.excess_bf16 = excess_bf16
 
     # ------------------------------------------------------------ parsing --
     @staticmethod
@@ -172,7 +187,12 @@ class Interp:
         for st in self._statements(body):
             if st.startswith("return") or st.startswith("func.return"):
                 rets = re.findall(r"%[\w#]+", st.split(":")[0])
-                return [[self._get(env, x)[r] for x in rets] for r in range(R)]
+                outs = [[self._get(env, x)[r] for x in rets] for r in range(R)]
+                if self.excess_bf16 and func == "main" and ":" in st:
+                    rt = all_types(st.split(":", 1)[1])
+                    outs = [[_cast(v, t.dt) if t.dt == "bf16" else v for v, t in zip(o, rt)]
+                            for o in outs]
+                return outs
             self._exec(st, env, R)
         raise ValueError("function has no return")
 
@@ -208,6 +228,8 @@ class Interp:
     def _op(self, op, rhs, a, t: TT, tys, env, r, all_args):
         dt = t.dt
         c = lambda x: _cast(x, dt)
+        if self.excess_bf16 and dt == "bf16" and op in _EXCESS_OPS:
+            c = lambda x: np.asarray(x, dtype=np.float64)
         if op == "constant":
             body = re.search(r"dense<(.*)>\s*:", rhs).group(1)
             return _const(body, t)
@@ -467,6 +489,6 @@ def dot_general(x, y, lb, rb, lc, rc):
     return np.einsum("".join(xs) + "," + "".join(ys) + "->" + "".join(out), x, y)
 
 
-def run(text: str, replica_args, func: str = "main"):
+def run(text: str, replica_args, func: str = "main", excess_bf16: bool = False):
     """Evaluate StableHLO `text`.  replica_args: list (one per replica) of arg lists."""
-    return Interp(text).run(replica_args, func)
+    return Interp(text, excess_bf16).run(replica_args, func)
