@@ -157,7 +157,7 @@ struct Builder {
     // residual chain (embedding + every block's output) is stored, not summed
     // again from a dozen tensors in each of its readers.
     if (!is_cheap(nd)) {
-      if (u.count(n) > 4 || amplified(n)) return true;
+      if (u.count(n) > 8 || amplified(n)) return true;
       std::set<int> seen;
       if (expr_cost(n, seen) > kRecomputeOps) return true;
     }
@@ -1048,6 +1048,92 @@ struct Builder {
 
 }  // namespace
 
+namespace {
+// Dimensions of a row-major tensor that the GEMM can address as one strided
+// group (they must be contiguous among themselves, in order).
+bool groupable(const TensorType& t, const std::vector<int64_t>& dims, int64_t* stride) {
+  std::vector<int64_t> st(t.rank(), 1);
+  for (int i = t.rank() - 2; i >= 0; --i) st[i] = st[i + 1] * t.dims[i + 1];
+  int64_t prev = -1, size = 1;
+  *stride = 0;
+  for (auto d : dims) {
+    if (t.dims[d] == 1) continue;
+    size *= t.dims[d];
+    if (prev >= 0 && st[prev] != st[d] * t.dims[d]) return false;
+    prev = d;
+    *stride = st[d];
+  }
+  if (size == 1) *stride = 0;
+  return true;
+}
+
+// A dot_general operand whose batch, free or contracting dimensions cannot be
+// addressed as strided groups by the GEMM (e.g. attention over [B, T, N, H]
+// with batch dims B and N) is read through an explicit transpose to batch,
+// free, contracting order.  As a graph node the transpose is planned like any
+// other fusible value: the kernel that produces the operand (a projection's
+// bias add) writes it in the GEMM's order, instead of a copy pass afterwards.
+void canonicalize_dot_operands(Graph& g) {
+  std::map<std::pair<int, std::vector<int64_t>>, int> made;  // (operand node, perm) -> transpose
+  const size_t n0 = g.nodes.size();
+  for (size_t n = 0; n < n0; ++n) {
+    if (g.nodes[n].dead || g.nodes[n].op != Op::DotGeneral) continue;
+    for (int side = 0; side < 2; ++side) {
+      Node& dn = g.nodes[n];
+      const ValueRef v = dn.operands[side];
+      const TensorType t = g.type(v);
+      std::vector<int64_t>& batch = side == 0 ? dn.lhs_batch : dn.rhs_batch;
+      std::vector<int64_t>& contract = side == 0 ? dn.lhs_contract : dn.rhs_contract;
+      std::vector<int64_t> free_dims;
+      for (int64_t d = 0; d < t.rank(); ++d)
+        if (std::find(batch.begin(), batch.end(), d) == batch.end() &&
+            std::find(contract.begin(), contract.end(), d) == contract.end())
+          free_dims.push_back(d);
+      int64_t sb, sf, sc;
+      const bool ok = groupable(t, batch, &sb) && groupable(t, free_dims, &sf) &&
+                      groupable(t, contract, &sc);
+      // one of the two matrix dimensions must be unit-stride (or trivial)
+      auto unit = [&](const std::vector<int64_t>& dims, int64_t s) {
+        int64_t size = 1;
+        for (auto d : dims) size *= t.dims[d];
+        return size == 1 || s == 1;
+      };
+      if (ok && (unit(free_dims, sf) || unit(contract, sc))) continue;
+      if (t.dtype != DType::F32 && t.dtype != DType::BF16) continue;
+      std::vector<int64_t> perm = batch;
+      perm.insert(perm.end(), free_dims.begin(), free_dims.end());
+      perm.insert(perm.end(), contract.begin(), contract.end());
+      int tn;
+      auto key = std::make_pair(v.node * 8 + v.idx, perm);
+      auto it = made.find(key);
+      if (it != made.end()) {
+        tn = it->second;
+      } else {
+        Node tr;
+        tr.op = Op::Transpose;
+        tr.operands = {v};
+        tr.dims = perm;
+        TensorType ot;
+        ot.dtype = t.dtype;
+        for (auto d : perm) ot.dims.push_back(t.dims[d]);
+        tr.results = {ot};
+        tr.name = g.nodes[v.node].name + ".T";
+        g.nodes.push_back(tr);
+        tn = (int)g.nodes.size() - 1;
+        made[key] = tn;
+      }
+      Node& dn2 = g.nodes[n];  // (push_back may have moved the nodes)
+      dn2.operands[side] = ValueRef{tn, 0};
+      std::vector<int64_t>& b2 = side == 0 ? dn2.lhs_batch : dn2.rhs_batch;
+      std::vector<int64_t>& c2 = side == 0 ? dn2.lhs_contract : dn2.rhs_contract;
+      const int64_t nb = (int64_t)b2.size(), nf = (int64_t)free_dims.size();
+      for (int64_t i = 0; i < nb; ++i) b2[i] = i;
+      for (size_t i = 0; i < c2.size(); ++i) c2[i] = nb + nf + (int64_t)i;
+    }
+  }
+}
+}  // namespace
+
 Plan build_plan(const Module& m) {
   Plan p;
   p.num_replicas = m.num_replicas;
@@ -1058,6 +1144,7 @@ Plan build_plan(const Module& m) {
   (void)ms;
   simplify(g);
   dce(g);
+  canonicalize_dot_operands(g);
   p.graph_dump = dump_graph(g);
   Builder b(p, g);
   b.run();
