@@ -467,8 +467,8 @@ NcclComms& comms_for(PJRT_Client* c, Exe& e) {
 }
 
 // Graph replay applies to single-device Executes of plans whose slots fit a
-// fixed 1 GiB (each slot gets its own buffer, no reuse); B200_GRAPHS=0 turns it
-// off.
+// fixed budget (each slot gets its own buffer, no reuse): B200_GRAPH_MAX_GB
+// (default 1), B200_GRAPHS=0 turns it off.
 GraphState* graph_state(Exe& e, const std::vector<PJRT_Device*>& devs) {
   if (devs.size() != 1) return nullptr;
   static const bool off = [] {
@@ -481,7 +481,12 @@ GraphState* graph_state(Exe& e, const std::vector<PJRT_Device*>& devs) {
     int64_t bytes = 0;
     for (auto& sl : p.slots)
       if (sl.kind != Slot::CONST) bytes += sl.bytes;
-    e.graph_ok = (bytes <= (1ll << 30) && p.steps.size() >= 4) ? 1 : 0;
+    static const int64_t limit = [] {
+      const char* v = std::getenv("B200_GRAPH_MAX_GB");
+      const double gb = v ? std::atof(v) : 1.0;
+      return (int64_t)(gb * (double)(1ll << 30));
+    }();
+    e.graph_ok = (bytes <= limit && p.steps.size() >= 4) ? 1 : 0;
   }
   if (!e.graph_ok) return nullptr;
   auto& g = e.graphs[devs[0]->dev->ordinal];
@@ -502,11 +507,14 @@ void build_graphs(Exe& e, GraphState& gs, PJRT_Device* pd, StepFn& exec_step,
     const Slot& sl = p.slots[s];
     if (sl.kind == Slot::CONST) {
       gs.ptr[0][s] = mod.consts.at(sl.index)->ptr;
-    } else {
+    } else if (sl.parent < 0) {
       gs.mem[s] = std::make_shared<DeviceMem>(&dev, (size_t)std::max<int64_t>(sl.bytes, 1));
       gs.ptr[0][s] = gs.mem[s]->ptr;
     }
   }
+  for (size_t s = 0; s < p.slots.size(); ++s)  // views into all-reduce buckets
+    if (p.slots[s].parent >= 0)
+      gs.ptr[0][s] = static_cast<uint8_t*>(gs.ptr[0][p.slots[s].parent]) + p.slots[s].offset;
   int64_t ws = 0;
   auto P = [&](int s) -> void* { return s < 0 ? nullptr : gs.ptr[0][s]; };
   for (const Step& st : p.steps)
@@ -643,9 +651,15 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
     B200_CUDA(cudaEventCreate(&t_stop));
     B200_CUDA(cudaEventRecord(t_start, devs[0]->dev->stream));
   }
-  auto ensure = [&](size_t d, int s) {
+  std::function<void(size_t, int)> ensure = [&](size_t d, int s) {
     if (s < 0 || ptr[d][s]) return;
     const Slot& sl = p.slots[s];
+    if (sl.parent >= 0) {  // a view into its parent (an all-reduce bucket piece)
+      ensure(d, sl.parent);
+      owned[d][s] = owned[d][sl.parent];
+      ptr[d][s] = static_cast<uint8_t*>(ptr[d][sl.parent]) + sl.offset;
+      return;
+    }
     owned[d][s] = std::make_shared<DeviceMem>(devs[d]->dev, (size_t)std::max<int64_t>(sl.bytes, 1));
     ptr[d][s] = owned[d][s]->ptr;
   };
@@ -665,6 +679,7 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
         dev.activate();
         uint8_t* bk = static_cast<uint8_t*>(ptr[d][bucket]);
         for (size_t k = 0; k < st.args.size(); k += 2) {
+          if (st.args[k].f == 1.f) continue;  // computed in the bucket already
           if (e.num_replicas == 1) {
             B200_CUDA(cudaMemcpyAsync(ptr[d][st.args[k + 1].slot], ptr[d][st.args[k].slot],
                                       (size_t)st.args[k + 1].i * es, cudaMemcpyDeviceToDevice, dev.stream));
@@ -685,8 +700,10 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
           dev.activate();
           const uint8_t* bk = static_cast<const uint8_t*>(ptr[d][bucket]);
           for (size_t k = 0; k < st.args.size(); k += 2)
-            B200_CUDA(cudaMemcpyAsync(ptr[d][st.args[k + 1].slot], bk + (size_t)st.args[k].i * es,
-                                      (size_t)st.args[k + 1].i * es, cudaMemcpyDeviceToDevice, dev.stream));
+            if (st.args[k].f != 1.f)  // (aliased pieces are read in place)
+              B200_CUDA(cudaMemcpyAsync(ptr[d][st.args[k + 1].slot], bk + (size_t)st.args[k].i * es,
+                                        (size_t)st.args[k + 1].i * es, cudaMemcpyDeviceToDevice,
+                                        dev.stream));
         }
       }
     } else if (st.kind == StepKind::AllReduce) {

@@ -544,6 +544,10 @@ struct Builder {
   // slot, offset in elements), args[2k+1] = (output slot, element count); the
   // bucket is the last output slot.
   void bucket_all_reduces() {
+    std::map<int, int> readers;  // slot -> steps reading it
+    for (const Step& s : p.steps)
+      for (int x : s.in)
+        if (x >= 0) ++readers[x];
     std::vector<Step> merged;
     for (size_t i = 0; i < p.steps.size();) {
       const Step& a = p.steps[i];
@@ -583,7 +587,23 @@ struct Builder {
       TensorType bt;
       bt.dtype = (DType)a.dtype;
       bt.dims = {off};
-      b.out.push_back(new_slot(Slot::TEMP, bt, "all_reduce_bucket"));
+      const int bucket = new_slot(Slot::TEMP, bt, "all_reduce_bucket");
+      b.out.push_back(bucket);
+      // A gradient that only this collective reads is computed in its piece
+      // of the bucket and its reduced value read from there (f = 1: no
+      // copies); outputs and parameters keep their own buffers.
+      const int64_t es = dtype_size(bt.dtype);
+      for (size_t k = 0; k < b.args.size(); k += 2) {
+        const int si = b.args[k].slot, so = b.args[k + 1].slot;
+        if (p.slots[si].kind != Slot::TEMP || p.slots[so].kind != Slot::TEMP || readers[si] != 1 ||
+            p.slots[si].parent >= 0 || p.slots[so].parent >= 0)
+          continue;
+        for (int x : {si, so}) {
+          p.slots[x].parent = bucket;
+          p.slots[x].offset = b.args[k].i * es;
+        }
+        b.args[k].f = 1.f;
+      }
       b.ip = a.ip;
       b.ip[0] = off;
       merged.push_back(b);
@@ -1009,6 +1029,13 @@ struct Builder {
           p.temp_last[s] = (int)i;
         }
     }
+    // a parent slot lives from its first view's first use to its last view's last
+    for (size_t s = 0; s < p.slots.size(); ++s) {
+      const int par = p.slots[s].parent;
+      if (par < 0 || p.temp_first[s] < 0) continue;
+      if (p.temp_first[par] < 0 || p.temp_first[s] < p.temp_first[par]) p.temp_first[par] = p.temp_first[s];
+      p.temp_last[par] = std::max(p.temp_last[par], p.temp_last[s]);
+    }
     // distinct kernel bodies, spread over units of similar code size
     std::map<std::string, std::string> seen;  // code with the name blanked -> kernel
     std::vector<const GenKernel*> uniq;
@@ -1158,7 +1185,9 @@ std::string dump_plan(const Plan& p) {
     const Slot& s = p.slots[i];
     static const char* kinds[] = {"param", "output", "temp", "const"};
     os << "  s" << i << " " << kinds[s.kind] << "[" << s.index << "] " << s.type.str() << " "
-       << s.what << "\n";
+       << s.what;
+    if (s.parent >= 0) os << " view=s" << s.parent << "+" << s.offset;
+    os << "\n";
   }
   os << "steps:\n";
   for (auto& st : p.steps) {

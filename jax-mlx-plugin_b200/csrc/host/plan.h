@@ -17,6 +17,11 @@ struct Slot {
   TensorType type;
   int64_t bytes = 0;
   std::string what;  // producing value, for dumps
+  // A view into another TEMP slot (byte offset): a gradient computed straight
+  // into its piece of an all-reduce bucket, and the reduced value read back
+  // from there.  The parent's lifetime covers its views'.
+  int parent = -1;
+  int64_t offset = 0;
 };
 
 struct Arg {

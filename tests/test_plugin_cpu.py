@@ -90,6 +90,10 @@ def test_config_programs_fuse_and_compile():
     assert steps.count("all_reduce_bucket in=") == 1 and steps.count("all_reduce in=") == 0
     bucket = [l for l in steps.splitlines() if "all_reduce_bucket" in l][0]
     assert bucket.split(" out=")[0].count(",") == 9  # 9 inputs, comma-terminated
+    # each gradient is computed in its piece of the bucket and read back from
+    # there: 9 inputs and 9 reduced values are views of the bucket slot
+    bslot = bucket.split(" out=")[1].split(",")[-2]
+    assert plan.split("steps:")[0].count(f"view={bslot}+") == 18
 
 
 def test_row_wise_kernels_share_one_pass():
