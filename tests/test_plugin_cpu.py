@@ -92,7 +92,7 @@ def test_config_programs_fuse_and_compile():
     assert bucket.split(" out=")[0].count(",") == 9  # 9 inputs, comma-terminated
     # each gradient is computed in its piece of the bucket and read back from
     # there: 9 inputs and 9 reduced values are views of the bucket slot
-    bslot = bucket.split(" out=")[1].split(",")[-2]
+    bslot = bucket.split(" out=")[1].split(" ip=")[0].rstrip(",").split(",")[-1]
     assert plan.split("steps:")[0].count(f"view={bslot}+") == 18
 
 
