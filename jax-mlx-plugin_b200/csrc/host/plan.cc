@@ -19,6 +19,7 @@
 #include <sstream>
 
 #include "codegen.h"
+#include "gemm_ws.h"
 #include "passes.h"
 
 namespace b200 {
@@ -275,7 +276,7 @@ struct Builder {
     return gr;
   }
   void emit_gemm(int a, int b, int c, int64_t batch, int64_t M, int64_t N, int64_t K,
-                 Group ab, Group am, Group ak, Group bb, Group bk, Group bn, DType in_dt,
+                 Group ab, Group am, Group ak, Group bb, Group bk, Group bn, int in_dt,
                  DType out_dt) {
     Step st;
     st.kind = StepKind::Gemm;
@@ -311,22 +312,19 @@ struct Builder {
     int ls = slot.at(L), rs = slot.at(R);
     TensorType lt = g.type(L), rt = g.type(R);
     const TensorType& ot = nd.results[0];
+    // Mixed f32 x bf16 operands (JAX's transpose rule for a bf16 dot with an
+    // f32 preferred_element_type emits them) are computed in f32, as XLA
+    // does: the GEMM splits the f32 side into bf16 hi + lo planes and reads
+    // the bf16 side as it is (exact: its lo plane would be zero).
+    int gemm_dt = (int)lt.dtype;
     if (lt.dtype != rt.dtype) {
-      // Mixed f32 x bf16 operands (JAX's transpose rule for a bf16 dot with an
-      // f32 preferred_element_type emits them): widen the bf16 side to f32, the
-      // type XLA computes such a product in.
-      auto widen = [&](int& s, TensorType& t) {
-        std::vector<int64_t> id(t.rank());
-        for (int i = 0; i < t.rank(); ++i) id[i] = i;
-        s = permuted_copy(s, id, "dot_widen", DType::F32);
-        t = p.slots[s].type;
-      };
-      if (lt.dtype == DType::BF16 && rt.dtype == DType::F32) widen(ls, lt);
-      else if (rt.dtype == DType::BF16 && lt.dtype == DType::F32) widen(rs, rt);
+      if (lt.dtype == DType::F32 && rt.dtype == DType::BF16) gemm_dt = B200_GEMM_DT_A_F32_B_BF16;
+      else if (lt.dtype == DType::BF16 && rt.dtype == DType::F32) gemm_dt = B200_GEMM_DT_A_BF16_B_F32;
       else throw PjrtErr(12, "dot_general with mixed operand types");
     }
-    if (lt.dtype != DType::F32 && lt.dtype != DType::BF16)
-      throw PjrtErr(12, std::string("dot_general on ") + dtype_name(lt.dtype) + " is not supported");
+    for (DType t : {lt.dtype, rt.dtype})
+      if (t != DType::F32 && t != DType::BF16)
+        throw PjrtErr(12, std::string("dot_general on ") + dtype_name(t) + " is not supported");
     auto free_dims = [](int rank, const std::vector<int64_t>& a, const std::vector<int64_t>& b) {
       std::vector<int64_t> f;
       for (int64_t d = 0; d < rank; ++d)
@@ -369,7 +367,7 @@ struct Builder {
     }
     if (ab.size != bb.size || ak.size != bk.size) throw PjrtErr(3, "dot_general: shape mismatch");
     int cs = temp_for(ValueRef{n, 0});
-    emit_gemm(ls, rs, cs, ab.size, am.size, bn.size, ak.size, ab, am, ak, bb, bk, bn, lt.dtype,
+    emit_gemm(ls, rs, cs, ab.size, am.size, bn.size, ak.size, ab, am, ak, bb, bk, bn, gemm_dt,
               ot.dtype);
   }
 
@@ -416,7 +414,7 @@ struct Builder {
     } else {
       cs = new_slot(Slot::TEMP, TensorType{ot.dtype, {M, N}}, "conv_out_MN");
     }
-    emit_gemm(as, ks, cs, 1, M, N, K, ab, am, ak, bb, bk, bn, lt.dtype, ot.dtype);
+    emit_gemm(as, ks, cs, 1, M, N, K, ab, am, ak, bb, bk, bn, (int)lt.dtype, ot.dtype);
     if (!direct) {
       // [M..., N] -> output dims: out dim d takes (m_roles position | feature)
       TensorType mn;

@@ -288,11 +288,15 @@ __global__ void __launch_bounds__(192, 1)
 // chunks into swizzled shared memory and store them with TMA (bulk groups,
 // double-buffered per warp).  With split-K the raw f32 partial sums go to the
 // workspace through the same TMA-store path.
-template <int BN, bool X3 = false>
+// SPL: which operands arrive as bf16 hi + lo planes of f32 values (bit 0: A,
+// bit 1: B); the others are bf16 as given.
+template <int BN, int SPL = 0>
 struct PcCfg {
   static constexpr int A_BYTES = 128 * 128;  // 128 rows x 64 bf16
   static constexpr int B_BYTES = BN * 128;
-  static constexpr int STAGE = (A_BYTES + B_BYTES) * (X3 ? 2 : 1);  // [A | B | A lo | B lo]
+  static constexpr int AL_OFF = A_BYTES + B_BYTES;                          // [A | B | A lo | B lo]
+  static constexpr int BL_OFF = AL_OFF + ((SPL & 1) ? A_BYTES : 0);
+  static constexpr int STAGE = BL_OFF + ((SPL & 2) ? B_BYTES : 0);
   static constexpr int STAGES = (192 * 1024 / STAGE) > 8 ? 8 : (192 * 1024 / STAGE);
   static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x (32 rows x 128 B)
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
@@ -311,15 +315,17 @@ struct PersArgs {
   int* err;
 };
 
-// X3 (f32 operands): A and B arrive as bf16 hi and lo planes (split_planes);
-// every K step issues hi*hi + hi*lo + lo*hi.
-template <int BN, typename TO, bool X3>
+// f32 operands (SPL bits) arrive as bf16 hi and lo planes (split_planes); every
+// K step issues hi*hi plus hi*lo for a split B and lo*hi for a split A (an
+// operand that is bf16 already has no lo part: a mixed f32 x bf16 product
+// takes two MMAs per step, two f32 operands three).
+template <int BN, typename TO, int SPL>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_pers(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
                  const __grid_constant__ CUtensorMap tC, const __grid_constant__ CUtensorMap tAl,
                  const __grid_constant__ CUtensorMap tBl, PersArgs p) {
   pdl_wait();
-  using Cfg = PcCfg<BN, X3>;
+  using Cfg = PcCfg<BN, SPL>;
   constexpr int S = Cfg::STAGES;
   constexpr int BK = 64;  // bf16 K elements per 128-byte row
   constexpr int E = 64;   // bf16 MN elements per 128-byte chunk
@@ -336,8 +342,8 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
   auto sA = [&](int s) { return smem + s * Cfg::STAGE; };
   auto sB = [&](int s) { return smem + s * Cfg::STAGE + A_BYTES; };
-  auto sAl = [&](int s) { return smem + s * Cfg::STAGE + A_BYTES + B_BYTES; };
-  auto sBl = [&](int s) { return smem + s * Cfg::STAGE + 2 * A_BYTES + B_BYTES; };
+  auto sAl = [&](int s) { return smem + s * Cfg::STAGE + Cfg::AL_OFF; };
+  auto sBl = [&](int s) { return smem + s * Cfg::STAGE + Cfg::BL_OFF; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_mn = p.tiles_m * p.tiles_n;
@@ -383,10 +389,8 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tA);
     tma_prefetch_desc(&tB);
     tma_prefetch_desc(&tC);
-    if (X3) {
-      tma_prefetch_desc(&tAl);
-      tma_prefetch_desc(&tBl);
-    }
+    if (SPL & 1) tma_prefetch_desc(&tAl);
+    if (SPL & 2) tma_prefetch_desc(&tBl);
   }
   if (warp == 0) {
     tmem_alloc(tslot, 2 * BN);
@@ -412,24 +416,28 @@ __global__ void __launch_bounds__(192, 1)
           }
           mbar_expect_tx(&full[s], Cfg::STAGE);
 #pragma unroll
-          for (int part = 0; part < (X3 ? 2 : 1); ++part) {
+          for (int part = 0; part < (SPL ? 2 : 1); ++part) {
             const CUtensorMap* ma = part ? &tAl : &tA;
             const CUtensorMap* mb = part ? &tBl : &tB;
             uint8_t* da = part ? sAl(s) : sA(s);
             uint8_t* db = part ? sBl(s) : sB(s);
-            if (!p.a_mn) {
-              tma_load_3d(da, ma, &full[s], kb * BK, m0, bz);
-            } else {
+            if (part == 0 || (SPL & 1)) {
+              if (!p.a_mn) {
+                tma_load_3d(da, ma, &full[s], kb * BK, m0, bz);
+              } else {
 #pragma unroll
-              for (int j = 0; j < 128 / E; ++j)
-                tma_load_3d(da + j * (BK * 128), ma, &full[s], m0 + j * E, kb * BK, bz);
+                for (int j = 0; j < 128 / E; ++j)
+                  tma_load_3d(da + j * (BK * 128), ma, &full[s], m0 + j * E, kb * BK, bz);
+              }
             }
-            if (!p.b_mn) {
-              tma_load_3d(db, mb, &full[s], kb * BK, n0, bz);
-            } else {
+            if (part == 0 || (SPL & 2)) {
+              if (!p.b_mn) {
+                tma_load_3d(db, mb, &full[s], kb * BK, n0, bz);
+              } else {
 #pragma unroll
-              for (int j = 0; j < BN / E; ++j)
-                tma_load_3d(db + j * (BK * 128), mb, &full[s], n0 + j * E, kb * BK, bz);
+                for (int j = 0; j < BN / E; ++j)
+                  tma_load_3d(db + j * (BK * 128), mb, &full[s], n0 + j * E, kb * BK, bz);
+              }
             }
           }
         }
@@ -467,10 +475,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             umma_f16(dt, adesc(a0, kk), bdesc(b0, kk), idesc, (i | kk) != 0);
-            if (X3) {
-              umma_f16(dt, adesc(a0, kk), bdesc(smem_u32(sBl(s)), kk), idesc, 1);
-              umma_f16(dt, adesc(smem_u32(sAl(s)), kk), bdesc(b0, kk), idesc, 1);
-            }
+            if (SPL & 2) umma_f16(dt, adesc(a0, kk), bdesc(smem_u32(sBl(s)), kk), idesc, 1);
+            if (SPL & 1) umma_f16(dt, adesc(smem_u32(sAl(s)), kk), bdesc(b0, kk), idesc, 1);
           }
           umma_commit(&empty[s]);
         }
@@ -845,6 +851,15 @@ __global__ void __launch_bounds__(256) split_planes(PlaneJob j0, PlaneJob j1) {
   }
 }
 
+// bf16 -> f32, element for element (the fallback for a mixed-type product).
+__global__ void __launch_bounds__(256)
+    widen_bf16(const __nv_bfloat16* __restrict__ x, float* __restrict__ y, int64_t n) {
+  pdl_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = __bfloat162float(x[i]);
+}
+
 // Sums the split-K partials in a fixed order (deterministic) and applies the
 // epilogue: C[b,m,n] = epi(alpha * sum_s ws[b*splits+s][m][n] (+ bias[n])).
 // One thread per 4 consecutive outputs of a row (N % 4 == 0; rows = batch * M
@@ -998,7 +1013,7 @@ int64_t operand_span(int64_t batch, int64_t sb, int64_t r, int64_t sr, int64_t c
   return (batch - 1) * sb + (r - 1) * sr + (c - 1) * sc + 1;
 }
 
-template <int BN, typename TO, bool X3 = false>
+template <int BN, typename TO, int SPL = 0>
 int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
                 int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
                 int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn,
@@ -1017,12 +1032,15 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
     return (uint64_t)(((v * ES) + 15) / 16 * 16);
   };
   // f32 operands: split into bf16 hi / lo planes with the same element strides
+  // (a bf16 operand is read as it is and must meet the same 16-byte rules)
   const void* a_lo = nullptr;
   const void* b_lo = nullptr;
   int64_t na = 0, nb = 0;
   void *ah = nullptr, *al = nullptr, *bh = nullptr, *bl = nullptr;
-  if (X3) {
+  if (SPL) {
     if (scratch.lent) return B200_ERR_UNSUPPORTED;  // planes need memory: use the tf32 kernel
+    if (!(SPL & 1) && ((uintptr_t)a & 15)) return B200_ERR_UNSUPPORTED;
+    if (!(SPL & 2) && ((uintptr_t)b & 15)) return B200_ERR_UNSUPPORTED;
     // the planes' row pitch (2-byte elements) must still be a multiple of 16 bytes
     auto ok16 = [](int64_t s) { return s == 1 || (s * 2) % 16 == 0; };
     if (!ok16(sAm) || !ok16(sAk) || !ok16(sBk) || !ok16(sBn) ||
@@ -1034,24 +1052,31 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   if (ws) {
     if (int rc2 = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &wsp)) return rc2;
   }
-  if (X3) {
+  if (SPL & 1) {
     na = operand_span(batch, sAb, M, sAm, K, sAk);
-    nb = operand_span(batch, sBb, K, sBk, N, sBn);
     if (int r = scratch.get_owned(2 * (size_t)na, st, &ah)) return r;
     if (int r = scratch.get_owned(2 * (size_t)na, st, &al)) return r;
+  }
+  if (SPL & 2) {
+    nb = operand_span(batch, sBb, K, sBk, N, sBn);
     if (int r = scratch.get_owned(2 * (size_t)nb, st, &bh)) return r;
     if (int r = scratch.get_owned(2 * (size_t)nb, st, &bl)) return r;
   }
   if (scratch.query) return kWorkspaceQueried;
-  if (X3) {
+  if (SPL) {
     const unsigned g = (unsigned)std::min<int64_t>((std::max(na, nb) + 1023) / 1024, 148 * 4);
     const PlaneJob ja{(const float*)a, (__nv_bfloat16*)ah, (__nv_bfloat16*)al, (int64_t)na};
     const PlaneJob jb{(const float*)b, (__nv_bfloat16*)bh, (__nv_bfloat16*)bl, (int64_t)nb};
-    B200_LAUNCH(split_planes, dim3(g, 2), dim3(256), 0, st, ja, jb);
-    a = ah;
-    b = bh;
-    a_lo = al;
-    b_lo = bl;
+    if (SPL == 3) B200_LAUNCH(split_planes, dim3(g, 2), dim3(256), 0, st, ja, jb);
+    else B200_LAUNCH(split_planes, dim3(g, 1), dim3(256), 0, st, SPL == 1 ? ja : jb, ja);
+    if (SPL & 1) {
+      a = ah;
+      a_lo = al;
+    }
+    if (SPL & 2) {
+      b = bh;
+      b_lo = bl;
+    }
   }
   CUtensorMap ta, tb, tc, tal, tbl;
   int rc;
@@ -1079,7 +1104,9 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
     rc = make_tmap(&tb, b, 3, dims, str, box, ES);
   }
   if (rc) return rc;
-  if (X3) {  // lo planes: same shapes and strides as the hi planes
+  tal = ta;  // (unused when the operand has no lo plane)
+  tbl = tb;
+  if (SPL & 1) {  // lo planes: same shapes and strides as the hi planes
     if (!a_mn) {
       uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
       uint64_t str[2] = {(uint64_t)(sAm * ES), bstride(sAb, sAm, M)};
@@ -1092,6 +1119,8 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
       rc = make_tmap(&tal, a_lo, 3, dims, str, box, ES);
     }
     if (rc) return rc;
+  }
+  if (SPL & 2) {
     if (!b_mn) {
       uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)batch};
       uint64_t str[2] = {(uint64_t)(sBn * ES), bstride(sBb, sBn, N)};
@@ -1104,9 +1133,6 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
       rc = make_tmap(&tbl, b_lo, 3, dims, str, box, ES);
     }
     if (rc) return rc;
-  } else {
-    tal = ta;
-    tbl = tb;
   }
   PersArgs p;
   p.M = (int)M;
@@ -1142,11 +1168,11 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
     rc = make_tmap(&tc, c, 3, dims, str, box, so);
   }
   if (rc) return rc;
-  const int smem = PcCfg<BN, X3>::SMEM;
-  if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pers<BN, TO, X3>, smem, "gemm_tc_pers")) return rc2;
+  const int smem = PcCfg<BN, SPL>::SMEM;
+  if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pers<BN, TO, SPL>, smem, "gemm_tc_pers")) return rc2;
   const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch * sp.splits;
   const unsigned grid = (unsigned)std::min<int64_t>(num_tiles, num_sms());
-  B200_LAUNCH(gemm_tc_pers<BN, TO, X3>, dim3(grid), dim3(192), smem, st, ta, tb, tc, tal, tbl, p);
+  B200_LAUNCH(gemm_tc_pers<BN, TO, SPL>, dim3(grid), dim3(192), smem, st, ta, tb, tc, tal, tbl, p);
   if (ws)
     return launch_splitk_reduce<TO>(wsp, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
   return B200_OK;
@@ -1230,12 +1256,49 @@ int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64
                  "gemm: dimension too large");
   B200_CHECK_ARG(epilogue >= 0 && epilogue <= 3, "gemm: bad epilogue");
   B200_CHECK_ARG(!(epilogue == 1 || epilogue == 2) || bias, "gemm: epilogue needs a bias");
-  B200_CHECK_ARG(in_dtype == B200_DT_F32 || in_dtype == B200_DT_BF16, "gemm: in_dtype must be F32 or BF16");
+  B200_CHECK_ARG(in_dtype == B200_DT_F32 || in_dtype == B200_DT_BF16 ||
+                     in_dtype == B200_GEMM_DT_A_F32_B_BF16 || in_dtype == B200_GEMM_DT_A_BF16_B_F32,
+                 "gemm: in_dtype must be F32, BF16 or a mixed F32 x BF16 code");
   B200_CHECK_ARG(out_dtype == B200_DT_F32 || out_dtype == B200_DT_BF16, "gemm: out_dtype must be F32 or BF16");
   if (ldc <= 0) ldc = N;
   if (M == 0 || N == 0) return B200_OK;
   auto st = (cudaStream_t)stream;
   if (K == 0) return set_error(B200_ERR_UNSUPPORTED, "gemm: K == 0 is not supported");
+  if (in_dtype == B200_GEMM_DT_A_F32_B_BF16 || in_dtype == B200_GEMM_DT_A_BF16_B_F32) {
+    const bool a32 = in_dtype == B200_GEMM_DT_A_F32_B_BF16;
+    const bool obf = out_dtype == B200_DT_BF16;
+    // persistent kernel: the f32 operand as bf16 hi + lo planes, the bf16 one as given
+    auto m16 = [](int64_t s) { return ((s * 2) & 15) == 0; };
+    int a_mn = -1, b_mn = -1;
+    if (sAk == 1 && m16(sAm) && (batch == 1 || m16(sAb))) a_mn = 0;
+    else if (sAm == 1 && m16(sAk) && (batch == 1 || m16(sAb))) a_mn = 1;
+    if (sBk == 1 && m16(sBn) && (batch == 1 || m16(sBb))) b_mn = 0;
+    else if (sBn == 1 && m16(sBk) && (batch == 1 || m16(sBb))) b_mn = 1;
+    if (!force_simt() && use_persistent() && f32_matmul_3x() && a_mn >= 0 && b_mn >= 0 && K * 2 >= 16) {
+      int prc;
+#define B200_PERSM(BN_, TO_)                                                                       \
+  prc = a32 ? launch_pers<BN_, TO_, 1>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, \
+                                       ldc, alpha, epilogue, a_mn, b_mn, st, scratch)              \
+            : launch_pers<BN_, TO_, 2>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, \
+                                       ldc, alpha, epilogue, a_mn, b_mn, st, scratch)
+      if (N <= 64) { if (obf) B200_PERSM(64, __nv_bfloat16); else B200_PERSM(64, float); }
+      else if (N <= 128) { if (obf) B200_PERSM(128, __nv_bfloat16); else B200_PERSM(128, float); }
+      else { if (obf) B200_PERSM(256, __nv_bfloat16); else B200_PERSM(256, float); }
+#undef B200_PERSM
+      if (prc != B200_ERR_UNSUPPORTED) return prc;
+    }
+    // anything else: the bf16 operand widened to f32 (same element offsets), then the f32 path
+    const void* src = a32 ? b : a;
+    const int64_t span = a32 ? operand_span(batch, sBb, K, sBk, N, sBn) : operand_span(batch, sAb, M, sAm, K, sAk);
+    void* wide = nullptr;
+    if (int r = scratch.get_owned(4 * (size_t)span, st, &wide)) return r;
+    if (!scratch.query) {
+      const unsigned g = (unsigned)std::min<int64_t>((span + 255) / 256, 148 * 8);
+      B200_LAUNCH(widen_bf16, dim3(g), dim3(256), 0, st, (const __nv_bfloat16*)src, (float*)wide, span);
+    }
+    return gemm_dispatch(a32 ? a : wide, a32 ? wide : b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb,
+                         sBk, sBn, ldc, alpha, B200_DT_F32, out_dtype, epilogue, stream, scratch);
+  }
   const int es = in_dtype == B200_DT_F32 ? 4 : 2;
   auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
   auto m16 = [&](int64_t s) { return ((s * es) & 15) == 0; };
@@ -1258,7 +1321,7 @@ int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64
         // bf16 hi/lo planes on the persistent kernel (3 bf16 MMAs per step)
         int prc;
 #define B200_PERS3(BN_, TO_)                                                                      \
-  prc = launch_pers<BN_, TO_, true>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, \
+  prc = launch_pers<BN_, TO_, 3>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, \
                                     ldc, alpha, epilogue, a_mn, b_mn, st, scratch)
         if (N <= 64) { if (obf) B200_PERS3(64, __nv_bfloat16); else B200_PERS3(64, float); }
         else if (N <= 128) { if (obf) B200_PERS3(128, __nv_bfloat16); else B200_PERS3(128, float); }

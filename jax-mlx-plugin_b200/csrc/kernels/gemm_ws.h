@@ -11,6 +11,14 @@
 extern "C" {
 #endif
 
+// Extra in_dtype values accepted by the entry points below (and by b200_gemm):
+// one f32 and one bf16 operand, as JAX's transpose rule emits for a bf16
+// dot_general with an f32 result.  The f32 operand is split into bf16 hi + lo
+// planes and the bf16 one is read as it is: two bf16 MMAs per K step, the
+// accuracy of three-plane f32 (the bf16 operand's lo plane is zero).
+#define B200_GEMM_DT_A_F32_B_BF16 100
+#define B200_GEMM_DT_A_BF16_B_F32 101
+
 // Bytes of workspace b200_gemm_ws needs for these arguments (same meaning as
 // b200_gemm's); 0 when none, -1 when the arguments are rejected.  Launches
 // nothing.

@@ -215,6 +215,39 @@ def test_gemm_layouts(a_t, b_t, dt):
     assert_close(got, ref, 2e-3 if dt == kernels.DT_F32 else 1e-2, f"gemm a_t={a_t} b_t={b_t}")
 
 
+# in_dtype codes for one f32 and one bf16 operand (csrc/kernels/gemm_ws.h)
+GEMM_DT_A_F32_B_BF16, GEMM_DT_A_BF16_B_F32 = 100, 101
+
+
+@pytest.mark.parametrize("a32", [True, False])
+@pytest.mark.parametrize("M,N,K,a_t,b_t,batch", [(296, 264, 200, False, False, 1),
+                                                 (256, 256, 64, True, False, 16),
+                                                 (256, 64, 256, False, True, 8),
+                                                 (100, 37, 12, False, False, 1)])
+def test_gemm_mixed_f32_bf16(a32, M, N, K, a_t, b_t, batch):
+    """One f32 and one bf16 operand (JAX's transpose rule for a bf16 dot with
+    an f32 result): the f32 side as bf16 hi + lo planes, the bf16 side read as
+    it is (the last shape takes the widen-to-f32 fallback: 12-element rows are
+    not 16-byte strided in bf16).  vs f64 on the same values, 2e-3 relative."""
+    rng = np.random.default_rng(M + N + K + a32)
+    a = rng.standard_normal((batch, M, K)).astype(np.float32)
+    b = rng.standard_normal((batch, K, N)).astype(np.float32)
+    A_phys = np.swapaxes(a, 1, 2).copy() if a_t else a
+    B_phys = np.swapaxes(b, 1, 2).copy() if b_t else b
+    A = dev(A_phys) if a32 else bf16_dev(A_phys)
+    Bm = bf16_dev(B_phys) if a32 else dev(B_phys)
+    a_val = host(A) if not a_t else np.swapaxes(host(A), 1, 2)
+    b_val = host(Bm) if not b_t else np.swapaxes(host(Bm), 1, 2)
+    sAb, sAm, sAk = M * K, (1 if a_t else K), (M if a_t else 1)
+    sBb, sBk, sBn = K * N, (1 if b_t else N), (K if b_t else 1)
+    C = torch.full((batch, M, N), float("nan"), device="cuda", dtype=torch.float32)
+    code = GEMM_DT_A_F32_B_BF16 if a32 else GEMM_DT_A_BF16_B_F32
+    kernels.gemm(A.data_ptr(), Bm.data_ptr(), C.data_ptr(), 0, batch, M, N, K, sAb, sAm, sAk, sBb,
+                 sBk, sBn, N, 1.0, code, kernels.DT_F32, 0, stream())
+    ref = np.einsum("bmk,bkn->bmn", a_val.astype(np.float64), b_val.astype(np.float64))
+    assert_close(host(C), ref, 2e-3, f"mixed gemm a32={a32} {batch}x{M}x{N}x{K}")
+
+
 @pytest.mark.parametrize("M,N,K", [(1024, 1024, 784), (1024, 1024, 1024), (128, 128, 32), (1, 64, 16),
                                    (200704, 32, 12)])
 def test_gemm_config_shapes_f32(M, N, K):
