@@ -66,7 +66,8 @@ class CodeGen {
   // out[j] = src[permuted j]: out dims are src dims[perm[i]] (a transpose copy).
   GenKernel permute(int src_slot, const std::vector<int64_t>& perm, int out_slot);
   // Several row-wise phases over the same OUT rows of RED elements in one
-  // kernel: one warp (RED <= 4096) or one block per row runs the phases in
+  // kernel: one warp (or, for rows above 4096 elements read by more than one
+  // phase, one 256-thread block) per row runs the phases in
   // order, with a barrier between them, so that a phase reads what earlier
   // phases wrote for its row (still in L1/L2) instead of a separate kernel
   // reading it back from HBM.  Every read of a phase output by a later phase

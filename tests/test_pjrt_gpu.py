@@ -427,8 +427,9 @@ def test_bf16_round_each_op_mode_matches_per_op_oracle(client, monkeypatch):
                                                   (2400, 6000, "bf16", "1"), (2400, 6000, "bf16", "0"),
                                                   (3000, 10, "f32", "0")])
 def test_logits_cross_entropy_row_groups(client, monkeypatch, rows, cols, dt, each_op):
-    """Loss, d logits and d bias of softmax cross-entropy over long rows (a block
-    per row above 4096 columns, a warp per row below) vs the interpreter.  f32:
+    """Loss, d logits and d bias of softmax cross-entropy over long rows (one
+    full pass over each row per kernel: a warp per row at any length) vs the
+    interpreter.  f32:
     1e-5 relative (no contraction); bf16 inputs and gradients: 1e-2 (one bf16
     ulp of the rounded outputs), in both bf16 rounding modes against the
     interpreter mode that rounds at the same places."""
