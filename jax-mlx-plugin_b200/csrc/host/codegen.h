@@ -113,6 +113,12 @@ class CodeGen {
   // through the coherent path, not the read-only cache).
   std::set<ValueRef> hidden_;
   std::set<int> coherent_;
+  // f32 nodes whose every use in the kernel being emitted ends in a bf16 value
+  // (a convert to bf16, or a bf16 output): their exp / log / tanh / divide
+  // use the approximate hardware forms, as bf16-typed nodes do -- the result
+  // is rounded to 8 significant bits anyway.
+  std::set<int> bf16_sink_;
+  void mark_bf16_sinks(const std::vector<ValueRef>& roots);
   // Set while emitting a reduction's combiner: bf16 partial results stay in
   // f32 and are rounded once when stored (XLA accumulates bf16 reductions in
   // f32 rather than rounding after every add).
