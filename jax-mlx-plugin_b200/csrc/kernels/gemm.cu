@@ -283,10 +283,12 @@ __global__ void __launch_bounds__(192, 1)
 // (t = blockIdx.x, += gridDim.x).  Warp 0 streams A/B k-blocks through an
 // S-stage TMA ring that runs continuously across tiles; warp 1 issues
 // tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators, so the
-// epilogue of tile i overlaps the MMAs of tile i+1; warps 2-5 drain TMEM
-// (tcgen05.ld), apply alpha / bias / ReLU, convert, write 32-row x 128-byte
-// chunks into swizzled shared memory and store them with TMA (bulk groups,
-// double-buffered per warp).  With split-K the raw f32 partial sums go to the
+// epilogue of tile i overlaps the MMAs of tile i+1; warps 2-9 drain TMEM
+// (tcgen05.ld; two warps per 32-lane quarter, each half of the tile's
+// columns), apply alpha / bias / ReLU, convert, write 32-row x 128-byte chunks
+// into swizzled shared memory and store them with TMA (bulk groups, one 4 KB
+// buffer per warp).  Eight draining warps keep the epilogue shorter than the
+// MMAs of a tile when K is short (an LM head's K = 512).  With split-K the raw f32 partial sums go to the
 // workspace through the same TMA-store path.
 // SPL: which operands arrive as bf16 hi + lo planes of f32 values (bit 0: A,
 // bit 1: B); the others are bf16 as given.
@@ -298,7 +300,7 @@ struct PcCfg {
   static constexpr int BL_OFF = AL_OFF + ((SPL & 1) ? A_BYTES : 0);
   static constexpr int STAGE = BL_OFF + ((SPL & 2) ? B_BYTES : 0);
   static constexpr int STAGES = (192 * 1024 / STAGE) > 8 ? 8 : (192 * 1024 / STAGE);
-  static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int EPI_BYTES = 8 * 4096;  // 8 epilogue warps x (32 rows x 128 B)
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
 };
 
@@ -319,8 +321,10 @@ struct PersArgs {
 // K step issues hi*hi plus hi*lo for a split B and lo*hi for a split A (an
 // operand that is bf16 already has no lo part: a mixed f32 x bf16 product
 // takes two MMAs per step, two f32 operands three).
+constexpr int kPersEpiWarps = 8;
+constexpr int kPersThreads = 64 + 32 * kPersEpiWarps;
 template <int BN, typename TO, int SPL>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kPersThreads, 1)
     gemm_tc_pers(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
                  const __grid_constant__ CUtensorMap tC, const __grid_constant__ CUtensorMap tAl,
                  const __grid_constant__ CUtensorMap tBl, PersArgs p) {
@@ -330,7 +334,6 @@ __global__ void __launch_bounds__(192, 1)
   constexpr int BK = 64;  // bf16 K elements per 128-byte row
   constexpr int E = 64;   // bf16 MN elements per 128-byte chunk
   constexpr int A_BYTES = Cfg::A_BYTES;
-  constexpr int B_BYTES = Cfg::B_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* epi_smem = smem + S * Cfg::STAGE;
@@ -382,7 +385,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kPersEpiWarps);
     }
     *abort = 0;
     mbar_fence_init();
@@ -485,10 +488,18 @@ __global__ void __launch_bounds__(192, 1)
         else mbar_arrive(&tfull[acc]);
       }
     }
-  } else {  // ---- warps 2..5: epilogue
+  } else {  // ---- warps 2..9: epilogue
     using TS = typename std::conditional<std::is_same<TO, float>::value, float, TO>::type;
     const int q = warp & 3;  // TMEM lane quarter this warp may read
-    uint8_t* stg = epi_smem + (warp - 2) * 8192;
+    const int half = (warp - 2) >> 2;  // which half of the tile's column chunks
+    uint8_t* stg = epi_smem + (warp - 2) * 4096;
+    // this warp's column chunks [c_lo, c_hi) out of `n` (all of them for half 0
+    // when there is a single chunk)
+    auto chunks = [&](int n, int& c_lo, int& c_hi) {
+      if (n < 2) { c_lo = 0; c_hi = half ? 0 : n; return; }
+      c_lo = half * (n / 2);
+      c_hi = half ? n : n / 2;
+    };
     int tl = 0, nstore = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tl) {
       int m0, n0, bz, ks, kb0, nkb;
@@ -502,8 +513,10 @@ __global__ void __launch_bounds__(192, 1)
       const int zc = p.out_ws ? bz * p.splits + ks : bz;
       if (p.out_ws) {
         // raw f32 partial sums: 32 columns per 128-byte chunk
+        int c_lo, c_hi;
+        chunks(BN / 32, c_lo, c_hi);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = c_lo; c < c_hi; ++c) {
           const int nc = n0 + c * 32;
           if (nc >= p.N || rowbase >= p.M) continue;
           float v[32];
@@ -513,8 +526,8 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.f;
           }
-          uint8_t* buf = stg + (nstore & 1) * 4096;
-          if (lane == 0 && nstore >= 2) bulk_wait_group_read<1>();
+          uint8_t* buf = stg;  // its previous store must have read it
+          if (lane == 0 && nstore >= 1) bulk_wait_group_read<0>();
           __syncwarp();
 #pragma unroll
           for (int u = 0; u < 8; ++u)
@@ -530,8 +543,10 @@ __global__ void __launch_bounds__(192, 1)
         }
       } else {
         constexpr int CW = 128 / (int)sizeof(TO);  // output columns per 128-byte chunk
+        int c_lo, c_hi;
+        chunks(BN / CW, c_lo, c_hi);
 #pragma unroll 1
-        for (int c = 0; c < BN / CW; ++c) {
+        for (int c = c_lo; c < c_hi; ++c) {
           const int nc = n0 + c * CW;
           if (nc >= p.N || rowbase >= p.M) continue;
           float v[CW];
@@ -552,8 +567,8 @@ __global__ void __launch_bounds__(192, 1)
             if (p.epi >= 2) x = fmaxf(x, 0.f);
             v[j] = x;
           }
-          uint8_t* buf = stg + (nstore & 1) * 4096;
-          if (lane == 0 && nstore >= 2) bulk_wait_group_read<1>();
+          uint8_t* buf = stg;  // its previous store must have read it
+          if (lane == 0 && nstore >= 1) bulk_wait_group_read<0>();
           __syncwarp();
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
@@ -1172,7 +1187,7 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pers<BN, TO, SPL>, smem, "gemm_tc_pers")) return rc2;
   const int64_t num_tiles = (int64_t)tiles_m * tiles_n * batch * sp.splits;
   const unsigned grid = (unsigned)std::min<int64_t>(num_tiles, num_sms());
-  B200_LAUNCH(gemm_tc_pers<BN, TO, SPL>, dim3(grid), dim3(192), smem, st, ta, tb, tc, tal, tbl, p);
+  B200_LAUNCH(gemm_tc_pers<BN, TO, SPL>, dim3(grid), dim3(kPersThreads), smem, st, ta, tb, tc, tal, tbl, p);
   if (ws)
     return launch_splitk_reduce<TO>(wsp, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
   return B200_OK;
