@@ -61,8 +61,10 @@ class CodeGen {
   // im2col for a convolution: A[m, k] (row-major, M x K) from the lhs operand.
   // k_roles: kernel dims (excluding k_out) in K order; m_roles: output dims
   // (excluding out_feature) in M order.
+  // With lo_slot >= 0 (f32 input), out_slot / lo_slot receive the patches as
+  // bf16 hi / lo planes for an f32 GEMM (x ~= hi + lo).
   GenKernel im2col(int node, int out_slot, const std::vector<int64_t>& k_roles,
-                   const std::vector<int64_t>& m_roles, int64_t M, int64_t K);
+                   const std::vector<int64_t>& m_roles, int64_t M, int64_t K, int lo_slot = -1);
   // out[j] = src[permuted j]: out dims are src dims[perm[i]] (a transpose copy).
   GenKernel permute(int src_slot, const std::vector<int64_t>& perm, int out_slot);
   // Several row-wise phases over the same OUT rows of RED elements in one

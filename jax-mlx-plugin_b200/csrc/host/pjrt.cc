@@ -466,6 +466,39 @@ NcclComms& comms_for(PJRT_Client* c, Exe& e) {
   return ref;
 }
 
+// A GEMM step's call.  st.in = {A, B[, bias]}; the bias is read only by the
+// bias epilogues (ip[11] 1 or 2).  st.args, when present, name the bf16 lo
+// planes of an A / B that a producer wrote split (slot -1: not split).
+template <typename PtrOf>
+static int64_t gemm_step_ws_bytes(const Step& st, PtrOf P, void* stream) {
+  const void* bias = (st.ip[11] == 1 || st.ip[11] == 2) ? P(st.in[2]) : nullptr;
+  const void* a_lo = st.args.size() >= 2 && st.args[0].slot >= 0 ? P(st.args[0].slot) : nullptr;
+  const void* b_lo = st.args.size() >= 2 && st.args[1].slot >= 0 ? P(st.args[1].slot) : nullptr;
+  if (a_lo || b_lo)
+    return b200_gemm_planes_workspace_bytes(P(st.in[0]), a_lo, P(st.in[1]), b_lo, P(st.out[0]), bias,
+                                            st.ip[0], st.ip[1], st.ip[2], st.ip[3], st.ip[4], st.ip[5],
+                                            st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10], st.fp[0],
+                                            st.dtype, st.dtype2, (int)st.ip[11], stream);
+  return b200_gemm_workspace_bytes(P(st.in[0]), P(st.in[1]), P(st.out[0]), bias, st.ip[0], st.ip[1],
+                                   st.ip[2], st.ip[3], st.ip[4], st.ip[5], st.ip[6], st.ip[7], st.ip[8],
+                                   st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2, (int)st.ip[11],
+                                   stream);
+}
+template <typename PtrOf>
+static int gemm_step_run(const Step& st, PtrOf P, void* stream, void* ws, size_t ws_bytes) {
+  const void* bias = (st.ip[11] == 1 || st.ip[11] == 2) ? P(st.in[2]) : nullptr;
+  const void* a_lo = st.args.size() >= 2 && st.args[0].slot >= 0 ? P(st.args[0].slot) : nullptr;
+  const void* b_lo = st.args.size() >= 2 && st.args[1].slot >= 0 ? P(st.args[1].slot) : nullptr;
+  if (a_lo || b_lo)
+    return b200_gemm_planes_ws(P(st.in[0]), a_lo, P(st.in[1]), b_lo, P(st.out[0]), bias, st.ip[0],
+                               st.ip[1], st.ip[2], st.ip[3], st.ip[4], st.ip[5], st.ip[6], st.ip[7],
+                               st.ip[8], st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2,
+                               (int)st.ip[11], stream, ws, ws_bytes);
+  return b200_gemm_ws(P(st.in[0]), P(st.in[1]), P(st.out[0]), bias, st.ip[0], st.ip[1], st.ip[2],
+                      st.ip[3], st.ip[4], st.ip[5], st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10],
+                      st.fp[0], st.dtype, st.dtype2, (int)st.ip[11], stream, ws, ws_bytes);
+}
+
 // Graph replay applies to single-device Executes of plans whose slots fit a
 // fixed budget (each slot gets its own buffer, no reuse): B200_GRAPH_MAX_GB
 // (default 1), B200_GRAPHS=0 turns it off.
@@ -519,12 +552,7 @@ void build_graphs(Exe& e, GraphState& gs, PJRT_Device* pd, StepFn& exec_step,
   auto P = [&](int s) -> void* { return s < 0 ? nullptr : gs.ptr[0][s]; };
   for (const Step& st : p.steps)
     if (st.kind == StepKind::Gemm)
-      ws = std::max<int64_t>(ws, b200_gemm_workspace_bytes(
-                                     P(st.in[0]), P(st.in[1]), P(st.out[0]),
-                                     st.in.size() > 2 ? P(st.in[2]) : nullptr, st.ip[0], st.ip[1],
-                                     st.ip[2], st.ip[3], st.ip[4], st.ip[5], st.ip[6], st.ip[7],
-                                     st.ip[8], st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2,
-                                     (int)st.ip[11], dev.stream));
+      ws = std::max<int64_t>(ws, gemm_step_ws_bytes(st, P, dev.stream));
   if (ws > 0) gs.gemm_ws = std::make_shared<DeviceMem>(&dev, (size_t)ws);
   gemm_ws_override = &gs.gemm_ws;
   try {
@@ -759,24 +787,16 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
           case StepKind::Gemm: {
             // split-K partials / bf16 planes come from the caching allocator
             // (released after the launch: stream order protects the reuse)
-            const void* ga = slotp(st.in[0]);
-            const void* gb = slotp(st.in[1]);
-            void* gc = slotp(st.out[0]);
-            const void* gbias = st.in.size() > 2 ? slotp(st.in[2]) : nullptr;
-            const int64_t wsb = b200_gemm_workspace_bytes(
-                ga, gb, gc, gbias, st.ip[0], st.ip[1], st.ip[2], st.ip[3], st.ip[4], st.ip[5],
-                st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10], st.fp[0], st.dtype, st.dtype2,
-                (int)st.ip[11], dev.stream);
+            auto SP = [&](int s) -> void* { return s < 0 ? nullptr : slotp(s); };
+            const int64_t wsb = gemm_step_ws_bytes(st, SP, dev.stream);
             std::shared_ptr<DeviceMem> ws;
             if (wsb > 0) {
               // graph capture / replay: the graph's fixed workspace
               if (gemm_ws_override && *gemm_ws_override) ws = *gemm_ws_override;
               else ws = std::make_shared<DeviceMem>(&dev, (size_t)wsb);
             }
-            kcheck(b200_gemm_ws(ga, gb, gc, gbias, st.ip[0], st.ip[1], st.ip[2], st.ip[3], st.ip[4],
-                                st.ip[5], st.ip[6], st.ip[7], st.ip[8], st.ip[9], st.ip[10], st.fp[0],
-                                st.dtype, st.dtype2, (int)st.ip[11], dev.stream,
-                                ws ? ws->ptr : nullptr, wsb > 0 ? (size_t)wsb : 0),
+            kcheck(gemm_step_run(st, SP, dev.stream, ws ? ws->ptr : nullptr,
+                                 wsb > 0 ? (size_t)wsb : 0),
                    "gemm");
             break;
           }

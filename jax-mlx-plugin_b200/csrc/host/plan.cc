@@ -390,9 +390,17 @@ struct Builder {
     for (auto d : m_roles) M *= ot.dims[d];
     for (auto d : k_roles) K *= kt.dims[d];
     const int64_t N = kt.dims[c.k_out];
-    TensorType at{lt.dtype, {M, K}};
-    int as = new_slot(Slot::TEMP, at, "im2col");
-    add_kernel(cg.im2col(n, as, k_roles, m_roles, M, K));
+    // f32 patches go straight to the GEMM's bf16 hi / lo planes when their
+    // rows are 16-byte multiples in bf16 (no f32 patch matrix, no split pass)
+    const bool planes = lt.dtype == DType::F32 && K % 8 == 0;
+    int as, al = -1;
+    if (planes) {
+      as = new_slot(Slot::TEMP, TensorType{DType::BF16, {M, K}}, "im2col_hi");
+      al = new_slot(Slot::TEMP, TensorType{DType::BF16, {M, K}}, "im2col_lo");
+    } else {
+      as = new_slot(Slot::TEMP, TensorType{lt.dtype, {M, K}}, "im2col");
+    }
+    add_kernel(cg.im2col(n, as, k_roles, m_roles, M, K, al));
     int ks = slot.at(nd.operands[1]);
     Group bk, bn;
     if (c.k_out == kt.rank() - 1) {
@@ -415,6 +423,14 @@ struct Builder {
       cs = new_slot(Slot::TEMP, TensorType{ot.dtype, {M, N}}, "conv_out_MN");
     }
     emit_gemm(as, ks, cs, 1, M, N, K, ab, am, ak, bb, bk, bn, (int)lt.dtype, ot.dtype);
+    if (planes) {  // A arrives split: its lo plane (see the executor's GEMM step)
+      Step& g = p.steps.back();
+      Arg alo, blo;
+      alo.slot = al;
+      blo.slot = -1;
+      g.args = {alo, blo};
+      g.in.push_back(al);
+    }
     if (!direct) {
       // [M..., N] -> output dims: out dim d takes (m_roles position | feature)
       TensorType mn;

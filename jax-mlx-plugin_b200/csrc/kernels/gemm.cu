@@ -866,6 +866,17 @@ __global__ void __launch_bounds__(256) split_planes(PlaneJob j0, PlaneJob j1) {
   }
 }
 
+// hi + lo bf16 planes -> f32 (the fallback when planes given by the caller
+// cannot feed the persistent kernel).
+__global__ void __launch_bounds__(256)
+    join_planes(const __nv_bfloat16* __restrict__ hi, const __nv_bfloat16* __restrict__ lo,
+                float* __restrict__ y, int64_t n) {
+  pdl_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = __bfloat162float(hi[i]) + __bfloat162float(lo[i]);
+}
+
 // bf16 -> f32, element for element (the fallback for a mixed-type product).
 __global__ void __launch_bounds__(256)
     widen_bf16(const __nv_bfloat16* __restrict__ x, float* __restrict__ y, int64_t n) {
@@ -1032,7 +1043,10 @@ template <int BN, typename TO, int SPL = 0>
 int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
                 int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
                 int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn,
-                cudaStream_t st, Scratch& scratch) {
+                cudaStream_t st, Scratch& scratch, const void* a_lo_in = nullptr,
+                const void* b_lo_in = nullptr) {
+  // a_lo_in / b_lo_in: the operand arrives split already (a / b are then its
+  // bf16 hi plane)
   constexpr int ES = 2, BK = 64, E = 64;
   const int tiles_m = (int)((M + 127) / 128), tiles_n = (int)((N + BN - 1) / BN);
   const int KB_all = (int)((K + BK - 1) / BK);
@@ -1054,8 +1068,9 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   void *ah = nullptr, *al = nullptr, *bh = nullptr, *bl = nullptr;
   if (SPL) {
     if (scratch.lent) return B200_ERR_UNSUPPORTED;  // planes need memory: use the tf32 kernel
-    if (!(SPL & 1) && ((uintptr_t)a & 15)) return B200_ERR_UNSUPPORTED;
-    if (!(SPL & 2) && ((uintptr_t)b & 15)) return B200_ERR_UNSUPPORTED;
+    if ((!(SPL & 1) || a_lo_in) && ((uintptr_t)a & 15)) return B200_ERR_UNSUPPORTED;
+    if ((!(SPL & 2) || b_lo_in) && ((uintptr_t)b & 15)) return B200_ERR_UNSUPPORTED;
+    if (((uintptr_t)a_lo_in & 15) || ((uintptr_t)b_lo_in & 15)) return B200_ERR_UNSUPPORTED;
     // the planes' row pitch (2-byte elements) must still be a multiple of 16 bytes
     auto ok16 = [](int64_t s) { return s == 1 || (s * 2) % 16 == 0; };
     if (!ok16(sAm) || !ok16(sAk) || !ok16(sBk) || !ok16(sBn) ||
@@ -1067,31 +1082,32 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   if (ws) {
     if (int rc2 = scratch.get(sizeof(float) * (size_t)sp.splits * batch * M * N, st, &wsp)) return rc2;
   }
-  if (SPL & 1) {
+  const bool split_a = (SPL & 1) && !a_lo_in, split_b = (SPL & 2) && !b_lo_in;
+  if (split_a) {
     na = operand_span(batch, sAb, M, sAm, K, sAk);
     if (int r = scratch.get_owned(2 * (size_t)na, st, &ah)) return r;
     if (int r = scratch.get_owned(2 * (size_t)na, st, &al)) return r;
   }
-  if (SPL & 2) {
+  if (split_b) {
     nb = operand_span(batch, sBb, K, sBk, N, sBn);
     if (int r = scratch.get_owned(2 * (size_t)nb, st, &bh)) return r;
     if (int r = scratch.get_owned(2 * (size_t)nb, st, &bl)) return r;
   }
   if (scratch.query) return kWorkspaceQueried;
-  if (SPL) {
+  if (split_a || split_b) {
     const unsigned g = (unsigned)std::min<int64_t>((std::max(na, nb) + 1023) / 1024, 148 * 4);
     const PlaneJob ja{(const float*)a, (__nv_bfloat16*)ah, (__nv_bfloat16*)al, (int64_t)na};
     const PlaneJob jb{(const float*)b, (__nv_bfloat16*)bh, (__nv_bfloat16*)bl, (int64_t)nb};
-    if (SPL == 3) B200_LAUNCH(split_planes, dim3(g, 2), dim3(256), 0, st, ja, jb);
-    else B200_LAUNCH(split_planes, dim3(g, 1), dim3(256), 0, st, SPL == 1 ? ja : jb, ja);
-    if (SPL & 1) {
-      a = ah;
-      a_lo = al;
-    }
-    if (SPL & 2) {
-      b = bh;
-      b_lo = bl;
-    }
+    if (split_a && split_b) B200_LAUNCH(split_planes, dim3(g, 2), dim3(256), 0, st, ja, jb);
+    else B200_LAUNCH(split_planes, dim3(g, 1), dim3(256), 0, st, split_a ? ja : jb, ja);
+  }
+  if (SPL & 1) {
+    a = split_a ? ah : a;
+    a_lo = split_a ? al : a_lo_in;
+  }
+  if (SPL & 2) {
+    b = split_b ? bh : b;
+    b_lo = split_b ? bl : b_lo_in;
   }
   CUtensorMap ta, tb, tc, tal, tbl;
   int rc;
@@ -1377,6 +1393,96 @@ int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64
 
 }  // namespace
 }  // namespace b200
+
+namespace b200 {
+namespace {
+// A GEMM whose f32 operand(s) arrive as bf16 hi + lo planes (a_lo / b_lo not
+// null; a / b then point at the hi planes).  in_dtype gives the logical types.
+int gemm_planes_dispatch(const void* a, const void* a_lo, const void* b, const void* b_lo, void* c,
+                         const void* bias, int64_t batch, int64_t M, int64_t N, int64_t K,
+                         int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb, int64_t sBk,
+                         int64_t sBn, int64_t ldc, float alpha, int in_dtype, int out_dtype,
+                         int epilogue, void* stream, Scratch& scratch) {
+  const bool a32 = in_dtype == B200_DT_F32 || in_dtype == B200_GEMM_DT_A_F32_B_BF16;
+  const bool b32 = in_dtype == B200_DT_F32 || in_dtype == B200_GEMM_DT_A_BF16_B_F32;
+  B200_CHECK_ARG((!a_lo || a32) && (!b_lo || b32), "gemm: planes given for a bf16 operand");
+  B200_CHECK_ARG(a && b && c && batch >= 1 && M > 0 && N > 0 && K > 0, "gemm: bad planes call");
+  if (ldc <= 0) ldc = N;
+  auto st = (cudaStream_t)stream;
+  const bool obf = out_dtype == B200_DT_BF16;
+  auto m16 = [](int64_t s) { return ((s * 2) & 15) == 0; };
+  int a_mn = -1, b_mn = -1;
+  if (sAk == 1 && m16(sAm) && (batch == 1 || m16(sAb))) a_mn = 0;
+  else if (sAm == 1 && m16(sAk) && (batch == 1 || m16(sAb))) a_mn = 1;
+  if (sBk == 1 && m16(sBn) && (batch == 1 || m16(sBb))) b_mn = 0;
+  else if (sBn == 1 && m16(sBk) && (batch == 1 || m16(sBb))) b_mn = 1;
+  const int spl = (a32 ? 1 : 0) | (b32 ? 2 : 0);
+  if (!force_simt() && use_persistent() && f32_matmul_3x() && a_mn >= 0 && b_mn >= 0 && spl) {
+    int prc = B200_ERR_UNSUPPORTED;
+#define B200_PERSP(BN_, TO_)                                                                        \
+  prc = spl == 3 ? launch_pers<BN_, TO_, 3>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, \
+                                            sBn, ldc, alpha, epilogue, a_mn, b_mn, st, scratch,     \
+                                            a_lo, b_lo)                                             \
+      : spl == 1 ? launch_pers<BN_, TO_, 1>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, \
+                                            sBn, ldc, alpha, epilogue, a_mn, b_mn, st, scratch,     \
+                                            a_lo, b_lo)                                             \
+                 : launch_pers<BN_, TO_, 2>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, \
+                                            sBn, ldc, alpha, epilogue, a_mn, b_mn, st, scratch,     \
+                                            a_lo, b_lo)
+    if (N <= 64) { if (obf) B200_PERSP(64, __nv_bfloat16); else B200_PERSP(64, float); }
+    else if (N <= 128) { if (obf) B200_PERSP(128, __nv_bfloat16); else B200_PERSP(128, float); }
+    else { if (obf) B200_PERSP(256, __nv_bfloat16); else B200_PERSP(256, float); }
+#undef B200_PERSP
+    if (prc != B200_ERR_UNSUPPORTED) return prc;
+  }
+  // otherwise: join the given planes back into f32 (x ~= hi + lo) and take the usual path
+  void* wa = nullptr;
+  void* wb = nullptr;
+  const int64_t na = operand_span(batch, sAb, M, sAm, K, sAk), nb = operand_span(batch, sBb, K, sBk, N, sBn);
+  if (a_lo) { if (int r = scratch.get_owned(4 * (size_t)na, st, &wa)) return r; }
+  if (b_lo) { if (int r = scratch.get_owned(4 * (size_t)nb, st, &wb)) return r; }
+  if (!scratch.query) {
+    if (a_lo)
+      B200_LAUNCH(join_planes, dim3((unsigned)std::min<int64_t>((na + 255) / 256, 148 * 8)), dim3(256), 0,
+                  st, (const __nv_bfloat16*)a, (const __nv_bfloat16*)a_lo, (float*)wa, na);
+    if (b_lo)
+      B200_LAUNCH(join_planes, dim3((unsigned)std::min<int64_t>((nb + 255) / 256, 148 * 8)), dim3(256), 0,
+                  st, (const __nv_bfloat16*)b, (const __nv_bfloat16*)b_lo, (float*)wb, nb);
+  }
+  return gemm_dispatch(a_lo ? wa : a, b_lo ? wb : b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk,
+                       sBn, ldc, alpha, in_dtype, out_dtype, epilogue, stream, scratch);
+}
+}  // namespace
+}  // namespace b200
+
+extern "C" int64_t b200_gemm_planes_workspace_bytes(
+    const void* a, const void* a_lo, const void* b, const void* b_lo, void* c, const void* bias,
+    int64_t batch, int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
+    int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int in_dtype, int out_dtype,
+    int epilogue, void* stream) {
+  b200::Scratch scratch;
+  scratch.query = true;
+  const int rc = b200::gemm_planes_dispatch(a, a_lo, b, b_lo, c, bias, batch, M, N, K, sAb, sAm, sAk,
+                                            sBb, sBk, sBn, ldc, alpha, in_dtype, out_dtype, epilogue,
+                                            stream, scratch);
+  if (rc != b200::kWorkspaceQueried && rc != B200_OK) return -1;
+  return (int64_t)scratch.queried;
+}
+
+extern "C" int b200_gemm_planes_ws(const void* a, const void* a_lo, const void* b, const void* b_lo,
+                                   void* c, const void* bias, int64_t batch, int64_t M, int64_t N,
+                                   int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
+                                   int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int in_dtype,
+                                   int out_dtype, int epilogue, void* stream, void* ws,
+                                   size_t ws_bytes) {
+  b200::Scratch scratch;
+  scratch.has_arena = true;
+  scratch.arena = static_cast<uint8_t*>(ws);
+  scratch.arena_bytes = ws ? ws_bytes : 0;
+  return b200::gemm_planes_dispatch(a, a_lo, b, b_lo, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb,
+                                    sBk, sBn, ldc, alpha, in_dtype, out_dtype, epilogue, stream,
+                                    scratch);
+}
 
 extern "C" int b200_gemm(const void* a, const void* b, void* c, const void* bias, int64_t batch,
                          int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,

@@ -36,6 +36,24 @@ B200_API int b200_gemm_ws(const void* a, const void* b, void* c, const void* bia
                           int in_dtype, int out_dtype, int epilogue, void* stream, void* ws,
                           size_t ws_bytes);
 
+// b200_gemm_ws / b200_gemm_workspace_bytes for f32 operands that arrive
+// already split into bf16 planes: when a_lo (b_lo) is not null, a (b) points
+// at the operand's bf16 hi plane and a_lo (b_lo) at its lo plane, both with the
+// operand's element strides (x ~= hi + lo, each rounded to nearest), so a
+// producer such as an im2col kernel can write the planes directly.  in_dtype
+// gives the logical types (B200_DT_F32 or a mixed code).
+B200_API int64_t b200_gemm_planes_workspace_bytes(
+    const void* a, const void* a_lo, const void* b, const void* b_lo, void* c, const void* bias,
+    int64_t batch, int64_t M, int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk,
+    int64_t sBb, int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int in_dtype, int out_dtype,
+    int epilogue, void* stream);
+B200_API int b200_gemm_planes_ws(const void* a, const void* a_lo, const void* b, const void* b_lo,
+                                 void* c, const void* bias, int64_t batch, int64_t M, int64_t N,
+                                 int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb,
+                                 int64_t sBk, int64_t sBn, int64_t ldc, float alpha, int in_dtype,
+                                 int out_dtype, int epilogue, void* stream, void* ws,
+                                 size_t ws_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -248,6 +248,40 @@ def test_gemm_mixed_f32_bf16(a32, M, N, K, a_t, b_t, batch):
     assert_close(host(C), ref, 2e-3, f"mixed gemm a32={a32} {batch}x{M}x{N}x{K}")
 
 
+@pytest.mark.parametrize("M,N,K,b_t", [(512, 96, 288, False), (300, 40, 576, True), (100, 37, 12, False)])
+def test_gemm_with_given_planes(M, N, K, b_t):
+    """An f32 A handed over as bf16 hi + lo planes (what the im2col kernels of
+    f32 convolutions write) with f32 B: the persistent kernel reads them
+    directly; K = 12 (rows not 16-byte strided in bf16) joins them back into
+    f32 for the fallback path.  vs f64 on hi + lo, 2e-3 relative."""
+    import ctypes as C
+    rng = np.random.default_rng(M + K)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    b = rng.standard_normal((K, N)).astype(np.float32)
+    hi = torch.from_numpy(a).to("cuda", torch.bfloat16)
+    lo = (torch.from_numpy(a).cuda() - hi.float()).to(torch.bfloat16)
+    Bm = dev(b.T.copy() if b_t else b)
+    sBk, sBn = (1, K) if b_t else (N, 1)
+    C_ = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float32)
+    lib = kernels.lib()
+    f = lib.b200_gemm_planes_ws
+    f.restype = C.c_int
+    f.argtypes = [C.c_void_p] * 6 + [C.c_int64] * 11 + [C.c_float, C.c_int, C.c_int, C.c_int,
+                                                         C.c_void_p, C.c_void_p, C.c_size_t]
+    q = lib.b200_gemm_planes_workspace_bytes
+    q.restype = C.c_int64
+    q.argtypes = f.argtypes[:-2]
+    args = [hi.data_ptr(), lo.data_ptr(), Bm.data_ptr(), None, C_.data_ptr(), None, 1, M, N, K, 0, K, 1,
+            0, sBk, sBn, N, 1.0, kernels.DT_F32, kernels.DT_F32, 0, stream()]
+    wsb = q(*args)
+    assert wsb >= 0
+    ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device="cuda")
+    kernels._check(f(*args, ws.data_ptr(), wsb), "gemm_planes_ws")
+    torch.cuda.synchronize()
+    ref = (hi.double() + lo.double()).cpu().numpy() @ b.astype(np.float64)
+    assert_close(host(C_), ref, 2e-3, f"gemm planes {M}x{N}x{K}")
+
+
 @pytest.mark.parametrize("M,N,K", [(1024, 1024, 784), (1024, 1024, 1024), (128, 128, 32), (1, 64, 16),
                                    (200704, 32, 12)])
 def test_gemm_config_shapes_f32(M, N, K):
