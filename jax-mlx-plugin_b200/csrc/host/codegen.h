@@ -85,6 +85,9 @@ class CodeGen {
 
   static std::string prelude();
   int counter = 0;
+  // f32 values stored as a GEMM's bf16 hi / lo planes: hi slot -> lo slot
+  // (the hi slot's type is bf16); set by the planner.
+  const std::map<int, int>* plane_lo = nullptr;
 
  private:
   // An element index: row-major linear form (lin) and/or per-dimension form
@@ -145,6 +148,9 @@ class CodeGen {
   Idx vec_idx(const std::vector<int64_t>& dims, const std::string& base, int lane);
   void vec_load(const std::string& dst, int slot, const std::string& base);
   void vec_store(int slot, const std::string& base, const std::vector<std::string>& vals, DType dt);
+  // Store a loop root: plain, or as hi / lo planes when the slot has a lo plane.
+  void store_root(int slot, const std::string& base, const std::vector<std::string>& vals, DType dt);
+  void store_root1(int slot, const std::string& at, const std::string& v, DType dt);
   std::string elementwise(const Node& n, const std::vector<std::string>& a, DType in_dt);
   std::string literal(const Node& n);
   std::string emit_region(const Graph& r, const std::vector<std::string>& args,

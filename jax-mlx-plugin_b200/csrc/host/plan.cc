@@ -67,13 +67,33 @@ struct Builder {
   std::map<ValueRef, int> slot;  // materialized values
   CodeGen cg;
   std::vector<GenKernel> kernels;
+  // f32 values whose only readers are GEMMs are stored as the GEMMs' bf16
+  // hi / lo planes (hi slot -> lo slot): no split pass in front of each GEMM
+  std::map<int, int> plane_lo;
 
   Builder(Plan& pl, Graph& gr)
       : p(pl), g(gr), u(compute_uses(gr)),
         cg(gr, pl.slots, [this](ValueRef v) {
           auto it = slot.find(v);
           return it == slot.end() ? -1 : it->second;
-        }) {}
+        }) {
+    cg.plane_lo = &plane_lo;
+  }
+  void maybe_planes(int n) {
+    const Node& nd = g.nodes[n];
+    if (nd.results.size() != 1 || nd.results[0].dtype != DType::F32 || u.output_refs[n] ||
+        u.users[n].empty())
+      return;
+    for (int c : u.users[n])
+      if (g.nodes[c].op != Op::DotGeneral) return;
+    const int s = slot.at(ValueRef{n, 0});
+    Slot& sl = p.slots[s];
+    sl.type.dtype = DType::BF16;
+    sl.bytes = sl.type.bytes();
+    sl.what += ".hi";
+    TensorType lt = sl.type;
+    plane_lo[s] = new_slot(Slot::TEMP, lt, nd.name + ".lo");
+  }
 
   int new_slot(Slot::Kind k, const TensorType& t, const std::string& what, int index = -1) {
     Slot s;
@@ -310,6 +330,8 @@ struct Builder {
     const Node& nd = g.nodes[n];
     ValueRef L = nd.operands[0], R = nd.operands[1];
     int ls = slot.at(L), rs = slot.at(R);
+    int llo = plane_lo.count(ls) ? plane_lo.at(ls) : -1;  // operand stored as planes
+    int rlo = plane_lo.count(rs) ? plane_lo.at(rs) : -1;
     TensorType lt = g.type(L), rt = g.type(R);
     const TensorType& ot = nd.results[0];
     // Mixed f32 x bf16 operands (JAX's transpose rule for a bf16 dot with an
@@ -344,7 +366,9 @@ struct Builder {
       perm.insert(perm.end(), lf.begin(), lf.end());
       perm.insert(perm.end(), nd.lhs_contract.begin(), nd.lhs_contract.end());
       ls = permuted_copy(ls, perm, "dot_lhs_T");
+      if (llo >= 0) llo = permuted_copy(llo, perm, "dot_lhs_T.lo");
       lt = p.slots[ls].type;
+      if (llo >= 0) lt.dtype = DType::F32;
       std::vector<int64_t> b(nd.lhs_batch.size()), f(lf.size()), c(nd.lhs_contract.size());
       int64_t k = 0;
       for (auto& x : b) x = k++;
@@ -357,7 +381,9 @@ struct Builder {
       perm.insert(perm.end(), rf.begin(), rf.end());
       perm.insert(perm.end(), nd.rhs_contract.begin(), nd.rhs_contract.end());
       rs = permuted_copy(rs, perm, "dot_rhs_T");
+      if (rlo >= 0) rlo = permuted_copy(rlo, perm, "dot_rhs_T.lo");
       rt = p.slots[rs].type;
+      if (rlo >= 0) rt.dtype = DType::F32;
       std::vector<int64_t> b(nd.rhs_batch.size()), f(rf.size()), c(nd.rhs_contract.size());
       int64_t k = 0;
       for (auto& x : b) x = k++;
@@ -369,6 +395,15 @@ struct Builder {
     int cs = temp_for(ValueRef{n, 0});
     emit_gemm(ls, rs, cs, ab.size, am.size, bn.size, ak.size, ab, am, ak, bb, bk, bn, gemm_dt,
               ot.dtype);
+    if (llo >= 0 || rlo >= 0) {  // operands given as planes
+      Step& gs = p.steps.back();
+      Arg alo, blo;
+      alo.slot = llo;
+      blo.slot = rlo;
+      gs.args = {alo, blo};
+      for (int x : {llo, rlo})
+        if (x >= 0) gs.in.push_back(x);
+    }
   }
 
   void lower_conv(int n) {
@@ -931,6 +966,7 @@ struct Builder {
             (g.nodes[pending[0]].results[0].dims != nd.results[0].dims || pending.size() >= 24))
           flush_loops();
         temp_for(ValueRef{n, 0});
+        maybe_planes(n);
         pending.push_back(n);
         continue;
       }
