@@ -137,6 +137,54 @@ def test_identical_kernels_compile_once_and_cache_on_disk(tmp_path, monkeypatch)
     assert not list(tmp_path.glob("*.tmp*"))
 
 
+def _plan_tables(text):
+    plan = pjrt.inspect(text, 1)
+    head, steps = plan.split("steps:")
+    slots = {}
+    for m in re.finditer(r"^\s+s(\d+) (\w+)\[-?\d+\] (\S+) (.*)$", head, flags=re.M):
+        slots[int(m.group(1))] = (m.group(2), m.group(3), m.group(4))
+    rows = []
+    for line in steps.strip().splitlines():
+        ins = line.split(" in=")[1].split(" out=")[0].rstrip(",")
+        rows.append((line.split()[0], [int(s[1:]) for s in ins.split(",") if s]))
+    return slots, rows
+
+
+def test_gemm_operands_arrive_as_planes():
+    """An f32 value read only by GEMMs is stored by the kernel that computes it
+    as two bf16 planes (hi and lo = the rounding remainder), which the GEMM
+    reads as its split operand: attention's dS in the transformer step, and
+    every im2col patch matrix of the CNN step (K a multiple of 8).  No f32
+    copy of such a value is stored."""
+    slots, rows = _plan_tables(programs.transformer_step(batch=2, seq=32, layers=1, d=64, heads=2,
+                                                         ffn=128, vocab=96))
+    planed = [ins for name, ins in rows if name == "gemm" and len(ins) == 3]
+    assert len(planed) >= 2
+    for ins in planed:
+        lo = slots[ins[2]]
+        assert lo[1].endswith("xbf16>") and lo[2].endswith(".lo")
+        hi = [slots[s] for s in ins[:2] if slots[s][2] == lo[2][:-3] + ".hi"]
+        assert len(hi) == 1 and hi[0][1] == lo[1]
+        # the f32 value itself is not a slot of the plan
+        assert not any(s[2] == lo[2][:-3] for s in slots.values())
+
+    slots, rows = _plan_tables(programs.cnn_step())
+    im2col_out = {s: slots[s][2] for s, v in slots.items() if v[2].startswith("im2col")}
+    # the first conv's patches have K = 3*3*1 = 9 columns: stored in f32
+    f32 = [s for s, n in im2col_out.items() if n == "im2col"]
+    assert [slots[s][1] for s in f32] == ["tensor<200704x9xf32>"]
+    for s in f32:
+        del im2col_out[s]
+    assert len(im2col_out) == 8 and all(n in ("im2col_hi", "im2col_lo") for n in im2col_out.values())
+    assert all(slots[s][1].endswith("xbf16>") for s in im2col_out)
+    gemms = [ins for name, ins in rows if name == "gemm"]
+    for s, n in im2col_out.items():
+        readers = [ins for ins in gemms if s in ins]
+        assert len(readers) == 1 and len(readers[0]) == 3
+        # hi is the A operand, lo the trailing plane input
+        assert readers[0].index(s) == (0 if n == "im2col_hi" else 2)
+
+
 def test_non_causal_and_bnth_attention_also_match():
     g = pjrt.inspect(programs.sdpa(2, 256, 4, 64, causal=False), 0)
     assert "fused_sdpa" in g and "causal=0" in g
