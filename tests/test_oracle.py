@@ -99,6 +99,29 @@ def test_bf16_rounding_is_round_to_nearest_even():
     np.testing.assert_array_equal(hlo_interp.bf16_bits_to_f32(bits), r)
 
 
+def test_bf16_chain_rounding_modes():
+    """x * y + z in bf16 with x = y = 1 + 2^-7, z = -(1 + 2^-6).  Rounding each
+    op (the default) drops the 2^-14 term of the product, so the sum is 0;
+    excess precision keeps the chain unrounded until the bf16 output, which
+    holds 2^-14 exactly.  A convert to bf16 inside the chain rounds in both
+    modes."""
+    from jax_b200.hlo import Builder
+    b = Builder("bf16_chain")
+    x, y, z = (b.param((4,), "bf16") for _ in range(3))
+    prod = x * y
+    held = b.convert(b.convert(prod, "f32"), "bf16")
+    text = b.module([prod + z, held + z])
+    one = np.float32(1 + 2.0 ** -7)
+    args = [np.full(4, one), np.full(4, one), np.full(4, np.float32(-(1 + 2.0 ** -6)))]
+    per_op = hlo_interp.run(text, [args])[0]
+    excess = hlo_interp.run(text, [args], excess_bf16=True)[0]
+    np.testing.assert_array_equal(per_op[0], 0.0)
+    np.testing.assert_array_equal(excess[0], 2.0 ** -14)
+    # the explicit f32 -> bf16 convert rounds the product in both modes
+    np.testing.assert_array_equal(per_op[1], 0.0)
+    np.testing.assert_array_equal(excess[1], 0.0)
+
+
 def test_sdpa_bwd_restatement_matches_autodiff():
     """restate.sdpa_bwd_ref (reference sdpa.py:65-87) equals reverse-mode autodiff
     of the attention forward, both evaluated by the interpreter in f64."""
