@@ -185,6 +185,23 @@ def test_gemm_operands_arrive_as_planes():
         assert readers[0].index(s) == (0 if n == "im2col_hi" else 2)
 
 
+def test_attention_operands_are_written_in_gemm_order():
+    """Attention over [B, T, N, H] contracts with batch dims (B, N) that are not
+    one strided group.  The q / k / v and dS values are written in the GEMMs'
+    batch order by the kernels that compute them, so the transformer step
+    has no standalone transpose (permute) kernel and every GEMM reads its
+    operands as they are stored."""
+    layers = 2
+    slots, rows = _plan_tables(programs.transformer_step(batch=2, seq=32, layers=layers, d=64,
+                                                         heads=2, ffn=128, vocab=96))
+    kinds = {name.split("_", 1)[-1] for name, _ in rows}
+    assert "permute" not in kinds and "gemm" in kinds
+    # the batched attention GEMMs ([B*N] x [T, T] and [T, H] products)
+    batched = [ins for name, ins in rows if name == "gemm"
+               and slots[ins[0]][1].startswith("tensor<2x2x32x")]
+    assert len(batched) == layers * 6  # QK^T and PV forward; 4 in the backward
+
+
 def test_non_causal_and_bnth_attention_also_match():
     g = pjrt.inspect(programs.sdpa(2, 256, 4, 64, causal=False), 0)
     assert "fused_sdpa" in g and "causal=0" in g
