@@ -405,6 +405,42 @@ class Executable:
             pass
 
 
+def kv_callbacks(store):
+    """The PJRT key-value callbacks over `store` (``set(key: str, value: bytes)``,
+    ``get(key: str) -> bytes``).  In a multi-process job the plugin's rank 0
+    publishes the NCCL unique id through the put callback and every other rank
+    reads it back through the get callback (values are raw bytes, zeros
+    included).  A value handed out by get stays alive until the plugin calls
+    its deleter.  Returns (get_cb, put_cb, keep): keep holds every ctypes
+    object that must outlive the client."""
+    values = {}
+
+    def deleter(p):
+        values.pop(p, None)
+
+    del_cb = VALUE_DELETER(deleter)
+
+    def kv_get(args):
+        a = args.contents
+        key = C.string_at(a.key, a.key_size).decode()
+        val = store.get(key)
+        buf = C.create_string_buffer(val, len(val))
+        addr = C.addressof(buf)
+        values[addr] = buf
+        a.value, a.value_size = addr, len(val)
+        a.value_deleter_callback = C.cast(del_cb, C.c_void_p)
+        return None
+
+    def kv_put(args):
+        a = args.contents
+        key = C.string_at(a.key, a.key_size).decode()
+        store.set(key, C.string_at(a.value, a.value_size))
+        return None
+
+    get_cb, put_cb = KV_GET_CB(kv_get), KV_PUT_CB(kv_put)
+    return get_cb, put_cb, [get_cb, put_cb, del_cb, values]
+
+
 class Client:
     """A PJRT client of the B200 plugin.
 
@@ -433,33 +469,8 @@ class Client:
         arr = (NamedValue * max(len(opts), 1))(*opts)
         get_cb = put_cb = None
         if kv is not None:
-            store = kv
-            values = {}
-
-            def deleter(p):
-                values.pop(p, None)
-
-            del_cb = VALUE_DELETER(deleter)
-
-            def kv_get(args):
-                a = args.contents
-                key = C.string_at(a.key, a.key_size).decode()
-                val = store.get(key)
-                buf = C.create_string_buffer(val, len(val))
-                addr = C.addressof(buf)
-                values[addr] = buf
-                a.value, a.value_size = addr, len(val)
-                a.value_deleter_callback = C.cast(del_cb, C.c_void_p)
-                return None
-
-            def kv_put(args):
-                a = args.contents
-                key = C.string_at(a.key, a.key_size).decode()
-                store.set(key, C.string_at(a.value, a.value_size))
-                return None
-
-            get_cb, put_cb = KV_GET_CB(kv_get), KV_PUT_CB(kv_put)
-            self._keep += [get_cb, put_cb, del_cb]
+            get_cb, put_cb, keep = kv_callbacks(kv)
+            self._keep += keep
         a = api().call("Client_Create", create_options=C.cast(arr, C.POINTER(NamedValue)),
                        num_options=len(opts),
                        kv_get_callback=C.cast(get_cb, C.c_void_p) if get_cb else None,

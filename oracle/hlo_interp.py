@@ -14,7 +14,8 @@ import this module.  It has its own small parser, independent of the plugin's
 C++ parser, so a parsing bug does not cancel out in the comparison.
 
 Replicated programs (``all_reduce``) are evaluated for all replicas in lockstep:
-``run(text, [args_replica0, args_replica1, ...])``.
+``run(text, [args_replica0, args_replica1, ...])``; or one replica per process,
+``run(text, [args], process_sum=f)`` with ``f`` summing over the processes.
 """
 from __future__ import annotations
 
@@ -133,12 +134,18 @@ class Interp:
     converts, non-elementwise ops such as reduce / dot_general and the
     program's outputs round to bf16) -- XLA's default excess-precision
     treatment of bf16 chains, which a fusing compiler follows.  Default: every
-    bf16 op's result is rounded."""
+    bf16 op's result is rounded.
 
-    def __init__(self, text: str, excess_bf16: bool = False):
+    process_sum: for a replicated program run with one replica per process,
+    a callable that sums an array over the processes (e.g. a torch.distributed
+    all_reduce); ``all_reduce`` results are then that sum of this process's
+    replicas."""
+
+    def __init__(self, text: str, excess_bf16: bool = False, process_sum=None):
         self.text = re.sub(r"\s*loc\([^)]*\)", "", text)
         self.funcs = self._split_funcs(self.text)
         self.excess_bf16 = excess_bf16
+        self.process_sum = process_sum
 
     # ------------------------------------------------------------ parsing --
     @staticmethod
@@ -222,6 +229,8 @@ class Interp:
             out.append(self._op(op, rhs, a, out_t, tys, env, r, args))
         if op == "all_reduce":
             s = sum(o for o in out)
+            if self.process_sum is not None:
+                s = self.process_sum(np.asarray(s, np.float64))
             out = [_cast(s, out_t.dt) for _ in range(R)]
         env[res] = out
 
@@ -489,6 +498,6 @@ def dot_general(x, y, lb, rb, lc, rc):
     return np.einsum("".join(xs) + "," + "".join(ys) + "->" + "".join(out), x, y)
 
 
-def run(text: str, replica_args, func: str = "main", excess_bf16: bool = False):
+def run(text: str, replica_args, func: str = "main", excess_bf16: bool = False, process_sum=None):
     """Evaluate StableHLO `text`.  replica_args: list (one per replica) of arg lists."""
-    return Interp(text, excess_bf16).run(replica_args, func)
+    return Interp(text, excess_bf16, process_sum).run(replica_args, func)
