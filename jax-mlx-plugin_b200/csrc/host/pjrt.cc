@@ -276,6 +276,11 @@ std::string kv_get(PJRT_Client* c, const std::string& key) {
     delete e;
     throw PjrtErr(4, "KV get '" + key + "' failed: " + m);
   }
+  // A callback that could not produce the value (a Python one whose store
+  // raised or timed out returns no error object) leaves it unset.
+  if (!a.value)
+    throw PjrtErr(4, "KV get '" + key + "' returned no value (the key-value store's get failed "
+                     "or timed out; did rank 0 reach its first collective?)");
   std::string v(a.value, a.value_size);
   if (a.value_deleter_callback) a.value_deleter_callback(a.value);
   return v;

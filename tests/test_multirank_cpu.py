@@ -146,6 +146,29 @@ def test_nccl_id_crosses_processes_through_kv_callbacks(tmp_path):
     assert got[0] == got[1] == _uid() and len(got[1]) == 128
 
 
+@pytest.mark.filterwarnings("ignore::pytest.PytestUnraisableExceptionWarning")
+def test_failed_store_get_leaves_value_unset():
+    """A store whose get raises (rank 0 gone, store timeout) cannot hand the
+    plugin an error object from Python; the callback then leaves the value
+    unset, which the plugin reports as a failed KV get naming the key."""
+    from jax_b200 import pjrt
+
+    class Broken:
+        def set(self, k, v):
+            pass
+
+        def get(self, k):
+            raise TimeoutError(k)
+
+    get_cb, _, _ = pjrt.kv_callbacks(Broken())
+    a = pjrt.KVGetArgs()
+    a.struct_size = C.sizeof(a)
+    key = UID_KEY.encode()
+    a.key, a.key_size = key, len(key)
+    get_cb(C.pointer(a))  # ctypes reports the exception and returns null
+    assert not a.value and a.value_size == 0
+
+
 def test_data_parallel_step_across_processes_equals_full_batch(tmp_path):
     from jax_b200 import programs
     from oracle import hlo_interp
