@@ -272,6 +272,9 @@ void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[
     const char* e = getenv("B200_PDL");
     return !(e && e[0] == '0');
   }();
+  // A kernel over an empty index space (a reduction with no outputs) has
+  // nothing to do; the driver would reject its zero-sized grid.
+  if (grid[0] <= 0 || grid[1] <= 0 || grid[2] <= 0) return;
   CUlaunchAttribute attr[1];
   attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
   attr[0].value.programmaticStreamSerializationAllowed = pdl ? 1 : 0;

@@ -1294,7 +1294,17 @@ int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64
   if (ldc <= 0) ldc = N;
   if (M == 0 || N == 0) return B200_OK;
   auto st = (cudaStream_t)stream;
-  if (K == 0) return set_error(B200_ERR_UNSUPPORTED, "gemm: K == 0 is not supported");
+  if (K == 0) {
+    // An empty sum: C = 0 (relu(0) = 0).  C is batch*M rows of N elements,
+    // ldc apart (the batch stride is M*ldc).  With a bias the result would be
+    // the bias broadcast, which no caller asks for with K == 0.
+    if (epilogue == 1 || epilogue == 2)
+      return set_error(B200_ERR_UNSUPPORTED, "gemm: K == 0 with a bias epilogue is not supported");
+    if (scratch.query) return B200_OK;
+    const size_t es = out_dtype == B200_DT_BF16 ? 2 : 4;
+    B200_CUDA_TRY(cudaMemset2DAsync(c, (size_t)ldc * es, 0, (size_t)N * es, (size_t)(batch * M), st));
+    return B200_OK;
+  }
   if (in_dtype == B200_GEMM_DT_A_F32_B_BF16 || in_dtype == B200_GEMM_DT_A_BF16_B_F32) {
     const bool a32 = in_dtype == B200_GEMM_DT_A_F32_B_BF16;
     const bool obf = out_dtype == B200_DT_BF16;

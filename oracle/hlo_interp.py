@@ -301,6 +301,8 @@ class Interp:
             f = {"add": np.sum, "maximum": np.max, "minimum": np.min, "multiply": np.prod}[kind]
             init = a[1]
             g = {"add": np.add, "maximum": np.maximum, "minimum": np.minimum, "multiply": np.multiply}[kind]
+            if np.size(a[0]) == 0:  # nothing to fold: every output is the init value
+                return c(np.broadcast_to(init, t.shape).copy())
             return c(g(f(a[0], axis=dims), init))
         if op == "dot_general":
             bd = re.search(r"batching_dims = \[([^\]]*)\] x \[([^\]]*)\]", rhs)

@@ -99,6 +99,19 @@ def test_bf16_rounding_is_round_to_nearest_even():
     np.testing.assert_array_equal(hlo_interp.bf16_bits_to_f32(bits), r)
 
 
+def test_reductions_over_empty_extents_give_init():
+    """StableHLO reduce folds the operand into the init value: over an empty
+    dimension each output is the init value itself (0 for sum, -inf for a
+    max with JAX's init); with no outputs the result is empty."""
+    from jax_b200.hlo import Builder
+    b = Builder("empty_reduce")
+    x, y = b.param((3, 0)), b.param((0, 5))
+    text = b.module([b.sum(x, [1]), b.max(x, [1]), b.max(y, [1])])
+    out = hlo_interp.run(text, [[np.zeros((3, 0), np.float32), np.zeros((0, 5), np.float32)]])[0]
+    assert out[0].tolist() == [0.0] * 3 and out[1].tolist() == [-np.inf] * 3
+    assert np.shape(out[2]) == (0,)
+
+
 def test_bf16_chain_rounding_modes():
     """x * y + z in bf16 with x = y = 1 + 2^-7, z = -(1 + 2^-6).  Rounding each
     op (the default) drops the 2^-14 term of the product, so the sum is 0;

@@ -57,6 +57,30 @@ def test_buffer_round_trip(client):
         assert not pjrt.api().call("Buffer_IsOnCpu", buffer=b.handle).is_on_cpu
 
 
+def test_empty_extents_match_oracle(client):
+    """Zero-size dimensions, as jax.numpy produces them: elementwise work over
+    no elements, reductions over an empty dimension (the init value: 0 for
+    sum, -inf for max) or with no outputs, and products with an empty
+    contracting dimension (all zeros) or no rows."""
+    from jax_b200.hlo import Builder
+    b = Builder("empty_extents")
+    x, y = b.param((4, 0)), b.param((0, 8))
+    w, u, v = b.param((0, 3)), b.param((0, 5)), b.param((5, 3))
+    text = b.module([b.sum(x, [1]), b.max(x, [1]), b.sum(y, [1]), b.exp(y) + y,
+                     b.dot_general(x, w, ([1], [0]), ([], [])),
+                     b.dot_general(u, v, ([1], [0]), ([], []))])
+    rng = np.random.default_rng(12)
+    inputs = [np.zeros((4, 0), np.float32), np.zeros((0, 8), np.float32), np.zeros((0, 3), np.float32),
+              np.zeros((0, 5), np.float32), rng.standard_normal((5, 3)).astype(np.float32)]
+    ref = hlo_interp.run(text, [inputs])[0]
+    for _ in range(2):  # the second execute reuses cached device blocks
+        got = run(client, text, inputs)
+        assert [g.shape for g in got] == [np.shape(r) for r in ref]
+        for g, r in zip(got, ref):
+            np.testing.assert_array_equal(g, np.asarray(r, np.float32))
+    assert got[1].tolist() == [-np.inf] * 4 and got[4].tolist() == [[0.0] * 3] * 4
+
+
 @pytest.mark.parametrize("case", cases(), ids=lambda c: c[0])
 def test_golden_cases_through_plugin(client, case):
     name, prog, inputs, expected = case
