@@ -92,7 +92,8 @@ B200_API int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v, 
  * sAm/sAk must be 1; same for B with (b,k,n).  C is dense row-major [batch,M,N]
  * unless ldc (elements between rows) says otherwise.  in_dtype F32 (TF32 MMA) or
  * BF16; out_dtype F32 or BF16; accumulation in f32.  epilogue: 0 none, 1 bias,
- * 2 bias+relu, 3 relu.
+ * 2 bias+relu, 3 relu.  M == 0 or N == 0: nothing is written; K == 0: C is
+ * set to zero (epilogue 0 or 3; a bias epilogue with K == 0 is rejected).
  * Replaces reference src/jax_mlx_pjrt.cpp:4577-4666 (dot_general ->
  * transpose/reshape -> mlx::core::matmul). */
 B200_API int b200_gemm(const void* a, const void* b, void* c, const void* bias, int64_t batch,
