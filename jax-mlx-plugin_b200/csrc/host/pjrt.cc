@@ -390,9 +390,15 @@ void replicas_from_options(const std::string& opts, int64_t* reps, int64_t* part
   });
 }
 
+// StableHLO text as given, or a portable artifact (MLIR bytecode, magic
+// "ML\xefR") converted to text.
+std::string program_text(const std::string& code) {
+  if (code.size() >= 4 && code.compare(0, 4, "ML\xefR") == 0) return bytecode_to_text(code);
+  return code;
+}
+
 std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std::string& opts) {
-  std::string text = code;
-  if (code.size() >= 4 && code.compare(0, 4, "ML\xefR") == 0) text = bytecode_to_text(code);
+  const std::string text = program_text(code);
   Module m = parse_module(text);
   int64_t reps = 1, parts = 1;
   replicas_from_options(opts, &reps, &parts);
@@ -1717,7 +1723,7 @@ __attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, s
   std::string res;
   int code = 0;
   try {
-    Module m = parse_module(std::string(mlir, len));
+    Module m = parse_module(program_text(std::string(mlir, len)));
     Plan p = build_plan(m);
     if (what == 0) res = p.graph_dump;
     else if (what == 1) res = dump_plan(p);

@@ -554,14 +554,16 @@ class Client:
             self.handle = None
 
 
-def inspect(mlir_text: str, what: int = 1) -> str:
-    """Run the compile pipeline without a device (see include/b200_pjrt_inspect.h)."""
+def inspect(mlir_text, what: int = 1) -> str:
+    """Run the compile pipeline without a device (see include/b200_pjrt_inspect.h).
+    mlir_text: StableHLO text (str) or the program's bytes (text, or a portable
+    artifact that needs jaxlib's MLIR C API in the process)."""
     lib = api().lib
     lib.b200_pjrt_inspect.argtypes = [C.c_char_p, C.c_size_t, C.c_int, C.POINTER(C.c_void_p)]
     lib.b200_pjrt_inspect.restype = C.c_int
     lib.b200_pjrt_free.argtypes = [C.c_void_p]
     out = C.c_void_p()
-    b = mlir_text.encode()
+    b = mlir_text if isinstance(mlir_text, bytes) else mlir_text.encode()
     rc = lib.b200_pjrt_inspect(b, len(b), what, C.byref(out))
     s = C.string_at(out.value).decode()
     lib.b200_pjrt_free(out)

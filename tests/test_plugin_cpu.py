@@ -233,6 +233,17 @@ def test_parse_errors_are_invalid_argument():
     assert e.value.code == 3
 
 
+def test_portable_artifact_without_mlir_c_api_is_unimplemented():
+    """A program given as MLIR bytecode (what jax hands a plugin) is converted
+    through the StableHLO C API that jaxlib loads; in a process without it the
+    compile fails with UNIMPLEMENTED and says to pass text instead."""
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.inspect(b"ML\xefR\x00\x01\x02stablehlo", 0)
+    assert e.value.code == 12 and "StableHLO C API" in str(e.value)
+    # text still goes straight to the parser
+    assert "fused_layer_norm" in pjrt.inspect(programs.layer_norm().encode(), 0)
+
+
 def test_unsupported_op_is_unimplemented():
     text = ('module @m { func.func public @main(%arg0: tensor<8xf32>) -> tensor<8xf32> {\n'
             '  %0 = "stablehlo.sort"(%arg0) <{dimension = 0 : i64}> ({\n'
