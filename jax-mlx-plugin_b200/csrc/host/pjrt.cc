@@ -398,6 +398,7 @@ std::string program_text(const std::string& code) {
 }
 
 std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std::string& opts) {
+  fault_point("compile");
   const std::string text = program_text(code);
   Module m = parse_module(text);
   int64_t reps = 1, parts = 1;
@@ -452,6 +453,7 @@ NcclComms& comms_for(PJRT_Client* c, Exe& e) {
   for (int64_t r = 0; r < e.num_replicas; ++r) ids.push_back((int)r);
   auto it = c->comms.find(ids);
   if (it != c->comms.end()) return *it->second;
+  fault_point("nccl_init");
   std::unique_ptr<NcclComms> comm;
   if (c->num_nodes == 1) {
     std::vector<Device*> devs;
@@ -621,6 +623,7 @@ void run_graphs(Exe& e, GraphState& gs, PJRT_Device* pd, const std::vector<void*
 }
 
 void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
+  fault_point("execute");
   Exe& e = *le->exe;
   PJRT_Client* c = e.client;
   const Plan& p = e.plan;
@@ -1723,6 +1726,7 @@ __attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, s
   std::string res;
   int code = 0;
   try {
+    fault_point("compile");
     Module m = parse_module(program_text(std::string(mlir, len)));
     Plan p = build_plan(m);
     if (what == 0) res = p.graph_dump;

@@ -7,6 +7,7 @@
 #include <nccl.h>
 #include <nvrtc.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstdio>
 #include <unistd.h>
@@ -22,6 +23,30 @@ void cuda_fail(cudaError_t e, const char* what) {
                 std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// ------------------------------------------------------- fault injection --
+void fault_point(const char* where) {
+  static const std::vector<std::string> points = [] {
+    std::vector<std::string> v;
+    const char* e = getenv("B200_FAULT");
+    std::string cur;
+    for (const char* q = e ? e : ""; ; ++q) {
+      if (*q == ',' || *q == '\0') {
+        if (!cur.empty()) v.push_back(cur);
+        cur.clear();
+        if (*q == '\0') break;
+      } else if (*q != ' ') {
+        cur += *q;
+      }
+    }
+    return v;
+  }();
+  if (points.empty()) return;
+  const std::string w(where);
+  if (std::find(points.begin(), points.end(), w) == points.end()) return;
+  const int code = w == "alloc" ? 8 : w == "nccl_init" ? 14 : 13;
+  throw PjrtErr(code, "injected fault at " + w + " (B200_FAULT)");
+}
+
 // ------------------------------------------------------------ allocator --
 size_t Allocator::round(size_t b) {
   if (b == 0) b = 1;
@@ -29,6 +54,7 @@ size_t Allocator::round(size_t b) {
   return (b + (2u << 20) - 1) & ~size_t((2u << 20) - 1);
 }
 void* Allocator::alloc(size_t bytes) {
+  fault_point("alloc");
   const size_t sz = round(bytes);
   std::lock_guard<std::mutex> lk(mu_);
   auto it = cache_.find(sz);

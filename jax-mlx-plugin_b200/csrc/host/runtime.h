@@ -91,6 +91,14 @@ std::unique_ptr<LoadedModule> load_module(Device& d, const std::vector<std::stri
                                           const std::vector<std::vector<std::string>>& names,
                                           const std::map<std::string, std::string>& alias);
 
+// Host-side fault injection.  B200_FAULT (read once per process) lists
+// failure points, comma-separated: alloc, compile, execute, nccl_init.  At a
+// listed point the plugin throws the error that the real failure there
+// raises (alloc: RESOURCE_EXHAUSTED, compile and execute: INTERNAL,
+// nccl_init: UNAVAILABLE), so a caller's error handling can be tested with no
+// GPU failing.  Unset: nothing happens.
+void fault_point(const char* where);
+
 // Launch a generated kernel.
 void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[3], int smem,
             std::vector<void*>& args);

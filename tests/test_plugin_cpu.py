@@ -233,6 +233,37 @@ def test_parse_errors_are_invalid_argument():
     assert e.value.code == 3
 
 
+_FAULT_PROBE = """
+import sys
+sys.path[:0] = [{root!r}, {pkg!r}]
+from jax_b200 import pjrt, programs
+try:
+    pjrt.inspect(programs.layer_norm(), 0)
+    print("ok")
+except pjrt.PjrtError as e:
+    print(e.code, e)
+"""
+
+
+@pytest.mark.parametrize("spec, expect", [
+    ("compile", "13 INTERNAL: injected fault at compile (B200_FAULT)"),
+    ("alloc, execute,nccl_init", "ok"),
+    ("", "ok"),
+])
+def test_fault_injection_is_host_side_and_named(spec, expect):
+    """B200_FAULT lists host-side failure points; the compile point fails the
+    compile pipeline with the error a real compile failure raises, and points
+    of later stages leave compilation alone.  (The process reads the variable
+    once, so each case runs in a fresh interpreter.)"""
+    import subprocess
+    import sys
+    env = dict(os.environ, B200_FAULT=spec)
+    code = _FAULT_PROBE.format(root=ROOT, pkg=os.path.join(ROOT, "jax-mlx-plugin_b200"))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-1500:]
+    assert r.stdout.strip() == expect
+
+
 def test_portable_artifact_without_mlir_c_api_is_unimplemented():
     """A program given as MLIR bytecode (what jax hands a plugin) is converted
     through the StableHLO C API that jaxlib loads; in a process without it the
