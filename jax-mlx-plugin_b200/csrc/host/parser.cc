@@ -2,6 +2,7 @@
 // line-by-line regex matcher like reference src/mlx_mlir_parser.h:36-2410).
 // Accepts the pretty printing that jax.jit(...).lower().as_text() and
 // mlirOperationPrint produce, and the generic "stablehlo.op"(...) form.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <functional>
@@ -1357,10 +1358,194 @@ class Parser {
 
 }  // namespace
 
+// Structural checks after parsing: the attribute lists and dimension numbers
+// that the planner and the code generator index by rank must have the
+// operand's rank and name dimensions that exist.  The parser fills defaults
+// for absent optional attributes, so every valid program passes; a program
+// whose attribute text was malformed is rejected here instead of being
+// indexed out of range later.
+namespace {
+void verify_graph(const Graph& g) {
+  auto fail = [&](const Node& n, const std::string& what) {
+    throw PjrtErr(3, std::string("invalid ") + op_name(n.op) + (n.name.empty() ? "" : " " + n.name) +
+                         ": " + what);
+  };
+  auto in_range = [](const std::vector<int64_t>& v, int64_t r) {
+    for (int64_t d : v)
+      if (d < 0 || d >= r) return false;
+    return true;
+  };
+  auto distinct = [](std::vector<int64_t> v) {
+    std::sort(v.begin(), v.end());
+    return std::adjacent_find(v.begin(), v.end()) == v.end();
+  };
+  for (size_t i = 0; i < g.nodes.size(); ++i) {
+    const Node& n = g.nodes[i];
+    for (const ValueRef& o : n.operands)
+      if (o.node < 0 || (size_t)o.node >= i || o.idx < 0 ||
+          (size_t)o.idx >= g.nodes[o.node].results.size())
+        fail(n, "operand refers to no earlier value");
+    for (const TensorType& t : n.results)
+      for (int64_t d : t.dims)
+        if (d < 0) fail(n, "negative dimension");
+    for (const auto& r : n.regions) verify_graph(*r);
+    if (n.results.empty() || n.op == Op::Return || n.op == Op::Tuple || n.op == Op::Call ||
+        n.op == Op::CustomCall || n.op == Op::OptimizationBarrier || n.op == Op::GetTupleElement)
+      continue;
+    const TensorType& rt = n.results[0];
+    const int R = rt.rank();
+    const int I = n.operands.empty() ? 0 : g.type(n.operands[0]).rank();
+    const std::vector<int64_t>* idims = n.operands.empty() ? nullptr : &g.type(n.operands[0]).dims;
+    // a body computes one value per reduced input from twice as many arguments
+    auto body = [&](size_t r, size_t outs, size_t params) {
+      if (n.regions.size() <= r) fail(n, "needs a body");
+      const Graph& b = *n.regions[r];
+      if (b.outputs.size() != outs) fail(n, "body returns " + std::to_string(b.outputs.size()) +
+                                                " values, needs " + std::to_string(outs));
+      for (const Node& x : b.nodes)
+        if (x.op == Op::Parameter && (x.param_index < 0 || (size_t)x.param_index >= params))
+          fail(n, "body parameter out of range");
+    };
+    switch (n.op) {
+      case Op::Reduce:
+      case Op::ReduceWindow:
+        if (n.operands.empty() || n.operands.size() % 2 != 0) fail(n, "needs inputs and as many init values");
+        body(0, n.operands.size() / 2, n.operands.size());
+        break;
+      case Op::Scatter:
+        if (n.operands.size() < 3 || n.operands.size() % 2 != 1) fail(n, "needs inputs, indices and updates");
+        body(0, (n.operands.size() - 1) / 2, n.operands.size() - 1);
+        break;
+      case Op::SelectAndScatter:
+        if (n.operands.size() != 3) fail(n, "needs operand, source and init value");
+        body(0, 1, 2);
+        body(1, 1, 2);
+        break;
+      case Op::AllReduce:  // one binary computation, applied to every operand
+        body(0, 1, 2);
+        break;
+      default:
+        break;
+    }
+    if (n.op >= Op::Neg && n.op <= Op::Convert) {
+      const size_t arity = n.op <= Op::Real ? 1
+                           : n.op <= Op::ShiftRightLogical || n.op == Op::Compare ? 2
+                           : n.op == Op::Select || n.op == Op::Clamp ? 3 : 1;
+      if (n.operands.size() != arity) fail(n, "needs " + std::to_string(arity) + " operands");
+      for (size_t k = 0; k < n.operands.size(); ++k) {
+        const TensorType& t = g.type(n.operands[k]);
+        const bool scalar_ok = (n.op == Op::Select && k == 0) || (n.op == Op::Clamp && k != 1);
+        if (t.dims != rt.dims && !(scalar_ok && t.rank() == 0))
+          fail(n, "operand shape differs from the result shape");
+      }
+      continue;
+    }
+    switch (n.op) {
+      case Op::BroadcastInDim:
+        if ((int)n.dims.size() != I || !in_range(n.dims, R)) fail(n, "bad broadcast_dimensions");
+        for (int k = 0; k < I; ++k)
+          if ((*idims)[k] != 1 && (*idims)[k] != rt.dims[n.dims[k]]) fail(n, "operand dimension mismatch");
+        break;
+      case Op::Transpose:
+        if ((int)n.dims.size() != I || I != R || !in_range(n.dims, I) || !distinct(n.dims))
+          fail(n, "permutation is not one of the operand's dimensions");
+        for (int k = 0; k < R; ++k)
+          if (rt.dims[k] != (*idims)[n.dims[k]]) fail(n, "result shape is not the permuted operand shape");
+        break;
+      case Op::Reshape:
+        if (g.type(n.operands.at(0)).numel() != rt.numel()) fail(n, "element count changes");
+        break;
+      case Op::Slice:
+        if ((int)n.start.size() != I || (int)n.limit.size() != I || (int)n.strides.size() != I)
+          fail(n, "start / limit / strides do not match the operand rank");
+        for (int k = 0; k < I; ++k)
+          if (n.start[k] < 0 || n.start[k] > n.limit[k] || n.limit[k] > (*idims)[k] || n.strides[k] < 1)
+            fail(n, "slice bounds out of range");
+        break;
+      case Op::DynamicSlice:
+        if ((int)n.limit.size() != I || (int)n.operands.size() != 1 + I) fail(n, "slice sizes / start indices do not match the operand rank");
+        for (int k = 0; k < I; ++k)
+          if (n.limit[k] < 0 || n.limit[k] > (*idims)[k]) fail(n, "slice size out of range");
+        break;
+      case Op::DynamicUpdateSlice:
+        if ((int)n.operands.size() != 2 + I || g.type(n.operands.at(1)).rank() != I)
+          fail(n, "update / start indices do not match the operand rank");
+        break;
+      case Op::Pad:
+        if ((int)n.pad_lo.size() != I || (int)n.pad_hi.size() != I ||
+            !(n.pad_interior.empty() || (int)n.pad_interior.size() == I))
+          fail(n, "padding does not match the operand rank");
+        for (int64_t v : n.pad_interior)
+          if (v < 0) fail(n, "negative interior padding");
+        break;
+      case Op::Concatenate:
+        if (n.axis < 0 || n.axis >= R) fail(n, "dimension out of range");
+        for (const ValueRef& o : n.operands)
+          if (g.type(o).rank() != R) fail(n, "operand rank differs from the result rank");
+        break;
+      case Op::Reverse:
+        if (!in_range(n.dims, I)) fail(n, "dimension out of range");
+        break;
+      case Op::Iota:
+        if (n.iota_dim < 0 || n.iota_dim >= R) fail(n, "iota_dimension out of range");
+        break;
+      case Op::Reduce:
+        if (n.operands.size() % 2 != 0 || n.regions.empty()) fail(n, "needs inputs, init values and a body");
+        if (!in_range(n.dims, I) || !distinct(n.dims)) fail(n, "dimensions out of range");
+        break;
+      case Op::ReduceWindow:
+        if ((int)n.window.size() != I || (int)n.window_strides.size() != I ||
+            (int)n.base_dilation.size() != I || (int)n.window_dilation.size() != I ||
+            (int)n.pad_lo.size() != I || (int)n.pad_hi.size() != I)
+          fail(n, "window attributes do not match the operand rank");
+        for (int k = 0; k < I; ++k)
+          if (n.window[k] < 1 || n.window_strides[k] < 1 || n.base_dilation[k] < 1 || n.window_dilation[k] < 1)
+            fail(n, "window sizes, strides and dilations must be positive");
+        if (n.regions.empty()) fail(n, "needs a body");
+        break;
+      case Op::SelectAndScatter:
+        if ((int)n.window.size() != I || (int)n.window_strides.size() != I || (int)n.pad_lo.size() != I)
+          fail(n, "window attributes do not match the operand rank");
+        for (int k = 0; k < I; ++k)
+          if (n.window[k] < 1 || n.window_strides[k] < 1) fail(n, "window sizes and strides must be positive");
+        break;
+      case Op::DotGeneral: {
+        if (n.operands.size() != 2) fail(n, "needs two operands");
+        const int rr = g.type(n.operands[1]).rank();
+        if (n.lhs_batch.size() != n.rhs_batch.size() || n.lhs_contract.size() != n.rhs_contract.size() ||
+            !in_range(n.lhs_batch, I) || !in_range(n.lhs_contract, I) || !in_range(n.rhs_batch, rr) ||
+            !in_range(n.rhs_contract, rr))
+          fail(n, "dimension numbers out of range");
+        break;
+      }
+      case Op::Convolution: {
+        const size_t sp = I >= 2 ? (size_t)(I - 2) : 0;
+        if (n.operands.size() != 2 || n.window_strides.size() != sp || n.lhs_dilation.size() != sp ||
+            n.rhs_dilation.size() != sp || n.pad_lo.size() != sp || n.pad_hi.size() != sp ||
+            n.conv.in_spatial.size() != sp || n.conv.k_spatial.size() != sp || n.conv.out_spatial.size() != sp)
+          fail(n, "window attributes do not match the number of spatial dimensions");
+        const int kr = g.type(n.operands[1]).rank();
+        if (!in_range(n.conv.in_spatial, I) || !in_range(n.conv.k_spatial, kr) || !in_range(n.conv.out_spatial, R) ||
+            !in_range({n.conv.in_batch, n.conv.in_feature}, I) || !in_range({n.conv.k_in, n.conv.k_out}, kr) ||
+            !in_range({n.conv.out_batch, n.conv.out_feature}, R))
+          fail(n, "dimension numbers out of range");
+        break;
+      }
+      default:
+        break;
+    }
+  }
+}
+}  // namespace
+
 Module parse_module(const std::string& text) {
   try {
     Parser p(text);
-    return p.run();
+    Module m = p.run();
+    for (const auto& f : m.funcs) verify_graph(*f.second);
+    return m;
+  } catch (const PjrtErr&) {
+    throw;
   } catch (const ParseError& e) {
     throw PjrtErr(3, e.what());
   } catch (const std::exception& e) {

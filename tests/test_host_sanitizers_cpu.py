@@ -76,3 +76,63 @@ def test_compile_pipeline_is_clean_under_asan_and_ubsan():
     # every golden case and config program compiles; the parse error and the
     # bytecode artifact fail at each of their 3 levels
     assert n_calls >= 90 and n_err == 6, r.stdout
+
+
+_FUZZ = r"""
+import ctypes as C, random, sys
+sys.path[:0] = [{root!r}, {pkg!r}, {tests!r}]
+lib = C.CDLL({lib!r})
+lib.b200_pjrt_inspect.argtypes = [C.c_char_p, C.c_size_t, C.c_int, C.POINTER(C.c_void_p)]
+lib.b200_pjrt_free.argtypes = [C.c_void_p]
+from cases import cases
+from jax_b200 import programs
+seeds = [t for _, t, *_ in cases()] + [programs.mlp_step(), programs.sdpa(), programs.layer_norm(),
+                                        programs.cnn_step()]
+pieces = list("{{}}()[]<>%:,=x0123456789-.\"@ \n") + ["tensor<", "stablehlo.", "dense<", "f32", "i32",
+                                                       "bf16", "0x", "1e40"]
+runs = accepted = 0
+for seed in {seeds!r}:
+    rng = random.Random(seed)
+    for _ in range({iters}):
+        t = rng.choice(seeds)
+        k = rng.randrange(4)
+        if k == 0:
+            t = t[:rng.randrange(len(t))]
+        elif k == 1:
+            for _ in range(rng.randint(1, 5)):
+                i = rng.randrange(len(t))
+                t = t[:i] + rng.choice(pieces) + t[i + 1:]
+        elif k == 2:
+            i = rng.randrange(len(t))
+            t = t[:i] + t[min(len(t), i + rng.randint(1, 40)):]
+        else:
+            i, j = rng.randrange(len(t)), rng.randrange(len(t))
+            t = t[:i] + t[j:j + rng.randint(1, 60)] + t[i:]
+        b = t.encode()
+        out = C.c_void_p()
+        rc = lib.b200_pjrt_inspect(b, len(b), rng.choice((0, 1, 2)), C.byref(out))
+        lib.b200_pjrt_free(out)
+        runs += 1
+        accepted += rc == 0
+print("runs", runs, "accepted", accepted)
+"""
+
+
+def test_mutated_programs_fail_cleanly_under_asan_and_ubsan():
+    """Seeded mutations of valid programs (truncations, replaced characters,
+    cut and duplicated spans) through the whole compile pipeline: each is
+    either compiled or rejected with an error, never read out of range."""
+    asan, ubsan = _runtime("libasan.so"), _runtime("libubsan.so")
+    if not (asan and ubsan):
+        pytest.skip("no AddressSanitizer / UBSan runtime for the host compiler")
+    r = subprocess.run(["make", "-j8", "sanitize"], cwd=os.path.join(PKG, "csrc"), capture_output=True,
+                       text=True, timeout=900)
+    assert r.returncode == 0, r.stderr[-3000:]
+    env = dict(os.environ, LD_PRELOAD=f"{asan}:{ubsan}", ASAN_OPTIONS="detect_leaks=0",
+               UBSAN_OPTIONS="print_stacktrace=1:halt_on_error=1")
+    code = _FUZZ.format(root=ROOT, pkg=PKG, tests=os.path.join(ROOT, "tests"), lib=SAN_LIB,
+                        seeds=[2, 4], iters=800)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, (r.stdout[-1000:], r.stderr[-4000:])
+    assert "runtime error" not in r.stderr and "AddressSanitizer" not in r.stderr, r.stderr[-4000:]
+    assert r.stdout.split()[:2] == ["runs", "1600"], r.stdout

@@ -275,6 +275,43 @@ def test_portable_artifact_without_mlir_c_api_is_unimplemented():
     assert "fused_layer_norm" in pjrt.inspect(programs.layer_norm().encode(), 0)
 
 
+_RW = ('module @m {{ func.func public @main(%arg0: tensor<2x4x4x3xf32>) -> tensor<2x2x2x3xf32> {{\n'
+       '  %0 = stablehlo.constant dense<0xFF800000> : tensor<f32>\n'
+       '  %1 = "stablehlo.reduce_window"(%arg0, %0) <{{padding = dense<0> : tensor<4x2xi64>, '
+       'window_dimensions = array<i64: {win}>, window_strides = array<i64: 1, 2, 2, 1>}}> ({{\n'
+       '  ^bb0(%a: tensor<f32>, %b: tensor<f32>):\n'
+       '    %m = stablehlo.maximum %a, %b : tensor<f32>\n'
+       '    stablehlo.return {ret}\n'
+       '  }}) : (tensor<2x4x4x3xf32>, tensor<f32>) -> tensor<2x2x2x3xf32>\n'
+       '  return %1 : tensor<2x2x2x3xf32>\n}} }}\n')
+_PAD = ('module @m {{ func.func public @main(%arg0: tensor<2x2xf32>) -> tensor<3x3xf32> {{\n'
+        '  %0 = stablehlo.constant dense<0.0> : tensor<f32>\n'
+        '  %1 = stablehlo.pad %arg0, %0, {low}, high = [0, 0], interior = [1, 1] : '
+        '(tensor<2x2xf32>, tensor<f32>) -> tensor<3x3xf32>\n'
+        '  return %1 : tensor<3x3xf32>\n}} }}\n')
+_NEG = ('module @m {{ func.func public @main(%arg0: tensor<4xf32>) -> tensor<4xf32> {{\n'
+        '  %0 = stablehlo.negate {arg}: tensor<4xf32>\n'
+        '  return %0 : tensor<4xf32>\n}} }}\n')
+
+
+@pytest.mark.parametrize("good, bad, what", [
+    (_RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>"), _RW.format(win="2, 1", ret="%m : tensor<f32>"),
+     "window attributes"),
+    (_RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>"), _RW.format(win="1, 2, 2, 1", ret=""),
+     "body returns 0 values"),
+    (_PAD.format(low="low = [0, 0]"), _PAD.format(low="lo = [0, 0]"), "padding"),
+    (_NEG.format(arg="%arg0 "), _NEG.format(arg=""), "needs 1 operands"),
+])
+def test_malformed_attributes_are_invalid_argument(good, bad, what):
+    """Programs whose attribute lists or bodies do not fit their operands (each
+    once drove the code generator out of range under a fuzzer) are rejected
+    right after parsing; the well-formed versions compile."""
+    assert pjrt.inspect(good, 1).startswith("slots")
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.inspect(bad, 1)
+    assert e.value.code == 3 and what in str(e.value), str(e.value)
+
+
 def test_unsupported_op_is_unimplemented():
     text = ('module @m { func.func public @main(%arg0: tensor<8xf32>) -> tensor<8xf32> {\n'
             '  %0 = "stablehlo.sort"(%arg0) <{dimension = 0 : i64}> ({\n'
