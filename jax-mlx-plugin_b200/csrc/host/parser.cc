@@ -1461,15 +1461,23 @@ void verify_graph(const Graph& g) {
         for (int k = 0; k < I; ++k)
           if (n.start[k] < 0 || n.start[k] > n.limit[k] || n.limit[k] > (*idims)[k] || n.strides[k] < 1)
             fail(n, "slice bounds out of range");
+        if (R != I) fail(n, "result rank differs from the operand rank");
+        for (int k = 0; k < I; ++k)
+          if (rt.dims[k] != (n.limit[k] - n.start[k] + n.strides[k] - 1) / n.strides[k])
+            fail(n, "result shape does not match the slice");
         break;
       case Op::DynamicSlice:
         if ((int)n.limit.size() != I || (int)n.operands.size() != 1 + I) fail(n, "slice sizes / start indices do not match the operand rank");
         for (int k = 0; k < I; ++k)
           if (n.limit[k] < 0 || n.limit[k] > (*idims)[k]) fail(n, "slice size out of range");
+        if (rt.dims != n.limit) fail(n, "result shape differs from the slice sizes");
         break;
       case Op::DynamicUpdateSlice:
         if ((int)n.operands.size() != 2 + I || g.type(n.operands.at(1)).rank() != I)
           fail(n, "update / start indices do not match the operand rank");
+        if (rt.dims != *idims) fail(n, "result shape differs from the operand shape");
+        for (int k = 0; k < I; ++k)
+          if (g.type(n.operands[1]).dims[k] > (*idims)[k]) fail(n, "update larger than the operand");
         break;
       case Op::Pad:
         if ((int)n.pad_lo.size() != I || (int)n.pad_hi.size() != I ||
@@ -1477,14 +1485,30 @@ void verify_graph(const Graph& g) {
           fail(n, "padding does not match the operand rank");
         for (int64_t v : n.pad_interior)
           if (v < 0) fail(n, "negative interior padding");
+        if (R != I) fail(n, "result rank differs from the operand rank");
+        for (int k = 0; k < I; ++k) {
+          const int64_t d = (*idims)[k], in = n.pad_interior.empty() ? 0 : n.pad_interior[k];
+          if (rt.dims[k] != n.pad_lo[k] + n.pad_hi[k] + d + (d > 0 ? (d - 1) * in : 0))
+            fail(n, "result shape does not match the padding");
+        }
         break;
       case Op::Concatenate:
         if (n.axis < 0 || n.axis >= R) fail(n, "dimension out of range");
-        for (const ValueRef& o : n.operands)
-          if (g.type(o).rank() != R) fail(n, "operand rank differs from the result rank");
+        {
+          int64_t along = 0;
+          for (const ValueRef& o : n.operands) {
+            const TensorType& t = g.type(o);
+            if (t.rank() != R) fail(n, "operand rank differs from the result rank");
+            for (int k = 0; k < R; ++k)
+              if (k != n.axis && t.dims[k] != rt.dims[k]) fail(n, "operand shapes differ off the axis");
+            along += t.dims[n.axis];
+          }
+          if (along != rt.dims[n.axis]) fail(n, "result size along the axis is not the operands' sum");
+        }
         break;
       case Op::Reverse:
         if (!in_range(n.dims, I)) fail(n, "dimension out of range");
+        if (rt.dims != *idims) fail(n, "result shape differs from the operand shape");
         break;
       case Op::Iota:
         if (n.iota_dim < 0 || n.iota_dim >= R) fail(n, "iota_dimension out of range");
@@ -1492,6 +1516,16 @@ void verify_graph(const Graph& g) {
       case Op::Reduce:
         if (n.operands.size() % 2 != 0 || n.regions.empty()) fail(n, "needs inputs, init values and a body");
         if (!in_range(n.dims, I) || !distinct(n.dims)) fail(n, "dimensions out of range");
+        {
+          std::vector<int64_t> kept;
+          for (int k = 0; k < I; ++k)
+            if (std::find(n.dims.begin(), n.dims.end(), k) == n.dims.end()) kept.push_back((*idims)[k]);
+          const size_t nin = n.operands.size() / 2;
+          if (n.results.size() != nin) fail(n, "needs one result per input");
+          for (size_t k = 0; k < nin; ++k)
+            if (g.type(n.operands[k]).dims != *idims || n.results[k].dims != kept)
+              fail(n, "result shape is not the operand shape without the reduced dimensions");
+        }
         break;
       case Op::ReduceWindow:
         if ((int)n.window.size() != I || (int)n.window_strides.size() != I ||
@@ -1502,12 +1536,29 @@ void verify_graph(const Graph& g) {
           if (n.window[k] < 1 || n.window_strides[k] < 1 || n.base_dilation[k] < 1 || n.window_dilation[k] < 1)
             fail(n, "window sizes, strides and dilations must be positive");
         if (n.regions.empty()) fail(n, "needs a body");
+        {
+          const size_t nin = n.operands.size() / 2;
+          if (n.results.size() != nin) fail(n, "needs one result per input");
+          for (size_t j = 0; j < nin; ++j) {
+            if (g.type(n.operands[j]).dims != *idims || n.results[j].rank() != I)
+              fail(n, "result rank differs from the operand rank");
+            for (int k = 0; k < I; ++k) {
+              const int64_t d = (*idims)[k];
+              const int64_t padded = n.pad_lo[k] + (d == 0 ? 0 : (d - 1) * n.base_dilation[k] + 1) + n.pad_hi[k];
+              const int64_t win = (n.window[k] - 1) * n.window_dilation[k] + 1;
+              const int64_t cnt = (padded == 0 || win > padded) ? 0 : (padded - win) / n.window_strides[k] + 1;
+              if (n.results[j].dims[k] != cnt) fail(n, "result shape does not match the windows");
+            }
+          }
+        }
         break;
       case Op::SelectAndScatter:
         if ((int)n.window.size() != I || (int)n.window_strides.size() != I || (int)n.pad_lo.size() != I)
           fail(n, "window attributes do not match the operand rank");
         for (int k = 0; k < I; ++k)
           if (n.window[k] < 1 || n.window_strides[k] < 1) fail(n, "window sizes and strides must be positive");
+        if (rt.dims != *idims || g.type(n.operands[1]).rank() != I)
+          fail(n, "result / source shapes do not match the operand");
         break;
       case Op::DotGeneral: {
         if (n.operands.size() != 2) fail(n, "needs two operands");
@@ -1516,8 +1567,32 @@ void verify_graph(const Graph& g) {
             !in_range(n.lhs_batch, I) || !in_range(n.lhs_contract, I) || !in_range(n.rhs_batch, rr) ||
             !in_range(n.rhs_contract, rr))
           fail(n, "dimension numbers out of range");
+        {
+          const TensorType& lt = g.type(n.operands[0]);
+          const TensorType& qt = g.type(n.operands[1]);
+          std::vector<int64_t> want;
+          for (size_t k = 0; k < n.lhs_batch.size(); ++k) {
+            if (lt.dims[n.lhs_batch[k]] != qt.dims[n.rhs_batch[k]]) fail(n, "batch sizes differ");
+            want.push_back(lt.dims[n.lhs_batch[k]]);
+          }
+          for (size_t k = 0; k < n.lhs_contract.size(); ++k)
+            if (lt.dims[n.lhs_contract[k]] != qt.dims[n.rhs_contract[k]]) fail(n, "contracting sizes differ");
+          auto free_of = [&](const TensorType& t, const std::vector<int64_t>& b, const std::vector<int64_t>& c) {
+            for (int k = 0; k < t.rank(); ++k)
+              if (std::find(b.begin(), b.end(), k) == b.end() && std::find(c.begin(), c.end(), k) == c.end())
+                want.push_back(t.dims[k]);
+          };
+          free_of(lt, n.lhs_batch, n.lhs_contract);
+          free_of(qt, n.rhs_batch, n.rhs_contract);
+          if (!distinct(n.lhs_batch) || !distinct(n.lhs_contract) || !distinct(n.rhs_batch) ||
+              !distinct(n.rhs_contract) || rt.dims != want)
+            fail(n, "result shape is not batch + lhs free + rhs free");
+        }
         break;
       }
+      case Op::Scatter:
+        if (rt.dims != *idims) fail(n, "result shape differs from the operand shape");
+        break;
       case Op::Convolution: {
         const size_t sp = I >= 2 ? (size_t)(I - 2) : 0;
         if (n.operands.size() != 2 || n.window_strides.size() != sp || n.lhs_dilation.size() != sp ||
@@ -1525,6 +1600,7 @@ void verify_graph(const Graph& g) {
             n.conv.in_spatial.size() != sp || n.conv.k_spatial.size() != sp || n.conv.out_spatial.size() != sp)
           fail(n, "window attributes do not match the number of spatial dimensions");
         const int kr = g.type(n.operands[1]).rank();
+        if (kr != I || R != I) fail(n, "kernel / result rank differs from the input rank");
         if (!in_range(n.conv.in_spatial, I) || !in_range(n.conv.k_spatial, kr) || !in_range(n.conv.out_spatial, R) ||
             !in_range({n.conv.in_batch, n.conv.in_feature}, I) || !in_range({n.conv.k_in, n.conv.k_out}, kr) ||
             !in_range({n.conv.out_batch, n.conv.out_feature}, R))

@@ -294,6 +294,11 @@ _NEG = ('module @m {{ func.func public @main(%arg0: tensor<4xf32>) -> tensor<4xf
         '  return %0 : tensor<4xf32>\n}} }}\n')
 
 
+_SLICE = ('module @m {{ func.func public @main(%arg0: tensor<8xf32>) -> tensor<{n}xf32> {{\n'
+          '  %0 = stablehlo.slice %arg0 [0:4] : (tensor<8xf32>) -> tensor<{n}xf32>\n'
+          '  return %0 : tensor<{n}xf32>\n}} }}\n')
+
+
 @pytest.mark.parametrize("good, bad, what", [
     (_RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>"), _RW.format(win="2, 1", ret="%m : tensor<f32>"),
      "window attributes"),
@@ -301,6 +306,10 @@ _NEG = ('module @m {{ func.func public @main(%arg0: tensor<4xf32>) -> tensor<4xf
      "body returns 0 values"),
     (_PAD.format(low="low = [0, 0]"), _PAD.format(low="lo = [0, 0]"), "padding"),
     (_NEG.format(arg="%arg0 "), _NEG.format(arg=""), "needs 1 operands"),
+    (_RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>"),
+     _RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>").replace("-> tensor<2x2x2x3xf32>\n", "-> tensor<22x3xf32>\n"),
+     "result rank differs"),
+    (_SLICE.format(n=4), _SLICE.format(n=6), "result shape does not match the slice"),
 ])
 def test_malformed_attributes_are_invalid_argument(good, bad, what):
     """Programs whose attribute lists or bodies do not fit their operands (each
