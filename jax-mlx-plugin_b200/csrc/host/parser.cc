@@ -1590,9 +1590,53 @@ void verify_graph(const Graph& g) {
         }
         break;
       }
-      case Op::Scatter:
+      case Op::Scatter: {
         if (rt.dims != *idims) fail(n, "result shape differs from the operand shape");
+        const ScatterDims& S = n.scatter;
+        const int ir = g.type(n.operands.at(1)).rank();
+        const int ur = g.type(n.operands.at(n.operands.size() - 1)).rank();
+        if (S.index_vector_dim < 0 || S.index_vector_dim > ir || !in_range(S.scatter_dims_to_operand_dims, I) ||
+            !in_range(S.inserted_window_dims, I) || !in_range(S.input_batching_dims, I) ||
+            !in_range(S.scatter_indices_batching_dims, ir) ||
+            S.input_batching_dims.size() != S.scatter_indices_batching_dims.size() ||
+            !in_range(S.update_window_dims, ur))
+          fail(n, "scatter dimension numbers out of range");
         break;
+      }
+      case Op::Gather: {
+        const GatherDims& G = n.gather;
+        const TensorType& it = g.type(n.operands.at(1));
+        const int ir = it.rank();
+        if ((int)G.slice_sizes.size() != I || G.index_vector_dim < 0 || G.index_vector_dim > ir ||
+            !in_range(G.start_index_map, I) || !in_range(G.collapsed_slice_dims, I) ||
+            !in_range(G.operand_batching_dims, I) || !in_range(G.start_indices_batching_dims, ir) ||
+            G.operand_batching_dims.size() != G.start_indices_batching_dims.size() ||
+            !in_range(G.offset_dims, R) || !distinct(G.offset_dims) || !distinct(G.start_index_map))
+          fail(n, "gather dimension numbers out of range");
+        for (int k = 0; k < I; ++k)
+          if (G.slice_sizes[k] < 0 || G.slice_sizes[k] > (*idims)[k]) fail(n, "slice size out of range");
+        const int64_t nvec = G.index_vector_dim < ir ? it.dims[G.index_vector_dim] : 1;
+        if ((int64_t)G.start_index_map.size() != nvec) fail(n, "start_index_map does not match the index vector");
+        // result: offset_dims take the kept slice sizes in order, the rest the
+        // indices' batch dimensions in order
+        std::vector<int64_t> offs, batch;
+        for (int k = 0; k < I; ++k)
+          if (std::find(G.collapsed_slice_dims.begin(), G.collapsed_slice_dims.end(), k) ==
+                  G.collapsed_slice_dims.end() &&
+              std::find(G.operand_batching_dims.begin(), G.operand_batching_dims.end(), k) ==
+                  G.operand_batching_dims.end())
+            offs.push_back(G.slice_sizes[k]);
+        for (int k = 0; k < ir; ++k)
+          if (k != G.index_vector_dim) batch.push_back(it.dims[k]);
+        if (offs.size() != G.offset_dims.size() || (size_t)R != offs.size() + batch.size())
+          fail(n, "result rank does not match the gather");
+        size_t oj = 0, bj = 0;
+        for (int k = 0; k < R; ++k) {
+          const bool off = std::find(G.offset_dims.begin(), G.offset_dims.end(), k) != G.offset_dims.end();
+          if (rt.dims[k] != (off ? offs[oj++] : batch[bj++])) fail(n, "result shape does not match the gather");
+        }
+        break;
+      }
       case Op::Convolution: {
         const size_t sp = I >= 2 ? (size_t)(I - 2) : 0;
         if (n.operands.size() != 2 || n.window_strides.size() != sp || n.lhs_dilation.size() != sp ||

@@ -298,6 +298,13 @@ _SLICE = ('module @m {{ func.func public @main(%arg0: tensor<8xf32>) -> tensor<{
           '  %0 = stablehlo.slice %arg0 [0:4] : (tensor<8xf32>) -> tensor<{n}xf32>\n'
           '  return %0 : tensor<{n}xf32>\n}} }}\n')
 
+_GATHER = ('module @m {{ func.func public @main(%arg0: tensor<12x8xf32>, %arg1: tensor<2x4x1xi32>) -> '
+           'tensor<2x4x{od}xf32> {{\n'
+           '  %0 = "stablehlo.gather"(%arg0, %arg1) <{{dimension_numbers = #stablehlo.gather<offset_dims = [2], '
+           'collapsed_slice_dims = [0], start_index_map = [0], index_vector_dim = 2>, indices_are_sorted = false, '
+           'slice_sizes = array<i64: 1, {ss}>}}> : (tensor<12x8xf32>, tensor<2x4x1xi32>) -> tensor<2x4x{od}xf32>\n'
+           '  return %0 : tensor<2x4x{od}xf32>\n}} }}\n')
+
 
 @pytest.mark.parametrize("good, bad, what", [
     (_RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>"), _RW.format(win="2, 1", ret="%m : tensor<f32>"),
@@ -310,6 +317,8 @@ _SLICE = ('module @m {{ func.func public @main(%arg0: tensor<8xf32>) -> tensor<{
      _RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>").replace("-> tensor<2x2x2x3xf32>\n", "-> tensor<22x3xf32>\n"),
      "result rank differs"),
     (_SLICE.format(n=4), _SLICE.format(n=6), "result shape does not match the slice"),
+    (_GATHER.format(ss=8, od=8), _GATHER.format(ss=9, od=9), "slice size out of range"),
+    (_GATHER.format(ss=8, od=8), _GATHER.format(ss=4, od=8), "result shape does not match the gather"),
 ])
 def test_malformed_attributes_are_invalid_argument(good, bad, what):
     """Programs whose attribute lists or bodies do not fit their operands (each
