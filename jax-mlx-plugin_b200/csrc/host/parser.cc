@@ -1601,6 +1601,21 @@ void verify_graph(const Graph& g) {
             S.input_batching_dims.size() != S.scatter_indices_batching_dims.size() ||
             !in_range(S.update_window_dims, ur))
           fail(n, "scatter dimension numbers out of range");
+        {
+          // the updates' scatter dimensions are the indices' batch dimensions
+          const TensorType& it = g.type(n.operands[1]);
+          const TensorType& ut = g.type(n.operands.back());
+          std::vector<int64_t> ibatch, ubatch;
+          for (int k = 0; k < ir; ++k)
+            if (k != S.index_vector_dim) ibatch.push_back(it.dims[k]);
+          for (int k = 0; k < ur; ++k)
+            if (std::find(S.update_window_dims.begin(), S.update_window_dims.end(), k) == S.update_window_dims.end())
+              ubatch.push_back(ut.dims[k]);
+          if (ibatch != ubatch) fail(n, "update scatter dimensions differ from the indices' batch dimensions");
+          const int64_t nvec = S.index_vector_dim < ir ? it.dims[S.index_vector_dim] : 1;
+          if ((int64_t)S.scatter_dims_to_operand_dims.size() != nvec)
+            fail(n, "scatter_dims_to_operand_dims does not match the index vector");
+        }
         break;
       }
       case Op::Gather: {
@@ -1649,6 +1664,18 @@ void verify_graph(const Graph& g) {
             !in_range({n.conv.in_batch, n.conv.in_feature}, I) || !in_range({n.conv.k_in, n.conv.k_out}, kr) ||
             !in_range({n.conv.out_batch, n.conv.out_feature}, R))
           fail(n, "dimension numbers out of range");
+        {
+          const std::vector<int64_t>& kd = g.type(n.operands[1]).dims;
+          for (size_t s2 = 0; s2 < sp; ++s2) {
+            const int64_t in = (*idims)[n.conv.in_spatial[s2]], k = kd[n.conv.k_spatial[s2]];
+            const int64_t padded = n.pad_lo[s2] + (in == 0 ? 0 : (in - 1) * n.lhs_dilation[s2] + 1) + n.pad_hi[s2];
+            const int64_t win = k == 0 ? 0 : (k - 1) * n.rhs_dilation[s2] + 1;
+            if (n.window_strides[s2] < 1 || n.lhs_dilation[s2] < 1 || n.rhs_dilation[s2] < 1)
+              fail(n, "strides and dilations must be positive");
+            const int64_t cnt = (padded <= 0 || win > padded) ? 0 : (padded - win) / n.window_strides[s2] + 1;
+            if (rt.dims[n.conv.out_spatial[s2]] != cnt) fail(n, "result spatial size does not match the window");
+          }
+        }
         break;
       }
       default:

@@ -79,7 +79,7 @@ def test_compile_pipeline_is_clean_under_asan_and_ubsan():
 
 
 _FUZZ = r"""
-import ctypes as C, random, sys
+import ctypes as C, random, re, sys
 sys.path[:0] = [{root!r}, {pkg!r}, {tests!r}]
 lib = C.CDLL({lib!r})
 lib.b200_pjrt_inspect.argtypes = [C.c_char_p, C.c_size_t, C.c_int, C.POINTER(C.c_void_p)]
@@ -90,13 +90,18 @@ seeds = [t for _, t, *_ in cases()] + [programs.mlp_step(), programs.sdpa(), pro
                                         programs.cnn_step()]
 pieces = list("{{}}()[]<>%:,=x0123456789-.\"@ \n") + ["tensor<", "stablehlo.", "dense<", "f32", "i32",
                                                        "bf16", "0x", "1e40"]
+number = re.compile(r"(?<![%\w.#])\d+(?![\w.])")
 runs = accepted = 0
 for seed in {seeds!r}:
     rng = random.Random(seed)
     for _ in range({iters}):
         t = rng.choice(seeds)
-        k = rng.randrange(4)
-        if k == 0:
+        k = rng.randrange(5)
+        if k == 4:  # an integer literal (a dimension, an attribute value) replaced
+            spans = [m.span() for m in number.finditer(t)]
+            a, e = rng.choice(spans)
+            t = t[:a] + str(rng.choice([0, 1, 2, 3, 5, 8, 16, 100])) + t[e:]
+        elif k == 0:
             t = t[:rng.randrange(len(t))]
         elif k == 1:
             for _ in range(rng.randint(1, 5)):
@@ -120,8 +125,9 @@ print("runs", runs, "accepted", accepted)
 
 def test_mutated_programs_fail_cleanly_under_asan_and_ubsan():
     """Seeded mutations of valid programs (truncations, replaced characters,
-    cut and duplicated spans) through the whole compile pipeline: each is
-    either compiled or rejected with an error, never read out of range."""
+    cut and duplicated spans, replaced integer literals, i.e. wrong shapes and
+    attribute values in valid syntax) through the whole compile pipeline: each
+    is either compiled or rejected with an error, never read out of range."""
     asan, ubsan = _runtime("libasan.so"), _runtime("libubsan.so")
     if not (asan and ubsan):
         pytest.skip("no AddressSanitizer / UBSan runtime for the host compiler")

@@ -306,6 +306,13 @@ _GATHER = ('module @m {{ func.func public @main(%arg0: tensor<12x8xf32>, %arg1: 
            '  return %0 : tensor<2x4x{od}xf32>\n}} }}\n')
 
 
+def _conv(out):
+    """The reference's conv case (1x8x8x3 * 3x3x3x16, SAME) with the output's
+    spatial size given as `out`."""
+    t = [c for c in cases() if c[0] == "conv_same_ones"][0][1]
+    return t.replace("1x8x8x16xf32", f"1x{out}x{out}x16xf32")
+
+
 @pytest.mark.parametrize("good, bad, what", [
     (_RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>"), _RW.format(win="2, 1", ret="%m : tensor<f32>"),
      "window attributes"),
@@ -319,6 +326,7 @@ _GATHER = ('module @m {{ func.func public @main(%arg0: tensor<12x8xf32>, %arg1: 
     (_SLICE.format(n=4), _SLICE.format(n=6), "result shape does not match the slice"),
     (_GATHER.format(ss=8, od=8), _GATHER.format(ss=9, od=9), "slice size out of range"),
     (_GATHER.format(ss=8, od=8), _GATHER.format(ss=4, od=8), "result shape does not match the gather"),
+    (_conv(8), _conv(9), "result spatial size does not match the window"),
 ])
 def test_malformed_attributes_are_invalid_argument(good, bad, what):
     """Programs whose attribute lists or bodies do not fit their operands (each
