@@ -1018,8 +1018,11 @@ class Parser {
         if (n.window_dilation.empty()) n.window_dilation.assign(r, 1);
         n.pad_lo.assign(r, 0);
         n.pad_hi.assign(r, 0);
+        if (pad.size() == 1) pad.assign(2 * r, pad[0]);  // splat: dense<v> pads every edge by v
         if (pad.size() == 2 * r)
           for (size_t i = 0; i < r; ++i) { n.pad_lo[i] = pad[2 * i]; n.pad_hi[i] = pad[2 * i + 1]; }
+        else if (!pad.empty())
+          n.pad_lo.clear();  // a list of the wrong length: rejected by the verifier
         break;
       }
       case Op::DotGeneral: {
@@ -1106,10 +1109,13 @@ class Parser {
           p_ = save;
         }
         size_t ns = n.conv.in_spatial.size();
+        if (pad.size() == 1) pad.assign(2 * ns, pad[0]);  // splat: dense<v> pads every edge by v
         for (size_t i = 0; i < ns && pad.size() == 2 * ns; ++i) {
           n.pad_lo.push_back(pad[2 * i]);
           n.pad_hi.push_back(pad[2 * i + 1]);
         }
+        if (!pad.empty() && pad.size() != 2 * ns)
+          n.pad_lo.assign(ns + 1, 0);  // a list of the wrong length: rejected by the verifier
         fill_conv_defaults(n);
         break;
       }
@@ -1442,7 +1448,7 @@ void verify_graph(const Graph& g) {
     }
     switch (n.op) {
       case Op::BroadcastInDim:
-        if ((int)n.dims.size() != I || !in_range(n.dims, R)) fail(n, "bad broadcast_dimensions");
+        if ((int)n.dims.size() != I || !in_range(n.dims, R) || !distinct(n.dims)) fail(n, "bad broadcast_dimensions");
         for (int k = 0; k < I; ++k)
           if ((*idims)[k] != 1 && (*idims)[k] != rt.dims[n.dims[k]]) fail(n, "operand dimension mismatch");
         break;
@@ -1559,6 +1565,12 @@ void verify_graph(const Graph& g) {
           if (n.window[k] < 1 || n.window_strides[k] < 1) fail(n, "window sizes and strides must be positive");
         if (rt.dims != *idims || g.type(n.operands[1]).rank() != I)
           fail(n, "result / source shapes do not match the operand");
+        if ((int)n.pad_hi.size() != I) fail(n, "padding does not match the operand rank");
+        for (int k = 0; k < I; ++k) {  // one source element per window
+          const int64_t padded = n.pad_lo[k] + (*idims)[k] + n.pad_hi[k];
+          const int64_t cnt = (padded <= 0 || n.window[k] > padded) ? 0 : (padded - n.window[k]) / n.window_strides[k] + 1;
+          if (g.type(n.operands[1]).dims[k] != cnt) fail(n, "source shape does not match the windows");
+        }
         break;
       case Op::DotGeneral: {
         if (n.operands.size() != 2) fail(n, "needs two operands");
@@ -1660,6 +1672,24 @@ void verify_graph(const Graph& g) {
           fail(n, "window attributes do not match the number of spatial dimensions");
         const int kr = g.type(n.operands[1]).rank();
         if (kr != I || R != I) fail(n, "kernel / result rank differs from the input rank");
+        {
+          auto perm = [&](int64_t a, int64_t b, const std::vector<int64_t>& sp2, int r) {
+            std::vector<int64_t> v = sp2;
+            v.push_back(a);
+            v.push_back(b);
+            return (int)v.size() == r && in_range(v, r) && distinct(v);
+          };
+          if (!perm(n.conv.in_batch, n.conv.in_feature, n.conv.in_spatial, I) ||
+              !perm(n.conv.k_in, n.conv.k_out, n.conv.k_spatial, kr) ||
+              !perm(n.conv.out_batch, n.conv.out_feature, n.conv.out_spatial, R))
+            fail(n, "dimension numbers are not a permutation of each operand's dimensions");
+          const std::vector<int64_t>& kdims = g.type(n.operands[1]).dims;
+          if (n.feature_groups == 1 && n.batch_groups == 1 &&
+              ((*idims)[n.conv.in_feature] != kdims[n.conv.k_in] ||
+               rt.dims[n.conv.out_feature] != kdims[n.conv.k_out] ||
+               rt.dims[n.conv.out_batch] != (*idims)[n.conv.in_batch]))
+            fail(n, "feature / batch sizes do not match");
+        }
         if (!in_range(n.conv.in_spatial, I) || !in_range(n.conv.k_spatial, kr) || !in_range(n.conv.out_spatial, R) ||
             !in_range({n.conv.in_batch, n.conv.in_feature}, I) || !in_range({n.conv.k_in, n.conv.k_out}, kr) ||
             !in_range({n.conv.out_batch, n.conv.out_feature}, R))

@@ -327,6 +327,12 @@ def _conv(out):
     (_GATHER.format(ss=8, od=8), _GATHER.format(ss=9, od=9), "slice size out of range"),
     (_GATHER.format(ss=8, od=8), _GATHER.format(ss=4, od=8), "result shape does not match the gather"),
     (_conv(8), _conv(9), "result spatial size does not match the window"),
+    # splat padding dense<1> pads both edges of every dimension by 1: windows
+    # [1, 2, 2, 1] at strides [1, 2, 2, 1] over 2x4x4x3 give 4x3x3x5, not 2x2x2x3
+    (_RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>").replace("dense<0> : tensor<4x2xi64>", "dense<1> : tensor<4x2xi64>")
+     .replace("tensor<2x2x2x3xf32>", "tensor<4x3x3x5xf32>"),
+     _RW.format(win="1, 2, 2, 1", ret="%m : tensor<f32>").replace("dense<0> : tensor<4x2xi64>", "dense<1> : tensor<4x2xi64>"),
+     "result shape does not match the windows"),
 ])
 def test_malformed_attributes_are_invalid_argument(good, bad, what):
     """Programs whose attribute lists or bodies do not fit their operands (each
