@@ -1213,8 +1213,12 @@ class Parser {
         ++pos;
       } while (accept(","));
       expect("]");
-      spatial.assign(sp.size(), 0);
-      for (auto& q : sp) spatial.at(q.first) = q.second;
+      spatial.assign(sp.size(), -1);
+      for (auto& q : sp) {
+        if (q.first < 0 || q.first >= (int64_t)sp.size() || spatial[q.first] >= 0)
+          fail("spatial dimensions must be listed once each, numbered from 0");
+        spatial[q.first] = q.second;
+      }
     };
     spec('l', c.in_spatial, c.in_batch, c.in_feature);
     expect("x");
