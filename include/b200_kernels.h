@@ -123,7 +123,12 @@ B200_API int b200_gemm(const void* a, const void* b, void* c, const void* bias, 
  * keeps the last call's contents: two calls that overlap on the GPU (different
  * streams, or host threads that do not order their calls) race on it.  Each
  * call writes every partial sum it reads, so nothing needs clearing between
- * calls.  Arguments, results and error codes are otherwise those of b200_gemm.
+ * calls.  in_dtype must be B200_DT_F32 or B200_DT_BF16: the mixed F32 x BF16
+ * codes need a widened or split copy of one operand, so they are refused with
+ * B200_ERR_UNSUPPORTED (as is any path that would need a buffer other than the
+ * fixed array).  b200_device_error reads this entry point's error word without
+ * allocating.  Arguments, results and error codes are otherwise those of
+ * b200_gemm.
  * No counterpart in the reference: it has no split-K scratch and allocates
  * through MLX. */
 B200_API int b200_gemm_noalloc(const void* a, const void* b, void* c, const void* bias,

@@ -41,6 +41,23 @@ __attribute__((visibility("default"))) void* b200_pjrt_device_stream(void* devic
 __attribute__((visibility("default"))) int b200_pjrt_execute_times(void* loaded_executable,
                                                                   double* ms, int max);
 
+/* The key-value exchange that Execute performs for the NCCL unique id of a
+ * multi-process run (one process per GPU), without a device: rank 0 puts
+ * `value` under `key` through put_callback, any other rank gets `key` through
+ * get_callback, with the PJRT_KeyValue*Callback_Args the plugin builds for
+ * PJRT_Client_Create's kv_get_callback / kv_put_callback (callback_error set,
+ * timeout from B200_KV_TIMEOUT_MS, default 120000).  Lets a deployment check
+ * its KV-store wiring and its error path before the first collective.  Returns
+ * 0 with the value written or read in *out (*out_len bytes, NUL-terminated;
+ * may hold zero bytes), or the PJRT error code with the message in *out: a
+ * callback's error object (made through callback_error) keeps its code.  Free
+ * *out with b200_pjrt_free().  The reference (single device) has no
+ * counterpart; jaxlib's distributed client supplies the callbacks. */
+__attribute__((visibility("default"))) int b200_pjrt_kv_exchange(
+    void* get_callback, void* get_user_arg, void* put_callback, void* put_user_arg, int rank,
+    const char* key, size_t key_len, const char* value, size_t value_len, char** out,
+    size_t* out_len);
+
 #ifdef __cplusplus
 }
 #endif

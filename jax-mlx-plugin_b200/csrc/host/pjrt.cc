@@ -262,19 +262,29 @@ int64_t kv_timeout_ms() {
   return v ? std::atoll(v) : 120000;
 }
 
-std::string kv_get(PJRT_Client* c, const std::string& key) {
-  if (!c->kv_get) throw PjrtErr(9, "multi-process execution needs the client's KV-store callbacks");
+// The error constructor handed to KV-store callbacks: jaxlib's C++ wrappers
+// report a failed or timed-out store operation by calling
+// (*args->callback_error)(code, message, size) and returning the result.
+PJRT_Error* kv_callback_error(PJRT_Error_Code code, const char* msg, size_t n) {
+  return new PJRT_Error{code, std::string(msg ? msg : "", msg ? n : 0)};
+}
+PJRT_CallbackError g_kv_callback_error = &kv_callback_error;
+
+std::string kv_get(PJRT_KeyValueGetCallback cb, void* user_arg, const std::string& key) {
+  if (!cb) throw PjrtErr(9, "multi-process execution needs the client's KV-store callbacks");
   PJRT_KeyValueGetCallback_Args a{};
   a.struct_size = sizeof(a);
   a.key = key.data();
   a.key_size = key.size();
   a.timeout_in_ms = (int)kv_timeout_ms();
-  a.user_arg = c->kv_get_arg;
-  PJRT_Error* e = c->kv_get(&a);
+  a.callback_error = &g_kv_callback_error;
+  a.user_arg = user_arg;
+  PJRT_Error* e = cb(&a);
   if (e) {
+    const int code = e->code ? (int)e->code : 4;
     std::string m = e->msg;
-    delete e;
-    throw PjrtErr(4, "KV get '" + key + "' failed: " + m);
+    delete e;  // made by kv_callback_error above
+    throw PjrtErr(code, "KV get '" + key + "' failed: " + m);
   }
   // A callback that could not produce the value (a Python one whose store
   // raised or timed out returns no error object) leaves it unset.
@@ -285,21 +295,28 @@ std::string kv_get(PJRT_Client* c, const std::string& key) {
   if (a.value_deleter_callback) a.value_deleter_callback(a.value);
   return v;
 }
-void kv_put(PJRT_Client* c, const std::string& key, const std::string& val) {
-  if (!c->kv_put) throw PjrtErr(9, "multi-process execution needs the client's KV-store callbacks");
+void kv_put(PJRT_KeyValuePutCallback cb, void* user_arg, const std::string& key,
+            const std::string& val) {
+  if (!cb) throw PjrtErr(9, "multi-process execution needs the client's KV-store callbacks");
   PJRT_KeyValuePutCallback_Args a{};
   a.struct_size = sizeof(a);
   a.key = key.data();
   a.key_size = key.size();
   a.value = val.data();
   a.value_size = val.size();
-  a.user_arg = c->kv_put_arg;
-  PJRT_Error* e = c->kv_put(&a);
+  a.callback_error = &g_kv_callback_error;
+  a.user_arg = user_arg;
+  PJRT_Error* e = cb(&a);
   if (e) {
+    const int code = e->code ? (int)e->code : 13;
     std::string m = e->msg;
     delete e;
-    throw PjrtErr(13, "KV put '" + key + "' failed: " + m);
+    throw PjrtErr(code, "KV put '" + key + "' failed: " + m);
   }
+}
+std::string kv_get(PJRT_Client* c, const std::string& key) { return kv_get(c->kv_get, c->kv_get_arg, key); }
+void kv_put(PJRT_Client* c, const std::string& key, const std::string& val) {
+  kv_put(c->kv_put, c->kv_put_arg, key, val);
 }
 
 // ---------------------------------------------- bytecode -> text (jaxlib) --
@@ -1769,6 +1786,34 @@ __attribute__((visibility("default"))) int b200_pjrt_execute_times(void* loaded_
   }
   e.timings.clear();
   return n;
+}
+
+__attribute__((visibility("default"))) int b200_pjrt_kv_exchange(
+    void* get_callback, void* get_user_arg, void* put_callback, void* put_user_arg, int rank,
+    const char* key, size_t key_len, const char* value, size_t value_len, char** out,
+    size_t* out_len) {
+  std::string res;
+  int code = 0;
+  try {
+    const std::string k(key ? key : "", key ? key_len : 0);
+    if (rank == 0) {
+      res.assign(value ? value : "", value ? value_len : 0);
+      kv_put(reinterpret_cast<PJRT_KeyValuePutCallback>(put_callback), put_user_arg, k, res);
+    } else {
+      res = kv_get(reinterpret_cast<PJRT_KeyValueGetCallback>(get_callback), get_user_arg, k);
+    }
+  } catch (const PjrtErr& e) {
+    code = e.code;
+    res = e.what();
+  } catch (const std::exception& e) {
+    code = 13;
+    res = e.what();
+  }
+  *out = (char*)std::malloc(res.size() + 1);
+  std::memcpy(*out, res.data(), res.size());
+  (*out)[res.size()] = 0;
+  if (out_len) *out_len = res.size();
+  return code;
 }
 
 __attribute__((visibility("default"))) void* b200_pjrt_device_stream(void* device) {

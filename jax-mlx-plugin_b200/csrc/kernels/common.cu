@@ -84,30 +84,46 @@ int allow_dynamic_smem(const void* fn, int bytes, const char* what) {
   return B200_OK;
 }
 
+namespace {
+std::mutex g_word_mu;
+int* g_words[64] = {nullptr};
+}  // namespace
+
 int* device_error_word() {
-  static std::mutex mu;
-  static int* words[64] = {nullptr};
   int dev = 0;
   cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lk(mu);
+  std::lock_guard<std::mutex> lk(g_word_mu);
   if (dev < 0 || dev >= 64) return nullptr;
-  if (!words[dev]) {
-    if (cudaMalloc(&words[dev], sizeof(int)) != cudaSuccess) return nullptr;
-    cudaMemset(words[dev], 0, sizeof(int));
+  if (!g_words[dev]) {
+    if (cudaMalloc(&g_words[dev], sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(g_words[dev], 0, sizeof(int));
     cudaDeviceSynchronize();
   }
-  return words[dev];
+  return g_words[dev];
+}
+
+// The current device's error word if some kernel has already been given it;
+// never allocates (nullptr when no launch on this device took the word yet).
+static int* device_error_word_if_made() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(g_word_mu);
+  if (dev < 0 || dev >= 64) return nullptr;
+  return g_words[dev];
 }
 
 }  // namespace b200
 
+// The allocation-free GEMM's word is read first and without allocating; the
+// shared word is read only if a launch on this device already made it, so a
+// process that only calls b200_gemm_noalloc never allocates here either.
 extern "C" int b200_device_error(int clear) {
-  int* w = b200::device_error_word();
-  if (!w) return -1;
-  int v = 0;
-  if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
-  if (clear && v) cudaMemset(w, 0, sizeof(int));
   const int v2 = b200::noalloc_error_take(clear);
-  if (v2 < 0) return -1;
-  return v ? v : v2;
+  int v = 0;
+  if (int* w = b200::device_error_word_if_made()) {
+    if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (clear && v) cudaMemset(w, 0, sizeof(int));
+  }
+  if (v) return v;
+  return v2;
 }

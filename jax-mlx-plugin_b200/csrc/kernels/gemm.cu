@@ -799,6 +799,12 @@ struct Scratch {
   // kernels in stream order).
   int get_owned(size_t bytes, cudaStream_t st, void** out) {
     const size_t rounded = (bytes + 255) / 256 * 256;
+    // Under b200_gemm_noalloc the only memory is the fixed array: a path that
+    // would need any other buffer is refused, never served by an allocation.
+    if (lent)
+      return set_error(B200_ERR_UNSUPPORTED,
+                       "gemm_noalloc: this operand layout needs a workspace buffer beyond the "
+                       "fixed split-K array");
     if (query) {
       queried += rounded;
       *out = reinterpret_cast<void*>((uintptr_t)4096);  // encodes descriptors; never launched
@@ -1591,6 +1597,11 @@ extern "C" int b200_gemm_noalloc(const void* a, const void* b, void* c, const vo
                                  int64_t sAm, int64_t sAk, int64_t sBb, int64_t sBk, int64_t sBn,
                                  int64_t ldc, float alpha, int in_dtype, int out_dtype,
                                  int epilogue, void* stream) {
+  if (in_dtype != B200_DT_F32 && in_dtype != B200_DT_BF16)
+    return b200::set_error(B200_ERR_UNSUPPORTED,
+                           "gemm_noalloc: in_dtype must be F32 or BF16 (the mixed F32 x BF16 codes "
+                           "need a widened or split copy of an operand, which this entry point "
+                           "cannot allocate)");
   b200::NoAllocDevice nd;
   if (int rc = b200::noalloc_device(&nd)) return rc;
   b200::Scratch scratch;

@@ -122,6 +122,8 @@ KVGetArgs = _struct("KVGetArgs", [("key", C.c_char_p), ("key_size", C.c_size_t),
 KVPutArgs = _struct("KVPutArgs", [("key", C.c_char_p), ("key_size", C.c_size_t),
                                   ("value", C.c_void_p), ("value_size", C.c_size_t),
                                   ("callback_error", C.c_void_p), ("user_arg", C.c_void_p)])
+# PJRT_CallbackError: the error constructor the plugin passes in each KV call
+CALLBACK_ERROR = C.CFUNCTYPE(C.c_void_p, C.c_int, C.c_char_p, C.c_size_t)
 KV_GET_CB = C.CFUNCTYPE(C.c_void_p, C.POINTER(KVGetArgs))
 KV_PUT_CB = C.CFUNCTYPE(C.c_void_p, C.POINTER(KVPutArgs))
 VALUE_DELETER = C.CFUNCTYPE(None, C.c_void_p)
@@ -420,10 +422,23 @@ def kv_callbacks(store):
 
     del_cb = VALUE_DELETER(deleter)
 
+    def fail(a, exc):
+        """A store failure as a PJRT error made by the plugin's callback_error
+        (DEADLINE_EXCEEDED for a timeout, UNKNOWN otherwise); without one the
+        value stays unset, which the plugin also reports as a failed get."""
+        if not a.callback_error:
+            return None
+        make = C.cast(a.callback_error, C.POINTER(CALLBACK_ERROR))[0]
+        msg = f"{type(exc).__name__}: {exc}".encode()
+        return make(4 if isinstance(exc, TimeoutError) else 2, msg, len(msg))
+
     def kv_get(args):
         a = args.contents
         key = C.string_at(a.key, a.key_size).decode()
-        val = store.get(key)
+        try:
+            val = store.get(key)
+        except Exception as exc:  # noqa: BLE001 -- reported to the plugin
+            return fail(a, exc)
         buf = C.create_string_buffer(val, len(val))
         addr = C.addressof(buf)
         values[addr] = buf
@@ -434,7 +449,10 @@ def kv_callbacks(store):
     def kv_put(args):
         a = args.contents
         key = C.string_at(a.key, a.key_size).decode()
-        store.set(key, C.string_at(a.value, a.value_size))
+        try:
+            store.set(key, C.string_at(a.value, a.value_size))
+        except Exception as exc:  # noqa: BLE001
+            return fail(a, exc)
         return None
 
     get_cb, put_cb = KV_GET_CB(kv_get), KV_PUT_CB(kv_put)
@@ -552,6 +570,29 @@ class Client:
         if self.handle:
             api().call("Client_Destroy", client=self.handle)
             self.handle = None
+
+
+def kv_exchange(store, rank: int, key: str, value: bytes = b"") -> bytes:
+    """The plugin's NCCL-id exchange over `store` without a device
+    (b200_pjrt_kv_exchange): rank 0 puts `value` under `key`, any other rank
+    gets it.  Raises PjrtError with the plugin's code when the store fails."""
+    lib = api().lib
+    fn = lib.b200_pjrt_kv_exchange
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t,
+                                      C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]
+    fn.restype = C.c_int
+    lib.b200_pjrt_free.argtypes = [C.c_void_p]
+    get_cb, put_cb, keep = kv_callbacks(store)
+    out, n = C.c_void_p(), C.c_size_t(0)
+    k = key.encode()
+    rc = fn(C.cast(get_cb, C.c_void_p), None, C.cast(put_cb, C.c_void_p), None, rank, k, len(k),
+            value, len(value), C.byref(out), C.byref(n))
+    res = C.string_at(out.value, n.value)
+    lib.b200_pjrt_free(out)
+    del keep
+    if rc:
+        raise PjrtError(rc, res.decode(errors="replace"))
+    return res
 
 
 def inspect(mlir_text, what: int = 1) -> str:

@@ -195,3 +195,70 @@ def test_bench_reference_arm_prints_once_under_torchrun():
     line = lines[0]
     assert line["impl"] == "reference" and line["n_gpus"] == WORLD and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["cores"] >= 1
+
+
+class _DictStore:
+    def __init__(self):
+        self.d = {}
+
+    def set(self, k, v):
+        self.d[k] = bytes(v)
+
+    def get(self, k):
+        if k not in self.d:
+            raise TimeoutError(f"key {k} not set within the store's timeout")
+        return self.d[k]
+
+
+def test_kv_exchange_round_trip_through_plugin():
+    """The plugin's NCCL-id exchange (rank 0 puts, others get) through the
+    Python callbacks: 128 bytes with zeros arrive unchanged."""
+    from jax_b200 import pjrt
+    st = _DictStore()
+    uid = _uid()
+    assert pjrt.kv_exchange(st, 0, UID_KEY, uid) == uid
+    assert st.d[UID_KEY] == uid
+    assert pjrt.kv_exchange(st, 1, UID_KEY) == uid
+
+
+def test_kv_store_errors_become_pjrt_errors_with_their_code():
+    """jaxlib's KV wrappers report a failed store call by building the error
+    through args->callback_error; the plugin must hand them a constructor and
+    turn the returned object into a PJRT error (here DEADLINE_EXCEEDED for a
+    get that timed out, UNKNOWN for a put that raised)."""
+    from jax_b200 import pjrt
+
+    class PutFails(_DictStore):
+        def set(self, k, v):
+            raise ConnectionError("store gone")
+
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.kv_exchange(_DictStore(), 1, UID_KEY)
+    assert e.value.code == 4 and UID_KEY in str(e.value) and "TimeoutError" in str(e.value)
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.kv_exchange(PutFails(), 0, UID_KEY, b"x")
+    assert e.value.code == 2 and "store gone" in str(e.value)
+
+
+def test_raw_kv_callback_error_keeps_its_code():
+    """A C-level get callback, as jaxlib writes it: on failure it returns
+    (*args->callback_error)(NOT_FOUND, msg, n) and the plugin reports code 5."""
+    from jax_b200 import pjrt
+    lib = pjrt.api().lib
+    msg = b"no such key"
+
+    def raw_get(args):
+        a = args.contents
+        assert a.callback_error, "plugin passed no callback_error"
+        make = C.cast(a.callback_error, C.POINTER(pjrt.CALLBACK_ERROR))[0]
+        return make(5, msg, len(msg))
+
+    cb = pjrt.KV_GET_CB(raw_get)
+    fn = lib.b200_pjrt_kv_exchange
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t,
+                                      C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]
+    out, n = C.c_void_p(), C.c_size_t(0)
+    rc = fn(C.cast(cb, C.c_void_p), None, None, None, 1, b"k", 1, None, 0, C.byref(out), C.byref(n))
+    text = C.string_at(out.value, n.value).decode()
+    lib.b200_pjrt_free(out)
+    assert rc == 5 and "no such key" in text
