@@ -1,0 +1,85 @@
+"""One rank of the two-process data-parallel GPU tests (tests/test_dp_gpu.py),
+launched by torchrun exactly as bench.py's ranks are: a gloo process group
+for the host side, the PJRT client on GPU LOCAL_RANK with node_id / num_nodes
+and the key-value callbacks over the process group's store (rank 0 publishes
+the NCCL unique id there), and the `num_replicas=2` step on this rank's half
+of the batch.
+
+    python -m torch.distributed.run --nproc-per-node=2 ... dp_rank_worker.py OUT KIND
+
+KIND is "mlp" (configs[2], SGD step) or "transformer" (configs[3]
+architecture at reduced size, gradients).  Writes OUT/rank<r>.npz with the
+outputs, or OUT/rank<r>.err with "<code> <message>" when Execute raises a
+PJRT error; OUT/rank<r>.stage names the last stage reached."""
+import os
+import sys
+from datetime import timedelta
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path[:0] = [HERE, ROOT, os.path.join(ROOT, "jax-mlx-plugin_b200")]
+
+
+def main():
+    out, kind = sys.argv[1], sys.argv[2]
+    rank = int(os.environ["RANK"])
+    local = int(os.environ["LOCAL_RANK"])
+
+    def stage(s):
+        with open(os.path.join(out, f"rank{rank}.stage"), "w") as f:
+            f.write(s)
+
+    stage("init")
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+    store = dist.distributed_c10d._get_default_store()
+
+    class KV:
+        def set(self, k, v):
+            store.set(k, v)
+
+        def get(self, k):
+            return bytes(store.get(k))
+
+    from jax_b200 import pjrt, programs
+    from test_dp_gpu import TR_SMALL, _kink_safe_mlp, _to_np, _tr_inputs
+    stage("client")
+    client = pjrt.Client({"visible_devices": [local], "node_id": rank, "num_nodes": 2}, kv=KV())
+    dev = client.addressable_devices[0]
+    stage("compile")
+    if kind == "mlp":
+        dims = (784, 1024, 1024, 1024, 10)
+        params, x, lab = _kink_safe_mlp(np.random.default_rng(53), dims, 1024)
+        sl = slice(512 * rank, 512 * (rank + 1))
+        exe = client.compile(programs.mlp_step(batch=512, dims=dims, num_replicas=2))
+        arrays = params + [x[sl], lab[sl]]
+        bf16 = 0
+    else:
+        names, params, zeros, count, tok, tgt = _tr_inputs(TR_SMALL, 54)
+        sl = slice(2 * rank, 2 * (rank + 1))
+        exe = client.compile(programs.transformer_step(**dict(TR_SMALL, batch=2), num_replicas=2,
+                                                       emit="grads"))
+        arrays = [pjrt.to_bf16_bits(p) for p in params] + zeros + zeros + [count, tok[sl], tgt[sl]]
+        bf16 = len(params)
+    args = [client.buffer_from_numpy(a, device=dev, bf16=i < bf16) for i, a in enumerate(arrays)]
+    stage("execute")
+    try:
+        outs = exe.execute([args])[0]
+        stage("read")
+        res = [_to_np(o) for o in outs]
+        np.savez(os.path.join(out, f"rank{rank}.npz"), *res)
+    except pjrt.PjrtError as e:
+        with open(os.path.join(out, f"rank{rank}.err"), "w") as f:
+            f.write(f"{e.code} {e}")
+    stage("barrier")
+    dist.barrier()
+    stage("done")
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -10,7 +10,8 @@ must end with the full-batch step.  Two launch forms:
   lists);
 * one process per GPU, as `bench.py` runs under torchrun (ncclCommInitRank
   with the unique id published by rank 0 through the client's key-value
-  callbacks over a torch.distributed TCPStore).  The `nccl_init` fault point
+  callbacks over the gloo process group's store; tests/dp_rank_worker.py
+  under torchrun).  The `nccl_init` fault point
   (B200_FAULT) is exercised here: both ranks get the injected UNAVAILABLE
   error from Execute, raised on the host before any collective starts.
 
@@ -18,7 +19,6 @@ Tolerances: contractions 2e-3 relative (elementwise on kink-safe inputs,
 normwise on the configuration's own Glorot / U(0,1) inputs); bf16 transformer
 gradients 3e-2 normwise against the excess-precision interpreter, as in the
 one-device tests.  Skipped with fewer than two GPUs."""
-import multiprocessing as mp
 import os
 import socket
 import sys
@@ -202,75 +202,25 @@ def test_dp2_transformer_grads_match_full_batch(client):
 
 
 # ------------------------------------------------- one process per GPU ----
-def _free_port():
+def _run_ranks(tmp_path, kind, fault=""):
+    """torchrun, two ranks, each running tests/dp_rank_worker.py as bench.py
+    runs its ranks.  Each rank records the stage it reached, so that a rank
+    that does not finish in time says where it stopped."""
+    import subprocess
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", B200_KV_TIMEOUT_MS="60000")
+    env.pop("B200_FAULT", None)
+    if fault:
+        env["B200_FAULT"] = fault
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-class _StoreKV:
-    def __init__(self, store):
-        self.store = store
-
-    def set(self, k, v):
-        self.store.set(k, v)
-
-    def get(self, k):
-        return bytes(self.store.get(k))
-
-
-def _rank_worker(rank, port, out, kind, fault):
-    """One rank: its own PJRT client on GPU `rank`, NCCL bootstrap through the
-    KV callbacks, the num_replicas=2 step on its half of the batch."""
-    sys.path[:0] = [ROOT, os.path.join(ROOT, "jax-mlx-plugin_b200")]
-    os.environ["NCCL_NVLS_ENABLE"] = "0"
-    if fault:
-        os.environ["B200_FAULT"] = fault
-    from datetime import timedelta
-    import torch.distributed as dist
-    from jax_b200 import pjrt as P, programs as G
-    store = dist.TCPStore("127.0.0.1", port, 2, rank == 0, timeout=timedelta(seconds=60))
-    client = P.Client({"visible_devices": [rank], "node_id": rank, "num_nodes": 2}, kv=_StoreKV(store))
-    dev = client.addressable_devices[0]
-    try:
-        if kind == "mlp":
-            dims = (784, 1024, 1024, 1024, 10)
-            params, x, lab = _kink_safe_mlp(np.random.default_rng(53), dims, 1024)
-            sl = slice(512 * rank, 512 * (rank + 1))
-            exe = client.compile(G.mlp_step(batch=512, dims=dims, num_replicas=2))
-            args = [client.buffer_from_numpy(a, device=dev) for a in params + [x[sl], lab[sl]]]
-            res = [o.to_numpy() for o in exe.execute([args])[0]]
-        else:
-            names, params, zeros, count, tok, tgt = _tr_inputs(TR_SMALL, 54)
-            sl = slice(2 * rank, 2 * (rank + 1))
-            exe = client.compile(G.transformer_step(**dict(TR_SMALL, batch=2), num_replicas=2,
-                                                    emit="grads"))
-            args = ([client.buffer_from_numpy(P.to_bf16_bits(p), device=dev, bf16=True) for p in params] +
-                    [client.buffer_from_numpy(a, device=dev) for a in zeros + zeros + [count, tok[sl], tgt[sl]]])
-            res = [_to_np(o) for o in exe.execute([args])[0]]
-        np.savez(os.path.join(out, f"rank{rank}.npz"), *res)
-    except P.PjrtError as e:
-        with open(os.path.join(out, f"rank{rank}.err"), "w") as f:
-            f.write(f"{e.code} {e}")
-    store.set(f"done{rank}", b"1")
-    store.wait([f"done{1 - rank}"])  # rank 0 keeps the store up until both are done
-    client.destroy()
-
-
-def _run_ranks(tmp_path, kind, fault=""):
-    ctx = mp.get_context("spawn")
-    port = _free_port()
-    ps = [ctx.Process(target=_rank_worker, args=(r, port, str(tmp_path), kind, fault)) for r in range(2)]
-    for p in ps:
-        p.start()
-    for p in ps:
-        p.join(300)
-    alive = [p for p in ps if p.is_alive()]
-    for p in alive:
-        p.kill()
-        p.join()
-    assert not alive, "a rank did not finish within 300 s"
-    assert [p.exitcode for p in ps] == [0, 0]
+        port = s.getsockname()[1]
+    cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+           os.path.join(ROOT, "tests", "dp_rank_worker.py"), str(tmp_path), kind]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    stages = {rk: (tmp_path / f"rank{rk}.stage").read_text() if (tmp_path / f"rank{rk}.stage").exists()
+              else "not started" for rk in range(2)}
+    assert r.returncode == 0, f"ranks failed (rc {r.returncode}), stages {stages}: {r.stderr[-3000:]}"
 
 
 @needs2
