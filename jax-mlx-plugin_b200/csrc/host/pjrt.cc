@@ -323,7 +323,10 @@ void kv_put(PJRT_Client* c, const std::string& key, const std::string& val) {
 // JAX hands the plugin a StableHLO portable artifact (MLIR bytecode).  As in
 // the reference (src/jax_mlx_pjrt.cpp:671-830) it is turned into text through
 // the MLIR/StableHLO C API that jaxlib has loaded in this process.
-std::string bytecode_to_text(const std::string& code) {
+// Path 1: the MLIR / StableHLO C API, when some library in the process exports
+// it (Reactant.jl does; reference src/jax_mlx_pjrt.cpp:671-745).  Returns false
+// when the API is not loaded.
+bool bytecode_via_c_api(const std::string& code, std::string* out) {
   struct StrRef { const char* data; size_t length; };
   struct Handle { void* ptr; };
   using CtxCreate = Handle (*)();
@@ -341,10 +344,7 @@ std::string bytecode_to_text(const std::string& code) {
   auto print = (Print)dlsym(self, "mlirOperationPrint");
   auto moddel = (ModDestroy)dlsym(self, "mlirModuleDestroy");
   auto reg = (Register)dlsym(self, "stablehloRegisterAllDialects");
-  if (!deser || !ctxc || !getop || !print)
-    throw PjrtErr(12,
-                  "program is MLIR bytecode but the StableHLO C API is not loaded in this "
-                  "process; pass StableHLO text (format \"mlir\") instead");
+  if (!deser || !ctxc || !getop || !print) return false;
   Handle ctx = ctxc();
   if (reg) reg(ctx);
   Handle mod = deser(StrRef{code.data(), code.size()}, ctx);
@@ -352,12 +352,116 @@ std::string bytecode_to_text(const std::string& code) {
     if (ctxd) ctxd(ctx);
     throw PjrtErr(3, "failed to deserialize the StableHLO portable artifact");
   }
-  std::string out;
   print(getop(mod), [](StrRef s, void* u) { static_cast<std::string*>(u)->append(s.data, s.length); },
-        &out);
+        out);
   if (moddel) moddel(mod);
   if (ctxd) ctxd(ctx);
-  return out;
+  return true;
+}
+
+// Path 2: jaxlib's Python bindings, when the plugin lives in a Python process
+// (the `jax.jit` case; reference src/jax_mlx_pjrt.cpp:747-822).  The CPython
+// entry points are looked up in the process (a Python executable exports
+// them), so the plugin does not link against libpython.  Under the GIL:
+//   ctx = jax._src.interpreters.mlir.make_ir_context()
+//   module = jaxlib.mlir._mlir_libs._stablehlo.deserialize_portable_artifact(ctx, code)
+//   text = str(module)
+// Returns false when Python is not running or either module cannot be
+// imported; a deserializer that raises is an INVALID_ARGUMENT error.
+bool bytecode_via_python(const std::string& code, std::string* out) {
+  using Obj = void*;
+  struct Py {
+    int (*IsInitialized)();
+    int (*GILEnsure)();
+    void (*GILRelease)(int);
+    Obj (*Import)(const char*);
+    Obj (*GetAttr)(Obj, const char*);
+    Obj (*CallObject)(Obj, Obj);
+    Obj (*Bytes)(const char*, ssize_t);
+    Obj (*Tuple)(ssize_t, ...);
+    Obj (*Str)(Obj);
+    const char* (*Utf8)(Obj, ssize_t*);
+    void (*DecRef)(Obj);
+    void (*Fetch)(Obj*, Obj*, Obj*);
+    void (*Clear)();
+  };
+  static const Py py = [] {
+    Py p{};
+    auto sym = [](const char* n) { return dlsym(RTLD_DEFAULT, n); };
+    p.IsInitialized = (int (*)())sym("Py_IsInitialized");
+    p.GILEnsure = (int (*)())sym("PyGILState_Ensure");
+    p.GILRelease = (void (*)(int))sym("PyGILState_Release");
+    p.Import = (Obj(*)(const char*))sym("PyImport_ImportModule");
+    p.GetAttr = (Obj(*)(Obj, const char*))sym("PyObject_GetAttrString");
+    p.CallObject = (Obj(*)(Obj, Obj))sym("PyObject_CallObject");
+    p.Bytes = (Obj(*)(const char*, ssize_t))sym("PyBytes_FromStringAndSize");
+    p.Tuple = (Obj(*)(ssize_t, ...))sym("PyTuple_Pack");
+    p.Str = (Obj(*)(Obj))sym("PyObject_Str");
+    p.Utf8 = (const char* (*)(Obj, ssize_t*))sym("PyUnicode_AsUTF8AndSize");
+    p.DecRef = (void (*)(Obj))sym("Py_DecRef");
+    p.Fetch = (void (*)(Obj*, Obj*, Obj*))sym("PyErr_Fetch");
+    p.Clear = (void (*)())sym("PyErr_Clear");
+    return p;
+  }();
+  if (!py.IsInitialized || !py.GILEnsure || !py.GILRelease || !py.Import || !py.GetAttr ||
+      !py.CallObject || !py.Bytes || !py.Tuple || !py.Str || !py.Utf8 || !py.DecRef ||
+      !py.Fetch || !py.Clear || !py.IsInitialized())
+    return false;
+  const int gil = py.GILEnsure();
+  std::vector<Obj> held;  // released (in reverse) before the GIL
+  auto keep = [&](Obj o) { if (o) held.push_back(o); return o; };
+  auto py_error = [&]() {
+    Obj t = nullptr, v = nullptr, tb = nullptr;
+    py.Fetch(&t, &v, &tb);
+    std::string msg = "unknown Python error";
+    if (v) {
+      if (Obj s = py.Str(v)) {
+        ssize_t n = 0;
+        if (const char* c = py.Utf8(s, &n)) msg.assign(c, (size_t)n);
+        py.DecRef(s);
+      }
+    }
+    for (Obj o : {t, v, tb}) if (o) py.DecRef(o);
+    py.Clear();
+    return msg;
+  };
+  bool ok = false;
+  std::string failure;
+  do {
+    Obj mlir = keep(py.Import("jax._src.interpreters.mlir"));
+    Obj shlo = mlir ? keep(py.Import("jaxlib.mlir._mlir_libs._stablehlo")) : nullptr;
+    if (!mlir || !shlo) { py.Clear(); break; }  // no jax in this process
+    Obj make_ctx = keep(py.GetAttr(mlir, "make_ir_context"));
+    Obj deser = keep(py.GetAttr(shlo, "deserialize_portable_artifact"));
+    if (!make_ctx || !deser) { py.Clear(); break; }
+    Obj ctx = keep(py.CallObject(make_ctx, nullptr));
+    if (!ctx) { failure = "make_ir_context() raised: " + py_error(); break; }
+    Obj bytes = keep(py.Bytes(code.data(), (ssize_t)code.size()));
+    Obj args = bytes ? keep(py.Tuple(2, ctx, bytes)) : nullptr;
+    Obj module = args ? keep(py.CallObject(deser, args)) : nullptr;
+    if (!module) { failure = "deserialize_portable_artifact raised: " + py_error(); break; }
+    Obj text = keep(py.Str(module));
+    ssize_t n = 0;
+    const char* c = text ? py.Utf8(text, &n) : nullptr;
+    if (!c) { failure = "str(module) failed: " + py_error(); break; }
+    out->assign(c, (size_t)n);
+    ok = true;
+  } while (false);
+  for (auto it = held.rbegin(); it != held.rend(); ++it) py.DecRef(*it);
+  py.GILRelease(gil);
+  if (!failure.empty()) throw PjrtErr(3, "StableHLO portable artifact: " + failure);
+  return ok;
+}
+
+// JAX hands the plugin a StableHLO portable artifact (MLIR bytecode); it is
+// turned into text by whichever MLIR front end the process has loaded.
+std::string bytecode_to_text(const std::string& code) {
+  std::string out;
+  if (bytecode_via_c_api(code, &out)) return out;
+  if (bytecode_via_python(code, &out)) return out;
+  throw PjrtErr(12,
+                "program is MLIR bytecode but neither the StableHLO C API nor jaxlib's Python "
+                "bindings are loaded in this process; pass StableHLO text (format \"mlir\") instead");
 }
 
 // Minimal protobuf walk: CompileOptionsProto.executable_build_options (3)

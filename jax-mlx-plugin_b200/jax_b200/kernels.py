@@ -11,8 +11,9 @@ from __future__ import annotations
 import ctypes as C
 import os
 
-_HERE = os.path.dirname(os.path.abspath(__file__))
-KERNELS_LIB = os.path.join(os.path.dirname(_HERE), "lib", "libb200_kernels.so")
+from .pjrt import LIB_DIR
+
+KERNELS_LIB = os.path.join(LIB_DIR, "libb200_kernels.so")
 
 DT_PRED, DT_S32, DT_U32, DT_F32, DT_BF16 = 1, 4, 8, 11, 13
 

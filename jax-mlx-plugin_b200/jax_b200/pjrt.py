@@ -17,7 +17,10 @@ from typing import Callable, Dict, List, Optional, Sequence
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_DIR = os.path.join(os.path.dirname(_HERE), "lib")
+# In-tree builds put the libraries in ../lib (csrc/Makefile); a wheel built with
+# `make -C csrc LIB=../jax_b200/lib` carries them inside the package.
+LIB_DIR = (os.path.join(_HERE, "lib") if os.path.exists(os.path.join(_HERE, "lib", "libb200_pjrt.so"))
+           else os.path.join(os.path.dirname(_HERE), "lib"))
 PJRT_LIB = os.path.join(LIB_DIR, "libb200_pjrt.so")
 
 # PJRT_Api function-pointer slots, in ABI (v0.90) order.  Must match

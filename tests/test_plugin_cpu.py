@@ -387,3 +387,154 @@ def test_backward_custom_calls_expand_to_kernels():
     plan = pjrt.inspect(programs.layer_norm_custom_calls(), 1)
     steps = plan.split("steps:")[1]
     assert "layer_norm " in steps and "_reduce" in steps
+
+
+def test_portable_artifact_through_jaxlib_python_bindings(monkeypatch):
+    """In a Python process with jaxlib (the `jax.jit` case) the plugin turns a
+    portable artifact into text through jaxlib's own bindings, under the GIL:
+    jax._src.interpreters.mlir.make_ir_context() and
+    jaxlib.mlir._mlir_libs._stablehlo.deserialize_portable_artifact(ctx, code).
+    Stub modules stand in for jaxlib here: the stub deserializer hands back the
+    StableHLO text of the LayerNorm program for one artifact and raises for
+    another, which the plugin reports as INVALID_ARGUMENT with the message."""
+    import sys
+    import types
+    text = programs.layer_norm(64, 256)
+    artifact = b"ML\xefR\x00vhlo-portable-artifact-1"
+    seen = {}
+
+    class Module:
+        def __init__(self, s):
+            self.s = s
+
+        def __str__(self):
+            return self.s
+
+    def make_ir_context():
+        seen["ctx"] = seen.get("ctx", 0) + 1
+        return object()
+
+    def deserialize_portable_artifact(ctx, code):
+        seen["code"] = bytes(code)
+        if code == artifact:
+            return Module(text)
+        raise ValueError("unsupported VHLO version")
+
+    mods = {}
+    for name in ("jax", "jax._src", "jax._src.interpreters", "jaxlib", "jaxlib.mlir",
+                 "jaxlib.mlir._mlir_libs"):
+        mods[name] = types.ModuleType(name)
+    mods["jax._src.interpreters.mlir"] = types.ModuleType("jax._src.interpreters.mlir")
+    mods["jax._src.interpreters.mlir"].make_ir_context = make_ir_context
+    mods["jaxlib.mlir._mlir_libs._stablehlo"] = types.ModuleType("jaxlib.mlir._mlir_libs._stablehlo")
+    mods["jaxlib.mlir._mlir_libs._stablehlo"].deserialize_portable_artifact = deserialize_portable_artifact
+    for name, m in mods.items():
+        monkeypatch.setitem(sys.modules, name, m)
+    graph = pjrt.inspect(artifact, 0)
+    assert "fused_layer_norm" in graph and seen["code"] == artifact and seen["ctx"] == 1
+    with pytest.raises(pjrt.PjrtError) as e:
+        pjrt.inspect(b"ML\xefR\x00other", 0)
+    assert e.value.code == 3 and "unsupported VHLO version" in str(e.value)
+
+
+def _stub_jax(monkeypatch):
+    """Stand-ins for the parts of jax that plugin.initialize() touches, which
+    record what the plugin registers."""
+    import sys
+    import types
+    rec = {"plugins": [], "lowerings": [], "calls": []}
+
+    class Primitive:
+        def __init__(self, name):
+            self.name, self.multiple_results = name, False
+
+        def def_abstract_eval(self, f):
+            self.abstract = f
+
+        def def_impl(self, f):
+            self.impl = f
+
+    class ShapedArray:
+        def __init__(self, shape, dtype):
+            self.shape, self.dtype = shape, dtype
+
+    class Result:
+        def __init__(self, n):
+            self.results = [f"r{i}" for i in range(n)]
+
+    def custom_call(call_target_name, result_types, operands, backend_config):
+        rec["calls"].append((call_target_name, list(result_types), list(operands), backend_config))
+        return Result(len(result_types))
+
+    mods = {n: types.ModuleType(n) for n in ("jax", "jax._src", "jax._src.interpreters")}
+    core = mods["jax._src.core"] = types.ModuleType("jax._src.core")
+    core.Primitive, core.ShapedArray = Primitive, ShapedArray
+    xb = mods["jax._src.xla_bridge"] = types.ModuleType("jax._src.xla_bridge")
+    xb.register_plugin = lambda name, library_path=None: rec["plugins"].append((name, library_path))
+    mlir = mods["jax._src.interpreters.mlir"] = types.ModuleType("jax._src.interpreters.mlir")
+    mlir.register_lowering = lambda prim, fn, platform=None: rec["lowerings"].append((prim, fn, platform))
+    mlir.aval_to_ir_type = lambda aval: f"type{tuple(aval.shape)}"
+    mlir.custom_call = custom_call
+    mlir.lower_fun = lambda fn, multiple_results: ("lower_fun", fn, multiple_results)
+    mods["jax"]._src = mods["jax._src"]
+    mods["jax._src"].core, mods["jax._src"].xla_bridge = core, xb
+    mods["jax._src"].interpreters = mods["jax._src.interpreters"]
+    mods["jax._src.interpreters"].mlir = mlir
+    for n, m in mods.items():
+        monkeypatch.setitem(sys.modules, n, m)
+    monkeypatch.delitem(sys.modules, "jax_mlx", raising=False)
+    return rec
+
+
+def test_plugin_initialize_registers_platform_and_four_lowerings(monkeypatch):
+    """initialize() against stub jax modules: the library is registered as
+    platform "b200", and the four fused-op primitives get custom-call
+    lowerings for "b200" (plus plain-JAX lowerings elsewhere) whose call
+    targets, operands, result types and backend_config JSON are the
+    reference's (src/jax_mlx/sdpa.py:97-135, layer_norm.py:86-122)."""
+    from jax_b200 import custom_calls, plugin
+    rec = _stub_jax(monkeypatch)
+    monkeypatch.setattr(custom_calls, "_PRIMS", {})
+    plugin.initialize()
+    assert rec["plugins"] == [("b200", pjrt.PJRT_LIB)]
+    b200 = {p.name: fn for p, fn, plat in rec["lowerings"] if plat == "b200"}
+    other = {p.name: fn for p, fn, plat in rec["lowerings"] if plat is None}
+    assert sorted(b200) == sorted(other) == sorted(custom_calls.TARGETS)
+    assert other["mlx_sdpa_bwd"][2] is True and other["mlx_sdpa"][2] is False
+
+    class Aval:
+        def __init__(self, *shape):
+            self.shape, self.dtype = shape, "float32"
+
+    class Ctx:
+        def __init__(self, n, shape):
+            self.avals_out = [Aval(*shape)] * n
+
+    qkv = (2, 128, 2, 64)
+    assert b200["mlx_sdpa"](Ctx(1, qkv), "q", "k", "v", scale=0.125) == ["r0"]
+    assert b200["mlx_sdpa_bwd"](Ctx(3, qkv), "q", "k", "v", "g", scale=0.125) == ["r0", "r1", "r2"]
+    assert b200["mlx_layer_norm"](Ctx(1, (8, 512)), "x", "w", "b", eps=1e-05) == ["r0"]
+    b200["mlx_layer_norm_bwd"](Ctx(3, (8, 512)), "x", "w", "b", "dy", eps=1e-05)
+    assert rec["calls"] == [
+        ("mlx_sdpa", ["type(2, 128, 2, 64)"], ["q", "k", "v"], '{"scale": 0.125}'),
+        ("mlx_sdpa_bwd", ["type(2, 128, 2, 64)"] * 3, ["q", "k", "v", "g"], '{"scale": 0.125}'),
+        ("mlx_layer_norm", ["type(8, 512)"], ["x", "w", "b"], '{"eps": 1e-05}'),
+        ("mlx_layer_norm_bwd", ["type(8, 512)"] * 3, ["x", "w", "b", "dy"], '{"eps": 1e-05}'),
+    ]
+    prims = custom_calls.primitives()
+    assert prims["mlx_sdpa_bwd"].multiple_results and not prims["mlx_sdpa"].multiple_results
+    out = prims["mlx_sdpa"].abstract(Aval(*qkv), Aval(*qkv), Aval(*qkv), scale=0.125)
+    assert out.shape == qkv
+
+
+def test_package_declares_jax_plugins_entry_point():
+    """pyproject.toml declares the entry point JAX scans (jax_plugins), and it
+    names a module with initialize()."""
+    import importlib
+    import tomllib
+    with open(os.path.join(ROOT, "jax-mlx-plugin_b200", "pyproject.toml"), "rb") as f:
+        meta = tomllib.load(f)
+    eps = meta["project"]["entry-points"]["jax_plugins"]
+    assert eps == {"b200": "jax_b200.plugin"}
+    mod = importlib.import_module(eps["b200"])
+    assert callable(mod.initialize) and mod.PLATFORM == "b200"
