@@ -51,6 +51,13 @@ class CodeGen {
   // reduced range is divided over gridDim.y blocks and out_slots receive
   // [split, OUT] partials, combined by reduce_partials.
   GenKernel reduce(int node, const std::vector<int>& out_slots, int split = 1);
+  // A reduction that keeps the input's innermost dimension (a bias or norm-gain
+  // gradient: sum over tokens of [tokens, features]) is emitted with each
+  // thread owning this many consecutive outputs, read as one vector load per
+  // operand and row: 8 or 4 when the innermost dimension splits into such
+  // groups, else 1 (one output per thread).
+  static int column_vec(const TensorType& in, const std::vector<int64_t>& reduce_dims);
+  static constexpr int kColWarps = 8;  // warps (rows in flight) per block of a vector column reduction
   GenKernel reduce_partials(int node, const std::vector<int>& partial_slots,
                             const std::vector<int>& out_slots, int split);
   GenKernel reduce_window(int node, const std::vector<int>& out_slots);
@@ -157,6 +164,10 @@ class CodeGen {
                           std::vector<std::string>* outs);
   std::string header(const std::string& name);
   GenKernel finish(const std::string& name, int64_t total, int64_t block, int64_t max_grid);
+  GenKernel reduce_columns(int node, const std::vector<int>& out_slots, int split,
+                           const std::string& name, const std::vector<std::string>& outp,
+                           const std::vector<int64_t>& kdims, const std::vector<int64_t>& rdims,
+                           const std::vector<int64_t>& kpos, const std::vector<int64_t>& rpos);
 };
 
 std::string ctype(DType t);     // register type

@@ -267,6 +267,18 @@ struct Builder {
     int64_t OUT = 1, RED = 1;
     for (int d = 0; d < it.rank(); ++d) (red.count(d) ? RED : OUT) *= it.dims[d];
     const bool rowlike = it.rank() > 0 && red.count(it.rank() - 1);
+    const int cv = rowlike ? 1 : CodeGen::column_vec(it, nd.dims);
+    if (cv > 1) {
+      // vector column reduction: blocks of kColWarps warps over 32 * cv
+      // outputs each; split the rows until about 8 blocks per SM, keeping at
+      // least 4 rows per warp and at most 64 partial rows to combine
+      if (RED < 8 * CodeGen::kColWarps) return 1;
+      const int64_t bx = (OUT / cv + 31) / 32;
+      int64_t split = (148 * 8) / std::max<int64_t>(bx, 1);
+      split = std::min<int64_t>(split, RED / (4 * CodeGen::kColWarps));
+      split = std::min<int64_t>(split, 64);
+      return (int)std::max<int64_t>(split, 1);
+    }
     const int64_t threads = rowlike ? OUT * 32 : OUT * (OUT < 148 * 32 * 4 ? 32 : 8);
     if (threads >= 148 * 512 || RED < 8192) return 1;
     int64_t split = (148 * 1024) / std::max<int64_t>(threads, 1);
