@@ -55,7 +55,8 @@ class CodeGen {
   // gradient: sum over tokens of [tokens, features]) is emitted with each
   // thread owning this many consecutive outputs, read as one vector load per
   // operand and row: 8 or 4 when the innermost dimension splits into such
-  // groups, else 1 (one output per thread).
+  // groups and there are at least 32 such groups, else 1 (one output per
+  // thread).
   static int column_vec(const TensorType& in, const std::vector<int64_t>& reduce_dims);
   static constexpr int kColWarps = 8;  // warps (rows in flight) per block of a vector column reduction
   GenKernel reduce_partials(int node, const std::vector<int>& partial_slots,

@@ -97,13 +97,13 @@ PER_LAYER = ("ln1_g", "ln1_b", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo",
              "ln2_g", "ln2_b", "w1", "b1", "w2", "b2")
 
 
-def _ln_bf16(x, g, b, eps=1e-6):
+def _ln_bf16(x, g, b, eps=1e-6, f32=torch.float32):
     """flax LayerNorm on bf16 activations: f32 statistics and affine, bf16 out."""
-    h = x.float()
+    h = x.to(f32)
     mean = h.mean(-1, keepdim=True)
     d = h - mean
     var = (d * d).mean(-1, keepdim=True)
-    return (d * torch.rsqrt(var + eps) * g.float() + b.float()).to(x.dtype)
+    return (d * torch.rsqrt(var + eps) * g.to(f32) + b.to(f32)).to(x.dtype)
 
 
 def _gelu_tanh(x):
@@ -111,38 +111,40 @@ def _gelu_tanh(x):
     return x * ((torch.tanh(inner) + 1.0) * 0.5)
 
 
-def _attention(q, k, v):
+def _attention(q, k, v, f32=torch.float32):
     B, T, N, H = q.shape
-    s = torch.einsum("btnh,bsnh->bnts", q.float(), k.float()) * (1.0 / math.sqrt(H))
+    s = torch.einsum("btnh,bsnh->bnts", q.to(f32), k.to(f32)) * (1.0 / math.sqrt(H))
     tri = torch.ones(T, T, dtype=torch.bool).tril()
-    s = torch.where(tri, s, torch.tensor(-0.7 * F32_MAX))
+    s = torch.where(tri, s, torch.tensor(-0.7 * F32_MAX, dtype=f32))
     p = torch.softmax(s, -1).to(v.dtype)
     return torch.einsum("bnts,bsnh->btnh", p, v)
 
 
-def transformer_loss(P: dict, tokens, targets, layers: int):
-    """Mean next-token cross-entropy (f32) of the pre-LN causal encoder."""
+def transformer_loss(P: dict, tokens, targets, layers: int, f32=torch.float32):
+    """Mean next-token cross-entropy (f32) of the pre-LN causal encoder.  `f32`
+    is the type of the program's f32 values (float64 to evaluate the program
+    with no rounding at all, given float64 parameters)."""
     B, T = tokens.shape
     x = P["tok_emb"][tokens.long()] + P["pos_emb"][None]
     for i in range(layers):
         L = lambda n: P[f"l{i}.{n}"]
-        y = _ln_bf16(x, L("ln1_g"), L("ln1_b"))
+        y = _ln_bf16(x, L("ln1_g"), L("ln1_b"), f32=f32)
         q, k, v = (torch.einsum("btd,dnh->btnh", y, L(w)) + L(bb)
                    for w, bb in (("wq", "bq"), ("wk", "bk"), ("wv", "bv")))
-        att = _attention(q, k, v)
+        att = _attention(q, k, v, f32)
         x = x + (torch.einsum("btnh,nhd->btd", att, L("wo")) + L("bo"))
-        y = _ln_bf16(x, L("ln2_g"), L("ln2_b"))
+        y = _ln_bf16(x, L("ln2_g"), L("ln2_b"), f32=f32)
         f = _gelu_tanh(y @ L("w1") + L("b1"))
         x = x + (f @ L("w2") + L("b2"))
-    y = _ln_bf16(x, P["lnf_g"], P["lnf_b"])
-    logits = (y @ P["w_head"] + P["b_head"]).reshape(B * T, -1).float()
+    y = _ln_bf16(x, P["lnf_g"], P["lnf_b"], f32=f32)
+    logits = (y @ P["w_head"] + P["b_head"]).reshape(B * T, -1).to(f32)
     return _cross_entropy(logits, targets.reshape(-1))
 
 
-def transformer_grads(names: List[str], params, tokens, targets, layers=6):
-    """value_and_grad of transformer_loss: (loss, bf16 gradients)."""
+def transformer_grads(names: List[str], params, tokens, targets, layers=6, f32=torch.float32):
+    """value_and_grad of transformer_loss: (loss, gradients in the parameters' type)."""
     ps = [p.detach().requires_grad_() for p in params]
-    loss = transformer_loss(dict(zip(names, ps)), tokens, targets, layers)
+    loss = transformer_loss(dict(zip(names, ps)), tokens, targets, layers, f32)
     grads = torch.autograd.grad(loss, ps)
     return loss.detach(), grads
 

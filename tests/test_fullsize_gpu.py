@@ -1,0 +1,142 @@
+"""GPU: the three training configurations at their full BASELINE sizes, on
+their own input distributions, against an oracle evaluated on the host.
+
+* configs[2] MLP, batch 1024, Glorot-uniform weights, U(0,1) inputs: loss and
+  every gradient against hand backprop in float64 (oracle/restate.py).
+* configs[4] CNN, batch 256, He-normal kernels, U(0,1) inputs: loss and every
+  gradient against the torch port (oracle/torch_port.py) run in float64.
+* configs[3] transformer, 64 x 256 tokens, 6 blocks, vocab 32000: loss and
+  every gradient against the torch port run in float32 on the same bf16
+  parameter values (no rounding of activations on the host side).
+
+Tolerances: loss 2e-3 relative.  Gradients normwise, because on arbitrary
+floats a ReLU pre-activation within rounding of zero may land on the other
+side of its kink and move the upstream gradients of that one sample (the
+kink-safe elementwise checks are in test_pjrt_gpu.py): 2e-3 for the f32
+programs (contractions); 3e-2 for the bf16 transformer, whose activations the
+plugin stores in bf16 while the oracle keeps them exact (the same bound the
+reduced-size test holds the default compile to).  The transformer's layer-norm
+gains and query / key weights are drawn wider than N(0, 0.02) so that attention
+is not flat and every gradient carries signal; its key-bias gradient, zero in
+exact arithmetic, is bounded against the query-bias gradient instead."""
+import numpy as np
+import pytest
+
+from helpers import assert_close
+from jax_b200 import kernels, pjrt, programs
+from oracle import hlo_interp, restate
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def client():
+    c = pjrt.Client()
+    yield c
+
+
+@pytest.fixture(autouse=True)
+def no_device_error():
+    kernels.device_error(clear=True)
+    yield
+    assert kernels.device_error(clear=True) == 0
+
+
+def _normwise(got, ref, tol, what):
+    g, r = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    assert g.shape == r.shape, f"{what}: shape {g.shape} vs {r.shape}"
+    assert np.isfinite(g).all(), f"{what}: non-finite values"
+    rel = np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-300)
+    assert rel <= tol, f"{what}: normwise difference {rel:.3e} > {tol}"
+    return rel
+
+
+def _run(client, text, arrays, bf16_first=0):
+    exe = client.compile(text)
+    bufs = [client.buffer_from_numpy(pjrt.to_bf16_bits(a), bf16=True) if i < bf16_first
+            else client.buffer_from_numpy(a) for i, a in enumerate(arrays)]
+    outs = []
+    for o in exe.execute([bufs])[0]:
+        a = o.to_numpy()
+        outs.append(pjrt.from_bf16_bits(a) if o.dtype == pjrt.BF16 else a)
+    return outs
+
+
+def test_mlp_full_config_glorot_inputs(client):
+    dims, batch = (784, 1024, 1024, 1024, 10), 1024
+    rng = np.random.default_rng(8)
+    params = []
+    for i in range(len(dims) - 1):
+        lim = np.sqrt(6.0 / (dims[i] + dims[i + 1]))
+        params.append(rng.uniform(-lim, lim, (dims[i], dims[i + 1])).astype(np.float32))
+        params.append(np.zeros(dims[i + 1], np.float32))
+    x = rng.random((batch, dims[0])).astype(np.float32)
+    lab = rng.integers(0, 10, batch).astype(np.int32)
+    got = _run(client, programs.mlp_step(batch=batch, dims=dims, emit="grads"), params + [x, lab])
+    loss, new = restate.mlp_step_ref(params, x, lab, lr=1.0)
+    assert_close(got[0], loss, 2e-3, "mlp loss")
+    for i, (p, g, r) in enumerate(zip(params, got[1:], new)):
+        _normwise(g, p.astype(np.float64) - r, 2e-3, f"mlp grad {i}")
+
+
+def test_cnn_full_batch_against_float64_port(client):
+    from oracle import torch_port as tp
+    rng = np.random.default_rng(15)
+    shapes = [(3, 3, 1, 32), (32,), (3, 3, 32, 64), (64,), (3136, 256), (256,), (256, 10), (10,)]
+    ps = []
+    for s in shapes:
+        if len(s) > 1:
+            ps.append((rng.standard_normal(s) * np.sqrt(2.0 / np.prod(s[:-1]))).astype(np.float32))
+        else:
+            ps.append(np.zeros(s, np.float32))
+    x = rng.random((256, 28, 28, 1)).astype(np.float32)
+    lab = rng.integers(0, 10, 256).astype(np.int32)
+    got = _run(client, programs.cnn_step(batch=256, emit="grads"), ps + [x, lab])
+    t64 = [torch.from_numpy(p).double() for p in ps]
+    loss, new = tp.cnn_step(t64, torch.from_numpy(x).double(), torch.from_numpy(lab), lr=1.0)
+    assert_close(got[0], float(loss), 2e-3, "cnn loss")
+    for i, (p, g, n) in enumerate(zip(t64, got[1:], new)):
+        _normwise(g, (p - n).numpy(), 2e-3, f"cnn grad {i}")
+
+
+def test_transformer_full_config_against_port(client):
+    from oracle import torch_port as tp
+    cfg = dict(batch=64, seq=256, layers=6, d=512, heads=8, ffn=2048, vocab=32000)
+    shapes = programs.transformer_param_shapes(cfg["layers"], cfg["d"], cfg["heads"], cfg["ffn"],
+                                               cfg["vocab"], cfg["seq"])
+    rng = np.random.default_rng(34)
+
+    def init(name, s):
+        leaf = name.split(".")[-1]
+        if leaf.endswith("_g"):
+            return 1 + 0.1 * rng.standard_normal(s)
+        if leaf in ("wq", "wk"):
+            return 0.1 * rng.standard_normal(s)
+        return 0.02 * rng.standard_normal(s)
+    names = [n for n, _ in shapes]
+    params = [hlo_interp.bf16_round(init(n, s).astype(np.float32)) for n, s in shapes]
+    zeros = [np.zeros(s, np.float32) for _, s in shapes]
+    tok = rng.integers(0, cfg["vocab"], (cfg["batch"], cfg["seq"])).astype(np.int32)
+    tgt = np.roll(tok, -1, axis=1)
+    got = _run(client, programs.transformer_step(**cfg, emit="grads"),
+               params + zeros + zeros + [np.array(0, np.int32), tok, tgt], bf16_first=len(params))
+    torch.set_num_threads(max(1, min(32, torch.get_num_threads())))
+    loss, grads = tp.transformer_grads(names, [torch.from_numpy(p) for p in params], torch.from_numpy(tok),
+                                       torch.from_numpy(tgt), layers=cfg["layers"])
+    assert_close(got[0], float(loss), 2e-3, "transformer loss")
+    gd = dict(zip(names, zip(got[1:], grads)))
+    failures = []
+    for n, (g, r) in gd.items():
+        r = r.double().numpy()
+        if n.endswith(".bk"):
+            scale = np.sqrt(np.mean(np.square(gd[n[:-2] + "bq"][1].double().numpy())))
+            if np.abs(g).max() > 0.1 * scale:
+                failures.append(f"{n}: max |grad| {np.abs(g).max():.3e} vs bq rms {scale:.3e}")
+            continue
+        try:
+            _normwise(g, r, 3e-2, f"transformer grad {n}")
+        except AssertionError as e:
+            failures.append(str(e))
+    assert not failures, "\n".join(failures)

@@ -169,3 +169,67 @@ def test_layer_norm_bwd_restatement_matches_autodiff():
     got = hlo_interp.run(b.module(grads), [[x, w, bb, dy]])[0]
     for gg, r in zip(got, restate.layer_norm_bwd_ref(x, w, dy, 1e-5)):
         np.testing.assert_allclose(gg, r, rtol=1e-9, atol=1e-12)
+
+
+# ------------------------------------------------ torch-CPU port (baseline) --
+def _t(a, dtype=None):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    return t.to(dtype) if dtype is not None else t
+
+
+def test_torch_port_mlp_and_cnn_match_interpreter():
+    """oracle/torch_port.py (timed as the CPU baseline, and the full-size
+    oracle of the CNN step) restates the same programs: in float64 it agrees
+    with the interpreter to 1e-10."""
+    import torch
+    from oracle import torch_port as tp
+    rng = np.random.default_rng(61)
+    dims, batch = (20, 16, 16, 5), 8
+    params, x, lab = _mlp_inputs(rng, dims, batch)
+    ref = hlo_interp.run(programs.mlp_step(batch=batch, dims=dims), [params + [x, lab]])[0]
+    loss, new = tp.mlp_step([_t(p, torch.float64) for p in params], _t(x, torch.float64), _t(lab))
+    assert abs(float(loss) - ref[0]) < 1e-10
+    for a, b in zip(new, ref[1:]):
+        np.testing.assert_allclose(a.numpy(), b, rtol=1e-10, atol=1e-12)
+    shapes = [(3, 3, 1, 32), (32,), (3, 3, 32, 64), (64,), (3136, 256), (256,), (256, 10), (10,)]
+    ps = [(rng.standard_normal(s) * (0.3 if len(s) > 1 else 0.05)).astype(np.float32) for s in shapes]
+    xc = rng.random((3, 28, 28, 1)).astype(np.float32)
+    lc = rng.integers(0, 10, 3).astype(np.int32)
+    ref = hlo_interp.run(programs.cnn_step(batch=3, emit="grads"), [ps + [xc, lc]])[0]
+    loss, new = tp.cnn_step([_t(p, torch.float64) for p in ps], _t(xc, torch.float64), _t(lc), lr=1.0)
+    assert abs(float(loss) - ref[0]) < 1e-10
+    for p, a, g in zip(ps, new, ref[1:]):
+        np.testing.assert_allclose(p - a.numpy(), g, rtol=1e-9, atol=1e-11)
+
+
+def test_torch_port_transformer_matches_interpreter():
+    """The transformer port in float64 (every op in f64, no bf16 rounding)
+    against the interpreter run with bf16 parameters widened to f64 the same
+    way: loss to 1e-9 and every gradient to 1e-7 normwise."""
+    import torch
+    from oracle import torch_port as tp
+    cfg = dict(batch=2, seq=32, layers=2, d=64, heads=2, ffn=128, vocab=97)
+    shapes = programs.transformer_param_shapes(cfg["layers"], cfg["d"], cfg["heads"], cfg["ffn"],
+                                               cfg["vocab"], cfg["seq"])
+    rng = np.random.default_rng(62)
+    params = [hlo_interp.bf16_round((rng.standard_normal(s) * (0.3 if len(s) > 1 else 0.1))
+                                    .astype(np.float32)) for _, s in shapes]
+    tok = rng.integers(0, cfg["vocab"], (cfg["batch"], cfg["seq"])).astype(np.int32)
+    tgt = np.roll(tok, -1, axis=1)
+    # the same program with f32 parameters: the interpreter evaluates it in f64
+    text = programs.transformer_step(**cfg, emit="grads").replace("bf16", "f32")
+    zeros = [np.zeros(s, np.float32) for _, s in shapes]
+    ref = hlo_interp.run(text, [params + zeros + zeros + [np.array(0, np.int32), tok, tgt]])[0]
+    names = [n for n, _ in shapes]
+    loss, grads = tp.transformer_grads(names, [_t(p, torch.float64) for p in params], _t(tok), _t(tgt),
+                                       layers=cfg["layers"], f32=torch.float64)
+    assert abs(float(loss) - ref[0]) < 1e-9 * abs(ref[0])
+    gd = {n: (g.numpy(), np.asarray(r, np.float64)) for n, g, r in zip(names, grads, ref[1:])}
+    for n, (g, r) in gd.items():
+        if n.endswith(".bk"):  # zero in exact arithmetic: both sides hold rounding noise
+            scale = np.linalg.norm(gd[n[:-2] + "bq"][1])
+            assert np.linalg.norm(g) < 1e-9 * scale and np.linalg.norm(r) < 1e-9 * scale
+            continue
+        rel = np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-300)
+        assert rel < 1e-7, f"{n}: {rel:.3e}"
