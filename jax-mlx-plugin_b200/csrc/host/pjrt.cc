@@ -518,7 +518,10 @@ std::string program_text(const std::string& code) {
   return code;
 }
 
-std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std::string& opts) {
+// prebuilt: cubins by nvrtc_key of their source (from a serialized
+// executable); a unit whose key is there is not compiled again.
+std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std::string& opts,
+                             const std::map<std::string, std::string>* prebuilt = nullptr) {
   fault_point("compile");
   const std::string text = program_text(code);
   Module m = parse_module(text);
@@ -539,7 +542,24 @@ std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std:
   e->compile_options = opts;
   e->name = m.name.empty() ? "main" : m.name;
   e->fingerprint = std::to_string(std::hash<std::string>()(text));
-  if (!e->plan.kernel_names.empty()) e->cubins = nvrtc_compile_all(e->plan.units, "b200_" + e->fingerprint);
+  if (!e->plan.kernel_names.empty()) {
+    std::vector<std::string> todo;
+    std::vector<size_t> todo_at;
+    e->cubins.assign(e->plan.units.size(), std::string());
+    for (size_t u = 0; u < e->plan.units.size(); ++u) {
+      auto it = prebuilt ? prebuilt->find(nvrtc_key(e->plan.units[u])) : decltype(prebuilt->end()){};
+      if (prebuilt && it != prebuilt->end()) {
+        e->cubins[u] = it->second;
+      } else {
+        todo.push_back(e->plan.units[u]);
+        todo_at.push_back(u);
+      }
+    }
+    if (!todo.empty()) {
+      auto built = nvrtc_compile_all(todo, "b200_" + e->fingerprint);
+      for (size_t i = 0; i < built.size(); ++i) e->cubins[todo_at[i]] = std::move(built[i]);
+    }
+  }
   for (auto& t : e->plan.output_types) {
     e->out_dim_sizes.push_back(t.dims.size());
     e->out_dims_flat.insert(e->out_dims_flat.end(), t.dims.begin(), t.dims.end());
@@ -1547,8 +1567,10 @@ struct SerializedBlob {
 static void delete_blob(PJRT_SerializedExecutable* b) { delete reinterpret_cast<SerializedBlob*>(b); }
 static void delete_opts(PJRT_SerializedCompileOptions* b) { delete reinterpret_cast<SerializedBlob*>(b); }
 static PJRT_Error* Executable_Serialize(PJRT_Executable_Serialize_Args* a) {
-  // Serialized form: magic, the program text and the compile options; loading
-  // it recompiles (the NVRTC cubin cache makes that cheap).
+  // Serialized form "B200EXE2": the program text, the compile options, and the
+  // generated kernels' cubins, each under the nvrtc_key of its source.  Loading
+  // re-plans the program (host work, milliseconds) and takes every kernel
+  // whose source still has the same key from the blob instead of compiling it.
   const Exe& e = *a->executable->exe;
   auto* blob = new SerializedBlob;
   auto put = [&](const std::string& s) {
@@ -1556,9 +1578,14 @@ static PJRT_Error* Executable_Serialize(PJRT_Executable_Serialize_Args* a) {
     blob->bytes.append((const char*)&n, 8);
     blob->bytes += s;
   };
-  blob->bytes = "B200EXE1";
+  blob->bytes = "B200EXE2";
   put(e.text);
   put(e.compile_options);
+  put(std::to_string(e.cubins.size()));
+  for (size_t u = 0; u < e.cubins.size(); ++u) {
+    put(nvrtc_key(e.plan.units.at(u)));
+    put(e.cubins[u]);
+  }
   a->serialized_bytes = blob->bytes.data();
   a->serialized_bytes_size = blob->bytes.size();
   a->serialized_executable = reinterpret_cast<PJRT_SerializedExecutable*>(blob);
@@ -1576,7 +1603,9 @@ static PJRT_Error* Executable_GetCompileOptions(PJRT_Executable_GetCompileOption
 static PJRT_Error* Executable_DeserializeAndLoad(PJRT_Executable_DeserializeAndLoad_Args* a) {
   PJRT_TRY
   std::string s(a->serialized_executable, a->serialized_executable_size);
-  if (s.size() < 16 || s.compare(0, 8, "B200EXE1") != 0) throw PjrtErr(3, "not a B200 serialized executable");
+  const bool v2 = s.size() >= 16 && s.compare(0, 8, "B200EXE2") == 0;
+  if (!v2 && (s.size() < 16 || s.compare(0, 8, "B200EXE1") != 0))
+    throw PjrtErr(3, "not a B200 serialized executable");
   size_t off = 8;
   auto get = [&]() {
     if (off + 8 > s.size()) throw PjrtErr(3, "truncated serialized executable");
@@ -1590,10 +1619,20 @@ static PJRT_Error* Executable_DeserializeAndLoad(PJRT_Executable_DeserializeAndL
   };
   std::string text = get();
   std::string opts = get();
+  std::map<std::string, std::string> prebuilt;
+  if (v2) {
+    const std::string count = get();
+    const long n = std::strtol(count.c_str(), nullptr, 10);
+    if (n < 0 || n > (1 << 20)) throw PjrtErr(3, "corrupt serialized executable");
+    for (long u = 0; u < n; ++u) {
+      std::string key = get();
+      prebuilt[key] = get();
+    }
+  }
   if (a->overridden_serialized_compile_options && a->overridden_serialized_compile_options_size)
     opts.assign(a->overridden_serialized_compile_options, a->overridden_serialized_compile_options_size);
   auto* le = new PJRT_LoadedExecutable;
-  le->exe = compile(a->client, text, opts);
+  le->exe = compile(a->client, text, opts, v2 ? &prebuilt : nullptr);
   a->loaded_executable = le;
   PJRT_CATCH
 }

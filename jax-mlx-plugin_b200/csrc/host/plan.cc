@@ -1025,6 +1025,23 @@ struct Builder {
         case Op::Scatter: {
           int out = temp_for(ValueRef{n, 0});
           auto it = slot.find(nd.operands[0]);
+          const Graph& comb = *nd.regions.at(0);
+          const Node& cn = comb.nodes.at(comb.outputs.at(0).node);
+          if (g.type(nd.operands[0]).dtype == DType::BF16 && cn.op == Op::Add && nd.operands.size() == 3) {
+            // A bf16 sum (an embedding gradient) is accumulated in an f32
+            // buffer and rounded once: no per-add bf16 rounding in whatever
+            // order the atomics land, only f32 addition order.
+            TensorType ft = g.type(nd.operands[0]);
+            ft.dtype = DType::F32;
+            const int acc = new_slot(Slot::TEMP, ft, "scatter_f32_accumulator");
+            std::vector<int64_t> ident(ft.rank());
+            for (int d = 0; d < ft.rank(); ++d) ident[d] = d;
+            if (it != slot.end()) add_kernel(cg.permute(it->second, ident, acc));
+            else add_kernel(cg.loop({nd.operands[0]}, {acc}));
+            add_kernel(cg.scatter(n, acc));
+            add_kernel(cg.permute(acc, ident, out));
+            break;
+          }
           if (it != slot.end()) {
             Step c;
             c.kind = StepKind::Copy;

@@ -176,12 +176,21 @@ std::string cache_path(const std::string& key) {
 }
 }  // namespace
 
+std::string nvrtc_key(const std::string& source) {
+  static const std::string opt_text = [] {
+    std::string t;
+    for (const char* o : kNvrtcOpts) t += std::string(o) + " ";
+    int ver[2] = {0, 0};
+    nvrtcVersion(&ver[0], &ver[1]);
+    return t + "nvrtc" + std::to_string(ver[0]) + "." + std::to_string(ver[1]) + " ";
+  }();
+  return source_key(opt_text + source);
+}
+
 std::string nvrtc_compile(const std::string& source, const std::string& name) {
   static std::mutex mu;
   static std::map<std::string, std::string> cache;
-  std::string opt_text;
-  for (const char* o : kNvrtcOpts) opt_text += std::string(o) + " ";
-  const std::string key = source_key(opt_text + source);
+  const std::string key = nvrtc_key(source);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -202,6 +211,13 @@ std::string nvrtc_compile(const std::string& source, const std::string& name) {
       }
     }
   }
+  static const bool no_jit = [] {
+    const char* v = getenv("B200_NO_JIT");
+    return v && v[0] == '1';
+  }();
+  if (no_jit)
+    throw PjrtErr(9, "generated kernels need compiling but B200_NO_JIT=1 forbids NVRTC here (load "
+                     "a serialized executable that carries its cubins)");
   nvrtcProgram prog;
   if (nvrtcCreateProgram(&prog, source.c_str(), (name + ".cu").c_str(), 0, nullptr, nullptr) !=
       NVRTC_SUCCESS)

@@ -570,3 +570,54 @@ def test_repeated_execute_replays_cuda_graph(client):
         assert_close(outs[0], loss, 2e-3, f"loss (call {seed - 19})")
         for p, g, r in zip(params, outs[1:], new):
             assert_close(g, p.astype(np.float64) - r, 2e-3, f"grad (call {seed - 19})")
+
+
+_NO_JIT_PROBE = """
+import sys
+sys.path[:0] = [{root!r}, {pkg!r}]
+import numpy as np
+from jax_b200 import pjrt, programs
+c = pjrt.Client()
+blob = open({blob!r}, "rb").read()
+exe = c.deserialize(blob)  # must not reach NVRTC (B200_NO_JIT=1)
+ins = np.load({inputs!r})
+args = [c.buffer_from_numpy(ins[f"arr_{{i}}"]) for i in range(len(ins.files))]
+outs = [o.to_numpy() for o in exe.execute([args])[0]]
+np.savez({out!r}, *outs)
+try:
+    c.compile(programs.mlp_step(batch=8, dims=(12, 16, 10)))
+    print("compiled")
+except pjrt.PjrtError as e:
+    print("refused", e.code)
+"""
+
+
+def test_serialized_executable_carries_its_kernels(client, tmp_path):
+    """Executable_Serialize stores the generated kernels' cubins beside the
+    program: a fresh process with B200_NO_JIT=1 (NVRTC forbidden) loads the
+    blob, runs it bit-identically to the original, and refuses a plain compile
+    of a program whose kernels it does not have (FAILED_PRECONDITION)."""
+    import os
+    import subprocess
+    import sys
+    rng = np.random.default_rng(71)
+    dims = (64, 128, 10)
+    params, x, lab = _exact_mlp_inputs(rng, dims, 32)
+    exe = client.compile(programs.mlp_step(batch=32, dims=dims, emit="grads"))
+    blob = exe.serialize()
+    assert blob[:8] == b"B200EXE2" and blob.count(b"\x7fELF") >= 1
+    want = [o.to_numpy() for o in exe.execute([[client.buffer_from_numpy(a) for a in params + [x, lab]]])[0]]
+    (tmp_path / "exe.bin").write_bytes(blob)
+    np.savez(tmp_path / "in.npz", *(params + [x, lab]))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = _NO_JIT_PROBE.format(root=root, pkg=os.path.join(root, "jax-mlx-plugin_b200"),
+                               blob=str(tmp_path / "exe.bin"), inputs=str(tmp_path / "in.npz"),
+                               out=str(tmp_path / "out.npz"))
+    env = dict(os.environ, B200_NO_JIT="1")
+    env.pop("B200_CACHE_DIR", None)
+    r = subprocess.run([sys.executable, "-c", src], env=env, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == "refused 9", r.stdout
+    got = np.load(tmp_path / "out.npz")
+    for i, w in enumerate(want):
+        np.testing.assert_array_equal(got[f"arr_{i}"], w)
