@@ -36,10 +36,31 @@ struct PJRT_Error {
   std::string msg;
 };
 
+// The outcome of an Execute's collectives as the NCCL watchdog saw it: set
+// when it aborted a communicator the Execute used, before the abort lets the
+// stuck kernels (and so the Execute's events) finish.
+struct CollectiveStatus {
+  std::mutex mu;
+  PJRT_Error_Code code = PJRT_Error_Code_OK;
+  std::string msg;
+  void fail(PJRT_Error_Code c, const std::string& m) {
+    std::lock_guard<std::mutex> lk(mu);
+    if (code == PJRT_Error_Code_OK) code = c, msg = m;
+  }
+  bool failed(PJRT_Error_Code* c, std::string* m) {
+    std::lock_guard<std::mutex> lk(mu);
+    if (code == PJRT_Error_Code_OK) return false;
+    *c = code;
+    *m = msg;
+    return true;
+  }
+};
+
 struct PJRT_Event {
   std::mutex mu;
   std::condition_variable cv;
   cudaEvent_t ev = nullptr;
+  std::shared_ptr<CollectiveStatus> status;  // the producing Execute's collectives
   int ordinal = -1;
   bool host_set = false;  // for host-completed events
   bool host_done = false;
@@ -94,6 +115,96 @@ struct PJRT_Client {
   std::map<std::vector<int>, std::unique_ptr<NcclComms>> comms;  // keyed by global device ids
   std::atomic<int64_t> comm_counter{0};
   PJRT_TopologyDescription topo;
+  std::unique_ptr<struct NcclWatchdog> watchdog;  // started with the first collective
+};
+
+// Host watchdog over the client's collectives (NCCL's own kernels wait for
+// peers without bound).  Each collective an Execute enqueues is followed by a
+// CUDA event; a thread polls the pending events every 2 ms and, while one is
+// not reached, the communicator's asynchronous error state.  On an NCCL error,
+// or when the event is still pending B200_NCCL_TIMEOUT_MS (default 600000)
+// after the collective was enqueued (a peer rank that left or stalled), it
+// marks the Execute failed (INTERNAL or DEADLINE_EXCEEDED) and aborts the
+// communicator (ncclCommAbort): the waiting kernels exit, the Execute's events
+// complete with that error, and every later collective on the communicator is
+// refused (ABORTED) instead of hanging.
+struct NcclWatchdog {
+  struct Item {
+    cudaEvent_t ev;
+    NcclComms* comms;
+    std::shared_ptr<CollectiveStatus> status;
+    std::chrono::steady_clock::time_point deadline;
+    std::string what;
+  };
+  std::mutex mu;
+  std::condition_variable cv;
+  std::vector<Item> items;
+  bool stop = false;
+  int64_t timeout_ms;
+  std::thread th;
+  NcclWatchdog() {
+    const char* v = std::getenv("B200_NCCL_TIMEOUT_MS");
+    timeout_ms = v && std::atoll(v) > 0 ? std::atoll(v) : 600000;
+    th = std::thread([this] { loop(); });
+  }
+  ~NcclWatchdog() {
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      stop = true;
+    }
+    cv.notify_all();
+    th.join();
+    for (auto& it : items) cudaEventDestroy(it.ev);
+  }
+  void watch(Device& d, NcclComms* comms, std::shared_ptr<CollectiveStatus> status,
+             const std::string& what) {
+    cudaEvent_t ev = nullptr;
+    d.activate();
+    B200_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    B200_CUDA(cudaEventRecord(ev, d.stream));
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      items.push_back({ev, comms, std::move(status),
+                       std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms), what});
+    }
+    cv.notify_all();
+  }
+  void loop() {
+    std::unique_lock<std::mutex> lk(mu);
+    while (!stop) {
+      if (items.empty()) {
+        cv.wait(lk, [&] { return stop || !items.empty(); });
+        continue;
+      }
+      cv.wait_for(lk, std::chrono::milliseconds(2));
+      const auto now = std::chrono::steady_clock::now();
+      for (size_t i = 0; i < items.size();) {
+        Item& it = items[i];
+        const cudaError_t r = cudaEventQuery(it.ev);
+        std::string why;
+        PJRT_Error_Code code = PJRT_Error_Code_INTERNAL;
+        if (r == cudaSuccess) {
+        } else if (r != cudaErrorNotReady) {
+          why = std::string("CUDA error while waiting for ") + it.what + ": " + cudaGetErrorString(r);
+        } else if (!(why = nccl_async_error(*it.comms)).empty()) {
+          why = it.what + ": " + why;
+        } else if (now >= it.deadline) {
+          code = PJRT_Error_Code_DEADLINE_EXCEEDED;
+          why = it.what + " did not complete within B200_NCCL_TIMEOUT_MS=" + std::to_string(timeout_ms) +
+                " ms (a peer rank left or stalled); the communicator was aborted";
+        } else {
+          ++i;
+          continue;
+        }
+        if (!why.empty()) {
+          it.status->fail(code, why);
+          nccl_abort(*it.comms, why);
+        }
+        cudaEventDestroy(it.ev);
+        items.erase(items.begin() + (long)i);
+      }
+    }
+  }
 };
 
 struct PJRT_Buffer {
@@ -219,6 +330,8 @@ bool event_ready(PJRT_Event* e, PJRT_Error_Code* code, std::string* msg) {
   if (r != cudaSuccess) {
     *code = PJRT_Error_Code_INTERNAL;
     *msg = cudaGetErrorString(r);
+  } else if (e->status) {
+    e->status->failed(code, msg);
   }
   return true;
 }
@@ -236,6 +349,8 @@ void event_wait(PJRT_Event* e, PJRT_Error_Code* code, std::string* msg) {
   if (r != cudaSuccess) {
     *code = PJRT_Error_Code_INTERNAL;
     *msg = cudaGetErrorString(r);
+  } else if (e->status) {
+    e->status->failed(code, msg);
   }
 }
 
@@ -593,7 +708,13 @@ NcclComms& comms_for(PJRT_Client* c, Exe& e) {
   std::vector<int> ids;
   for (int64_t r = 0; r < e.num_replicas; ++r) ids.push_back((int)r);
   auto it = c->comms.find(ids);
-  if (it != c->comms.end()) return *it->second;
+  if (it != c->comms.end()) {
+    std::lock_guard<std::mutex> lk(it->second->mu);
+    if (it->second->aborted)
+      throw PjrtErr(10, "the NCCL communicator of these replicas was aborted earlier (" +
+                            it->second->abort_reason + "); no further collectives run on it");
+    return *it->second;
+  }
   fault_point("nccl_init");
   std::unique_ptr<NcclComms> comm;
   if (c->num_nodes == 1) {
@@ -848,6 +969,14 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
   };
   std::shared_ptr<DeviceMem>* gemm_ws_override = nullptr;
   // one step of the plan on every device, with slot pointers `ptr`
+  // collectives of this Execute: followed by events the client's NCCL
+  // watchdog polls (its verdict reaches the Execute's events through cst)
+  std::shared_ptr<CollectiveStatus> cst;
+  auto watch_collectives = [&](const std::vector<Device*>& dd, NcclComms& comm, const char* what) {
+    if (!cst) cst = std::make_shared<CollectiveStatus>();
+    if (!c->watchdog) c->watchdog = std::make_unique<NcclWatchdog>();
+    for (Device* d : dd) c->watchdog->watch(*d, &comm, cst, std::string(what) + " of " + e.name);
+  };
   auto exec_step = [&](size_t si, std::vector<std::vector<void*>>& ptr) {
     const Step& st = p.steps[si];
     if (st.kind == StepKind::AllReduce && !st.args.empty()) {
@@ -878,6 +1007,7 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
       if (e.num_replicas != 1) {
         NcclComms& comm = comms_for(c, e);
         nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1]);
+        watch_collectives(dd, comm, "all_reduce bucket");
         for (size_t d = 0; d < nd; ++d) {
           Device& dev = *devs[d]->dev;
           dev.activate();
@@ -907,6 +1037,7 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
       } else {
         NcclComms& comm = comms_for(c, e);
         nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1]);
+        watch_collectives(dd, comm, "all_reduce");
       }
     } else {
       for (size_t d = 0; d < nd; ++d) {
@@ -1010,6 +1141,7 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
   }
   for (size_t d = 0; d < nd; ++d) {
     auto ev = record_event(*devs[d]->dev);
+    ev->status = cst;
     if (a->device_complete_events) a->device_complete_events[d] = handle_of(ev);
     for (size_t o = 0; o < p.output_slots.size(); ++o) {
       int s = p.output_slots[o];
@@ -1294,8 +1426,9 @@ static PJRT_Error* Client_Destroy(PJRT_Client_Destroy_Args* a) {
   PJRT_Client* c = a->client;
   for (auto& d : c->local) {
     d->activate();
-    cudaStreamSynchronize(d->stream);
+    cudaStreamSynchronize(d->stream);  // the watchdog still guards collectives here
   }
+  c->watchdog.reset();
   c->comms.clear();
   for (auto& d : c->local) {
     d->activate();
@@ -1752,7 +1885,9 @@ static PJRT_Error* Buffer_ToHostBuffer(PJRT_Buffer_ToHostBuffer_Args* a) {
   std::lock_guard<std::recursive_mutex> lk(d.mu);
   d.activate();
   if (need) B200_CUDA(cudaMemcpyAsync(a->dst, b->mem->ptr, need, cudaMemcpyDeviceToHost, d.stream));
-  a->event = handle_of(record_event(d));
+  auto ev = record_event(d);
+  if (b->ready) ev->status = b->ready->status;  // a failed collective upstream fails the copy
+  a->event = handle_of(ev);
   PJRT_CATCH
 }
 static PJRT_Error* Buffer_CopyRawToHost(PJRT_Buffer_CopyRawToHost_Args* a) {
@@ -1764,7 +1899,9 @@ static PJRT_Error* Buffer_CopyRawToHost(PJRT_Buffer_CopyRawToHost_Args* a) {
   d.activate();
   B200_CUDA(cudaMemcpyAsync(a->dst, (char*)b->mem->ptr + a->offset, (size_t)a->transfer_size,
                             cudaMemcpyDeviceToHost, d.stream));
-  a->event = handle_of(record_event(d));
+  auto ev = record_event(d);
+  if (b->ready) ev->status = b->ready->status;
+  a->event = handle_of(ev);
   PJRT_CATCH
 }
 static PJRT_Error* Buffer_CopyToDevice(PJRT_Buffer_CopyToDevice_Args* a) {

@@ -346,6 +346,8 @@ struct Nccl {
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   std::string why;
   static Nccl& get() {
     static Nccl n = [] {
@@ -368,6 +370,8 @@ struct Nccl {
       x.GroupStart = (decltype(x.GroupStart))sym("ncclGroupStart");
       x.GroupEnd = (decltype(x.GroupEnd))sym("ncclGroupEnd");
       x.GetErrorString = (decltype(x.GetErrorString))sym("ncclGetErrorString");
+      x.CommGetAsyncError = (decltype(x.CommGetAsyncError))sym("ncclCommGetAsyncError");
+      x.CommAbort = (decltype(x.CommAbort))sym("ncclCommAbort");
       if (!x.AllReduce || !x.CommInitAll || !x.CommInitRank) x.why = "libnccl lacks symbols";
       return x;
     }();
@@ -386,8 +390,32 @@ bool nccl_available(std::string* why) {
 }
 NcclComms::~NcclComms() {
   auto& n = Nccl::get();
+  std::lock_guard<std::mutex> lk(mu);
+  if (aborted) return;  // ncclCommAbort already released them
   for (void* c : comms)
     if (c && n.CommDestroy) n.CommDestroy((ncclComm_t)c);
+}
+std::string nccl_async_error(NcclComms& c) {
+  auto& n = Nccl::get();
+  if (!n.CommGetAsyncError) return "";
+  std::lock_guard<std::mutex> lk(c.mu);
+  if (c.aborted) return "";
+  for (void* x : c.comms) {
+    ncclResult_t st = ncclSuccess;
+    if (x && n.CommGetAsyncError((ncclComm_t)x, &st) == ncclSuccess && st != ncclSuccess &&
+        st != ncclInProgress)
+      return std::string("NCCL asynchronous error: ") + (n.GetErrorString ? n.GetErrorString(st) : "?");
+  }
+  return "";
+}
+void nccl_abort(NcclComms& c, const std::string& reason) {
+  auto& n = Nccl::get();
+  std::lock_guard<std::mutex> lk(c.mu);
+  if (c.aborted) return;
+  c.aborted = true;
+  c.abort_reason = reason;
+  for (void* x : c.comms)
+    if (x && n.CommAbort) n.CommAbort((ncclComm_t)x);
 }
 std::vector<char> nccl_unique_id() {
   auto& n = Nccl::get();

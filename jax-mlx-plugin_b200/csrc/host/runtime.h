@@ -115,8 +115,20 @@ struct Nccl;
 // Multi-process: `unique_id` (128 bytes) exchanged by the caller.
 struct NcclComms {
   std::vector<void*> comms;  // ncclComm_t per local device
+  // Set (once) when the communicator was aborted: every later collective on
+  // it fails with this reason instead of waiting for peers that may be gone.
+  std::mutex mu;
+  bool aborted = false;
+  std::string abort_reason;
   ~NcclComms();
 };
+// The first asynchronous NCCL error of any of the communicator's ranks here
+// (ncclCommGetAsyncError), or "" while all are healthy.
+std::string nccl_async_error(NcclComms& c);
+// ncclCommAbort on every local rank (its kernels stop waiting for peers and
+// exit); the communicator is unusable afterwards.  Safe to call from a thread
+// other than the one issuing collectives; a second call does nothing.
+void nccl_abort(NcclComms& c, const std::string& reason);
 bool nccl_available(std::string* why);
 std::vector<char> nccl_unique_id();
 std::unique_ptr<NcclComms> nccl_init_all(const std::vector<Device*>& devs);

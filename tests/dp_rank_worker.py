@@ -10,7 +10,13 @@ of the batch.
 KIND is "mlp" (configs[2], SGD step) or "transformer" (configs[3]
 architecture at reduced size, gradients).  Writes OUT/rank<r>.npz with the
 outputs, or OUT/rank<r>.err with "<code> <message>" when Execute raises a
-PJRT error; OUT/rank<r>.stage names the last stage reached."""
+PJRT error; OUT/rank<r>.stage names the last stage reached.
+
+KIND "leave": both ranks run one data-parallel step; then rank 1 leaves (it
+exits between steps, with nothing of its own in flight) and rank 0 runs the
+next step, whose all-reduce can never complete.  The plugin's NCCL watchdog
+must end it with an error (B200_NCCL_TIMEOUT_MS), and the step after that must
+be refused at once.  Rank 0 writes OUT/leave.txt: the codes it saw."""
 import os
 import sys
 from datetime import timedelta
@@ -51,6 +57,8 @@ def main():
     client = pjrt.Client({"visible_devices": [local], "node_id": rank, "num_nodes": 2}, kv=KV())
     dev = client.addressable_devices[0]
     stage("compile")
+    if kind == "leave":
+        return leave(rank, out, stage, client, dev, store, dist)
     if kind == "mlp":
         dims = (784, 1024, 1024, 1024, 10)
         params, x, lab = _kink_safe_mlp(np.random.default_rng(53), dims, 1024)
@@ -79,6 +87,47 @@ def main():
     dist.barrier()
     stage("done")
     dist.destroy_process_group()
+
+
+def leave(rank, out, stage, client, dev, store, dist):
+    import time
+    from jax_b200 import pjrt, programs
+    dims = (64, 128, 10)
+    rng = np.random.default_rng(55)
+    params = [(rng.standard_normal(s) * 0.1).astype(np.float32)
+              for s in ((64, 128), (128,), (128, 10), (10,))]
+    x = rng.random((16, 64)).astype(np.float32)
+    lab = rng.integers(0, 10, 16).astype(np.int32)
+    exe = client.compile(programs.mlp_step(batch=8, dims=dims, num_replicas=2))
+    args = [client.buffer_from_numpy(a, device=dev) for a in params + [x[8 * rank:8 * rank + 8],
+                                                                       lab[8 * rank:8 * rank + 8]]]
+    stage("step1")
+    loss1 = float(exe.execute([args])[0][0].to_numpy())
+    if rank == 1:
+        stage("left")
+        store.set("b200_test/rank1_left", b"1")
+        dist.destroy_process_group()
+        os._exit(0)  # leaves between steps: no kernel or collective of its own in flight
+    store.wait(["b200_test/rank1_left"])
+    time.sleep(2.0)
+    res = [f"step1 {loss1:.6f}"]
+    stage("step2")
+    t0 = time.time()
+    try:
+        exe.execute([args])[0][0].to_numpy()
+        res.append("step2 ok")
+    except pjrt.PjrtError as e:
+        res.append(f"step2 {e.code} {time.time() - t0:.1f}s {e}")
+    stage("step3")
+    try:
+        exe.execute([args])[0][0].to_numpy()
+        res.append("step3 ok")
+    except pjrt.PjrtError as e:
+        res.append(f"step3 {e.code} {e}")
+    with open(os.path.join(out, "leave.txt"), "w") as f:
+        f.write("\n".join(res) + "\n")
+    stage("done")
+    os._exit(0)  # rank 1 is gone: no process-group teardown with it
 
 
 if __name__ == "__main__":

@@ -202,7 +202,7 @@ def test_dp2_transformer_grads_match_full_batch(client):
 
 
 # ------------------------------------------------- one process per GPU ----
-def _run_ranks(tmp_path, kind, fault=""):
+def _run_ranks(tmp_path, kind, fault="", extra_env=None):
     """torchrun, two ranks, each running tests/dp_rank_worker.py as bench.py
     runs its ranks.  Each rank records the stage it reached, so that a rank
     that does not finish in time says where it stopped."""
@@ -211,6 +211,7 @@ def _run_ranks(tmp_path, kind, fault=""):
     env.pop("B200_FAULT", None)
     if fault:
         env["B200_FAULT"] = fault
+    env.update(extra_env or {})
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
@@ -270,3 +271,22 @@ def test_dp2_nccl_init_fault_point(tmp_path):
         assert not (tmp_path / f"rank{r}.npz").exists()
         msg = (tmp_path / f"rank{r}.err").read_text()
         assert msg.startswith("14 ") and "injected fault at nccl_init" in msg, msg
+
+
+@needs2
+def test_dp2_peer_leaves_watchdog_aborts(tmp_path):
+    """A rank that leaves between steps: the surviving rank's next all-reduce
+    cannot complete.  With B200_NCCL_TIMEOUT_MS=3000 the plugin's NCCL
+    watchdog aborts the communicator, the step's result reports the error
+    (DEADLINE_EXCEEDED, or INTERNAL when NCCL itself reports the lost peer
+    first) within seconds instead of hanging, and the next step is refused with
+    ABORTED before anything is launched.  NVLS is off (NCCL_NVLS_ENABLE=0), so
+    no multicast object spans the ranks."""
+    _run_ranks(tmp_path, "leave", extra_env={"B200_NCCL_TIMEOUT_MS": "3000"})
+    lines = (tmp_path / "leave.txt").read_text().splitlines()
+    assert lines[0].startswith("step1 ")
+    code2 = int(lines[1].split()[1])
+    assert code2 in (4, 13), lines[1]
+    assert float(lines[1].split()[2].rstrip("s")) < 60, lines[1]
+    assert "aborted" in lines[1] or "NCCL" in lines[1], lines[1]
+    assert lines[2].startswith("step3 10 ") and "aborted" in lines[2], lines[2]
