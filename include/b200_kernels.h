@@ -68,8 +68,10 @@ B200_API int b200_ln_bwd(const void* x, const void* gamma, const float* mean, co
 /* Scaled dot-product attention forward, layout BTNH (batch, seq, heads, dim):
  *   O[b,t,n,:] = softmax_s(scale * Q[b,t,n,:].K[b,s,n,:] + mask) V[b,s,n,:]
  * with mask = -0.7*FLT_MAX where causal and s > t (JAX's large-negative fill).
- * q: [B,T,N,D]; k, v: [B,S,N,D]; o: [B,T,N,D]; dtype F32 (tensor cores in TF32,
- * softmax in f32) or BF16 (kind::f16 MMAs, f32 accumulate).  D must be 64.
+ * q: [B,T,N,D]; k, v: [B,S,N,D]; o: [B,T,N,D]; dtype F32 (each f32 operand
+ * split into bf16 hi + lo parts and every product taken as hi*hi + hi*lo +
+ * lo*hi in kind::f16 MMAs with f32 accumulation; softmax in f32) or BF16 (one
+ * kind::f16 MMA per product, f32 accumulate).  D must be 64.
  * Replaces reference src/jax_mlx_pjrt.cpp:4440-4446 / :8111-8150
  * (mlx::fast::scaled_dot_product_attention) and src/jax_mlx/sdpa.py:19-31. */
 B200_API int b200_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int64_t B,
@@ -90,8 +92,10 @@ B200_API int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v, 
  *   C_b[m,n] = alpha * sum_k A_b[m,k] * B_b[k,n]  (+ bias[n]) (+ relu)
  * A element (b,m,k) at a + b*sAb + m*sAm + k*sAk (strides in elements), one of
  * sAm/sAk must be 1; same for B with (b,k,n).  C is dense row-major [batch,M,N]
- * unless ldc (elements between rows) says otherwise.  in_dtype F32 (TF32 MMA) or
- * BF16; out_dtype F32 or BF16; accumulation in f32.  epilogue: 0 none, 1 bias,
+ * unless ldc (elements between rows) says otherwise.  in_dtype F32 (operands
+ * split into bf16 hi + lo planes, three kind::f16 MMAs per step; 3xTF32 where
+ * no plane workspace can be had) or BF16; out_dtype F32 or BF16; accumulation
+ * in f32.  epilogue: 0 none, 1 bias,
  * 2 bias+relu, 3 relu.  M == 0 or N == 0: nothing is written; K == 0: C is
  * set to zero (epilogue 0 or 3; a bias epilogue with K == 0 is rejected).
  * Replaces reference src/jax_mlx_pjrt.cpp:4577-4666 (dot_general ->

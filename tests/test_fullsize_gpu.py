@@ -14,11 +14,15 @@ floats a ReLU pre-activation within rounding of zero may land on the other
 side of its kink and move the upstream gradients of that one sample (the
 kink-safe elementwise checks are in test_pjrt_gpu.py): 2e-3 for the f32
 programs (contractions); 3e-2 for the bf16 transformer, whose activations the
-plugin stores in bf16 while the oracle keeps them exact (the same bound the
-reduced-size test holds the default compile to).  The transformer's layer-norm
-gains and query / key weights are drawn wider than N(0, 0.02) so that attention
-is not flat and every gradient carries signal; its key-bias gradient, zero in
-exact arithmetic, is bounded against the query-bias gradient instead."""
+plugin stores in bf16 while the oracle keeps them exact.  The transformer's
+parameters are N(0, 0.02) with layer-norm gains around flax's ones: there the
+torch port itself, run in bf16 with a rounding after every op, stays within
+1.5e-2 normwise of its float32 run on every gradient (measured on 16
+sequences).  (With wider query / key weights, N(0, 0.1), the same two runs
+differ by up to 18% on the first layers: the gradients are then dominated by
+bf16 rounding noise, and no bf16 result can be held to a tight bound against
+exact arithmetic.)  The key-bias gradient, zero in exact arithmetic, is
+bounded against the query-bias gradient instead."""
 import numpy as np
 import pytest
 
@@ -108,13 +112,9 @@ def test_transformer_full_config_against_port(client):
                                                cfg["vocab"], cfg["seq"])
     rng = np.random.default_rng(34)
 
-    def init(name, s):
+    def init(name, s):  # N(0, 0.02); layer-norm gains around flax's ones
         leaf = name.split(".")[-1]
-        if leaf.endswith("_g"):
-            return 1 + 0.1 * rng.standard_normal(s)
-        if leaf in ("wq", "wk"):
-            return 0.1 * rng.standard_normal(s)
-        return 0.02 * rng.standard_normal(s)
+        return (1.0 if leaf.endswith("_g") else 0.0) + 0.02 * rng.standard_normal(s)
     names = [n for n, _ in shapes]
     params = [hlo_interp.bf16_round(init(n, s).astype(np.float32)) for n, s in shapes]
     zeros = [np.zeros(s, np.float32) for _, s in shapes]
