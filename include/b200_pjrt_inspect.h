@@ -18,7 +18,8 @@ extern "C" {
 /* Compile `mlir` (StableHLO text) without a device.  what: 0 = optimized graph
  * (after call inlining, SDPA/LayerNorm matching), 1 = execution plan (slots and
  * steps), 2 = generated CUDA C, 3 = also NVRTC-compile the CUDA C for sm_100a
- * and return "ok <cubin bytes>".  Returns 0 and a malloc'd string in *out, or
+ * and return "ok <cubin bytes>", 4 = the key each compile unit's cubin is filed
+ * under (one per line; a serialized executable carries its cubins by these).  Returns 0 and a malloc'd string in *out, or
  * the PJRT error code and the message in *out.  Free *out with
  * b200_pjrt_free(). */
 __attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, size_t len,

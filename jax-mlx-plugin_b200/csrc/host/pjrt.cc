@@ -671,6 +671,12 @@ std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std:
       }
     }
     if (!todo.empty()) {
+      if (prebuilt && env_flag("B200_NO_JIT"))
+        throw PjrtErr(9, "serialized executable: " + std::to_string(todo.size()) + " of " +
+                             std::to_string(e->plan.units.size()) +
+                             " kernel units of the re-planned program have no cubin in it (first "
+                             "missing key " + nvrtc_key(todo[0]) + ", " + std::to_string(prebuilt->size()) +
+                             " carried) and B200_NO_JIT=1 forbids compiling them");
       auto built = nvrtc_compile_all(todo, "b200_" + e->fingerprint);
       for (size_t i = 0; i < built.size(); ++i) e->cubins[todo_at[i]] = std::move(built[i]);
     }
@@ -2029,6 +2035,9 @@ __attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, s
     if (what == 0) res = p.graph_dump;
     else if (what == 1) res = dump_plan(p);
     else if (what == 2) res = p.source;
+    else if (what == 4) {
+      for (auto& u : p.units) res += nvrtc_key(u) + "\n";
+    }
     else if (what == 3) {
       size_t n = 0;
       if (!p.kernel_names.empty())

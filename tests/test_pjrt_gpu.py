@@ -592,6 +592,19 @@ except pjrt.PjrtError as e:
 """
 
 
+def _blob_keys(blob):
+    """Unit keys carried by a B200EXE2 blob: magic, then length-prefixed text,
+    options, unit count, and (key, cubin) per unit."""
+    import struct
+    off, fields = 8, []
+    while off < len(blob):
+        (n,) = struct.unpack_from("<Q", blob, off)
+        fields.append(blob[off + 8:off + 8 + n])
+        off += 8 + n
+    count = int(fields[2])
+    return [fields[3 + 2 * i].decode() for i in range(count)]
+
+
 def test_serialized_executable_carries_its_kernels(client, tmp_path):
     """Executable_Serialize stores the generated kernels' cubins beside the
     program: a fresh process with B200_NO_JIT=1 (NVRTC forbidden) loads the
@@ -606,6 +619,9 @@ def test_serialized_executable_carries_its_kernels(client, tmp_path):
     exe = client.compile(programs.mlp_step(batch=32, dims=dims, emit="grads"))
     blob = exe.serialize()
     assert blob[:8] == b"B200EXE2" and blob.count(b"\x7fELF") >= 1
+    keys = _blob_keys(blob)
+    text = programs.mlp_step(batch=32, dims=dims, emit="grads")
+    assert keys == pjrt.inspect(text, 4).split(), (keys, pjrt.inspect(text, 4))
     want = [o.to_numpy() for o in exe.execute([[client.buffer_from_numpy(a) for a in params + [x, lab]]])[0]]
     (tmp_path / "exe.bin").write_bytes(blob)
     np.savez(tmp_path / "in.npz", *(params + [x, lab]))
