@@ -551,8 +551,10 @@ struct WsCfg {
   static constexpr int Q_OFF = 0;                                  // Q hi [, lo]
   static constexpr int KV_OFF = Q_OFF + PARTS * QB;                // slot s: K hi, [K lo,] V hi [, V lo]
   static constexpr int KV_SLOT = 2 * PARTS * KB;
-  static constexpr int ST_OFF = KV_OFF + SLOTS * KV_SLOT;          // f32 staging (X3): K, V of one block
-  static constexpr int ST_BYTES = X3 ? 2 * 64 * 256 : 0;
+  // f32 staging (X3): K and V of two blocks (buffer b of K at ST_OFF + b * 2 * 16 KB,
+  // V 16 KB after it), so block j+1's loads land while block j is being split
+  static constexpr int ST_OFF = KV_OFF + SLOTS * KV_SLOT;
+  static constexpr int ST_BYTES = X3 ? 2 * 2 * 64 * 256 : 0;
   static constexpr int QST_OFF = KV_OFF + 2 * KV_SLOT;             // f32 Q staging aliases K/V slot 2
   static constexpr int RED_OFF = ST_OFF + ST_BYTES;                // softmax max / sum exchange
   static constexpr int BAR_OFF = RED_OFF + 2 * 2 * 128 * 4;
@@ -612,8 +614,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   auto k_lo = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + C::KB; };
   auto v_hi = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + C::PARTS * C::KB; };
   auto v_lo = [&](int s) { return smem + C::KV_OFF + s * C::KV_SLOT + 3 * C::KB; };
-  uint8_t* k_st = smem + C::ST_OFF;
-  uint8_t* v_st = smem + C::ST_OFF + 64 * 256;
+  auto k_st = [&](int bf) { return smem + C::ST_OFF + bf * 2 * 64 * 256; };
+  auto v_st = [&](int bf) { return smem + C::ST_OFF + bf * 2 * 64 * 256 + 64 * 256; };
   uint8_t* q_st = smem + C::QST_OFF;
   float* red = reinterpret_cast<float*>(smem + C::RED_OFF);  // [2 block parities][2 halves][128 rows]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
@@ -629,17 +631,22 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   uint64_t* ob_free = bars + 19;   // [2]
   uint64_t* mx_bar = bars + 21;    // [4 quarters][2]: both halves' block maxima written
   uint64_t* l_bar = bars + 29;     // [4 quarters]: both halves' row sums written
-  uint64_t* kst_full = bars + 33;  // f32 K staging loaded
-  uint64_t* vst_full = bars + 34;  // f32 V staging loaded
-  uint64_t* kst_used = bars + 35;  // f32 K staging split (count 4 warps)
-  uint64_t* vst_used = bars + 36;  // f32 V staging split
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 37);
+  uint64_t* kst_full = bars + 33;  // [2] f32 K staging buffer loaded
+  uint64_t* vst_full = bars + 35;  // [2] f32 V staging buffer loaded
+  uint64_t* kst_used = bars + 37;  // [2] f32 K staging buffer split (count 4 warps)
+  uint64_t* vst_used = bars + 39;  // [2] f32 V staging buffer split
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 41);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // one-dimensional grid, query tile slowest: with a causal mask every CTA
+  // of the first (N * B) holds a last (heaviest) query tile, and lighter tiles
+  // follow, so SMs that finish early pick up the light work (longest first)
   const int nq = (p.T + 127) / 128;
-  const int qt = p.causal ? nq - 1 - (int)blockIdx.x : (int)blockIdx.x;
-  const int n = blockIdx.y, b = blockIdx.z;
+  const int nb = p.N * p.B;
+  const int tile = (int)blockIdx.x / nb, nbi = (int)blockIdx.x % nb;
+  const int qt = p.causal ? nq - 1 - tile : tile;
+  const int n = nbi % p.N, b = nbi / p.N;
   const int t0 = qt * 128;
   const int nkb_all = (p.S + 63) / 64;
   const int nkb = p.causal ? min(nkb_all, (t0 + 127) / 64 + 1) : nkb_all;
@@ -661,10 +668,12 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     }
     for (int i = 0; i < 8; ++i) mbar_init(&mx_bar[i], 2);
     for (int i = 0; i < 4; ++i) mbar_init(&l_bar[i], 2);
-    mbar_init(kst_full, 1);
-    mbar_init(vst_full, 1);
-    mbar_init(kst_used, 4);
-    mbar_init(vst_used, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kst_full[i], 1);
+      mbar_init(&vst_full[i], 1);
+      mbar_init(&kst_used[i], 4);
+      mbar_init(&vst_used[i], 4);
+    }
     *abort = 0;
     mbar_fence_init();
   }
@@ -698,14 +707,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       for (int j = 0; j < nkb; ++j) {
         const int ks = j % NS, kuse = j / NS;
         if (X3) {
-          // one f32 staging buffer each for K and V: block j's K may land once
-          // block j-1's K has been split (while its V is being split)
-          if (j >= 1 && !mbar_wait(kst_used, (j - 1) & 1, abort, p.err, 211)) break;
-          mbar_expect_tx(kst_full, 64 * 64 * 4);
-          for (int c = 0; c < 2; ++c) tma_load_4d(k_st + c * 64 * 128, &tK, kst_full, c * 32, n, j * 64, b);
-          if (j >= 1 && !mbar_wait(vst_used, (j - 1) & 1, abort, p.err, 210)) break;
-          mbar_expect_tx(vst_full, 64 * 64 * 4);
-          for (int c = 0; c < 2; ++c) tma_load_4d(v_st + c * 64 * 128, &tV, vst_full, c * 32, n, j * 64, b);
+          // two f32 staging buffers each for K and V: block j's K may land in
+          // buffer j % 2 once block j-2's K has been split out of it
+          const int bf = j & 1;
+          if (j >= 2 && !mbar_wait(&kst_used[bf], ((j - 2) >> 1) & 1, abort, p.err, 211)) break;
+          mbar_expect_tx(&kst_full[bf], 64 * 64 * 4);
+          for (int c = 0; c < 2; ++c)
+            tma_load_4d(k_st(bf) + c * 64 * 128, &tK, &kst_full[bf], c * 32, n, j * 64, b);
+          if (j >= 2 && !mbar_wait(&vst_used[bf], ((j - 2) >> 1) & 1, abort, p.err, 210)) break;
+          mbar_expect_tx(&vst_full[bf], 64 * 64 * 4);
+          for (int c = 0; c < 2; ++c)
+            tma_load_4d(v_st(bf) + c * 64 * 128, &tV, &vst_full[bf], c * 32, n, j * 64, b);
         } else {
           if (j >= NS && !mbar_wait(&kv_free[ks], (kuse - 1) & 1, abort, p.err, 211)) break;
           mbar_expect_tx(&kv_full[ks], 2 * 64 * 64 * 2);
@@ -773,18 +785,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         for (int j = 0; j < nkb; ++j) {
           const int ks = j % NS, kuse = j / NS;
           ok = j < NS || mbar_wait(&kv_free[ks], (kuse - 1) & 1, abort, p.err, 219);
-          ok = ok && mbar_wait(kst_full, j & 1, abort, p.err, 218);
+          const int bf = j & 1;
+          ok = ok && mbar_wait(&kst_full[bf], (j >> 1) & 1, abort, p.err, 218);
           if (!__all_sync(0xffffffffu, ok)) break;
-          split_rows(k_st, k_hi(ks), k_lo(ks), 64, ctid);
+          split_rows(k_st(bf), k_hi(ks), k_lo(ks), 64, ctid);
           __syncwarp();
-          if (lane == 0) mbar_arrive(kst_used);
-          ok = mbar_wait(vst_full, j & 1, abort, p.err, 224);
+          if (lane == 0) mbar_arrive(&kst_used[bf]);
+          ok = mbar_wait(&vst_full[bf], (j >> 1) & 1, abort, p.err, 224);
           if (!__all_sync(0xffffffffu, ok)) break;
-          split_rows(v_st, v_hi(ks), v_lo(ks), 64, ctid);
+          split_rows(v_st(bf), v_hi(ks), v_lo(ks), 64, ctid);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive(vst_used);
+            mbar_arrive(&vst_used[bf]);
             mbar_arrive(&kv_conv[ks]);
           }
         }
@@ -964,8 +977,9 @@ int launch_ws(const void* q, const void* k, const void* v, void* o, int64_t B, i
   a.err = device_error_word();
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_ws<X3>, C::SMEM, "sdpa_fwd_ws")) return rc;
-  dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
-  B200_LAUNCH(sdpa_fwd_ws<X3>, grid, dim3(kWsThreads), C::SMEM, s, tq, tk, tv, a);
+  const int64_t ctas = (T + 127) / 128 * N * B;
+  if (ctas >= (1ll << 31)) return set_error(B200_ERR_INVALID, "sdpa: too many query tiles");
+  B200_LAUNCH(sdpa_fwd_ws<X3>, dim3((unsigned)ctas), dim3(kWsThreads), C::SMEM, s, tq, tk, tv, a);
   return B200_OK;
 }
 
