@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <set>
 #include <thread>
 
 #include "b200_kernels.h"
@@ -156,12 +157,12 @@ struct NcclWatchdog {
     th.join();
     for (auto& it : items) cudaEventDestroy(it.ev);
   }
-  void watch(Device& d, NcclComms* comms, std::shared_ptr<CollectiveStatus> status,
+  void watch(Device& d, cudaStream_t stream, NcclComms* comms, std::shared_ptr<CollectiveStatus> status,
              const std::string& what) {
     cudaEvent_t ev = nullptr;
     d.activate();
     B200_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-    B200_CUDA(cudaEventRecord(ev, d.stream));
+    B200_CUDA(cudaEventRecord(ev, stream));
     {
       std::lock_guard<std::mutex> lk(mu);
       items.push_back({ev, comms, std::move(status),
@@ -978,10 +979,90 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
   // collectives of this Execute: followed by events the client's NCCL
   // watchdog polls (its verdict reaches the Execute's events through cst)
   std::shared_ptr<CollectiveStatus> cst;
-  auto watch_collectives = [&](const std::vector<Device*>& dd, NcclComms& comm, const char* what) {
+  auto watch_collectives = [&](const std::vector<Device*>& dd, const std::vector<cudaStream_t>& ss,
+                               NcclComms& comm, const char* what) {
     if (!cst) cst = std::make_shared<CollectiveStatus>();
     if (!c->watchdog) c->watchdog = std::make_unique<NcclWatchdog>();
-    for (Device* d : dd) c->watchdog->watch(*d, &comm, cst, std::string(what) + " of " + e.name);
+    for (size_t i = 0; i < dd.size(); ++i)
+      c->watchdog->watch(*dd[i], ss[i], &comm, cst, std::string(what) + " of " + e.name);
+  };
+  // Collectives in flight on the communication streams (eager execution with
+  // B200_OVERLAP_COLLECTIVES): the slots they read or write, the event each
+  // device's communication stream records when it is done, and the temps whose
+  // release waits for it.  A later step touching one of those slots first makes
+  // its compute stream wait for the event; so does the end of the Execute.
+  struct InFlight {
+    std::set<int> slots;
+    std::vector<cudaEvent_t> done;
+    std::vector<int> release;
+  };
+  std::vector<InFlight> inflight;
+  bool async_coll = false;
+  auto root_of = [&](int sl) { return sl >= 0 && p.slots[sl].parent >= 0 ? p.slots[sl].parent : sl; };
+  auto retire = [&](InFlight& f) {
+    for (size_t d = 0; d < nd; ++d) {
+      Device& dev = *devs[d]->dev;
+      dev.activate();
+      B200_CUDA(cudaStreamWaitEvent(dev.stream, f.done[d], 0));
+      cudaEventDestroy(f.done[d]);
+      for (int sl : f.release) {
+        owned[d][sl].reset();
+        ptr[d][sl] = nullptr;
+      }
+    }
+  };
+  auto wait_for_slots = [&](const Step& st) {
+    if (inflight.empty()) return;
+    std::set<int> touched;
+    for (auto* v : {&st.in, &st.out})
+      for (int sl : *v)
+        if (sl >= 0) touched.insert(root_of(sl));
+    for (auto& a : st.args)
+      if (a.slot >= 0) touched.insert(root_of(a.slot));
+    for (size_t i = 0; i < inflight.size();) {
+      bool hit = false;
+      for (int sl : touched) hit = hit || inflight[i].slots.count(sl);
+      if (!hit) {
+        ++i;
+        continue;
+      }
+      retire(inflight[i]);
+      inflight.erase(inflight.begin() + (long)i);
+    }
+  };
+  // Order a collective on each device's communication stream after the
+  // compute stream's work so far; returns those streams.
+  auto comm_streams = [&](const std::vector<Device*>& dd) {
+    std::vector<cudaStream_t> ss;
+    for (Device* d : dd) {
+      d->activate();
+      if (!d->comm_stream) B200_CUDA(cudaStreamCreateWithFlags(&d->comm_stream, cudaStreamNonBlocking));
+      cudaEvent_t ev;
+      B200_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+      B200_CUDA(cudaEventRecord(ev, d->stream));
+      B200_CUDA(cudaStreamWaitEvent(d->comm_stream, ev, 0));
+      cudaEventDestroy(ev);
+      ss.push_back(d->comm_stream);
+    }
+    return ss;
+  };
+  auto track = [&](const Step& st, const std::vector<Device*>& dd, const std::vector<cudaStream_t>& ss,
+                   size_t si) {
+    InFlight f;
+    for (auto* v : {&st.in, &st.out})
+      for (int sl : *v)
+        if (sl >= 0) f.slots.insert(root_of(sl));
+    for (size_t d = 0; d < dd.size(); ++d) {
+      dd[d]->activate();
+      cudaEvent_t ev;
+      B200_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+      B200_CUDA(cudaEventRecord(ev, ss[d]));
+      f.done.push_back(ev);
+    }
+    for (auto* v : {&st.in, &st.out})
+      for (int sl : *v)
+        if (sl >= 0 && p.slots[sl].kind == Slot::TEMP && p.temp_last[sl] == (int)si) f.release.push_back(sl);
+    inflight.push_back(std::move(f));
   };
   auto exec_step = [&](size_t si, std::vector<std::vector<void*>>& ptr) {
     const Step& st = p.steps[si];
@@ -1012,8 +1093,11 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
       }
       if (e.num_replicas != 1) {
         NcclComms& comm = comms_for(c, e);
-        nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1]);
-        watch_collectives(dd, comm, "all_reduce bucket");
+        std::vector<cudaStream_t> ss;
+        if (async_coll) ss = comm_streams(dd);
+        else for (Device* d : dd) ss.push_back(d->stream);
+        nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1], ss);
+        watch_collectives(dd, ss, comm, "all_reduce bucket");
         for (size_t d = 0; d < nd; ++d) {
           Device& dev = *devs[d]->dev;
           dev.activate();
@@ -1022,8 +1106,9 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
             if (st.args[k].f != 1.f)  // (aliased pieces are read in place)
               B200_CUDA(cudaMemcpyAsync(ptr[d][st.args[k + 1].slot], bk + (size_t)st.args[k].i * es,
                                         (size_t)st.args[k + 1].i * es, cudaMemcpyDeviceToDevice,
-                                        dev.stream));
+                                        ss[d]));
         }
+        if (async_coll) track(st, dd, ss, si);
       }
     } else if (st.kind == StepKind::AllReduce) {
       std::vector<Device*> dd;
@@ -1042,8 +1127,12 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
         }
       } else {
         NcclComms& comm = comms_for(c, e);
-        nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1]);
-        watch_collectives(dd, comm, "all_reduce");
+        std::vector<cudaStream_t> ss;
+        if (async_coll) ss = comm_streams(dd);
+        else for (Device* d : dd) ss.push_back(d->stream);
+        nccl_all_reduce(dd, comm, in, out, st.ip[0], (DType)st.dtype, (int)st.ip[1], ss);
+        watch_collectives(dd, ss, comm, "all_reduce");
+        if (async_coll) track(st, dd, ss, si);
       }
     } else {
       for (size_t d = 0; d < nd; ++d) {
@@ -1115,12 +1204,14 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
     }
   } else {
   if (gs) gs->eager_runs++;
+  async_coll = overlap_collectives() && e.num_replicas > 1;
   for (size_t si = 0; si < p.steps.size(); ++si) {
     const Step& st = p.steps[si];
     for (size_t d = 0; d < nd; ++d) {
       for (int s : st.out) ensure(d, s);
       for (int s : st.in) ensure(d, s);
     }
+    wait_for_slots(st);
     exec_step(si, ptr);
     if (env_flag("B200_SYNC_STEPS")) {
       for (size_t d = 0; d < nd; ++d) {
@@ -1129,15 +1220,19 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
         if (r != cudaSuccess) throw PjrtErr(13, "step " + st.name + " failed: " + cudaGetErrorString(r));
       }
     }
-    // release temps whose last use was this step (stream order makes reuse safe)
-    for (size_t d = 0; d < nd; ++d)
-      for (auto* v : {&st.in, &st.out})
-        for (int s : *v)
-          if (s >= 0 && p.slots[s].kind == Slot::TEMP && p.temp_last[s] == (int)si) {
-            owned[d][s].reset();
-            ptr[d][s] = nullptr;
-          }
+    // release temps whose last use was this step (stream order makes reuse
+    // safe; a collective in flight releases its own when it is waited for)
+    if (!(async_coll && st.kind == StepKind::AllReduce && e.num_replicas != 1))
+      for (size_t d = 0; d < nd; ++d)
+        for (auto* v : {&st.in, &st.out})
+          for (int s : *v)
+            if (s >= 0 && p.slots[s].kind == Slot::TEMP && p.temp_last[s] == (int)si) {
+              owned[d][s].reset();
+              ptr[d][s] = nullptr;
+            }
   }
+  for (auto& f : inflight) retire(f);  // outputs are complete only after every collective
+  inflight.clear();
   }
   if (timing) {
     devs[0]->dev->activate();

@@ -935,6 +935,54 @@ struct Builder {
       else if (nd.op == Op::AllReduce && !in_dep) mid.push_back(n);
       else tail.push_back(n);
     }
+    if (overlap_collectives() && mid.size() >= 2) {
+      // Data-parallel gradients are ready at different points of the
+      // backward pass.  Order the collectives by when their operands are
+      // ready and cut them into buckets of about B200_BUCKET_MB (default 12)
+      // MB; each bucket goes right after the node that completes its last
+      // operand, so its all-reduce (run on the communication stream) overlaps
+      // the rest of the backward pass.
+      std::vector<int> pos(g.nodes.size(), -1);
+      for (size_t i = 0; i < head.size(); ++i) pos[head[i]] = (int)i;
+      auto ready = [&](int n) {
+        int r = -1;
+        for (auto& o : g.nodes[n].operands) r = std::max(r, pos[o.node]);
+        return r;
+      };
+      std::stable_sort(mid.begin(), mid.end(), [&](int a, int b) { return ready(a) < ready(b); });
+      static const int64_t limit = [] {
+        const char* v = std::getenv("B200_BUCKET_MB");
+        const double mb = v ? std::atof(v) : 12.0;
+        return (int64_t)(std::max(mb, 0.001) * (1 << 20));
+      }();
+      std::map<int, std::vector<int>> after;  // head position -> collectives placed after it
+      std::vector<int> cur;
+      int64_t bytes = 0;
+      for (int n : mid) {
+        cur.push_back(n);
+        for (auto& r : g.nodes[n].results) bytes += r.bytes();
+        if (bytes >= limit) {
+          auto& dst = after[ready(cur.back())];
+          dst.insert(dst.end(), cur.begin(), cur.end());
+          cur.clear();
+          bytes = 0;
+        }
+      }
+      if (!cur.empty()) {
+        auto& dst = after[ready(cur.back())];
+        dst.insert(dst.end(), cur.begin(), cur.end());
+      }
+      std::vector<int> out;
+      auto it0 = after.find(-1);
+      if (it0 != after.end()) out.insert(out.end(), it0->second.begin(), it0->second.end());
+      for (size_t i = 0; i < head.size(); ++i) {
+        out.push_back(head[i]);
+        auto it = after.find((int)i);
+        if (it != after.end()) out.insert(out.end(), it->second.begin(), it->second.end());
+      }
+      out.insert(out.end(), tail.begin(), tail.end());
+      return out;
+    }
     head.insert(head.end(), mid.begin(), mid.end());
     head.insert(head.end(), tail.begin(), tail.end());
     return head;

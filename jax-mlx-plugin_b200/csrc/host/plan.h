@@ -74,6 +74,9 @@ struct Plan {
 };
 
 // Compile a parsed module into a Plan (throws PjrtErr on unsupported input).
+// B200_OVERLAP_COLLECTIVES (runtime.cc): gradient all-reduces in buckets
+// placed where their gradients are ready, run on a communication stream.
+bool overlap_collectives();
 Plan build_plan(const Module& m);
 
 // Human-readable listing of the plan (steps, kernels, slots).

@@ -449,9 +449,17 @@ std::unique_ptr<NcclComms> nccl_init_rank(Device* dev, int nranks, int rank,
   c->comms.push_back(comm);
   return c;
 }
+bool overlap_collectives() {
+  static const bool on = [] {
+    const char* v = getenv("B200_OVERLAP_COLLECTIVES");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 void nccl_all_reduce(const std::vector<Device*>& devs, NcclComms& c,
                      const std::vector<const void*>& in, const std::vector<void*>& out,
-                     int64_t count, DType dt, int op) {
+                     int64_t count, DType dt, int op, const std::vector<cudaStream_t>& streams) {
   auto& n = Nccl::get();
   ncclDataType_t t;
   switch (dt) {
@@ -469,7 +477,7 @@ void nccl_all_reduce(const std::vector<Device*>& devs, NcclComms& c,
   for (size_t i = 0; i < devs.size(); ++i) {
     devs[i]->activate();
     nccl_check(n.AllReduce(in[i], out[i], (size_t)count, t, ops[op], (ncclComm_t)c.comms.at(i),
-                           devs[i]->stream),
+                           streams.empty() ? devs[i]->stream : streams.at(i)),
                "ncclAllReduce");
   }
   nccl_check(n.GroupEnd(), "ncclGroupEnd");

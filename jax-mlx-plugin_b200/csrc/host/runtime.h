@@ -49,6 +49,10 @@ class Allocator {
 struct Device {
   int ordinal = 0;  // CUDA device ordinal in this process
   cudaStream_t stream = nullptr;
+  // Data-parallel collectives run here, ordered after the compute stream by
+  // events, so that a gradient bucket's all-reduce overlaps the rest of the
+  // backward pass (created with the first collective).
+  cudaStream_t comm_stream = nullptr;
   std::unique_ptr<Allocator> alloc;
   std::recursive_mutex mu;  // serializes submission to the stream
   std::string name;
@@ -105,6 +109,12 @@ std::unique_ptr<LoadedModule> load_module(Device& d, const std::vector<std::stri
 // GPU failing.  Unset: nothing happens.
 void fault_point(const char* where);
 
+// B200_OVERLAP_COLLECTIVES (default 1): gradient all-reduces are cut into
+// buckets placed where their gradients are ready, and run on each device's
+// communication stream; 0 runs them after the backward pass on the compute
+// stream.
+bool overlap_collectives();
+
 // Launch a generated kernel.
 void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[3], int smem,
             std::vector<void*>& args);
@@ -134,8 +144,10 @@ std::vector<char> nccl_unique_id();
 std::unique_ptr<NcclComms> nccl_init_all(const std::vector<Device*>& devs);
 std::unique_ptr<NcclComms> nccl_init_rank(Device* dev, int nranks, int rank,
                                           const std::vector<char>& uid);
+// On each device's `streams[i]` (its compute stream when empty).
 void nccl_all_reduce(const std::vector<Device*>& devs, NcclComms& c,
                      const std::vector<const void*>& in, const std::vector<void*>& out,
-                     int64_t count, DType dt, int op);
+                     int64_t count, DType dt, int op,
+                     const std::vector<cudaStream_t>& streams = {});
 
 }  // namespace b200
