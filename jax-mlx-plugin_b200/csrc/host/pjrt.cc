@@ -672,12 +672,15 @@ std::shared_ptr<Exe> compile(PJRT_Client* c, const std::string& code, const std:
       }
     }
     if (!todo.empty()) {
-      if (prebuilt && env_flag("B200_NO_JIT"))
+      if (prebuilt && env_flag("B200_NO_JIT")) {
+        std::string carried;
+        for (auto& kv : *prebuilt) carried += " [" + kv.first + "]";
         throw PjrtErr(9, "serialized executable: " + std::to_string(todo.size()) + " of " +
                              std::to_string(e->plan.units.size()) +
                              " kernel units of the re-planned program have no cubin in it (first "
-                             "missing key " + nvrtc_key(todo[0]) + ", " + std::to_string(prebuilt->size()) +
-                             " carried) and B200_NO_JIT=1 forbids compiling them");
+                             "missing key [" + nvrtc_key(todo[0]) + "]; carried:" + carried +
+                             ") and B200_NO_JIT=1 forbids compiling them");
+      }
       auto built = nvrtc_compile_all(todo, "b200_" + e->fingerprint);
       for (size_t i = 0; i < built.size(); ++i) e->cubins[todo_at[i]] = std::move(built[i]);
     }

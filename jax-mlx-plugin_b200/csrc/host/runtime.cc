@@ -388,12 +388,19 @@ bool nccl_available(std::string* why) {
   if (why) *why = n.why;
   return n.why.empty();
 }
+// Teardown is local: ncclCommAbort frees this process's ranks without the
+// synchronization with peers that ncclCommDestroy's implicit finalize does, so
+// a process whose peers already left (or are leaving at the same time) does
+// not wait on them.  The owner has drained its streams before this runs.
 NcclComms::~NcclComms() {
   auto& n = Nccl::get();
   std::lock_guard<std::mutex> lk(mu);
   if (aborted) return;  // ncclCommAbort already released them
-  for (void* c : comms)
-    if (c && n.CommDestroy) n.CommDestroy((ncclComm_t)c);
+  for (void* c : comms) {
+    if (!c) continue;
+    if (n.CommAbort) n.CommAbort((ncclComm_t)c);
+    else if (n.CommDestroy) n.CommDestroy((ncclComm_t)c);
+  }
 }
 std::string nccl_async_error(NcclComms& c) {
   auto& n = Nccl::get();
