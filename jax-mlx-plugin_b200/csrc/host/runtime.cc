@@ -176,13 +176,16 @@ std::string cache_path(const std::string& key) {
 }
 }  // namespace
 
+// The key names the source and the options, not the NVRTC build: an sm_100a
+// cubin from any NVRTC release loads on any driver that runs this plugin, and
+// one process may resolve libnvrtc to another release than the next (a
+// framework imported first can bring its own).  The on-disk cache file name
+// adds the NVRTC version on top.
 std::string nvrtc_key(const std::string& source) {
   static const std::string opt_text = [] {
     std::string t;
     for (const char* o : kNvrtcOpts) t += std::string(o) + " ";
-    int ver[2] = {0, 0};
-    nvrtcVersion(&ver[0], &ver[1]);
-    return t + "nvrtc" + std::to_string(ver[0]) + "." + std::to_string(ver[1]) + " ";
+    return t;
   }();
   return source_key(opt_text + source);
 }

@@ -80,9 +80,9 @@ struct DeviceMem {
 // B200_NO_JIT=1: refuse to compile (an executable must arrive with its
 // cubins, e.g. through PJRT_Executable_DeserializeAndLoad).
 std::string nvrtc_compile(const std::string& source, const std::string& name);
-// The key nvrtc_compile files a source's cubin under: it names the source, the
-// NVRTC options and the NVRTC version, so a cubin stored under it (e.g. in a
-// serialized executable) is valid for exactly that compile.
+// The key nvrtc_compile files a source's cubin under: it names the source and
+// the NVRTC options, so a cubin stored under it (e.g. in a serialized
+// executable) is valid for exactly that source.
 std::string nvrtc_key(const std::string& source);
 // Several sources compiled on parallel threads (one cubin each, same order).
 std::vector<std::string> nvrtc_compile_all(const std::vector<std::string>& sources,
