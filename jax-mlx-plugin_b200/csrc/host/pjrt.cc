@@ -1267,6 +1267,20 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
 // ------------------------------------------------------ client creation --
 std::string device_kind() { return "NVIDIA B200"; }
 
+// Clients still alive when the process exits (a caller that never destroyed
+// its client): their collective watchdogs are stopped and communicators
+// released by an exit hook, before the CUDA runtime's own teardown, so no
+// helper thread or NCCL resource outlives the runtime under it.
+std::mutex g_clients_mu;
+std::set<PJRT_Client*> g_clients;
+void teardown_live_clients() {
+  std::lock_guard<std::mutex> lk(g_clients_mu);
+  for (PJRT_Client* c : g_clients) {
+    c->watchdog.reset();
+    c->comms.clear();
+  }
+}
+
 PJRT_Client* create_client(const PJRT_Client_Create_Args* args) {
   auto c = std::make_unique<PJRT_Client>();
   std::vector<int> visible;
@@ -1359,6 +1373,12 @@ PJRT_Client* create_client(const PJRT_Client_Create_Args* args) {
     }
   for (auto* d : c->device_ptrs) c->topo.descs.push_back(&d->desc);
   c->topo.version = c->version;
+  {
+    std::lock_guard<std::mutex> lk(g_clients_mu);
+    static const bool hooked = (std::atexit(teardown_live_clients), true);
+    (void)hooked;
+    g_clients.insert(c.get());
+  }
   return c.release();
 }
 
@@ -1531,6 +1551,10 @@ static PJRT_Error* Client_Destroy(PJRT_Client_Destroy_Args* a) {
   for (auto& d : c->local) {
     d->activate();
     cudaStreamSynchronize(d->stream);  // the watchdog still guards collectives here
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_clients_mu);
+    g_clients.erase(c);
   }
   c->watchdog.reset();
   c->comms.clear();

@@ -37,6 +37,10 @@ def main():
         with open(os.path.join(out, f"rank{rank}.stage"), "w") as f:
             f.write(s)
 
+    import faulthandler
+    fault_log = open(os.path.join(out, f"rank{rank}.fault"), "w")
+    faulthandler.enable(file=fault_log, all_threads=True)
+
     stage("init")
     import torch
     import torch.distributed as dist
@@ -75,6 +79,7 @@ def main():
         bf16 = len(params)
     args = [client.buffer_from_numpy(a, device=dev, bf16=i < bf16) for i, a in enumerate(arrays)]
     stage("execute")
+    outs = None
     try:
         outs = exe.execute([args])[0]
         stage("read")
@@ -85,6 +90,10 @@ def main():
             f.write(f"{e.code} {e}")
     stage("barrier")
     dist.barrier()
+    outs = None  # every buffer and executable goes before the client
+    del args, exe, outs
+    stage("client_destroy")
+    client.destroy()
     stage("done")
     dist.destroy_process_group()
 

@@ -221,7 +221,10 @@ def _run_ranks(tmp_path, kind, fault="", extra_env=None):
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     stages = {rk: (tmp_path / f"rank{rk}.stage").read_text() if (tmp_path / f"rank{rk}.stage").exists()
               else "not started" for rk in range(2)}
-    assert r.returncode == 0, f"ranks failed (rc {r.returncode}), stages {stages}: {r.stderr[-3000:]}"
+    faults = {rk: (tmp_path / f"rank{rk}.fault").read_text()[-2500:] for rk in range(2)
+              if (tmp_path / f"rank{rk}.fault").exists()}
+    assert r.returncode == 0, (f"ranks failed (rc {r.returncode}), stages {stages}, faults {faults}: "
+                               f"{r.stderr[-2000:]}")
 
 
 @needs2
