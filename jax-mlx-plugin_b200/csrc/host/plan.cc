@@ -270,13 +270,14 @@ struct Builder {
     const int cv = rowlike ? 1 : CodeGen::column_vec(it, nd.dims);
     if (cv > 1) {
       // vector column reduction: blocks of kColWarps warps over 32 * cv
-      // outputs each; split the rows until about 8 blocks per SM, keeping at
-      // least 4 rows per warp and at most 64 partial rows to combine
+      // outputs each; split the rows until about 8 blocks per SM (a full SM
+      // of loads in flight), keeping at least 4 rows per warp and at most 512
+      // partial rows to combine
       if (RED < 8 * CodeGen::kColWarps) return 1;
       const int64_t bx = (OUT / cv + 31) / 32;
       int64_t split = (148 * 8) / std::max<int64_t>(bx, 1);
       split = std::min<int64_t>(split, RED / (4 * CodeGen::kColWarps));
-      split = std::min<int64_t>(split, 64);
+      split = std::min<int64_t>(split, 512);
       return (int)std::max<int64_t>(split, 1);
     }
     const int64_t threads = rowlike ? OUT * 32 : OUT * (OUT < 148 * 32 * 4 ? 32 : 8);
