@@ -73,6 +73,12 @@ class CodeGen {
   // bf16 hi / lo planes for an f32 GEMM (x ~= hi + lo).
   GenKernel im2col(int node, int out_slot, const std::vector<int64_t>& k_roles,
                    const std::vector<int64_t>& m_roles, int64_t M, int64_t K, int lo_slot = -1);
+  // The same patches stored transposed ([K, M], M innermost) as bf16 hi / lo
+  // planes, eight M columns per thread; only when the innermost M role is the
+  // output batch dimension, fed by the input's innermost dimension, with M a
+  // multiple of 8 and the input an f32 slot (see plan.cc:lower_conv).
+  GenKernel im2col_t(int node, int out_slot, const std::vector<int64_t>& k_roles,
+                     const std::vector<int64_t>& m_roles, int64_t M, int64_t K, int lo_slot);
   // out[j] = src[permuted j]: out dims are src dims[perm[i]] (a transpose copy).
   GenKernel permute(int src_slot, const std::vector<int64_t>& perm, int out_slot);
   // Several row-wise phases over the same OUT rows of RED elements in one

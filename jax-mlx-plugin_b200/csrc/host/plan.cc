@@ -441,14 +441,29 @@ struct Builder {
     // f32 patches go straight to the GEMM's bf16 hi / lo planes when their
     // rows are 16-byte multiples in bf16 (no f32 patch matrix, no split pass)
     const bool planes = lt.dtype == DType::F32 && K % 8 == 0;
+    // A weight-gradient-shaped convolution (innermost M role = output batch,
+    // read from the input's innermost dimension) writes its patches
+    // transposed, [K, M] with eight channels of one input pixel per thread;
+    // the GEMM reads that A MN-major.
+    const bool transposed = lt.dtype == DType::F32 && !m_roles.empty() &&
+                            m_roles.back() == c.out_batch && ot.dims[c.out_batch] % 8 == 0 &&
+                            c.in_batch == lt.rank() - 1 &&
+                            !(k_roles.back() == c.k_in && kt.dims[c.k_in] % 8 == 0 &&
+                              c.in_feature == lt.rank() - 1) &&
+                            slot.count(nd.operands[0]) != 0;
     int as, al = -1;
-    if (planes) {
+    if (transposed) {
+      as = new_slot(Slot::TEMP, TensorType{DType::BF16, {K, M}}, "im2col_t_hi");
+      al = new_slot(Slot::TEMP, TensorType{DType::BF16, {K, M}}, "im2col_t_lo");
+      add_kernel(cg.im2col_t(n, as, k_roles, m_roles, M, K, al));
+    } else if (planes) {
       as = new_slot(Slot::TEMP, TensorType{DType::BF16, {M, K}}, "im2col_hi");
       al = new_slot(Slot::TEMP, TensorType{DType::BF16, {M, K}}, "im2col_lo");
+      add_kernel(cg.im2col(n, as, k_roles, m_roles, M, K, al));
     } else {
       as = new_slot(Slot::TEMP, TensorType{lt.dtype, {M, K}}, "im2col");
+      add_kernel(cg.im2col(n, as, k_roles, m_roles, M, K, al));
     }
-    add_kernel(cg.im2col(n, as, k_roles, m_roles, M, K, al));
     int ks = slot.at(nd.operands[1]);
     Group bk, bn;
     if (c.k_out == kt.rank() - 1) {
@@ -463,6 +478,7 @@ struct Builder {
     }
     Group ab, am, ak, bb;
     am.size = M; am.stride = K; ak.size = K; ak.stride = 1;
+    if (transposed) { am.stride = 1; ak.stride = M; }
     const bool direct = c.out_feature == ot.rank() - 1;
     int cs;
     if (direct) {
@@ -471,7 +487,7 @@ struct Builder {
       cs = new_slot(Slot::TEMP, TensorType{ot.dtype, {M, N}}, "conv_out_MN");
     }
     emit_gemm(as, ks, cs, 1, M, N, K, ab, am, ak, bb, bk, bn, (int)lt.dtype, ot.dtype);
-    if (planes) {  // A arrives split: its lo plane (see the executor's GEMM step)
+    if (planes || transposed) {  // A arrives split: its lo plane (see the executor's GEMM step)
       Step& g = p.steps.back();
       Arg alo, blo;
       alo.slot = al;
