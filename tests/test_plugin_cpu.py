@@ -175,14 +175,19 @@ def test_gemm_operands_arrive_as_planes():
     assert [slots[s][1] for s in f32] == ["tensor<200704x9xf32>"]
     for s in f32:
         del im2col_out[s]
-    assert len(im2col_out) == 8 and all(n in ("im2col_hi", "im2col_lo") for n in im2col_out.values())
+    # the weight gradient of the second conv stores its patches transposed
+    # ([K, M], eight channels of one pixel per thread); the rest as [M, K]
+    assert len(im2col_out) == 8 and all(n in ("im2col_hi", "im2col_lo", "im2col_t_hi", "im2col_t_lo")
+                                        for n in im2col_out.values())
+    assert sorted(slots[s][1] for s, n in im2col_out.items() if n.startswith("im2col_t")) == \
+        ["tensor<50176x288xbf16>"] * 2
     assert all(slots[s][1].endswith("xbf16>") for s in im2col_out)
     gemms = [ins for name, ins in rows if name == "gemm"]
     for s, n in im2col_out.items():
         readers = [ins for ins in gemms if s in ins]
         assert len(readers) == 1 and len(readers[0]) == 3
         # hi is the A operand, lo the trailing plane input
-        assert readers[0].index(s) == (0 if n == "im2col_hi" else 2)
+        assert readers[0].index(s) == (0 if n.endswith("_hi") else 2)
 
 
 def test_attention_operands_are_written_in_gemm_order():
