@@ -137,7 +137,9 @@ class CodeGen {
   // use the approximate hardware forms, as bf16-typed nodes do -- the result
   // is rounded to 8 significant bits anyway.
   std::set<int> bf16_sink_;
-  void mark_bf16_sinks(const std::vector<ValueRef>& roots);
+  // out_slots (optional, parallel to roots): a root stored as a GEMM's bf16
+  // hi / lo planes (about 16 significant bits) counts as a bf16 sink too.
+  void mark_bf16_sinks(const std::vector<ValueRef>& roots, const std::vector<int>* out_slots = nullptr);
   // Set while emitting a reduction's combiner: bf16 partial results stay in
   // f32 and are rounded once when stored (XLA accumulates bf16 reductions in
   // f32 rather than rounding after every add).
