@@ -88,6 +88,32 @@ B200_API int b200_sdpa_fwd_strided(const void* q, const void* k, const void* v, 
                                    const int64_t* strides, float scale, int causal, int dtype,
                                    void* stream);
 
+/* b200_sdpa_fwd_strided that also writes each query row's softmax statistic
+ * lse2[b, n, t] = log2(sum_s 2^(scale * log2(e) * q_t.k_s)) (masked keys
+ * excluded), f32 [B, N, T] contiguous, for b200_sdpa_bwd.  Tensor-core path
+ * only: D == 64, scale > 0, 16-byte aligned operands and strides; anything
+ * else returns B200_ERR_UNSUPPORTED. */
+B200_API int b200_sdpa_fwd_lse(const void* q, const void* k, const void* v, void* o, float* lse2,
+                               int64_t B, int64_t T, int64_t S, int64_t N, int64_t D,
+                               const int64_t* strides, float scale, int causal, int dtype,
+                               void* stream);
+
+/* Attention backward for O = softmax(scale * Q K^T + mask) V (S == T):
+ *   dV = P^T dO,  dS = P * (dO V^T - rowsum(dO * O)) * scale,
+ *   dQ = dS K,    dK = dS^T Q,
+ * with P recomputed from lse2 (b200_sdpa_fwd_lse) and never stored.  All of
+ * q, k, v, o, dout, dq, dk, dv are bf16 with the head dim contiguous; strides
+ * (elements) are (b, t, n) for q, k, v, o, dout, dq, dk, dv in that order (24
+ * values, each a multiple of 8).  Needs D == 64 and T <= 256; other shapes
+ * and dtypes return B200_ERR_UNSUPPORTED.  P and dS enter the tensor-core
+ * products as bf16, accumulation is f32.  Replaces reference
+ * src/jax_mlx_pjrt.cpp:8152-8206 (mlx_sdpa_bwd through mx::vjp) and the math
+ * of src/jax_mlx/sdpa.py:65-87. */
+B200_API int b200_sdpa_bwd(const void* q, const void* k, const void* v, const void* o,
+                           const void* dout, const float* lse2, void* dq, void* dk, void* dv,
+                           int64_t B, int64_t T, int64_t N, int64_t D, const int64_t* strides,
+                           float scale, int causal, int dtype, void* stream);
+
 /* Batched GEMM on tcgen05: for b in [0,batch):
  *   C_b[m,n] = alpha * sum_k A_b[m,k] * B_b[k,n]  (+ bias[n]) (+ relu)
  * A element (b,m,k) at a + b*sAb + m*sAm + k*sAk (strides in elements), one of

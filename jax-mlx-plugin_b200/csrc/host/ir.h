@@ -60,7 +60,7 @@ enum class Op : uint16_t {
   // structure
   Call, Return, OptimizationBarrier, Tuple, GetTupleElement,
   // fused ops created by the pattern matcher
-  FusedSdpa, FusedLayerNorm,
+  FusedSdpa, FusedLayerNorm, FusedSdpaBwd,
   NumOps
 };
 const char* op_name(Op op);
@@ -141,7 +141,7 @@ struct Node {
   int64_t channel_id = 0;
   // fused ops (pattern matcher): scalar parameters
   float f_scale = 1.f, f_eps = 0.f;
-  int i_flags = 0;                 // FusedSdpa: bit0 causal; FusedLayerNorm: bit0 rms, bit1 has residual, bit2 has gamma, bit3 has beta, bit4 emits h
+  int i_flags = 0;                 // FusedSdpa: bit0 causal, bit1 emits row statistics; FusedSdpaBwd: bit0 causal; FusedLayerNorm: bit0 rms, bit1 has residual, bit2 has gamma, bit3 has beta, bit4 emits h
   bool dead = false;
 };
 

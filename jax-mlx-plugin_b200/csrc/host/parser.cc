@@ -90,6 +90,7 @@ static const std::pair<const char*, Op> kOpNames[] = {
     {"return", Op::Return}, {"optimization_barrier", Op::OptimizationBarrier},
     {"tuple", Op::Tuple}, {"get_tuple_element", Op::GetTupleElement},
     {"fused_sdpa", Op::FusedSdpa}, {"fused_layer_norm", Op::FusedLayerNorm},
+    {"fused_sdpa_bwd", Op::FusedSdpaBwd},
 };
 
 const char* op_name(Op op) {

@@ -444,98 +444,131 @@ struct Matcher {
     return true;
   }
 
+  // The forward chain ending at dot_general node `i`:
+  //   d1 = dot_general(Q, K) -> [* scale] -> [select(mask, ., -big)] ->
+  //   softmax -> [convert] -> d2 = dot_general(P, V)
+  // with batch {B, N}, Q / K contracted over the head dim and P over keys.
+  struct AttnFwd {
+    std::set<int> nodes;  // d1 .. d2, without the mask chain
+    int d1 = -1, d2 = -1;
+    ValueRef p, pb, e, sum;  // softmax quotient, its convert (== p if none), exp, row-sum reduce
+    ValueRef mask{-1, 0};    // select predicate (through broadcasts), if masked
+    int keep = 0;            // select operand that carries the logits (1 or 2)
+    double scale = 1.0;
+    int causal = 0;
+    int64_t qb = 0, qn = 0, qt = 0, qd = 0, kb = 0, kn = 0, ks = 0, kd = 0;
+    int64_t vb = 0, vn = 0, vs = 0, vd = 0;
+    int64_t B = 0, T = 0, S = 0, H = 0, D = 0;
+  };
+
+  bool attn_forward(int i, AttnFwd& f) const {
+    const Node& d2 = g.nodes[i];
+    if (d2.dead || d2.op != Op::DotGeneral) return false;
+    f.d2 = i;
+    f.nodes.insert(i);
+    // lhs of the second dot: softmax output, maybe converted
+    ValueRef pv = d2.operands[0];
+    f.pb = pv;
+    if (N(pv).op == Op::Convert) { f.nodes.insert(pv.node); pv = N(pv).operands[0]; }
+    f.p = pv;
+    ValueRef logits;
+    if (!softmax(pv, &logits, f.nodes)) return false;
+    f.e = N(pv).operands[0];
+    f.sum = strip_bcast(N(pv).operands[1]);
+    if (N(logits).op == Op::Convert) { f.nodes.insert(logits.node); logits = N(logits).operands[0]; }
+    // optional causal select
+    if (N(logits).op == Op::Select) {
+      const Node& s = N(logits);
+      int keep = -1;
+      for (int side = 1; side <= 2; ++side) {
+        auto c = scalar_const(s.operands[side]);
+        if (c && *c < -1e30) keep = 3 - side;
+      }
+      if (keep < 0) return false;
+      std::vector<int> mch;
+      ValueRef msrc = strip_bcast(s.operands[0], &mch);
+      auto mask = host_eval(g, msrc, 1 << 24);
+      if (!mask) return false;
+      // mask source dims must end with (T, S); leading dims are 1
+      const auto& md = mask->type.dims;
+      if (md.size() < 2) return false;
+      const int64_t T = md[md.size() - 2], S = md[md.size() - 1];
+      bool lead1 = true;
+      for (size_t k = 0; k + 2 < md.size(); ++k) lead1 &= md[k] == 1;
+      if (!lead1) return false;
+      bool is_tril = true, all_true = true;
+      for (int64_t t = 0; t < T && (is_tril || all_true); ++t)
+        for (int64_t sidx = 0; sidx < S; ++sidx) {
+          bool m = mask->v[t * S + sidx] != 0;
+          if (keep == 2) m = !m;  // select(pred, -big, x): pred marks masked-out
+          if (m != (sidx <= t)) is_tril = false;
+          if (!m) all_true = false;
+        }
+      if (!is_tril && !all_true) return false;
+      f.causal = is_tril && !all_true;
+      f.keep = keep;
+      f.mask = msrc;
+      f.nodes.insert(logits.node);
+      for (int c : mch)
+        if (u.count(c) == 1) f.nodes.insert(c);
+      logits = s.operands[keep];
+    }
+    // optional scale
+    {
+      const Node& m = N(logits);
+      if (m.op == Op::Mul || m.op == Op::Div) {
+        for (int side = 0; side < 2; ++side) {
+          if (m.op == Op::Div && side == 0) continue;
+          auto c = scalar_const(m.operands[side]);
+          if (c) {
+            f.scale = m.op == Op::Mul ? *c : 1.0 / *c;
+            f.nodes.insert(logits.node);
+            logits = m.operands[1 - side];
+            break;
+          }
+        }
+      }
+    }
+    const Node& d1 = N(logits);
+    if (d1.op != Op::DotGeneral) return false;
+    f.d1 = logits.node;
+    f.nodes.insert(logits.node);
+    // roles of Q, K in d1 and of P, V in d2
+    const TensorType &qt = g.type(d1.operands[0]), &kt = g.type(d1.operands[1]);
+    const TensorType& vt = g.type(d2.operands[1]);
+    if (!roles(d1.lhs_batch, d1.lhs_contract, qt.rank(), &f.qb, &f.qn, &f.qt, &f.qd)) return false;
+    if (!roles(d1.rhs_batch, d1.rhs_contract, kt.rank(), &f.kb, &f.kn, &f.ks, &f.kd)) return false;
+    // d1 result is [B, N, T, S]; d2 lhs is that, batch {0,1}, contract {3}
+    if (d2.lhs_batch != std::vector<int64_t>{0, 1} || d2.lhs_contract != std::vector<int64_t>{3})
+      return false;
+    if (vt.rank() != 4 || d2.rhs_batch.size() != 2 || d2.rhs_contract.size() != 1) return false;
+    f.vb = d2.rhs_batch[0], f.vn = d2.rhs_batch[1], f.vs = d2.rhs_contract[0], f.vd = -1;
+    for (int64_t k = 0; k < 4; ++k)
+      if (k != f.vb && k != f.vn && k != f.vs) f.vd = k;
+    f.B = qt.dims[f.qb], f.T = qt.dims[f.qt], f.H = qt.dims[f.qn], f.D = qt.dims[f.qd];
+    f.S = kt.dims[f.ks];
+    if (kt.dims[f.kb] != f.B || kt.dims[f.kn] != f.H || kt.dims[f.kd] != f.D) return false;
+    if (vt.dims[f.vb] != f.B || vt.dims[f.vn] != f.H || vt.dims[f.vs] != f.S) return false;
+    if (qt.dtype != kt.dtype || qt.dtype != vt.dtype) return false;
+    if (qt.dtype != DType::F32 && qt.dtype != DType::BF16) return false;
+    if (f.D != 64) return false;
+    return true;
+  }
+
+  static std::vector<int64_t> dense_strides(const TensorType& t) {
+    std::vector<int64_t> s(t.rank(), 1);
+    for (int k = t.rank() - 2; k >= 0; --k) s[k] = s[k + 1] * t.dims[k + 1];
+    return s;
+  }
+
   int match_sdpa() {
     int count = 0;
     for (size_t i = 0; i < g.nodes.size(); ++i) {
-      Node& d2 = g.nodes[i];
-      if (d2.dead || d2.op != Op::DotGeneral) continue;
-      std::set<int> nodes;
-      nodes.insert((int)i);
-      // lhs of the second dot: softmax output, maybe converted
-      ValueRef pv = d2.operands[0];
-      if (N(pv).op == Op::Convert) { nodes.insert(pv.node); pv = N(pv).operands[0]; }
-      ValueRef logits;
-      if (!softmax(pv, &logits, nodes)) continue;
-      if (N(logits).op == Op::Convert) { nodes.insert(logits.node); logits = N(logits).operands[0]; }
-      // optional causal select
-      int causal = 0;
-      if (N(logits).op == Op::Select) {
-        const Node& s = N(logits);
-        int keep = -1;
-        double neg = 0;
-        for (int side = 1; side <= 2; ++side) {
-          auto c = scalar_const(s.operands[side]);
-          if (c && *c < -1e30) { keep = 3 - side; neg = *c; }
-        }
-        (void)neg;
-        if (keep < 0) continue;
-        std::vector<int> mch;
-        ValueRef msrc = strip_bcast(s.operands[0], &mch);
-        auto mask = host_eval(g, msrc, 1 << 24);
-        if (!mask) continue;
-        // mask source dims must end with (T, S); leading dims are 1
-        const auto& md = mask->type.dims;
-        if (md.size() < 2) continue;
-        const int64_t T = md[md.size() - 2], S = md[md.size() - 1];
-        bool lead1 = true;
-        for (size_t k = 0; k + 2 < md.size(); ++k) lead1 &= md[k] == 1;
-        if (!lead1) continue;
-        bool is_tril = true, all_true = true;
-        for (int64_t t = 0; t < T && (is_tril || all_true); ++t)
-          for (int64_t sidx = 0; sidx < S; ++sidx) {
-            bool m = mask->v[t * S + sidx] != 0;
-            if (keep == 2) m = !m;  // select(pred, -big, x): pred marks masked-out
-            if (m != (sidx <= t)) is_tril = false;
-            if (!m) all_true = false;
-          }
-        if (!is_tril && !all_true) continue;
-        causal = is_tril && !all_true;
-        nodes.insert(logits.node);
-        for (int c : mch)
-          if (u.count(c) == 1) nodes.insert(c);
-        logits = s.operands[keep];
-      }
-      // optional scale
-      double scale = 1.0;
-      {
-        const Node& m = N(logits);
-        if (m.op == Op::Mul || m.op == Op::Div) {
-          for (int side = 0; side < 2; ++side) {
-            if (m.op == Op::Div && side == 0) continue;
-            auto c = scalar_const(m.operands[side]);
-            if (c) {
-              scale = m.op == Op::Mul ? *c : 1.0 / *c;
-              nodes.insert(logits.node);
-              logits = m.operands[1 - side];
-              break;
-            }
-          }
-        }
-      }
-      const Node& d1 = N(logits);
-      if (d1.op != Op::DotGeneral) continue;
-      nodes.insert(logits.node);
-      // roles of Q, K in d1 and of P, V in d2
-      const TensorType &qt = g.type(d1.operands[0]), &kt = g.type(d1.operands[1]);
-      const TensorType& vt = g.type(d2.operands[1]);
-      int64_t qb = 0, qn = 0, qt_ = 0, qd = 0, kb = 0, kn = 0, ks = 0, kd = 0;
-      if (!roles(d1.lhs_batch, d1.lhs_contract, qt.rank(), &qb, &qn, &qt_, &qd)) continue;
-      if (!roles(d1.rhs_batch, d1.rhs_contract, kt.rank(), &kb, &kn, &ks, &kd)) continue;
-      // d1 result is [B, N, T, S]; d2 lhs is that, batch {0,1}, contract {3}
-      if (d2.lhs_batch != std::vector<int64_t>{0, 1} || d2.lhs_contract != std::vector<int64_t>{3})
-        continue;
-      if (vt.rank() != 4 || d2.rhs_batch.size() != 2 || d2.rhs_contract.size() != 1) continue;
-      int64_t vb = d2.rhs_batch[0], vn = d2.rhs_batch[1], vs = d2.rhs_contract[0], vd = -1;
-      for (int64_t k = 0; k < 4; ++k)
-        if (k != vb && k != vn && k != vs) vd = k;
-      if (qd != 3 || kd != 3 || vd != 3) continue;  // head dim must be contiguous
-      const int64_t B = qt.dims[qb], T = qt.dims[qt_], H = qt.dims[qn], D = qt.dims[qd];
-      const int64_t S = kt.dims[ks];
-      if (kt.dims[kb] != B || kt.dims[kn] != H || kt.dims[kd] != D) continue;
-      if (vt.dims[vb] != B || vt.dims[vn] != H || vt.dims[vs] != S) continue;
-      if (qt.dtype != kt.dtype || qt.dtype != vt.dtype) continue;
-      if (qt.dtype != DType::F32 && qt.dtype != DType::BF16) continue;
-      if (D != 64) continue;
+      AttnFwd f;
+      if (!attn_forward((int)i, f)) continue;
+      const Node& d1 = N(f.d1);
+      const Node& d2 = N(f.d2);
+      if (f.qd != 3 || f.kd != 3 || f.vd != 3) continue;  // head dim must be contiguous
       // output: d2 gives [B, N, T, D]; an exclusive transpose to BTND is folded in
       ValueRef outv{(int)i, 0};
       std::vector<int64_t> out_perm = {0, 1, 2, 3};  // out tensor dim k holds role out_perm[k]
@@ -544,39 +577,466 @@ struct Matcher {
         if (tr.op == Op::Transpose) {
           outv = ValueRef{u.users[i][0], 0};
           out_perm = tr.dims;
-          nodes.insert(outv.node);
+          f.nodes.insert(outv.node);
         }
       }
-      std::set<int> inner = nodes;
+      std::set<int> inner = f.nodes;
       inner.erase(outv.node);
       if (!closed(inner, {outv.node})) continue;
       // strides (elements) of role b,t,n in Q/K/V/O; role order of d2 output: B,N,T,D
-      auto strides4 = [](const TensorType& t) {
-        std::vector<int64_t> s(4, 1);
-        for (int k = 2; k >= 0; --k) s[k] = s[k + 1] * t.dims[k + 1];
-        return s;
-      };
-      auto qs = strides4(qt), ks_ = strides4(kt), vs_ = strides4(vt);
+      auto qs = dense_strides(g.type(d1.operands[0])), ks_ = dense_strides(g.type(d1.operands[1]));
+      auto vs_ = dense_strides(g.type(d2.operands[1]));
       const TensorType& ot = g.type(outv);
-      auto os = strides4(ot);
+      auto os = dense_strides(ot);
       // role r (0=B,1=N,2=T,3=D) sits at output position p where out_perm[p] == r
       int64_t o_pos[4];
       for (int p = 0; p < 4; ++p) o_pos[out_perm[p]] = p;
       if (o_pos[3] != 3) continue;
-      Node f;
-      f.op = Op::FusedSdpa;
-      f.operands = {d1.operands[0], d1.operands[1], d2.operands[1]};
-      f.results = {ot};
-      f.name = g.nodes[outv.node].name;
-      f.f_scale = (float)scale;
-      f.i_flags = causal;
+      Node fn;
+      fn.op = Op::FusedSdpa;
+      fn.operands = {d1.operands[0], d1.operands[1], d2.operands[1]};
+      fn.results = {ot};
+      fn.name = g.nodes[outv.node].name;
+      fn.f_scale = (float)f.scale;
+      fn.i_flags = f.causal;
       // dims: B T S N D ; strides: q(b,t,n) k(b,s,n) v(b,s,n) o(b,t,n)
-      f.dims = {B, T, S, H, D};
-      f.strides = {qs[qb], qs[qt_], qs[qn], ks_[kb], ks_[ks], ks_[kn],
-                   vs_[vb], vs_[vs], vs_[vn], os[o_pos[0]], os[o_pos[2]], os[o_pos[1]]};
-      int fid = g.add(std::move(f));
+      fn.dims = {f.B, f.T, f.S, f.H, f.D};
+      fn.strides = {qs[f.qb], qs[f.qt], qs[f.qn], ks_[f.kb], ks_[f.ks], ks_[f.kn],
+                    vs_[f.vb], vs_[f.vs], vs_[f.vn], os[o_pos[0]], os[o_pos[2]], os[o_pos[1]]};
+      int fid = g.add(std::move(fn));
       replace_uses(outv, ValueRef{fid, 0});
-      for (int n : nodes) g.nodes[n].dead = true;
+      for (int n : f.nodes) g.nodes[n].dead = true;
+      u = compute_uses(g);
+      ++count;
+    }
+    return count;
+  }
+
+  // ------------------------------------------- attention with its backward --
+  // Role letters of a tensor's dims: b batch, n head, t query, s key, h head dim.
+  using Roles = std::string;
+  // A value seen through its transposes: the source and each role's element
+  // stride in the (dense, row-major) source.
+  struct View {
+    ValueRef src;
+    std::map<char, int64_t> st;
+    bool operator==(const View& o) const { return src == o.src && st == o.st; }
+  };
+  View view_of(ValueRef v, Roles r) const {
+    for (int k = 0; k < 8 && N(v).op == Op::Transpose; ++k) {
+      const Node& t = N(v);
+      Roles rs(r.size(), '?');
+      for (size_t d = 0; d < t.dims.size(); ++d) rs[t.dims[d]] = r[d];
+      r = rs;
+      v = t.operands[0];
+    }
+    View w;
+    w.src = v;
+    auto st = dense_strides(g.type(v));
+    for (size_t d = 0; d < r.size(); ++d) w.st[r[d]] = st[d];
+    return w;
+  }
+  static bool has(const std::vector<int64_t>& v, int64_t x) {
+    return std::find(v.begin(), v.end(), x) != v.end();
+  }
+  // Roles of the other operand of dot `d`, given one operand's: paired batch
+  // and contracting dims share a role, the single free dim gets `free_role`.
+  static std::optional<Roles> other_roles(const Node& d, bool known_lhs, const Roles& known,
+                                          int other_rank, char free_role) {
+    const auto& kb = known_lhs ? d.lhs_batch : d.rhs_batch;
+    const auto& kc = known_lhs ? d.lhs_contract : d.rhs_contract;
+    const auto& ob = known_lhs ? d.rhs_batch : d.lhs_batch;
+    const auto& oc = known_lhs ? d.rhs_contract : d.lhs_contract;
+    if (kb.size() != ob.size() || kc.size() != oc.size()) return std::nullopt;
+    Roles r(other_rank, '?');
+    for (size_t k = 0; k < kb.size(); ++k) r[ob[k]] = known[kb[k]];
+    for (size_t k = 0; k < kc.size(); ++k) r[oc[k]] = known[kc[k]];
+    int free = 0;
+    for (auto& c : r)
+      if (c == '?') { c = free_role; ++free; }
+    if (free != 1) return std::nullopt;
+    return r;
+  }
+  // Roles of a dot_general result: batch dims, then lhs free, then rhs free.
+  static Roles dot_out_roles(const Node& d, const Roles& lr, const Roles& rr) {
+    Roles o;
+    for (auto b : d.lhs_batch) o += lr[b];
+    for (int k = 0; k < (int)lr.size(); ++k)
+      if (!has(d.lhs_batch, k) && !has(d.lhs_contract, k)) o += lr[k];
+    for (int k = 0; k < (int)rr.size(); ++k)
+      if (!has(d.rhs_batch, k) && !has(d.rhs_contract, k)) o += rr[k];
+    return o;
+  }
+  // The contracted role of a dot whose operands carry roles lr / rr (all
+  // pairs must agree), or 0.
+  static char contracted(const Node& d, const Roles& lr, const Roles& rr) {
+    for (size_t k = 0; k < d.lhs_batch.size(); ++k)
+      if (lr[d.lhs_batch[k]] != rr[d.rhs_batch[k]]) return 0;
+    if (d.lhs_contract.size() != 1 || d.rhs_contract.size() != 1) return 0;
+    const char c = lr[d.lhs_contract[0]];
+    return c == rr[d.rhs_contract[0]] ? c : 0;
+  }
+  // Follow v through exclusive convert / transpose consumers; returns the last
+  // value and its roles.
+  ValueRef follow_out(ValueRef v, Roles& r) const {
+    for (int k = 0; k < 4; ++k) {
+      if (u.count(v.node) != 1 || u.output_refs[v.node]) break;
+      const Node& c = N(u.users[v.node][0]);
+      if (c.op == Op::Convert) {
+        v = ValueRef{u.users[v.node][0], 0};
+        continue;
+      }
+      if (c.op == Op::Transpose) {
+        Roles rs;
+        for (auto d : c.dims) rs += r[d];
+        r = rs;
+        v = ValueRef{u.users[v.node][0], 0};
+        continue;
+      }
+      break;
+    }
+    return v;
+  }
+
+  // Symbolic form of the softmax backward: every value of the region between
+  // dP and dS is a monomial factor c * P^p * sum^s * mask^m (no dP), or a sum
+  // of terms, each a monomial times dP or times the row sum of (monomial * dP).
+  // exp(x - max) is P * sum.
+  struct Mono {
+    int p = 0, s = 0, m = 0;
+    double c = 1.0;
+  };
+  struct Term {
+    Mono out, in;
+    bool rowsum = false;
+  };
+  struct Sym {
+    bool lin = false;  // terms (linear in dP) or a factor
+    Mono f;
+    std::vector<Term> t;
+  };
+  static Mono mono_mul(Mono a, const Mono& b, int sign = 1) {
+    a.p += sign * b.p;
+    a.s += sign * b.s;
+    a.m = std::max(a.m, b.m);
+    a.c = sign > 0 ? a.c * b.c : a.c / b.c;
+    return a;
+  }
+  std::optional<Sym> sym_eval(ValueRef v, const AttnFwd& f, ValueRef dp, int64_t S,
+                              std::map<ValueRef, std::optional<Sym>>& memo, int depth) const {
+    auto it = memo.find(v);
+    if (it != memo.end()) return it->second;
+    auto done = [&](std::optional<Sym> r) { memo[v] = r; return r; };
+    if (depth > 64) return done(std::nullopt);
+    Sym r;
+    if (v == dp) {
+      r.lin = true;
+      r.t.push_back(Term{});
+      return done(r);
+    }
+    if (v == f.p) { r.f.p = 1; return done(r); }
+    if (v == f.e) { r.f.p = 1; r.f.s = 1; return done(r); }
+    if (strip_bcast(v) == f.sum) { r.f.s = 1; return done(r); }
+    if (auto c = scalar_const(v)) { r.f.c = *c; return done(r); }
+    const Node& n = N(v);
+    auto ev = [&](int k) { return sym_eval(n.operands[k], f, dp, S, memo, depth + 1); };
+    switch (n.op) {
+      case Op::Mul: {
+        auto a = ev(0), b = ev(1);
+        if (!a || !b || (a->lin && b->lin)) return done(std::nullopt);
+        if (!a->lin && !b->lin) { r.f = mono_mul(a->f, b->f); return done(r); }
+        if (b->lin) std::swap(a, b);  // terms * factor
+        r = *a;
+        for (auto& t : r.t) t.out = mono_mul(t.out, b->f);
+        return done(r);
+      }
+      case Op::Div: {
+        auto a = ev(0), b = ev(1);
+        if (!a || !b || b->lin || b->f.m || b->f.c == 0.0) return done(std::nullopt);
+        if (!a->lin) { r.f = mono_mul(a->f, b->f, -1); return done(r); }
+        r = *a;
+        for (auto& t : r.t) t.out = mono_mul(t.out, b->f, -1);
+        return done(r);
+      }
+      case Op::Add: case Op::Sub: {
+        auto a = ev(0), b = ev(1);
+        if (!a || !b || !a->lin || !b->lin) return done(std::nullopt);
+        r = *a;
+        for (Term t : b->t) {
+          if (n.op == Op::Sub) t.out.c = -t.out.c;
+          r.t.push_back(t);
+        }
+        return done(r);
+      }
+      case Op::Neg: {
+        auto a = ev(0);
+        if (!a) return done(std::nullopt);
+        r = *a;
+        if (r.lin) for (auto& t : r.t) t.out.c = -t.out.c;
+        else r.f.c = -r.f.c;
+        return done(r);
+      }
+      case Op::Select: {
+        // select(mask, terms, 0) with the forward's mask and kept side
+        if (f.mask.node < 0 || !(strip_bcast(n.operands[0]) == f.mask)) return done(std::nullopt);
+        auto z = scalar_const(n.operands[3 - f.keep]);
+        if (!z || *z != 0.0) return done(std::nullopt);
+        auto a = ev(f.keep);
+        if (!a || !a->lin) return done(std::nullopt);
+        r = *a;
+        for (auto& t : r.t) t.out.m = 1;
+        return done(r);
+      }
+      case Op::Reduce: {
+        // sum over the key axis of terms without row sums
+        const TensorType& in = g.type(n.operands[0]);
+        if (reduce_kind(n) != Op::Add || n.operands.size() != 2 || in.rank() != 4 ||
+            n.dims != std::vector<int64_t>{3} || in.dims[3] != S)
+          return done(std::nullopt);
+        auto init = scalar_const(n.operands[1]);
+        auto a = ev(0);
+        if (!init || *init != 0.0 || !a || !a->lin) return done(std::nullopt);
+        r = *a;
+        for (auto& t : r.t) {
+          if (t.rowsum) return done(std::nullopt);
+          t.rowsum = true;
+          t.in = t.out;  // the non-row-constant part stays inside the sum
+          t.in.s = 0;
+          t.in.c = 1.0;
+          t.out.p = 0;
+          t.out.m = 0;
+        }
+        return done(r);
+      }
+      case Op::Reshape: case Op::BroadcastInDim: case Op::Convert: {
+        // layout ops between the row shape [B,N,T](,1) and [B,N,T,S]
+        const TensorType &it = g.type(n.operands[0]), &ot = n.results[0];
+        if (n.op == Op::Convert && (it.dtype != DType::F32 || ot.dtype != DType::F32))
+          return done(std::nullopt);
+        if (n.op != Op::Convert) {
+          auto lead = [](const TensorType& t) {
+            return std::vector<int64_t>(t.dims.begin(), t.dims.begin() + std::min(3, t.rank()));
+          };
+          if (it.rank() < 3 || ot.rank() < 3 || lead(it) != lead(ot)) return done(std::nullopt);
+          if (n.op == Op::BroadcastInDim)
+            for (int d = 0; d < std::min(3, it.rank()); ++d)
+              if (n.dims[d] != d) return done(std::nullopt);
+        }
+        return done(ev(0));
+      }
+      default:
+        return done(std::nullopt);
+    }
+  }
+  // Merge equal terms; true when the form is scale * (P dP - P rowsum(P dP))
+  // (mask factors allowed anywhere: P is zero where the mask is).
+  static bool is_softmax_bwd(std::vector<Term> t, double scale) {
+    std::vector<Term> m;
+    for (auto& x : t) {
+      bool merged = false;
+      for (auto& y : m)
+        if (y.rowsum == x.rowsum && y.out.p == x.out.p && y.out.s == x.out.s && y.out.m == x.out.m &&
+            (!x.rowsum || (y.in.p == x.in.p && y.in.s == x.in.s && y.in.m == x.in.m))) {
+          y.out.c += x.out.c;
+          merged = true;
+          break;
+        }
+      if (!merged) m.push_back(x);
+    }
+    double big = 0;
+    for (auto& x : m) big = std::max(big, std::fabs(x.out.c));
+    std::vector<Term> nz;
+    for (auto& x : m)
+      if (std::fabs(x.out.c) > 1e-9 * big) nz.push_back(x);
+    if (nz.size() != 2) return false;
+    const Term* d = nz[0].rowsum ? &nz[1] : &nz[0];
+    const Term* r = nz[0].rowsum ? &nz[0] : &nz[1];
+    if (d->rowsum || !r->rowsum) return false;
+    auto near = [](double a, double b) { return std::fabs(a - b) <= 1e-6 * std::fabs(b); };
+    return d->out.p == 1 && d->out.s == 0 && near(d->out.c, scale) && r->out.p == 1 && r->out.s == 0 &&
+           r->in.p == 1 && r->in.s == 0 && near(r->out.c, -scale);
+  }
+
+  // Causal or full attention whose probabilities also feed its backward (a
+  // jax.grad / value_and_grad program): the forward chain plus
+  //   dV = P^T dO, dP = dO V^T, dS = softmax-bwd(P, dP) * scale,
+  //   dQ = dS K, dK = dS^T Q
+  // becomes FusedSdpa (O and the row statistic) + FusedSdpaBwd (dQ, dK, dV).
+  // bf16 operands, head dim 64, T == S <= 256 (the backward kernel's limits).
+  int match_sdpa_train() {
+    int count = 0;
+    for (size_t i = 0; i < g.nodes.size(); ++i) {
+      AttnFwd f;
+      if (!attn_forward((int)i, f)) continue;
+      if (N(f.pb).op != Op::Convert) continue;  // bf16 probabilities
+      if (g.type(f.pb).dtype != DType::BF16 || f.T != f.S || f.T > 256) continue;
+      const Node& d1 = N(f.d1);
+      const Node& d2 = N(f.d2);
+      Roles qr(4, '?'), kr(4, '?'), vr(4, '?');
+      qr[f.qb] = 'b', qr[f.qn] = 'n', qr[f.qt] = 't', qr[f.qd] = 'h';
+      kr[f.kb] = 'b', kr[f.kn] = 'n', kr[f.ks] = 's', kr[f.kd] = 'h';
+      vr[f.vb] = 'b', vr[f.vn] = 'n', vr[f.vs] = 's', vr[f.vd] = 'h';
+      const View qv = view_of(d1.operands[0], qr), kv = view_of(d1.operands[1], kr);
+      const View vv = view_of(d2.operands[1], vr);
+      // dV = dot(P, dO): P's only consumer besides d2
+      const auto& pbu = u.users[f.pb.node];
+      if (pbu.size() != 2 || u.output_refs[f.pb.node]) continue;
+      const int dvi = pbu[0] == f.d2 ? pbu[1] : pbu[0];
+      const Node& dvn = N(dvi);
+      if (dvn.op != Op::DotGeneral || dvn.operands[0] == dvn.operands[1]) continue;
+      const bool p_lhs = dvn.operands[0] == f.pb;
+      const ValueRef gx = dvn.operands[p_lhs ? 1 : 0];
+      auto gr = other_roles(dvn, p_lhs, "bnts", g.type(gx).rank(), 'h');
+      if (!gr || contracted(dvn, p_lhs ? "bnts" : *gr, p_lhs ? *gr : "bnts") != 't') continue;
+      const View gv = view_of(gx, *gr);
+      Roles dvr = p_lhs ? dot_out_roles(dvn, "bnts", *gr) : dot_out_roles(dvn, *gr, "bnts");
+      // dP = dot(dO, V) with result roles b n t s, and its f32 value
+      int dpi = -1;
+      for (size_t k = 0; k < g.nodes.size() && dpi < 0; ++k) {
+        const Node& c = g.nodes[k];
+        if (c.dead || c.op != Op::DotGeneral || (int)k == dvi) continue;
+        if (g.type(c.operands[0]).rank() != 4 || g.type(c.operands[1]).rank() != 4) continue;
+        Roles lr(4, '?'), rr(4, '?');
+        // lhs: dO (roles from its batch / contract dims), rhs: V
+        auto try_roles = [&](const std::vector<int64_t>& bd, const std::vector<int64_t>& cd, char fr,
+                             Roles& out) {
+          if (bd.size() != 2 || cd.size() != 1) return false;
+          out[bd[0]] = 'b', out[bd[1]] = 'n', out[cd[0]] = 'h';
+          for (auto& ch : out)
+            if (ch == '?') ch = fr;
+          return true;
+        };
+        if (!try_roles(c.lhs_batch, c.lhs_contract, 't', lr) || !try_roles(c.rhs_batch, c.rhs_contract, 's', rr))
+          continue;
+        if (!(view_of(c.operands[0], lr) == gv) || !(view_of(c.operands[1], rr) == vv)) continue;
+        if (dot_out_roles(c, lr, rr) != "bnts") continue;
+        dpi = (int)k;
+      }
+      if (dpi < 0) continue;
+      ValueRef dp{dpi, 0};
+      if (g.type(dp).dtype != DType::F32) {
+        if (u.count(dpi) != 1 || u.output_refs[dpi] || N(u.users[dpi][0]).op != Op::Convert) continue;
+        dp = ValueRef{u.users[dpi][0], 0};
+        if (g.type(dp).dtype != DType::F32) continue;
+      }
+      // dS: the value both remaining products read; search forward from dP
+      std::set<int> region;
+      std::vector<int> stack = {dp.node};
+      std::set<int> dots;
+      bool bad = false;
+      while (!stack.empty() && !bad) {
+        const int x = stack.back();
+        stack.pop_back();
+        if (!region.insert(x).second) continue;
+        if (region.size() > 64) bad = true;
+        for (int c : u.users[x]) {
+          const Op op = g.nodes[c].op;
+          if (op == Op::DotGeneral) dots.insert(c);
+          else if (op == Op::Add || op == Op::Sub || op == Op::Mul || op == Op::Div || op == Op::Neg ||
+                   op == Op::Select || op == Op::Reduce || op == Op::Reshape ||
+                   op == Op::BroadcastInDim || op == Op::Convert)
+            stack.push_back(c);
+          else bad = true;
+        }
+      }
+      if (bad || dots.size() != 2) continue;
+      const int da = *dots.begin(), db = *dots.rbegin();
+      ValueRef ds{-1, 0};
+      for (const auto& o : N(da).operands)
+        for (const auto& o2 : N(db).operands)
+          if (o == o2 && region.count(o.node)) ds = o;
+      if (ds.node < 0 || g.type(ds).dtype != DType::F32) continue;
+      std::map<ValueRef, std::optional<Sym>> memo;
+      auto sym = sym_eval(ds, f, dp, f.S, memo, 0);
+      if (!sym || !sym->lin || !is_softmax_bwd(sym->t, f.scale)) continue;
+      // dQ = dot(dS, K) over keys, dK = dot(dS, Q) over queries
+      ValueRef dqf{-1, 0}, dkf{-1, 0};
+      Roles dqr, dkr;
+      bool ok = true;
+      for (int di : {da, db}) {
+        const Node& dn = N(di);
+        const bool s_lhs = dn.operands[0] == ds;
+        const ValueRef other = dn.operands[s_lhs ? 1 : 0];
+        if (dn.operands[0] == dn.operands[1]) { ok = false; break; }
+        auto orl = other_roles(dn, s_lhs, "bnts", g.type(other).rank(), 'h');
+        if (!orl) { ok = false; break; }
+        const char c = contracted(dn, s_lhs ? "bnts" : *orl, s_lhs ? *orl : "bnts");
+        Roles outr = s_lhs ? dot_out_roles(dn, "bnts", *orl) : dot_out_roles(dn, *orl, "bnts");
+        if (c == 's') {  // dQ: the other operand is K (its query role is 's' there)
+          Roles kk = *orl;
+          if (!(view_of(other, kk) == kv)) { ok = false; break; }
+          dqr = outr;
+          dqf = follow_out(ValueRef{di, 0}, dqr);
+        } else if (c == 't') {  // dK: the other operand is Q (roles t for its rows)
+          Roles qq = *orl;
+          if (!(view_of(other, qq) == qv)) { ok = false; break; }
+          dkr = outr;
+          dkf = follow_out(ValueRef{di, 0}, dkr);
+        } else {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok || dqf.node < 0 || dkf.node < 0) continue;
+      ValueRef dvf = follow_out(ValueRef{dvi, 0}, dvr);
+      // O: d2's result [B, N, T, D], through an exclusive transpose
+      Roles orr = "bnth";
+      ValueRef of{f.d2, 0};
+      if (u.count(f.d2) == 1 && !u.output_refs[f.d2] && N(u.users[f.d2][0]).op == Op::Transpose)
+        of = follow_out(of, orr);
+      for (ValueRef x : {dqf, dkf, dvf, of})
+        if (g.type(x).dtype != DType::BF16) ok = false;
+      for (ValueRef x : {qv.src, kv.src, vv.src, gv.src})
+        if (g.type(x).dtype != DType::BF16) ok = false;
+      if (!ok) continue;
+      // strides by role; the head dim must be contiguous and every stride a
+      // multiple of 8 elements (16 bytes)
+      auto rs = [&](ValueRef x, const Roles& r) {
+        std::map<char, int64_t> m;
+        auto st = dense_strides(g.type(x));
+        for (size_t d = 0; d < r.size(); ++d) m[r[d]] = st[d];
+        return m;
+      };
+      auto oS = rs(of, orr), dqS = rs(dqf, dqr), dkS = rs(dkf, dkr), dvS = rs(dvf, dvr);
+      // dK's and dV's row role is the key 's'
+      std::vector<std::map<char, int64_t>> all = {qv.st, kv.st, vv.st, oS, gv.st, dqS, dkS, dvS};
+      const char row[8] = {'t', 's', 's', 't', 't', 't', 's', 's'};
+      std::vector<int64_t> strides;
+      for (int k = 0; k < 8 && ok; ++k) {
+        auto& m = all[k];
+        if (!m.count('b') || !m.count('n') || !m.count(row[k]) || !m.count('h') || m['h'] != 1) ok = false;
+        else strides.insert(strides.end(), {m['b'], m[row[k]], m['n']});
+      }
+      for (auto x : strides) ok = ok && x % 8 == 0;
+      if (!ok) continue;
+      Node fw;
+      fw.op = Op::FusedSdpa;
+      fw.operands = {qv.src, kv.src, vv.src};
+      TensorType lt;
+      lt.dtype = DType::F32;
+      lt.dims = {f.B, f.H, f.T};
+      fw.results = {g.type(of), lt};
+      fw.name = g.nodes[of.node].name;
+      fw.f_scale = (float)f.scale;
+      fw.i_flags = f.causal | 2;
+      fw.dims = {f.B, f.T, f.S, f.H, f.D};
+      fw.strides = std::vector<int64_t>(strides.begin(), strides.begin() + 12);
+      const int fid = g.add(std::move(fw));
+      Node bw;
+      bw.op = Op::FusedSdpaBwd;
+      bw.operands = {qv.src, kv.src, vv.src, ValueRef{fid, 0}, gv.src, ValueRef{fid, 1}};
+      bw.results = {g.type(dqf), g.type(dkf), g.type(dvf)};
+      bw.name = g.nodes[dqf.node].name;
+      bw.f_scale = (float)f.scale;
+      bw.i_flags = f.causal;
+      bw.dims = {f.B, f.T, f.S, f.H, f.D};
+      bw.strides = strides;
+      const int bid = g.add(std::move(bw));
+      replace_uses(of, ValueRef{fid, 0});
+      replace_uses(dqf, ValueRef{bid, 0});
+      replace_uses(dkf, ValueRef{bid, 1});
+      replace_uses(dvf, ValueRef{bid, 2});
+      dce(g);
       u = compute_uses(g);
       ++count;
     }
@@ -842,8 +1302,9 @@ MatchStats match_patterns(Graph& g) {
   MatchStats st;
   Matcher m(g);
   st.sdpa = m.match_sdpa();
+  st.sdpa_train = m.match_sdpa_train();
   st.layer_norm = m.match_layer_norm();
-  if (st.sdpa || st.layer_norm) dce(g);
+  if (st.sdpa || st.sdpa_train || st.layer_norm) dce(g);
   return st;
 }
 
@@ -857,7 +1318,8 @@ std::string dump_graph(const Graph& g) {
       os << (k ? ", " : "") << "%" << n.operands[k].node
          << (n.operands[k].idx ? "#" + std::to_string(n.operands[k].idx) : "");
     os << ")";
-    if (n.op == Op::FusedSdpa) os << " {scale=" << n.f_scale << ", causal=" << (n.i_flags & 1) << "}";
+    if (n.op == Op::FusedSdpa || n.op == Op::FusedSdpaBwd)
+      os << " {scale=" << n.f_scale << ", causal=" << (n.i_flags & 1) << "}";
     if (n.op == Op::FusedLayerNorm) os << " {eps=" << n.f_eps << ", flags=" << n.i_flags << "}";
     if (n.op == Op::CustomCall) os << " {target=" << n.target << "}";
     os << " :";

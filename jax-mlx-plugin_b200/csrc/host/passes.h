@@ -36,11 +36,13 @@ std::optional<HostTensor> host_eval(const Graph& g, ValueRef v, int64_t max_elem
 
 // Pattern matchers (the fusion rules of the north star):
 //   dot_general -> [scale] -> [causal select] -> softmax -> dot_general -> FusedSdpa
+//   the same chain plus its backward (dV, dP, softmax vjp, dQ, dK)
+//                                           -> FusedSdpa (with row statistics) + FusedSdpaBwd
 //   [residual add] -> mean/var -> normalize -> [gamma] -> [beta]  -> FusedLayerNorm
 // Both refuse to fuse when an intermediate value has a consumer outside the
 // pattern (reference src/jax_mlx_pjrt.cpp:1843-1855 applies the same guard).
 struct MatchStats {
-  int sdpa = 0, layer_norm = 0;
+  int sdpa = 0, sdpa_train = 0, layer_norm = 0;
 };
 MatchStats match_patterns(Graph& g);
 

@@ -1162,11 +1162,26 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
                    "layer_norm");
             break;
           case StepKind::Sdpa:
-            kcheck(b200_sdpa_fwd_strided(slotp(st.in[0]), slotp(st.in[1]), slotp(st.in[2]),
-                                         slotp(st.out[0]), st.ip[0], st.ip[1], st.ip[2], st.ip[3],
-                                         st.ip[4], st.ip.data() + 5, st.fp[0], (int)st.ip[17],
-                                         st.dtype, dev.stream),
-                   "sdpa");
+            if (st.out.size() > 1)
+              kcheck(b200_sdpa_fwd_lse(slotp(st.in[0]), slotp(st.in[1]), slotp(st.in[2]),
+                                       slotp(st.out[0]), (float*)slotp(st.out[1]), st.ip[0], st.ip[1],
+                                       st.ip[2], st.ip[3], st.ip[4], st.ip.data() + 5, st.fp[0],
+                                       (int)st.ip[17], st.dtype, dev.stream),
+                     "sdpa");
+            else
+              kcheck(b200_sdpa_fwd_strided(slotp(st.in[0]), slotp(st.in[1]), slotp(st.in[2]),
+                                           slotp(st.out[0]), st.ip[0], st.ip[1], st.ip[2], st.ip[3],
+                                           st.ip[4], st.ip.data() + 5, st.fp[0], (int)st.ip[17],
+                                           st.dtype, dev.stream),
+                     "sdpa");
+            break;
+          case StepKind::SdpaBwd:
+            kcheck(b200_sdpa_bwd(slotp(st.in[0]), slotp(st.in[1]), slotp(st.in[2]), slotp(st.in[3]),
+                                 slotp(st.in[4]), (const float*)slotp(st.in[5]), slotp(st.out[0]),
+                                 slotp(st.out[1]), slotp(st.out[2]), st.ip[0], st.ip[1], st.ip[2],
+                                 st.ip[3], st.ip.data() + 4, st.fp[0], (int)st.ip[28], st.dtype,
+                                 dev.stream),
+                   "sdpa_bwd");
             break;
           case StepKind::Gemm: {
             // split-K partials / bf16 planes come from the caching allocator

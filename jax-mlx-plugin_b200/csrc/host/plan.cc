@@ -543,7 +543,24 @@ struct Builder {
     st.name = "sdpa";
     st.in = {slot.at(nd.operands[0]), slot.at(nd.operands[1]), slot.at(nd.operands[2])};
     st.out = {temp_for(ValueRef{n, 0})};
+    if (nd.i_flags & 2) st.out.push_back(temp_for(ValueRef{n, 1}));  // row statistics
     st.ip = nd.dims;  // B T S N D
+    st.ip.insert(st.ip.end(), nd.strides.begin(), nd.strides.end());
+    st.ip.push_back(nd.i_flags & 1);
+    st.fp = {nd.f_scale};
+    st.dtype = (int)g.type(nd.operands[0]).dtype;
+    p.steps.push_back(st);
+    p.num_sdpa++;
+  }
+  // Attention backward (b200_sdpa_bwd): in q, k, v, o, dO, row statistics;
+  // out dQ, dK, dV.  ip: B T N D, 24 strides, causal.
+  void lower_fused_sdpa_bwd(int n, const Node& nd) {
+    Step st;
+    st.kind = StepKind::SdpaBwd;
+    st.name = "sdpa_bwd";
+    for (const auto& o : nd.operands) st.in.push_back(slot.at(o));
+    st.out = {temp_for(ValueRef{n, 0}), temp_for(ValueRef{n, 1}), temp_for(ValueRef{n, 2})};
+    st.ip = {nd.dims[0], nd.dims[1], nd.dims[3], nd.dims[4]};
     st.ip.insert(st.ip.end(), nd.strides.begin(), nd.strides.end());
     st.ip.push_back(nd.i_flags & 1);
     st.fp = {nd.f_scale};
@@ -1123,6 +1140,7 @@ struct Builder {
         case Op::DotGeneral: lower_dot(n); break;
         case Op::Convolution: lower_conv(n); break;
         case Op::FusedSdpa: lower_fused_sdpa(n, nd); break;
+        case Op::FusedSdpaBwd: lower_fused_sdpa_bwd(n, nd); break;
         case Op::FusedLayerNorm: lower_fused_ln(n, nd); break;
         case Op::AllReduce: lower_all_reduce(n, nd); break;
         case Op::CustomCall:

@@ -34,7 +34,8 @@ struct Arg {
 enum class StepKind {
   Kernel,     // NVRTC-generated kernel: name, grid/block, args
   LayerNorm,  // b200_ln_residual_fwd
-  Sdpa,       // tcgen05 attention
+  Sdpa,       // tcgen05 attention (with row statistics when it has a second output)
+  SdpaBwd,    // tcgen05 attention backward
   Gemm,       // tcgen05 or SIMT GEMM
   AllReduce,  // NCCL sum over replicas
   Copy,       // device-to-device copy of slot bytes

@@ -31,6 +31,7 @@ struct SdpaArgs {
   int causal;
   void* o;
   int64_t o_sb, o_st, o_sn;
+  float* lse;  // optional [B, N, T]: per-row log2 of sum_s 2^(scale*log2(e)*q.k_s)
   int* err;
 };
 
@@ -910,7 +911,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       ok = __all_sync(0xffffffffu, w) != 0;
     }
     if (ok && t < p.T) {
-      const float inv = 1.f / (lb[row] + lb[128 + row]);
+      const float lsum = lb[row] + lb[128 + row];
+      const float inv = 1.f / lsum;
+      if (p.lse && h == 0) p.lse[((int64_t)b * p.N + n) * p.T + t] = m_run + log2f(lsum);
       const int64_t off = (int64_t)b * p.o_sb + (int64_t)t * p.o_st + (int64_t)n * p.o_sn + h * 32;
       if (X3) {
         float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + off);
@@ -944,7 +947,8 @@ __global__ void __launch_bounds__(kWsThreads, 1)
 
 template <bool X3>
 int launch_ws(const void* q, const void* k, const void* v, void* o, int64_t B, int64_t T,
-              int64_t S, int64_t N, const int64_t* st, float scale, int causal, cudaStream_t s) {
+              int64_t S, int64_t N, const int64_t* st, float scale, int causal, cudaStream_t s,
+              float* lse = nullptr) {
   using C = WsCfg<X3>;
   constexpr int ES = X3 ? 4 : 2;
   constexpr uint32_t inner = X3 ? 32 : 64;  // 128-byte rows
@@ -963,7 +967,7 @@ int launch_ws(const void* q, const void* k, const void* v, void* o, int64_t B, i
     const uint64_t sv[3] = {(uint64_t)(st[8] * ES), (uint64_t)(st[7] * ES), (uint64_t)(st[6] * ES)};
     if (int rc = make_tmap(&tv, v, 4, dims, sv, box, ES)) return rc;
   }
-  SdpaArgs a;
+  SdpaArgs a{};
   a.B = (int)B;
   a.T = (int)T;
   a.S = (int)S;
@@ -974,6 +978,7 @@ int launch_ws(const void* q, const void* k, const void* v, void* o, int64_t B, i
   a.o_sb = st[9];
   a.o_st = st[10];
   a.o_sn = st[11];
+  a.lse = lse;
   a.err = device_error_word();
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_ws<X3>, C::SMEM, "sdpa_fwd_ws")) return rc;
@@ -1053,7 +1058,7 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, int64_t B, i
     const uint64_t sv[3] = {(uint64_t)(st[8] * ES), (uint64_t)(st[7] * ES), (uint64_t)(st[6] * ES)};
     if (int rc = make_tmap(&tv, v, 4, dims, sv, box, ES, /*atom32=*/ES == 4)) return rc;
   }
-  SdpaArgs a;
+  SdpaArgs a{};
   a.B = (int)B;
   a.T = (int)T;
   a.S = (int)S;
@@ -1089,7 +1094,7 @@ int launch_x3(const void* q, const void* k, const void* v, void* o, int64_t B, i
     const uint64_t sv[3] = {(uint64_t)(st[8] * 4), (uint64_t)(st[7] * 4), (uint64_t)(st[6] * 4)};
     if (int rc = make_tmap(&tv, v, 4, dims, sv, box, 4, /*atom32=*/true)) return rc;
   }
-  SdpaArgs a;
+  SdpaArgs a{};
   a.B = (int)B;
   a.T = (int)T;
   a.S = (int)S;
@@ -1105,6 +1110,316 @@ int launch_x3(const void* q, const void* k, const void* v, void* o, int64_t B, i
   if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_tc_x3, X3Cfg::SMEM, "sdpa_fwd_tc_x3")) return rc;
   dim3 grid((unsigned)((T + 127) / 128), (unsigned)N, (unsigned)B);
   B200_LAUNCH(sdpa_fwd_tc_x3, grid, dim3(128), X3Cfg::SMEM, s, tq, tk, tv, a);
+  return B200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Attention backward, bf16, head dim 64, T == S <= 256 (flash-style: P is
+// recomputed from the forward's row statistics, the [T, S] matrices never
+// touch HBM).
+//
+// One CTA = one (batch, head); Q, dO, K and V (at most 2 tiles of 128 rows
+// each) are loaded once by TMA and stay in shared memory.  Query tile i and
+// key tile j form a pair (j outer; causal: i >= j).  Per pair, 288 threads:
+//   warp 8     lane 0 issues S = Q_i K_j^T and dP = dO_i V_j^T (tcgen05,
+//              M = N = 128) into TMEM, waits for P / dS, then accumulates
+//              dV_j += P^T dO_i, dK_j += dS^T Q_i (A operands MN-major) and
+//              dQ_i += dS K_j (B MN-major) in TMEM;
+//   warps 0-7  warp w reads TMEM lane quarter w % 4 (32 query rows) and key
+//              half w / 4 of S and dP, forms P = 2^(S*scale*log2e - lse2)
+//              and dS = P (dP - D) scale in f32, with D = rowsum(dO * O),
+//              and writes both as bf16 into shared memory (two 64-key
+//              chunks of 128-byte rows, 16-byte units XOR row % 8); after the
+//              last pair of key tile j they store dK_j and dV_j, and at the
+//              end every dQ_i.
+// TMEM columns: S 0-127, dP 128-255, dV 256-319, dK 320-383, dQ_i 384 + 64 i.
+// Math: the vjp of softmax(QK^T*scale)V (reference src/jax_mlx/sdpa.py:65-87,
+// whose mlx_sdpa_bwd the reference runs through mx::vjp,
+// src/jax_mlx_pjrt.cpp:8152-8206).
+struct BwdArgs {
+  int B, T, N;
+  float scale;
+  int causal;
+  const float* lse2;  // [B, N, T]: log2 of each row's sum_s 2^(scale*log2(e)*q.k_s)
+  const __nv_bfloat16* o;
+  int64_t o_sb, o_st, o_sn;
+  const __nv_bfloat16* dout;
+  int64_t do_sb, do_st, do_sn;
+  __nv_bfloat16* dq;
+  int64_t dq_sb, dq_st, dq_sn;
+  __nv_bfloat16* dk;
+  int64_t dk_sb, dk_st, dk_sn;
+  __nv_bfloat16* dv;
+  int64_t dv_sb, dv_st, dv_sn;
+  int* err;
+};
+
+struct BwdCfg {
+  static constexpr int TILE = 128 * 128;  // 128 rows x 128 B (64 bf16)
+  static constexpr int Q_OFF = 0;         // 2 tiles each
+  static constexpr int DO_OFF = Q_OFF + 2 * TILE;
+  static constexpr int K_OFF = DO_OFF + 2 * TILE;
+  static constexpr int V_OFF = K_OFF + 2 * TILE;
+  static constexpr int P_OFF = V_OFF + 2 * TILE;  // 2 chunks of 64 keys
+  static constexpr int DS_OFF = P_OFF + 2 * TILE;
+  static constexpr int BAR_OFF = DS_OFF + 2 * TILE;
+  static constexpr int SMEM = BAR_OFF + 256 + 1024;
+};
+constexpr int kBwdThreads = 288;
+
+__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    d[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
+                      pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    sdpa_bwd_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
+                const __grid_constant__ CUtensorMap tV, const __grid_constant__ CUtensorMap tDO,
+                BwdArgs p) {
+  pdl_wait();
+  using C = BwdCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* ld_full = bars + 0;   // every Q / dO / K / V tile landed
+  uint64_t* sd_full = bars + 1;   // S and dP of the current pair in TMEM
+  uint64_t* pds_full = bars + 2;  // P and dS in shared memory (8 warps)
+  uint64_t* acc_done = bars + 3;  // the pair's dV / dK / dQ MMAs complete
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = (int)blockIdx.x % p.N, b = (int)blockIdx.x / p.N;
+  const int nt = (p.T + 127) / 128;
+  auto tile = [&](int off, int i) { return smem + off + i * C::TILE; };
+
+  if (tid == 0) {
+    mbar_init(ld_full, 1);
+    mbar_init(sd_full, 1);
+    mbar_init(pds_full, 8);
+    mbar_init(acc_done, 1);
+    *abort = 0;
+    mbar_fence_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tS = tmem, tDP = tmem + 128u, tDV = tmem + 256u, tDK = tmem + 320u;
+
+  if (warp == 8) {
+    if (lane == 0) {  // ---- TMA and MMA issue
+      tma_prefetch_desc(&tQ);
+      tma_prefetch_desc(&tK);
+      tma_prefetch_desc(&tV);
+      tma_prefetch_desc(&tDO);
+      mbar_expect_tx(ld_full, 4 * nt * C::TILE);
+      for (int i = 0; i < nt; ++i) {
+        tma_load_4d(tile(C::Q_OFF, i), &tQ, ld_full, 0, n, i * 128, b);
+        tma_load_4d(tile(C::DO_OFF, i), &tDO, ld_full, 0, n, i * 128, b);
+        tma_load_4d(tile(C::K_OFF, i), &tK, ld_full, 0, n, i * 128, b);
+        tma_load_4d(tile(C::V_OFF, i), &tV, ld_full, 0, n, i * 128, b);
+      }
+      constexpr uint32_t idesc_s = umma_idesc(1u, 0, 0, 128, 128);  // K-major x K-major
+      constexpr uint32_t idesc_t = umma_idesc(1u, 1, 1, 64, 128);   // P^T / dS^T times dO / Q
+      constexpr uint32_t idesc_q = umma_idesc(1u, 0, 1, 64, 128);   // dS times K
+      const uint32_t pp = smem_u32(smem + C::P_OFF), ds = smem_u32(smem + C::DS_OFF);
+      bool ok = mbar_wait(ld_full, 0, abort, p.err, 231);
+      int pair = 0;
+      for (int j = 0; ok && j < nt; ++j) {
+        const int i0 = p.causal ? j : 0;
+        const uint32_t kt = smem_u32(tile(C::K_OFF, j)), vt = smem_u32(tile(C::V_OFF, j));
+        for (int i = i0; i < nt; ++i, ++pair) {
+          const uint32_t qt = smem_u32(tile(C::Q_OFF, i)), dot = smem_u32(tile(C::DO_OFF, i));
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tS, umma_desc(qt + kk * 32, 16, 1024), umma_desc(kt + kk * 32, 16, 1024), idesc_s,
+                     kk != 0);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tDP, umma_desc(dot + kk * 32, 16, 1024), umma_desc(vt + kk * 32, 16, 1024),
+                     idesc_s, kk != 0);
+          umma_commit(sd_full);
+          ok = mbar_wait(pds_full, pair & 1, abort, p.err, 232);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t tDQ = tmem + 384u + 64u * (uint32_t)i;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            // 16 queries = 16 rows of 128 B in P / dS (MN-major A: the two
+            // 64-key chunks 16 KB apart) and in dO / Q (MN-major B)
+            const uint32_t ka = (uint32_t)(i != i0 || kk != 0);
+            umma_f16(tDV, umma_desc(pp + kk * 2048, 16384, 1024), umma_desc(dot + kk * 2048, 8192, 1024),
+                     idesc_t, ka);
+            umma_f16(tDK, umma_desc(ds + kk * 2048, 16384, 1024), umma_desc(qt + kk * 2048, 8192, 1024),
+                     idesc_t, ka);
+            // 16 keys: 32 bytes of a dS row (K-major A), 16 rows of K (MN-major B)
+            umma_f16(tDQ, umma_desc(ds + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                     umma_desc(kt + kk * 2048, 8192, 1024), idesc_q, (uint32_t)(j != 0 || kk != 0));
+          }
+          umma_commit(acc_done);
+        }
+      }
+    }
+  } else {  // ---- warps 0-7: P, dS and the stores
+    const int qq = warp & 3, h = warp >> 2;
+    const int r = qq * 32 + lane;  // row within a 128-row tile (= TMEM lane)
+    const uint32_t lane_base = (uint32_t)(qq * 32) << 16;
+    const float sl2 = p.scale * 1.4426950408889634f;
+    float lse0 = 0.f, lse1 = 0.f, d0 = 0.f, d1 = 0.f;
+    for (int i = 0; i < nt; ++i) {  // row statistics and D = rowsum(dO * O)
+      const int t = i * 128 + r;
+      if (t >= p.T) continue;
+      const float l = p.lse2[((int64_t)b * p.N + n) * p.T + t];
+      const uint4* o4 = reinterpret_cast<const uint4*>(p.o + (int64_t)b * p.o_sb + (int64_t)t * p.o_st +
+                                                       (int64_t)n * p.o_sn);
+      const uint4* g4 = reinterpret_cast<const uint4*>(p.dout + (int64_t)b * p.do_sb +
+                                                       (int64_t)t * p.do_st + (int64_t)n * p.do_sn);
+      float acc = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint4 x = o4[u], y = g4[u];
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[c]));
+          const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ys[c]));
+          acc = fmaf(a.x, g.x, fmaf(a.y, g.y, acc));
+        }
+      }
+      if (i == 0) { lse0 = l; d0 = acc; } else { lse1 = l; d1 = acc; }
+    }
+    bool ok = true;
+    int pair = 0;
+    float v[32];
+    for (int j = 0; ok && j < nt; ++j) {
+      const int i0 = p.causal ? j : 0;
+      for (int i = i0; i < nt; ++i, ++pair) {
+        bool w = mbar_wait(sd_full, pair & 1, abort, p.err, 233);
+        // P / dS of the previous pair are read by its MMAs until acc_done
+        if (w && pair > 0) w = mbar_wait(acc_done, (pair - 1) & 1, abort, p.err, 234);
+        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+        tc_fence_after();
+        const int t = i * 128 + r;
+        const bool row_ok = t < p.T;
+        const float li = i ? lse1 : lse0, di = i ? d1 : d0;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int col = h * 64 + c * 32;  // column within the key tile
+          float sv[32];
+          tmem_ld32(tS + lane_base + (uint32_t)col, sv);
+          tmem_ld32(tDP + lane_base + (uint32_t)col, v);
+          const int kb = j * 128 + col;
+          uint32_t pw[16], dw[16];
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = kb + 2 * x + e;
+              const bool valid = row_ok && key < p.T && (!p.causal || key <= t);
+              pv[e] = valid ? ex2(fmaf(sv[2 * x + e], sl2, -li)) : 0.f;
+              dv[e] = pv[e] * (v[2 * x + e] - di) * p.scale;
+            }
+            pw[x] = pack_bf16x2(pv[0], pv[1]);
+            dw[x] = pack_bf16x2(dv[0], dv[1]);
+          }
+          uint8_t* prow = smem + C::P_OFF + h * C::TILE + r * 128;
+          uint8_t* drow = smem + C::DS_OFF + h * C::TILE + r * 128;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int off = ((c * 4 + u) ^ (r & 7)) << 4;
+            *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
+            *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pds_full);
+        if (i == nt - 1) {  // key tile j is complete once this pair's MMAs are
+          w = mbar_wait(acc_done, pair & 1, abort, p.err, 235);
+          if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+          tc_fence_after();
+          const int key = j * 128 + r;
+          tmem_ld32(tDV + lane_base + (uint32_t)(h * 32), v);
+          if (key < p.T)
+            store_row32_bf16(p.dv + (int64_t)b * p.dv_sb + (int64_t)key * p.dv_st + (int64_t)n * p.dv_sn + h * 32, v);
+          tmem_ld32(tDK + lane_base + (uint32_t)(h * 32), v);
+          if (key < p.T)
+            store_row32_bf16(p.dk + (int64_t)b * p.dk_sb + (int64_t)key * p.dk_st + (int64_t)n * p.dk_sn + h * 32, v);
+          tc_fence_before();
+        }
+      }
+    }
+    if (ok) {  // every MMA has completed (the last key tile's wait above)
+      for (int i = 0; i < nt; ++i) {
+        const int t = i * 128 + r;
+        tmem_ld32(tmem + 384u + 64u * (uint32_t)i + lane_base + (uint32_t)(h * 32), v);
+        if (t < p.T)
+          store_row32_bf16(p.dq + (int64_t)b * p.dq_sb + (int64_t)t * p.dq_st + (int64_t)n * p.dq_sn + h * 32, v);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && tid == 0) {  // let MMAs still in flight drain before TMEM is freed
+    const uint64_t t1 = globaltimer();
+    while (globaltimer() - t1 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int launch_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+               const float* lse2, void* dq, void* dk, void* dv, int64_t B, int64_t T, int64_t N,
+               const int64_t* st, float scale, int causal, cudaStream_t s) {
+  // st: (b, t, n) element strides of q, k, v, o, dout, dq, dk, dv
+  CUtensorMap tq, tk, tv, tdo;
+  const void* src[4] = {q, k, v, dout};
+  const int sidx[4] = {0, 1, 2, 4};
+  CUtensorMap* maps[4] = {&tq, &tk, &tv, &tdo};
+  for (int m = 0; m < 4; ++m) {
+    const int64_t* x = st + 3 * sidx[m];
+    const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)T, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)(x[2] * 2), (uint64_t)(x[1] * 2), (uint64_t)(x[0] * 2)};
+    const uint32_t box[4] = {64, 1, 128, 1};
+    if (int rc = make_tmap(maps[m], src[m], 4, dims, str, box, 2)) return rc;
+  }
+  BwdArgs a{};
+  a.B = (int)B;
+  a.T = (int)T;
+  a.N = (int)N;
+  a.scale = scale;
+  a.causal = causal;
+  a.lse2 = lse2;
+  a.o = (const __nv_bfloat16*)o;
+  a.o_sb = st[9], a.o_st = st[10], a.o_sn = st[11];
+  a.dout = (const __nv_bfloat16*)dout;
+  a.do_sb = st[12], a.do_st = st[13], a.do_sn = st[14];
+  a.dq = (__nv_bfloat16*)dq;
+  a.dq_sb = st[15], a.dq_st = st[16], a.dq_sn = st[17];
+  a.dk = (__nv_bfloat16*)dk;
+  a.dk_sb = st[18], a.dk_st = st[19], a.dk_sn = st[20];
+  a.dv = (__nv_bfloat16*)dv;
+  a.dv_sb = st[21], a.dv_st = st[22], a.dv_sn = st[23];
+  a.err = device_error_word();
+  if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
+  if (int rc = allow_dynamic_smem((const void*)sdpa_bwd_tc, BwdCfg::SMEM, "sdpa_bwd_tc")) return rc;
+  B200_LAUNCH(sdpa_bwd_tc, dim3((unsigned)(B * N)), dim3(kBwdThreads), BwdCfg::SMEM, s, tq, tk, tv,
+              tdo, a);
   return B200_OK;
 }
 
@@ -1169,4 +1484,47 @@ extern "C" int b200_sdpa_fwd(const void* q, const void* k, const void* v, void* 
   const int64_t st[12] = {T * N * D, N * D, D, S * N * D, N * D, D,
                           S * N * D, N * D, D, T * N * D, N * D, D};
   return b200_sdpa_fwd_strided(q, k, v, o, B, T, S, N, D, st, scale, causal, dtype, stream);
+}
+
+extern "C" int b200_sdpa_fwd_lse(const void* q, const void* k, const void* v, void* o, float* lse2,
+                                 int64_t B, int64_t T, int64_t S, int64_t N, int64_t D,
+                                 const int64_t* st, float scale, int causal, int dtype,
+                                 void* stream) {
+  using namespace b200;
+  B200_CHECK_ARG(q && k && v && o && lse2 && st, "sdpa_fwd_lse: null argument");
+  B200_CHECK_ARG(B > 0 && T > 0 && S > 0 && N > 0 && D > 0, "sdpa_fwd_lse: bad shape");
+  B200_CHECK_ARG(B < 65536 && N < 65536 && T < (1 << 30) && S < (1 << 30),
+                 "sdpa_fwd_lse: shape too large");
+  B200_CHECK_ARG(dtype == B200_DT_F32 || dtype == B200_DT_BF16,
+                 "sdpa_fwd_lse: dtype must be F32 or BF16");
+  const int es = dtype == B200_DT_F32 ? 4 : 2;
+  bool tc = D == 64 && scale > 0.f;
+  for (int i = 0; i < 12; ++i) tc = tc && ((st[i] * es) % 16 == 0);
+  const void* ptrs[4] = {q, k, v, o};
+  for (int i = 0; i < 4; ++i) tc = tc && ((uintptr_t)ptrs[i] % 16 == 0);
+  if (!tc)
+    return set_error(B200_ERR_UNSUPPORTED,
+                     "sdpa_fwd_lse: needs D == 64, scale > 0 and 16-byte aligned operands and strides");
+  auto s = (cudaStream_t)stream;
+  if (es == 4) return launch_ws<true>(q, k, v, o, B, T, S, N, st, scale, causal, s, lse2);
+  return launch_ws<false>(q, k, v, o, B, T, S, N, st, scale, causal, s, lse2);
+}
+
+extern "C" int b200_sdpa_bwd(const void* q, const void* k, const void* v, const void* o,
+                             const void* dout, const float* lse2, void* dq, void* dk, void* dv,
+                             int64_t B, int64_t T, int64_t N, int64_t D, const int64_t* st,
+                             float scale, int causal, int dtype, void* stream) {
+  using namespace b200;
+  B200_CHECK_ARG(q && k && v && o && dout && lse2 && dq && dk && dv && st, "sdpa_bwd: null argument");
+  B200_CHECK_ARG(B > 0 && T > 0 && N > 0 && D > 0, "sdpa_bwd: bad shape");
+  B200_CHECK_ARG((int64_t)B * N < (1ll << 31), "sdpa_bwd: too many (batch, head) pairs");
+  if (dtype != B200_DT_BF16 || D != 64 || T > 256)
+    return set_error(B200_ERR_UNSUPPORTED, "sdpa_bwd: needs bf16, head dim 64 and T <= 256");
+  bool al = true;
+  for (int i = 0; i < 24; ++i) al = al && (st[i] % 8 == 0);
+  const void* ptrs[8] = {q, k, v, o, dout, dq, dk, dv};
+  for (int i = 0; i < 8; ++i) al = al && ((uintptr_t)ptrs[i] % 16 == 0);
+  if (!al) return set_error(B200_ERR_UNSUPPORTED, "sdpa_bwd: operands and strides must be 16-byte aligned");
+  return launch_bwd(q, k, v, o, dout, lse2, dq, dk, dv, B, T, N, st, scale, causal,
+                    (cudaStream_t)stream);
 }

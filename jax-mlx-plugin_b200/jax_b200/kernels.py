@@ -28,6 +28,10 @@ EXPORTS = {
                                                                     C.c_void_p]),
     "b200_sdpa_fwd_strided": (C.c_int, [C.c_void_p] * 4 + [C.c_int64] * 5 +
                               [C.POINTER(C.c_int64), C.c_float, C.c_int, C.c_int, C.c_void_p]),
+    "b200_sdpa_fwd_lse": (C.c_int, [C.c_void_p] * 5 + [C.c_int64] * 5 +
+                          [C.POINTER(C.c_int64), C.c_float, C.c_int, C.c_int, C.c_void_p]),
+    "b200_sdpa_bwd": (C.c_int, [C.c_void_p] * 9 + [C.c_int64] * 4 +
+                      [C.POINTER(C.c_int64), C.c_float, C.c_int, C.c_int, C.c_void_p]),
     "b200_gemm": (C.c_int, [C.c_void_p] * 4 + [C.c_int64] * 11 + [C.c_float, C.c_int, C.c_int,
                                                                   C.c_int, C.c_void_p]),
     "b200_gemm_noalloc": (C.c_int, [C.c_void_p] * 4 + [C.c_int64] * 11 +
@@ -85,6 +89,22 @@ def sdpa_fwd_strided(q, k, v, o, B, T, S, N, D, strides, scale, causal, dtype, s
     arr = (C.c_int64 * 12)(*strides)
     _check(lib().b200_sdpa_fwd_strided(q, k, v, o, B, T, S, N, D, arr, scale, int(causal), dtype,
                                        stream), "sdpa_fwd_strided")
+
+
+def sdpa_fwd_lse(q, k, v, o, lse2, B, T, S, N, D, strides, scale, causal, dtype, stream):
+    """sdpa_fwd_strided that also writes the rows' log2-sum-exp2 statistic
+    (f32 [B, N, T]) for sdpa_bwd."""
+    arr = (C.c_int64 * 12)(*strides)
+    _check(lib().b200_sdpa_fwd_lse(q, k, v, o, lse2, B, T, S, N, D, arr, scale, int(causal), dtype,
+                                   stream), "sdpa_fwd_lse")
+
+
+def sdpa_bwd(q, k, v, o, dout, lse2, dq, dk, dv, B, T, N, D, strides, scale, causal, dtype, stream):
+    """dQ, dK, dV of attention (bf16, D == 64, T <= 256); strides: (b, t, n) of
+    q, k, v, o, dout, dq, dk, dv (24 values)."""
+    arr = (C.c_int64 * 24)(*strides)
+    _check(lib().b200_sdpa_bwd(q, k, v, o, dout, lse2, dq, dk, dv, B, T, N, D, arr, scale,
+                               int(causal), dtype, stream), "sdpa_bwd")
 
 
 def gemm(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc, alpha, in_dtype,

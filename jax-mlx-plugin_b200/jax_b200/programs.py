@@ -218,6 +218,47 @@ def _causal_attention(b: Builder, q: V, k: V, v: V) -> V:
     return b.transpose(enc, [0, 2, 1, 3])
 
 
+def attention_vjp(B=2, T=256, N=2, H=64, causal=True, dt="bf16", form="autodiff") -> str:
+    """O and the vjp (dQ, dK, dV) of jax.nn.dot_product_attention for the
+    output cotangent dO; inputs Q, K, V, dO [B, T, N, H].
+
+    form="autodiff": the gradient as ``grad`` of sum(O * dO) derives it
+    (quotient rule through the softmax, as the transformer step has it);
+    form="custom_jvp": the backward of ``jax.nn.softmax``'s custom JVP
+    rule transposed, dx = y * g - y * sum(y * g), written out by hand."""
+    b = Builder("jit_attention_vjp")
+    q, k, v, g = (b.param((B, T, N, H), dt) for _ in range(4))
+    if form == "autodiff":
+        o = _causal_attention(b, q, k, v) if causal else None
+        if o is None:
+            raise ValueError("form='autodiff' builds the causal attention of the transformer")
+        loss = b.sum(b.convert(o, "f32") * b.convert(g, "f32"), [0, 1, 2, 3])
+        dq, dk, dv = b.grad(loss, [q, k, v])
+        return b.module([o, dq, dk, dv])
+    scale = 1.0 / math.sqrt(H)
+    qt, kt, vt, gt = (b.transpose(x, [0, 2, 1, 3]) for x in (q, k, v, g))  # [B,N,T,H]
+    logits = b.dot_general(qt, kt, ([3], [3]), ([0, 1], [0, 1]), out_dt="f32") * scale
+    if causal:
+        row, col = b.iota((T, T), 0), b.iota((T, T), 1)
+        mask = b.broadcast_to(b.reshape(b.compare(row, col, "GE", "SIGNED"), (1, 1, T, T)),
+                              logits.shape)
+        logits = b.select(mask, logits, b.constant(-0.7 * F32_MAX, "f32", logits.shape))
+    y = softmax(b, logits)
+    yb = b.convert(y, dt)
+    o = b.transpose(b.dot_general(yb, vt, ([3], [2]), ([0, 1], [0, 1])), [0, 2, 1, 3])
+    dv = b.transpose(b.dot_general(yb, gt, ([2], [2]), ([0, 1], [0, 1])), [0, 2, 1, 3])
+    dy = b.convert(b.dot_general(gt, vt, ([3], [3]), ([0, 1], [0, 1])), "f32")
+    yg = y * dy
+    dx = yg - y * b.broadcast_in_dim(b.sum(yg, [3]), yg.shape, [0, 1, 2])
+    if causal:
+        dx = b.select(mask, dx, b.constant(0.0, "f32", dx.shape))
+    ds = dx * scale
+    dq = b.dot_general(ds, kt, ([3], [2]), ([0, 1], [0, 1]))
+    dk = b.dot_general(ds, qt, ([2], [2]), ([0, 1], [0, 1]))
+    dq, dk = (b.transpose(b.convert(x, dt), [0, 2, 1, 3]) for x in (dq, dk))
+    return b.module([o, dq, dk, dv])
+
+
 TRANSFORMER_PARAMS_PER_LAYER = ("ln1_g", "ln1_b", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo",
                                 "ln2_g", "ln2_b", "w1", "b1", "w2", "b2")
 

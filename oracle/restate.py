@@ -36,15 +36,19 @@ def sdpa_ref(q, k, v, scale=None, causal=False):
     return np.transpose(w @ vb, (0, 2, 1, 3))
 
 
-def sdpa_bwd_ref(q, k, v, g, scale):
-    """dQ, dK, dV of non-causal softmax(Q K^T scale) V, layout (B, T, N, H).
+def sdpa_bwd_ref(q, k, v, g, scale, causal=False):
+    """dQ, dK, dV of softmax(Q K^T scale [+ causal fill]) V, layout (B, T, N, H).
 
     Follows reference src/jax_mlx/sdpa.py:65-87 (_mlx_sdpa_bwd_impl): weights =
     softmax(logits), dv = weights^T g, d_weights = g v^T, d_scores = weights *
     (d_weights - sum(d_weights * weights, -1)) * scale, dq = d_scores k,
-    dk = d_scores^T q."""
+    dk = d_scores^T q.  `causal` fills logits of keys after the query with
+    -0.7 * finfo(f32).max first, as sdpa_ref does (their weights are 0)."""
     q, k, v, g = (np.transpose(np.asarray(a, dtype=np.float64), (0, 2, 1, 3)) for a in (q, k, v, g))
     logits = q @ np.swapaxes(k, -1, -2) * scale
+    if causal:
+        T, S = logits.shape[-2:]
+        logits = np.where(np.tril(np.ones((T, S), bool)), logits, -0.7 * np.finfo(np.float32).max)
     w = np.exp(logits - logits.max(-1, keepdims=True))
     w /= w.sum(-1, keepdims=True)
     dv = np.swapaxes(w, -1, -2) @ g

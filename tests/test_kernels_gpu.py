@@ -156,6 +156,60 @@ def test_sdpa_bf16(causal):
     assert_close(host(O), ref, 2e-2, "sdpa bf16")
 
 
+@pytest.mark.parametrize("B,T,N,causal", [(2, 256, 3, True), (2, 256, 3, False), (3, 128, 2, True),
+                                          (2, 200, 2, True), (1, 77, 2, False), (1, 1, 1, True)])
+def test_sdpa_bwd_bf16(B, T, N, causal):
+    """Forward with row statistics, then the fused backward, against the float64
+    closed form on the same bf16 inputs.  bf16 outputs, P and dS enter the
+    products as bf16: 2e-2 relative with a floor of 2e-2 * rms(reference)."""
+    rng = np.random.default_rng(B * 100 + T + N + causal)
+    q, k, v, g = (rng.standard_normal((B, T, N, 64)).astype(np.float32) for _ in range(4))
+    Q, K, V, G = (bf16_dev(a) for a in (q, k, v, g))
+    O = torch.empty_like(Q)
+    lse = torch.empty((B, N, T), device="cuda")
+    dense = [T * N * 64, N * 64, 64]
+    kernels.sdpa_fwd_lse(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), lse.data_ptr(), B, T,
+                         T, N, 64, dense * 4, 0.125, causal, kernels.DT_BF16, stream())
+    qh, kh, vh, gh = (host(a) for a in (Q, K, V, G))
+    assert_close(host(O), restate.sdpa_ref(qh, kh, vh, 0.125, causal), 2e-2, "sdpa fwd")
+    s = np.einsum("btnh,bsnh->bnts", qh.astype(np.float64), kh.astype(np.float64)) * 0.125
+    if causal:
+        s = np.where(np.tril(np.ones((T, T), bool)), s, -np.inf)
+    mx = s.max(-1, keepdims=True)
+    ref_lse = (mx[..., 0] + np.log(np.exp(s - mx).sum(-1))) / np.log(2.0)
+    assert_close(host(lse), ref_lse, 1e-5, "lse2")
+    dQ, dK, dV = (torch.empty_like(Q) for _ in range(3))
+    kernels.sdpa_bwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), G.data_ptr(), lse.data_ptr(),
+                     dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), B, T, N, 64, dense * 8, 0.125, causal,
+                     kernels.DT_BF16, stream())
+    rq, rk, rv = restate.sdpa_bwd_ref(qh, kh, vh, gh, 0.125, causal)
+    assert_close(host(dV), rv, 2e-2, "dv")
+    assert_close(host(dK), rk, 2e-2, "dk")
+    assert_close(host(dQ), rq, 2e-2, "dq")
+
+
+def test_sdpa_bwd_bnth_strides():
+    """BNTH inputs and BTNH outputs through the strides (the plugin's layouts)."""
+    rng = np.random.default_rng(31)
+    B, N, T = 2, 4, 256
+    qb, kb, vb, gb = (rng.standard_normal((B, N, T, 64)).astype(np.float32) for _ in range(4))
+    Q, K, V, G = (bf16_dev(a) for a in (qb, kb, vb, gb))
+    O = torch.empty((B, N, T, 64), device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty((B, N, T), device="cuda")
+    bnth, btnh = [N * T * 64, 64, T * 64], [T * N * 64, N * 64, 64]
+    kernels.sdpa_fwd_lse(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), lse.data_ptr(), B, T,
+                         T, N, 64, bnth * 4, 0.125, True, kernels.DT_BF16, stream())
+    dQ, dK, dV = (torch.empty((B, T, N, 64), device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    kernels.sdpa_bwd(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), G.data_ptr(), lse.data_ptr(),
+                     dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), B, T, N, 64, bnth * 5 + btnh * 3, 0.125,
+                     True, kernels.DT_BF16, stream())
+    tr = lambda a: np.transpose(a, (0, 2, 1, 3))
+    rq, rk, rv = restate.sdpa_bwd_ref(*(tr(host(a)) for a in (Q, K, V, G)), 0.125, True)
+    assert_close(host(dV), rv, 2e-2, "dv")
+    assert_close(host(dK), rk, 2e-2, "dk")
+    assert_close(host(dQ), rq, 2e-2, "dq")
+
+
 def test_sdpa_bnth_strides_and_simt_fallback():
     """BNTH views through the strided entry point, and head dim 32 (SIMT path)."""
     rng = np.random.default_rng(23)

@@ -154,6 +154,22 @@ def test_sdpa_bwd_restatement_matches_autodiff():
         np.testing.assert_allclose(gg, r, rtol=1e-9, atol=1e-12)
 
 
+@pytest.mark.parametrize("form,causal", [("autodiff", True), ("custom_jvp", True), ("custom_jvp", False)])
+def test_attention_vjp_programs_match_closed_form(form, causal):
+    """Both written forms of attention's vjp (programs.attention_vjp: the
+    quotient-rule gradient and jax.nn.softmax's custom-JVP backward) evaluate,
+    in f64, to restate.sdpa_bwd_ref -- the math the fused backward kernel runs."""
+    from jax_b200 import programs
+    rng = np.random.default_rng(17)
+    shp = (1, 24, 2, 64)
+    q, k, v, g = (rng.standard_normal(shp) for _ in range(4))
+    text = programs.attention_vjp(B=1, T=24, N=2, H=64, causal=causal, dt="f32", form=form)
+    o, dq, dk, dv = hlo_interp.run(text, [[q, k, v, g]])[0]
+    np.testing.assert_allclose(o, restate.sdpa_ref(q, k, v, 0.125, causal), rtol=1e-9, atol=1e-12)
+    for got, ref in zip((dq, dk, dv), restate.sdpa_bwd_ref(q, k, v, g, 0.125, causal)):
+        np.testing.assert_allclose(got, ref, rtol=1e-9, atol=1e-12)
+
+
 def test_layer_norm_bwd_restatement_matches_autodiff():
     from jax_b200.hlo import Builder
     rng = np.random.default_rng(6)

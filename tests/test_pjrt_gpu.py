@@ -111,6 +111,30 @@ def test_sdpa_config(client):
     assert_close(o, restate.sdpa_ref(q, k, v, 0.125, True), 2e-3, "causal sdpa")
 
 
+@pytest.mark.parametrize("form,causal,T", [("autodiff", True, 256), ("custom_jvp", True, 256),
+                                           ("custom_jvp", False, 256), ("custom_jvp", True, 200),
+                                           ("custom_jvp", False, 130)])
+def test_attention_vjp_fused(client, form, causal, T):
+    """Attention and its vjp in bf16 (the transformer's form, and jax.nn.softmax's
+    custom-JVP form), planned as the tcgen05 forward with row statistics plus
+    the fused backward; against the float64 closed form on the same bf16
+    inputs.  bf16 outputs, P and dS enter the products as bf16: 2e-2 relative
+    with a floor of 2e-2 * rms(reference)."""
+    B, N = 2, 4
+    text = programs.attention_vjp(B=B, T=T, N=N, H=64, causal=causal, form=form)
+    plan = pjrt.inspect(text, 1)
+    assert "sdpa_bwd in=" in plan and "gemm in=" not in plan
+    rng = np.random.default_rng(T + causal)
+    arrs = [hlo_interp.bf16_round(rng.standard_normal((B, T, N, 64)).astype(np.float32)) for _ in range(4)]
+    o, dq, dk, dv = run(client, text, arrs, bf16_args=(0, 1, 2, 3))
+    q, k, v, g = arrs
+    assert_close(o, restate.sdpa_ref(q, k, v, 0.125, causal), 2e-2, "o")
+    rq, rk, rv = restate.sdpa_bwd_ref(q, k, v, g, 0.125, causal)
+    assert_close(dv, rv, 2e-2, "dv")
+    assert_close(dk, rk, 2e-2, "dk")
+    assert_close(dq, rq, 2e-2, "dq")
+
+
 def test_sdpa_unfused_fallback_agrees(client):
     """With the softmax probabilities also returned, the chain is not fused: the
     GEMM + generated-kernel path must give the same output."""

@@ -109,9 +109,59 @@ def test_row_wise_kernels_share_one_pass():
     steps = pjrt.inspect(programs.softmax_then_transposed_sum(), 1).split("steps:")[1]
     names = [l.split()[0] for l in steps.strip().splitlines()]
     assert names == ["k0_rows", "k1_reduce"]
-    # transformer step: every layer norm, attention softmax and the loss
+    # transformer step: every layer norm and the loss
     steps = pjrt.inspect(programs.transformer_step(), 1).split("steps:")[1]
-    assert steps.count("_rows in=") >= 6 * 4 + 2
+    assert steps.count("_rows in=") >= 6 * 3 + 2
+
+
+def _step_names(text):
+    steps = pjrt.inspect(text, 1).split("steps:")[1]
+    return [l.split()[0] for l in steps.strip().splitlines()]
+
+
+def test_attention_with_its_backward_fuses():
+    """Attention whose probabilities also feed its backward (dV = P^T dO,
+    dP = dO V^T, the softmax vjp, dQ = dS K, dK = dS^T Q) becomes one forward
+    kernel that keeps the row statistics plus one backward kernel: no GEMM,
+    softmax row group or transpose is left.  The softmax vjp is recognized by
+    its value (a symbolic form in P, the row sum and dP), so the quotient-rule
+    form of generic autodiff and the form of jax.nn.softmax's custom JVP both
+    match."""
+    for form, causal in (("autodiff", True), ("custom_jvp", True), ("custom_jvp", False)):
+        names = _step_names(programs.attention_vjp(form=form, causal=causal))
+        assert names.count("sdpa") == 1 and names.count("sdpa_bwd") == 1, (form, names)
+        assert "gemm" not in names and not any(n.endswith("_rows") for n in names), (form, names)
+    # outside the backward kernel's limits (T > 256; f32) the chain stays unfused
+    for kw in (dict(T=384), dict(dt="f32")):
+        names = _step_names(programs.attention_vjp(form="custom_jvp", **kw))
+        assert "sdpa_bwd" not in names and "gemm" in names, (kw, names)
+    names = _step_names(programs.transformer_step())
+    assert names.count("sdpa") == 6 and names.count("sdpa_bwd") == 6
+
+
+def test_attention_backward_with_another_value_is_not_fused():
+    """A backward whose dS is not the softmax vjp (wrong sign of the row-sum
+    term, or a scale other than the forward's) keeps its unfused plan."""
+    from jax_b200.hlo import Builder
+    from jax_b200.programs import softmax
+    B, T, N, H = 1, 128, 2, 64
+    for sign, sc in ((+1.0, 0.125), (-1.0, 0.25)):
+        b = Builder("jit_attention_vjp_altered")
+        q, k, v, g = (b.param((B, T, N, H), "bf16") for _ in range(4))
+        qt, kt, vt, gt = (b.transpose(x, [0, 2, 1, 3]) for x in (q, k, v, g))
+        logits = b.dot_general(qt, kt, ([3], [3]), ([0, 1], [0, 1]), out_dt="f32") * 0.125
+        y = softmax(b, logits)
+        yb = b.convert(y, "bf16")
+        o = b.dot_general(yb, vt, ([3], [2]), ([0, 1], [0, 1]))
+        dv = b.dot_general(yb, gt, ([2], [2]), ([0, 1], [0, 1]))
+        dy = b.convert(b.dot_general(gt, vt, ([3], [3]), ([0, 1], [0, 1])), "f32")
+        yg = y * dy
+        dx = yg + y * b.broadcast_in_dim(b.sum(yg, [3]), yg.shape, [0, 1, 2]) * sign
+        ds = dx * sc
+        dq = b.convert(b.dot_general(ds, kt, ([3], [2]), ([0, 1], [0, 1])), "bf16")
+        dk = b.convert(b.dot_general(ds, qt, ([2], [2]), ([0, 1], [0, 1])), "bf16")
+        names = _step_names(b.module([o, dq, dk, dv]))
+        assert "sdpa_bwd" not in names, (sign, sc, names)
 
 
 def test_identical_kernels_compile_once_and_cache_on_disk(tmp_path, monkeypatch):
