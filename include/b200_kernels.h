@@ -105,8 +105,9 @@ B200_API int b200_sdpa_fwd_lse(const void* q, const void* k, const void* v, void
  * q, k, v, o, dout, dq, dk, dv are bf16 with the head dim contiguous; strides
  * (elements) are (b, t, n) for q, k, v, o, dout, dq, dk, dv in that order (24
  * values, each a multiple of 8).  Needs D == 64 and T <= 256; other shapes
- * and dtypes return B200_ERR_UNSUPPORTED.  P and dS enter the tensor-core
- * products as bf16, accumulation is f32.  Replaces reference
+ * and dtypes return B200_ERR_UNSUPPORTED.  P enters the tensor-core products
+ * as bf16 (as jax.nn.dot_product_attention rounds the probabilities), dS as
+ * bf16 hi + lo parts (about 16 significant bits); accumulation is f32.  Replaces reference
  * src/jax_mlx_pjrt.cpp:8152-8206 (mlx_sdpa_bwd through mx::vjp) and the math
  * of src/jax_mlx/sdpa.py:65-87. */
 B200_API int b200_sdpa_bwd(const void* q, const void* k, const void* v, const void* o,

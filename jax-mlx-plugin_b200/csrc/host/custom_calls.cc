@@ -15,7 +15,11 @@
 //     dx = rstd (g - mean(g) - xhat mean(g xhat)), dw = sum(dy xhat), db = sum(dy).
 //
 // Arithmetic runs in f32 whatever the operand type (bf16 operands are widened
-// and the results rounded back), as MLX accumulates these in f32.
+// and the results rounded back), as MLX accumulates these in f32.  bf16
+// attention with head dim 64 and at most 256 positions skips the expansion:
+// fused_sdpa_bwd_call puts the tcgen05 forward (which keeps each row's
+// softmax statistic) and the fused backward kernel in its place, with f32
+// accumulation, P rounded to bf16 for dV and dS kept to about 16 bits.
 #include "custom_calls.h"
 
 #include <cstdio>
@@ -223,6 +227,45 @@ std::string layer_norm_bwd(const Node& n, const std::vector<TensorType>& in) {
 }
 
 }  // namespace
+
+bool fused_sdpa_bwd_call(const Node& n, const std::vector<ValueRef>& ops, Graph& dst,
+                         std::vector<ValueRef>& outs) {
+  if (n.target != "mlx_sdpa_bwd" || ops.size() != 4 || n.results.size() != 3) return false;
+  const TensorType& t = dst.type(ops[0]);
+  if (t.dtype != DType::BF16 || t.rank() != 4 || t.dims[3] != 64 || t.dims[1] > 256) return false;
+  for (const auto& o : ops)
+    if (dst.type(o) != t) return false;
+  for (const auto& r : n.results)
+    if (r != t) return false;
+  const float scale = config_value(n.backend_config, "scale", 1.0f);
+  if (!(scale > 0.f)) return false;
+  const int64_t B = t.dims[0], T = t.dims[1], N = t.dims[2], D = t.dims[3];
+  const std::vector<int64_t> st = {T * N * D, N * D, D};  // (b, t, n) of a dense BTNH tensor
+  Node fw;
+  fw.op = Op::FusedSdpa;
+  fw.operands = {ops[0], ops[1], ops[2]};
+  TensorType lt;
+  lt.dtype = DType::F32;
+  lt.dims = {B, N, T};
+  fw.results = {t, lt};
+  fw.name = n.name + ".fwd";
+  fw.f_scale = scale;
+  fw.i_flags = 2;  // no mask, row statistics
+  fw.dims = {B, T, T, N, D};
+  for (int k = 0; k < 4; ++k) fw.strides.insert(fw.strides.end(), st.begin(), st.end());
+  const int fid = dst.add(std::move(fw));
+  Node bw;
+  bw.op = Op::FusedSdpaBwd;
+  bw.operands = {ops[0], ops[1], ops[2], ValueRef{fid, 0}, ops[3], ValueRef{fid, 1}};
+  bw.results = n.results;
+  bw.name = n.name;
+  bw.f_scale = scale;
+  bw.dims = {B, T, T, N, D};
+  for (int k = 0; k < 8; ++k) bw.strides.insert(bw.strides.end(), st.begin(), st.end());
+  const int bid = dst.add(std::move(bw));
+  outs = {ValueRef{bid, 0}, ValueRef{bid, 1}, ValueRef{bid, 2}};
+  return true;
+}
 
 bool expands_custom_call(const std::string& target) {
   return target == "mlx_sdpa_bwd" || target == "mlx_layer_norm_bwd";

@@ -6,6 +6,8 @@
 // mask that JAX emits for is_causal=True.
 #include "passes.h"
 
+#include <cstdlib>
+
 #include "custom_calls.h"
 
 #include <cmath>
@@ -40,11 +42,15 @@ void inline_into(const Module& m, const Graph& src, const std::vector<ValueRef>&
       continue;
     }
     if (n.op == Op::CustomCall && expands_custom_call(n.target)) {
+      std::vector<ValueRef> r;
+      if (fused_sdpa_bwd_call(n, ops, dst, r)) {  // the fused attention kernels
+        map[i] = r;
+        continue;
+      }
       // backward custom calls become ordinary StableHLO (custom_calls.cc)
       std::vector<TensorType> types;
       for (auto& o : ops) types.push_back(dst.type(o));
       Module sub = parse_module(custom_call_expansion(n, types));
-      std::vector<ValueRef> r;
       inline_into(sub, *sub.main(), ops, dst, r, depth + 1);
       if (r.size() != n.results.size()) throw PjrtErr(13, "custom call expansion result count");
       for (size_t k = 0; k < r.size(); ++k)
@@ -1302,7 +1308,12 @@ MatchStats match_patterns(Graph& g) {
   MatchStats st;
   Matcher m(g);
   st.sdpa = m.match_sdpa();
-  st.sdpa_train = m.match_sdpa_train();
+  // B200_BF16_ROUND_EACH_OP=1 compiles a program that rounds after every bf16
+  // op (to be compared element by element with an interpreter that does the
+  // same); the fused attention backward rounds only at its outputs, so that
+  // mode keeps the attention backward as the program writes it.
+  const char* each = getenv("B200_BF16_ROUND_EACH_OP");
+  if (!(each && each[0] == '1')) st.sdpa_train = m.match_sdpa_train();
   st.layer_norm = m.match_layer_norm();
   if (st.sdpa || st.sdpa_train || st.layer_norm) dce(g);
   return st;

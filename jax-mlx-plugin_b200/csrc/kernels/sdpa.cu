@@ -1124,14 +1124,17 @@ int launch_x3(const void* q, const void* k, const void* v, void* o, int64_t B, i
 //   warp 8     lane 0 issues S = Q_i K_j^T and dP = dO_i V_j^T (tcgen05,
 //              M = N = 128) into TMEM, waits for P / dS, then accumulates
 //              dV_j += P^T dO_i, dK_j += dS^T Q_i (A operands MN-major) and
-//              dQ_i += dS K_j (B MN-major) in TMEM;
+//              dQ_i += dS K_j (B MN-major) in TMEM, each dS product as two
+//              MMAs (bf16 hi and lo parts);
 //   warps 0-7  warp w reads TMEM lane quarter w % 4 (32 query rows) and key
 //              half w / 4 of S and dP, forms P = 2^(S*scale*log2e - lse2)
 //              and dS = P (dP - D) scale in f32, with D = rowsum(dO * O),
-//              and writes both as bf16 into shared memory (two 64-key
-//              chunks of 128-byte rows, 16-byte units XOR row % 8); after the
-//              last pair of key tile j they store dK_j and dV_j, and at the
-//              end every dQ_i.
+//              and writes P as bf16 (the precision jax.nn.dot_product_attention
+//              gives the probabilities) and dS as bf16 hi + lo (about 16
+//              significant bits, like the f32 dS of the unfused program) into
+//              shared memory (two 64-key chunks of 128-byte rows, 16-byte
+//              units XOR row % 8); after the last pair of key tile j they
+//              store dK_j and dV_j, and at the end every dQ_i.
 // TMEM columns: S 0-127, dP 128-255, dV 256-319, dK 320-383, dQ_i 384 + 64 i.
 // Math: the vjp of softmax(QK^T*scale)V (reference src/jax_mlx/sdpa.py:65-87,
 // whose mlx_sdpa_bwd the reference runs through mx::vjp,
@@ -1161,9 +1164,11 @@ struct BwdCfg {
   static constexpr int K_OFF = DO_OFF + 2 * TILE;
   static constexpr int V_OFF = K_OFF + 2 * TILE;
   static constexpr int P_OFF = V_OFF + 2 * TILE;  // 2 chunks of 64 keys
-  static constexpr int DS_OFF = P_OFF + 2 * TILE;
-  static constexpr int BAR_OFF = DS_OFF + 2 * TILE;
+  static constexpr int DS_OFF = P_OFF + 2 * TILE;  // dS as bf16 hi ...
+  static constexpr int DSL_OFF = DS_OFF + 2 * TILE;  // ... and lo (rounded residual)
+  static constexpr int BAR_OFF = DSL_OFF + 2 * TILE;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
+  static_assert(SMEM <= 232448, "shared memory above the 227 KB per-block limit");
 };
 constexpr int kBwdThreads = 288;
 
@@ -1231,6 +1236,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t idesc_t = umma_idesc(1u, 1, 1, 64, 128);   // P^T / dS^T times dO / Q
       constexpr uint32_t idesc_q = umma_idesc(1u, 0, 1, 64, 128);   // dS times K
       const uint32_t pp = smem_u32(smem + C::P_OFF), ds = smem_u32(smem + C::DS_OFF);
+      const uint32_t dsl = smem_u32(smem + C::DSL_OFF);
       bool ok = mbar_wait(ld_full, 0, abort, p.err, 231);
       int pair = 0;
       for (int j = 0; ok && j < nt; ++j) {
@@ -1261,9 +1267,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                      idesc_t, ka);
             umma_f16(tDK, umma_desc(ds + kk * 2048, 16384, 1024), umma_desc(qt + kk * 2048, 8192, 1024),
                      idesc_t, ka);
+            umma_f16(tDK, umma_desc(dsl + kk * 2048, 16384, 1024), umma_desc(qt + kk * 2048, 8192, 1024),
+                     idesc_t, 1);
             // 16 keys: 32 bytes of a dS row (K-major A), 16 rows of K (MN-major B)
-            umma_f16(tDQ, umma_desc(ds + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                     umma_desc(kt + kk * 2048, 8192, 1024), idesc_q, (uint32_t)(j != 0 || kk != 0));
+            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_f16(tDQ, umma_desc(ds + aoff, 16, 1024), umma_desc(kt + kk * 2048, 8192, 1024), idesc_q,
+                     (uint32_t)(j != 0 || kk != 0));
+            umma_f16(tDQ, umma_desc(dsl + aoff, 16, 1024), umma_desc(kt + kk * 2048, 8192, 1024), idesc_q, 1);
           }
           umma_commit(acc_done);
         }
@@ -1318,7 +1328,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           tmem_ld32(tS + lane_base + (uint32_t)col, sv);
           tmem_ld32(tDP + lane_base + (uint32_t)col, v);
           const int kb = j * 128 + col;
-          uint32_t pw[16], dw[16];
+          uint32_t pw[16], dw[16], dl[16];
 #pragma unroll
           for (int x = 0; x < 16; ++x) {
             float pv[2], dv[2];
@@ -1330,15 +1340,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               dv[e] = pv[e] * (v[2 * x + e] - di) * p.scale;
             }
             pw[x] = pack_bf16x2(pv[0], pv[1]);
-            dw[x] = pack_bf16x2(dv[0], dv[1]);
+            __nv_bfloat162 hh = __floats2bfloat162_rn(dv[0], dv[1]);
+            dw[x] = *reinterpret_cast<uint32_t*>(&hh);
+            const float2 hf = __bfloat1622float2(hh);
+            dl[x] = pack_bf16x2(dv[0] - hf.x, dv[1] - hf.y);
           }
           uint8_t* prow = smem + C::P_OFF + h * C::TILE + r * 128;
           uint8_t* drow = smem + C::DS_OFF + h * C::TILE + r * 128;
+          uint8_t* lrow = smem + C::DSL_OFF + h * C::TILE + r * 128;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int off = ((c * 4 + u) ^ (r & 7)) << 4;
             *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
             *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+            *reinterpret_cast<uint4*>(lrow + off) = make_uint4(dl[4 * u], dl[4 * u + 1], dl[4 * u + 2], dl[4 * u + 3]);
           }
         }
         fence_proxy_async_smem();

@@ -36,14 +36,20 @@ def sdpa_ref(q, k, v, scale=None, causal=False):
     return np.transpose(w @ vb, (0, 2, 1, 3))
 
 
-def sdpa_bwd_ref(q, k, v, g, scale, causal=False):
+def sdpa_bwd_ref(q, k, v, g, scale, causal=False, probs_bf16=False, o=None):
     """dQ, dK, dV of softmax(Q K^T scale [+ causal fill]) V, layout (B, T, N, H).
 
     Follows reference src/jax_mlx/sdpa.py:65-87 (_mlx_sdpa_bwd_impl): weights =
     softmax(logits), dv = weights^T g, d_weights = g v^T, d_scores = weights *
     (d_weights - sum(d_weights * weights, -1)) * scale, dq = d_scores k,
     dk = d_scores^T q.  `causal` fills logits of keys after the query with
-    -0.7 * finfo(f32).max first, as sdpa_ref does (their weights are 0)."""
+    -0.7 * finfo(f32).max first, as sdpa_ref does (their weights are 0).
+    `probs_bf16` rounds the weights to bf16 where jax.nn.dot_product_attention
+    on bf16 operands does (``probs.astype(value.dtype)``), i.e. in dv; the
+    softmax backward keeps them exact.  `o` (B, T, N, H), when given, replaces
+    the row term sum(d_weights * weights) by sum(g * o) -- the same value
+    when o is the exact output -- as flash-style backward kernels compute it
+    from the forward's stored (rounded) output."""
     q, k, v, g = (np.transpose(np.asarray(a, dtype=np.float64), (0, 2, 1, 3)) for a in (q, k, v, g))
     logits = q @ np.swapaxes(k, -1, -2) * scale
     if causal:
@@ -51,9 +57,17 @@ def sdpa_bwd_ref(q, k, v, g, scale, causal=False):
         logits = np.where(np.tril(np.ones((T, S), bool)), logits, -0.7 * np.finfo(np.float32).max)
     w = np.exp(logits - logits.max(-1, keepdims=True))
     w /= w.sum(-1, keepdims=True)
-    dv = np.swapaxes(w, -1, -2) @ g
+    wv = w
+    if probs_bf16:
+        from .hlo_interp import bf16_round
+        wv = bf16_round(w.astype(np.float32)).astype(np.float64)
+    dv = np.swapaxes(wv, -1, -2) @ g
     dw = g @ np.swapaxes(v, -1, -2)
-    ds = w * (dw - (dw * w).sum(-1, keepdims=True)) * scale
+    if o is None:
+        rowterm = (dw * w).sum(-1, keepdims=True)
+    else:
+        rowterm = (g * np.transpose(np.asarray(o, dtype=np.float64), (0, 2, 1, 3))).sum(-1)[..., None]
+    ds = w * (dw - rowterm) * scale
     dq = ds @ k
     dk = np.swapaxes(ds, -1, -2) @ q
     t = lambda a: np.transpose(a, (0, 2, 1, 3))

@@ -137,6 +137,12 @@ def test_attention_with_its_backward_fuses():
         assert "sdpa_bwd" not in names and "gemm" in names, (kw, names)
     names = _step_names(programs.transformer_step())
     assert names.count("sdpa") == 6 and names.count("sdpa_bwd") == 6
+    # the reference's mlx_sdpa_bwd custom call: bf16 runs the forward with row
+    # statistics and the fused backward; f32 keeps the compile-time expansion
+    names = _step_names(programs.sdpa_custom_calls(2, 128, 2, 64, 0.125, "bf16"))
+    assert names == ["sdpa", "sdpa", "sdpa_bwd"], names
+    names = _step_names(programs.sdpa_custom_calls(2, 128, 2, 64, 0.125, "f32"))
+    assert "sdpa_bwd" not in names and "gemm" in names, names
 
 
 def test_attention_backward_with_another_value_is_not_fused():
