@@ -456,6 +456,55 @@ def dominant_gemm_time(rig: Rig, launches: int = 20):
     return t, 2.0 * M * N * K
 
 
+def attention_kernel_times(rig: Rig, batch: int, launches: int = 20):
+    """The transformer's fused attention kernels at the step's per-GPU shape
+    ([batch, 256, 8, 64] bf16, causal, scale 1/8), timed live through the C ABI:
+    the forward with row statistics (b200_sdpa_fwd_lse) and the backward
+    (b200_sdpa_bwd), each `launches` launches over three rotating input /
+    output sets (each above 100 MB at batch 64) between one event pair on the
+    plugin's stream.  Algorithmic FLOPs count the causal half of each product:
+    forward 2 products (Q K^T, P V), backward 5 (S, dP, dV, dK, dQ)."""
+    from jax_b200 import kernels
+    torch = rig.torch
+    B, T, N, H = batch, TR_CFG["seq"], TR_CFG["heads"], TR_CFG["d"] // TR_CFG["heads"]
+    st = rig.client.device_stream(rig.dev)
+    dense = [T * N * H, N * H, H]
+
+    def mk():
+        q, k, v, g = (torch.randn(B, T, N, H, device="cuda", dtype=torch.bfloat16) for _ in range(4))
+        o = torch.empty_like(q)
+        lse = torch.empty(B, N, T, device="cuda")
+        return q, k, v, g, o, lse, torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    sets = [mk() for _ in range(3)]
+
+    def fwd(i):
+        q, k, v, g, o, lse, dq, dk, dv = sets[i % 3]
+        kernels.sdpa_fwd_lse(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), B, T,
+                             T, N, H, dense * 4, 0.125, True, kernels.DT_BF16, st)
+
+    def bwd(i):
+        q, k, v, g, o, lse, dq, dk, dv = sets[i % 3]
+        kernels.sdpa_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), g.data_ptr(), lse.data_ptr(),
+                         dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, T, N, H, dense * 8, 0.125, True,
+                         kernels.DT_BF16, st)
+    out = {}
+    for name, fn, nprod in (("fwd", fwd, 2), ("bwd", bwd, 5)):
+        for i in range(6):
+            fwd(i)
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(rig.stream)
+        for i in range(launches):
+            fn(i)
+        e1.record(rig.stream)
+        torch.cuda.synchronize()
+        out[name] = (e0.elapsed_time(e1) * 1e-3 / launches, nprod * 2.0 * B * N * T * T * H / 2)
+    del sets
+    torch.cuda.empty_cache()
+    return out
+
+
 def _mlp_args(rng, batch):
     params = []
     for i in range(len(MLP_DIMS) - 1):
@@ -738,6 +787,18 @@ def roofline_for(workload: str, res: dict, world: int, pk: dict, pk_kind: str, t
                                   "per_launch_us": dt * 1e6, "per_launch_flops": dfl,
                                   "timing": "20 C-ABI launches over 2 rotating 1.1 GB operand sets, "
                                             "one event pair on the plugin's stream"}
+    if "attention" in res:
+        att = {}
+        for name, (t, fl) in res["attention"].items():
+            att[name] = {"kernel": "sdpa_fwd_ws<bf16> + row statistics" if name == "fwd" else "sdpa_bwd_tc",
+                         "per_launch_us": t * 1e6, "per_launch_flops": fl, "achieved": fl / t / 1e12,
+                         "peak": pk["bf16_tflops"], "frac": fl / t / 1e12 / pk["bf16_tflops"],
+                         "peak_kind": pk_kind + " bf16 dense (burst)"}
+        att["shape_btnh"] = [TR_CFG["batch"] // world, TR_CFG["seq"], TR_CFG["heads"],
+                             TR_CFG["d"] // TR_CFG["heads"]]
+        att["flops"] = "causal half of each product: forward 2, backward 5"
+        att["timing"] = "20 C-ABI launches over 3 rotating input / output sets, one event pair"
+        out["attention_kernels"] = att
     return out
 
 
@@ -752,6 +813,7 @@ def run_ours(rig: Rig, workload: str, a, world: int, rank: int) -> dict:
     res = bench_train(rig, workload, a.steps, a.warmup, world, rank)
     if workload == "transformer":
         res["dominant"] = dominant_gemm_time(rig)
+        res["attention"] = attention_kernel_times(rig, TR_CFG["batch"] // world)
     return res
 
 

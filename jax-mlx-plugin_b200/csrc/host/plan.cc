@@ -272,7 +272,7 @@ struct Builder {
       // vector column reduction: blocks of kColWarps warps over 32 * cv
       // outputs each; split the rows until about 8 blocks per SM (a full SM
       // of loads in flight), keeping at least 4 rows per warp and at most 512
-      // partial rows to combine
+      // partial rows to combine (32 warps per combine block, 16 rows each)
       if (RED < 8 * CodeGen::kColWarps) return 1;
       const int64_t bx = (OUT / cv + 31) / 32;
       int64_t split = (148 * 8) / std::max<int64_t>(bx, 1);

@@ -1120,21 +1120,26 @@ int launch_x3(const void* q, const void* k, const void* v, void* o, int64_t B, i
 //
 // One CTA = one (batch, head); Q, dO, K and V (at most 2 tiles of 128 rows
 // each) are loaded once by TMA and stay in shared memory.  Query tile i and
-// key tile j form a pair (j outer; causal: i >= j).  Per pair, 288 threads:
-//   warp 8     lane 0 issues S = Q_i K_j^T and dP = dO_i V_j^T (tcgen05,
-//              M = N = 128) into TMEM, waits for P / dS, then accumulates
-//              dV_j += P^T dO_i, dK_j += dS^T Q_i (A operands MN-major) and
-//              dQ_i += dS K_j (B MN-major) in TMEM, each dS product as two
-//              MMAs (bf16 hi and lo parts);
-//   warps 0-7  warp w reads TMEM lane quarter w % 4 (32 query rows) and key
-//              half w / 4 of S and dP, forms P = 2^(S*scale*log2e - lse2)
-//              and dS = P (dP - D) scale in f32, with D = rowsum(dO * O),
-//              and writes P as bf16 (the precision jax.nn.dot_product_attention
-//              gives the probabilities) and dS as bf16 hi + lo (about 16
-//              significant bits, like the f32 dS of the unfused program) into
-//              shared memory (two 64-key chunks of 128-byte rows, 16-byte
-//              units XOR row % 8); after the last pair of key tile j they
-//              store dK_j and dV_j, and at the end every dQ_i.
+// key tile j form a pair (j outer; causal: i >= j).  17 warps (544 threads):
+//   warps 0-15 warp w reads TMEM lane quarter w % 4 (32 query rows) and key
+//     columns 32 (w / 4) .. +31 of S and dP, forms P = 2^(S*scale*log2e -
+//     lse2) and dS = P (dP - D) scale in f32, with D = rowsum(dO * O), and
+//     writes P as bf16 (the precision jax.nn.dot_product_attention gives the
+//     probabilities) and dS as bf16 hi + lo (about 16 significant bits, like
+//     the f32 dS of the unfused program) into shared memory (two 64-key chunks
+//     of 128-byte rows, 16-byte units XOR row % 8); after the last pair of key
+//     tile j the warps store dK_j and dV_j, and at the end every dQ_i;
+//   warp 16   lane 0 issues the TMA loads and the MMAs: S = Q_i K_j^T
+//     and dP = dO_i V_j^T (M = N = 128) into TMEM, and once P / dS are in
+//     shared memory dV_j += P^T dO_i, dK_j += dS^T Q_i (A operands MN-major)
+//     and dQ_i += dS K_j (B MN-major), each dS product as two MMAs (hi, lo).
+//     The next pair's S / dP are issued as soon as every warp holds the
+//     current ones in registers, so the tensor core runs them and the
+//     previous pair's dV / dK / dQ while the warps compute (issuing blocks
+//     while the tensor core's queue is full, so it has a warp of its own).
+// D is formed first with coalesced loads of O and dO (8 lanes per 128-byte
+// row) and kept in shared memory.  dK_j / dV_j go out through the K_j / V_j
+// tiles (free once key tile j is done) and dQ_i through Q_i, as TMA stores.
 // TMEM columns: S 0-127, dP 128-255, dV 256-319, dK 320-383, dQ_i 384 + 64 i.
 // Math: the vjp of softmax(QK^T*scale)V (reference src/jax_mlx/sdpa.py:65-87,
 // whose mlx_sdpa_bwd the reference runs through mx::vjp,
@@ -1163,53 +1168,69 @@ struct BwdCfg {
   static constexpr int DO_OFF = Q_OFF + 2 * TILE;
   static constexpr int K_OFF = DO_OFF + 2 * TILE;
   static constexpr int V_OFF = K_OFF + 2 * TILE;
-  static constexpr int P_OFF = V_OFF + 2 * TILE;  // 2 chunks of 64 keys
-  static constexpr int DS_OFF = P_OFF + 2 * TILE;  // dS as bf16 hi ...
+  static constexpr int P_OFF = V_OFF + 2 * TILE;     // 2 chunks of 64 keys
+  static constexpr int DS_OFF = P_OFF + 2 * TILE;    // dS as bf16 hi ...
   static constexpr int DSL_OFF = DS_OFF + 2 * TILE;  // ... and lo (rounded residual)
-  static constexpr int BAR_OFF = DSL_OFF + 2 * TILE;
+  static constexpr int D_OFF = DSL_OFF + 2 * TILE;  // D per query row (f32, 2 tiles)
+  static constexpr int BAR_OFF = D_OFF + 2 * 128 * 4;
   static constexpr int SMEM = BAR_OFF + 256 + 1024;
   static_assert(SMEM <= 232448, "shared memory above the 227 KB per-block limit");
 };
-constexpr int kBwdThreads = 288;
-
-__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, const float* v) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    d[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
-                      pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
-}
+constexpr int kBwdWarps = 16;                       // compute warps
+constexpr int kBwdThreads = (kBwdWarps + 1) * 32;  // + the issue warp
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     sdpa_bwd_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                 const __grid_constant__ CUtensorMap tV, const __grid_constant__ CUtensorMap tDO,
-                BwdArgs p) {
+                const __grid_constant__ CUtensorMap mDQ, const __grid_constant__ CUtensorMap mDK,
+                const __grid_constant__ CUtensorMap mDV, BwdArgs p) {
   pdl_wait();
   using C = BwdCfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* ld_full = bars + 0;   // every Q / dO / K / V tile landed
-  uint64_t* sd_full = bars + 1;   // S and dP of the current pair in TMEM
-  uint64_t* pds_full = bars + 2;  // P and dS in shared memory (8 warps)
-  uint64_t* acc_done = bars + 3;  // the pair's dV / dK / dQ MMAs complete
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
+  uint64_t* sd_full = bars + 1;   // S and dP of a pair in TMEM (one phase per pair)
+  uint64_t* s_free = bars + 2;    // S and dP read into registers (16 warps)
+  uint64_t* pds_full = bars + 3;  // P and dS in shared memory (16 warps)
+  uint64_t* acc_done = bars + 4;  // the pair's dV / dK / dQ MMAs complete
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 5);
   volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool issuer = tid == kBwdWarps * 32;
   const int n = (int)blockIdx.x % p.N, b = (int)blockIdx.x / p.N;
   const int nt = (p.T + 127) / 128;
   auto tile = [&](int off, int i) { return smem + off + i * C::TILE; };
+  // the pairs in order: key tile j outer, query tile i inner (causal: i >= j)
+  const int np = p.causal ? nt * (nt + 1) / 2 : nt * nt;
+  auto pair_i = [&](int k) {
+    if (!p.causal) return k % nt;
+    for (int j = 0; j < nt; ++j) {
+      if (k < nt - j) return j + k;
+      k -= nt - j;
+    }
+    return 0;
+  };
+  auto pair_j = [&](int k) {
+    if (!p.causal) return k / nt;
+    for (int j = 0; j < nt; ++j) {
+      if (k < nt - j) return j;
+      k -= nt - j;
+    }
+    return 0;
+  };
 
-  if (tid == 0) {
+  if (issuer) {
     mbar_init(ld_full, 1);
     mbar_init(sd_full, 1);
-    mbar_init(pds_full, 8);
+    mbar_init(s_free, kBwdWarps);
+    mbar_init(pds_full, kBwdWarps);
     mbar_init(acc_done, 1);
     *abort = 0;
     mbar_fence_init();
   }
-  if (warp == 8) {
+  if (warp == kBwdWarps) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
@@ -1219,170 +1240,227 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tmem = *tslot;
   const uint32_t tS = tmem, tDP = tmem + 128u, tDV = tmem + 256u, tDK = tmem + 320u;
 
-  if (warp == 8) {
-    if (lane == 0) {  // ---- TMA and MMA issue
-      tma_prefetch_desc(&tQ);
-      tma_prefetch_desc(&tK);
-      tma_prefetch_desc(&tV);
-      tma_prefetch_desc(&tDO);
-      mbar_expect_tx(ld_full, 4 * nt * C::TILE);
-      for (int i = 0; i < nt; ++i) {
-        tma_load_4d(tile(C::Q_OFF, i), &tQ, ld_full, 0, n, i * 128, b);
-        tma_load_4d(tile(C::DO_OFF, i), &tDO, ld_full, 0, n, i * 128, b);
-        tma_load_4d(tile(C::K_OFF, i), &tK, ld_full, 0, n, i * 128, b);
-        tma_load_4d(tile(C::V_OFF, i), &tV, ld_full, 0, n, i * 128, b);
-      }
-      constexpr uint32_t idesc_s = umma_idesc(1u, 0, 0, 128, 128);  // K-major x K-major
-      constexpr uint32_t idesc_t = umma_idesc(1u, 1, 1, 64, 128);   // P^T / dS^T times dO / Q
-      constexpr uint32_t idesc_q = umma_idesc(1u, 0, 1, 64, 128);   // dS times K
-      const uint32_t pp = smem_u32(smem + C::P_OFF), ds = smem_u32(smem + C::DS_OFF);
-      const uint32_t dsl = smem_u32(smem + C::DSL_OFF);
-      bool ok = mbar_wait(ld_full, 0, abort, p.err, 231);
-      int pair = 0;
-      for (int j = 0; ok && j < nt; ++j) {
-        const int i0 = p.causal ? j : 0;
-        const uint32_t kt = smem_u32(tile(C::K_OFF, j)), vt = smem_u32(tile(C::V_OFF, j));
-        for (int i = i0; i < nt; ++i, ++pair) {
-          const uint32_t qt = smem_u32(tile(C::Q_OFF, i)), dot = smem_u32(tile(C::DO_OFF, i));
-          tc_fence_after();
+  // ---- MMA issue (thread 0)
+  constexpr uint32_t idesc_s = umma_idesc(1u, 0, 0, 128, 128);  // K-major x K-major
+  constexpr uint32_t idesc_t = umma_idesc(1u, 1, 1, 64, 128);   // P^T / dS^T times dO / Q
+  constexpr uint32_t idesc_q = umma_idesc(1u, 0, 1, 64, 128);   // dS times K
+  auto issue_sd = [&](int k) {  // S and dP of pair k
+    const uint32_t qt = smem_u32(tile(C::Q_OFF, pair_i(k))), dot = smem_u32(tile(C::DO_OFF, pair_i(k)));
+    const uint32_t kt = smem_u32(tile(C::K_OFF, pair_j(k))), vt = smem_u32(tile(C::V_OFF, pair_j(k)));
+    tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tS, umma_desc(qt + kk * 32, 16, 1024), umma_desc(kt + kk * 32, 16, 1024), idesc_s,
-                     kk != 0);
+    for (int kk = 0; kk < 4; ++kk)
+      umma_f16(tS, umma_desc(qt + kk * 32, 16, 1024), umma_desc(kt + kk * 32, 16, 1024), idesc_s, kk != 0);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tDP, umma_desc(dot + kk * 32, 16, 1024), umma_desc(vt + kk * 32, 16, 1024),
-                     idesc_s, kk != 0);
-          umma_commit(sd_full);
-          ok = mbar_wait(pds_full, pair & 1, abort, p.err, 232);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t tDQ = tmem + 384u + 64u * (uint32_t)i;
+    for (int kk = 0; kk < 4; ++kk)
+      umma_f16(tDP, umma_desc(dot + kk * 32, 16, 1024), umma_desc(vt + kk * 32, 16, 1024), idesc_s, kk != 0);
+    umma_commit(sd_full);
+  };
+  auto issue_acc = [&](int k) {  // dV, dK, dQ of pair k
+    const int i = pair_i(k), j = pair_j(k);
+    const int i0 = p.causal ? j : 0;
+    const uint32_t pp = smem_u32(smem + C::P_OFF), ds = smem_u32(smem + C::DS_OFF);
+    const uint32_t dsl = smem_u32(smem + C::DSL_OFF);
+    const uint32_t qt = smem_u32(tile(C::Q_OFF, i)), dot = smem_u32(tile(C::DO_OFF, i));
+    const uint32_t kt = smem_u32(tile(C::K_OFF, j));
+    const uint32_t tDQ = tmem + 384u + 64u * (uint32_t)i;
+    // descriptors are built once; a byte offset moves the start address field
+    // (bits 0-13, in 16-byte units)
+    const uint64_t dP = umma_desc(pp, 16384, 1024), dDS = umma_desc(ds, 16384, 1024);
+    const uint64_t dDSL = umma_desc(dsl, 16384, 1024), dDO = umma_desc(dot, 8192, 1024);
+    const uint64_t dQt = umma_desc(qt, 8192, 1024), dKt = umma_desc(kt, 8192, 1024);
+    const uint64_t dDSk = umma_desc(ds, 16, 1024), dDSLk = umma_desc(dsl, 16, 1024);
+    tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            // 16 queries = 16 rows of 128 B in P / dS (MN-major A: the two
-            // 64-key chunks 16 KB apart) and in dO / Q (MN-major B)
-            const uint32_t ka = (uint32_t)(i != i0 || kk != 0);
-            umma_f16(tDV, umma_desc(pp + kk * 2048, 16384, 1024), umma_desc(dot + kk * 2048, 8192, 1024),
-                     idesc_t, ka);
-            umma_f16(tDK, umma_desc(ds + kk * 2048, 16384, 1024), umma_desc(qt + kk * 2048, 8192, 1024),
-                     idesc_t, ka);
-            umma_f16(tDK, umma_desc(dsl + kk * 2048, 16384, 1024), umma_desc(qt + kk * 2048, 8192, 1024),
-                     idesc_t, 1);
-            // 16 keys: 32 bytes of a dS row (K-major A), 16 rows of K (MN-major B)
-            const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_f16(tDQ, umma_desc(ds + aoff, 16, 1024), umma_desc(kt + kk * 2048, 8192, 1024), idesc_q,
-                     (uint32_t)(j != 0 || kk != 0));
-            umma_f16(tDQ, umma_desc(dsl + aoff, 16, 1024), umma_desc(kt + kk * 2048, 8192, 1024), idesc_q, 1);
+    for (int kk = 0; kk < 8; ++kk) {
+      // 16 queries = 16 rows of 128 B in P / dS (MN-major A: the two 64-key
+      // chunks 16 KB apart) and in dO / Q (MN-major B)
+      const uint32_t ka = (uint32_t)(i != i0 || kk != 0);
+      const uint64_t o16 = (uint64_t)(kk * 2048 >> 4);
+      umma_f16(tDV, dP + o16, dDO + o16, idesc_t, ka);
+      umma_f16(tDK, dDS + o16, dQt + o16, idesc_t, ka);
+      umma_f16(tDK, dDSL + o16, dQt + o16, idesc_t, 1);
+      // 16 keys: 32 bytes of a dS row (K-major A), 16 rows of K (MN-major B)
+      const uint64_t a16 = (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+      umma_f16(tDQ, dDSk + a16, dKt + o16, idesc_q, (uint32_t)(j != 0 || kk != 0));
+      umma_f16(tDQ, dDSLk + a16, dKt + o16, idesc_q, 1);
+    }
+    umma_commit(acc_done);
+  };
+  if (issuer) {
+    tma_prefetch_desc(&tQ);
+    tma_prefetch_desc(&tK);
+    tma_prefetch_desc(&tV);
+    tma_prefetch_desc(&tDO);
+    tma_prefetch_desc(&mDQ);
+    tma_prefetch_desc(&mDK);
+    tma_prefetch_desc(&mDV);
+    mbar_expect_tx(ld_full, 4 * nt * C::TILE);
+    for (int i = 0; i < nt; ++i) {
+      tma_load_4d(tile(C::Q_OFF, i), &tQ, ld_full, 0, n, i * 128, b);
+      tma_load_4d(tile(C::DO_OFF, i), &tDO, ld_full, 0, n, i * 128, b);
+      tma_load_4d(tile(C::K_OFF, i), &tK, ld_full, 0, n, i * 128, b);
+      tma_load_4d(tile(C::V_OFF, i), &tV, ld_full, 0, n, i * 128, b);
+    }
+  }
+
+  // ---- D = rowsum(dO * O) per query row (while the tiles load): a compute
+  // warp takes 8 rows per tile, 8 lanes per 128-byte row
+  float* dsm = reinterpret_cast<float*>(smem + C::D_OFF);
+  if (warp < kBwdWarps) {
+    for (int i = 0; i < nt; ++i)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = warp * 8 + h * 4 + (lane >> 3), t = i * 128 + row;
+        float acc = 0.f;
+        if (t < p.T) {
+          const uint4 x = reinterpret_cast<const uint4*>(p.o + (int64_t)b * p.o_sb + (int64_t)t * p.o_st +
+                                                         (int64_t)n * p.o_sn)[lane & 7];
+          const uint4 y = reinterpret_cast<const uint4*>(p.dout + (int64_t)b * p.do_sb + (int64_t)t * p.do_st +
+                                                         (int64_t)n * p.do_sn)[lane & 7];
+          const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[c]));
+            const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ys[c]));
+            acc = fmaf(a.x, g.x, fmaf(a.y, g.y, acc));
           }
-          umma_commit(acc_done);
         }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+        if ((lane & 7) == 0) dsm[i * 128 + row] = acc;
+      }
+  }
+  __syncthreads();
+  const int qq = warp & 3, cg = warp >> 2;
+  const int r = qq * 32 + lane;  // row within a 128-row tile (= TMEM lane)
+  const uint32_t lane_base = (uint32_t)(qq * 32) << 16;
+  const float sl2 = p.scale * 1.4426950408889634f;
+  float lse0 = 0.f, lse1 = 0.f, d0 = 0.f, d1 = 0.f;
+  for (int i = 0; i < nt; ++i) {
+    const int t = i * 128 + r;
+    if (t >= p.T) continue;
+    const float l = p.lse2[((int64_t)b * p.N + n) * p.T + t];
+    if (i == 0) { lse0 = l; d0 = dsm[r]; } else { lse1 = l; d1 = dsm[128 + r]; }
+  }
+  if (warp == kBwdWarps) {
+    if (issuer) {  // ---- MMA issue
+      bool ok = mbar_wait(ld_full, 0, abort, p.err, 231);
+      if (ok) issue_sd(0);
+      for (int k = 0; ok && k < np; ++k) {
+        ok = mbar_wait(s_free, k & 1, abort, p.err, 232);
+        if (!ok) break;
+        if (k + 1 < np) issue_sd(k + 1);  // the S / dP buffers are free again
+        ok = mbar_wait(pds_full, k & 1, abort, p.err, 236);
+        if (ok) issue_acc(k);
       }
     }
-  } else {  // ---- warps 0-7: P, dS and the stores
-    const int qq = warp & 3, h = warp >> 2;
-    const int r = qq * 32 + lane;  // row within a 128-row tile (= TMEM lane)
-    const uint32_t lane_base = (uint32_t)(qq * 32) << 16;
-    const float sl2 = p.scale * 1.4426950408889634f;
-    float lse0 = 0.f, lse1 = 0.f, d0 = 0.f, d1 = 0.f;
-    for (int i = 0; i < nt; ++i) {  // row statistics and D = rowsum(dO * O)
-      const int t = i * 128 + r;
-      if (t >= p.T) continue;
-      const float l = p.lse2[((int64_t)b * p.N + n) * p.T + t];
-      const uint4* o4 = reinterpret_cast<const uint4*>(p.o + (int64_t)b * p.o_sb + (int64_t)t * p.o_st +
-                                                       (int64_t)n * p.o_sn);
-      const uint4* g4 = reinterpret_cast<const uint4*>(p.dout + (int64_t)b * p.do_sb +
-                                                       (int64_t)t * p.do_st + (int64_t)n * p.do_sn);
-      float acc = 0.f;
+  } else {  // ---- warps 0-15
+    // A 128 x 64 f32 accumulator (TMEM columns `tcol`) -> bf16 tile in
+    // shared memory (128-byte rows, 16-byte units XOR row % 8, the TMA
+    // layout): this warp's lane quarter, columns 16 cg .. +15
+    auto stage = [&](uint32_t tcol, uint8_t* dst) {
+      float v[16];
+      tmem_ld16(tcol + lane_base + (uint32_t)(cg * 16), v);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint4 x = o4[u], y = g4[u];
-        const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[c]));
-          const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ys[c]));
-          acc = fmaf(a.x, g.x, fmaf(a.y, g.y, acc));
-        }
+      for (int u = 0; u < 2; ++u)
+        *reinterpret_cast<uint4*>(dst + r * 128 + (((cg * 2 + u) ^ (r & 7)) << 4)) =
+            make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                       pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+    };
+    // dK_j and dV_j once the last pair of key tile j has completed (rows are
+    // keys), staged in the K_j / V_j tiles and written by one TMA store each
+    auto store_kv = [&](int j) {
+      stage(tDV, tile(C::V_OFF, j));
+      stage(tDK, tile(C::K_OFF, j));
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, %0;" ::"n"(kBwdWarps * 32) : "memory");
+      if (tid == 0) {
+        tma_store_4d(&mDV, tile(C::V_OFF, j), 0, n, j * 128, b);
+        tma_store_4d(&mDK, tile(C::K_OFF, j), 0, n, j * 128, b);
+        bulk_commit_group();
       }
-      if (i == 0) { lse0 = l; d0 = acc; } else { lse1 = l; d1 = acc; }
-    }
+    };
+    const int col = cg * 32;  // this warp's key columns within a tile
+    uint8_t* prow = smem + C::P_OFF + (cg >> 1) * C::TILE + r * 128;
+    uint8_t* drow = smem + C::DS_OFF + (cg >> 1) * C::TILE + r * 128;
+    uint8_t* lrow = smem + C::DSL_OFF + (cg >> 1) * C::TILE + r * 128;
     bool ok = true;
-    int pair = 0;
-    float v[32];
-    for (int j = 0; ok && j < nt; ++j) {
-      const int i0 = p.causal ? j : 0;
-      for (int i = i0; i < nt; ++i, ++pair) {
-        bool w = mbar_wait(sd_full, pair & 1, abort, p.err, 233);
-        // P / dS of the previous pair are read by its MMAs until acc_done
-        if (w && pair > 0) w = mbar_wait(acc_done, (pair - 1) & 1, abort, p.err, 234);
+    for (int k = 0; k < np; ++k) {
+      const int i = pair_i(k), j = pair_j(k);
+      bool w = mbar_wait(sd_full, k & 1, abort, p.err, 233);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[32], dr[32];
+      tmem_ld32_async(tS + lane_base + (uint32_t)col, sr);
+      tmem_ld32_async(tDP + lane_base + (uint32_t)col, dr);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);  // the next pair's S / dP may overwrite TMEM now
+      const int t = i * 128 + r;
+      const bool row_ok = t < p.T;
+      const float li = i ? lse1 : lse0, di = i ? d1 : d0;
+      const int kb = j * 128 + col;
+      // keys up to `lim` count: below T, at or before the query when causal,
+      // none for a padding row (one compare per element)
+      const int lim = !row_ok ? -1 : p.causal ? min(t, p.T - 1) : p.T - 1;
+      uint32_t pw[16], dw[16], dl[16];
+#pragma unroll
+      for (int x = 0; x < 16; ++x) {
+        float pv[2], dv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = kb + 2 * x + e;
+          const bool valid = key <= lim;
+          pv[e] = valid ? ex2(fmaf(__uint_as_float(sr[2 * x + e]), sl2, -li)) : 0.f;
+          dv[e] = pv[e] * (__uint_as_float(dr[2 * x + e]) - di) * p.scale;
+        }
+        pw[x] = pack_bf16x2(pv[0], pv[1]);
+        __nv_bfloat162 hh = __floats2bfloat162_rn(dv[0], dv[1]);
+        dw[x] = *reinterpret_cast<uint32_t*>(&hh);
+        const float2 hf = __bfloat1622float2(hh);
+        dl[x] = pack_bf16x2(dv[0] - hf.x, dv[1] - hf.y);
+      }
+      // P / dS of the previous pair are read by its MMAs until acc_done; a key
+      // tile finished by that pair is stored before the next MMAs reuse its
+      // accumulators
+      if (k > 0) {
+        w = mbar_wait(acc_done, (k - 1) & 1, abort, p.err, 234);
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
         tc_fence_after();
-        const int t = i * 128 + r;
-        const bool row_ok = t < p.T;
-        const float li = i ? lse1 : lse0, di = i ? d1 : d0;
+        if (pair_j(k - 1) != j) store_kv(pair_j(k - 1));
+      }
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int col = h * 64 + c * 32;  // column within the key tile
-          float sv[32];
-          tmem_ld32(tS + lane_base + (uint32_t)col, sv);
-          tmem_ld32(tDP + lane_base + (uint32_t)col, v);
-          const int kb = j * 128 + col;
-          uint32_t pw[16], dw[16], dl[16];
-#pragma unroll
-          for (int x = 0; x < 16; ++x) {
-            float pv[2], dv[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int key = kb + 2 * x + e;
-              const bool valid = row_ok && key < p.T && (!p.causal || key <= t);
-              pv[e] = valid ? ex2(fmaf(sv[2 * x + e], sl2, -li)) : 0.f;
-              dv[e] = pv[e] * (v[2 * x + e] - di) * p.scale;
-            }
-            pw[x] = pack_bf16x2(pv[0], pv[1]);
-            __nv_bfloat162 hh = __floats2bfloat162_rn(dv[0], dv[1]);
-            dw[x] = *reinterpret_cast<uint32_t*>(&hh);
-            const float2 hf = __bfloat1622float2(hh);
-            dl[x] = pack_bf16x2(dv[0] - hf.x, dv[1] - hf.y);
-          }
-          uint8_t* prow = smem + C::P_OFF + h * C::TILE + r * 128;
-          uint8_t* drow = smem + C::DS_OFF + h * C::TILE + r * 128;
-          uint8_t* lrow = smem + C::DSL_OFF + h * C::TILE + r * 128;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int off = ((c * 4 + u) ^ (r & 7)) << 4;
-            *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
-            *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
-            *reinterpret_cast<uint4*>(lrow + off) = make_uint4(dl[4 * u], dl[4 * u + 1], dl[4 * u + 2], dl[4 * u + 3]);
-          }
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(pds_full);
-        if (i == nt - 1) {  // key tile j is complete once this pair's MMAs are
-          w = mbar_wait(acc_done, pair & 1, abort, p.err, 235);
-          if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-          tc_fence_after();
-          const int key = j * 128 + r;
-          tmem_ld32(tDV + lane_base + (uint32_t)(h * 32), v);
-          if (key < p.T)
-            store_row32_bf16(p.dv + (int64_t)b * p.dv_sb + (int64_t)key * p.dv_st + (int64_t)n * p.dv_sn + h * 32, v);
-          tmem_ld32(tDK + lane_base + (uint32_t)(h * 32), v);
-          if (key < p.T)
-            store_row32_bf16(p.dk + (int64_t)b * p.dk_sb + (int64_t)key * p.dk_st + (int64_t)n * p.dk_sn + h * 32, v);
-          tc_fence_before();
-        }
+      for (int u = 0; u < 4; ++u) {
+        const int off = (((cg & 1) * 4 + u) ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + off) = make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
+        *reinterpret_cast<uint4*>(drow + off) = make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+        *reinterpret_cast<uint4*>(lrow + off) = make_uint4(dl[4 * u], dl[4 * u + 1], dl[4 * u + 2], dl[4 * u + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_full);
+    }
+    if (ok) {
+      const bool w = mbar_wait(acc_done, (np - 1) & 1, abort, p.err, 235);
+      ok = __all_sync(0xffffffffu, w) != 0;
+    }
+    if (ok) {  // every MMA has completed
+      tc_fence_after();
+      store_kv(pair_j(np - 1));
+      // dQ_i staged in the Q_i tiles (no MMA reads them any more)
+      for (int i = 0; i < nt; ++i) stage(tmem + 384u + 64u * (uint32_t)i, tile(C::Q_OFF, i));
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, %0;" ::"n"(kBwdWarps * 32) : "memory");
+      if (tid == 0) {
+        for (int i = 0; i < nt; ++i) tma_store_4d(&mDQ, tile(C::Q_OFF, i), 0, n, i * 128, b);
+        bulk_commit_group();
       }
     }
-    if (ok) {  // every MMA has completed (the last key tile's wait above)
-      for (int i = 0; i < nt; ++i) {
-        const int t = i * 128 + r;
-        tmem_ld32(tmem + 384u + 64u * (uint32_t)i + lane_base + (uint32_t)(h * 32), v);
-        if (t < p.T)
-          store_row32_bf16(p.dq + (int64_t)b * p.dq_sb + (int64_t)t * p.dq_st + (int64_t)n * p.dq_sn + h * 32, v);
-      }
-    }
+    if (tid == 0) bulk_wait_group_read<0>();  // shared memory stays valid until read
   }
   tc_fence_before();
   __syncthreads();
@@ -1392,7 +1470,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   }
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kBwdWarps) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -1402,11 +1480,11 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
                const float* lse2, void* dq, void* dk, void* dv, int64_t B, int64_t T, int64_t N,
                const int64_t* st, float scale, int causal, cudaStream_t s) {
   // st: (b, t, n) element strides of q, k, v, o, dout, dq, dk, dv
-  CUtensorMap tq, tk, tv, tdo;
-  const void* src[4] = {q, k, v, dout};
-  const int sidx[4] = {0, 1, 2, 4};
-  CUtensorMap* maps[4] = {&tq, &tk, &tv, &tdo};
-  for (int m = 0; m < 4; ++m) {
+  CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
+  const void* src[7] = {q, k, v, dout, dq, dk, dv};
+  const int sidx[7] = {0, 1, 2, 4, 5, 6, 7};
+  CUtensorMap* maps[7] = {&tq, &tk, &tv, &tdo, &tdq, &tdk, &tdv};
+  for (int m = 0; m < 7; ++m) {
     const int64_t* x = st + 3 * sidx[m];
     const uint64_t dims[4] = {64, (uint64_t)N, (uint64_t)T, (uint64_t)B};
     const uint64_t str[3] = {(uint64_t)(x[2] * 2), (uint64_t)(x[1] * 2), (uint64_t)(x[0] * 2)};
@@ -1434,7 +1512,7 @@ int launch_bwd(const void* q, const void* k, const void* v, const void* o, const
   if (!a.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
   if (int rc = allow_dynamic_smem((const void*)sdpa_bwd_tc, BwdCfg::SMEM, "sdpa_bwd_tc")) return rc;
   B200_LAUNCH(sdpa_bwd_tc, dim3((unsigned)(B * N)), dim3(kBwdThreads), BwdCfg::SMEM, s, tq, tk, tv,
-              tdo, a);
+              tdo, tdq, tdk, tdv, a);
   return B200_OK;
 }
 
