@@ -590,9 +590,17 @@ __device__ __forceinline__ void split_rows(const uint8_t* st, uint8_t* hi, uint8
   }
 }
 
-// Thread roles (448 threads): warps 0-7 softmax, warp 8 TMA, warp 9 MMA issue,
-// warps 10-13 f32 split.
-constexpr int kWsThreads = 448;
+// Thread roles: warps 0-7 softmax, warp 8 TMA, warp 9 MMA issue, and for f32
+// inputs warps 10-13 split (448 threads, 512 TMEM columns, one CTA per SM).
+// bf16 inputs run 320 threads in 256 TMEM columns with one O buffer, so that
+// two CTAs share an SM and one's softmax hides the other's waits.
+template <bool X3>
+struct WsShape {
+  static constexpr int THREADS = X3 ? 448 : 320;
+  static constexpr int MIN_CTAS = X3 ? 1 : 2;
+  static constexpr uint32_t TMEM_COLS = X3 ? 512 : 256;
+  static constexpr int NOB = X3 ? 2 : 1;  // O buffers in TMEM
+};
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -601,7 +609,7 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 template <bool X3>
-__global__ void __launch_bounds__(kWsThreads, 1)
+__global__ void __launch_bounds__(WsShape<X3>::THREADS, WsShape<X3>::MIN_CTAS)
     sdpa_fwd_ws(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                 const __grid_constant__ CUtensorMap tV, SdpaArgs p) {
   pdl_wait();
@@ -679,19 +687,21 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     mbar_fence_init();
   }
   if (warp == 0) {
-    tmem_alloc(tslot, 512);
+    tmem_alloc(tslot, WsShape<X3>::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  // TMEM columns (f32 / packed bf16x2, 64 wide each): S buffers at 0 and 64,
-  // O buffers at 128 and 192, P buffers at 256 and 320 (hi in the first 32
-  // columns, lo in the last 32)
+  // TMEM columns (f32 / packed bf16x2): S buffers at 0 and 64; f32 inputs: O
+  // buffers at 128 and 192, P buffers at 256 and 320 (hi in the first 32
+  // columns, lo in the last 32); bf16 inputs: one O buffer at 128, P buffers
+  // (32 packed columns) at 192 and 224
+  constexpr int NOB = WsShape<X3>::NOB;
   auto tS = [&](int s) { return tmem + (uint32_t)(s * 64); };
   auto tO = [&](int s) { return tmem + 128u + (uint32_t)(s * 64); };
-  auto tP = [&](int s) { return tmem + 256u + (uint32_t)(s * 64); };
+  auto tP = [&](int s) { return X3 ? tmem + 256u + (uint32_t)(s * 64) : tmem + 192u + (uint32_t)(s * 32); };
 
   if (warp == 8) {
     if (lane == 0 && nkb > 0) {  // ---- TMA producer
@@ -754,8 +764,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         }
         if (j >= 1) {
           const int jj = j - 1, ks1 = jj % NS, b1 = jj & 1, use1 = jj >> 1;
+          const int ob = jj % NOB, ouse = jj / NOB;  // O buffer of block jj and its use count
           ok = mbar_wait(&p_full[b1], use1 & 1, abort, p.err, 215);
-          if (ok && jj >= 2) ok = mbar_wait(&ob_free[b1], (use1 - 1) & 1, abort, p.err, 216);
+          if (ok && jj >= NOB) ok = mbar_wait(&ob_free[ob], (ouse - 1) & 1, abort, p.err, 216);
           if (!ok) break;
           tc_fence_after();
           const uint32_t vh = smem_u32(v_hi(ks1)), vl = smem_u32(v_lo(ks1));
@@ -763,13 +774,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {
             // P in TMEM: 16 keys = 8 packed columns; V: MN-major, 16 keys = 16 rows of 128 B
             const uint32_t pa = tP(b1) + kk * 8, vb = kk * 2048;
-            umma_f16_ts(tO(b1), pa, umma_desc(vh + vb, 8192, 1024), idesc_o, kk != 0);
+            umma_f16_ts(tO(ob), pa, umma_desc(vh + vb, 8192, 1024), idesc_o, kk != 0);
             if (X3) {
-              umma_f16_ts(tO(b1), pa, umma_desc(vl + vb, 8192, 1024), idesc_o, 1);
-              umma_f16_ts(tO(b1), pa + 32, umma_desc(vh + vb, 8192, 1024), idesc_o, 1);
+              umma_f16_ts(tO(ob), pa, umma_desc(vl + vb, 8192, 1024), idesc_o, 1);
+              umma_f16_ts(tO(ob), pa + 32, umma_desc(vh + vb, 8192, 1024), idesc_o, 1);
             }
           }
-          umma_commit(&o_full[b1]);
+          umma_commit(&o_full[ob]);
           umma_commit(&kv_free[ks1]);
         }
       }
@@ -817,17 +828,17 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     float m_hist0 = -INFINITY, m_hist1 = -INFINITY;
     bool ok = true;
     auto fold = [&](int jj) {  // o = o * 2^(m_acc - m_jj) + (P_jj V_jj)[this half]
-      const int s1 = jj & 1;
-      bool w = mbar_wait(&o_full[s1], (jj >> 1) & 1, abort, p.err, 220);
+      const int s1 = jj & 1, ob = jj % NOB;
+      bool w = mbar_wait(&o_full[ob], (jj / NOB) & 1, abort, p.err, 220);
       if (!__all_sync(0xffffffffu, w)) return false;
       tc_fence_after();
       const float mj = s1 ? m_hist1 : m_hist0;
       const float a = m_acc == -INFINITY ? 0.f : ex2(m_acc - mj);
       float v[32];
-      tmem_ld32(tO(s1) + lane_base + h * 32, v);
+      tmem_ld32(tO(ob) + lane_base + h * 32, v);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ob_free[s1]);
+      if (lane == 0) mbar_arrive(&ob_free[ob]);
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], a, v[i]);
       m_acc = mj;
@@ -941,7 +952,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, WsShape<X3>::TMEM_COLS);
   }
 }
 
@@ -984,7 +995,7 @@ int launch_ws(const void* q, const void* k, const void* v, void* o, int64_t B, i
   if (int rc = allow_dynamic_smem((const void*)sdpa_fwd_ws<X3>, C::SMEM, "sdpa_fwd_ws")) return rc;
   const int64_t ctas = (T + 127) / 128 * N * B;
   if (ctas >= (1ll << 31)) return set_error(B200_ERR_INVALID, "sdpa: too many query tiles");
-  B200_LAUNCH(sdpa_fwd_ws<X3>, dim3((unsigned)ctas), dim3(kWsThreads), C::SMEM, s, tq, tk, tv, a);
+  B200_LAUNCH(sdpa_fwd_ws<X3>, dim3((unsigned)ctas), dim3(WsShape<X3>::THREADS), C::SMEM, s, tq, tk, tv, a);
   return B200_OK;
 }
 
