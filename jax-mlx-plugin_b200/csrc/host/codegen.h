@@ -137,6 +137,9 @@ class CodeGen {
   // use the approximate hardware forms, as bf16-typed nodes do -- the result
   // is rounded to 8 significant bits anyway.
   std::set<int> bf16_sink_;
+  // Inside a row group's loop phase (b = o * RED + r, r < RED): the row count
+  // and length, else 0.
+  int64_t row_loop_out_ = 0, row_loop_red_ = 0;
   // out_slots (optional, parallel to roots): a root stored as a GEMM's bf16
   // hi / lo planes (about 16 significant bits) counts as a bf16 sink too.
   void mark_bf16_sinks(const std::vector<ValueRef>& roots, const std::vector<int>* out_slots = nullptr);

@@ -912,6 +912,9 @@ __global__ void __launch_bounds__(256)
     const int m = (int)(row - b * M);
     const float* src = ws + b * splits * mn_all + (int64_t)m * N + n;
     float4 x = *reinterpret_cast<const float4*>(src);
+    // unrolled: the loads of 8 splits are in flight together, the sums stay
+    // in split order
+#pragma unroll 8
     for (int k = 1; k < splits; ++k) {
       const float4 y = *reinterpret_cast<const float4*>(src + (int64_t)k * mn_all);
       x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
@@ -941,6 +944,7 @@ __global__ void __launch_bounds__(256)
     const int m = (int)(mn / N), n = (int)(mn - (int64_t)m * N);
     const float* src = ws + b * splits * mn_all + mn;
     float x = 0.f;
+#pragma unroll 8
     for (int k = 0; k < splits; ++k) x += src[(int64_t)k * mn_all];
     x *= alpha;
     if (epi == 1 || epi == 2) x += Io<TO>::to_f(reinterpret_cast<const TO*>(bias)[n]);

@@ -509,9 +509,11 @@ def test_logits_cross_entropy_row_groups(client, monkeypatch, rows, cols, dt, ea
 def test_row_softmax_statistics_edge_values(client, cols):
     """One-pass row max + sum of exponentials (warp and block per row) vs the
     interpreter's two passes: rows with -inf entries (masked positions), a row
-    of -inf only (NaN, as exp(-inf - -inf) gives), a row holding +inf (NaN)
-    and a row of huge finite values.  1e-5 relative on finite outputs; NaN at
-    the same places."""
+    of -inf only (NaN, as exp(-inf - -inf) gives), a row holding +inf (NaN),
+    a row of huge finite values, and rows filled with JAX's mask value
+    -0.7 * FLT_MAX (all of it: a uniform softmax; all but three entries; huge
+    negative finite values).  1e-5 relative on finite outputs; NaN at the same
+    places."""
     rows = 2400
     rng = np.random.default_rng(cols)
     x = (rng.standard_normal((rows, cols)) * 4).astype(np.float32)
@@ -519,6 +521,11 @@ def test_row_softmax_statistics_edge_values(client, cols):
     x[5, :] = -np.inf
     x[7, cols // 2] = np.inf
     x[9, :] = np.float32(3e38)
+    fill = np.float32(-0.7 * np.finfo(np.float32).max)
+    x[11, :] = fill
+    x[13, :] = fill
+    x[13, cols - 3:] = rng.standard_normal(3).astype(np.float32)
+    x[15, :] = np.float32(-3e38)
     text = programs.row_softmax(rows, cols)
     got = run(client, text, [x])
     with np.errstate(invalid="ignore", over="ignore"):
