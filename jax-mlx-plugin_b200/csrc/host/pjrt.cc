@@ -1150,7 +1150,9 @@ void execute(PJRT_LoadedExecutable* le, PJRT_LoadedExecutable_Execute_Args* a) {
             vals.reserve(st.args.size());
             for (auto& arg : st.args) vals.push_back(slotp(arg.slot));
             std::vector<void*> args;
-            for (auto& v : vals) args.push_back(&v);
+            if (st.table) args.push_back(vals.data());  // one parameter: the pointer table
+            else
+              for (auto& v : vals) args.push_back(&v);
             launch(dev, mod.fns.at(st.name), st.grid, st.block, st.smem, args);
             break;
           }

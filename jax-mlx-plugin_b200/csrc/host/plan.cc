@@ -1022,6 +1022,137 @@ struct Builder {
     return head;
   }
 
+  // Loop kernels that compile to the same code and whose outputs nothing later
+  // reads or rewrites (an optimizer's per-parameter updates) run as one
+  // launch: the batched kernel takes every member's pointers in one table and
+  // blockIdx.y picks the member.  The launch goes where the last member was;
+  // the other members move later, which is safe when no step in between
+  // writes their inputs.  A member's kernel body is used unchanged (it
+  // indexes with blockIdx.x / gridDim.x only).
+  void batch_leaf_loops() {
+    const size_t n = p.steps.size();
+    std::vector<std::vector<int>> readers(p.slots.size()), writers(p.slots.size());
+    for (size_t i = 0; i < n; ++i) {
+      for (int sl : p.steps[i].in)
+        if (sl >= 0) readers[sl].push_back((int)i);
+      for (int sl : p.steps[i].out)
+        if (sl >= 0) writers[sl].push_back((int)i);
+    }
+    auto later = [](const std::vector<int>& v, int i) {
+      return std::any_of(v.begin(), v.end(), [&](int x) { return x > i; });
+    };
+    std::map<std::string, const GenKernel*> by_name;
+    for (auto& k : kernels) by_name[k.name] = &k;
+    auto body_key = [&](const GenKernel& k) {
+      std::string key = k.code;
+      const size_t at = key.find(" " + k.name + "(");
+      if (at != std::string::npos) key.replace(at + 1, k.name.size(), "@");
+      return key;
+    };
+    std::map<std::string, std::vector<int>> groups;  // code -> steps, in order
+    for (size_t i = 0; i < n; ++i) {
+      const Step& st = p.steps[i];
+      if (st.kind != StepKind::Kernel || st.table || st.grid[1] != 1 || st.block[1] != 1) continue;
+      auto it = by_name.find(st.name);
+      if (it == by_name.end() || st.name.find("_loop") == std::string::npos) continue;
+      bool leaf = true;
+      for (int sl : st.out) leaf = leaf && sl >= 0 && !later(readers[sl], (int)i) && writers[sl].size() == 1;
+      for (int sl : st.in) leaf = leaf && sl >= 0;
+      if (!leaf) continue;
+      groups[body_key(*it->second)].push_back((int)i);
+    }
+    std::set<int> removed;
+    std::map<int, Step> replaced;
+    int made = 0;
+    for (auto& g : groups) {
+      std::vector<int> members = g.second;
+      if (members.size() < 2) continue;
+      const GenKernel& k0 = *by_name.at(p.steps[members[0]].name);
+      const size_t K = k0.ptr_slots.size();
+      // a member may move to the batch only if nothing writes its inputs
+      // between its place and the batch's
+      const int last = members.back();
+      std::vector<int> ok;
+      for (int m : members) {
+        bool safe = true;
+        for (int sl : p.steps[m].in)
+          for (int w : writers[sl]) safe = safe && !(w > m && w <= last);
+        if (safe) ok.push_back(m);
+      }
+      // kernel parameters stay under 4 KB: at most 480 pointers per launch
+      const size_t per = std::max<size_t>(1, 480 / std::max<size_t>(K, 1));
+      for (size_t c0 = 0; c0 < ok.size(); c0 += per) {
+        std::vector<int> chunk(ok.begin() + c0, ok.begin() + std::min(ok.size(), c0 + per));
+        if (chunk.size() < 2) continue;
+        const int at = chunk.back();
+        GenKernel bk;
+        bk.name = k0.name + "_x" + std::to_string(chunk.size()) + "_" + std::to_string(made++);
+        bk.code = batched_code(k0, bk.name, (int)chunk.size());
+        bk.ptr_slots.clear();
+        Step bs = p.steps[at];
+        bs.name = bk.name;
+        bs.table = true;
+        bs.grid[1] = (int64_t)chunk.size();
+        bs.args.clear();
+        bs.in.clear();
+        bs.out.clear();
+        for (int m : chunk) {
+          const Step& ms = p.steps[m];
+          bs.args.insert(bs.args.end(), ms.args.begin(), ms.args.end());
+          bs.in.insert(bs.in.end(), ms.in.begin(), ms.in.end());
+          bs.out.insert(bs.out.end(), ms.out.begin(), ms.out.end());
+          if (m != at) removed.insert(m);
+        }
+        kernels.push_back(std::move(bk));
+        replaced[at] = std::move(bs);
+      }
+    }
+    if (replaced.empty()) return;
+    std::vector<Step> steps;
+    for (size_t i = 0; i < n; ++i) {
+      if (removed.count((int)i)) continue;
+      auto it = replaced.find((int)i);
+      steps.push_back(it != replaced.end() ? std::move(it->second) : std::move(p.steps[i]));
+    }
+    p.steps = std::move(steps);
+  }
+  // The code of kernel `k` as a batched kernel `name` of `count` members: its
+  // pointer parameters come from a table argument (member blockIdx.y).
+  static std::string batched_code(const GenKernel& k, const std::string& name, int count) {
+    const std::string& c = k.code;
+    const size_t np = c.find(" " + k.name + "(");
+    const size_t open = np + 1 + k.name.size();
+    const size_t close = c.find(") {", open);
+    if (np == std::string::npos || close == std::string::npos)
+      throw PjrtErr(13, "batched kernel: unexpected generated signature");
+    const std::string params = c.substr(open + 1, close - open - 1);
+    const std::string head = c.substr(0, np + 1);  // extern "C" __global__ ... void
+    std::vector<std::string> decl;
+    size_t pos = 0;
+    while (pos < params.size()) {
+      size_t e = params.find(", ", pos);
+      if (e == std::string::npos) e = params.size();
+      decl.push_back(params.substr(pos, e - pos));
+      pos = e + 2;
+    }
+    const size_t K = decl.size();
+    std::ostringstream o;
+    o << "struct " << name << "_tab { void* p[" << K * count << "]; };\n";
+    o << head << name << "(const __grid_constant__ " << name << "_tab t) {\n";
+    o << "  const int member = blockIdx.y;\n";
+    for (size_t i = 0; i < K; ++i) {
+      // "<type> pN": the type without its __restrict__, for the cast
+      const std::string& d = decl[i];
+      const size_t sp = d.rfind(' ');
+      std::string type = d.substr(0, sp), var = d.substr(sp + 1), bare = type;
+      const size_t r = bare.find(" __restrict__");
+      if (r != std::string::npos) bare.erase(r, 13);
+      o << "  " << type << " " << var << " = (" << bare << ")t.p[member * " << K << " + " << i << "];\n";
+    }
+    o << c.substr(close + 3);  // the body after "{"
+    return o.str();
+  }
+
   void run() {
     auto order = group_all_reduces(topo());
     // parameters
@@ -1180,6 +1311,7 @@ struct Builder {
         p.output_slots.push_back(o);
       }
     }
+    batch_leaf_loops();
     // temp lifetimes
     p.temp_first.assign(p.slots.size(), -1);
     p.temp_last.assign(p.slots.size(), -1);

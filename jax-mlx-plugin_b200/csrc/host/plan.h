@@ -51,6 +51,10 @@ struct Step {
   std::vector<int64_t> ip;   // integer parameters
   std::vector<float> fp;     // float parameters
   int dtype = 0, dtype2 = 0;
+  // Kernel: the pointer arguments go to the kernel as one table (an array of
+  // pointers passed by value), as a batched launch of several steps' work
+  // takes them (blockIdx.y selects a member's set).
+  bool table = false;
 };
 
 struct Plan {

@@ -114,6 +114,21 @@ def test_row_wise_kernels_share_one_pass():
     assert steps.count("_rows in=") >= 6 * 3 + 2
 
 
+def test_leaf_loops_with_one_body_run_as_one_launch():
+    """The optimizer's per-parameter updates compile to a few distinct kernel
+    bodies (one per parameter shape); the ones with the same body run as one
+    launch whose pointer table holds every member's buffers."""
+    steps = pjrt.inspect(programs.transformer_step(), 1).split("steps:")[1].strip().splitlines()
+    batched = [l for l in steps if re.match(r"k\d+_loop_x\d+_\d+ ", l.strip())]
+    sizes = sorted(int(re.search(r"_x(\d+)_", l).group(1)) for l in batched)
+    # five distinct update bodies (by parameter shape) repeat across the
+    # blocks; the embeddings and the head have shapes of their own
+    assert sizes == [6, 12, 24, 26, 30], sizes
+    assert len(steps) < 340
+    kernels = pjrt.inspect(programs.transformer_step(), 2)
+    assert kernels.count("const __grid_constant__") >= len(batched)
+
+
 def _step_names(text):
     steps = pjrt.inspect(text, 1).split("steps:")[1]
     return [l.split()[0] for l in steps.strip().splitlines()]
