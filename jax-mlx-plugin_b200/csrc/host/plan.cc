@@ -1022,14 +1022,21 @@ struct Builder {
     return head;
   }
 
-  // Loop kernels that compile to the same code and whose outputs nothing later
-  // reads or rewrites (an optimizer's per-parameter updates) run as one
-  // launch: the batched kernel takes every member's pointers in one table and
-  // blockIdx.y picks the member.  The launch goes where the last member was;
-  // the other members move later, which is safe when no step in between
-  // writes their inputs.  A member's kernel body is used unchanged (it
-  // indexes with blockIdx.x / gridDim.x only).
-  void batch_leaf_loops() {
+  // Generated loop and reduction kernels that compile to the same code run as
+  // one launch when they can meet at one place: the batched kernel takes every
+  // member's pointers in one table and blockIdx.z picks the member (the
+  // bodies index with blockIdx.x / .y only).  The launch goes where the last
+  // member was; an earlier member may move there when no step in between
+  // reads its outputs or writes its inputs or outputs.  Repeated until
+  // nothing moves: an optimizer's per-parameter updates batch first (nothing
+  // reads them), then the gradient reductions they read (bias and norm-gain
+  // column sums, and their partial-sum combines), which now have no reader
+  // before the batch.
+  void batch_steps() {
+    for (int pass = 0; pass < 4; ++pass)
+      if (!batch_pass()) break;
+  }
+  bool batch_pass() {
     const size_t n = p.steps.size();
     std::vector<std::vector<int>> readers(p.slots.size()), writers(p.slots.size());
     for (size_t i = 0; i < n; ++i) {
@@ -1038,8 +1045,8 @@ struct Builder {
       for (int sl : p.steps[i].out)
         if (sl >= 0) writers[sl].push_back((int)i);
     }
-    auto later = [](const std::vector<int>& v, int i) {
-      return std::any_of(v.begin(), v.end(), [&](int x) { return x > i; });
+    auto between = [](const std::vector<int>& v, int lo, int hi) {
+      return std::any_of(v.begin(), v.end(), [&](int x) { return x > lo && x <= hi; });
     };
     std::map<std::string, const GenKernel*> by_name;
     for (auto& k : kernels) by_name[k.name] = &k;
@@ -1049,50 +1056,50 @@ struct Builder {
       if (at != std::string::npos) key.replace(at + 1, k.name.size(), "@");
       return key;
     };
+    auto kind_ok = [](const std::string& name) {
+      return name.find("_loop") != std::string::npos || name.find("_reduce") != std::string::npos;
+    };
     std::map<std::string, std::vector<int>> groups;  // code -> steps, in order
     for (size_t i = 0; i < n; ++i) {
       const Step& st = p.steps[i];
-      if (st.kind != StepKind::Kernel || st.table || st.grid[1] != 1 || st.block[1] != 1) continue;
+      if (st.kind != StepKind::Kernel || st.table || st.grid[2] != 1 || !kind_ok(st.name)) continue;
       auto it = by_name.find(st.name);
-      if (it == by_name.end() || st.name.find("_loop") == std::string::npos) continue;
-      bool leaf = true;
-      for (int sl : st.out) leaf = leaf && sl >= 0 && !later(readers[sl], (int)i) && writers[sl].size() == 1;
-      for (int sl : st.in) leaf = leaf && sl >= 0;
-      if (!leaf) continue;
-      groups[body_key(*it->second)].push_back((int)i);
+      if (it == by_name.end()) continue;
+      bool ok = true;
+      for (int sl : st.out) ok = ok && sl >= 0 && writers[sl].size() == 1;
+      for (int sl : st.in) ok = ok && sl >= 0;
+      if (ok) groups[body_key(*it->second)].push_back((int)i);
     }
     std::set<int> removed;
-    std::map<int, Step> replaced;
-    int made = 0;
+    std::map<int, std::vector<Step>> placed;  // batches, at their last member
     for (auto& g : groups) {
-      std::vector<int> members = g.second;
+      const std::vector<int>& members = g.second;
       if (members.size() < 2) continue;
       const GenKernel& k0 = *by_name.at(p.steps[members[0]].name);
       const size_t K = k0.ptr_slots.size();
-      // a member may move to the batch only if nothing writes its inputs
-      // between its place and the batch's
       const int last = members.back();
       std::vector<int> ok;
       for (int m : members) {
         bool safe = true;
-        for (int sl : p.steps[m].in)
-          for (int w : writers[sl]) safe = safe && !(w > m && w <= last);
+        const Step& ms = p.steps[m];
+        for (int sl : ms.out) safe = safe && !between(readers[sl], m, last);
+        for (int sl : ms.in) safe = safe && !between(writers[sl], m, last);
         if (safe) ok.push_back(m);
       }
-      // kernel parameters stay under 4 KB: at most 480 pointers per launch
+      if (ok.size() < 2 || ok.back() != last) continue;
+      // kernel parameters stay under 4 KB: at most 480 pointers per launch;
+      // every chunk is placed at the last member (all members can move there)
       const size_t per = std::max<size_t>(1, 480 / std::max<size_t>(K, 1));
       for (size_t c0 = 0; c0 < ok.size(); c0 += per) {
         std::vector<int> chunk(ok.begin() + c0, ok.begin() + std::min(ok.size(), c0 + per));
         if (chunk.size() < 2) continue;
-        const int at = chunk.back();
         GenKernel bk;
-        bk.name = k0.name + "_x" + std::to_string(chunk.size()) + "_" + std::to_string(made++);
+        bk.name = k0.name + "_x" + std::to_string(chunk.size()) + "_" + std::to_string(batched_++);
         bk.code = batched_code(k0, bk.name, (int)chunk.size());
-        bk.ptr_slots.clear();
-        Step bs = p.steps[at];
+        Step bs = p.steps[chunk.back()];
         bs.name = bk.name;
         bs.table = true;
-        bs.grid[1] = (int64_t)chunk.size();
+        bs.grid[2] = (int64_t)chunk.size();
         bs.args.clear();
         bs.in.clear();
         bs.out.clear();
@@ -1101,23 +1108,30 @@ struct Builder {
           bs.args.insert(bs.args.end(), ms.args.begin(), ms.args.end());
           bs.in.insert(bs.in.end(), ms.in.begin(), ms.in.end());
           bs.out.insert(bs.out.end(), ms.out.begin(), ms.out.end());
-          if (m != at) removed.insert(m);
+          removed.insert(m);
         }
         kernels.push_back(std::move(bk));
-        replaced[at] = std::move(bs);
+        placed[last].push_back(std::move(bs));
       }
     }
-    if (replaced.empty()) return;
+    if (placed.empty()) return false;
     std::vector<Step> steps;
     for (size_t i = 0; i < n; ++i) {
+      auto it = placed.find((int)i);
+      if (it != placed.end()) {
+        for (auto& b : it->second) steps.push_back(std::move(b));
+        if (!removed.count((int)i)) steps.push_back(std::move(p.steps[i]));
+        continue;
+      }
       if (removed.count((int)i)) continue;
-      auto it = replaced.find((int)i);
-      steps.push_back(it != replaced.end() ? std::move(it->second) : std::move(p.steps[i]));
+      steps.push_back(std::move(p.steps[i]));
     }
     p.steps = std::move(steps);
+    return true;
   }
+  int batched_ = 0;
   // The code of kernel `k` as a batched kernel `name` of `count` members: its
-  // pointer parameters come from a table argument (member blockIdx.y).
+  // pointer parameters come from a table argument (member blockIdx.z).
   static std::string batched_code(const GenKernel& k, const std::string& name, int count) {
     const std::string& c = k.code;
     const size_t np = c.find(" " + k.name + "(");
@@ -1139,7 +1153,7 @@ struct Builder {
     std::ostringstream o;
     o << "struct " << name << "_tab { void* p[" << K * count << "]; };\n";
     o << head << name << "(const __grid_constant__ " << name << "_tab t) {\n";
-    o << "  const int member = blockIdx.y;\n";
+    o << "  const int member = blockIdx.z;\n";
     for (size_t i = 0; i < K; ++i) {
       // "<type> pN": the type without its __restrict__, for the cast
       const std::string& d = decl[i];
@@ -1311,7 +1325,7 @@ struct Builder {
         p.output_slots.push_back(o);
       }
     }
-    batch_leaf_loops();
+    batch_steps();
     // temp lifetimes
     p.temp_first.assign(p.slots.size(), -1);
     p.temp_last.assign(p.slots.size(), -1);
@@ -1330,10 +1344,15 @@ struct Builder {
       if (p.temp_first[par] < 0 || p.temp_first[s] < p.temp_first[par]) p.temp_first[par] = p.temp_first[s];
       p.temp_last[par] = std::max(p.temp_last[par], p.temp_last[s]);
     }
-    // distinct kernel bodies, spread over units of similar code size
+    // distinct kernel bodies, spread over units of similar code size (kernels
+    // no step launches -- members of a batched launch -- are left out)
+    std::set<std::string> launched;
+    for (auto& st : p.steps)
+      if (st.kind == StepKind::Kernel) launched.insert(st.name);
     std::map<std::string, std::string> seen;  // code with the name blanked -> kernel
     std::vector<const GenKernel*> uniq;
     for (auto& k : kernels) {
+      if (!launched.count(k.name)) continue;
       std::string key = k.code;
       const size_t at = key.find(" " + k.name + "(");
       if (at != std::string::npos) key.replace(at + 1, k.name.size(), "@");

@@ -53,7 +53,7 @@ struct Step {
   int dtype = 0, dtype2 = 0;
   // Kernel: the pointer arguments go to the kernel as one table (an array of
   // pointers passed by value), as a batched launch of several steps' work
-  // takes them (blockIdx.y selects a member's set).
+  // takes them (blockIdx.z selects a member's set).
   bool table = false;
 };
 
