@@ -616,6 +616,246 @@ __global__ void __launch_bounds__(kPersThreads, 1)
   }
 }
 
+// Two-SM persistent bf16 GEMM: a cluster of two CTAs (a pair, on the two SMs
+// of one TPC) computes 256 x 256 output tiles with tcgen05.mma.cta_group::2.
+// Each CTA loads its own 128 rows of A and 128 of B's 256 columns per k-block
+// (32 KB instead of the one-SM tile's 48 KB for 128 x 256 outputs), so a tile
+// needs a third fewer operand bytes per SM, and the six-stage ring holds
+// 192 KB in flight.  Roles as in gemm_tc_pers: warp 0 of each CTA streams its
+// halves (both CTAs' loads complete on the rank-0 CTA's stage barrier, which
+// rank 0 arms with the pair's byte count); warp 1 of rank 0 issues the MMAs
+// (M = 256, N = 256, K = 16) into one of two TMEM accumulators and commits
+// stage and accumulator barriers to both CTAs; warps 2-9 of each CTA drain
+// their CTA's 128 accumulator rows and report on rank 0's barrier.  All
+// waits are bounded.
+struct PairCfg {
+  static constexpr int A_BYTES = 128 * 128;  // this CTA's 128 rows x 64 bf16
+  static constexpr int B_BYTES = 128 * 128;  // 128 of the tile's 256 columns x 64 bf16
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int EPI_BYTES = 8 * 4096;
+  static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
+  static_assert(SMEM <= 232448, "shared memory above the 227 KB per-block limit");
+};
+
+template <typename TO>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
+    gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
+                 const __grid_constant__ CUtensorMap tC, PersArgs p) {
+  pdl_wait();
+  using Cfg = PairCfg;
+  constexpr int S = Cfg::STAGES;
+  constexpr int BN = 256;  // the pair tile's columns (each CTA loads half of B)
+  constexpr int BK = 64;
+  constexpr int E = 64;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* epi_smem = smem + S * Cfg::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;   // [2] accumulator ready (both CTAs)
+  uint64_t* tempty = tfull + 2;  // [2] accumulator drained (rank 0: both CTAs' warps)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 1);
+  auto sA = [&](int s) { return smem + s * Cfg::STAGE; };
+  auto sB = [&](int s) { return smem + s * Cfg::STAGE + Cfg::A_BYTES; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = (int)cluster_rank();
+  const int pair = (int)blockIdx.x >> 1, npairs = (int)gridDim.x >> 1;
+  const int tiles_mn = p.tiles_m * p.tiles_n;
+  const int num_tiles = tiles_mn * p.batch;
+  auto decode = [&](int t, int& m0, int& n0, int& bz) {
+    const int bs = t / tiles_mn, r = t - bs * tiles_mn;
+    int mi, ni;
+    if (p.group > 1) {
+      const int gsz = p.group * p.tiles_n;
+      const int g = r / gsz, gm0 = g * p.group;
+      const int gm = min(p.group, p.tiles_m - gm0);
+      const int in = r - g * gsz;
+      mi = gm0 + in % gm;
+      ni = in / gm;
+    } else if (p.n_fast) {
+      ni = r % p.tiles_n;
+      mi = r / p.tiles_n;
+    } else {
+      mi = r % p.tiles_m;
+      ni = r / p.tiles_m;
+    }
+    m0 = mi * 256;
+    n0 = ni * BN;
+    bz = bs;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kPersEpiWarps);
+    }
+    *abort = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tA);
+    tma_prefetch_desc(&tB);
+    tma_prefetch_desc(&tC);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(tslot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const int kb_all = p.kb_all;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer (both CTAs)
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < num_tiles; t += npairs) {
+        int m0, n0, bz;
+        decode(t, m0, n0, bz);
+        const int mr = m0 + rank * 128, nr = n0 + rank * 128;  // this CTA's rows / columns
+        for (int kb = 0; kb < kb_all; ++kb, ++it) {
+          const int s = it % S;
+          if (it >= S && !mbar_wait(&empty[s], ((it / S) + 1) & 1, abort, p.err, 121)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = pair_leader_addr(smem_u32(&full[s]));
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * Cfg::STAGE);
+          if (!p.a_mn) {
+            tma_load_3d_pair(sA(s), &tA, bar, kb * BK, mr, bz);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 128 / E; ++j) tma_load_3d_pair(sA(s) + j * (BK * 128), &tA, bar, mr + j * E, kb * BK, bz);
+          }
+          if (!p.b_mn) {
+            tma_load_3d_pair(sB(s), &tB, bar, kb * BK, nr, bz);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 128 / E; ++j) tma_load_3d_pair(sB(s) + j * (BK * 128), &tB, bar, nr + j * E, kb * BK, bz);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {  // ---- MMA issuer (the pair's rank 0)
+      const uint32_t idesc = umma_idesc(1u, (uint32_t)p.a_mn, (uint32_t)p.b_mn, BN, 256);
+      constexpr uint32_t KSTEP_MN = 16 * 128;
+      auto desc = [&](uint32_t base, int kk, int mn) {
+        return mn ? umma_desc(base + kk * KSTEP_MN, BK * 128, 1024) : umma_desc(base + kk * 32, 16, 1024);
+      };
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < num_tiles; t += npairs, ++tl) {
+        const int acc = tl & 1;
+        if (tl >= 2 && !mbar_wait(&tempty[acc], ((tl >> 1) + 1) & 1, abort, p.err, 122)) break;
+        tc_fence_after();
+        const uint32_t dt = tmem + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kb_all; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort, p.err, 123)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_pair(dt, desc(a0, kk, p.a_mn), desc(b0, kk, p.b_mn), idesc, (kb | kk) != 0);
+          umma_commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc]);
+      }
+    }
+  } else {  // ---- warps 2..9 of both CTAs: epilogue of this CTA's 128 rows
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stg = epi_smem + (warp - 2) * 4096;
+    constexpr int CW = 128 / (int)sizeof(TO);  // output columns per 128-byte chunk
+    constexpr int NCH = BN / CW;
+    int tl = 0, nstore = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++tl) {
+      int m0, n0, bz;
+      decode(t, m0, n0, bz);
+      const int acc = tl & 1;
+      bool ok = mbar_wait(&tfull[acc], (tl >> 1) & 1, abort, p.err, 124);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const int rowbase = m0 + rank * 128 + q * 32;
+#pragma unroll 1
+      for (int c = half * (NCH / 2); c < (half + 1) * (NCH / 2); ++c) {
+        const int nc = n0 + c * CW;
+        if (nc >= p.N || rowbase >= p.M) continue;
+        float v[CW];
+        tmem_ld32(trow + (uint32_t)(c * CW), v);
+        if (CW == 64) tmem_ld32(trow + (uint32_t)(c * CW + 32), v + 32);
+#pragma unroll
+        for (int j = 0; j < CW; ++j) {
+          float x = v[j] * p.alpha;
+          if (p.epi == 1 || p.epi == 2) {
+            const int n = nc + j;
+            x += n < p.N ? load_bias<TO>(p.bias, n) : 0.f;
+          }
+          if (p.epi >= 2) x = fmaxf(x, 0.f);
+          v[j] = x;
+        }
+        uint8_t* buf = stg;  // its previous store must have read it
+        if (lane == 0 && nstore >= 1) bulk_wait_group_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          uint4 w;
+          if (sizeof(TO) == 4) {
+            w = make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                           __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
+          } else {
+            auto pk = [&](int j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(v[j], v[j + 1]);
+              return *reinterpret_cast<uint32_t*>(&h);
+            };
+            w = make_uint4(pk(8 * u), pk(8 * u + 2), pk(8 * u + 4), pk(8 * u + 6));
+          }
+          *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) = w;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tC, buf, nc, rowbase, bz);
+          bulk_commit_group();
+        }
+        ++nstore;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(pair_leader_addr(smem_u32(&tempty[acc])));
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort && threadIdx.x == 0) {
+    // let copies and MMAs already in flight land before shared memory / TMEM go away
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < 2000000ull) {
+    }
+  }
+  cluster_sync_all();  // neither CTA leaves while the other may still signal it
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 2 * BN);
+  }
+}
+
 // SIMT fallback: 64x64 tile, 256 threads, 4x4 outputs per thread, f32 FMA.
 template <typename TI, typename TO>
 __global__ void __launch_bounds__(256)
@@ -1219,6 +1459,108 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   return B200_OK;
 }
 
+// The two-SM GEMM for bf16 operands: 256 x 256 tiles, no split-K (shapes
+// with too few tiles to fill the GPU stay on the one-SM kernel, which can
+// split K).  B200_GEMM_PAIR=0 turns it off.
+bool use_pair() {
+  static bool on = [] {
+    const char* v = std::getenv("B200_GEMM_PAIR");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
+template <typename TO>
+int launch_pair(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
+                int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb, int64_t sBk,
+                int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn, cudaStream_t st,
+                Scratch& scratch) {
+  constexpr int ES = 2, BK = 64, E = 64;
+  const int64_t tiles_m = (M + 255) / 256, tiles_n = (N + 255) / 256;
+  const int64_t num_tiles = tiles_m * tiles_n * batch;
+  if (M < 256 || N < 256 || num_tiles < num_sms() / 2 || num_tiles >= (1ll << 30)) return B200_ERR_UNSUPPORTED;
+  const int so = (int)sizeof(TO);
+  if (((uintptr_t)c & 15) != 0 || (ldc * so) % 16 != 0 || (batch > 1 && ((M * ldc * so) % 16) != 0))
+    return B200_ERR_UNSUPPORTED;
+  if (scratch.query) return kWorkspaceQueried;
+  auto bstride = [&](int64_t s, int64_t outer_stride, int64_t outer_dim) -> uint64_t {
+    const int64_t v = batch == 1 ? outer_stride * outer_dim : s;
+    return (uint64_t)(((v * ES) + 15) / 16 * 16);
+  };
+  CUtensorMap ta, tb, tc;
+  int rc;
+  if (!a_mn) {
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sAm * ES), bstride(sAb, sAm, M)};
+    uint32_t box[3] = {(uint32_t)BK, 128, 1};
+    rc = make_tmap(&ta, a, 3, dims, str, box, ES);
+  } else {
+    uint64_t dims[3] = {(uint64_t)M, (uint64_t)K, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sAk * ES), bstride(sAb, sAk, K)};
+    uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
+    rc = make_tmap(&ta, a, 3, dims, str, box, ES);
+  }
+  if (rc) return rc;
+  if (!b_mn) {  // each CTA loads 128 of the tile's 256 columns
+    uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sBn * ES), bstride(sBb, sBn, N)};
+    uint32_t box[3] = {(uint32_t)BK, 128, 1};
+    rc = make_tmap(&tb, b, 3, dims, str, box, ES);
+  } else {
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(sBk * ES), bstride(sBb, sBk, K)};
+    uint32_t box[3] = {(uint32_t)E, (uint32_t)BK, 1};
+    rc = make_tmap(&tb, b, 3, dims, str, box, ES);
+  }
+  if (rc) return rc;
+  {
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)batch};
+    uint64_t str[2] = {(uint64_t)(ldc * so), (uint64_t)(((M * ldc * so) + 15) / 16 * 16)};
+    uint32_t box[3] = {(uint32_t)(128 / so), 32, 1};
+    rc = make_tmap(&tc, c, 3, dims, str, box, so);
+  }
+  if (rc) return rc;
+  PersArgs p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.alpha = alpha;
+  p.bias = bias;
+  p.epi = epi;
+  p.tiles_m = (int)tiles_m;
+  p.tiles_n = (int)tiles_n;
+  p.batch = (int)batch;
+  p.splits = 1;
+  p.kb_all = (int)((K + BK - 1) / BK);
+  p.kb_per_split = p.kb_all;
+  p.n_fast = tiles_n <= tiles_m ? 1 : 0;
+  p.group = (tiles_m >= 16 && tiles_n >= 16) ? 8 : 1;
+  p.out_ws = 0;
+  p.err = scratch.err ? scratch.err : device_error_word();
+  if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
+  const int smem = PairCfg::SMEM;
+  if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pair<TO>, smem, "gemm_tc_pair")) return rc2;
+  // Clusters live inside one GPC, so fewer than num_sms / 2 pairs may fit at
+  // once; a persistent grid larger than that would run a second wave.
+  static int max_pairs = [&] {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(num_sms() & ~1);
+    cfg.blockDim = dim3(kPersThreads);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_tc_pair<TO>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    return n;
+  }();
+  const unsigned grid = (unsigned)(2 * std::min<int64_t>(num_tiles, max_pairs));
+  B200_LAUNCH(gemm_tc_pair<TO>, dim3(grid), dim3(kPersThreads), smem, st, ta, tb, tc, p);
+  return B200_OK;
+}
+
 bool use_persistent() {
   static bool on = [] {
     const char* v = std::getenv("B200_GEMM_PERSISTENT");
@@ -1392,6 +1734,13 @@ int gemm_dispatch(const void* a, const void* b, void* c, const void* bias, int64
 #define B200_PERS(BN_, TO_)                                                                       \
   prc = launch_pers<BN_, TO_>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,  \
                               alpha, epilogue, a_mn, b_mn, st, scratch)
+        prc = B200_ERR_UNSUPPORTED;
+        if (N > 128 && use_pair())
+          prc = obf ? launch_pair<__nv_bfloat16>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk,
+                                                 sBn, ldc, alpha, epilogue, a_mn, b_mn, st, scratch)
+                    : launch_pair<float>(a, b, c, bias, batch, M, N, K, sAb, sAm, sAk, sBb, sBk, sBn, ldc,
+                                         alpha, epilogue, a_mn, b_mn, st, scratch);
+        if (prc != B200_ERR_UNSUPPORTED) return prc;
         if (N <= 64) { if (obf) B200_PERS(64, __nv_bfloat16); else B200_PERS(64, float); }
         else if (N <= 128) { if (obf) B200_PERS(128, __nv_bfloat16); else B200_PERS(128, float); }
         else { if (obf) B200_PERS(256, __nv_bfloat16); else B200_PERS(256, float); }

@@ -280,6 +280,42 @@ def test_gemm_layouts(a_t, b_t, dt):
     assert_close(got, ref, 2e-3 if dt == kernels.DT_F32 else 1e-2, f"gemm a_t={a_t} b_t={b_t}")
 
 
+def _kernel_names(fn):
+    """Names of the CUDA kernels `fn` launches (CUPTI sees every kernel of the
+    process, ones launched from this package's libraries included)."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+@pytest.mark.parametrize("out_dt", [kernels.DT_BF16, kernels.DT_F32])
+@pytest.mark.parametrize("M,N,K,a_t,b_t,batch,epi", [(2520, 2376, 200, False, False, 1, 0),
+                                                     (2520, 2376, 200, False, True, 1, 1),
+                                                     (2520, 2376, 200, True, False, 1, 2),
+                                                     (2520, 2376, 200, True, True, 1, 0),
+                                                     (1000, 744, 128, False, True, 8, 1),
+                                                     (4200, 4160, 72, False, True, 1, 0)])
+def test_gemm_two_sm_pairs(M, N, K, a_t, b_t, batch, epi, out_dt):
+    """bf16 GEMMs with at least 74 tiles of 256 x 256 run on the two-SM kernel
+    (one 256-row MMA per SM pair, cta_group::2): ragged M, N and K, every
+    operand layout, a batch, the bias and bias+relu epilogues and the grouped
+    tile order (17 x 17 tiles).  vs f64 on the bf16 values, 1e-2 relative."""
+    res = {}
+
+    def run():
+        res["v"] = _gemm_case(M, N, K, a_t, b_t, kernels.DT_BF16, batch=batch, epi=epi,
+                              seed=M + N + K + 2 * a_t + b_t, out_dt=out_dt)
+
+    names = _kernel_names(run)
+    got, ref, tc = res["v"]
+    assert tc
+    if names:
+        assert any("gemm_tc_pair" in n for n in names), sorted(names)
+    assert_close(got, ref, 1e-2, f"pair gemm {batch}x{M}x{N}x{K} a_t={a_t} b_t={b_t} epi={epi}")
+
+
 # in_dtype codes for one f32 and one bf16 operand (csrc/kernels/gemm_ws.h)
 GEMM_DT_A_F32_B_BF16, GEMM_DT_A_BF16_B_F32 = 100, 101
 
