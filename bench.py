@@ -228,8 +228,10 @@ class Rig:
         return ts
 
     def _timed(self, fn, steps: int, flush: bool):
+        from jax_b200.pjrt import kernel_launches
         torch = self.torch
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        n0 = kernel_launches()
         for i in range(steps):
             if flush:
                 # evict L2 by reading 2 GB (a read leaves clean lines: no write-back
@@ -241,6 +243,8 @@ class Rig:
             ev[i][0].record(self.stream)
             fn()
             ev[i][1].record(self.stream)
+        # this package's kernels launched by the timed steps (library counters)
+        self.timed_launches = kernel_launches() - n0
         torch.cuda.synchronize()
         return [a.elapsed_time(b) * 1e-3 for a, b in ev]  # seconds
 
@@ -262,13 +266,6 @@ class Rig:
             bs.append(b)
             evs.append(ev)
         return bs, evs
-
-
-def plan_launches(text: str) -> int:
-    from jax_b200 import pjrt
-    plan = pjrt.inspect(text, 1)
-    steps = plan.split("steps:")[1].strip().splitlines()
-    return sum(1 for s in steps if not s.strip().startswith(("copy", "all_reduce")))
 
 
 def _await_all(evs):
@@ -297,13 +294,13 @@ def bench_ln(rig: Rig, steps, warmup):
     text = programs.layer_norm()
     exe = rig.client.compile(text)
     args = rig.bufs(ln_inputs())
-    launches = plan_launches(text)
     holder = []
 
     def step():
         holder[:] = exe.execute([args])
     with ClockSampler(rig.local_rank) as clk:
         ts = rig.time_steps(step, steps, warmup)
+    launches = rig.timed_launches / steps
     t = _device_mean(exe, steps, ts)
     # end to end: pinned host inputs -> device -> execute -> host, per step
     host_in = rig.host_inputs(ln_inputs())
@@ -377,6 +374,7 @@ def bench_sdpa(rig: Rig, steps, warmup):
     holder = []
     with ClockSampler(rig.local_rank) as clk:
         ts = rig.time_steps(lambda: holder.__setitem__(slice(None), exe.execute([args])), steps, warmup)
+    launches = rig.timed_launches / steps
     t = _device_mean(exe, steps, ts)
     host_in = rig.host_inputs(arrays)
     out_np = rig.torch.empty(SDPA_SHAPE, dtype=rig.torch.float32).pin_memory().numpy()
@@ -390,7 +388,7 @@ def bench_sdpa(rig: Rig, steps, warmup):
     exe.device_times_ms()
     return {"value": SDPA_FLOPS / t / 1e12, "t": t, "e2e_t": e2e_t,
             "h2d": 3 * int(np.prod(SDPA_SHAPE)) * 4, "d2h": int(np.prod(SDPA_SHAPE)) * 4,
-            "launches_per_step": plan_launches(text), "clocks": clk.summary(),
+            "launches_per_step": launches, "clocks": clk.summary(),
             "tensor_path": "tcgen05 kind::f16 (f32 inputs as bf16 hi+lo, 3 products)"}
 
 
@@ -419,7 +417,8 @@ def bench_gemm(rig: Rig, steps, warmup, shape, dtype="bf16", trans=""):
         ts = rig.time_steps(step, steps, warmup)
     t = float(np.mean(ts))
     fl = 2.0 * M * N * K
-    return {"value": fl / t / 1e12, "t": t, "launches_per_step": 1, "clocks": clk.summary(),
+    return {"value": fl / t / 1e12, "t": t, "launches_per_step": rig.timed_launches / steps,
+            "clocks": clk.summary(),
             "flops_per_step": fl}
 
 
@@ -585,9 +584,10 @@ def bench_train(rig: Rig, kind, steps, warmup, world=1, rank=0, with_e2e=True):
         args[:n_state] = outs[1:1 + n_state]
     with ClockSampler(rig.local_rank) as clk:
         ts = rig.time_steps(step, steps, warmup, flush=False)
+    launches = rig.timed_launches / steps
     exe.device_times_ms()
     t = float(np.mean(ts))  # back-to-back steps: host launch overhead is part of a training step
-    res = {"value": gb / t, "t": t, "launches_per_step": plan_launches(text), "clocks": clk.summary(),
+    res = {"value": gb / t, "t": t, "launches_per_step": launches, "clocks": clk.summary(),
            "flops_per_step": STEP_FLOPS[kind], "tflops": STEP_FLOPS[kind] / t / 1e12, "global_batch": gb}
     if with_e2e:
         host_in = rig.host_inputs(batch_arrays)
@@ -776,7 +776,7 @@ def roofline_for(workload: str, res: dict, world: int, pk: dict, pk_kind: str, t
     ach = STEP_FLOPS[workload] / world / t_max / 1e12
     out = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
            "peak_kind": pk_kind + " bf16 dense (sustained)", "traffic": None,
-           "kernel": f"whole jitted step ({res['launches_per_step']} launches), per GPU",
+           "kernel": f"whole jitted step ({res['launches_per_step']:g} launches), per GPU",
            "per_step_flops": STEP_FLOPS[workload] // world}
     if "dominant" in res:
         dt, dfl = res["dominant"]
@@ -841,7 +841,7 @@ def line_for(workload, res, a, world, t_max, e2e_max, pk, pk_kind, with_cpu: boo
                        "path": "PJRT BufferFromHostBuffer (pinned) -> Execute -> ToHostBuffer, every step"}
     line["roofline"] = roofline_for(workload, res, world, pk, pk_kind, t_max)
     line["clocks"] = res.get("clocks")
-    line["gpu_launches"] = res["launches_per_step"] * a.steps
+    line["gpu_launches"] = int(round(res["launches_per_step"] * a.steps))
     if "tflops" in res:
         line["tflops_per_step_whole_job"] = STEP_FLOPS[workload] / t_max / 1e12
     if "last_loss" in res:

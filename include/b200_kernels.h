@@ -37,6 +37,12 @@ enum { B200_DT_PRED = 1, B200_DT_S32 = 4, B200_DT_U32 = 8, B200_DT_F32 = 11, B20
 B200_API const char* b200_last_error(void);
 /* Library version string "b200-kernels <semver> sm_100a". */
 B200_API const char* b200_kernels_version(void);
+/* How many kernels this library has launched in this process, every kernel an
+ * entry point below starts counted (a split-K GEMM counts its partial-sum
+ * reduction too).  For counting the launches of a timed region: read it before
+ * and after.  The reference has no counterpart (MLX launches its own kernels
+ * inside mx::eval). */
+B200_API uint64_t b200_kernel_launches(void);
 
 /* Fused residual-add + LayerNorm / RMSNorm forward over the last axis.
  *   h = x + residual        (residual may be NULL: h = x)

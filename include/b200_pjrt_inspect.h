@@ -10,6 +10,7 @@
 #ifndef B200_PJRT_INSPECT_H_
 #define B200_PJRT_INSPECT_H_
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -31,6 +32,13 @@ __attribute__((visibility("default"))) void b200_pjrt_free(char* p);
  * addressable.  For profiling and event timing only: work enqueued on it by the
  * caller is ordered with the plugin's work. */
 __attribute__((visibility("default"))) void* b200_pjrt_device_stream(void* device);
+
+/* How many of its generated kernels (the CUDA C of fused loops, rows,
+ * reductions, gathers and scatters) the plugin has launched in this process.
+ * The hand-written kernels an Execute calls are counted by libb200_kernels.so's
+ * b200_kernel_launches(); the two together are every kernel an Execute starts.
+ * The reference has no counterpart. */
+__attribute__((visibility("default"))) uint64_t b200_pjrt_kernel_launches(void);
 
 /* With B200_TIMING=1 in the environment, every Execute records CUDA events on
  * the first device's stream around its launch sequence (after host-side

@@ -2196,6 +2196,10 @@ __attribute__((visibility("default"))) int b200_pjrt_inspect(const char* mlir, s
 }
 __attribute__((visibility("default"))) void b200_pjrt_free(char* p) { std::free(p); }
 
+__attribute__((visibility("default"))) uint64_t b200_pjrt_kernel_launches(void) {
+  return (uint64_t)b200::g_generated_launches.load(std::memory_order_relaxed);
+}
+
 __attribute__((visibility("default"))) int b200_pjrt_execute_times(void* loaded_executable,
                                                                   double* ms, int max) {
   auto* le = static_cast<PJRT_LoadedExecutable*>(loaded_executable);

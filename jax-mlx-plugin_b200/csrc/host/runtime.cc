@@ -335,7 +335,10 @@ void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cu_check(Driver::get().LaunchKernelEx(&cfg, f, args.data(), nullptr), "cuLaunchKernelEx");
+  g_generated_launches.fetch_add(1, std::memory_order_relaxed);
 }
+
+std::atomic<unsigned long long> g_generated_launches{0};
 
 // ------------------------------------------------------------------ NCCL --
 struct Nccl {

@@ -115,6 +115,8 @@ void fault_point(const char* where);
 // stream.
 bool overlap_collectives();
 
+// Generated kernels launched by launch() in this process.
+extern std::atomic<unsigned long long> g_generated_launches;
 // Launch a generated kernel.
 void launch(Device& d, CUfunction f, const int64_t grid[3], const int64_t block[3], int smem,
             std::vector<void*>& args);

@@ -23,6 +23,13 @@ bool pdl_enabled() {
 extern "C" const char* b200_last_error(void) { return b200::g_last_error.c_str(); }
 extern "C" const char* b200_kernels_version(void) { return "b200-kernels 0.1.0 sm_100a"; }
 
+namespace b200 {
+std::atomic<unsigned long long> g_kernel_launches{0};
+}  // namespace b200
+extern "C" uint64_t b200_kernel_launches(void) {
+  return (uint64_t)b200::g_kernel_launches.load(std::memory_order_relaxed);
+}
+
 // ------------------------------------------------------------ TMA + errors --
 #include <cudaTypedefs.h>
 

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <atomic>
 #include <string>
 #include <utility>
 
@@ -66,6 +67,9 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // previous kernel to finish before it starts, as a plain <<<>>> launch does).
 bool pdl_enabled();
 
+// Kernels this library has launched in this process (b200_kernel_launches()).
+extern std::atomic<unsigned long long> g_kernel_launches;
+
 // cudaLaunchKernelEx with the programmatic-serialization attribute; the kernel
 // must begin with pdl_wait().
 template <typename... KArgs, typename... Args>
@@ -81,7 +85,9 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e == cudaSuccess) g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return e;
 }
 
 // launch_k + the launch-error check, returning from the calling function.

@@ -620,8 +620,8 @@ __global__ void __launch_bounds__(kPersThreads, 1)
 // of one TPC) computes 256 x 256 output tiles with tcgen05.mma.cta_group::2.
 // Each CTA loads its own 128 rows of A and 128 of B's 256 columns per k-block
 // (32 KB instead of the one-SM tile's 48 KB for 128 x 256 outputs), so a tile
-// needs a third fewer operand bytes per SM, and the six-stage ring holds
-// 192 KB in flight.  Roles as in gemm_tc_pers: warp 0 of each CTA streams its
+// needs a third fewer operand bytes per SM, and the five-stage ring holds
+// 160 KB in flight.  Roles as in gemm_tc_pers: warp 0 of each CTA streams its
 // halves (both CTAs' loads complete on the rank-0 CTA's stage barrier, which
 // rank 0 arms with the pair's byte count); warp 1 of rank 0 issues the MMAs
 // (M = 256, N = 256, K = 16) into one of two TMEM accumulators and commits
@@ -632,8 +632,8 @@ struct PairCfg {
   static constexpr int A_BYTES = 128 * 128;  // this CTA's 128 rows x 64 bf16
   static constexpr int B_BYTES = 128 * 128;  // 128 of the tile's 256 columns x 64 bf16
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 6;
-  static constexpr int EPI_BYTES = 8 * 4096;
+  static constexpr int STAGES = 5;
+  static constexpr int EPI_BYTES = 8 * 8192;  // 8 KB of output staging per epilogue warp
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
   static_assert(SMEM <= 232448, "shared memory above the 227 KB per-block limit");
 };
@@ -664,8 +664,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
   const int rank = (int)cluster_rank();
   const int pair = (int)blockIdx.x >> 1, npairs = (int)gridDim.x >> 1;
   const int tiles_mn = p.tiles_m * p.tiles_n;
-  const int num_tiles = tiles_mn * p.batch;
-  auto decode = [&](int t, int& m0, int& n0, int& bz) {
+  const int num_tiles = tiles_mn * p.batch * p.splits;  // work units: tiles x K splits
+  auto decode = [&](int t, int& m0, int& n0, int& bz, int& ks, int& kb0, int& nkb) {
     const int bs = t / tiles_mn, r = t - bs * tiles_mn;
     int mi, ni;
     if (p.group > 1) {
@@ -684,7 +684,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
     }
     m0 = mi * 256;
     n0 = ni * BN;
-    bz = bs;
+    bz = bs / p.splits;
+    ks = bs - bz * p.splits;
+    kb0 = ks * p.kb_per_split;
+    nkb = max(0, min(p.kb_all, kb0 + p.kb_per_split) - kb0);
   };
 
   if (threadIdx.x == 0) {
@@ -711,18 +714,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const int kb_all = p.kb_all;
 
   if (warp == 0) {
     if (lane == 0) {  // ---- TMA producer (both CTAs)
       int it = 0;
       bool ok = true;
       for (int t = pair; ok && t < num_tiles; t += npairs) {
-        int m0, n0, bz;
-        decode(t, m0, n0, bz);
+        int m0, n0, bz, ks, kb0, nkb;
+        decode(t, m0, n0, bz, ks, kb0, nkb);
         const int mr = m0 + rank * 128, nr = n0 + rank * 128;  // this CTA's rows / columns
-        for (int kb = 0; kb < kb_all; ++kb, ++it) {
-          const int s = it % S;
+        for (int i = 0; i < nkb; ++i, ++it) {
+          const int s = it % S, kb = kb0 + i;
           if (it >= S && !mbar_wait(&empty[s], ((it / S) + 1) & 1, abort, p.err, 121)) {
             ok = false;
             break;
@@ -754,11 +756,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
       int it = 0, tl = 0;
       bool ok = true;
       for (int t = pair; ok && t < num_tiles; t += npairs, ++tl) {
+        int m0, n0, bz, ks, kb0, nkb;
+        decode(t, m0, n0, bz, ks, kb0, nkb);
         const int acc = tl & 1;
         if (tl >= 2 && !mbar_wait(&tempty[acc], ((tl >> 1) + 1) & 1, abort, p.err, 122)) break;
         tc_fence_after();
         const uint32_t dt = tmem + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kb_all; ++kb, ++it) {
+        for (int i = 0; i < nkb; ++i, ++it) {
           const int s = it % S;
           if (!mbar_wait(&full[s], (it / S) & 1, abort, p.err, 123)) {
             ok = false;
@@ -768,7 +772,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
           const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16_pair(dt, desc(a0, kk, p.a_mn), desc(b0, kk, p.b_mn), idesc, (kb | kk) != 0);
+            umma_f16_pair(dt, desc(a0, kk, p.a_mn), desc(b0, kk, p.b_mn), idesc, (i | kk) != 0);
           umma_commit_pair(&empty[s]);
         }
         if (!ok) break;
@@ -776,15 +780,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
       }
     }
   } else {  // ---- warps 2..9 of both CTAs: epilogue of this CTA's 128 rows
+    // Each warp drains 32 rows x 128 columns per tile in rounds of two
+    // 128-byte-wide boxes (8 KB of staging): one proxy fence per round, the
+    // accumulator released as soon as its last columns are in registers, and
+    // the staging reused once the previous round's stores have read it.
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    uint8_t* stg = epi_smem + (warp - 2) * 4096;
-    constexpr int CW = 128 / (int)sizeof(TO);  // output columns per 128-byte chunk
-    constexpr int NCH = BN / CW;
-    int tl = 0, nstore = 0;
+    uint8_t* stg = epi_smem + (warp - 2) * 8192;
+    constexpr int CW = 128 / (int)sizeof(TO);  // output columns per 128-byte box
+    constexpr int NB = (BN / 2) / CW;          // boxes per warp and tile: 2 (bf16), 4 (f32)
+    int tl = 0;
+    bool pending = false;
     for (int t = pair; t < num_tiles; t += npairs, ++tl) {
-      int m0, n0, bz;
-      decode(t, m0, n0, bz);
+      int m0, n0, bz, ks, kb0, nkb;
+      decode(t, m0, n0, bz, ks, kb0, nkb);
+      const int zc = bz * p.splits + ks;  // output slice: the batch entry, or its split's partials
       const int acc = tl & 1;
       bool ok = mbar_wait(&tfull[acc], (tl >> 1) & 1, abort, p.err, 124);
       if (!__all_sync(0xffffffffu, ok)) break;
@@ -792,51 +802,68 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const int rowbase = m0 + rank * 128 + q * 32;
 #pragma unroll 1
-      for (int c = half * (NCH / 2); c < (half + 1) * (NCH / 2); ++c) {
-        const int nc = n0 + c * CW;
-        if (nc >= p.N || rowbase >= p.M) continue;
-        float v[CW];
-        tmem_ld32(trow + (uint32_t)(c * CW), v);
-        if (CW == 64) tmem_ld32(trow + (uint32_t)(c * CW + 32), v + 32);
-#pragma unroll
-        for (int j = 0; j < CW; ++j) {
-          float x = v[j] * p.alpha;
-          if (p.epi == 1 || p.epi == 2) {
-            const int n = nc + j;
-            x += n < p.N ? load_bias<TO>(p.bias, n) : 0.f;
-          }
-          if (p.epi >= 2) x = fmaxf(x, 0.f);
-          v[j] = x;
+      for (int r = 0; r < NB / 2; ++r) {
+        if (pending) {  // the previous round's stores must have read the staging
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
         }
-        uint8_t* buf = stg;  // its previous store must have read it
-        if (lane == 0 && nstore >= 1) bulk_wait_group_read<0>();
-        __syncwarp();
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          uint4 w;
-          if (sizeof(TO) == 4) {
-            w = make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
-                           __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
-          } else {
-            auto pk = [&](int j) {
-              __nv_bfloat162 h = __floats2bfloat162_rn(v[j], v[j + 1]);
-              return *reinterpret_cast<uint32_t*>(&h);
-            };
-            w = make_uint4(pk(8 * u), pk(8 * u + 2), pk(8 * u + 4), pk(8 * u + 6));
+        for (int i = 0; i < 2; ++i) {
+          const int c = half * NB + 2 * r + i;
+          uint32_t raw[CW];
+          tmem_ld32_async(trow + (uint32_t)(c * CW), raw);
+          if (CW == 64) tmem_ld32_async(trow + (uint32_t)(c * CW + 32), raw + 32);
+          tmem_wait_ld();
+          if (nkb == 0) {  // an empty K range: the accumulator was never written
+#pragma unroll
+            for (int j = 0; j < CW; ++j) raw[j] = 0u;
           }
-          *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) = w;
+          if (r == NB / 2 - 1 && i == 1) {  // every column of the accumulator is read
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(pair_leader_addr(smem_u32(&tempty[acc])));
+          }
+          const int nc = n0 + c * CW;
+          float v[CW];
+#pragma unroll
+          for (int j = 0; j < CW; ++j) {
+            float x = __uint_as_float(raw[j]) * p.alpha;
+            if (p.epi == 1 || p.epi == 2) {
+              const int n = nc + j;
+              x += n < p.N ? load_bias<TO>(p.bias, n) : 0.f;
+            }
+            if (p.epi >= 2) x = fmaxf(x, 0.f);
+            v[j] = x;
+          }
+          uint8_t* buf = stg + i * 4096;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            uint4 w;
+            if (sizeof(TO) == 4) {
+              w = make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                             __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
+            } else {
+              auto pk = [&](int j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(v[j], v[j + 1]);
+                return *reinterpret_cast<uint32_t*>(&h);
+              };
+              w = make_uint4(pk(8 * u), pk(8 * u + 2), pk(8 * u + 4), pk(8 * u + 6));
+            }
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) = w;
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_3d(&tC, buf, nc, rowbase, bz);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int nc = n0 + (half * NB + 2 * r + i) * CW;
+            if (nc < p.N && rowbase < p.M) tma_store_3d(&tC, stg + i * 4096, nc, rowbase, zc);
+          }
           bulk_commit_group();
         }
-        ++nstore;
+        pending = true;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(pair_leader_addr(smem_u32(&tempty[acc])));
     }
     if (lane == 0) bulk_wait_group_all();
     __syncwarp();
@@ -1459,9 +1486,11 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   return B200_OK;
 }
 
-// The two-SM GEMM for bf16 operands: 256 x 256 tiles, no split-K (shapes
-// with too few tiles to fill the GPU stay on the one-SM kernel, which can
-// split K).  B200_GEMM_PAIR=0 turns it off.
+// The two-SM GEMM for bf16 operands: 256 x 256 tiles.  With fewer tiles than
+// SM pairs, K is split so that about one (tile, K range) unit lands on each
+// pair; the units write raw f32 partial sums which splitk_reduce adds in split
+// order (alpha, bias and activation applied there).  Shapes that neither fill
+// the pairs nor split stay on the one-SM kernel.  B200_GEMM_PAIR=0 turns it off.
 bool use_pair() {
   static bool on = [] {
     const char* v = std::getenv("B200_GEMM_PAIR");
@@ -1470,18 +1499,70 @@ bool use_pair() {
   return on;
 }
 
+// K splits for `tiles` pair tiles over `pairs` resident pairs: one unit per
+// pair, or two when one leaves more than a tenth of the pairs idle; at least
+// four k-blocks per unit.
+SplitPlan plan_pair_splits(int64_t tiles, int kblocks, int64_t batch, int64_t pairs) {
+  SplitPlan sp;
+  sp.per_split = std::max(kblocks, 1);
+  if (tiles >= pairs) return sp;
+  auto plan = [&](int64_t want) {
+    SplitPlan r;
+    want = std::min<int64_t>({want, kblocks / 4, 64, 65535 / std::max<int64_t>(batch, 1)});
+    if (want <= 1) return r;
+    r.per_split = (int)((kblocks + want - 1) / want);
+    r.splits = (kblocks + r.per_split - 1) / r.per_split;
+    return r;
+  };
+  auto busy = [&](const SplitPlan& r) {  // fraction of pair slots doing work
+    const int64_t units = tiles * r.splits;
+    return (double)units / (double)(((units + pairs - 1) / pairs) * pairs);
+  };
+  const SplitPlan one = plan(pairs / tiles);
+  if (one.splits > 1 && busy(one) >= 0.9) return one;
+  const SplitPlan two = plan(2 * pairs / tiles);
+  return busy(two) > busy(one) ? two : one;
+}
+
 template <typename TO>
 int launch_pair(const void* a, const void* b, void* c, const void* bias, int64_t batch, int64_t M,
                 int64_t N, int64_t K, int64_t sAb, int64_t sAm, int64_t sAk, int64_t sBb, int64_t sBk,
                 int64_t sBn, int64_t ldc, float alpha, int epi, int a_mn, int b_mn, cudaStream_t st,
                 Scratch& scratch) {
   constexpr int ES = 2, BK = 64, E = 64;
+  const int smem = PairCfg::SMEM;
+  // Clusters live inside one GPC, so fewer than num_sms / 2 pairs may fit at
+  // once; a persistent grid larger than that would run a second wave.
+  static const int max_pairs = [&] {
+    if (allow_dynamic_smem((const void*)gemm_tc_pair<float>, smem, "gemm_tc_pair")) return num_sms() / 2;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(num_sms() & ~1);
+    cfg.blockDim = dim3(kPersThreads);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_tc_pair<float>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    return n;
+  }();
   const int64_t tiles_m = (M + 255) / 256, tiles_n = (N + 255) / 256;
-  const int64_t num_tiles = tiles_m * tiles_n * batch;
-  if (M < 256 || N < 256 || num_tiles < num_sms() / 2 || num_tiles >= (1ll << 30)) return B200_ERR_UNSUPPORTED;
+  const int64_t tiles = tiles_m * tiles_n * batch;
+  const int KB_all = (int)((K + BK - 1) / BK);
+  if (M < 256 || N < 256 || tiles >= (1ll << 30)) return B200_ERR_UNSUPPORTED;
+  const SplitPlan sp = plan_pair_splits(tiles, KB_all, batch, max_pairs);
+  const bool ws = sp.splits > 1;
+  if (!ws && tiles < max_pairs) return B200_ERR_UNSUPPORTED;
   const int so = (int)sizeof(TO);
-  if (((uintptr_t)c & 15) != 0 || (ldc * so) % 16 != 0 || (batch > 1 && ((M * ldc * so) % 16) != 0))
+  if (ws ? (N * 4) % 16 != 0
+         : (((uintptr_t)c & 15) != 0 || (ldc * so) % 16 != 0 || (batch > 1 && ((M * ldc * so) % 16) != 0)))
     return B200_ERR_UNSUPPORTED;
+  const size_t ws_bytes = ws ? sizeof(float) * (size_t)sp.splits * batch * M * N : 0;
+  if (ws && scratch.lent && ws_bytes > scratch.lent_bytes) return B200_ERR_UNSUPPORTED;
+  float* wsp = nullptr;
+  if (ws) {
+    if (int rc2 = scratch.get(ws_bytes, st, &wsp)) return rc2;
+  }
   if (scratch.query) return kWorkspaceQueried;
   auto bstride = [&](int64_t s, int64_t outer_stride, int64_t outer_dim) -> uint64_t {
     const int64_t v = batch == 1 ? outer_stride * outer_dim : s;
@@ -1513,7 +1594,12 @@ int launch_pair(const void* a, const void* b, void* c, const void* bias, int64_t
     rc = make_tmap(&tb, b, 3, dims, str, box, ES);
   }
   if (rc) return rc;
-  {
+  if (ws) {  // partials: [batch * splits][M][N] f32
+    uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)(batch * sp.splits)};
+    uint64_t str[2] = {(uint64_t)(N * 4), (uint64_t)(M * N * 4)};
+    uint32_t box[3] = {32, 32, 1};
+    rc = make_tmap(&tc, wsp, 3, dims, str, box, 4);
+  } else {
     uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)batch};
     uint64_t str[2] = {(uint64_t)(ldc * so), (uint64_t)(((M * ldc * so) + 15) / 16 * 16)};
     uint32_t box[3] = {(uint32_t)(128 / so), 32, 1};
@@ -1526,37 +1612,27 @@ int launch_pair(const void* a, const void* b, void* c, const void* bias, int64_t
   p.K = (int)K;
   p.a_mn = a_mn;
   p.b_mn = b_mn;
-  p.alpha = alpha;
-  p.bias = bias;
-  p.epi = epi;
+  p.alpha = ws ? 1.f : alpha;
+  p.bias = ws ? nullptr : bias;
+  p.epi = ws ? 0 : epi;
   p.tiles_m = (int)tiles_m;
   p.tiles_n = (int)tiles_n;
   p.batch = (int)batch;
-  p.splits = 1;
-  p.kb_all = (int)((K + BK - 1) / BK);
-  p.kb_per_split = p.kb_all;
+  p.splits = sp.splits;
+  p.kb_all = KB_all;
+  p.kb_per_split = sp.per_split;
   p.n_fast = tiles_n <= tiles_m ? 1 : 0;
   p.group = (tiles_m >= 16 && tiles_n >= 16) ? 8 : 1;
-  p.out_ws = 0;
+  p.out_ws = ws ? 1 : 0;
   p.err = scratch.err ? scratch.err : device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
-  const int smem = PairCfg::SMEM;
+  const unsigned grid = (unsigned)(2 * std::min<int64_t>(tiles * sp.splits, max_pairs));
+  if (ws) {
+    if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pair<float>, smem, "gemm_tc_pair")) return rc2;
+    B200_LAUNCH(gemm_tc_pair<float>, dim3(grid), dim3(kPersThreads), smem, st, ta, tb, tc, p);
+    return launch_splitk_reduce<TO>(wsp, (TO*)c, bias, batch, M, N, sp.splits, ldc, alpha, epi, st);
+  }
   if (int rc2 = allow_dynamic_smem((const void*)gemm_tc_pair<TO>, smem, "gemm_tc_pair")) return rc2;
-  // Clusters live inside one GPC, so fewer than num_sms / 2 pairs may fit at
-  // once; a persistent grid larger than that would run a second wave.
-  static int max_pairs = [&] {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(num_sms() & ~1);
-    cfg.blockDim = dim3(kPersThreads);
-    cfg.dynamicSmemBytes = smem;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_tc_pair<TO>, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      n = num_sms() / 2;
-    }
-    return n;
-  }();
-  const unsigned grid = (unsigned)(2 * std::min<int64_t>(num_tiles, max_pairs));
   B200_LAUNCH(gemm_tc_pair<TO>, dim3(grid), dim3(kPersThreads), smem, st, ta, tb, tc, p);
   return B200_OK;
 }

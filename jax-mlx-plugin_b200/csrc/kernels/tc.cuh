@@ -290,9 +290,11 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
           smem_u32(bar))
       : "memory");
 }
-// Arrive (release, cluster scope) on a barrier given by its shared::cluster address.
+// Arrive on a barrier given by its shared::cluster address (this CTA's or the
+// peer's).  Default semantics (release at CTA scope): what the arrive orders
+// for its waiter is TMEM reads, which tcgen05.fence::before_thread_sync covers.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // UMMA shared-memory layouts (descriptor bits 61-63).

@@ -38,6 +38,7 @@ EXPORTS = {
                           [C.c_float, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "b200_gemm_uses_tensor_cores": (C.c_int, [C.c_void_p, C.c_void_p] + [C.c_int64] * 8 + [C.c_int]),
     "b200_device_error": (C.c_int, [C.c_int]),
+    "b200_kernel_launches": (C.c_uint64, []),
 }
 
 _lib = None

@@ -598,6 +598,17 @@ def kv_exchange(store, rank: int, key: str, value: bytes = b"") -> bytes:
     return res
 
 
+def kernel_launches() -> int:
+    """Kernels started so far in this process: the plugin's generated kernels
+    (b200_pjrt_kernel_launches) plus the hand-written ones of the kernel library
+    it calls (b200_kernel_launches).  Read before and after a region to count
+    its launches."""
+    from . import kernels
+    f = api().lib.b200_pjrt_kernel_launches
+    f.restype, f.argtypes = C.c_uint64, []
+    return int(f()) + int(kernels.lib().b200_kernel_launches())
+
+
 def inspect(mlir_text, what: int = 1) -> str:
     """Run the compile pipeline without a device (see include/b200_pjrt_inspect.h).
     mlir_text: StableHLO text (str) or the program's bytes (text, or a portable

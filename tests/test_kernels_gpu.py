@@ -296,23 +296,32 @@ def _kernel_names(fn):
                                                      (2520, 2376, 200, True, False, 1, 2),
                                                      (2520, 2376, 200, True, True, 1, 0),
                                                      (1000, 744, 128, False, True, 8, 1),
-                                                     (4200, 4160, 72, False, True, 1, 0)])
+                                                     (4200, 4160, 72, False, True, 1, 0),
+                                                     (512, 512, 8192, True, False, 1, 0),
+                                                     (600, 520, 3000, True, False, 1, 2),
+                                                     (256, 512, 2048, False, True, 4, 1)])
 def test_gemm_two_sm_pairs(M, N, K, a_t, b_t, batch, epi, out_dt):
-    """bf16 GEMMs with at least 74 tiles of 256 x 256 run on the two-SM kernel
-    (one 256-row MMA per SM pair, cta_group::2): ragged M, N and K, every
-    operand layout, a batch, the bias and bias+relu epilogues and the grouped
-    tile order (17 x 17 tiles).  vs f64 on the bf16 values, 1e-2 relative."""
+    """bf16 GEMMs run on the two-SM kernel (one 256-row MMA per SM pair,
+    cta_group::2): with at least 74 tiles of 256 x 256 whole, with fewer (the
+    last three shapes: weight-gradient-like, long K) as K splits whose f32
+    partials are summed afterwards.  Ragged M, N and K, every operand layout,
+    a batch, the bias and bias+relu epilogues and the grouped tile order
+    (17 x 17 tiles).  vs f64 on the bf16 values, 1e-2 relative."""
     res = {}
 
     def run():
         res["v"] = _gemm_case(M, N, K, a_t, b_t, kernels.DT_BF16, batch=batch, epi=epi,
                               seed=M + N + K + 2 * a_t + b_t, out_dt=out_dt)
 
+    n0 = kernels.lib().b200_kernel_launches()
     names = _kernel_names(run)
+    launched = kernels.lib().b200_kernel_launches() - n0
     got, ref, tc = res["v"]
     assert tc
     if names:
         assert any("gemm_tc_pair" in n for n in names), sorted(names)
+    split = -(-M // 256) * -(-N // 256) * batch < 74  # fewer tiles than SM pairs: K splits + their sum
+    assert launched == (2 if split else 1), launched
     assert_close(got, ref, 1e-2, f"pair gemm {batch}x{M}x{N}x{K} a_t={a_t} b_t={b_t} epi={epi}")
 
 
