@@ -317,6 +317,28 @@ struct PersArgs {
   int* err;
 };
 
+// alpha, bias and activation over one thread's CW consecutive outputs of a
+// row, starting at column nc.  The mode tests sit outside the element loops:
+// inside a fully unrolled loop they were two uniform branches per element,
+// which made the plain case (alpha 1, no bias) cost several times its
+// arithmetic.  Multiplying by an alpha of 1 is skipped (x * 1 == x exactly).
+template <typename TO, int CW>
+__device__ __forceinline__ void epilogue_row(float* v, const PersArgs& p, int nc) {
+  if (p.alpha != 1.f) {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] *= p.alpha;
+  }
+  if (p.epi == 1 || p.epi == 2) {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] += nc + j < p.N ? load_bias<TO>(p.bias, nc + j) : 0.f;
+  }
+  if (p.epi >= 2) {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = fmaxf(v[j], 0.f);
+  }
+}
+
+
 // f32 operands (SPL bits) arrive as bf16 hi and lo planes (split_planes); every
 // K step issues hi*hi plus hi*lo for a split B and lo*hi for a split A (an
 // operand that is bf16 already has no lo part: a mixed f32 x bf16 product
@@ -557,16 +579,7 @@ __global__ void __launch_bounds__(kPersThreads, 1)
 #pragma unroll
             for (int j = 0; j < CW; ++j) v[j] = 0.f;
           }
-#pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            float x = v[j] * p.alpha;
-            if (p.epi == 1 || p.epi == 2) {
-              const int n = nc + j;
-              x += n < p.N ? load_bias<TO>(p.bias, n) : 0.f;
-            }
-            if (p.epi >= 2) x = fmaxf(x, 0.f);
-            v[j] = x;
-          }
+          epilogue_row<TO, CW>(v, p, nc);
           uint8_t* buf = stg;  // its previous store must have read it
           if (lane == 0 && nstore >= 1) bulk_wait_group_read<0>();
           __syncwarp();
@@ -826,15 +839,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
           const int nc = n0 + c * CW;
           float v[CW];
 #pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            float x = __uint_as_float(raw[j]) * p.alpha;
-            if (p.epi == 1 || p.epi == 2) {
-              const int n = nc + j;
-              x += n < p.N ? load_bias<TO>(p.bias, n) : 0.f;
-            }
-            if (p.epi >= 2) x = fmaxf(x, 0.f);
-            v[j] = x;
-          }
+          for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(raw[j]);
+          epilogue_row<TO, CW>(v, p, nc);
           uint8_t* buf = stg + i * 4096;
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
@@ -1029,6 +1035,27 @@ SplitPlan plan_splits(int64_t tiles, int kblocks, int min_blocks, int64_t batch)
   sp.per_split = (int)((kblocks + want - 1) / want);
   sp.splits = (kblocks + sp.per_split - 1) / sp.per_split;
   return sp;
+}
+
+// The order in which a persistent grid walks its output tiles.  When one
+// operand's whole panel (all its rows of one batch entry) is small enough to
+// stay in L2 (24 MB) while the other streams past, the walk runs along that
+// operand's tiles fastest: it stays resident and each panel of the other is
+// read from memory once (the LM head's 16 MB of activations against 32 MB of
+// weights and 1 GB of logits written meanwhile).  Otherwise groups of `group`
+// M tiles are walked N-major, so the tiles resident at once cover a squarish
+// block of C whose A and B panels stay in L2.
+void tile_order(int64_t M, int64_t N, int64_t K, int64_t tiles_m, int64_t tiles_n, int group,
+                PersArgs& p) {
+  const double a_bytes = 2.0 * M * K, b_bytes = 2.0 * N * K;
+  constexpr double kResident = 24.0 * (1 << 20);
+  if (std::min(a_bytes, b_bytes) <= kResident) {
+    p.n_fast = b_bytes <= a_bytes ? 1 : 0;  // N fastest: B is the resident panel
+    p.group = 1;
+    return;
+  }
+  p.n_fast = tiles_n <= tiles_m ? 1 : 0;
+  p.group = (tiles_m >= 2 * group && tiles_n >= 16) ? group : 1;
 }
 
 // Where split-K partial sums live.  b200_gemm takes stream-ordered memory from
@@ -1457,9 +1484,7 @@ int launch_pers(const void* a, const void* b, void* c, const void* bias, int64_t
   p.splits = sp.splits;
   p.kb_per_split = sp.per_split;
   p.kb_all = KB_all;
-  p.n_fast = tiles_n <= tiles_m ? 1 : 0;
-  // large 2-D tile grids: 16 M tiles x (num_sms / 16) N tiles are resident at once
-  p.group = (tiles_m >= 32 && tiles_n >= 16) ? 16 : 1;
+  tile_order(M, N, K, tiles_m, tiles_n, 16, p);
   p.out_ws = ws ? 1 : 0;
   p.err = scratch.err ? scratch.err : device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
@@ -1621,8 +1646,7 @@ int launch_pair(const void* a, const void* b, void* c, const void* bias, int64_t
   p.splits = sp.splits;
   p.kb_all = KB_all;
   p.kb_per_split = sp.per_split;
-  p.n_fast = tiles_n <= tiles_m ? 1 : 0;
-  p.group = (tiles_m >= 16 && tiles_n >= 16) ? 8 : 1;
+  tile_order(M, N, K, tiles_m, tiles_n, 8, p);
   p.out_ws = ws ? 1 : 0;
   p.err = scratch.err ? scratch.err : device_error_word();
   if (!p.err) return set_error(B200_ERR_CUDA, "could not allocate the device error word");
