@@ -633,8 +633,8 @@ __global__ void __launch_bounds__(kPersThreads, 1)
 // of one TPC) computes 256 x 256 output tiles with tcgen05.mma.cta_group::2.
 // Each CTA loads its own 128 rows of A and 128 of B's 256 columns per k-block
 // (32 KB instead of the one-SM tile's 48 KB for 128 x 256 outputs), so a tile
-// needs a third fewer operand bytes per SM, and the five-stage ring holds
-// 160 KB in flight.  Roles as in gemm_tc_pers: warp 0 of each CTA streams its
+// needs a third fewer operand bytes per SM, and the six-stage ring holds
+// 192 KB in flight.  Roles as in gemm_tc_pers: warp 0 of each CTA streams its
 // halves (both CTAs' loads complete on the rank-0 CTA's stage barrier, which
 // rank 0 arms with the pair's byte count); warp 1 of rank 0 issues the MMAs
 // (M = 256, N = 256, K = 16) into one of two TMEM accumulators and commits
@@ -645,8 +645,8 @@ struct PairCfg {
   static constexpr int A_BYTES = 128 * 128;  // this CTA's 128 rows x 64 bf16
   static constexpr int B_BYTES = 128 * 128;  // 128 of the tile's 256 columns x 64 bf16
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 5;
-  static constexpr int EPI_BYTES = 8 * 8192;  // 8 KB of output staging per epilogue warp
+  static constexpr int STAGES = 6;
+  static constexpr int EPI_BYTES = 8 * 4096;  // 4 KB of output staging per epilogue warp
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 + 256;
   static_assert(SMEM <= 232448, "shared memory above the 227 KB per-block limit");
 };
@@ -793,13 +793,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
       }
     }
   } else {  // ---- warps 2..9 of both CTAs: epilogue of this CTA's 128 rows
-    // Each warp drains 32 rows x 128 columns per tile in rounds of two
-    // 128-byte-wide boxes (8 KB of staging): one proxy fence per round, the
-    // accumulator released as soon as its last columns are in registers, and
-    // the staging reused once the previous round's stores have read it.
+    // Each warp drains 32 rows x 128 columns per tile, one 128-byte-wide box
+    // (4 KB of staging) at a time: the accumulator is released as soon as its
+    // last columns are in registers, and the staging is rewritten once the
+    // previous box's store has read it.
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
-    uint8_t* stg = epi_smem + (warp - 2) * 8192;
+    uint8_t* stg = epi_smem + (warp - 2) * 4096;
     constexpr int CW = 128 / (int)sizeof(TO);  // output columns per 128-byte box
     constexpr int NB = (BN / 2) / CW;          // boxes per warp and tile: 2 (bf16), 4 (f32)
     int tl = 0;
@@ -815,57 +815,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersThreads, 1)
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const int rowbase = m0 + rank * 128 + q * 32;
 #pragma unroll 1
-      for (int r = 0; r < NB / 2; ++r) {
-        if (pending) {  // the previous round's stores must have read the staging
+      for (int i = 0; i < NB; ++i) {
+        const int c = half * NB + i;
+        uint32_t raw[CW];
+        tmem_ld32_async(trow + (uint32_t)(c * CW), raw);
+        if (CW == 64) tmem_ld32_async(trow + (uint32_t)(c * CW + 32), raw + 32);
+        tmem_wait_ld();
+        if (nkb == 0) {  // an empty K range: the accumulator was never written
+#pragma unroll
+          for (int j = 0; j < CW; ++j) raw[j] = 0u;
+        }
+        if (i == NB - 1) {  // every column of the accumulator is read
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(pair_leader_addr(smem_u32(&tempty[acc])));
+        }
+        const int nc = n0 + c * CW;
+        float v[CW];
+#pragma unroll
+        for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(raw[j]);
+        epilogue_row<TO, CW>(v, p, nc);
+        if (pending) {  // the previous box's store must have read the staging
           if (lane == 0) bulk_wait_group_read<0>();
           __syncwarp();
         }
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int c = half * NB + 2 * r + i;
-          uint32_t raw[CW];
-          tmem_ld32_async(trow + (uint32_t)(c * CW), raw);
-          if (CW == 64) tmem_ld32_async(trow + (uint32_t)(c * CW + 32), raw + 32);
-          tmem_wait_ld();
-          if (nkb == 0) {  // an empty K range: the accumulator was never written
-#pragma unroll
-            for (int j = 0; j < CW; ++j) raw[j] = 0u;
+        for (int u = 0; u < 8; ++u) {
+          uint4 w;
+          if (sizeof(TO) == 4) {
+            w = make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                           __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
+          } else {
+            auto pk = [&](int j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(v[j], v[j + 1]);
+              return *reinterpret_cast<uint32_t*>(&h);
+            };
+            w = make_uint4(pk(8 * u), pk(8 * u + 2), pk(8 * u + 4), pk(8 * u + 6));
           }
-          if (r == NB / 2 - 1 && i == 1) {  // every column of the accumulator is read
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(pair_leader_addr(smem_u32(&tempty[acc])));
-          }
-          const int nc = n0 + c * CW;
-          float v[CW];
-#pragma unroll
-          for (int j = 0; j < CW; ++j) v[j] = __uint_as_float(raw[j]);
-          epilogue_row<TO, CW>(v, p, nc);
-          uint8_t* buf = stg + i * 4096;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            uint4 w;
-            if (sizeof(TO) == 4) {
-              w = make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
-                             __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3]));
-            } else {
-              auto pk = [&](int j) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(v[j], v[j + 1]);
-                return *reinterpret_cast<uint32_t*>(&h);
-              };
-              w = make_uint4(pk(8 * u), pk(8 * u + 2), pk(8 * u + 4), pk(8 * u + 6));
-            }
-            *reinterpret_cast<uint4*>(buf + lane * 128 + ((u ^ (lane & 7)) << 4)) = w;
-          }
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) = w;
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const int nc = n0 + (half * NB + 2 * r + i) * CW;
-            if (nc < p.N && rowbase < p.M) tma_store_3d(&tC, stg + i * 4096, nc, rowbase, zc);
-          }
+          if (nc < p.N && rowbase < p.M) tma_store_3d(&tC, stg, nc, rowbase, zc);
           bulk_commit_group();
         }
         pending = true;
