@@ -625,3 +625,21 @@ def test_package_declares_jax_plugins_entry_point():
     assert eps == {"b200": "jax_b200.plugin"}
     mod = importlib.import_module(eps["b200"])
     assert callable(mod.initialize) and mod.PLATFORM == "b200"
+
+
+def test_row_reduction_through_a_reshape_loads_each_vector_once():
+    """A row reduction over a reshape that keeps the innermost dim ([4, 8, 64]
+    bf16 logits seen as [32, 64] rows) plus a broadcast bias: each vector group
+    of the logits is one 16-byte load, and the bias column is the row position
+    itself, with no integer division or remainder inside the row loop."""
+    from jax_b200.hlo import Builder
+    b = Builder("row_reduce_through_reshape")
+    x = b.param((4, 8, 64), "bf16")
+    bias = b.param((64,), "bf16")
+    y = b.reshape(x + b.broadcast_in_dim(bias, (4, 8, 64), [2]), (32, 64))
+    m = b.max(b.convert(y, "f32"), [1])
+    source = pjrt.inspect(b.module([m]), 2)
+    body = source[source.index("for (int r = "):source.index("for (int off = 16")]
+    # one vector load of the logits and one of the bias per group of 8
+    assert body.count("__ldg(reinterpret_cast<const uint4*>(") == 2, body
+    assert "% 64" not in body and "/ 64" not in body, body
