@@ -770,7 +770,8 @@ def roofline_for(workload: str, res: dict, world: int, pk: dict, pk_kind: str, t
     if workload == "gemm":
         return {"bound": "tensor", "achieved": res["value"], "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": res["value"] / pk["bf16_tflops"], "peak_kind": pk_kind, "traffic": None,
-                "kernel": "gemm_tc_pers"}
+                "kernel": "b200_gemm: gemm_tc_pair (two-SM 256 x 256 tiles, K splits when tiles are few) "
+                          "or gemm_tc_pers (one-SM tiles) by shape"}
     # training steps: the whole step on one GPU's share of the FLOPs
     peak = pk["bf16_tflops_sustained"]
     ach = STEP_FLOPS[workload] / world / t_max / 1e12
@@ -780,7 +781,7 @@ def roofline_for(workload: str, res: dict, world: int, pk: dict, pk_kind: str, t
            "per_step_flops": STEP_FLOPS[workload] // world}
     if "dominant" in res:
         dt, dfl = res["dominant"]
-        out["dominant_kernel"] = {"kernel": "gemm_tc_pers<256, bf16> LM head 16384x32000x512",
+        out["dominant_kernel"] = {"kernel": "gemm_tc_pair<bf16> LM head 16384x32000x512",
                                   "achieved": dfl / dt / 1e12, "peak": pk["bf16_tflops"],
                                   "frac": dfl / dt / 1e12 / pk["bf16_tflops"],
                                   "peak_kind": pk_kind + " bf16 dense (burst)",
