@@ -456,7 +456,7 @@ def _normwise(got, ref):
     return float(np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30))
 
 
-def test_transformer_step_full_config_matches_torch_port(client):
+def test_transformer_step_full_config_with_sharp_attention(client):
     """configs[3] at full size (6 blocks, d 512, vocab 32000, 64 x 256 tokens,
     attention far from flat) against the torch-CPU restatement of the same
     program (oracle/torch_port.py) evaluated twice: in float64 (no rounding at
@@ -499,52 +499,6 @@ def test_transformer_step_full_config_matches_torch_port(client):
     print(f"full transformer: worst ratio to the bf16 port's error {worst[0]:.2f} ({worst[1]}: "
           f"{worst[2]:.3e} vs {worst[3]:.3e}); median {sorted(r[0] for r in ratios)[len(ratios) // 2]:.2f}")
     assert not failures, "\n".join(failures)
-
-
-def test_cnn_step_full_batch_matches_torch_port(client):
-    """configs[4] at full size (batch 256, He-normal weights, U(0, 1) images):
-    loss and every applied SGD update against the torch-CPU port (f32
-    convolutions and products); loss within 1e-4, updates within 5e-3
-    normwise."""
-    import torch
-    from oracle import torch_port
-    rng = np.random.default_rng(17)
-    shapes = [(3, 3, 1, 32), (32,), (3, 3, 32, 64), (64,), (3136, 256), (256,), (256, 10), (10,)]
-    ps = [(rng.standard_normal(s) * np.sqrt(2.0 / int(np.prod(s[:-1])))).astype(np.float32)
-          if len(s) > 1 else np.zeros(s, np.float32) for s in shapes]
-    x = rng.random((256, 28, 28, 1)).astype(np.float32)
-    lab = rng.integers(0, 10, 256).astype(np.int32)
-    outs = run(client, programs.cnn_step(), ps + [x, lab])
-    loss, new = torch_port.cnn_step([torch.from_numpy(p) for p in ps], torch.from_numpy(x),
-                                    torch.from_numpy(lab))
-    rel_loss = abs(float(outs[0]) - float(loss)) / abs(float(loss))
-    rels = [_normwise(p - g, p - r.numpy()) for p, g, r in zip(ps, outs[1:], new)]
-    print(f"full cnn: loss difference {rel_loss:.2e}, update normwise {max(rels):.2e}")
-    assert rel_loss <= 1e-4
-    assert max(rels) <= 5e-3, rels
-
-
-def test_mlp_step_full_config_matches_torch_port(client):
-    """configs[2] on its own distributions (Glorot-uniform weights, U(0, 1)
-    inputs, batch 1024): loss and every applied SGD update against the
-    torch-CPU port; loss within 1e-4, updates within 5e-3 normwise (a
-    pre-activation within rounding of a ReLU kink may switch sides, which an
-    elementwise check could not allow)."""
-    import torch
-    from oracle import torch_port
-    rng = np.random.default_rng(18)
-    dims = (784, 1024, 1024, 1024, 10)
-    params = _mlp_params(rng, dims)
-    x = rng.random((1024, dims[0])).astype(np.float32)
-    lab = rng.integers(0, 10, 1024).astype(np.int32)
-    outs = run(client, programs.mlp_step(), params + [x, lab])
-    loss, new = torch_port.mlp_step([torch.from_numpy(p) for p in params], torch.from_numpy(x),
-                                    torch.from_numpy(lab))
-    rel_loss = abs(float(outs[0]) - float(loss)) / abs(float(loss))
-    rels = [_normwise(p - g, p - r.numpy()) for p, g, r in zip(params, outs[1:], new)]
-    print(f"full mlp: loss difference {rel_loss:.2e}, update normwise {max(rels):.2e}")
-    assert rel_loss <= 1e-4
-    assert max(rels) <= 5e-3, rels
 
 
 # ------------------------------------------------------- bf16 rounding modes
