@@ -643,3 +643,33 @@ def test_row_reduction_through_a_reshape_loads_each_vector_once():
     # one vector load of the logits and one of the bias per group of 8
     assert body.count("__ldg(reinterpret_cast<const uint4*>(") == 2, body
     assert "% 64" not in body and "/ 64" not in body, body
+
+
+def test_gemm_k_splits_on_sm_pairs():
+    """The split-K plan of the two-SM GEMM, read through the workspace query
+    (host logic only: no kernel runs).  With fewer 256 x 256 tiles than the 74
+    SM pairs of a B200, K is split so that about one unit lands on each pair
+    (two when one would leave more than a tenth of the pairs idle), and the
+    workspace holds splits x M x N f32 partials; with enough tiles nothing is
+    split."""
+    lib = kernels.lib()
+    f = lib.b200_gemm_workspace_bytes
+    f.restype = C.c_int64
+    f.argtypes = [C.c_void_p] * 4 + [C.c_int64] * 11 + [C.c_float, C.c_int, C.c_int, C.c_int,
+                                                        C.c_void_p]
+    fake = 1 << 20  # 16-byte aligned stand-in addresses: the query dereferences nothing
+
+    def splits(M, N, K, a_t):
+        sAm, sAk = (1, M) if a_t else (K, 1)
+        ws = f(fake, fake, fake, None, 1, M, N, K, M * K, sAm, sAk, K * N, N, 1, N, 1.0,
+               kernels.DT_BF16, kernels.DT_BF16, 0, None)
+        assert ws >= 0 and ws % (4 * M * N) == 0, ws
+        return ws // (4 * M * N)
+    # the transformer's weight gradients (activations transposed, K = 16384 tokens)
+    assert splits(512, 512, 16384, True) == 18    # 4 tiles x 18 = 72 units
+    assert splits(2048, 512, 16384, True) == 9    # 16 tiles: 64 units idle 14%, so 144
+    assert splits(512, 2048, 16384, True) == 9
+    assert splits(1024, 1024, 1024, False) == 4   # K = 16 blocks: at least 4 per unit
+    # 128 and 1024 tiles: whole tiles, no partials
+    assert splits(16384, 512, 512, False) == 0
+    assert splits(8192, 8192, 8192, False) == 0
